@@ -1,0 +1,228 @@
+/*
+ * qora_cuda.h — C ABI of libqora_cuda.so, the sm_100a decode engine that sits behind
+ * QORA's SmolLM3-3B forward step.
+ *
+ * Every entry point returns a qora_status (0 = ok). No C++ exception or panic crosses
+ * this boundary; the message of the last failure on the calling thread is available
+ * from qora_last_error(). An engine is driven by one host thread at a time.
+ *
+ * The reference exposes the same path as plain Rust functions; each declaration below
+ * names the reference interface it replaces (path:line inside the qora crate).
+ */
+#ifndef QORA_CUDA_H
+#define QORA_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int qora_status;
+
+#define QORA_OK              0
+#define QORA_ERR_INVALID     1  /* bad argument, shape or file contents              */
+#define QORA_ERR_IO          2  /* file could not be opened / short read             */
+#define QORA_ERR_CUDA        3  /* CUDA runtime error (message has the CUDA string)  */
+#define QORA_ERR_OOM         4  /* device allocation failed                          */
+#define QORA_ERR_RANGE       5  /* token id / position / sequence beyond capacity    */
+#define QORA_ERR_TIMEOUT     6  /* a bounded device-side wait gave up                */
+#define QORA_ERR_UNSUPPORTED 7  /* feature not available in this build / config      */
+#define QORA_ERR_NCCL        8  /* collective failure (tensor-parallel engines)      */
+
+#define QORA_FORMAT_F16 0u
+#define QORA_FORMAT_Q4  1u
+
+/* ------------------------------------------------------------------------------------
+ * Borrowed host views of the weights (replace `WeightRef` / `GpuLayerRef` /
+ * `DecodeWeights::layer_ref` / `embed_ref`, src/gemv.rs:66-96, :248-271).
+ * Orientation (src/gemv.rs:23-38): projections are input-major [k = in][n = out];
+ * Q4 groups of 32 run along n, a group is 16 packed bytes (low nibble = even element)
+ * plus one f16 scale, value = (q - 8) * scale. The embedding is [k = vocab][n = hidden].
+ * The engine copies (and may re-tile) what it needs and keeps no host pointer.
+ * ---------------------------------------------------------------------------------- */
+typedef struct qora_matrix_view {
+    const uint8_t*  packed;  /* Q4: k*n/2 bytes, row ki at ki*(n/2)             */
+    const uint16_t* scales;  /* Q4: k*n/32 f16 bit patterns, row ki at ki*(n/32) */
+    const uint16_t* data;    /* F16: k*n f16 bit patterns, row-major [k][n]      */
+    uint64_t k;
+    uint64_t n;
+} qora_matrix_view;
+
+typedef struct qora_layer_view {
+    qora_matrix_view q_proj, k_proj, v_proj, o_proj, gate_proj, up_proj, down_proj;
+    const uint16_t* input_norm_gamma;      /* [hidden] f16 */
+    const uint16_t* post_attn_norm_gamma;  /* [hidden] f16 */
+    uint32_t num_heads, num_kv_heads, head_dim, num_kv_groups;
+} qora_layer_view;
+
+typedef struct qora_weights_view {
+    uint32_t format;            /* QORA_FORMAT_F16 or QORA_FORMAT_Q4 (src/save.rs:170) */
+    uint32_t num_layers;
+    uint32_t vocab;
+    uint32_t hidden;
+    uint32_t rope_half_dim;
+    const uint8_t* no_rope_layers;   /* [num_layers]; nonzero = APPLY RoPE (src/gemv.rs:885,903) */
+    const qora_layer_view* layers;   /* [num_layers] */
+    qora_matrix_view embed;          /* tied embedding / lm_head, k = vocab, n = hidden */
+    const uint16_t* final_norm_gamma;/* [hidden] f16 */
+    const float* rope_cos;           /* [rope_rows][rope_half_dim] f32 */
+    const float* rope_sin;
+    uint64_t rope_rows;              /* number of positions in the tables */
+} qora_weights_view;
+
+typedef struct qora_engine qora_engine;
+typedef struct qora_kv qora_kv;
+
+/* Engine options. Zero-initialise and set what you need. */
+typedef struct qora_engine_options {
+    int32_t  n_gpus;        /* tensor-parallel degree; 0 or 1 = single GPU          */
+    int32_t  first_device;  /* CUDA ordinal of rank 0 (ranks use first_device + r) */
+    uint32_t flags;         /* reserved, must be 0                                  */
+} qora_engine_options;
+
+/* Last error message of the calling thread ("" if none). */
+const char* qora_last_error(void);
+
+/* Library version string. */
+const char* qora_version(void);
+
+/* Load a .qora file and upload it. Replaces `save::load_model` (src/save.rs:154) +
+ * the cortex upload `load_model_gpu` (src/gpu_loader.rs:134). */
+qora_status qora_engine_create_from_file(const char* qora_path,
+                                         const qora_engine_options* opts,
+                                         qora_engine** out);
+
+/* Upload borrowed host weights (the slices `DecodeWeights` holds, src/gemv.rs:195-206). */
+qora_status qora_engine_create(const qora_weights_view* weights,
+                               const qora_engine_options* opts,
+                               qora_engine** out);
+
+void qora_engine_destroy(qora_engine* engine);
+
+/* Geometry of a loaded engine. */
+qora_status qora_engine_info(const qora_engine* engine, uint32_t* num_layers,
+                             uint32_t* vocab, uint32_t* hidden, uint32_t* format,
+                             uint64_t* device_bytes);
+
+/* KV cache with capacity max_seq positions for `batch` independent sequences, f32,
+ * token-major [seq][kv_heads][head_dim] per layer. Replaces `empty_kv_cache`
+ * (src/gemv.rs:159) / `RawKvCache` (src/gemv.rs:156). batch must be 1 for now. */
+qora_status qora_kv_create(qora_engine* engine, uint32_t max_seq, uint32_t batch,
+                           qora_kv** out);
+void qora_kv_destroy(qora_kv* kv);
+
+/* Current length (positions filled) of sequence seq_idx. */
+qora_status qora_kv_length(const qora_kv* kv, uint32_t seq_idx, uint32_t* len);
+
+/* Reset sequence seq_idx to empty (the reference builds a fresh RawKvCache). */
+qora_status qora_kv_reset(qora_kv* kv, uint32_t seq_idx);
+
+/* Import seq_len positions of one layer, token-major [seq_len][kv_heads][head_dim] f32
+ * host arrays (the `(Vec<f32>, Vec<f32>, usize)` of RawKvCache, src/gemv.rs:156). After
+ * importing every layer with the same seq_len, the sequence length becomes seq_len. */
+qora_status qora_kv_import(qora_kv* kv, uint32_t layer, const float* k, const float* v,
+                           uint32_t seq_len, uint32_t seq_idx);
+
+/* Export the first seq_len positions of one layer to host arrays (same layout). */
+qora_status qora_kv_export(const qora_kv* kv, uint32_t layer, float* k, float* v,
+                           uint32_t seq_len, uint32_t seq_idx);
+
+/* Prompt pass. Replaces `raw_prefill` (src/gemv.rs:1027): the n ids are appended at
+ * positions len..len+n-1 of sequence seq_idx; the logits of the last id are written to
+ * logits_or_null ([vocab] f32) if non-NULL, and its argmax (first maximum) to argmax_out
+ * if non-NULL. */
+qora_status qora_prefill(qora_engine* engine, qora_kv* kv, const uint32_t* ids,
+                         uint32_t n, uint32_t seq_idx, float* logits_or_null,
+                         uint32_t* argmax_out);
+
+/* One decode step. Replaces `forward_decode_raw` (src/gemv.rs:872) followed by the
+ * greedy branch of `sample_token_top_k` (src/generate.rs:346-352). tokens: [batch] host
+ * ids; logits_or_null: [batch][vocab] host f32 (parity / sampling mode) or NULL (greedy
+ * fast path: only argmax_out [batch] is read back). */
+qora_status qora_decode_step(qora_engine* engine, qora_kv* kv, const uint32_t* tokens,
+                             float* logits_or_null, uint32_t* argmax_out);
+
+/* Greedy generation of n_tokens starting from `first_token` entirely on the device
+ * (token feedback without host round trips; the loop of src/main.rs:105-117 and
+ * src/generate.rs:299-331 with temperature 0 and no penalties / EOS stop). Writes
+ * the n_tokens argmax ids to out_tokens. */
+qora_status qora_generate_greedy(qora_engine* engine, qora_kv* kv, uint32_t first_token,
+                                 uint32_t n_tokens, uint32_t* out_tokens);
+
+/* One decoder layer at batch 1 (the body of the layer loop, src/gemv.rs:883-1012):
+ * x ([hidden] host f32) is the residual stream in and out; the layer's K/V row is
+ * appended at the sequence's current length of that layer, which then grows by one. */
+qora_status qora_layer_step(qora_engine* engine, qora_kv* kv, uint32_t layer,
+                            float* x_inout);
+
+/* ------------------------------------------------------------------------------------
+ * Kernel-level entry points on DEVICE pointers (cudaStream_t passed as void*; NULL =
+ * legacy default stream). Used for parity tests and the GEMV bandwidth benchmark.
+ * ---------------------------------------------------------------------------------- */
+
+/* Q4 GEMV in the reference layout: y[n] = x[k] . W[k][n] (replaces `gemv_q4`,
+ * src/gemv.rs:646-675, and `gemv_q4_avx512`, src/simd.rs:44-83). packed/scales are the
+ * F1-layout arrays as in the file; n % 32 == 0. Scratch for the split-K partial sums is
+ * allocated on first use and cached by the library (per device). */
+qora_status qora_q4_gemv(const float* d_x, const uint8_t* d_packed,
+                         const uint16_t* d_scales, uint64_t k, uint64_t n, float* d_y,
+                         void* stream);
+
+/* Bit-exact dequantisation of rows [row0, row0+rows) of a Q4 matrix to f32
+ * ((q-8)*f32(scale), src/gemv.rs:727-731). d_out: rows*n floats. */
+qora_status qora_q4_dequant(const uint8_t* d_packed, const uint16_t* d_scales,
+                            uint64_t n, uint64_t row0, uint64_t rows, float* d_out,
+                            void* stream);
+
+/* Fused gate/up: out[n] = silu(x.Wg) * (x.Wu) (replaces `fused_gate_up_q4`,
+ * src/gemv.rs:412-502). */
+qora_status qora_q4_gate_up(const float* d_x, const uint8_t* d_gate_packed,
+                            const uint16_t* d_gate_scales, const uint8_t* d_up_packed,
+                            const uint16_t* d_up_scales, uint64_t k, uint64_t n,
+                            float* d_out, void* stream);
+
+/* Row-dot Q4 lm_head + first-maximum argmax over rows (replaces `lm_head_parallel_q4`,
+ * src/gemv.rs:825-864, and the greedy branch of src/generate.rs:346-352). d_logits may
+ * be NULL; d_argmax receives one uint32. */
+qora_status qora_q4_lm_head(const float* d_x, const uint8_t* d_packed,
+                            const uint16_t* d_scales, uint64_t vocab, uint64_t hidden,
+                            float* d_logits, uint32_t* d_argmax, void* stream);
+
+
+/* ------------------------------------------------------------------------------------
+ * Measurement entry points (no counterpart in the reference, which only times whole
+ * calls with Instant, src/main.rs:105-117 and src/generate.rs:134-139, :255-260).
+ * ---------------------------------------------------------------------------------- */
+
+/* qora_generate_greedy, and *device_ms receives the time of the n_tokens decode steps
+ * measured with CUDA events on the engine's stream. */
+qora_status qora_generate_greedy_timed(qora_engine* engine, qora_kv* kv, uint32_t first_token,
+                                       uint32_t n_tokens, uint32_t* out_tokens,
+                                       float* device_ms);
+
+#define QORA_KERNEL_QKV       0  /* RMSNorm + q|k|v GEMV + RoPE + KV append, per layer */
+#define QORA_KERNEL_ATTENTION 1  /* split-KV decode attention, per layer               */
+#define QORA_KERNEL_O         2  /* o_proj GEMV + residual, per layer                  */
+#define QORA_KERNEL_GATE_UP   3  /* RMSNorm + gate/up GEMV + SwiGLU, per layer         */
+#define QORA_KERNEL_DOWN      4  /* down_proj GEMV + residual, per layer               */
+#define QORA_KERNEL_LM_HEAD   5  /* final RMSNorm + lm_head + argmax                   */
+
+/* Launch one kernel family `reps` times over every layer in order (so consecutive
+ * launches read different weights) between CUDA events on the engine's stream; returns
+ * the mean device time of one launch and the algorithmic bytes one launch moves
+ * (weights + input vector + output vector; for attention the K/V rows read). The KV
+ * state of `kv` (its current length) sets the attention length. */
+qora_status qora_engine_time_kernel(qora_engine* engine, qora_kv* kv, int kernel,
+                                    uint32_t reps, float* ms_per_launch,
+                                    uint64_t* bytes_per_launch, uint32_t* launches);
+
+/* Number of kernel launches one decode step makes (the captured graph's nodes). */
+qora_status qora_engine_launches_per_step(const qora_engine* engine, uint32_t* launches);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QORA_CUDA_H */

@@ -1,0 +1,1217 @@
+// qora_engine.cu — libqora_cuda.so: the C ABI of include/qora_cuda.h over the sm_100a
+// kernels (q4_gemv.cuh, attention.cuh, lm_head.cuh, small_kernels.cuh).
+//
+// Device layout (HBM), per engine:
+//   per layer   q|k|v fused Q4 matrix, o, gate/up fused (interleaved per 128 outputs) and
+//               down, each re-tiled "tile-major": for column tile t (8 groups = 256
+//               outputs) and row r, 144 contiguous bytes = 8 x 16 packed bytes followed
+//               by the 8 f16 scales. A tile is one contiguous stream of K*144 bytes.
+//               Dequantised values are unchanged (same nibbles, same f16 scales).
+//               Norm gains as f32 (exact widening of the f16 values).
+//   embedding   Q4 [vocab][hidden] as in the file (row-dot lm_head + row lookup).
+//   RoPE tables f32 [rows][64] as in the file.
+//   KV cache    per layer f32 [max_seq][kv_heads*128] (token-major like RawKvCache).
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "../../include/qora_cuda.h"
+#include "attention.cuh"
+#include "common.cuh"
+#include "lm_head.cuh"
+#include "q4_gemv.cuh"
+#include "small_kernels.cuh"
+
+using namespace qora;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+qora_status fail(qora_status st, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  std::vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return st;
+}
+
+#define QCUDA(call)                                                                   \
+  do {                                                                                \
+    cudaError_t e_ = (call);                                                          \
+    if (e_ != cudaSuccess)                                                            \
+      return fail(e_ == cudaErrorMemoryAllocation ? QORA_ERR_OOM : QORA_ERR_CUDA,     \
+                  "%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_), __FILE__, __LINE__); \
+  } while (0)
+
+#define QCHECK(expr)                 \
+  do {                               \
+    qora_status s_ = (expr);         \
+    if (s_ != QORA_OK) return s_;    \
+  } while (0)
+
+int sm_count(int dev) {
+  int n = 0;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+// ------------------------------------------------------------------ GEMV planning
+struct GemvShape {
+  int K = 0, tiles = 0;
+  SplitPlan plan{};
+  int seg_cap = 0;  // floats of dynamic shared memory
+};
+
+GemvShape plan_gemv(int K, int tiles, int ctas_wanted) {
+  GemvShape s;
+  s.K = K;
+  s.tiles = tiles;
+  const long long total = (long long)tiles * K;
+  const int ctas = (int)std::min<long long>(ctas_wanted, total);
+  s.plan.ctas = ctas;
+  s.plan.total = total;
+  auto owner = [&](long long p) { return (int)(((p + 1) * (long long)ctas - 1) / total); };
+  int mx = 1;
+  for (int t = 0; t < tiles; ++t)
+    mx = std::max(mx, owner((long long)(t + 1) * K - 1) - owner((long long)t * K) + 1);
+  s.plan.max_slots = mx;
+  s.seg_cap = (int)((total + ctas - 1) / ctas) + 1;
+  return s;
+}
+
+size_t partial_floats(const GemvShape& s) {
+  return (size_t)s.tiles * s.plan.max_slots * kTileCols;
+}
+
+template <class Pro, class Epi>
+qora_status launch_gemv(const Q4Src& src, const GemvShape& sh, float* partials, unsigned* counters,
+                        const Pro& pro, const Epi& epi, cudaStream_t stream) {
+  SplitPlan plan = sh.plan;
+  plan.partials = partials;
+  plan.counters = counters;
+  const size_t smem = (size_t)sh.seg_cap * sizeof(float);
+  auto kern = q4_gemv_kernel<Pro, Epi>;
+  if (smem > 48 * 1024) {
+    if (smem > 200 * 1024) return fail(QORA_ERR_INVALID, "GEMV segment too long (%zu B)", smem);
+    QCUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  }
+  kern<<<plan.ctas, kGemvThreads, smem, stream>>>(src, plan, pro, epi);
+  QCUDA(cudaGetLastError());
+  return QORA_OK;
+}
+
+// ------------------------------------------------------------------ host-side re-tiling
+struct GroupRef {
+  const qora_matrix_view* m;  // nullptr: zero padding
+  int g;
+};
+
+// Tile-major Q4 bytes for fused group list `refs` (all sources share K rows).
+std::vector<uint8_t> build_tiled(int K, const std::vector<GroupRef>& refs) {
+  const int G = (int)refs.size();
+  const int tiles = (G + kTileGroups - 1) / kTileGroups;
+  std::vector<uint8_t> buf((size_t)tiles * K * kTiledRowBytes, 0);
+  for (int r = 0; r < K; ++r) {
+    for (int f = 0; f < tiles * kTileGroups; ++f) {
+      const int t = f / kTileGroups, gi = f % kTileGroups;
+      uint8_t* dst = buf.data() + ((size_t)t * K + r) * kTiledRowBytes;
+      if (f >= G || refs[f].m == nullptr) continue;  // zeros: scale 0 -> contributes 0
+      const qora_matrix_view* m = refs[f].m;
+      const size_t gpr = m->n / kGroup;
+      std::memcpy(dst + gi * 16, m->packed + ((size_t)r * gpr + refs[f].g) * 16, 16);
+      std::memcpy(dst + kTileGroups * 16 + gi * 2, m->scales + (size_t)r * gpr + refs[f].g, 2);
+    }
+  }
+  return buf;
+}
+
+struct DevQ4 {
+  uint8_t* buf = nullptr;
+  int K = 0, G = 0, tiles = 0;
+  Q4Src src() const {
+    Q4Src s{};
+    s.p[0] = s.p[1] = buf;
+    s.s[0] = s.s[1] = buf + kTileGroups * 16;
+    s.tile_stride_p = s.tile_stride_s = (long long)K * kTiledRowBytes;
+    s.row_stride_p = s.row_stride_s = kTiledRowBytes;
+    s.split = 0;
+    s.K = K;
+    s.G = G;
+    s.tiles = tiles;
+    return s;
+  }
+};
+
+// Q4Src over the reference F1 layout (packed [K][n/2], scales [K][n/32]) on the device.
+Q4Src f1_src(const uint8_t* packed, const uint16_t* scales, int K, int n) {
+  Q4Src s{};
+  const int G = n / kGroup;
+  s.p[0] = s.p[1] = packed;
+  s.s[0] = s.s[1] = reinterpret_cast<const uint8_t*>(scales);
+  s.tile_stride_p = kTileGroups * 16;
+  s.tile_stride_s = kTileGroups * 2;
+  s.row_stride_p = (long long)G * 16;
+  s.row_stride_s = (long long)G * 2;
+  s.split = 0;
+  s.K = K;
+  s.G = G;
+  s.tiles = (G + kTileGroups - 1) / kTileGroups;
+  return s;
+}
+
+// gate/up given as two F1 matrices: tile t = gate groups 4t..4t+3 | up groups 4t..4t+3.
+Q4Src f1_pair_src(const uint8_t* gp, const uint16_t* gs, const uint8_t* upk, const uint16_t* us,
+                  int K, int n) {
+  Q4Src s{};
+  const int G = n / kGroup;
+  s.p[0] = gp;
+  s.p[1] = upk;
+  s.s[0] = reinterpret_cast<const uint8_t*>(gs);
+  s.s[1] = reinterpret_cast<const uint8_t*>(us);
+  s.tile_stride_p = (kTileGroups / 2) * 16;
+  s.tile_stride_s = (kTileGroups / 2) * 2;
+  s.row_stride_p = (long long)G * 16;
+  s.row_stride_s = (long long)G * 2;
+  s.split = kTileGroups / 2;
+  s.K = K;
+  s.G = G;
+  s.tiles = (G + kTileGroups / 2 - 1) / (kTileGroups / 2);
+  return s;
+}
+
+std::vector<float> f16_to_f32(const uint16_t* h, size_t n) {
+  std::vector<float> out(n);
+  for (size_t i = 0; i < n; ++i) {
+    __half_raw r;
+    r.x = h[i];
+    out[i] = __half2float(__half(r));
+  }
+  return out;
+}
+
+struct LayerDev {
+  DevQ4 qkv, o, gu, down;
+  float* g_in = nullptr;
+  float* g_post = nullptr;
+  int rope = 0;
+  int nq = 0, nkv = 0;
+};
+
+}  // namespace
+
+// ================================================================== engine / kv objects
+struct qora_engine {
+  int device = 0;
+  int sms = 148;
+  cudaStream_t stream = nullptr;
+  uint32_t format = QORA_FORMAT_Q4;
+  uint32_t num_layers = 0, vocab = 0, hidden = 0, inter = 0;
+  uint32_t nh = 0, nkv = 0, rope_rows = 0;
+  std::vector<LayerDev> layers;
+  uint8_t* embed_packed = nullptr;
+  uint16_t* embed_scales = nullptr;
+  float* final_gamma = nullptr;
+  float* rope_cos = nullptr;
+  float* rope_sin = nullptr;
+  // activations
+  float *x = nullptr, *q = nullptr, *attn = nullptr, *h = nullptr, *logits = nullptr;
+  // GEMV scratch
+  GemvShape sh_qkv, sh_o, sh_gu, sh_down;
+  float* partials = nullptr;
+  unsigned* counters = nullptr;
+  int max_tiles = 0;
+  // lm_head scratch
+  int lm_ctas = 0;
+  float* lm_part_v = nullptr;
+  unsigned* lm_part_i = nullptr;
+  unsigned* lm_counter = nullptr;
+  std::vector<void*> allocs;
+  uint64_t device_bytes = 0;
+
+  template <typename T>
+  qora_status alloc(T** p, size_t count) {
+    void* d = nullptr;
+    const size_t bytes = std::max<size_t>(count * sizeof(T), 16);
+    cudaError_t e = cudaMalloc(&d, bytes);
+    if (e != cudaSuccess)
+      return fail(QORA_ERR_OOM, "cudaMalloc(%zu) failed: %s", bytes, cudaGetErrorString(e));
+    allocs.push_back(d);
+    device_bytes += bytes;
+    *p = static_cast<T*>(d);
+    return QORA_OK;
+  }
+  ~qora_engine() {
+    if (stream) cudaStreamSynchronize(stream);
+    for (void* p : allocs) cudaFree(p);
+    if (stream) cudaStreamDestroy(stream);
+  }
+};
+
+struct qora_kv {
+  qora_engine* e = nullptr;
+  uint32_t max_seq = 0;
+  float* k = nullptr;  // [layers][max_seq][nkv*128]
+  float* v = nullptr;
+  std::vector<uint32_t> len;
+  StepState* st = nullptr;
+  StepState* st_host = nullptr;  // pinned staging
+  unsigned* ring = nullptr;      // greedy output ring [max_seq]
+  uint32_t* ids = nullptr;       // prefill ids [max_seq]
+  int attn_nc = 0;
+  float* attn_o = nullptr;
+  float* attn_ml = nullptr;
+  unsigned* attn_counters = nullptr;
+  cudaGraphExec_t graph = nullptr;
+  std::vector<void*> allocs;
+  ~qora_kv() {
+    if (e) {
+      cudaSetDevice(e->device);
+      cudaStreamSynchronize(e->stream);
+    }
+    if (graph) cudaGraphExecDestroy(graph);
+    for (void* p : allocs) cudaFree(p);
+    if (st_host) cudaFreeHost(st_host);
+  }
+  template <typename T>
+  qora_status alloc(T** p, size_t count) {
+    void* d = nullptr;
+    const size_t bytes = std::max<size_t>(count * sizeof(T), 16);
+    cudaError_t err = cudaMalloc(&d, bytes);
+    if (err != cudaSuccess)
+      return fail(QORA_ERR_OOM, "cudaMalloc(%zu) failed: %s", bytes, cudaGetErrorString(err));
+    allocs.push_back(d);
+    *p = static_cast<T*>(d);
+    return QORA_OK;
+  }
+  size_t layer_stride() const { return (size_t)max_seq * e->nkv * kHeadDim; }
+};
+
+namespace {
+
+qora_status validate_view(const qora_weights_view* w) {
+  if (!w) return fail(QORA_ERR_INVALID, "weights view is NULL");
+  if (w->format == QORA_FORMAT_F16)
+    return fail(QORA_ERR_UNSUPPORTED, "F16 weights are not supported by this build yet");
+  if (w->format != QORA_FORMAT_Q4) return fail(QORA_ERR_INVALID, "unknown format %u", w->format);
+  if (w->num_layers == 0 || !w->layers) return fail(QORA_ERR_INVALID, "no layers");
+  if (w->hidden == 0 || w->hidden % 1024 != 0 || w->hidden > 4096)
+    return fail(QORA_ERR_UNSUPPORTED, "hidden=%u must be a multiple of 1024 up to 4096", w->hidden);
+  if (w->rope_half_dim != kHalfDim)
+    return fail(QORA_ERR_UNSUPPORTED, "rope_half_dim=%u, only 64 supported", w->rope_half_dim);
+  if (w->embed.k != w->vocab || w->embed.n != w->hidden || !w->embed.packed || !w->embed.scales)
+    return fail(QORA_ERR_INVALID, "embedding must be Q4 [vocab][hidden]");
+  if (!w->final_norm_gamma || !w->no_rope_layers || !w->rope_cos || !w->rope_sin)
+    return fail(QORA_ERR_INVALID, "missing final norm / rope tables / no_rope_layers");
+  const qora_layer_view& L0 = w->layers[0];
+  for (uint32_t i = 0; i < w->num_layers; ++i) {
+    const qora_layer_view& L = w->layers[i];
+    if (L.head_dim != kHeadDim) return fail(QORA_ERR_UNSUPPORTED, "layer %u head_dim=%u", i, L.head_dim);
+    if (L.num_kv_heads == 0 || L.num_heads != L.num_kv_heads * kGrp || L.num_kv_groups != kGrp)
+      return fail(QORA_ERR_UNSUPPORTED, "layer %u: heads %u/%u groups %u (need 4 query heads per KV head)",
+                  i, L.num_heads, L.num_kv_heads, L.num_kv_groups);
+    if (L.num_heads != L0.num_heads || L.num_kv_heads != L0.num_kv_heads || L.gate_proj.n != L0.gate_proj.n)
+      return fail(QORA_ERR_UNSUPPORTED, "layer %u geometry differs from layer 0", i);
+    const uint64_t H = w->hidden, nq = (uint64_t)L.num_heads * kHeadDim, nk = (uint64_t)L.num_kv_heads * kHeadDim;
+    const uint64_t I = L.gate_proj.n;
+    struct { const qora_matrix_view* m; uint64_t k, n; const char* name; } want[7] = {
+        {&L.q_proj, H, nq, "q_proj"}, {&L.k_proj, H, nk, "k_proj"}, {&L.v_proj, H, nk, "v_proj"},
+        {&L.o_proj, nq, H, "o_proj"}, {&L.gate_proj, H, I, "gate_proj"}, {&L.up_proj, H, I, "up_proj"},
+        {&L.down_proj, I, H, "down_proj"}};
+    for (auto& wm : want) {
+      if (wm.m->k != wm.k || wm.m->n != wm.n || !wm.m->packed || !wm.m->scales)
+        return fail(QORA_ERR_INVALID, "layer %u %s: shape %llux%llu, expected %llux%llu (Q4)", i, wm.name,
+                    (unsigned long long)wm.m->k, (unsigned long long)wm.m->n,
+                    (unsigned long long)wm.k, (unsigned long long)wm.n);
+    }
+    if (I % 128 != 0 || I == 0) return fail(QORA_ERR_UNSUPPORTED, "intermediate %llu not a multiple of 128", (unsigned long long)I);
+    if (!L.input_norm_gamma || !L.post_attn_norm_gamma) return fail(QORA_ERR_INVALID, "layer %u norms missing", i);
+  }
+  return QORA_OK;
+}
+
+qora_status upload(qora_engine* e, void* dst, const void* src, size_t bytes) {
+  QCUDA(cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice));
+  return QORA_OK;
+}
+
+qora_status upload_q4(qora_engine* e, int K, const std::vector<GroupRef>& refs, DevQ4& out) {
+  out.K = K;
+  out.G = (int)refs.size();
+  out.tiles = (out.G + kTileGroups - 1) / kTileGroups;
+  std::vector<uint8_t> host = build_tiled(K, refs);
+  QCHECK(e->alloc(&out.buf, host.size()));
+  return upload(e, out.buf, host.data(), host.size());
+}
+
+qora_status build_layer(qora_engine* e, const qora_weights_view* w, uint32_t i) {
+  const qora_layer_view& L = w->layers[i];
+  LayerDev& d = e->layers[i];
+  const int H = (int)w->hidden;
+  std::vector<GroupRef> refs;
+  auto add_all = [&](const qora_matrix_view& m) {
+    for (int g = 0; g < (int)(m.n / kGroup); ++g) refs.push_back({&m, g});
+  };
+  refs.clear();
+  add_all(L.q_proj);
+  add_all(L.k_proj);
+  add_all(L.v_proj);
+  QCHECK(upload_q4(e, H, refs, d.qkv));
+  refs.clear();
+  add_all(L.o_proj);
+  QCHECK(upload_q4(e, (int)L.o_proj.k, refs, d.o));
+  refs.clear();
+  const int gI = (int)(L.gate_proj.n / kGroup);
+  for (int t = 0; t < gI / 4; ++t) {
+    for (int j = 0; j < 4; ++j) refs.push_back({&L.gate_proj, 4 * t + j});
+    for (int j = 0; j < 4; ++j) refs.push_back({&L.up_proj, 4 * t + j});
+  }
+  QCHECK(upload_q4(e, H, refs, d.gu));
+  refs.clear();
+  add_all(L.down_proj);
+  QCHECK(upload_q4(e, (int)L.down_proj.k, refs, d.down));
+  std::vector<float> g1 = f16_to_f32(L.input_norm_gamma, H), g2 = f16_to_f32(L.post_attn_norm_gamma, H);
+  QCHECK(e->alloc(&d.g_in, H));
+  QCHECK(e->alloc(&d.g_post, H));
+  QCHECK(upload(e, d.g_in, g1.data(), H * 4));
+  QCHECK(upload(e, d.g_post, g2.data(), H * 4));
+  d.rope = w->no_rope_layers[i] ? 1 : 0;
+  d.nq = (int)(L.num_heads * kHeadDim);
+  d.nkv = (int)(L.num_kv_heads * kHeadDim);
+  return QORA_OK;
+}
+
+qora_status engine_init(qora_engine* e, const qora_weights_view* w) {
+  const qora_layer_view& L0 = w->layers[0];
+  e->format = w->format;
+  e->num_layers = w->num_layers;
+  e->vocab = w->vocab;
+  e->hidden = w->hidden;
+  e->inter = (uint32_t)L0.gate_proj.n;
+  e->nh = L0.num_heads;
+  e->nkv = L0.num_kv_heads;
+  e->rope_rows = (uint32_t)w->rope_rows;
+  e->sms = sm_count(e->device);
+  QCUDA(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
+  e->layers.resize(w->num_layers);
+
+  // layers re-tiled on host worker threads (allocation + upload per layer)
+  {
+    const unsigned nthreads = std::max(1u, std::min(8u, std::thread::hardware_concurrency()));
+    std::vector<qora_status> st(w->num_layers, QORA_OK);
+    std::vector<std::string> errs(w->num_layers);
+    std::mutex alloc_mu;
+    std::vector<std::thread> pool;
+    std::atomic<uint32_t> next{0};
+    for (unsigned t = 0; t < nthreads; ++t) {
+      pool.emplace_back([&] {
+        cudaSetDevice(e->device);
+        for (;;) {
+          const uint32_t i = next.fetch_add(1);
+          if (i >= w->num_layers) break;
+          // allocation bookkeeping is not thread-safe: build into a private engine shell
+          qora_engine tmp;
+          tmp.device = e->device;
+          tmp.layers.resize(w->num_layers);
+          st[i] = build_layer(&tmp, w, i);
+          if (st[i] != QORA_OK) errs[i] = g_last_error;
+          std::lock_guard<std::mutex> lk(alloc_mu);
+          e->layers[i] = tmp.layers[i];
+          e->allocs.insert(e->allocs.end(), tmp.allocs.begin(), tmp.allocs.end());
+          e->device_bytes += tmp.device_bytes;
+          tmp.allocs.clear();
+        }
+      });
+    }
+    for (auto& th : pool) th.join();
+    for (uint32_t i = 0; i < w->num_layers; ++i)
+      if (st[i] != QORA_OK) return fail(st[i], "layer %u: %s", i, errs[i].c_str());
+  }
+
+  const size_t H = w->hidden, V = w->vocab;
+  QCHECK(e->alloc(&e->embed_packed, V * H / 2));
+  QCHECK(e->alloc(&e->embed_scales, V * H / kGroup));
+  QCHECK(upload(e, e->embed_packed, w->embed.packed, V * H / 2));
+  QCHECK(upload(e, e->embed_scales, w->embed.scales, V * H / kGroup * 2));
+  std::vector<float> fg = f16_to_f32(w->final_norm_gamma, H);
+  QCHECK(e->alloc(&e->final_gamma, H));
+  QCHECK(upload(e, e->final_gamma, fg.data(), H * 4));
+  const size_t rt = (size_t)w->rope_rows * kHalfDim;
+  QCHECK(e->alloc(&e->rope_cos, rt));
+  QCHECK(e->alloc(&e->rope_sin, rt));
+  QCHECK(upload(e, e->rope_cos, w->rope_cos, rt * 4));
+  QCHECK(upload(e, e->rope_sin, w->rope_sin, rt * 4));
+
+  const int nq = (int)(e->nh * kHeadDim);
+  QCHECK(e->alloc(&e->x, H));
+  QCHECK(e->alloc(&e->q, nq));
+  QCHECK(e->alloc(&e->attn, nq));
+  QCHECK(e->alloc(&e->h, e->inter));
+  QCHECK(e->alloc(&e->logits, V));
+
+  const int ctas = 2 * e->sms;
+  const LayerDev& d0 = e->layers[0];
+  e->sh_qkv = plan_gemv(d0.qkv.K, d0.qkv.tiles, ctas);
+  e->sh_o = plan_gemv(d0.o.K, d0.o.tiles, ctas);
+  e->sh_gu = plan_gemv(d0.gu.K, d0.gu.tiles, ctas);
+  e->sh_down = plan_gemv(d0.down.K, d0.down.tiles, ctas);
+  size_t pf = 0;
+  for (const GemvShape* s : {&e->sh_qkv, &e->sh_o, &e->sh_gu, &e->sh_down}) {
+    pf = std::max(pf, partial_floats(*s));
+    e->max_tiles = std::max(e->max_tiles, s->tiles);
+  }
+  QCHECK(e->alloc(&e->partials, pf));
+  QCHECK(e->alloc(&e->counters, e->max_tiles));
+  QCUDA(cudaMemset(e->counters, 0, e->max_tiles * sizeof(unsigned)));
+
+  e->lm_ctas = 2 * e->sms;
+  QCHECK(e->alloc(&e->lm_part_v, e->lm_ctas));
+  QCHECK(e->alloc(&e->lm_part_i, e->lm_ctas));
+  QCHECK(e->alloc(&e->lm_counter, 1));
+  QCUDA(cudaMemset(e->lm_counter, 0, sizeof(unsigned)));
+  QCUDA(cudaDeviceSynchronize());
+  return QORA_OK;
+}
+
+// ------------------------------------------------------------------ step launches
+qora_status launch_lm_head(int hidden, const LmArgs& a, int ctas, cudaStream_t s) {
+  switch (hidden) {
+    case 1024: lm_head_kernel<1><<<ctas, kLmThreads, 0, s>>>(a); break;
+    case 2048: lm_head_kernel<2><<<ctas, kLmThreads, 0, s>>>(a); break;
+    case 3072: lm_head_kernel<3><<<ctas, kLmThreads, 0, s>>>(a); break;
+    case 4096: lm_head_kernel<4><<<ctas, kLmThreads, 0, s>>>(a); break;
+    default: return fail(QORA_ERR_UNSUPPORTED, "lm_head: hidden %d", hidden);
+  }
+  QCUDA(cudaGetLastError());
+  return QORA_OK;
+}
+
+qora_status launch_layer(qora_engine* e, qora_kv* kv, uint32_t li) {
+  const LayerDev& d = e->layers[li];
+  cudaStream_t s = e->stream;
+  float* kc = kv->k + li * kv->layer_stride();
+  float* vc = kv->v + li * kv->layer_stride();
+  EpiQKV eq{e->q, kc, vc, kv->st, e->rope_cos, e->rope_sin, d.nq, d.nkv, d.rope,
+            (int)std::min<uint32_t>(kv->max_seq, d.rope ? e->rope_rows : kv->max_seq)};
+  QCHECK(launch_gemv(d.qkv.src(), e->sh_qkv, e->partials, e->counters,
+                     ProNorm{e->x, d.g_in, (int)e->hidden}, eq, s));
+  AttnArgs aa{};
+  aa.q = e->q;
+  aa.kc = kc;
+  aa.vc = vc;
+  aa.out = e->attn;
+  aa.st = kv->st;
+  aa.nkv = (int)e->nkv;
+  aa.nc = kv->attn_nc;
+  aa.scale = 1.0f / std::sqrt((float)kHeadDim);
+  aa.part_o = kv->attn_o;
+  aa.part_ml = kv->attn_ml;
+  aa.counters = kv->attn_counters;
+  attn_decode_kernel<<<dim3(e->nkv, kv->attn_nc), kAttnThreads, 0, s>>>(aa);
+  QCUDA(cudaGetLastError());
+  QCHECK(launch_gemv(d.o.src(), e->sh_o, e->partials, e->counters, ProPlain{e->attn},
+                     EpiResidual{e->x, (int)e->hidden}, s));
+  QCHECK(launch_gemv(d.gu.src(), e->sh_gu, e->partials, e->counters,
+                     ProNorm{e->x, d.g_post, (int)e->hidden}, EpiSwiGLU{e->h, (int)e->inter}, s));
+  QCHECK(launch_gemv(d.down.src(), e->sh_down, e->partials, e->counters, ProPlain{e->h},
+                     EpiResidual{e->x, (int)e->hidden}, s));
+  return QORA_OK;
+}
+
+// the whole decode step (what the CUDA graph holds)
+qora_status launch_step(qora_engine* e, qora_kv* kv, int* launches) {
+  cudaStream_t s = e->stream;
+  embed_q4_kernel<<<1, 256, 0, s>>>(e->embed_packed, e->embed_scales, (int)e->vocab,
+                                    (int)e->hidden, kv->st, e->x);
+  QCUDA(cudaGetLastError());
+  int n = 1;
+  for (uint32_t li = 0; li < e->num_layers; ++li) {
+    QCHECK(launch_layer(e, kv, li));
+    n += 5;
+  }
+  LmArgs la{};
+  la.x = e->x;
+  la.gamma = e->final_gamma;
+  la.packed = e->embed_packed;
+  la.scales = e->embed_scales;
+  la.vocab = (int)e->vocab;
+  la.logits = e->logits;
+  la.argmax_out = &kv->st->argmax;
+  la.part_v = e->lm_part_v;
+  la.part_i = e->lm_part_i;
+  la.counter = e->lm_counter;
+  QCHECK(launch_lm_head((int)e->hidden, la, e->lm_ctas, s));
+  advance_kernel<<<1, 1, 0, s>>>(kv->st, kv->ring, (int)kv->max_seq);
+  QCUDA(cudaGetLastError());
+  n += 2;
+  if (launches) *launches = n;
+  return QORA_OK;
+}
+
+qora_status ensure_graph(qora_engine* e, qora_kv* kv) {
+  if (kv->graph) return QORA_OK;
+  cudaGraph_t g = nullptr;
+  QCUDA(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+  qora_status st = launch_step(e, kv, nullptr);
+  cudaError_t ce = cudaStreamEndCapture(e->stream, &g);
+  if (st != QORA_OK) {
+    if (g) cudaGraphDestroy(g);
+    return st;
+  }
+  if (ce != cudaSuccess) return fail(QORA_ERR_CUDA, "graph capture: %s", cudaGetErrorString(ce));
+  ce = cudaGraphInstantiate(&kv->graph, g, 0);
+  cudaGraphDestroy(g);
+  if (ce != cudaSuccess) return fail(QORA_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(ce));
+  return QORA_OK;
+}
+
+qora_status check_uniform_len(const qora_kv* kv, uint32_t* len) {
+  const uint32_t l = kv->len[0];
+  for (uint32_t x : kv->len)
+    if (x != l) return fail(QORA_ERR_INVALID, "KV layers have different lengths (layer_step use?)");
+  *len = l;
+  return QORA_OK;
+}
+
+qora_status set_state(qora_engine* e, qora_kv* kv, int pos, int token, int step) {
+  kv->st_host->pos = pos;
+  kv->st_host->token = token;
+  kv->st_host->argmax = 0;
+  kv->st_host->step = step;
+  kv->st_host->error = 0;
+  QCUDA(cudaMemcpyAsync(kv->st, kv->st_host, sizeof(StepState), cudaMemcpyHostToDevice, e->stream));
+  return QORA_OK;
+}
+
+qora_status check_step_error(qora_engine* e, qora_kv* kv) {
+  QCUDA(cudaMemcpyAsync(kv->st_host, kv->st, sizeof(StepState), cudaMemcpyDeviceToHost, e->stream));
+  QCUDA(cudaStreamSynchronize(e->stream));
+  if (kv->st_host->error) return fail(QORA_ERR_RANGE, "device rejected a token id");
+  return QORA_OK;
+}
+
+struct EntryScratch {
+  float* partials = nullptr;
+  size_t partial_floats = 0;
+  unsigned* counters = nullptr;
+  size_t ncounters = 0;
+  float* lm_v = nullptr;
+  unsigned* lm_i = nullptr;
+  unsigned* lm_c = nullptr;
+  int lm_n = 0;
+};
+std::mutex g_entry_mu;
+std::map<int, EntryScratch> g_entry;
+
+qora_status entry_scratch(int dev, size_t pf, size_t nc, int lm_n, EntryScratch** out) {
+  EntryScratch& s = g_entry[dev];
+  if (s.partial_floats < pf) {
+    if (s.partials) cudaFree(s.partials);
+    s.partials = nullptr;
+    QCUDA(cudaMalloc(&s.partials, pf * sizeof(float)));
+    s.partial_floats = pf;
+  }
+  if (s.ncounters < nc) {
+    if (s.counters) cudaFree(s.counters);
+    s.counters = nullptr;
+    QCUDA(cudaMalloc(&s.counters, nc * sizeof(unsigned)));
+    QCUDA(cudaMemset(s.counters, 0, nc * sizeof(unsigned)));
+    s.ncounters = nc;
+  }
+  if (s.lm_n < lm_n) {
+    if (s.lm_v) cudaFree(s.lm_v);
+    if (s.lm_i) cudaFree(s.lm_i);
+    if (s.lm_c) cudaFree(s.lm_c);
+    s.lm_v = nullptr;
+    s.lm_i = nullptr;
+    s.lm_c = nullptr;
+    QCUDA(cudaMalloc(&s.lm_v, lm_n * sizeof(float)));
+    QCUDA(cudaMalloc(&s.lm_i, lm_n * sizeof(unsigned)));
+    QCUDA(cudaMalloc(&s.lm_c, sizeof(unsigned)));
+    QCUDA(cudaMemset(s.lm_c, 0, sizeof(unsigned)));
+    s.lm_n = lm_n;
+  }
+  *out = &s;
+  return QORA_OK;
+}
+
+
+// ------------------------------------------------------------------ .qora reader
+// load_model (src/save.rs:154-210) into host vectors, then the borrowed view.
+struct FileMat {
+  uint64_t k = 0, n = 0;
+  std::vector<uint8_t> packed;
+  std::vector<uint16_t> scales, data;
+};
+struct FileModel {
+  uint8_t format = 0;
+  uint32_t num_layers = 0, vocab = 0, hidden = 0, half = 0;
+  std::vector<uint8_t> no_rope;
+  struct Layer {
+    FileMat m[7];
+    std::vector<uint16_t> g1, g2;
+    uint32_t nh = 0, nkv = 0, hd = 0, grp = 0;
+  };
+  std::vector<Layer> layers;
+  FileMat embed;
+  std::vector<uint16_t> final_norm;
+  std::vector<float> cos_t, sin_t;
+};
+
+struct FileReader {
+  FILE* f = nullptr;
+  std::string err;
+  bool ok = true;
+  void need(void* dst, size_t n) {
+    if (ok && n && std::fread(dst, 1, n, f) != n) { ok = false; err = "short read"; }
+  }
+  uint32_t u32() { uint32_t v = 0; need(&v, 4); return v; }
+  uint64_t u64() { uint64_t v = 0; need(&v, 8); return v; }
+  uint8_t u8() { uint8_t v = 0; need(&v, 1); return v; }
+  template <typename T> void vec(std::vector<T>& out) {
+    const uint64_t len = u64();
+    if (!ok) return;
+    if (len > (1ull << 36)) { ok = false; err = "implausible vector length"; return; }
+    out.resize(len);
+    need(out.data(), len * sizeof(T));
+  }
+  void mat(uint8_t fmt, FileMat& m) {
+    m.k = u64();
+    m.n = u64();
+    if (fmt == 1) {
+      vec(m.packed);
+      vec(m.scales);
+      if (ok && (m.n % kGroup || m.packed.size() != m.k * m.n / 2 || m.scales.size() != m.k * m.n / kGroup)) {
+        ok = false;
+        err = "q4 weight size mismatch";
+      }
+    } else if (fmt == 0) {
+      vec(m.data);
+      if (ok && m.data.size() != m.k * m.n) { ok = false; err = "f16 weight size mismatch"; }
+    } else {
+      ok = false;
+      err = "Unknown format id " + std::to_string(fmt);
+    }
+  }
+};
+
+qora_status read_qora_file(const char* path, FileModel& fm) {
+  FileReader r;
+  r.f = std::fopen(path, "rb");
+  if (!r.f) return fail(QORA_ERR_IO, "cannot open %s", path);
+  std::setvbuf(r.f, nullptr, _IOFBF, 8 << 20);
+  char magic[4] = {0, 0, 0, 0};
+  r.need(magic, 4);
+  if (r.ok && std::memcmp(magic, "QOR3", 4) != 0) { r.ok = false; r.err = "Invalid magic bytes"; }
+  const uint32_t version = r.u32();
+  if (r.ok && version != 1) { r.ok = false; r.err = "Unsupported version " + std::to_string(version) + ", expected 1"; }
+  fm.format = r.u8();
+  fm.num_layers = r.u32();
+  fm.vocab = r.u32();
+  fm.hidden = r.u32();
+  fm.half = r.u32();
+  r.vec(fm.no_rope);
+  if (r.ok && fm.num_layers > 4096) { r.ok = false; r.err = "implausible layer count"; }
+  if (r.ok) fm.layers.resize(fm.num_layers);
+  for (uint32_t i = 0; r.ok && i < fm.num_layers; ++i) {
+    auto& L = fm.layers[i];
+    for (int w = 0; w < 7 && r.ok; ++w) r.mat(fm.format, L.m[w]);
+    r.vec(L.g1);
+    r.vec(L.g2);
+    L.nh = r.u32();
+    L.nkv = r.u32();
+    L.hd = r.u32();
+    L.grp = r.u32();
+  }
+  if (r.ok) r.mat(fm.format, fm.embed);
+  r.vec(fm.final_norm);
+  r.vec(fm.cos_t);
+  r.vec(fm.sin_t);
+  const bool io_short = !r.ok && r.err == "short read";
+  std::fclose(r.f);
+  if (!r.ok) return fail(io_short ? QORA_ERR_IO : QORA_ERR_INVALID, "%s: %s", path, r.err.c_str());
+  if (fm.no_rope.size() != fm.num_layers) return fail(QORA_ERR_INVALID, "no_rope_layers length != num_layers");
+  for (uint32_t i = 0; i < fm.num_layers; ++i) {
+    if (fm.layers[i].g1.size() != fm.hidden || fm.layers[i].g2.size() != fm.hidden)
+      return fail(QORA_ERR_INVALID, "layer %u norm length != hidden", i);
+  }
+  if (fm.final_norm.size() != fm.hidden) return fail(QORA_ERR_INVALID, "final norm length != hidden");
+  if (fm.cos_t.size() != fm.sin_t.size() || fm.half == 0 || fm.cos_t.size() % fm.half)
+    return fail(QORA_ERR_INVALID, "RoPE tables malformed");
+  return QORA_OK;
+}
+
+qora_matrix_view mview(const FileMat& m) {
+  qora_matrix_view v{};
+  v.packed = m.packed.empty() ? nullptr : m.packed.data();
+  v.scales = m.scales.empty() ? nullptr : m.scales.data();
+  v.data = m.data.empty() ? nullptr : m.data.data();
+  v.k = m.k;
+  v.n = m.n;
+  return v;
+}
+
+}  // namespace
+
+// ================================================================== C ABI
+extern "C" {
+
+const char* qora_last_error(void) { return g_last_error.c_str(); }
+
+const char* qora_version(void) { return "qora-b200 0.1.0 (sm_100a)"; }
+
+qora_status qora_engine_create(const qora_weights_view* weights, const qora_engine_options* opts,
+                               qora_engine** out) {
+  if (!out) return fail(QORA_ERR_INVALID, "out is NULL");
+  *out = nullptr;
+  QCHECK(validate_view(weights));
+  const int n_gpus = opts ? opts->n_gpus : 1;
+  if (n_gpus > 1)
+    return fail(QORA_ERR_UNSUPPORTED, "tensor-parallel engines (n_gpus=%d) are not in this build", n_gpus);
+  if (opts && opts->flags != 0) return fail(QORA_ERR_INVALID, "options.flags must be 0");
+  int ndev = 0;
+  QCUDA(cudaGetDeviceCount(&ndev));
+  const int dev = opts ? opts->first_device : 0;
+  if (dev < 0 || dev >= ndev) return fail(QORA_ERR_INVALID, "device %d out of range (%d devices)", dev, ndev);
+  QCUDA(cudaSetDevice(dev));
+  std::unique_ptr<qora_engine> e(new qora_engine());
+  e->device = dev;
+  QCHECK(engine_init(e.get(), weights));
+  *out = e.release();
+  return QORA_OK;
+}
+
+qora_status qora_engine_create_from_file(const char* qora_path, const qora_engine_options* opts,
+                                         qora_engine** out) {
+  if (!qora_path || !out) return fail(QORA_ERR_INVALID, "NULL argument");
+  *out = nullptr;
+  FileModel fm;
+  QCHECK(read_qora_file(qora_path, fm));
+  std::vector<qora_layer_view> lv(fm.num_layers);
+  for (uint32_t i = 0; i < fm.num_layers; ++i) {
+    auto& L = fm.layers[i];
+    qora_layer_view& v = lv[i];
+    v.q_proj = mview(L.m[0]);
+    v.k_proj = mview(L.m[1]);
+    v.v_proj = mview(L.m[2]);
+    v.o_proj = mview(L.m[3]);
+    v.gate_proj = mview(L.m[4]);
+    v.up_proj = mview(L.m[5]);
+    v.down_proj = mview(L.m[6]);
+    v.input_norm_gamma = L.g1.data();
+    v.post_attn_norm_gamma = L.g2.data();
+    v.num_heads = L.nh;
+    v.num_kv_heads = L.nkv;
+    v.head_dim = L.hd;
+    v.num_kv_groups = L.grp;
+  }
+  qora_weights_view w{};
+  w.format = fm.format;
+  w.num_layers = fm.num_layers;
+  w.vocab = fm.vocab;
+  w.hidden = fm.hidden;
+  w.rope_half_dim = fm.half;
+  w.no_rope_layers = fm.no_rope.data();
+  w.layers = lv.data();
+  w.embed = mview(fm.embed);
+  w.final_norm_gamma = fm.final_norm.data();
+  w.rope_cos = fm.cos_t.data();
+  w.rope_sin = fm.sin_t.data();
+  w.rope_rows = fm.cos_t.size() / fm.half;
+  return qora_engine_create(&w, opts, out);
+}
+
+void qora_engine_destroy(qora_engine* engine) {
+  if (!engine) return;
+  cudaSetDevice(engine->device);
+  delete engine;
+}
+
+qora_status qora_engine_info(const qora_engine* e, uint32_t* num_layers, uint32_t* vocab,
+                             uint32_t* hidden, uint32_t* format, uint64_t* device_bytes) {
+  if (!e) return fail(QORA_ERR_INVALID, "engine is NULL");
+  if (num_layers) *num_layers = e->num_layers;
+  if (vocab) *vocab = e->vocab;
+  if (hidden) *hidden = e->hidden;
+  if (format) *format = e->format;
+  if (device_bytes) *device_bytes = e->device_bytes;
+  return QORA_OK;
+}
+
+qora_status qora_kv_create(qora_engine* e, uint32_t max_seq, uint32_t batch, qora_kv** out) {
+  if (!e || !out) return fail(QORA_ERR_INVALID, "NULL argument");
+  *out = nullptr;
+  if (batch != 1) return fail(QORA_ERR_UNSUPPORTED, "batch=%u: only batch 1 in this build", batch);
+  if (max_seq == 0) return fail(QORA_ERR_INVALID, "max_seq must be > 0");
+  bool any_rope = false;
+  for (auto& L : e->layers) any_rope |= (L.rope != 0);
+  if (any_rope && max_seq > e->rope_rows)
+    return fail(QORA_ERR_RANGE, "max_seq %u exceeds the %u RoPE table rows", max_seq, e->rope_rows);
+  QCUDA(cudaSetDevice(e->device));
+  std::unique_ptr<qora_kv> kv(new qora_kv());
+  kv->e = e;
+  kv->max_seq = max_seq;
+  kv->len.assign(e->num_layers, 0);
+  const size_t per = kv->layer_stride() * e->num_layers;
+  QCHECK(kv->alloc(&kv->k, per));
+  QCHECK(kv->alloc(&kv->v, per));
+  QCHECK(kv->alloc(&kv->st, 1));
+  QCHECK(kv->alloc(&kv->ring, max_seq));
+  QCHECK(kv->alloc(&kv->ids, max_seq));
+  QCUDA(cudaMallocHost(&kv->st_host, sizeof(StepState)));
+  kv->attn_nc = std::max<int>(std::max(1, e->sms / (int)e->nkv), (int)((max_seq + kAttnMaxChunk - 1) / kAttnMaxChunk));
+  QCHECK(kv->alloc(&kv->attn_o, (size_t)e->nkv * kv->attn_nc * kGrp * kHeadDim));
+  QCHECK(kv->alloc(&kv->attn_ml, (size_t)e->nkv * kv->attn_nc * kGrp * 2));
+  QCHECK(kv->alloc(&kv->attn_counters, e->nkv));
+  QCUDA(cudaMemset(kv->attn_counters, 0, e->nkv * sizeof(unsigned)));
+  QCUDA(cudaMemset(kv->st, 0, sizeof(StepState)));
+  QCUDA(cudaDeviceSynchronize());
+  *out = kv.release();
+  return QORA_OK;
+}
+
+void qora_kv_destroy(qora_kv* kv) { delete kv; }
+
+qora_status qora_kv_length(const qora_kv* kv, uint32_t seq_idx, uint32_t* len) {
+  if (!kv || !len) return fail(QORA_ERR_INVALID, "NULL argument");
+  if (seq_idx != 0) return fail(QORA_ERR_RANGE, "seq_idx %u", seq_idx);
+  *len = kv->len[0];
+  return QORA_OK;
+}
+
+qora_status qora_kv_reset(qora_kv* kv, uint32_t seq_idx) {
+  if (!kv) return fail(QORA_ERR_INVALID, "NULL kv");
+  if (seq_idx != 0) return fail(QORA_ERR_RANGE, "seq_idx %u", seq_idx);
+  std::fill(kv->len.begin(), kv->len.end(), 0u);
+  return QORA_OK;
+}
+
+qora_status qora_kv_import(qora_kv* kv, uint32_t layer, const float* k, const float* v,
+                           uint32_t seq_len, uint32_t seq_idx) {
+  if (!kv || (!k && seq_len) || (!v && seq_len)) return fail(QORA_ERR_INVALID, "NULL argument");
+  if (seq_idx != 0) return fail(QORA_ERR_RANGE, "seq_idx %u", seq_idx);
+  if (layer >= kv->e->num_layers) return fail(QORA_ERR_RANGE, "layer %u", layer);
+  if (seq_len > kv->max_seq) return fail(QORA_ERR_RANGE, "seq_len %u > max_seq %u", seq_len, kv->max_seq);
+  QCUDA(cudaSetDevice(kv->e->device));
+  const size_t bytes = (size_t)seq_len * kv->e->nkv * kHeadDim * sizeof(float);
+  if (bytes) {
+    QCUDA(cudaMemcpy(kv->k + layer * kv->layer_stride(), k, bytes, cudaMemcpyHostToDevice));
+    QCUDA(cudaMemcpy(kv->v + layer * kv->layer_stride(), v, bytes, cudaMemcpyHostToDevice));
+  }
+  kv->len[layer] = seq_len;
+  return QORA_OK;
+}
+
+qora_status qora_kv_export(const qora_kv* kv, uint32_t layer, float* k, float* v, uint32_t seq_len,
+                           uint32_t seq_idx) {
+  if (!kv || !k || !v) return fail(QORA_ERR_INVALID, "NULL argument");
+  if (seq_idx != 0) return fail(QORA_ERR_RANGE, "seq_idx %u", seq_idx);
+  if (layer >= kv->e->num_layers) return fail(QORA_ERR_RANGE, "layer %u", layer);
+  if (seq_len > kv->len[layer]) return fail(QORA_ERR_RANGE, "seq_len %u > length %u", seq_len, kv->len[layer]);
+  QCUDA(cudaSetDevice(kv->e->device));
+  QCUDA(cudaStreamSynchronize(kv->e->stream));
+  const size_t bytes = (size_t)seq_len * kv->e->nkv * kHeadDim * sizeof(float);
+  QCUDA(cudaMemcpy(k, kv->k + layer * kv->layer_stride(), bytes, cudaMemcpyDeviceToHost));
+  QCUDA(cudaMemcpy(v, kv->v + layer * kv->layer_stride(), bytes, cudaMemcpyDeviceToHost));
+  return QORA_OK;
+}
+
+qora_status qora_decode_step(qora_engine* e, qora_kv* kv, const uint32_t* tokens,
+                             float* logits_or_null, uint32_t* argmax_out) {
+  if (!e || !kv || !tokens || kv->e != e) return fail(QORA_ERR_INVALID, "bad engine/kv/tokens");
+  if (tokens[0] >= e->vocab) return fail(QORA_ERR_RANGE, "token %u >= vocab %u", tokens[0], e->vocab);
+  uint32_t len = 0;
+  QCHECK(check_uniform_len(kv, &len));
+  if (len >= kv->max_seq) return fail(QORA_ERR_RANGE, "KV cache full (%u positions)", kv->max_seq);
+  QCUDA(cudaSetDevice(e->device));
+  QCHECK(ensure_graph(e, kv));
+  QCHECK(set_state(e, kv, (int)len, (int)tokens[0], 0));
+  QCUDA(cudaGraphLaunch(kv->graph, e->stream));
+  QCUDA(cudaMemcpyAsync(kv->st_host, kv->st, sizeof(StepState), cudaMemcpyDeviceToHost, e->stream));
+  if (logits_or_null)
+    QCUDA(cudaMemcpyAsync(logits_or_null, e->logits, (size_t)e->vocab * 4, cudaMemcpyDeviceToHost, e->stream));
+  QCUDA(cudaStreamSynchronize(e->stream));
+  if (kv->st_host->error) return fail(QORA_ERR_RANGE, "device rejected token id");
+  if (argmax_out) argmax_out[0] = kv->st_host->argmax;
+  for (auto& l : kv->len) l = len + 1;
+  return QORA_OK;
+}
+
+qora_status qora_prefill(qora_engine* e, qora_kv* kv, const uint32_t* ids, uint32_t n,
+                         uint32_t seq_idx, float* logits_or_null, uint32_t* argmax_out) {
+  if (!e || !kv || kv->e != e || (!ids && n)) return fail(QORA_ERR_INVALID, "bad arguments");
+  if (seq_idx != 0) return fail(QORA_ERR_RANGE, "seq_idx %u", seq_idx);
+  if (n == 0) return fail(QORA_ERR_INVALID, "empty prompt");
+  for (uint32_t i = 0; i < n; ++i)
+    if (ids[i] >= e->vocab) return fail(QORA_ERR_RANGE, "token %u at %u >= vocab %u", ids[i], i, e->vocab);
+  uint32_t len = 0;
+  QCHECK(check_uniform_len(kv, &len));
+  if ((uint64_t)len + n > kv->max_seq)
+    return fail(QORA_ERR_RANGE, "prompt of %u after %u positions exceeds max_seq %u", n, len, kv->max_seq);
+  QCUDA(cudaSetDevice(e->device));
+  QCHECK(ensure_graph(e, kv));
+  QCUDA(cudaMemcpyAsync(kv->ids, ids, (size_t)n * 4, cudaMemcpyHostToDevice, e->stream));
+  QCHECK(set_state(e, kv, (int)len, (int)ids[0], 0));
+  for (uint32_t i = 0; i < n; ++i) {
+    QCUDA(cudaMemcpyAsync(&kv->st->token, kv->ids + i, 4, cudaMemcpyDeviceToDevice, e->stream));
+    QCUDA(cudaGraphLaunch(kv->graph, e->stream));
+  }
+  QCUDA(cudaMemcpyAsync(kv->st_host, kv->st, sizeof(StepState), cudaMemcpyDeviceToHost, e->stream));
+  if (logits_or_null)
+    QCUDA(cudaMemcpyAsync(logits_or_null, e->logits, (size_t)e->vocab * 4, cudaMemcpyDeviceToHost, e->stream));
+  QCUDA(cudaStreamSynchronize(e->stream));
+  if (kv->st_host->error) return fail(QORA_ERR_RANGE, "device rejected token id");
+  if (argmax_out) *argmax_out = kv->st_host->argmax;
+  for (auto& l : kv->len) l = len + n;
+  return QORA_OK;
+}
+
+qora_status qora_generate_greedy(qora_engine* e, qora_kv* kv, uint32_t first_token,
+                                 uint32_t n_tokens, uint32_t* out_tokens) {
+  if (!e || !kv || kv->e != e || (!out_tokens && n_tokens)) return fail(QORA_ERR_INVALID, "bad arguments");
+  if (first_token >= e->vocab) return fail(QORA_ERR_RANGE, "token %u >= vocab", first_token);
+  uint32_t len = 0;
+  QCHECK(check_uniform_len(kv, &len));
+  if ((uint64_t)len + n_tokens > kv->max_seq)
+    return fail(QORA_ERR_RANGE, "%u tokens after %u positions exceed max_seq %u", n_tokens, len, kv->max_seq);
+  if (n_tokens == 0) return QORA_OK;
+  QCUDA(cudaSetDevice(e->device));
+  QCHECK(ensure_graph(e, kv));
+  QCHECK(set_state(e, kv, (int)len, (int)first_token, 0));
+  for (uint32_t i = 0; i < n_tokens; ++i) QCUDA(cudaGraphLaunch(kv->graph, e->stream));
+  QCUDA(cudaMemcpyAsync(out_tokens, kv->ring, (size_t)n_tokens * 4, cudaMemcpyDeviceToHost, e->stream));
+  QCHECK(check_step_error(e, kv));
+  for (auto& l : kv->len) l = len + n_tokens;
+  return QORA_OK;
+}
+
+qora_status qora_layer_step(qora_engine* e, qora_kv* kv, uint32_t layer, float* x_inout) {
+  if (!e || !kv || kv->e != e || !x_inout) return fail(QORA_ERR_INVALID, "bad arguments");
+  if (layer >= e->num_layers) return fail(QORA_ERR_RANGE, "layer %u", layer);
+  const uint32_t len = kv->len[layer];
+  if (len >= kv->max_seq) return fail(QORA_ERR_RANGE, "KV cache full");
+  QCUDA(cudaSetDevice(e->device));
+  QCUDA(cudaMemcpyAsync(e->x, x_inout, (size_t)e->hidden * 4, cudaMemcpyHostToDevice, e->stream));
+  QCHECK(set_state(e, kv, (int)len, 0, 0));
+  QCHECK(launch_layer(e, kv, layer));
+  QCUDA(cudaMemcpyAsync(x_inout, e->x, (size_t)e->hidden * 4, cudaMemcpyDeviceToHost, e->stream));
+  QCUDA(cudaStreamSynchronize(e->stream));
+  kv->len[layer] = len + 1;
+  return QORA_OK;
+}
+
+qora_status qora_generate_greedy_timed(qora_engine* e, qora_kv* kv, uint32_t first_token,
+                                       uint32_t n_tokens, uint32_t* out_tokens, float* device_ms) {
+  if (!e || !kv || kv->e != e || (!out_tokens && n_tokens) || !device_ms)
+    return fail(QORA_ERR_INVALID, "bad arguments");
+  if (first_token >= e->vocab) return fail(QORA_ERR_RANGE, "token %u >= vocab", first_token);
+  uint32_t len = 0;
+  QCHECK(check_uniform_len(kv, &len));
+  if ((uint64_t)len + n_tokens > kv->max_seq)
+    return fail(QORA_ERR_RANGE, "%u tokens after %u positions exceed max_seq %u", n_tokens, len, kv->max_seq);
+  QCUDA(cudaSetDevice(e->device));
+  QCHECK(ensure_graph(e, kv));
+  QCHECK(set_state(e, kv, (int)len, (int)first_token, 0));
+  cudaEvent_t a = nullptr, b = nullptr;
+  QCUDA(cudaEventCreate(&a));
+  QCUDA(cudaEventCreate(&b));
+  cudaEventRecord(a, e->stream);
+  for (uint32_t i = 0; i < n_tokens; ++i) {
+    cudaError_t ce = cudaGraphLaunch(kv->graph, e->stream);
+    if (ce != cudaSuccess) {
+      cudaEventDestroy(a);
+      cudaEventDestroy(b);
+      return fail(QORA_ERR_CUDA, "cudaGraphLaunch: %s", cudaGetErrorString(ce));
+    }
+  }
+  cudaEventRecord(b, e->stream);
+  cudaError_t ce = cudaEventSynchronize(b);
+  float ms = 0.0f;
+  if (ce == cudaSuccess) ce = cudaEventElapsedTime(&ms, a, b);
+  cudaEventDestroy(a);
+  cudaEventDestroy(b);
+  if (ce != cudaSuccess) return fail(QORA_ERR_CUDA, "event timing: %s", cudaGetErrorString(ce));
+  *device_ms = ms;
+  if (n_tokens)
+    QCUDA(cudaMemcpyAsync(out_tokens, kv->ring, (size_t)n_tokens * 4, cudaMemcpyDeviceToHost, e->stream));
+  QCHECK(check_step_error(e, kv));
+  for (auto& l : kv->len) l = len + n_tokens;
+  return QORA_OK;
+}
+
+qora_status qora_engine_time_kernel(qora_engine* e, qora_kv* kv, int kernel, uint32_t reps,
+                                    float* ms_per_launch, uint64_t* bytes_per_launch,
+                                    uint32_t* launches) {
+  if (!e || !kv || kv->e != e || !ms_per_launch || reps == 0) return fail(QORA_ERR_INVALID, "bad arguments");
+  if (kernel < QORA_KERNEL_QKV || kernel > QORA_KERNEL_LM_HEAD) return fail(QORA_ERR_INVALID, "kernel %d", kernel);
+  uint32_t len = 0;
+  QCHECK(check_uniform_len(kv, &len));
+  if (len >= kv->max_seq) return fail(QORA_ERR_RANGE, "KV cache full");
+  QCUDA(cudaSetDevice(e->device));
+  QCHECK(set_state(e, kv, (int)len, 0, 0));
+  const uint64_t H = e->hidden, I = e->inter, nq = (uint64_t)e->nh * kHeadDim, nk = (uint64_t)e->nkv * kHeadDim;
+  auto q4b = [](uint64_t k, uint64_t n) { return k * n / 2 + k * n / kGroup * 2; };
+  uint64_t bytes = 0;
+  switch (kernel) {
+    case QORA_KERNEL_QKV: bytes = q4b(H, nq + 2 * nk) + 2 * H * 4 + (nq + 2 * nk) * 4; break;
+    case QORA_KERNEL_ATTENTION: bytes = (uint64_t)(len + 1) * 2 * nk * 4 + 2 * nq * 4; break;
+    case QORA_KERNEL_O: bytes = q4b(nq, H) + nq * 4 + 2 * H * 4; break;
+    case QORA_KERNEL_GATE_UP: bytes = 2 * q4b(H, I) + 2 * H * 4 + I * 4; break;
+    case QORA_KERNEL_DOWN: bytes = q4b(I, H) + I * 4 + 2 * H * 4; break;
+    case QORA_KERNEL_LM_HEAD: bytes = q4b(e->vocab, H) + 2 * H * 4 + (uint64_t)e->vocab * 4; break;
+  }
+  auto run_once = [&](uint32_t li) -> qora_status {
+    const LayerDev& d = e->layers[li];
+    cudaStream_t s = e->stream;
+    float* kc = kv->k + li * kv->layer_stride();
+    float* vc = kv->v + li * kv->layer_stride();
+    switch (kernel) {
+      case QORA_KERNEL_QKV: {
+        EpiQKV eq{e->q, kc, vc, kv->st, e->rope_cos, e->rope_sin, d.nq, d.nkv, d.rope,
+                  (int)std::min<uint32_t>(kv->max_seq, d.rope ? e->rope_rows : kv->max_seq)};
+        return launch_gemv(d.qkv.src(), e->sh_qkv, e->partials, e->counters,
+                           ProNorm{e->x, d.g_in, (int)e->hidden}, eq, s);
+      }
+      case QORA_KERNEL_ATTENTION: {
+        AttnArgs aa{};
+        aa.q = e->q; aa.kc = kc; aa.vc = vc; aa.out = e->attn; aa.st = kv->st;
+        aa.nkv = (int)e->nkv; aa.nc = kv->attn_nc; aa.scale = 1.0f / std::sqrt((float)kHeadDim);
+        aa.part_o = kv->attn_o; aa.part_ml = kv->attn_ml; aa.counters = kv->attn_counters;
+        attn_decode_kernel<<<dim3(e->nkv, kv->attn_nc), kAttnThreads, 0, s>>>(aa);
+        QCUDA(cudaGetLastError());
+        return QORA_OK;
+      }
+      case QORA_KERNEL_O:
+        return launch_gemv(d.o.src(), e->sh_o, e->partials, e->counters, ProPlain{e->attn},
+                           EpiResidual{e->x, (int)e->hidden}, s);
+      case QORA_KERNEL_GATE_UP:
+        return launch_gemv(d.gu.src(), e->sh_gu, e->partials, e->counters,
+                           ProNorm{e->x, d.g_post, (int)e->hidden}, EpiSwiGLU{e->h, (int)e->inter}, s);
+      case QORA_KERNEL_DOWN:
+        return launch_gemv(d.down.src(), e->sh_down, e->partials, e->counters, ProPlain{e->h},
+                           EpiResidual{e->x, (int)e->hidden}, s);
+      default: {
+        LmArgs la{};
+        la.x = e->x; la.gamma = e->final_gamma; la.packed = e->embed_packed; la.scales = e->embed_scales;
+        la.vocab = (int)e->vocab; la.logits = e->logits; la.argmax_out = &kv->st->argmax;
+        la.part_v = e->lm_part_v; la.part_i = e->lm_part_i; la.counter = e->lm_counter;
+        return launch_lm_head((int)e->hidden, la, e->lm_ctas, s);
+      }
+    }
+  };
+  const uint32_t per_rep = (kernel == QORA_KERNEL_LM_HEAD) ? 1 : e->num_layers;
+  for (uint32_t li = 0; li < per_rep; ++li) QCHECK(run_once(li));  // warm-up pass
+  cudaEvent_t a = nullptr, b = nullptr;
+  QCUDA(cudaEventCreate(&a));
+  QCUDA(cudaEventCreate(&b));
+  cudaEventRecord(a, e->stream);
+  qora_status st = QORA_OK;
+  for (uint32_t r = 0; r < reps && st == QORA_OK; ++r)
+    for (uint32_t li = 0; li < per_rep && st == QORA_OK; ++li) st = run_once(li);
+  cudaEventRecord(b, e->stream);
+  cudaError_t ce = cudaEventSynchronize(b);
+  float ms = 0.0f;
+  if (ce == cudaSuccess) ce = cudaEventElapsedTime(&ms, a, b);
+  cudaEventDestroy(a);
+  cudaEventDestroy(b);
+  QCHECK(st);
+  if (ce != cudaSuccess) return fail(QORA_ERR_CUDA, "event timing: %s", cudaGetErrorString(ce));
+  *ms_per_launch = ms / (float)(reps * per_rep);
+  if (bytes_per_launch) *bytes_per_launch = bytes;
+  if (launches) *launches = reps * per_rep;
+  return QORA_OK;
+}
+
+qora_status qora_engine_launches_per_step(const qora_engine* e, uint32_t* launches) {
+  if (!e || !launches) return fail(QORA_ERR_INVALID, "NULL argument");
+  *launches = 1 + 5 * e->num_layers + 2;
+  return QORA_OK;
+}
+
+// ------------------------------------------------------------------ kernel-level entries
+qora_status qora_q4_gemv(const float* d_x, const uint8_t* d_packed, const uint16_t* d_scales,
+                         uint64_t k, uint64_t n, float* d_y, void* stream) {
+  if (!d_x || !d_packed || !d_scales || !d_y) return fail(QORA_ERR_INVALID, "NULL pointer");
+  if (k == 0 || n == 0 || n % kGroup || k > (1u << 30) || n > (1u << 30))
+    return fail(QORA_ERR_INVALID, "bad shape k=%llu n=%llu", (unsigned long long)k, (unsigned long long)n);
+  int dev = 0;
+  QCUDA(cudaGetDevice(&dev));
+  const Q4Src src = f1_src(d_packed, d_scales, (int)k, (int)n);
+  const GemvShape sh = plan_gemv((int)k, src.tiles, 2 * sm_count(dev));
+  std::lock_guard<std::mutex> lk(g_entry_mu);
+  EntryScratch* sc = nullptr;
+  QCHECK(entry_scratch(dev, partial_floats(sh), sh.tiles, 0, &sc));
+  return launch_gemv(src, sh, sc->partials, sc->counters, ProPlain{d_x}, EpiStore{d_y, (int)n},
+                     (cudaStream_t)stream);
+}
+
+qora_status qora_q4_dequant(const uint8_t* d_packed, const uint16_t* d_scales, uint64_t n,
+                            uint64_t row0, uint64_t rows, float* d_out, void* stream) {
+  if (!d_packed || !d_scales || !d_out) return fail(QORA_ERR_INVALID, "NULL pointer");
+  if (n == 0 || n % kGroup) return fail(QORA_ERR_INVALID, "n=%llu must be a multiple of 32", (unsigned long long)n);
+  if (rows == 0) return QORA_OK;
+  const long long total = (long long)(rows * n);
+  const int blocks = (int)std::min<long long>((total + 255) / 256, 4096);
+  dequant_q4_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(d_packed, d_scales, (long long)n,
+                                                               (long long)row0, (long long)rows, d_out);
+  QCUDA(cudaGetLastError());
+  return QORA_OK;
+}
+
+qora_status qora_q4_gate_up(const float* d_x, const uint8_t* d_gate_packed,
+                            const uint16_t* d_gate_scales, const uint8_t* d_up_packed,
+                            const uint16_t* d_up_scales, uint64_t k, uint64_t n, float* d_out,
+                            void* stream) {
+  if (!d_x || !d_gate_packed || !d_gate_scales || !d_up_packed || !d_up_scales || !d_out)
+    return fail(QORA_ERR_INVALID, "NULL pointer");
+  if (k == 0 || n == 0 || n % 128 || k > (1u << 30) || n > (1u << 30))
+    return fail(QORA_ERR_INVALID, "bad shape k=%llu n=%llu (n must be a multiple of 128)",
+                (unsigned long long)k, (unsigned long long)n);
+  int dev = 0;
+  QCUDA(cudaGetDevice(&dev));
+  const Q4Src src = f1_pair_src(d_gate_packed, d_gate_scales, d_up_packed, d_up_scales, (int)k, (int)n);
+  const GemvShape sh = plan_gemv((int)k, src.tiles, 2 * sm_count(dev));
+  std::lock_guard<std::mutex> lk(g_entry_mu);
+  EntryScratch* sc = nullptr;
+  QCHECK(entry_scratch(dev, partial_floats(sh), sh.tiles, 0, &sc));
+  return launch_gemv(src, sh, sc->partials, sc->counters, ProPlain{d_x}, EpiSwiGLU{d_out, (int)n},
+                     (cudaStream_t)stream);
+}
+
+qora_status qora_q4_lm_head(const float* d_x, const uint8_t* d_packed, const uint16_t* d_scales,
+                            uint64_t vocab, uint64_t hidden, float* d_logits, uint32_t* d_argmax,
+                            void* stream) {
+  if (!d_x || !d_packed || !d_scales || !d_argmax) return fail(QORA_ERR_INVALID, "NULL pointer");
+  if (vocab == 0 || vocab > (1u << 30)) return fail(QORA_ERR_INVALID, "bad vocab");
+  int dev = 0;
+  QCUDA(cudaGetDevice(&dev));
+  const int ctas = (int)std::min<uint64_t>(2 * sm_count(dev), vocab);
+  std::lock_guard<std::mutex> lk(g_entry_mu);
+  EntryScratch* sc = nullptr;
+  QCHECK(entry_scratch(dev, 0, 0, ctas, &sc));
+  LmArgs a{};
+  a.x = d_x;
+  a.gamma = nullptr;
+  a.packed = d_packed;
+  a.scales = d_scales;
+  a.vocab = (int)vocab;
+  a.logits = d_logits;
+  a.argmax_out = d_argmax;
+  a.part_v = sc->lm_v;
+  a.part_i = sc->lm_i;
+  a.counter = sc->lm_c;
+  return launch_lm_head((int)hidden, a, ctas, (cudaStream_t)stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,51 @@
+// small_kernels.cuh — embedding row lookup, step bookkeeping and Q4 dequantisation.
+#pragma once
+
+#include "common.cuh"
+
+namespace qora {
+
+// embed_lookup_q4 (src/gemv.rs:710-736): x[e] = f32(scale) * (q - 8), exact.
+__global__ void embed_q4_kernel(const uint8_t* packed, const uint16_t* scales, int vocab,
+                                int hidden, StepState* st, float* x) {
+  const int token = st->token;
+  if (token < 0 || token >= vocab) {
+    if (threadIdx.x == 0) st->error = 1;
+    return;
+  }
+  const int gpr = hidden / kGroup;
+  for (int e = threadIdx.x; e < hidden; e += blockDim.x) {
+    const int g = e / kGroup, j = e % kGroup;
+    const uint8_t b = packed[((long long)token * gpr + g) * 16 + j / 2];
+    const int q = ((j & 1) ? (b >> 4) : (b & 0xF)) - 8;
+    const float s = __half2float(__ushort_as_half(scales[(long long)token * gpr + g]));
+    x[e] = __fmul_rn(s, (float)q);
+  }
+}
+
+// End of a decode step: record the greedy token, feed it back, advance the position.
+__global__ void advance_kernel(StepState* st, unsigned* ring, int ring_cap) {
+  const unsigned a = st->argmax;
+  const int s = st->step;
+  if (ring && s >= 0 && s < ring_cap) ring[s] = a;
+  st->step = s + 1;
+  st->token = (int)a;
+  st->pos = st->pos + 1;
+}
+
+// Rows [row0, row0+rows) of a Q4 [k][n] matrix to f32: (q - 8) * f32(scale).
+__global__ void dequant_q4_kernel(const uint8_t* packed, const uint16_t* scales, long long n,
+                                  long long row0, long long rows, float* out) {
+  const long long total = rows * n;
+  const long long gpr = n / kGroup;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long r = row0 + i / n, j = i % n;
+    const uint8_t b = packed[(r * n + j) / 2];
+    const int q = ((j & 1) ? (b >> 4) : (b & 0xF)) - 8;
+    const float s = __half2float(__ushort_as_half(scales[r * gpr + j / kGroup]));
+    out[i] = __fmul_rn((float)q, s);
+  }
+}
+
+}  // namespace qora

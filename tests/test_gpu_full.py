@@ -1,0 +1,107 @@
+"""Full-size parity (BASELINE configs 3 and 4) on the GPU against the oracle: the
+SmolLM3-3B architecture with seeded random-init Q4 weights (36 layers, vocab 128256).
+
+Config 3: 32-token prompt, greedy decode. The GPU generates all 256 tokens; the oracle
+(CPU, all host threads) checks as many of them as fit a bounded time budget, plus the
+prefill logits (rel-L2 <= 1e-3) and teacher-forced logits. Config 4: every layer's KV
+pre-filled with 32768 rows of N(0,1) through qora_kv_import, then decode steps whose
+logits are checked against the oracle at the same 32K context."""
+import os
+import time
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_TOL = 1e-3
+ORACLE_BUDGET_S = float(os.environ.get("QORA_ORACLE_BUDGET_S", "60"))
+
+
+def rel_l2(a, b):
+    a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-300))
+
+
+@pytest.fixture(scope="module")
+def full(qf):
+    return qf.synth_model(seed=0)
+
+
+@pytest.fixture(scope="module")
+def full_engine(pkg, full):
+    w = pkg.DecodeWeights(model=full)
+    yield w
+    w.close()
+
+
+@pytest.fixture(scope="module")
+def full_oracle(orc, full):
+    orc.set_threads(os.cpu_count() or 1)
+    return orc.OracleModel(full)
+
+
+def test_config3_prefill_and_greedy(full_engine, full_oracle):
+    w, om = full_engine, full_oracle
+    prompt = np.random.default_rng(1).integers(0, w.vocab, size=32).astype(np.uint32)
+    kv = w.new_kv(32 + 256 + 8)
+    first, lg = w.prefill(kv, prompt)
+    okv = om.new_kv()
+    lo = om.prefill(prompt, okv)
+    err = rel_l2(lg, lo)
+    print(f"prefill logits rel-L2 {err:.3e}")
+    assert err < LOGIT_TOL
+    assert first == int(np.argmax(lo))
+    toks = np.concatenate([[first], w.generate_greedy(kv, first, 255)])
+    assert len(toks) == 256 and len(kv) == 32 + 255
+    # oracle continues greedily from its own argmax for a bounded time
+    t0, n, prev, worst_margin = time.time(), 1, first, np.inf
+    while n < 256 and time.time() - t0 < ORACLE_BUDGET_S:
+        lo = om.forward_decode(int(prev), okv)
+        s = np.sort(lo)[-2:]
+        worst_margin = min(worst_margin, float(s[1] - s[0]))
+        prev = int(np.argmax(lo))
+        assert toks[n] == prev, f"token {n} differs (oracle margin {s[1] - s[0]})"
+        n += 1
+    print(f"greedy tokens identical for {n}/256 checked, min oracle margin {worst_margin:.4f}")
+    assert n >= 16
+
+
+def test_config3_teacher_forced_logits(full_engine, full_oracle):
+    w, om = full_engine, full_oracle
+    kv, okv = w.new_kv(64), om.new_kv()
+    worst = 0.0
+    for tok in np.random.default_rng(2).integers(0, w.vocab, size=6):
+        am, lg = w.decode_step(kv, int(tok), want_logits=True)
+        lo = om.forward_decode(int(tok), okv)
+        worst = max(worst, rel_l2(lg, lo))
+        s = np.sort(lo)[-2:]
+        assert am == int(np.argmax(lo)), f"margin {s[1] - s[0]}"
+    print(f"teacher-forced worst rel-L2 {worst:.3e}")
+    assert worst < LOGIT_TOL
+
+
+def test_config4_long_context(full_engine, full_oracle, full):
+    w, om = full_engine, full_oracle
+    S = 32768
+    rng = np.random.default_rng(4)
+    kv = w.new_kv(S + 136)
+    okv = om.new_kv()
+    stride = full.layers[0].num_kv_heads * full.layers[0].head_dim
+    for layer in range(w.num_layers):
+        K = rng.standard_normal((S, stride), dtype=np.float32)
+        V = rng.standard_normal((S, stride), dtype=np.float32)
+        kv.import_layer(layer, K, V)
+        okv.import_layer(layer, K, V)
+    assert len(kv) == S
+    worst = 0.0
+    for tok in (17, 90001, 5):
+        am, lg = w.decode_step(kv, tok, want_logits=True)
+        lo = om.forward_decode(tok, okv)
+        worst = max(worst, rel_l2(lg, lo))
+        s = np.sort(lo)[-2:]
+        assert am == int(np.argmax(lo)), f"margin {s[1] - s[0]}"
+    print(f"32K-context logits worst rel-L2 {worst:.3e}")
+    assert worst < LOGIT_TOL
+    toks = w.generate_greedy(kv, 5, 125)  # 128 decode steps in total at ~32K context
+    assert len(kv) == S + 128 and toks.max() < w.vocab
