@@ -79,8 +79,12 @@ typedef struct qora_kv qora_kv;
 typedef struct qora_engine_options {
     int32_t  n_gpus;        /* tensor-parallel degree; 0 or 1 = single GPU          */
     int32_t  first_device;  /* CUDA ordinal of rank 0 (ranks use first_device + r) */
-    uint32_t flags;         /* reserved, must be 0                                  */
+    uint32_t flags;         /* QORA_FLAG_* bits                                     */
 } qora_engine_options;
+
+/* Run each decode step as a CUDA graph of per-operation kernels instead of the
+ * persistent single-kernel step (diagnostics and cross-checking). */
+#define QORA_FLAG_PER_OP_KERNELS 1u
 
 /* Last error message of the calling thread ("" if none). */
 const char* qora_last_error(void);
@@ -217,6 +221,12 @@ qora_status qora_generate_greedy_timed(qora_engine* engine, qora_kv* kv, uint32_
 qora_status qora_engine_time_kernel(qora_engine* engine, qora_kv* kv, int kernel,
                                     uint32_t reps, float* ms_per_launch,
                                     uint64_t* bytes_per_launch, uint32_t* launches);
+
+/* Diagnostics of the persistent decode kernel: when enabled, every CTA records
+ * %globaltimer stamps at its phase boundaries during each step (overwritten by the next
+ * step). get_trace copies up to `cap` u64 values and reports how many exist. */
+qora_status qora_engine_set_trace(qora_engine* engine, int enable);
+qora_status qora_engine_get_trace(qora_engine* engine, uint64_t* out, size_t cap, size_t* n);
 
 /* Number of kernel launches one decode step makes (the captured graph's nodes). */
 qora_status qora_engine_launches_per_step(const qora_engine* engine, uint32_t* launches);

@@ -20,8 +20,9 @@ constexpr int kLmWarps = kLmThreads / 32;
 struct LmArgs {
   const float* x;        // [hidden] input (pre-norm if gamma != nullptr)
   const float* gamma;    // final norm gains (f32) or nullptr
-  const uint8_t* packed; // [vocab][hidden/2]
-  const uint16_t* scales;// [vocab][hidden/32]
+  const uint8_t* packed; // row r packed nibbles at packed + r*row_stride_p (hidden/2 bytes)
+  const uint8_t* scales; // row r f16 scales at scales + r*row_stride_s (hidden/32 values)
+  long long row_stride_p, row_stride_s;
   int vocab;
   float* logits;         // [vocab] or nullptr
   unsigned* argmax_out;  // one value
@@ -72,8 +73,8 @@ __global__ void __launch_bounds__(kLmThreads, 2) lm_head_kernel(const LmArgs a) 
   const float k64 = 18446744073709551616.0f;  // 2^64
 
   for (long long r = r0 + warp; r < r1; r += kLmWarps) {
-    const uint4* wp = reinterpret_cast<const uint4*>(a.packed + r * (H / 2)) + lane * GPL;
-    const unsigned short* sp = reinterpret_cast<const unsigned short*>(a.scales) + r * (H / 32) + lane * GPL;
+    const uint4* wp = reinterpret_cast<const uint4*>(a.packed + r * a.row_stride_p) + lane * GPL;
+    const unsigned short* sp = reinterpret_cast<const unsigned short*>(a.scales + r * a.row_stride_s) + lane * GPL;
     uint4 w[GPL];
     unsigned short sc[GPL];
 #pragma unroll

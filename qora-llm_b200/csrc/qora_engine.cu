@@ -28,6 +28,7 @@
 #include "attention.cuh"
 #include "common.cuh"
 #include "lm_head.cuh"
+#include "megakernel.cuh"
 #include "q4_gemv.cuh"
 #include "small_kernels.cuh"
 
@@ -220,8 +221,8 @@ struct qora_engine {
   uint32_t num_layers = 0, vocab = 0, hidden = 0, inter = 0;
   uint32_t nh = 0, nkv = 0, rope_rows = 0;
   std::vector<LayerDev> layers;
-  uint8_t* embed_packed = nullptr;
-  uint16_t* embed_scales = nullptr;
+  uint8_t* lm_table = nullptr;   // embedding rows: hidden/2 packed bytes | hidden/32 f16 scales
+  long long lm_row_bytes = 0;
   float* final_gamma = nullptr;
   float* rope_cos = nullptr;
   float* rope_sin = nullptr;
@@ -237,8 +238,24 @@ struct qora_engine {
   float* lm_part_v = nullptr;
   unsigned* lm_part_i = nullptr;
   unsigned* lm_counter = nullptr;
+  // persistent decode megakernel (shared buffers; per-cache parts live in qora_kv)
+  bool mk_ok = false;
+  std::string mk_why;
+  int mk_G = 0;
+  int mk_slots[4] = {0, 0, 0, 0};
+  int mk_sub0[4] = {0, 0, 0, 0}, mk_subn[4] = {0, 0, 0, 0}, mk_segs[4] = {0, 0, 0, 0};
+  int mk_cpl = 0, mk_ncnt = 0;
+  float* mk_xbuf = nullptr;
+  float* mk_part[4] = {nullptr, nullptr, nullptr, nullptr};
+  unsigned* mk_cnt = nullptr;
+  float* mk_lm_v = nullptr;
+  unsigned* mk_lm_i = nullptr;
+  unsigned long long* mk_trace = nullptr;
+  size_t mk_trace_n = 0;
+  bool use_mega = true;
   std::vector<void*> allocs;
   uint64_t device_bytes = 0;
+  std::vector<qora_kv*> kvs;  // live caches; detached (device state freed) on destroy
 
   template <typename T>
   qora_status alloc(T** p, size_t count) {
@@ -252,11 +269,7 @@ struct qora_engine {
     *p = static_cast<T*>(d);
     return QORA_OK;
   }
-  ~qora_engine() {
-    if (stream) cudaStreamSynchronize(stream);
-    for (void* p : allocs) cudaFree(p);
-    if (stream) cudaStreamDestroy(stream);
-  }
+  ~qora_engine();
 };
 
 struct qora_kv {
@@ -274,15 +287,29 @@ struct qora_kv {
   float* attn_ml = nullptr;
   unsigned* attn_counters = nullptr;
   cudaGraphExec_t graph = nullptr;
+  bool mk_ready = false;
+  mk::Args mk_args{};
+  mk::Layer* mk_layers = nullptr;
+  float* mk_att_o = nullptr;
+  float* mk_att_ml = nullptr;
   std::vector<void*> allocs;
+  // free the device-side state (the engine's stream must be idle or synchronised)
+  void release_device() {
+    if (graph) cudaGraphExecDestroy(graph);
+    graph = nullptr;
+    for (void* p : allocs) cudaFree(p);
+    allocs.clear();
+    if (st_host) cudaFreeHost(st_host);
+    st_host = nullptr;
+  }
   ~qora_kv() {
     if (e) {
       cudaSetDevice(e->device);
       cudaStreamSynchronize(e->stream);
+      auto& v = e->kvs;
+      v.erase(std::remove(v.begin(), v.end(), this), v.end());
     }
-    if (graph) cudaGraphExecDestroy(graph);
-    for (void* p : allocs) cudaFree(p);
-    if (st_host) cudaFreeHost(st_host);
+    release_device();
   }
   template <typename T>
   qora_status alloc(T** p, size_t count) {
@@ -297,6 +324,17 @@ struct qora_kv {
   }
   size_t layer_stride() const { return (size_t)max_seq * e->nkv * kHeadDim; }
 };
+
+qora_engine::~qora_engine() {
+  if (stream) cudaStreamSynchronize(stream);
+  for (qora_kv* kv : kvs) {  // caches outliving their engine become inert shells
+    kv->release_device();
+    kv->e = nullptr;
+  }
+  kvs.clear();
+  for (void* p : allocs) cudaFree(p);
+  if (stream) cudaStreamDestroy(stream);
+}
 
 namespace {
 
@@ -392,6 +430,8 @@ qora_status build_layer(qora_engine* e, const qora_weights_view* w, uint32_t i) 
   return QORA_OK;
 }
 
+qora_status mega_init(qora_engine* e);
+
 qora_status engine_init(qora_engine* e, const qora_weights_view* w) {
   const qora_layer_view& L0 = w->layers[0];
   e->format = w->format;
@@ -440,10 +480,19 @@ qora_status engine_init(qora_engine* e, const qora_weights_view* w) {
   }
 
   const size_t H = w->hidden, V = w->vocab;
-  QCHECK(e->alloc(&e->embed_packed, V * H / 2));
-  QCHECK(e->alloc(&e->embed_scales, V * H / kGroup));
-  QCHECK(upload(e, e->embed_packed, w->embed.packed, V * H / 2));
-  QCHECK(upload(e, e->embed_scales, w->embed.scales, V * H / kGroup * 2));
+  {
+    // row-interleaved copy: one contiguous row per token serves both the embedding lookup
+    // and the row-dot lm_head stream (same nibbles and f16 scales as the file)
+    e->lm_row_bytes = (long long)(H / 2 + H / kGroup * 2);
+    std::vector<uint8_t> host((size_t)V * e->lm_row_bytes);
+    for (size_t v = 0; v < V; ++v) {
+      uint8_t* dst = host.data() + v * e->lm_row_bytes;
+      std::memcpy(dst, w->embed.packed + v * (H / 2), H / 2);
+      std::memcpy(dst + H / 2, w->embed.scales + v * (H / kGroup), H / kGroup * 2);
+    }
+    QCHECK(e->alloc(&e->lm_table, host.size()));
+    QCHECK(upload(e, e->lm_table, host.data(), host.size()));
+  }
   std::vector<float> fg = f16_to_f32(w->final_norm_gamma, H);
   QCHECK(e->alloc(&e->final_gamma, H));
   QCHECK(upload(e, e->final_gamma, fg.data(), H * 4));
@@ -480,7 +529,191 @@ qora_status engine_init(qora_engine* e, const qora_weights_view* w) {
   QCHECK(e->alloc(&e->lm_part_i, e->lm_ctas));
   QCHECK(e->alloc(&e->lm_counter, 1));
   QCUDA(cudaMemset(e->lm_counter, 0, sizeof(unsigned)));
+  QCHECK(mega_init(e));
   QCUDA(cudaDeviceSynchronize());
+  return QORA_OK;
+}
+
+// ------------------------------------------------------------------ megakernel set-up
+template <int GPL>
+qora_status mega_occupancy(int* blocks) {
+  auto kern = mk::decode_megakernel<GPL>;
+  QCUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mk::smem_bytes()));
+  QCUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks, kern, mk::kThreads, mk::smem_bytes()));
+  return QORA_OK;
+}
+
+// Segments (tile, first row, end row) of CTA lc of a g-CTA subset over a tiles x K
+// matrix, in the order the kernel walks them (mirrors mk::for_each_segment).
+template <class F>
+void host_segments(int K, int tiles, int g, int lc, F&& f) {
+  const long long total = (long long)tiles * K;
+  const long long lin0 = (long long)lc * total / g, lin1 = (long long)(lc + 1) * total / g;
+  for (long long p = lin0; p < lin1;) {
+    const long long t = p / K, r0 = p - t * K;
+    const long long pe = std::min(lin1, (t + 1) * K);
+    f((int)t, (int)r0, (int)(pe - t * K));
+    p = pe;
+  }
+}
+
+// Decide whether the persistent kernel can run this geometry and allocate its buffers.
+// q|k|v runs on the last gq CTAs and o_proj on the go CTAs before them, so that their
+// few split-K partials can be summed directly by the consumers; gate/up and down run on
+// every CTA.
+qora_status mega_init(qora_engine* e) {
+  e->mk_ok = false;
+  const int H = (int)e->hidden, G = e->sms;
+  const LayerDev& d0 = e->layers[0];
+  const int nh = (int)e->nh;
+  auto no = [&](const char* why) {
+    e->mk_why = why;
+    return QORA_OK;
+  };
+  if (H != 1024 && H != 2048) return no("hidden must be 1024 or 2048");
+  if (nh != 8 && nh != 16) return no("num_heads must be 8 or 16");
+  if (G < 16 || G > mk::kMaxUnits) return no("SM count outside the supported range");
+  const int gq = std::min(48, G / 3), go = std::min(32, G / 4);
+  const int sub0[4] = {G - gq, G - gq - go, 0, 0};
+  const int subn[4] = {gq, go, G, G};
+  const DevQ4* mats[4] = {&d0.qkv, &d0.o, &d0.gu, &d0.down};
+  for (int m = 0; m < 4; ++m) {
+    const long long total = (long long)mats[m]->tiles * mats[m]->K;
+    if (total < subn[m]) return no("matrix too small for one segment per CTA");
+    if ((total + subn[m] - 1) / subn[m] + 1 > mk::kXsCap) return no("per-CTA rows exceed the shared input buffer");
+    int segs = 0;
+    for (int lc = 0; lc < subn[m]; ++lc) {
+      bool bad = false;
+      host_segments(mats[m]->K, mats[m]->tiles, subn[m], lc, [&](int, int r0, int r1) {
+        ++segs;
+        // o_proj: the attention rows of one segment must come from at most 8 heads
+        if (m == 1 && (r1 - 1) / kHeadDim - r0 / kHeadDim + 1 > 8) bad = true;
+      });
+      if (bad) return no("o_proj segment spans too many heads");
+    }
+    e->mk_sub0[m] = sub0[m];
+    e->mk_subn[m] = subn[m];
+    e->mk_segs[m] = segs;
+  }
+  if (H > mk::kBFloats) return no("hidden larger than the shared x buffer");
+  if ((int)e->nkv * kHeadDim > mk::kMaxVItems * mk::kCT) return no("too many KV heads for the P.V pass");
+  if ((int)e->nkv * kHeadDim * 2 > 1024) return no("new k|v row larger than its shared buffer");
+  if ((int)e->nh > 16 || (int)e->nh % (int)e->nkv != 0 || (int)(e->nh / e->nkv) > 4) return no("head grouping");
+  if (e->lm_row_bytes > mk::kStageBytes) return no("embedding row larger than a stage");
+  if ((int)e->nkv * kHeadDim * 4 > mk::kStageBytes) return no("KV row larger than a stage");
+  int blocks = 0;
+  if (H == 2048) QCHECK(mega_occupancy<2>(&blocks)); else QCHECK(mega_occupancy<1>(&blocks));
+  if (blocks < 1) return no("megakernel does not fit one CTA per SM");
+  e->mk_G = G;
+  for (int m = 0; m < 4; ++m) {
+    GemvShape sh = plan_gemv(mats[m]->K, mats[m]->tiles, subn[m]);
+    e->mk_slots[m] = sh.plan.max_slots;
+    QCHECK(e->alloc(&e->mk_part[m], (size_t)mats[m]->tiles * sh.plan.max_slots * kTileCols));
+  }
+  e->mk_cpl = 3 + d0.gu.tiles + d0.down.tiles + 1;
+  e->mk_ncnt = (int)e->num_layers * e->mk_cpl + 2;
+  QCHECK(e->alloc(&e->mk_cnt, e->mk_ncnt));
+  QCUDA(cudaMemset(e->mk_cnt, 0, (size_t)e->mk_ncnt * sizeof(unsigned)));
+  QCHECK(e->alloc(&e->mk_xbuf, (size_t)(e->num_layers + 1) * H));
+  QCHECK(e->alloc(&e->mk_lm_v, G));
+  QCHECK(e->alloc(&e->mk_lm_i, G));
+  e->mk_ok = true;
+  return QORA_OK;
+}
+
+qora_status mega_prepare(qora_engine* e, qora_kv* kv) {
+  if (kv->mk_ready) return QORA_OK;
+  const int L = (int)e->num_layers, G = e->mk_G;
+  std::vector<mk::Layer> hl(L);
+  for (int i = 0; i < L; ++i) {
+    const LayerDev& d = e->layers[i];
+    hl[i].w[0] = d.qkv.buf;
+    hl[i].w[1] = d.o.buf;
+    hl[i].w[2] = d.gu.buf;
+    hl[i].w[3] = d.down.buf;
+    hl[i].g_in = d.g_in;
+    hl[i].g_post = d.g_post;
+    hl[i].kc = kv->k + (size_t)i * kv->layer_stride();
+    hl[i].vc = kv->v + (size_t)i * kv->layer_stride();
+    hl[i].rope = d.rope;
+  }
+  QCHECK(kv->alloc(&kv->mk_layers, L));
+  QCUDA(cudaMemcpy(kv->mk_layers, hl.data(), L * sizeof(mk::Layer), cudaMemcpyHostToDevice));
+  const int max_units = std::max<int>(G, (int)((kv->max_seq + mk::kMaxAttnChunk - 1) / mk::kMaxAttnChunk));
+  QCHECK(kv->alloc(&kv->mk_att_o, (size_t)max_units * e->nh * kHeadDim));
+  QCHECK(kv->alloc(&kv->mk_att_ml, (size_t)max_units * e->nh * 2));
+  mk::Args& a = kv->mk_args;
+  a = mk::Args{};
+  a.layers = kv->mk_layers;
+  a.L = L;
+  const LayerDev& d0 = e->layers[0];
+  const DevQ4* mats[4] = {&d0.qkv, &d0.o, &d0.gu, &d0.down};
+  for (int m = 0; m < 4; ++m) {
+    a.K[m] = mats[m]->K;
+    a.tiles[m] = mats[m]->tiles;
+    a.slots[m] = e->mk_slots[m];
+    a.part[m] = e->mk_part[m];
+    a.sub0[m] = e->mk_sub0[m];
+    a.subn[m] = e->mk_subn[m];
+    a.segs[m] = e->mk_segs[m];
+  }
+  a.H = (int)e->hidden;
+  a.I = (int)e->inter;
+  a.nq = d0.nq;
+  a.nkvw = d0.nkv;
+  a.nh = (int)e->nh;
+  a.nkvh = (int)e->nkv;
+  a.grp = kGrp;
+  a.vocab = (int)e->vocab;
+  a.lm_row_bytes = (int)e->lm_row_bytes;
+  {
+    // embedding rows per stage: as many as fit, a multiple of the consumer warps if possible
+    int rows = (int)(mk::kStageBytes / e->lm_row_bytes);
+    if (rows >= mk::kCW) rows -= rows % mk::kCW;
+    a.lm_rows_per_stage = rows;
+  }
+  a.lm = e->lm_table;
+  a.final_gamma = e->final_gamma;
+  a.cos_t = e->rope_cos;
+  a.sin_t = e->rope_sin;
+  bool any_rope = false;
+  for (auto& Ld : e->layers) any_rope |= (Ld.rope != 0);
+  a.max_pos = (int)std::min<uint32_t>(kv->max_seq, any_rope ? e->rope_rows : kv->max_seq);
+  a.xbuf = e->mk_xbuf;
+  a.logits = e->logits;
+  a.att_o = kv->mk_att_o;
+  a.att_ml = kv->mk_att_ml;
+  a.max_units = max_units;
+  a.cnt = e->mk_cnt;
+  a.cpl = e->mk_cpl;
+  a.n_cnt = e->mk_ncnt;
+  a.lm_v = e->mk_lm_v;
+  a.lm_i = e->mk_lm_i;
+  a.st = kv->st;
+  a.ring = kv->ring;
+  a.ring_cap = (int)kv->max_seq;
+  a.timeout_ns = 2000000000ull;
+  a.trace = e->mk_trace;
+  kv->mk_ready = true;
+  return QORA_OK;
+}
+
+qora_status launch_mega(qora_engine* e, qora_kv* kv) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(e->mk_G);
+  cfg.blockDim = dim3(mk::kThreads);
+  cfg.dynamicSmemBytes = mk::smem_bytes();
+  cfg.stream = e->stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (e->hidden == 2048) {
+    QCUDA(cudaLaunchKernelEx(&cfg, mk::decode_megakernel<2>, kv->mk_args));
+  } else {
+    QCUDA(cudaLaunchKernelEx(&cfg, mk::decode_megakernel<1>, kv->mk_args));
+  }
   return QORA_OK;
 }
 
@@ -532,7 +765,7 @@ qora_status launch_layer(qora_engine* e, qora_kv* kv, uint32_t li) {
 // the whole decode step (what the CUDA graph holds)
 qora_status launch_step(qora_engine* e, qora_kv* kv, int* launches) {
   cudaStream_t s = e->stream;
-  embed_q4_kernel<<<1, 256, 0, s>>>(e->embed_packed, e->embed_scales, (int)e->vocab,
+  embed_q4_kernel<<<1, 256, 0, s>>>(e->lm_table, e->lm_row_bytes, (int)e->vocab,
                                     (int)e->hidden, kv->st, e->x);
   QCUDA(cudaGetLastError());
   int n = 1;
@@ -543,8 +776,9 @@ qora_status launch_step(qora_engine* e, qora_kv* kv, int* launches) {
   LmArgs la{};
   la.x = e->x;
   la.gamma = e->final_gamma;
-  la.packed = e->embed_packed;
-  la.scales = e->embed_scales;
+  la.packed = e->lm_table;
+  la.scales = e->lm_table + e->hidden / 2;
+  la.row_stride_p = la.row_stride_s = e->lm_row_bytes;
   la.vocab = (int)e->vocab;
   la.logits = e->logits;
   la.argmax_out = &kv->st->argmax;
@@ -576,6 +810,23 @@ qora_status ensure_graph(qora_engine* e, qora_kv* kv) {
   return QORA_OK;
 }
 
+// prepare whichever decode path this engine uses (graph of per-op kernels, or the
+// persistent megakernel)
+bool kv_uses_mega(const qora_engine* e, const qora_kv* kv) {
+  return e->mk_ok && e->use_mega && kv->max_seq <= (uint32_t)(mk::kMaxAttnChunk * mk::kMaxUnits);
+}
+
+qora_status step_prepare(qora_engine* e, qora_kv* kv) {
+  if (kv_uses_mega(e, kv)) return mega_prepare(e, kv);
+  return ensure_graph(e, kv);
+}
+
+qora_status step_launch(qora_engine* e, qora_kv* kv) {
+  if (kv_uses_mega(e, kv)) return launch_mega(e, kv);
+  QCUDA(cudaGraphLaunch(kv->graph, e->stream));
+  return QORA_OK;
+}
+
 qora_status check_uniform_len(const qora_kv* kv, uint32_t* len) {
   const uint32_t l = kv->len[0];
   for (uint32_t x : kv->len)
@@ -597,6 +848,7 @@ qora_status set_state(qora_engine* e, qora_kv* kv, int pos, int token, int step)
 qora_status check_step_error(qora_engine* e, qora_kv* kv) {
   QCUDA(cudaMemcpyAsync(kv->st_host, kv->st, sizeof(StepState), cudaMemcpyDeviceToHost, e->stream));
   QCUDA(cudaStreamSynchronize(e->stream));
+  if (kv->st_host->error == 2) return fail(QORA_ERR_TIMEOUT, "a bounded device-side wait timed out");
   if (kv->st_host->error) return fail(QORA_ERR_RANGE, "device rejected a token id");
   return QORA_OK;
 }
@@ -779,7 +1031,8 @@ qora_status qora_engine_create(const qora_weights_view* weights, const qora_engi
   const int n_gpus = opts ? opts->n_gpus : 1;
   if (n_gpus > 1)
     return fail(QORA_ERR_UNSUPPORTED, "tensor-parallel engines (n_gpus=%d) are not in this build", n_gpus);
-  if (opts && opts->flags != 0) return fail(QORA_ERR_INVALID, "options.flags must be 0");
+  if (opts && (opts->flags & ~QORA_FLAG_PER_OP_KERNELS))
+    return fail(QORA_ERR_INVALID, "unknown option flags 0x%x", opts->flags);
   int ndev = 0;
   QCUDA(cudaGetDeviceCount(&ndev));
   const int dev = opts ? opts->first_device : 0;
@@ -787,6 +1040,7 @@ qora_status qora_engine_create(const qora_weights_view* weights, const qora_engi
   QCUDA(cudaSetDevice(dev));
   std::unique_ptr<qora_engine> e(new qora_engine());
   e->device = dev;
+  e->use_mega = !(opts && (opts->flags & QORA_FLAG_PER_OP_KERNELS));
   QCHECK(engine_init(e.get(), weights));
   *out = e.release();
   return QORA_OK;
@@ -877,6 +1131,7 @@ qora_status qora_kv_create(qora_engine* e, uint32_t max_seq, uint32_t batch, qor
   QCUDA(cudaMemset(kv->attn_counters, 0, e->nkv * sizeof(unsigned)));
   QCUDA(cudaMemset(kv->st, 0, sizeof(StepState)));
   QCUDA(cudaDeviceSynchronize());
+  e->kvs.push_back(kv.get());
   *out = kv.release();
   return QORA_OK;
 }
@@ -900,6 +1155,7 @@ qora_status qora_kv_reset(qora_kv* kv, uint32_t seq_idx) {
 qora_status qora_kv_import(qora_kv* kv, uint32_t layer, const float* k, const float* v,
                            uint32_t seq_len, uint32_t seq_idx) {
   if (!kv || (!k && seq_len) || (!v && seq_len)) return fail(QORA_ERR_INVALID, "NULL argument");
+  if (!kv->e) return fail(QORA_ERR_INVALID, "the KV cache's engine was destroyed");
   if (seq_idx != 0) return fail(QORA_ERR_RANGE, "seq_idx %u", seq_idx);
   if (layer >= kv->e->num_layers) return fail(QORA_ERR_RANGE, "layer %u", layer);
   if (seq_len > kv->max_seq) return fail(QORA_ERR_RANGE, "seq_len %u > max_seq %u", seq_len, kv->max_seq);
@@ -916,6 +1172,7 @@ qora_status qora_kv_import(qora_kv* kv, uint32_t layer, const float* k, const fl
 qora_status qora_kv_export(const qora_kv* kv, uint32_t layer, float* k, float* v, uint32_t seq_len,
                            uint32_t seq_idx) {
   if (!kv || !k || !v) return fail(QORA_ERR_INVALID, "NULL argument");
+  if (!kv->e) return fail(QORA_ERR_INVALID, "the KV cache's engine was destroyed");
   if (seq_idx != 0) return fail(QORA_ERR_RANGE, "seq_idx %u", seq_idx);
   if (layer >= kv->e->num_layers) return fail(QORA_ERR_RANGE, "layer %u", layer);
   if (seq_len > kv->len[layer]) return fail(QORA_ERR_RANGE, "seq_len %u > length %u", seq_len, kv->len[layer]);
@@ -935,13 +1192,14 @@ qora_status qora_decode_step(qora_engine* e, qora_kv* kv, const uint32_t* tokens
   QCHECK(check_uniform_len(kv, &len));
   if (len >= kv->max_seq) return fail(QORA_ERR_RANGE, "KV cache full (%u positions)", kv->max_seq);
   QCUDA(cudaSetDevice(e->device));
-  QCHECK(ensure_graph(e, kv));
+  QCHECK(step_prepare(e, kv));
   QCHECK(set_state(e, kv, (int)len, (int)tokens[0], 0));
-  QCUDA(cudaGraphLaunch(kv->graph, e->stream));
+  QCHECK(step_launch(e, kv));
   QCUDA(cudaMemcpyAsync(kv->st_host, kv->st, sizeof(StepState), cudaMemcpyDeviceToHost, e->stream));
   if (logits_or_null)
     QCUDA(cudaMemcpyAsync(logits_or_null, e->logits, (size_t)e->vocab * 4, cudaMemcpyDeviceToHost, e->stream));
   QCUDA(cudaStreamSynchronize(e->stream));
+  if (kv->st_host->error == 2) return fail(QORA_ERR_TIMEOUT, "a bounded device-side wait timed out");
   if (kv->st_host->error) return fail(QORA_ERR_RANGE, "device rejected token id");
   if (argmax_out) argmax_out[0] = kv->st_host->argmax;
   for (auto& l : kv->len) l = len + 1;
@@ -960,17 +1218,18 @@ qora_status qora_prefill(qora_engine* e, qora_kv* kv, const uint32_t* ids, uint3
   if ((uint64_t)len + n > kv->max_seq)
     return fail(QORA_ERR_RANGE, "prompt of %u after %u positions exceeds max_seq %u", n, len, kv->max_seq);
   QCUDA(cudaSetDevice(e->device));
-  QCHECK(ensure_graph(e, kv));
+  QCHECK(step_prepare(e, kv));
   QCUDA(cudaMemcpyAsync(kv->ids, ids, (size_t)n * 4, cudaMemcpyHostToDevice, e->stream));
   QCHECK(set_state(e, kv, (int)len, (int)ids[0], 0));
   for (uint32_t i = 0; i < n; ++i) {
     QCUDA(cudaMemcpyAsync(&kv->st->token, kv->ids + i, 4, cudaMemcpyDeviceToDevice, e->stream));
-    QCUDA(cudaGraphLaunch(kv->graph, e->stream));
+    QCHECK(step_launch(e, kv));
   }
   QCUDA(cudaMemcpyAsync(kv->st_host, kv->st, sizeof(StepState), cudaMemcpyDeviceToHost, e->stream));
   if (logits_or_null)
     QCUDA(cudaMemcpyAsync(logits_or_null, e->logits, (size_t)e->vocab * 4, cudaMemcpyDeviceToHost, e->stream));
   QCUDA(cudaStreamSynchronize(e->stream));
+  if (kv->st_host->error == 2) return fail(QORA_ERR_TIMEOUT, "a bounded device-side wait timed out");
   if (kv->st_host->error) return fail(QORA_ERR_RANGE, "device rejected token id");
   if (argmax_out) *argmax_out = kv->st_host->argmax;
   for (auto& l : kv->len) l = len + n;
@@ -987,9 +1246,9 @@ qora_status qora_generate_greedy(qora_engine* e, qora_kv* kv, uint32_t first_tok
     return fail(QORA_ERR_RANGE, "%u tokens after %u positions exceed max_seq %u", n_tokens, len, kv->max_seq);
   if (n_tokens == 0) return QORA_OK;
   QCUDA(cudaSetDevice(e->device));
-  QCHECK(ensure_graph(e, kv));
+  QCHECK(step_prepare(e, kv));
   QCHECK(set_state(e, kv, (int)len, (int)first_token, 0));
-  for (uint32_t i = 0; i < n_tokens; ++i) QCUDA(cudaGraphLaunch(kv->graph, e->stream));
+  for (uint32_t i = 0; i < n_tokens; ++i) QCHECK(step_launch(e, kv));
   QCUDA(cudaMemcpyAsync(out_tokens, kv->ring, (size_t)n_tokens * 4, cudaMemcpyDeviceToHost, e->stream));
   QCHECK(check_step_error(e, kv));
   for (auto& l : kv->len) l = len + n_tokens;
@@ -1021,18 +1280,18 @@ qora_status qora_generate_greedy_timed(qora_engine* e, qora_kv* kv, uint32_t fir
   if ((uint64_t)len + n_tokens > kv->max_seq)
     return fail(QORA_ERR_RANGE, "%u tokens after %u positions exceed max_seq %u", n_tokens, len, kv->max_seq);
   QCUDA(cudaSetDevice(e->device));
-  QCHECK(ensure_graph(e, kv));
+  QCHECK(step_prepare(e, kv));
   QCHECK(set_state(e, kv, (int)len, (int)first_token, 0));
   cudaEvent_t a = nullptr, b = nullptr;
   QCUDA(cudaEventCreate(&a));
   QCUDA(cudaEventCreate(&b));
   cudaEventRecord(a, e->stream);
   for (uint32_t i = 0; i < n_tokens; ++i) {
-    cudaError_t ce = cudaGraphLaunch(kv->graph, e->stream);
-    if (ce != cudaSuccess) {
+    const qora_status ls = step_launch(e, kv);
+    if (ls != QORA_OK) {
       cudaEventDestroy(a);
       cudaEventDestroy(b);
-      return fail(QORA_ERR_CUDA, "cudaGraphLaunch: %s", cudaGetErrorString(ce));
+      return ls;
     }
   }
   cudaEventRecord(b, e->stream);
@@ -1103,7 +1362,8 @@ qora_status qora_engine_time_kernel(qora_engine* e, qora_kv* kv, int kernel, uin
                            EpiResidual{e->x, (int)e->hidden}, s);
       default: {
         LmArgs la{};
-        la.x = e->x; la.gamma = e->final_gamma; la.packed = e->embed_packed; la.scales = e->embed_scales;
+        la.x = e->x; la.gamma = e->final_gamma; la.packed = e->lm_table; la.scales = e->lm_table + e->hidden / 2;
+        la.row_stride_p = la.row_stride_s = e->lm_row_bytes;
         la.vocab = (int)e->vocab; la.logits = e->logits; la.argmax_out = &kv->st->argmax;
         la.part_v = e->lm_part_v; la.part_i = e->lm_part_i; la.counter = e->lm_counter;
         return launch_lm_head((int)e->hidden, la, e->lm_ctas, s);
@@ -1133,9 +1393,33 @@ qora_status qora_engine_time_kernel(qora_engine* e, qora_kv* kv, int kernel, uin
   return QORA_OK;
 }
 
+qora_status qora_engine_set_trace(qora_engine* e, int enable) {
+  if (!e) return fail(QORA_ERR_INVALID, "NULL engine");
+  if (!e->mk_ok) return fail(QORA_ERR_UNSUPPORTED, "no persistent decode kernel: %s", e->mk_why.c_str());
+  QCUDA(cudaSetDevice(e->device));
+  if (enable && !e->mk_trace) {
+    e->mk_trace_n = (size_t)e->mk_G * (mk::kTracePerCta + mk::kTraceLayers + mk::kTraceFine);
+    QCHECK(e->alloc(&e->mk_trace, e->mk_trace_n));
+    QCUDA(cudaMemset(e->mk_trace, 0, e->mk_trace_n * 8));
+  }
+  unsigned long long* t = enable ? e->mk_trace : nullptr;
+  for (qora_kv* kv : e->kvs) kv->mk_args.trace = t;
+  return QORA_OK;
+}
+
+qora_status qora_engine_get_trace(qora_engine* e, uint64_t* out, size_t cap, size_t* n) {
+  if (!e || !n) return fail(QORA_ERR_INVALID, "NULL argument");
+  *n = e->mk_trace ? e->mk_trace_n : 0;
+  if (!e->mk_trace || !out) return QORA_OK;
+  QCUDA(cudaSetDevice(e->device));
+  QCUDA(cudaStreamSynchronize(e->stream));
+  QCUDA(cudaMemcpy(out, e->mk_trace, std::min(cap, e->mk_trace_n) * 8, cudaMemcpyDeviceToHost));
+  return QORA_OK;
+}
+
 qora_status qora_engine_launches_per_step(const qora_engine* e, uint32_t* launches) {
   if (!e || !launches) return fail(QORA_ERR_INVALID, "NULL argument");
-  *launches = 1 + 5 * e->num_layers + 2;
+  *launches = (e->mk_ok && e->use_mega) ? 1u : 1 + 5 * e->num_layers + 2;
   return QORA_OK;
 }
 
@@ -1204,7 +1488,9 @@ qora_status qora_q4_lm_head(const float* d_x, const uint8_t* d_packed, const uin
   a.x = d_x;
   a.gamma = nullptr;
   a.packed = d_packed;
-  a.scales = d_scales;
+  a.scales = reinterpret_cast<const uint8_t*>(d_scales);
+  a.row_stride_p = (long long)(hidden / 2);
+  a.row_stride_s = (long long)(hidden / kGroup * 2);
   a.vocab = (int)vocab;
   a.logits = d_logits;
   a.argmax_out = d_argmax;

@@ -5,21 +5,21 @@
 
 namespace qora {
 
-// embed_lookup_q4 (src/gemv.rs:710-736): x[e] = f32(scale) * (q - 8), exact.
-__global__ void embed_q4_kernel(const uint8_t* packed, const uint16_t* scales, int vocab,
+// embed_lookup_q4 (src/gemv.rs:710-736): x[e] = f32(scale) * (q - 8), exact. The table
+// is row-interleaved: row v = hidden/2 packed bytes followed by hidden/32 f16 scales.
+__global__ void embed_q4_kernel(const uint8_t* table, long long row_bytes, int vocab,
                                 int hidden, StepState* st, float* x) {
   const int token = st->token;
   if (token < 0 || token >= vocab) {
     if (threadIdx.x == 0) st->error = 1;
     return;
   }
-  const int gpr = hidden / kGroup;
+  const uint8_t* row = table + (long long)token * row_bytes;
+  const uint16_t* sc = reinterpret_cast<const uint16_t*>(row + hidden / 2);
   for (int e = threadIdx.x; e < hidden; e += blockDim.x) {
-    const int g = e / kGroup, j = e % kGroup;
-    const uint8_t b = packed[((long long)token * gpr + g) * 16 + j / 2];
-    const int q = ((j & 1) ? (b >> 4) : (b & 0xF)) - 8;
-    const float s = __half2float(__ushort_as_half(scales[(long long)token * gpr + g]));
-    x[e] = __fmul_rn(s, (float)q);
+    const uint8_t b = row[e / 2];
+    const int q = ((e & 1) ? (b >> 4) : (b & 0xF)) - 8;
+    x[e] = __fmul_rn(__half2float(__ushort_as_half(sc[e / kGroup])), (float)q);
   }
 }
 

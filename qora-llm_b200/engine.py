@@ -26,6 +26,8 @@ from .qora_format import Model
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libqora_cuda.so")
 
+FLAG_PER_OP_KERNELS = 1  # QORA_FLAG_PER_OP_KERNELS
+
 STATUS = {0: "OK", 1: "INVALID", 2: "IO", 3: "CUDA", 4: "OOM", 5: "RANGE", 6: "TIMEOUT",
           7: "UNSUPPORTED", 8: "NCCL"}
 
@@ -53,6 +55,8 @@ SIGNATURES = {
     "qora_engine_time_kernel": (C.c_int, [_vp, _vp, C.c_int, _u32, _P(C.c_float), _P(_u64),
                                           _P(_u32)]),
     "qora_engine_launches_per_step": (C.c_int, [_vp, _P(_u32)]),
+    "qora_engine_set_trace": (C.c_int, [_vp, C.c_int]),
+    "qora_engine_get_trace": (C.c_int, [_vp, _vp, C.c_size_t, _P(C.c_size_t)]),
     "qora_q4_gemv": (C.c_int, [_vp, _vp, _vp, _u64, _u64, _vp, _vp]),
     "qora_q4_dequant": (C.c_int, [_vp, _vp, _u64, _u64, _u64, _vp, _vp]),
     "qora_q4_gate_up": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _u64, _u64, _vp, _vp]),
@@ -97,8 +101,9 @@ class DecodeWeights:
     """An engine: the model resident on the GPU (the `DecodeWeights` of src/gemv.rs:195)."""
 
     def __init__(self, model: Optional[Model] = None, path: Optional[str] = None,
-                 device: int = 0, n_gpus: int = 1):
-        opts = abi.EngineOptions(n_gpus, device, 0)
+                 device: int = 0, n_gpus: int = 1, per_op_kernels: bool = False):
+        self.per_op_kernels = per_op_kernels
+        opts = abi.EngineOptions(n_gpus, device, FLAG_PER_OP_KERNELS if per_op_kernels else 0)
         h = C.c_void_p()
         if path is not None:
             check(lib().qora_engine_create_from_file(os.fsencode(path), C.byref(opts), C.byref(h)))
@@ -171,6 +176,17 @@ class DecodeWeights:
         check(lib().qora_engine_time_kernel(self.h, kv.h, self.KERNELS[kernel], int(reps),
                                             C.byref(ms), C.byref(nb), C.byref(nl)))
         return ms.value, nb.value, nl.value
+
+    def set_trace(self, on: bool = True):
+        """Record per-CTA phase timestamps of the persistent decode kernel."""
+        check(lib().qora_engine_set_trace(self.h, 1 if on else 0))
+
+    def get_trace(self) -> np.ndarray:
+        n = C.c_size_t()
+        check(lib().qora_engine_get_trace(self.h, None, 0, C.byref(n)))
+        out = np.zeros(n.value, np.uint64)
+        check(lib().qora_engine_get_trace(self.h, _ptr(out), out.size, C.byref(n)))
+        return out
 
     def launches_per_step(self) -> int:
         n = _u32()

@@ -25,9 +25,10 @@ def small(qf):
                           num_heads=8, num_kv_heads=2, head_dim=128, rope_rows=256)
 
 
-@pytest.fixture(scope="module")
-def small_engine(pkg, small):
-    w = pkg.DecodeWeights(model=small)
+@pytest.fixture(scope="module", params=["megakernel", "per_op_kernels"])
+def small_engine(request, pkg, small):
+    """Both decode paths: the persistent single-kernel step and the graph of per-op kernels."""
+    w = pkg.DecodeWeights(model=small, per_op_kernels=request.param == "per_op_kernels")
     yield w
     w.close()
 
@@ -116,7 +117,7 @@ def test_decode_step_matches_generate(small_engine):
 def test_file_engine_equals_view_engine(tmp_path, pkg, qf, small, small_engine):
     p = tmp_path / "small.qora"
     qf.write_qora(small, p)
-    wf = pkg.load_model(str(p))
+    wf = pkg.DecodeWeights(path=str(p), per_op_kernels=small_engine.per_op_kernels)
     ka, kb = small_engine.new_kv(16), wf.new_kv(16)
     for tok in (1, 2, 3):
         _, la = small_engine.decode_step(ka, tok, want_logits=True)
@@ -161,3 +162,26 @@ def test_deterministic(small_engine):
         outs.append([w.decode_step(kv, t, want_logits=True)[1] for t in (3, 1, 4, 1, 5)])
     for a, b in zip(*outs):
         assert np.array_equal(a, b)
+
+
+def test_paths_agree(pkg, small):
+    a = pkg.DecodeWeights(model=small)
+    b = pkg.DecodeWeights(model=small, per_op_kernels=True)
+    assert a.launches_per_step() == 1 and b.launches_per_step() > 1
+    ka, kb = a.new_kv(64), b.new_kv(64)
+    for tok in (7, 700, 70):
+        am, la = a.decode_step(ka, tok, want_logits=True)
+        bm, lb = b.decode_step(kb, tok, want_logits=True)
+        assert am == bm and rel_l2(la, lb) < 1e-5
+    a.close()
+    b.close()
+
+
+def test_engine_destroyed_before_cache(pkg, small):
+    w = pkg.DecodeWeights(model=small)
+    kv = w.new_kv(8)
+    w.decode_step(kv, 1)
+    w.close()  # the cache outlives its engine: it becomes inert, not dangling
+    with pytest.raises(pkg.QoraError, match="INVALID"):
+        kv.import_layer(0, np.zeros((1, 256), np.float32), np.zeros((1, 256), np.float32))
+    kv.close()
