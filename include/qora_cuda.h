@@ -174,6 +174,24 @@ qora_status qora_q4_gemv(const float* d_x, const uint8_t* d_packed,
                          const uint16_t* d_scales, uint64_t k, uint64_t n, float* d_y,
                          void* stream);
 
+/* The same Q4 GEMV with no allocation at all (no counterpart in the reference, which
+ * has no device memory): the split-K partial sums and arrival counters live in one
+ * fixed-size file-scope device array of the library (QORA_GEMV_STATIC_FLOATS floats
+ * of partials + QORA_GEMV_STATIC_TILES counters per device). For callers that must not
+ * allocate: a host that owns every byte of device memory up front (a serving process
+ * that pre-reserves HBM, an allocator-free embedding, code paths where a hidden
+ * cudaMalloc would synchronise the device). Shapes whose plan needs more scratch than
+ * the array holds are rejected with QORA_ERR_UNSUPPORTED. The first call on a device
+ * looks up the array's address (a one-time set-up step; make it before any stream
+ * capture). Every call shares the array: the counters start at zero and each call
+ * leaves them at zero, so calls must not overlap in time (concurrent calls on
+ * different streams of one device race on the shared partials). */
+#define QORA_GEMV_STATIC_FLOATS (512u * 1024u)
+#define QORA_GEMV_STATIC_TILES 1024u
+qora_status qora_q4_gemv_static(const float* d_x, const uint8_t* d_packed,
+                                const uint16_t* d_scales, uint64_t k, uint64_t n,
+                                float* d_y, void* stream);
+
 /* Bit-exact dequantisation of rows [row0, row0+rows) of a Q4 matrix to f32
  * ((q-8)*f32(scale), src/gemv.rs:727-731). d_out: rows*n floats. */
 qora_status qora_q4_dequant(const uint8_t* d_packed, const uint16_t* d_scales,

@@ -1440,6 +1440,49 @@ qora_status qora_q4_gemv(const float* d_x, const uint8_t* d_packed, const uint16
                      (cudaStream_t)stream);
 }
 
+// Scratch of qora_q4_gemv_static: QORA_GEMV_STATIC_FLOATS split-K partials followed by
+// QORA_GEMV_STATIC_TILES arrival counters (zero-initialised at module load; every
+// launch's last arriver of a tile puts its counter back to zero).
+static __device__ __align__(256) float g_gemv_static_scratch[QORA_GEMV_STATIC_FLOATS + QORA_GEMV_STATIC_TILES];
+constexpr int kStaticMaxDevices = 64;
+static std::mutex g_static_mu;
+static void* g_static_addr[kStaticMaxDevices] = {};
+
+qora_status qora_q4_gemv_static(const float* d_x, const uint8_t* d_packed, const uint16_t* d_scales,
+                                uint64_t k, uint64_t n, float* d_y, void* stream) {
+  if (!d_x || !d_packed || !d_scales || !d_y) return fail(QORA_ERR_INVALID, "NULL pointer");
+  if (k == 0 || n == 0 || n % kGroup || k > (1u << 30) || n > (1u << 30))
+    return fail(QORA_ERR_INVALID, "bad shape k=%llu n=%llu", (unsigned long long)k, (unsigned long long)n);
+  int dev = 0;
+  QCUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kStaticMaxDevices) return fail(QORA_ERR_UNSUPPORTED, "device ordinal %d", dev);
+  const Q4Src src = f1_src(d_packed, d_scales, (int)k, (int)n);
+  const GemvShape sh = plan_gemv((int)k, src.tiles, 2 * sm_count(dev));
+  if ((size_t)sh.tiles > QORA_GEMV_STATIC_TILES || partial_floats(sh) > QORA_GEMV_STATIC_FLOATS)
+    return fail(QORA_ERR_UNSUPPORTED,
+                "k=%llu n=%llu needs %zu partial floats and %d tile counters; the static scratch "
+                "holds %u and %u",
+                (unsigned long long)k, (unsigned long long)n, partial_floats(sh), sh.tiles,
+                QORA_GEMV_STATIC_FLOATS, QORA_GEMV_STATIC_TILES);
+  void* base = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_static_mu);
+    if (!g_static_addr[dev]) {
+      // one-time per device, with `dev` current: resolve the array's device address
+      void* p = nullptr;
+      const cudaError_t ce = cudaGetSymbolAddress(&p, g_gemv_static_scratch);
+      if (ce != cudaSuccess || !p)
+        return fail(QORA_ERR_CUDA, "cudaGetSymbolAddress: %s", cudaGetErrorString(ce));
+      g_static_addr[dev] = p;
+    }
+    base = g_static_addr[dev];
+  }
+  float* partials = static_cast<float*>(base);
+  unsigned* counters = reinterpret_cast<unsigned*>(partials + QORA_GEMV_STATIC_FLOATS);
+  return launch_gemv(src, sh, partials, counters, ProPlain{d_x}, EpiStore{d_y, (int)n},
+                     (cudaStream_t)stream);
+}
+
 qora_status qora_q4_dequant(const uint8_t* d_packed, const uint16_t* d_scales, uint64_t n,
                             uint64_t row0, uint64_t rows, float* d_out, void* stream) {
   if (!d_packed || !d_scales || !d_out) return fail(QORA_ERR_INVALID, "NULL pointer");

@@ -58,6 +58,7 @@ SIGNATURES = {
     "qora_engine_set_trace": (C.c_int, [_vp, C.c_int]),
     "qora_engine_get_trace": (C.c_int, [_vp, _vp, C.c_size_t, _P(C.c_size_t)]),
     "qora_q4_gemv": (C.c_int, [_vp, _vp, _vp, _u64, _u64, _vp, _vp]),
+    "qora_q4_gemv_static": (C.c_int, [_vp, _vp, _vp, _u64, _u64, _vp, _vp]),
     "qora_q4_dequant": (C.c_int, [_vp, _vp, _u64, _u64, _u64, _vp, _vp]),
     "qora_q4_gate_up": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _u64, _u64, _vp, _vp]),
     "qora_q4_lm_head": (C.c_int, [_vp, _vp, _vp, _u64, _u64, _vp, _vp, _vp]),
@@ -266,6 +267,11 @@ def _stream_ptr(stream):
 
 def q4_gemv(x_ptr, packed_ptr, scales_ptr, k, n, y_ptr, stream=None):
     check(lib().qora_q4_gemv(x_ptr, packed_ptr, scales_ptr, k, n, y_ptr, _stream_ptr(stream)))
+
+
+def q4_gemv_static(x_ptr, packed_ptr, scales_ptr, k, n, y_ptr, stream=None):
+    """qora_q4_gemv on the library's fixed static scratch (allocates nothing)."""
+    check(lib().qora_q4_gemv_static(x_ptr, packed_ptr, scales_ptr, k, n, y_ptr, _stream_ptr(stream)))
 
 
 def q4_dequant(packed_ptr, scales_ptr, n, row0, rows, out_ptr, stream=None):
