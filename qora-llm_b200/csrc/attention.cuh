@@ -15,8 +15,9 @@ constexpr int kGrp = 4;             // query heads per KV head (num_kv_groups)
 
 struct AttnArgs {
   const float* q;      // [nh * 128] (RoPE applied)
-  const float* kc;     // layer K cache [max_seq][nkv*128]
+  const float* kc;     // layer K cache, head-major [nkv][max_seq][128]
   const float* vc;
+  long long hs;        // head stride (max_seq * 128)
   float* out;          // [nh * 128]
   const StepState* st; // length = st->pos + 1 (the row appended by this step included)
   int nkv;             // KV heads in this cache
@@ -40,7 +41,6 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
   const int s0 = min(len, c * chunk);
   const int s1 = min(len, s0 + chunk);
   const int n = s1 - s0;
-  const int stride = a.nkv * kHeadDim;
 
   for (int i = tid; i < kGrp * kHeadDim; i += kAttnThreads)
     qs[i / kHeadDim][i % kHeadDim] = a.q[(j * kGrp) * kHeadDim + i];
@@ -48,7 +48,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
 
   // scores: warp w takes positions s0+w, s0+w+4, ...; lane covers dims 4*lane..4*lane+3
   for (int s = s0 + warp; s < s1; s += kAttnThreads / 32) {
-    const float4 k4 = __ldg(reinterpret_cast<const float4*>(a.kc + (long long)s * stride + j * kHeadDim) + lane);
+    const float4 k4 = __ldg(reinterpret_cast<const float4*>(a.kc + j * a.hs + (long long)s * kHeadDim) + lane);
 #pragma unroll
     for (int h = 0; h < kGrp; ++h) {
       const float4 q4 = *reinterpret_cast<const float4*>(&qs[h][lane * 4]);
@@ -86,9 +86,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
   {
     const int d = tid;
     float o[kGrp] = {0.0f, 0.0f, 0.0f, 0.0f};
-    const float* vp = a.vc + (long long)s0 * stride + j * kHeadDim + d;
+    const float* vp = a.vc + j * a.hs + (long long)s0 * kHeadDim + d;
     for (int i = 0; i < n; ++i) {
-      const float v = __ldg(vp + (long long)i * stride);
+      const float v = __ldg(vp + (long long)i * kHeadDim);
 #pragma unroll
       for (int h = 0; h < kGrp; ++h) o[h] = __fmaf_rn(sc[h][i], v, o[h]);
     }

@@ -10,19 +10,28 @@
 // needs, published by other CTAs through gpu-scope release/acquire counters. While
 // consumers wait on a dependency the producer keeps filling the ring.
 //
-// Per layer (CTA subsets in brackets; split-K partials in global memory):
-//   QKV  [last 48 CTAs] fused RMSNorm + q|k|v GEMV -> partials          (qkv_parts)
-//   ATTN [units]  each unit reduces the q (and, for the unit holding the new position,
-//        k/v) partials itself, applies RoPE, appends the KV row, attends over its
-//        chunk of positions (cached K/V rows stream through the ring) -> (m, l, o)
-//   O    [32 CTAs] merge the attention partials of the rows it needs, GEMV -> partials
-//   GU   [all] x_mid = x_in + sum of O partials (each CTA, full vector), RMSNorm,
-//        gate|up GEMV -> partials per tile                                (gu_arr[t])
-//   DOWN [all] SwiGLU of the rows it needs from the gate/up partials, GEMV; the last
-//        CTA of an output tile adds x_in + O partials + down partials -> x_out (dn_done)
+// Per layer (CTA sets in brackets):
+//   QKV  [one CTA per 32-column group of q|k|v] RMSNorm(x) . W over all rows -> final
+//        q|k|v values (before RoPE), no split-K                               (c_qkv)
+//   ATTN [one CTA per (kv head, chunk of positions)] RoPE on its 4 query heads (and,
+//        for the chunk holding the new position, on k, which it appends with v to the
+//        head-major cache), scores, softmax numerators, P.V -> (m, l, o)     (c_att)
+//   O    [one CTA per 32-column group of o_proj] merge the (m, l, o) partials of all
+//        heads, GEMV over all rows, x_mid = x + o for its columns            (c_o)
+//   GU   [all] RMSNorm(x_mid) . [gate|up], split-K over 256-column tiles -> partials
+//   DOWN [all] SwiGLU of its rows from the gate/up partials, split-K GEMV; the last CTA
+//        of an output tile writes x_next = x_mid + down for the tile      (dn_done)
 // then lm_head rows (a contiguous slice per CTA) with a fused first-maximum argmax.
-// QKV and O run on small disjoint subsets so that their few partials can be reduced by
-// the consumers directly, which removes a reduction hop from each of them.
+//
+// Instruction-cache discipline: B200's per-SM instruction cache holds ~60 KB of code
+// (measured: straight-line code runs at ~2.7 cycles per instruction up to 61 KB and
+// 4-11 beyond 76 KB), and a layer executes every phase once, so the code of one layer
+// must stay below that. Every phase is a separate non-inlined function taking only
+// scalars (the consumer state is rebuilt in registers; nothing lives in local memory,
+// whose L1 is a few KB next to this kernel's shared memory), all GEMVs share two
+// streaming loops, and non-critical loops are not unrolled. Every dependent global read
+// of a phase is issued as one batch, so a phase costs one L2 round trip, not one per
+// value; counters are polled with relaxed loads and one acquire fence.
 //
 // Every wait (dependency counter, stage barrier, ring slot) is bounded by a timeout; on
 // expiry the CTA records QORA_ERR_TIMEOUT in the step state, stops computing, drains the
@@ -41,39 +50,41 @@ namespace mk {
 constexpr int kCW = 15;                // consumer warps
 constexpr int kCT = kCW * 32;          // consumer threads
 constexpr int kThreads = kCT + 32;     // + one producer warp
-constexpr int kStageBytes = 17280;     // 120 tiled rows of 144 B = 15 embedding rows
-constexpr int kStageRows = kStageBytes / kTiledRowBytes;
+constexpr int kStageBytes = 17280;     // 960 one-group rows = 120 eight-group rows = 15 embedding rows
 constexpr int kStages = 11;
-constexpr int kMaxVItems = 2;          // (kv head, dim) items per thread in the P.V pass
-constexpr int kMaxAttnChunk = 192;
-constexpr int kMinAttnChunk = 16;
-constexpr int kMaxUnits = 256;         // attention units per step (merge weights buffer)
 constexpr int kBar = 1;                // named barrier of the consumer warps
-// shared scratch (floats): XS = inputs of this CTA's GEMV segments; B = x copy / merge
-// weights / cross-warp reduction; Y = a tile's 256 sums; MISC = small reductions
-constexpr int kXsCap = 1536;
-constexpr int kBFloats = kCW * kTileCols;       // 3840
+constexpr int kKVRows = kStageBytes / (kHeadDim * 4);  // K or V rows of one head per stage (33)
+constexpr int kMinAttnChunk = 64;
+constexpr int kMaxAttnChunk = 1024;
+constexpr int kMaxUnits = 256;         // attention units (kv head x chunk); units <= CTAs
+constexpr int kHeadsPerKV = 4;         // query heads per KV head (SmolLM3-3B: 16 / 4)
+// shared scratch (floats): XS = inputs of this CTA's GEMV (pre-scaled by 2^64); B = x
+// copy / cross-warp reduction / merge weights / epilogue parts; Y = a segment's reduced
+// sums; MISC = small reductions and tables; TAB = split-K slots per tile
+constexpr int kXsCap = 2048;
+constexpr int kXsPer = (kXsCap + kCT - 1) / kCT;  // xs entries per thread (5)
 constexpr int kOffB = kXsCap;
+constexpr int kBFloats = kCW * 256;
 constexpr int kOffY = kOffB + kBFloats;
-constexpr int kOffMisc = kOffY + kTileCols;
-constexpr int kScratchFloats = 6272;            // 24.5 KB
-// attention layout: q [2048] | scores [16][kMaxAttnChunk] | (m,l) [16][2] | new k,v rows
-constexpr int kAttQ = 0, kAttS = 2048, kAttML = kAttS + 16 * kMaxAttnChunk, kAttKV = kAttML + 32;
-static_assert(kOffMisc + 256 <= kScratchFloats, "scratch layout");
-static_assert(kAttKV + 1024 <= kScratchFloats, "attention scratch");
-static_assert(8 * kMaxUnits + 8 <= kBFloats, "merge weights");
-
-constexpr size_t smem_bytes() {
-  return (size_t)kStages * kStageBytes + (size_t)kScratchFloats * 4 + 2 * kStages * 8 + 64;
-}
+constexpr int kOffMisc = kOffY + 256;
+constexpr int kOffTab = kOffMisc + 64;
+constexpr int kMaxTabTiles = 128;
+constexpr int kScratchFloats = kOffTab + kMaxTabTiles;
+// attention (overlaps XS and B): q [4][128] | scores [4][kMaxAttnChunk] | (m,l) [4][2] | new k,v
+constexpr int kAttQ = 0, kAttS = 512, kAttML = kAttS + 4 * kMaxAttnChunk, kAttKV = kAttML + 8;
+constexpr int kDnParts = 7;            // down epilogue: partial sums of the slots, [7][64] float4
+static_assert(kAttKV + 256 <= kOffY, "attention scratch");
+static_assert(kDnParts * 64 * 4 <= kBFloats && kDnParts * 64 <= kCT, "down epilogue");
+constexpr float kTwo64 = 18446744073709551616.0f;
 
 enum Mat { QKV = 0, OPR = 1, GU = 2, DOWN = 3 };
 
 struct Layer {
-  const uint8_t* w[4];  // tile-major Q4: q|k|v, o, gate/up (interleaved per 128), down
+  const uint8_t* w[4];  // QKV, OPR: one-group tiles [group][K/8][8 rows x 16 B | 8 scales];
+                        // GU, DOWN: eight-group tiles [tile][K][8 groups x 16 B | 8 scales]
   const float* g_in;
   const float* g_post;
-  float* kc;            // K cache [max_seq][nkvw]
+  float* kc;            // K cache, head-major [kv head][max_seq][128]
   float* vc;
   int rope;
   int pad;
@@ -83,21 +94,22 @@ struct Args {
   const Layer* layers;
   int L;
   int K[4], tiles[4], slots[4];
-  int sub0[4], subn[4];       // CTA subset [sub0, sub0+subn) that runs each matrix
-  int segs[4];                // segments (CTA x tile pieces) of each matrix
-  int H, I, nq, nkvw, nh, nkvh, grp, vocab;
+  int sub0[4], subn[4];       // CTA set [sub0, sub0+subn) that runs each matrix
+  int H, nq, nkvw, nh, nkvh, vocab;
   int lm_row_bytes, lm_rows_per_stage;
+  long long head_stride;      // floats between KV heads of a layer's cache (max_seq * 128)
   const uint8_t* lm;          // [vocab][H/2 packed | H/16 scales]
   const float* final_gamma;
   const float* cos_t;
   const float* sin_t;
   int max_pos;                // positions the KV cache (and RoPE table) can hold
-  float* xbuf;                // [L+1][H] residual stream (x_0 = embedding, x_{L+1} = out)
+  float* xbuf;                // [L+1][H] residual stream into each layer (x_0 = embedding)
+  float* xmid;                // [L][H] residual after attention
+  float* qkv;                 // [nq + 2 nkvw] this step's q|k|v (before RoPE)
   float* logits;              // [vocab]
-  float* part[4];             // split-K partials [tiles][slots][256]
-  float* att_o;               // [max_units][nh][128]
-  float* att_ml;              // [max_units][nh][2]
-  int max_units;
+  float* part[4];             // GU, DOWN split-K partials [tiles][slots][256]
+  float* att_o;               // [kMaxUnits][4][128]
+  float* att_ml;              // [kMaxUnits][4][2]
   unsigned* cnt;              // dependency counters, zero between launches
   int cpl;                    // counters per layer
   int n_cnt;
@@ -110,186 +122,221 @@ struct Args {
   unsigned long long* trace;  // optional phase timestamps, or nullptr
 };
 
+constexpr size_t smem_bytes() {
+  return (size_t)kStages * kStageBytes + (size_t)kScratchFloats * 4 + 2 * kStages * 8 + 64 +
+         ((sizeof(Args) + 15) / 16) * 16;
+}
+
+// Dynamic shared memory: ring | scratch | full[kStages] | empty[kStages] | flags[16] | Args
+extern __shared__ __align__(128) uint8_t g_mk_smem[];
+QORA_DEV float* sm_scratch() { return reinterpret_cast<float*>(g_mk_smem + (size_t)kStages * kStageBytes); }
+QORA_DEV uint64_t* sm_full() { return reinterpret_cast<uint64_t*>(sm_scratch() + kScratchFloats); }
+QORA_DEV uint64_t* sm_empty() { return sm_full() + kStages; }
+QORA_DEV volatile int* sm_flags() { return reinterpret_cast<volatile int*>(sm_empty() + kStages); }
+QORA_DEV Args* sm_args() { return reinterpret_cast<Args*>(reinterpret_cast<uint8_t*>(sm_empty() + kStages) + 64); }
+// flags: [0] abort, [1] last-arriver, [2] pos, [3] chunks issued, [4] producer done,
+// [5] token, [6] fine-trace counter, [7] current layer
+
 // Trace layout: per CTA kTracePerCta u64 globaltimer stamps written by consumer thread 0:
-// [0] start, [1] after embedding, then per layer L at 2 + 8L + {0: x ready, 1: QKV done,
-// 2: attention done, 3: attention partials ready, 4: O done, 5: x_mid ready, 6: GU done,
-// 7: DOWN done}, then [2+8*kTraceLayers] lm start, [+1] end. Then, per CTA, one stamp per
-// layer when the producer has issued that layer's last copy; then kTraceFine stamps of
-// layer 1 at finer points (stages, barriers) per CTA.
+// [0] start, [1] after embedding, then per layer L at 2 + 8L + {0: x ready (QKV CTAs),
+// 1: QKV done, 2: attention done, 3: attention partials ready (O CTAs), 4: O done,
+// 5: x_mid ready, 6: GU done, 7: DOWN done}, then [2+8*kTraceLayers] lm start, [+1] end.
+// Then, per CTA, one stamp per layer when the producer has issued that layer's last
+// copy; then kTraceFine stamps of layer 1 at finer points (stages, barriers) per CTA.
 constexpr int kTraceLayers = 64;
 constexpr int kTracePerCta = 2 + 8 * kTraceLayers + 2;
 constexpr int kTraceFine = 64;
-QORA_DEV void stamp(const Args& a, int c, int idx) {
-  if (a.trace && threadIdx.x == 0) a.trace[(long long)c * kTracePerCta + idx] = ptx::globaltimer();
-}
 
-// ---- counter layout (per layer L) ----
-QORA_DEV int c_qkv_parts(const Args& a, int L) { return L * a.cpl + 0; }
-QORA_DEV int c_att(const Args& a, int L) { return L * a.cpl + 1; }
-QORA_DEV int c_o_parts(const Args& a, int L) { return L * a.cpl + 2; }
+// ---- counter layout (per layer L)
+QORA_DEV int c_qkv(const Args& a, int L) { return L * a.cpl + 0; }   // QKV groups done
+QORA_DEV int c_att(const Args& a, int L) { return L * a.cpl + 1; }   // attention units done
+QORA_DEV int c_o(const Args& a, int L) { return L * a.cpl + 2; }     // O groups done
 QORA_DEV int c_gu_arr(const Args& a, int L, int t) { return L * a.cpl + 3 + t; }
 QORA_DEV int c_dn_arr(const Args& a, int L, int t) { return L * a.cpl + 3 + a.tiles[GU] + t; }
 QORA_DEV int c_dn_done(const Args& a, int L) { return L * a.cpl + 3 + a.tiles[GU] + a.tiles[DOWN]; }
 QORA_DEV int c_lm(const Args& a) { return a.L * a.cpl; }
 
-QORA_DEV void attn_plan(int len, int G, int& chunk, int& nu) {
-  chunk = (len + G - 1) / G;
+// Attention units: (kv head, chunk of `chunk` positions), about one unit per CTA.
+QORA_DEV void attn_plan(int len, int G, int nkvh, int& chunk, int& nch) {
+  chunk = (len * nkvh + G - 1) / G;
   chunk = max(kMinAttnChunk, min(kMaxAttnChunk, chunk));
-  nu = (len + chunk - 1) / chunk;
+  nch = (len + chunk - 1) / chunk;
 }
 
-// split-K slots of tile t of matrix m (its subset's CTAs whose range touches the tile)
-QORA_DEV int nslots(const Args& a, int m, int t) {
-  const long long K = a.K[m], total = (long long)a.tiles[m] * K;
-  const int g = a.subn[m];
-  return owner_cta((long long)(t + 1) * K - 1, total, g) - owner_cta((long long)t * K, total, g) + 1;
-}
+// ---- split-K geometry (32-bit: the host checks set size x tiles x K < 2^31)
+// CTA lc of a g-CTA set owns rows [lc*T/g, (lc+1)*T/g) of the tiles*K flattened rows
+QORA_DEV int owner32(unsigned p, unsigned total, unsigned g) { return (int)(((p + 1u) * g - 1u) / total); }
 
-// Sum of the split-K partials of output o of tile t (slot order: deterministic).
-QORA_DEV float sum_slots(const Args& a, int m, int t, int o) {
-  const float* p = a.part[m] + (long long)t * a.slots[m] * kTileCols + o;
-  const int ns = nslots(a, m, t);
-  float s = 0.0f;
-#pragma unroll 4
-  for (int k = 0; k < ns; ++k) s += __ldcg(p + (long long)k * kTileCols);
-  return s;
-}
-
-// Shared state of one CTA.
-struct Smem {
-  uint8_t* ring;
-  float* scratch;
-  uint64_t* full;
-  uint64_t* empty;
-  volatile int* flags;  // [0] abort, [1] last-arriver, [3] chunks issued, [4] producer done
+struct Span {
+  int lin0, n;
 };
-
-QORA_DEV Smem carve(uint8_t* base) {
-  Smem s;
-  s.ring = base;
-  s.scratch = reinterpret_cast<float*>(base + (size_t)kStages * kStageBytes);
-  s.full = reinterpret_cast<uint64_t*>(base + (size_t)kStages * kStageBytes + kScratchFloats * 4);
-  s.empty = s.full + kStages;
-  s.flags = reinterpret_cast<volatile int*>(s.empty + kStages);
-  return s;
+QORA_DEV Span span_of(const Args& a, int m, int c) {
+  const int lc = c - a.sub0[m];
+  const unsigned g = (unsigned)a.subn[m];
+  if (lc < 0 || lc >= (int)g) return Span{0, 0};
+  const unsigned total = (unsigned)a.tiles[m] * (unsigned)a.K[m];
+  const unsigned l0 = (unsigned)lc * total / g, l1 = (unsigned)(lc + 1) * total / g;
+  return Span{(int)l0, (int)(l1 - l0)};
 }
 
-// Segments of CTA c in the flattened (tile, row) space of matrix m: f(t, r0, r1, slot).
+QORA_DEV int nslots(const Args& a, int m, int t) {
+  const unsigned K = (unsigned)a.K[m], total = (unsigned)a.tiles[m] * K, g = (unsigned)a.subn[m];
+  return owner32((unsigned)(t + 1) * K - 1u, total, g) - owner32((unsigned)t * K, total, g) + 1;
+}
+
+QORA_DEV int row_bytes(int m) { return m < GU ? 18 : 144; }
+
+// tile pieces of CTA c's span: f(t, r0, r1)
 template <class F>
-QORA_DEV void for_each_segment(const Args& a, int m, int c, F&& f) {
-  const int lc = c - a.sub0[m], g = a.subn[m];
-  if (lc < 0 || lc >= g) return;
-  const long long K = a.K[m], total = (long long)a.tiles[m] * K;
-  const long long lin0 = (long long)lc * total / g, lin1 = (long long)(lc + 1) * total / g;
-  for (long long p = lin0; p < lin1;) {
-    const long long t = p / K, r0 = p - t * K;
-    const long long pe = min(lin1, (t + 1) * K);
-    const int slot = lc - owner_cta(t * K, total, g);
-    f((int)t, (int)r0, (int)(pe - t * K), slot);
+QORA_DEV void for_each_seg(const Args& a, int m, int c, F&& f) {
+  const Span sp = span_of(a, m, c);
+  const int K = a.K[m];
+  for (int p = sp.lin0, e = sp.lin0 + sp.n; p < e;) {
+    const int t = p / K, r0 = p - t * K, pe = min(e, (t + 1) * K);
+    f(t, r0, pe - t * K);
     p = pe;
   }
 }
 
-// ------------------------------------------------------------------ the chunk sequence
+QORA_DEV float4 f4add(float4 a, float4 b) {
+  return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
+}
+QORA_DEV float4 ldcg4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
+
+// ------------------------------------------------------------------ the producer
 // The producer walks exactly this sequence of (source, bytes) copies; the consumers
 // consume the same sequence in the same order (see the phases below).
-template <class F, class E>
-QORA_DEV void for_each_chunk(const Args& a, int c, int G, int pos, F&& f, E&& layer_end) {
-  const int len = pos + 1;
-  int chunk, nu;
-  attn_plan(len, G, chunk, nu);
-  const int kvrow = a.nkvw * 4;
-  const int kv_rows_stage = kStageBytes / kvrow;
-  auto gemv = [&](int m, int L) {
-    const uint8_t* base = a.layers[L].w[m];
-    const long long K = a.K[m];
-    for_each_segment(a, m, c, [&](int t, int r0, int r1, int) {
-      for (int r = r0; r < r1; r += kStageRows) {
-        const int n = min(kStageRows, r1 - r);
-        f(base + ((long long)t * K + r) * kTiledRowBytes, (uint32_t)(n * kTiledRowBytes));
-      }
-    });
-  };
-  for (int L = 0; L < a.L; ++L) {
-    gemv(QKV, L);
-    for (int u = c; u < nu; u += G) {
-      const int s0 = u * chunk, s1 = min(len, s0 + chunk), sc1 = min(s1, pos);
-      for (int kvs = 0; kvs < 2; ++kvs) {
-        const float* src = kvs ? a.layers[L].vc : a.layers[L].kc;
-        for (int s = s0; s < sc1; s += kv_rows_stage) {
-          const int n = min(kv_rows_stage, sc1 - s);
-          f(reinterpret_cast<const uint8_t*>(src + (long long)s * a.nkvw), (uint32_t)(n * kvrow));
-        }
+constexpr uint32_t kDead = 0xFFFFFFFFu;  // producer state after an abort: issue nothing
+
+// one bulk copy into the next ring slot (bounded wait for the slot to be released);
+// returns the next chunk index, or kDead once the CTA has given up
+__device__ __noinline__ uint32_t issue(const uint8_t* src, uint32_t bytes, uint32_t chunk) {
+  if (chunk == kDead) return kDead;
+  volatile int* flags = sm_flags();
+  uint64_t* full = sm_full();
+  uint64_t* empty = sm_empty();
+  const uint32_t s = chunk % kStages;
+  const uint32_t parity = ((chunk / kStages) & 1u) ^ 1u;
+  if (!ptx::mbar_try_wait(&empty[s], parity)) {
+    const uint64_t t0 = ptx::globaltimer();
+    while (!ptx::mbar_try_wait(&empty[s], parity)) {
+      if (flags[0] != 0) return kDead;  // consumers gave up: stop issuing
+      if (ptx::globaltimer() - t0 > sm_args()->timeout_ns) {
+        flags[0] = 1;
+        atomicExch(&sm_args()->st->error, 2);
+        return kDead;
       }
     }
-    gemv(OPR, L);
-    gemv(GU, L);
-    gemv(DOWN, L);
-    layer_end(L);
   }
-  const long long v0 = (long long)c * a.vocab / G, v1 = (long long)(c + 1) * a.vocab / G;
-  for (long long r = v0; r < v1; r += a.lm_rows_per_stage) {
-    const long long n = min((long long)a.lm_rows_per_stage, v1 - r);
-    f(a.lm + r * a.lm_row_bytes, (uint32_t)(n * a.lm_row_bytes));
-  }
+  ptx::mbar_arrive_expect_tx(&full[s], bytes);
+  ptx::bulk_g2s(g_mk_smem + (size_t)s * kStageBytes, src, bytes, &full[s]);
+  flags[3] = (int)(chunk + 1);  // copies issued (drain() waits for the last ones)
+  return chunk + 1;
 }
 
-// ------------------------------------------------------------------ consumer helpers
-struct Cons {
-  const Args& a;
-  Smem sm;
-  int c, G, tid, lane, warp, pos, token;
-  int layer = 0;
-  int fine = 0;
-  uint32_t chunk = 0;
-  uint32_t stage_idx = 0;
-  bool stage_ok = false;  // warp-uniform: the current stage landed and the CTA is healthy
+__device__ __noinline__ uint32_t produce_gemv(int m, int L, uint32_t chunk) {
+  const Args& a = *sm_args();
+  const uint8_t* base = a.layers[L].w[m];
+  const int rb = row_bytes(m), rps = kStageBytes / rb;
+  const long long K = a.K[m];
+  for_each_seg(a, m, blockIdx.x, [&](int t, int r0, int r1) {
+#pragma unroll 1
+    for (int r = r0; r < r1; r += rps)
+      chunk = issue(base + ((long long)t * K + r) * rb, (uint32_t)(min(rps, r1 - r) * rb), chunk);
+  });
+  return chunk;
+}
 
+// the cached K rows, then V rows, of this CTA's attention unit (if it has one)
+__device__ __noinline__ uint32_t produce_kv(int L, uint32_t chunk) {
+  const Args& a = *sm_args();
+  const int c = blockIdx.x, pos = sm_flags()[2], len = pos + 1;
+  int csz, nch;
+  attn_plan(len, gridDim.x, a.nkvh, csz, nch);
+  if (c >= a.nkvh * nch) return chunk;
+  const int g = c % a.nkvh, s0 = (c / a.nkvh) * csz, sc1 = min(min(len, s0 + csz), pos);
+#pragma unroll 1
+  for (int kvs = 0; kvs < 2; ++kvs) {
+    const float* src = (kvs ? a.layers[L].vc : a.layers[L].kc) + g * a.head_stride;
+#pragma unroll 1
+    for (int s = s0; s < sc1; s += kKVRows)
+      chunk = issue(reinterpret_cast<const uint8_t*>(src + (long long)s * kHeadDim),
+                    (uint32_t)(min(kKVRows, sc1 - s) * kHeadDim * 4), chunk);
+  }
+  return chunk;
+}
+
+__device__ __noinline__ uint32_t produce_lm(uint32_t chunk) {
+  const Args& a = *sm_args();
+  const int c = blockIdx.x, G = gridDim.x;
+  const int v0 = (int)((long long)c * a.vocab / G), v1 = (int)((long long)(c + 1) * a.vocab / G);
+#pragma unroll 1
+  for (int r = v0; r < v1; r += a.lm_rows_per_stage)
+    chunk = issue(a.lm + (long long)r * a.lm_row_bytes,
+                  (uint32_t)(min(a.lm_rows_per_stage, v1 - r) * a.lm_row_bytes), chunk);
+  return chunk;
+}
+
+// ------------------------------------------------------------------ consumer state
+// fine-grained trace stamp of layer 1 (thread 0, tracing enabled)
+__device__ __noinline__ void fstamp_write() {
+  volatile int* flags = sm_flags();
+  const int fine = flags[6];
+  if (fine < kTraceFine)
+    sm_args()->trace[(long long)gridDim.x * (kTracePerCta + kTraceLayers) + (long long)blockIdx.x * kTraceFine +
+                     fine] = ptx::globaltimer();
+  flags[6] = fine + 1;
+}
+
+struct Cons {
+  const Args* ap;         // shared-memory copy of the kernel arguments
+  uint8_t* ring;
+  float* scratch;
+  uint64_t* full;
+  uint64_t* empty;
+  volatile int* flags;
+  int c, G, tid, lane, warp, pos;
+  uint32_t chunk;
+  uint32_t stage_idx;
+  bool stage_ok;          // warp-uniform: the current stage landed and the CTA is healthy
+
+  QORA_DEV const Args& a() const { return *ap; }
+  QORA_DEV int ns(int m, int t) const {  // split-K slots of tile t (GU, DOWN)
+    return reinterpret_cast<const int*>(scratch + kOffTab)[(m == GU ? 0 : ap->tiles[GU]) + t];
+  }
   // consistent across the consumer warps between named barriers
-  QORA_DEV bool aborted() const { return sm.flags[0] != 0; }
+  QORA_DEV bool aborted() const { return flags[0] != 0; }
   // uniform within the calling warp at any point
-  QORA_DEV bool aborted_w() const { return __shfl_sync(0xffffffffu, sm.flags[0] != 0, 0); }
+  QORA_DEV bool aborted_w() const { return __shfl_sync(0xffffffffu, flags[0] != 0, 0); }
 
   QORA_DEV void set_abort(int code) {
-    sm.flags[0] = 1;
-    atomicExch(&a.st->error, code);
+    flags[0] = 1;
+    atomicExch(&ap->st->error, code);
   }
 
   QORA_DEV void bar() { ptx::named_bar(kBar, kCT); }
 
-  // barrier that also agrees on the abort state: every consumer gets the same answer, so
-  // it may gate code that contains further barriers (the producer can raise the flag at
-  // any time, so a plain read after a barrier is not enough)
-  QORA_DEV bool sync_aborted() {
-    const int v = sm.flags[0] != 0;
-    int r;
-    asm volatile(
-        "{\n .reg .pred p;\n setp.ne.s32 p, %1, 0;\n bar.red.or.pred p, 1, %2, p;\n"
-        " selp.s32 %0, 1, 0, p;\n}\n"
-        : "=r"(r)
-        : "r"(v), "r"(kCT)
-        : "memory");
-    return r != 0;
+  QORA_DEV void stamp(int idx) {
+    if (ap->trace && tid == 0) ap->trace[(long long)c * kTracePerCta + idx] = ptx::globaltimer();
   }
 
   QORA_DEV void fstamp() {
-    if (a.trace && layer == 1 && tid == 0 && fine < kTraceFine)
-      a.trace[(long long)G * (kTracePerCta + kTraceLayers) + (long long)c * kTraceFine + fine] =
-          ptx::globaltimer();
-    if (layer == 1) ++fine;
+    if (tid == 0 && flags[7] == 1 && ap->trace) fstamp_write();
   }
 
-  // thread 0 spins (bounded) until *p >= target; no barrier
+  // thread 0 spins (bounded) until *p >= target, then an acquire fence; no barrier
   QORA_DEV void spin_ge(const unsigned* p, unsigned target) {
     if (aborted()) return;
-    if (ptx::ld_acquire(p) >= target) return;
-    const uint64_t t0 = ptx::globaltimer();
-    while (ptx::ld_acquire(p) < target) {
-      if (ptx::globaltimer() - t0 > a.timeout_ns) {
-        set_abort(2);
-        return;
+    if (ptx::ld_relaxed(p) < target) {
+      const uint64_t t0 = ptx::globaltimer();
+      while (ptx::ld_relaxed(p) < target) {
+        if (ptx::globaltimer() - t0 > ap->timeout_ns) {
+          set_abort(2);
+          return;
+        }
       }
     }
+    ptx::fence_acq_rel_gpu();
   }
 
   // thread 0 waits until *p >= target; all consumers then see the outcome
@@ -305,13 +352,13 @@ struct Cons {
     const uint32_t parity = (chunk / kStages) & 1u;
     if (aborted_w()) {
       stage_ok = false;
-      return sm.ring;
+      return ring;
     }
     bool timed_out = false;
-    if (!ptx::mbar_try_wait(&sm.full[stage_idx], parity)) {
+    if (!ptx::mbar_try_wait(&full[stage_idx], parity)) {
       const uint64_t t0 = ptx::globaltimer();
-      while (!ptx::mbar_try_wait(&sm.full[stage_idx], parity)) {
-        if (ptx::globaltimer() - t0 > a.timeout_ns) {
+      while (!ptx::mbar_try_wait(&full[stage_idx], parity)) {
+        if (ptx::globaltimer() - t0 > ap->timeout_ns) {
           timed_out = true;
           break;
         }
@@ -319,38 +366,18 @@ struct Cons {
     }
     stage_ok = __all_sync(0xffffffffu, !timed_out);
     if (!stage_ok && lane == 0) set_abort(2);
-    return sm.ring + (size_t)stage_idx * kStageBytes;
+    return ring + (size_t)stage_idx * kStageBytes;
   }
 
   QORA_DEV void release_stage() {
     __syncwarp();
-    if (lane == 0 && stage_ok) ptx::mbar_arrive(&sm.empty[stage_idx]);
+    if (lane == 0 && stage_ok) ptx::mbar_arrive(&empty[stage_idx]);
     ++chunk;
-  }
-
-  // After an abort: wait (bounded) for the producer to stop and for the copies it issued
-  // last to land, so that no bulk copy targets this CTA's shared memory after it exits.
-  QORA_DEV void drain() {
-    bar();
-    if (tid == 0 && aborted()) {
-      const uint64_t t0 = ptx::globaltimer();
-      while (sm.flags[4] == 0 && ptx::globaltimer() - t0 < a.timeout_ns) {
-      }
-      const uint32_t issued = (uint32_t)sm.flags[3];
-      const uint32_t first = issued > (uint32_t)kStages ? issued - kStages : 0u;
-      for (uint32_t j = first; j < issued; ++j) {
-        const uint64_t t1 = ptx::globaltimer();
-        while (!ptx::mbar_try_wait(&sm.full[j % kStages], (j / kStages) & 1u) &&
-               ptx::globaltimer() - t1 < a.timeout_ns) {
-        }
-      }
-    }
-    bar();
   }
 
   // block sum over consumer threads (fixed order), result in every thread
   QORA_DEV float csum(float v) {
-    float* red = sm.scratch + kOffMisc;
+    float* red = scratch + kOffMisc;
     v = warp_sum(v);
     if (lane == 0) red[warp] = v;
     bar();
@@ -367,73 +394,119 @@ struct Cons {
   }
 };
 
-QORA_DEV void load_vec(Cons& C, float* dst, const float* src, int n) {
-  for (int i = C.tid; i < n; i += kCT) dst[i] = __ldcg(src + i);
+// the consumer view of this CTA, rebuilt in registers by every phase (phases take only
+// scalars: nothing of the consumer state lives in local memory)
+QORA_DEV Cons make_cons(uint32_t chunk) {
+  Cons C;
+  C.ap = sm_args();
+  C.ring = g_mk_smem;
+  C.scratch = sm_scratch();
+  C.full = sm_full();
+  C.empty = sm_empty();
+  C.flags = sm_flags();
+  C.c = blockIdx.x;
+  C.G = gridDim.x;
+  C.tid = threadIdx.x;
+  C.lane = threadIdx.x & 31;
+  C.warp = threadIdx.x >> 5;
+  C.pos = C.flags[2];
+  C.chunk = chunk;
+  C.stage_idx = 0;
+  C.stage_ok = false;
+  return C;
 }
 
-QORA_DEV float rms_inv_of(Cons& C, const float* sx, int H) {
-  float s = 0.0f;
-  for (int i = C.tid; i < H; i += kCT) s = __fmaf_rn(sx[i], sx[i], s);
-  const float tot = C.csum(s);
-  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)H), 1e-6f)));
+QORA_DEV float rms_inv_from(float sumsq, int H) {
+  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sumsq, (float)H), 1e-6f)));
 }
 
-// x_mid = x_in + (sum of the O partials) for every column, into shared memory sx
-QORA_DEV void build_x_mid(Cons& C, float* sx, const float* x_in, int H) {
-  const Args& a = C.a;
-  for (int i = C.tid; i < H; i += kCT) {
-    const float xi = __ldcg(x_in + i);
-    sx[i] = __fadd_rn(xi, sum_slots(a, OPR, i / kTileCols, i % kTileCols));
+// x (H floats, global) -> sB (shared) as float4, returns this thread's sum of squares
+QORA_DEV float load_x(const Cons& C, float* sB, const float* x, int H) {
+  float ss = 0.0f;
+#pragma unroll 1
+  for (int b = C.tid; b < H / 4; b += kCT) {
+    const float4 v = ldcg4(x + 4 * b);
+    reinterpret_cast<float4*>(sB)[b] = v;
+    ss = __fmaf_rn(v.x, v.x, ss);
+    ss = __fmaf_rn(v.y, v.y, ss);
+    ss = __fmaf_rn(v.z, v.z, ss);
+    ss = __fmaf_rn(v.w, v.w, ss);
+  }
+  return ss;
+}
+
+// Rows of this thread's xs entries i = tid + j*kCT of a span: (lin0 + i) mod K, stepped
+// without divisions (kCT < K for every matrix).
+QORA_DEV int row_next(int r, int K) {
+  r += kCT;
+  return r >= K ? r - K : r;
+}
+
+QORA_DEV void prefetch_gains(const Cons& C, const float* g, Span sp, int K, float (&gam)[kXsPer]) {
+  int r = (sp.lin0 + C.tid) % K;
+#pragma unroll
+  for (int j = 0; j < kXsPer; ++j, r = row_next(r, K)) gam[j] = (C.tid + j * kCT < sp.n) ? __ldg(g + r) : 0.0f;
+}
+
+// xs[i] = x[row] * inv * gamma[row] * 2^64 for the span's rows (gains prefetched)
+QORA_DEV void fill_norm_inputs(const Cons& C, const float* sB, float inv, const float (&gam)[kXsPer], Span sp,
+                               int K) {
+  float* xs = C.scratch;
+  int r = (sp.lin0 + C.tid) % K;
+#pragma unroll
+  for (int j = 0; j < kXsPer; ++j, r = row_next(r, K)) {
+    const int i = C.tid + j * kCT;
+    if (i < sp.n) xs[i] = __fmul_rn(__fmul_rn(sB[r], inv), gam[j]) * kTwo64;
   }
 }
 
-// One GEMV phase for this CTA (nothing if the CTA is outside the matrix's subset).
-// pro(t, r0, r1, xs) fills xs[0..r1-r0) with the inputs of rows r0..r1 of one segment
-// (it may wait and use barriers; every consumer calls it); all segments' inputs are
-// prepared before streaming. After each segment's partial is stored, done(t, slot)
-// runs on every consumer (it publishes the partial / detects the last arriver).
-template <class Pro, class Done>
-QORA_DEV void gemv_phase(Cons& C, int m, int L, Pro&& pro, Done&& done) {
-  const Args& a = C.a;
-  float* xs = C.sm.scratch;
-  float* red = C.sm.scratch + kOffB;
-  const int gi = C.lane & 7, sub = C.lane >> 3;
-  const float kX = 18446744073709551616.0f;  // 2^64
+// ------------------------------------------------------------------ phases
+__device__ __noinline__ void seg_done(int m, int L, int t, int slot);
 
-  // 1) inputs of every segment
-  int n_in = 0;
-  for_each_segment(a, m, C.c, [&](int t, int r0, int r1, int) {
-    C.fstamp();
-    if (!C.sync_aborted()) pro(t, r0, r1, xs + n_in);
-    n_in += r1 - r0;
-  });
-  if (n_in == 0) return;  // CTA not in this matrix's subset (uniform)
-  C.bar();
-  for (int i = C.tid; i < n_in; i += kCT) xs[i] *= kX;
-  C.bar();
-  C.fstamp();
-
-  // 2) stream and accumulate
+// Stream this CTA's segments of matrix m (TG groups per tile) through the ring and
+// reduce each segment's 32*TG sums into Y, then run seg_done. xs holds the (pre-scaled)
+// inputs of all segments back to back. Lane (sub, gi) takes group gi of rows sub and
+// sub + 15*(32/TG) of each warp's share of a stage.
+template <int TG>
+__device__ __noinline__ uint32_t gemv_stream(int m, int L, uint32_t chunk) {
+  constexpr int W = 32 / TG;        // rows per warp pass
+  constexpr int RPS = kStageBytes / (18 * TG);  // rows per stage
+  static_assert(TG == 1 || TG == 8, "tile width");
+  Cons C = make_cons(chunk);
+  const Args& a = C.a();
+  const float* xs = C.scratch;
+  float* red = C.scratch + kOffB;
+  float* y = C.scratch + kOffY;
+  const int gi = C.lane % TG, sub = C.lane / TG;
+  const Span sp = span_of(a, m, C.c);
+  const int K = a.K[m], lc = C.c - a.sub0[m];
+  const unsigned total = (unsigned)a.tiles[m] * (unsigned)K;
   int off = 0;
-  for_each_segment(a, m, C.c, [&](int t, int r0, int r1, int slot) {
+#pragma unroll 1
+  for (int p = sp.lin0, e = sp.lin0 + sp.n; p < e;) {
+    const int t = p / K, r0 = p - t * K, r1 = min(e, (t + 1) * K) - t * K;
+    const int slot = lc - owner32((unsigned)t * K, total, (unsigned)a.subn[m]);
     float2 acc[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) acc[i] = make_float2(0.0f, 0.0f);
     float cs = 0.0f;
-    for (int cr = r0; cr < r1; cr += kStageRows) {
+#pragma unroll 1
+    for (int cr = r0; cr < r1; cr += RPS) {
       const uint8_t* stg = C.acquire_stage();
-      const int R = min(kStageRows, r1 - cr);
+      const int R = min(RPS, r1 - cr);
       if (C.stage_ok) {
         const float* xr = xs + off + (cr - r0);
-        // two rows per lane per stage, both rows' loads issued before the math
-        const int i0 = C.warp * 4 + sub, i1 = i0 + kCW * 4;
+        const int i0 = C.warp * W + sub, i1 = i0 + kCW * W;
         const bool v0 = i0 < R, v1 = i1 < R;
-        const uint8_t* row0 = stg + (v0 ? i0 : 0) * kTiledRowBytes;
-        const uint8_t* row1 = stg + (v1 ? i1 : 0) * kTiledRowBytes;
-        const uint4 w0 = *reinterpret_cast<const uint4*>(row0 + gi * 16);
-        const uint4 w1 = *reinterpret_cast<const uint4*>(row1 + gi * 16);
-        const uint16_t s0 = *reinterpret_cast<const uint16_t*>(row0 + kTileGroups * 16 + gi * 2);
-        const uint16_t s1 = *reinterpret_cast<const uint16_t*>(row1 + kTileGroups * 16 + gi * 2);
+        // 144-byte blocks: TG == 8 one row of 8 groups, TG == 1 eight rows of one group
+        const int j0 = v0 ? i0 : 0, j1 = v1 ? i1 : 0;
+        const uint8_t* blk0 = stg + (TG == 8 ? j0 : j0 >> 3) * 144;
+        const uint8_t* blk1 = stg + (TG == 8 ? j1 : j1 >> 3) * 144;
+        const int q0 = TG == 8 ? gi : (j0 & 7), q1 = TG == 8 ? gi : (j1 & 7);
+        const uint4 w0 = *reinterpret_cast<const uint4*>(blk0 + q0 * 16);
+        const uint4 w1 = *reinterpret_cast<const uint4*>(blk1 + q1 * 16);
+        const uint16_t s0 = *reinterpret_cast<const uint16_t*>(blk0 + 128 + q0 * 2);
+        const uint16_t s1 = *reinterpret_cast<const uint16_t*>(blk1 + 128 + q1 * 2);
         const float c0 = v0 ? __half2float(__ushort_as_half(s0)) * xr[i0] : 0.0f;
         const float c1 = v1 ? __half2float(__ushort_as_half(s1)) * xr[i1] : 0.0f;
         cs += c0 + c1;
@@ -445,446 +518,496 @@ QORA_DEV void gemv_phase(Cons& C, int m, int L, Pro&& pro, Done&& done) {
     }
     off += r1 - r0;
 
-    // finalize this lane's 32 outputs, then a transposing reduction over the 4 row
-    // lanes of each group: afterwards lane (sub, gi) holds 8 summed outputs
+    // this lane's 32 outputs, then a transposing reduction over the W lanes of each
+    // group (masks 16 .. TG): afterwards lane (sub, gi) holds outputs sub*TG + [0, TG)
     const float bias = cs * 4.3368086899420177e-19f;  // 8 * 2^-64
-    float yv[32];
+    float v[32];
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
-      yv[2 * i] = __fmaf_rn(acc[i].x, q4_scale_of_pos((2 * i) & 7), -bias);
-      yv[2 * i + 1] = __fmaf_rn(acc[i].y, q4_scale_of_pos((2 * i + 1) & 7), -bias);
+      v[2 * i] = __fmaf_rn(acc[i].x, q4_scale_of_pos((2 * i) & 7), -bias);
+      v[2 * i + 1] = __fmaf_rn(acc[i].y, q4_scale_of_pos((2 * i + 1) & 7), -bias);
     }
-    const bool hi16 = (sub & 2) != 0, hi8 = (sub & 1) != 0;
-    float h[16];
 #pragma unroll
-    for (int e = 0; e < 16; ++e) {
-      const float send = hi16 ? yv[e] : yv[16 + e];
-      const float keep = hi16 ? yv[16 + e] : yv[e];
-      h[e] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
-    }
-    float q8[8];
+    for (int msk = 16; msk >= TG; msk >>= 1) {
+      const bool hi = (C.lane & msk) != 0;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const float send = hi8 ? h[e] : h[8 + e];
-      const float keep = hi8 ? h[8 + e] : h[e];
-      q8[e] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+      for (int e2 = 0; e2 < msk; ++e2) {
+        const float send = hi ? v[e2] : v[msk + e2];
+        const float keep = hi ? v[msk + e2] : v[e2];
+        v[e2] = keep + __shfl_xor_sync(0xffffffffu, send, msk);
+      }
     }
-    {
-      const int base = C.warp * kTileCols + gi * kGroup + (hi16 ? 16 : 0) + (hi8 ? 8 : 0);
-      float4* dst = reinterpret_cast<float4*>(red + base);
-      dst[0] = make_float4(q8[0], q8[1], q8[2], q8[3]);
-      dst[1] = make_float4(q8[4], q8[5], q8[6], q8[7]);
-    }
+    float* dst = red + C.warp * (32 * TG) + gi * 32 + sub * TG;
+#pragma unroll
+    for (int e2 = 0; e2 < TG; ++e2) dst[e2] = v[e2];
     C.bar();
-    float* part = a.part[m] + ((long long)t * a.slots[m] + slot) * kTileCols;
-    if (C.tid < kTileCols) {
-      const int o = C.tid;
+    if (C.tid < 32 * TG) {
       float s = 0.0f;
 #pragma unroll
-      for (int w = 0; w < kCW; ++w) s += red[w * kTileCols + o];
-      __stcg(part + o, s);
+      for (int w = 0; w < kCW; ++w) s += red[w * 32 * TG + C.tid];
+      y[C.tid] = s;
     }
     C.bar();
     C.fstamp();
-    done(t, slot);
+    seg_done(m, L, t, slot);
     C.fstamp();
-  });
+    p += r1 - r0;
+  }
+  return C.chunk;
 }
 
-// ------------------------------------------------------------------ the kernel
-template <int GPL>
-__global__ void __launch_bounds__(kThreads, 1) decode_megakernel(const Args a) {
-  extern __shared__ __align__(128) uint8_t smem_raw[];
-  Smem sm = carve(smem_raw);
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int c = blockIdx.x, G = gridDim.x;
-  const int pos = a.st->pos;
-  const int token = a.st->token;
-
-  if (tid == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      ptx::mbar_init(&sm.full[s], 1);
-      ptx::mbar_init(&sm.empty[s], kCW);
-    }
-    sm.flags[0] = (token < 0 || token >= a.vocab || pos < 0 || pos >= a.max_pos) ? 1 : 0;
-    sm.flags[1] = 0;
-    sm.flags[3] = 0;
-    sm.flags[4] = 0;
-    ptx::fence_mbar_init();
-  }
-  __syncthreads();  // last block-wide barrier: the producer warp leaves below
-
-  if (warp == kCW) {
-    // ---------------- producer: stream this CTA's bytes in consumption order
-    if (lane == 0) {
-      uint32_t chunk = 0;
-      bool dead = sm.flags[0] != 0;
-      for_each_chunk(
-          a, c, G, pos,
-          [&](const uint8_t* src, uint32_t bytes) {
-            if (dead) return;
-            const uint32_t s = chunk % kStages;
-            const uint32_t parity = ((chunk / kStages) & 1u) ^ 1u;
-            if (!ptx::mbar_try_wait(&sm.empty[s], parity)) {
-              const uint64_t t0 = ptx::globaltimer();
-              while (!ptx::mbar_try_wait(&sm.empty[s], parity)) {
-                if (sm.flags[0] != 0) {  // consumers gave up: stop issuing
-                  dead = true;
-                  return;
-                }
-                if (ptx::globaltimer() - t0 > a.timeout_ns) {
-                  dead = true;
-                  sm.flags[0] = 1;
-                  atomicExch(&a.st->error, 2);
-                  return;
-                }
-              }
-            }
-            ptx::mbar_arrive_expect_tx(&sm.full[s], bytes);
-            ptx::bulk_g2s(sm.ring + (size_t)s * kStageBytes, src, bytes, &sm.full[s]);
-            ++chunk;
-          },
-          [&](int L) {
-            if (a.trace && L < kTraceLayers)
-              a.trace[(long long)G * kTracePerCta + (long long)c * kTraceLayers + L] = ptx::globaltimer();
-          });
-      sm.flags[3] = (int)chunk;
-      __threadfence_block();
-      sm.flags[4] = 1;
-    }
+// What happens to a finished segment: q|k|v and o_proj results are final (one group
+// per CTA); gate/up and down store their split-K partial; the last down segment of an
+// output tile writes the next residual for the tile.
+__device__ __noinline__ void seg_done(int m, int L, int t, int slot) {
+  Cons C = make_cons(0);
+  const Args& a = C.a();
+  const float* y = C.scratch + kOffY;
+  const int H = a.H;
+  if (m == QKV) {
+    if (C.tid < 32) a.qkv[t * 32 + C.tid] = y[C.tid];
+    C.publish(a.cnt + c_qkv(a, L));
     return;
   }
+  if (m == OPR) {
+    if (C.tid < 32) {
+      const long long col = (long long)L * H + t * 32 + C.tid;
+      a.xmid[col] = __fadd_rn(__ldcg(a.xbuf + col), y[C.tid]);
+    }
+    C.publish(a.cnt + c_o(a, L));
+    return;
+  }
+  if (C.tid < 256) __stcg(a.part[m] + ((long long)t * a.slots[m] + slot) * 256 + C.tid, y[C.tid]);
+  if (m == GU) {
+    C.publish(a.cnt + c_gu_arr(a, L, t));
+    return;
+  }
+  C.bar();
+  if (C.tid == 0) {
+    const unsigned prev = ptx::atom_add_acqrel(a.cnt + c_dn_arr(a, L, t), 1u);
+    C.flags[1] = (prev == (unsigned)(C.ns(DOWN, t) - 1));
+  }
+  C.bar();
+  if (C.flags[1]) {
+    float4* parts = reinterpret_cast<float4*>(C.scratch + kOffB);  // [kDnParts][64]
+    const int b = C.tid & 63, p = C.tid >> 6;
+    const long long col = (long long)L * H + t * 256 + 4 * b;
+    const float4 xm = (C.tid < 64) ? ldcg4(a.xmid + col) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (p < kDnParts) {
+      const int ns = C.ns(DOWN, t);
+      const float* pd = a.part[DOWN] + (long long)t * a.slots[DOWN] * 256 + 4 * b;
+      float4 s = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll 1
+      for (int k0 = p; k0 < ns; k0 += 4 * kDnParts) {
+        float4 v[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[j] = (k0 + j * kDnParts < ns) ? ldcg4(pd + (k0 + j * kDnParts) * 256) : s;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (k0 + j * kDnParts < ns) s = f4add(s, v[j]);
+      }
+      parts[p * 64 + b] = s;
+    }
+    C.bar();
+    if (C.tid < 64) {
+      float4 d = parts[b];
+#pragma unroll 1
+      for (int q = 1; q < kDnParts; ++q) d = f4add(d, parts[q * 64 + b]);
+      *reinterpret_cast<float4*>(a.xbuf + col + H) = f4add(xm, d);
+    }
+    C.publish(a.cnt + c_dn_done(a, L));
+  }
+  C.bar();
+}
 
-  // ---------------- consumers
-  stamp(a, c, 0);
-  Cons C{a, sm, c, G, tid, lane, warp, pos, token};
-  if (sm.flags[0] && tid == 0) atomicExch(&a.st->error, 1);
+// QKV: RMSNorm(x) . W for this CTA's 32-column group, all rows
+__device__ __noinline__ uint32_t qkv_phase(int L, uint32_t chunk) {
+  Cons C = make_cons(chunk);
+  const Args& a = C.a();
+  const Span sp = span_of(a, QKV, C.c);
+  if (sp.n == 0) return chunk;
   const int H = a.H;
-  float* sB = sm.scratch + kOffB;  // x copy for the norms
-  float* sMisc = sm.scratch + kOffMisc;
+  float* sB = C.scratch + kOffB;
+  float gam[kXsPer];
+  prefetch_gains(C, a.layers[L].g_in, sp, H, gam);
+  float ss = 0.0f;
+  if (L > 0) {
+    C.wait_ge(a.cnt + c_dn_done(a, L - 1), (unsigned)a.tiles[DOWN]);
+    ss = load_x(C, sB, a.xbuf + (long long)L * H, H);
+  } else {
+#pragma unroll 1
+    for (int i = C.tid; i < H; i += kCT) ss = __fmaf_rn(sB[i], sB[i], ss);
+  }
+  C.stamp(2 + 8 * min(L, kTraceLayers - 1) + 0);
+  const float inv = rms_inv_from(C.csum(ss), H);
+  fill_norm_inputs(C, sB, inv, gam, sp, H);
+  C.bar();
+  C.fstamp();
+  return gemv_stream<1>(QKV, L, C.chunk);
+}
 
-  // embedding row (embed_lookup_q4, src/gemv.rs:710-736): every CTA builds x_0 locally
-  if (!C.aborted()) {
-    const uint8_t* row = a.lm + (long long)token * a.lm_row_bytes;
-    const uint16_t* sc = reinterpret_cast<const uint16_t*>(row + H / 2);
-    for (int e = tid; e < H; e += kCT) {
-      const uint8_t b = row[e >> 1];
-      const int q = ((e & 1) ? (b >> 4) : (b & 0xF)) - 8;
-      const float v = __fmul_rn(__half2float(__ushort_as_half(sc[e / kGroup])), (float)q);
-      sB[e] = v;
-      if (c == 0) a.xbuf[e] = v;
+// 4 query heads . one K row (8 lanes per row, 16 dims each); lane li == 0 writes
+QORA_DEV void kscore(const float* sq, const float* krow, float* sc, int idx, bool valid, int li) {
+  float d[kHeadsPerKV] = {0.0f, 0.0f, 0.0f, 0.0f};
+  if (valid) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float4 k4 = reinterpret_cast<const float4*>(krow + li * 16)[j];
+#pragma unroll
+      for (int h = 0; h < kHeadsPerKV; ++h) {
+        const float4 q4 = reinterpret_cast<const float4*>(sq + h * kHeadDim + li * 16)[j];
+        d[h] = __fmaf_rn(q4.x, k4.x, d[h]);
+        d[h] = __fmaf_rn(q4.y, k4.y, d[h]);
+        d[h] = __fmaf_rn(q4.z, k4.z, d[h]);
+        d[h] = __fmaf_rn(q4.w, k4.w, d[h]);
+      }
+    }
+  }
+  const float scale = 0.08838834764831845f;  // 1/sqrt(128): the f32 quotient of 1 and f32 sqrt(128)
+#pragma unroll
+  for (int h = 0; h < kHeadsPerKV; ++h) {
+    float v = d[h];
+    v += __shfl_xor_sync(0xffffffffu, v, 1);
+    v += __shfl_xor_sync(0xffffffffu, v, 2);
+    v += __shfl_xor_sync(0xffffffffu, v, 4);
+    if (valid && li == 0) sc[h * kMaxAttnChunk + idx] = __fmul_rn(v, scale);
+  }
+}
+
+// ATTN: unit u = c = (kv head g = u % nkvh, chunk u / nkvh) for the 4 query heads of g
+// (src/gemv.rs:914-989, softmax_raw :782-793; RoPE src/gemv.rs:757-778)
+__device__ __noinline__ uint32_t attention_phase(int L, uint32_t chunk) {
+  Cons C = make_cons(chunk);
+  const Args& a = C.a();
+  const int pos = C.pos, len = pos + 1, tid = C.tid, lane = C.lane, warp = C.warp;
+  int csz, nch;
+  attn_plan(len, C.G, a.nkvh, csz, nch);
+  const int u = C.c;
+  if (u >= a.nkvh * nch) return chunk;
+  const int g = u % a.nkvh;
+  const int s0 = (u / a.nkvh) * csz, s1 = min(len, s0 + csz), sc1 = min(s1, pos), n = s1 - s0;
+  const bool has_pos = pos < s1;
+  const Layer& ly = a.layers[L];
+  float* kc = ly.kc + g * a.head_stride;
+  float* vc = ly.vc + g * a.head_stride;
+  float* sq = C.scratch + kAttQ;
+  float* sc = C.scratch + kAttS;
+  float* sml = C.scratch + kAttML;
+  float* skv = C.scratch + kAttKV;
+  C.wait_ge(a.cnt + c_qkv(a, L), (unsigned)a.subn[QKV]);
+  C.fstamp();
+  // RoPE pairs (d, d+64): threads 0..255 the 4 query heads, 256..319 k; 320..447 copy v
+  if (tid < 320 && (tid < 256 || has_pos)) {
+    const bool isk = tid >= 256;
+    const int hh = (tid >> 6) & 3, d = tid & 63;
+    const float* src = isk ? a.qkv + a.nq + g * kHeadDim : a.qkv + (g * kHeadsPerKV + hh) * kHeadDim;
+    const float x1 = __ldcg(src + d), x2 = __ldcg(src + d + kHalfDim);
+    float y1 = x1, y2 = x2;
+    if (ly.rope) {
+      const float cs = __ldg(a.cos_t + (long long)pos * kHalfDim + d);
+      const float sn = __ldg(a.sin_t + (long long)pos * kHalfDim + d);
+      y1 = __fsub_rn(__fmul_rn(x1, cs), __fmul_rn(x2, sn));
+      y2 = __fadd_rn(__fmul_rn(x2, cs), __fmul_rn(x1, sn));
+    }
+    if (!isk) {
+      sq[hh * kHeadDim + d] = y1;
+      sq[hh * kHeadDim + d + kHalfDim] = y2;
+    } else {
+      skv[d] = y1;
+      skv[d + kHalfDim] = y2;
+      kc[(long long)pos * kHeadDim + d] = y1;
+      kc[(long long)pos * kHeadDim + d + kHalfDim] = y2;
+    }
+  } else if (tid >= 320 && tid < 448 && has_pos) {
+    const int d = tid - 320;
+    const float v = __ldcg(a.qkv + a.nq + a.nkvw + g * kHeadDim + d);
+    skv[kHeadDim + d] = v;
+    vc[(long long)pos * kHeadDim + d] = v;
+  }
+  C.bar();
+  // scores: 4 rows per warp pass (8 lanes each), 60 row slots >= kKVRows
+  const int li = lane & 7, ri = warp * 4 + (lane >> 3);
+#pragma unroll 1
+  for (int s = s0; s < sc1; s += kKVRows) {
+    const uint8_t* stg = C.acquire_stage();
+    const int nr = min(kKVRows, sc1 - s);
+    if (C.stage_ok)
+      kscore(sq, reinterpret_cast<const float*>(stg) + min(ri, nr - 1) * kHeadDim, sc, s - s0 + ri, ri < nr, li);
+    C.release_stage();
+    C.fstamp();
+  }
+  if (has_pos && warp == 0 && !C.aborted_w()) kscore(sq, skv, sc, pos - s0, (lane >> 3) == 0, li);
+  C.bar();
+  // chunk softmax numerators, one warp per query head
+  if (warp < kHeadsPerKV && !C.aborted_w()) {
+    float* row = sc + warp * kMaxAttnChunk;
+    float mx = -INFINITY;
+#pragma unroll 1
+    for (int i = lane; i < n; i += 32) mx = fmaxf(mx, row[i]);
+    mx = warp_max(mx);
+    float l = 0.0f;
+#pragma unroll 1
+    for (int i = lane; i < n; i += 32) {
+      const float e = expf(row[i] - mx);
+      row[i] = e;
+      l += e;
+    }
+    l = warp_sum(l);
+    if (lane == 0) {
+      sml[warp * 2] = mx;
+      sml[warp * 2 + 1] = l;
     }
   }
   C.bar();
-  stamp(a, c, 1);
-
-  int chunk_sz, nu;
-  attn_plan(pos + 1, G, chunk_sz, nu);
-  const float att_scale = __fdiv_rn(1.0f, __fsqrt_rn((float)kHeadDim));
-
-  for (int L = 0; L < a.L; ++L) {
-    const Layer& ly = a.layers[L];
-    C.layer = L;
-    const float* x_in = a.xbuf + (long long)L * H;
-    float* x_out = a.xbuf + (long long)(L + 1) * H;
-    const int tb = 2 + 8 * min(L, kTraceLayers - 1);
-
-    // ===== QKV (subset): RMSNorm(x_in) . Wqkv -> partials
-    const bool in_qkv = (c >= a.sub0[QKV] && c < a.sub0[QKV] + a.subn[QKV]);
-    if (in_qkv) {
-      if (L > 0) {
-        C.wait_ge(a.cnt + c_dn_done(a, L - 1), (unsigned)a.tiles[DOWN]);
-        if (!C.aborted()) load_vec(C, sB, x_in, H);
-        C.bar();
-      }
-      stamp(a, c, tb + 0);
-      const float inv = C.sync_aborted() ? 1.0f : rms_inv_of(C, sB, H);
-      gemv_phase(
-          C, QKV, L,
-          [&](int, int r0, int r1, float* xs) {
-            for (int i = C.tid; i < r1 - r0; i += kCT)
-              xs[i] = __fmul_rn(__fmul_rn(sB[r0 + i], inv), __ldg(ly.g_in + r0 + i));
-          },
-          [&](int, int) { C.publish(a.cnt + c_qkv_parts(a, L)); });
-    }
-    stamp(a, c, tb + 1);
-
-    // ===== ATTN (units of `chunk_sz` positions, all query heads)
-    {
-      const int kvrow = a.nkvw * 4;
-      const int rps = kStageBytes / kvrow;
-      float* sq = sm.scratch + kAttQ;    // [nh][128] (RoPE applied)
-      float* sc = sm.scratch + kAttS;    // [nh][kMaxAttnChunk]
-      float* sml = sm.scratch + kAttML;  // [nh][2]
-      float* skv = sm.scratch + kAttKV;  // new k row [nkvw] | new v row [nkvw]
-      const int gq = lane >> 3, li = lane & 7;  // K pass: 4 row groups x 8 lanes of 16 dims
-      const int nv = a.nkvh * kHeadDim;         // P.V items: (kv head, dim)
-      bool ready = false;
-      for (int u = c; u < nu; u += G) {
-        const int s0 = u * chunk_sz, s1 = min(pos + 1, s0 + chunk_sz), sc1 = min(s1, pos);
-        const int n = s1 - s0;
-        const bool has_pos = pos >= s0 && pos < s1;
-        if (!ready) {
-          C.wait_ge(a.cnt + c_qkv_parts(a, L), (unsigned)a.segs[QKV]);
-          C.fstamp();
-          // q (and k|v for the unit holding the new position) from the QKV partials,
-          // RoPE on q and k (src/gemv.rs:757-778); k|v appended to the cache
-          if (!C.aborted()) {
-            const int ncols = a.nq + 2 * a.nkvw;
-            for (int i = tid; i < ncols / 2; i += kCT) {
-              // pair (col, col + 64) within one head: i -> head hh, dim d < 64
-              const int hh = i / kHalfDim, d = i % kHalfDim;
-              const int col = hh * kHeadDim + d;
-              if (col >= a.nq && !has_pos) continue;
-              const float x1 = sum_slots(a, QKV, col / kTileCols, col % kTileCols);
-              const float x2 = sum_slots(a, QKV, (col + kHalfDim) / kTileCols, (col + kHalfDim) % kTileCols);
-              float y1 = x1, y2 = x2;
-              if (ly.rope && col < a.nq + a.nkvw) {
-                const float cs = a.cos_t[(long long)pos * kHalfDim + d];
-                const float sn = a.sin_t[(long long)pos * kHalfDim + d];
-                y1 = __fsub_rn(__fmul_rn(x1, cs), __fmul_rn(x2, sn));
-                y2 = __fadd_rn(__fmul_rn(x2, cs), __fmul_rn(x1, sn));
-              }
-              if (col < a.nq) {
-                sq[col] = y1;
-                sq[col + kHalfDim] = y2;
-              } else {
-                const int kc = col - a.nq;  // within k|v
-                skv[kc] = y1;
-                skv[kc + kHalfDim] = y2;
-                float* dst = (kc < a.nkvw) ? ly.kc + (long long)pos * a.nkvw + kc
-                                           : ly.vc + (long long)pos * a.nkvw + (kc - a.nkvw);
-                dst[0] = y1;
-                dst[kHalfDim] = y2;
-              }
-            }
-          }
-          C.bar();
-          ready = true;
-        }
-        // one K row per 8-lane group; every lane of the warp executes the shuffles
-        auto score = [&](int hq, const float* krow, int idx, bool valid) {
-          float acc = 0.0f;
-          if (valid) {
-            const float4* kp = reinterpret_cast<const float4*>(krow + (hq / a.grp) * kHeadDim + li * 16);
-            const float4* qp = reinterpret_cast<const float4*>(sq + hq * kHeadDim + li * 16);
+  C.fstamp();
+  // P.V: thread d < 128 accumulates dim d of the 4 heads
+  float o[kHeadsPerKV] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 1
+  for (int s = s0; s < sc1; s += kKVRows) {
+    const uint8_t* stg = C.acquire_stage();
+    const int nr = min(kKVRows, sc1 - s);
+    if (C.stage_ok && tid < kHeadDim) {
+      const float* vr = reinterpret_cast<const float*>(stg) + tid;
+#pragma unroll 1
+      for (int i = 0; i < nr; ++i) {
+        const float v = vr[i * kHeadDim];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const float4 k4 = kp[j];
-              const float4 q4 = qp[j];
-              acc = __fmaf_rn(q4.x, k4.x, acc);
-              acc = __fmaf_rn(q4.y, k4.y, acc);
-              acc = __fmaf_rn(q4.z, k4.z, acc);
-              acc = __fmaf_rn(q4.w, k4.w, acc);
-            }
-          }
-          acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-          acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-          acc += __shfl_xor_sync(0xffffffffu, acc, 4);
-          if (valid && li == 0) sc[hq * kMaxAttnChunk + idx] = __fmul_rn(acc, att_scale);
-        };
-        for (int s = s0; s < sc1; s += rps) {
-          const uint8_t* stg = C.acquire_stage();
-          const int nr = min(rps, sc1 - s);
-          if (C.stage_ok) {  // warp-uniform
-            for (int hq = warp; hq < a.nh; hq += kCW)
-              for (int ib = 0; ib < nr; ib += 4) {
-                const int i = ib + gq;
-                score(hq, reinterpret_cast<const float*>(stg + min(i, nr - 1) * kvrow), s - s0 + i, i < nr);
-              }
-          }
-          C.release_stage();
-          C.fstamp();
-        }
-        if (!C.aborted_w() && has_pos)  // warp-uniform: the new row, from shared memory
-          for (int hq = warp; hq < a.nh; hq += kCW) score(hq, skv, pos - s0, gq == 0);
-        C.bar();
-        // chunk softmax numerators: query heads spread over warps
-        if (!C.aborted_w()) {
-          for (int hq = warp; hq < a.nh; hq += kCW) {
-            float* row = sc + hq * kMaxAttnChunk;
-            float mx = -INFINITY;
-            for (int i = lane; i < n; i += 32) mx = fmaxf(mx, row[i]);
-            mx = warp_max(mx);
-            float l = 0.0f;
-            for (int i = lane; i < n; i += 32) {
-              const float e = expf(row[i] - mx);
-              row[i] = e;
-              l += e;
-            }
-            l = warp_sum(l);
-            if (lane == 0) {
-              sml[hq * 2] = mx;
-              sml[hq * 2 + 1] = l;
-            }
-          }
-        }
-        C.bar();
-        C.fstamp();
-        // P.V: item (kv head g, dim d) accumulates the grp query heads that share g
-        float o[kMaxVItems][4];
-#pragma unroll
-        for (int k = 0; k < kMaxVItems; ++k)
-#pragma unroll
-          for (int j = 0; j < 4; ++j) o[k][j] = 0.0f;
-        for (int s = s0; s < sc1; s += rps) {
-          const uint8_t* stg = C.acquire_stage();
-          const int nr = min(rps, sc1 - s);
-          if (C.stage_ok) {
-#pragma unroll
-            for (int k = 0; k < kMaxVItems; ++k) {
-              const int it = tid + k * kCT;
-              if (it < nv) {
-                const int g = it / kHeadDim, d = it % kHeadDim;
-                for (int i = 0; i < nr; ++i) {
-                  const float v = reinterpret_cast<const float*>(stg + i * kvrow)[g * kHeadDim + d];
-                  const int idx = s - s0 + i;
-#pragma unroll
-                  for (int j = 0; j < 4; ++j)
-                    if (j < a.grp) o[k][j] = __fmaf_rn(sc[(g * a.grp + j) * kMaxAttnChunk + idx], v, o[k][j]);
-                }
-              }
-            }
-          }
-          C.release_stage();
-          C.fstamp();
-        }
-        if (!C.aborted()) {
-#pragma unroll
-          for (int k = 0; k < kMaxVItems; ++k) {
-            const int it = tid + k * kCT;
-            if (it < nv) {
-              const int g = it / kHeadDim, d = it % kHeadDim;
-              if (has_pos) {
-                const float v = skv[a.nkvw + g * kHeadDim + d];
-#pragma unroll
-                for (int j = 0; j < 4; ++j)
-                  if (j < a.grp) o[k][j] = __fmaf_rn(sc[(g * a.grp + j) * kMaxAttnChunk + (pos - s0)], v, o[k][j]);
-              }
-#pragma unroll
-              for (int j = 0; j < 4; ++j)
-                if (j < a.grp) __stcg(a.att_o + ((long long)u * a.nh + g * a.grp + j) * kHeadDim + d, o[k][j]);
-            }
-          }
-          if (tid < a.nh) {
-            __stcg(a.att_ml + ((long long)u * a.nh + tid) * 2, sml[tid * 2]);
-            __stcg(a.att_ml + ((long long)u * a.nh + tid) * 2 + 1, sml[tid * 2 + 1]);
-          }
-        }
-        C.publish(a.cnt + c_att(a, L));
-        C.bar();
+        for (int h = 0; h < kHeadsPerKV; ++h) o[h] = __fmaf_rn(sc[h * kMaxAttnChunk + s - s0 + i], v, o[h]);
       }
     }
-    stamp(a, c, tb + 2);
-
-    // ===== O projection (subset): merge attention partials for the rows it needs
-    const bool in_o = (c >= a.sub0[OPR] && c < a.sub0[OPR] + a.subn[OPR]);
-    if (in_o) {
-      C.wait_ge(a.cnt + c_att(a, L), (unsigned)nu);
-      stamp(a, c, tb + 3);
-      float* mw = sm.scratch + kOffB;  // [<=8 heads][kMaxUnits] weights, then 1/L per head
-      gemv_phase(
-          C, OPR, L,
-          [&](int, int r0, int r1, float* xs) {
-            const int h0 = r0 / kHeadDim, h1 = (r1 - 1) / kHeadDim;
-            const int nhs = h1 - h0 + 1;  // <= 8 (host checks the segment length)
-            // per head: M = max m_u, w_u = exp(m_u - M), 1/L with L = sum l_u w_u
-            if (warp < nhs) {
-              const int h = h0 + warp;
-              float mx = -INFINITY;
-              for (int u = lane; u < nu; u += 32) mx = fmaxf(mx, __ldcg(a.att_ml + ((long long)u * a.nh + h) * 2));
-              mx = warp_max(mx);
-              float l = 0.0f;
-              for (int u = lane; u < nu; u += 32) {
-                const float2 ml = __ldcg(reinterpret_cast<const float2*>(a.att_ml + ((long long)u * a.nh + h) * 2));
-                const float w = expf(ml.x - mx);
-                mw[warp * kMaxUnits + u] = w;
-                l = __fmaf_rn(ml.y, w, l);
-              }
-              l = warp_sum(l);
-              if (lane == 0) mw[8 * kMaxUnits + warp] = __fdiv_rn(1.0f, l);
-            }
-            C.bar();
-            for (int i = C.tid; i < r1 - r0; i += kCT) {
-              const int r = r0 + i, h = r / kHeadDim, dd = r % kHeadDim, j = h - h0;
-              const float* op = a.att_o + (long long)h * kHeadDim + dd;
-              float acc = 0.0f;
-#pragma unroll 4
-              for (int u = 0; u < nu; ++u)
-                acc = __fmaf_rn(__ldcg(op + (long long)u * a.nh * kHeadDim), mw[j * kMaxUnits + u], acc);
-              xs[i] = __fmul_rn(acc, mw[8 * kMaxUnits + j]);
-            }
-            C.bar();
-          },
-          [&](int, int) { C.publish(a.cnt + c_o_parts(a, L)); });
-    }
-    stamp(a, c, tb + 4);
-
-    // ===== gate/up (all): x_mid = x_in + O partials, RMSNorm, GEMV -> partials per tile
-    C.wait_ge(a.cnt + c_o_parts(a, L), (unsigned)a.segs[OPR]);
-    stamp(a, c, tb + 5);
-    {
-      if (!C.aborted()) build_x_mid(C, sB, x_in, H);
-      C.bar();
-      const float inv2 = C.sync_aborted() ? 1.0f : rms_inv_of(C, sB, H);
-      gemv_phase(
-          C, GU, L,
-          [&](int, int r0, int r1, float* xs) {
-            for (int i = C.tid; i < r1 - r0; i += kCT)
-              xs[i] = __fmul_rn(__fmul_rn(sB[r0 + i], inv2), __ldg(ly.g_post + r0 + i));
-          },
-          [&](int t, int) { C.publish(a.cnt + c_gu_arr(a, L, t)); });
-    }
-    stamp(a, c, tb + 6);
-
-    // ===== down (all): SwiGLU of the rows it needs from the gate/up partials; the last
-    // CTA of each output tile writes x_out = x_in + O + down for the tile
-    gemv_phase(
-        C, DOWN, L,
-        [&](int, int r0, int r1, float* xs) {
-          const int t0 = r0 / (kTileCols / 2), t1 = (r1 - 1) / (kTileCols / 2);
-          if (C.tid == 0)
-            for (int tg = t0; tg <= t1; ++tg) C.spin_ge(a.cnt + c_gu_arr(a, L, tg), (unsigned)nslots(a, GU, tg));
-          if (C.sync_aborted()) return;
-          for (int i = C.tid; i < r1 - r0; i += kCT) {
-            const int r = r0 + i, tg = r / (kTileCols / 2), o = r % (kTileCols / 2);
-            const float g = sum_slots(a, GU, tg, o);
-            const float u = sum_slots(a, GU, tg, kTileCols / 2 + o);
-            const float sg = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
-            xs[i] = __fmul_rn(sg, u);
-          }
-        },
-        [&](int t, int) {
-          if (C.tid == 0) {
-            const unsigned prev = ptx::atom_add_acqrel(a.cnt + c_dn_arr(a, L, t), 1u);
-            C.sm.flags[1] = (prev == (unsigned)(nslots(a, DOWN, t) - 1));
-          }
-          C.bar();
-          if (C.sm.flags[1]) {
-            if (C.tid < kTileCols) {
-              const int col = t * kTileCols + C.tid;
-              if (col < H) {
-                const float xm = __fadd_rn(__ldcg(x_in + col), sum_slots(a, OPR, t, C.tid));
-                x_out[col] = __fadd_rn(xm, sum_slots(a, DOWN, t, C.tid));
-              }
-            }
-            C.publish(a.cnt + c_dn_done(a, L));
-          }
-          C.bar();
-        });
-    stamp(a, c, tb + 7);
+    C.release_stage();
+    C.fstamp();
   }
+  if (tid < kHeadDim && !C.aborted()) {
+    if (has_pos) {
+      const float v = skv[kHeadDim + tid];
+#pragma unroll
+      for (int h = 0; h < kHeadsPerKV; ++h) o[h] = __fmaf_rn(sc[h * kMaxAttnChunk + pos - s0], v, o[h]);
+    }
+#pragma unroll
+    for (int h = 0; h < kHeadsPerKV; ++h) __stcg(a.att_o + ((long long)u * kHeadsPerKV + h) * kHeadDim + tid, o[h]);
+    if (tid < 2 * kHeadsPerKV) __stcg(a.att_ml + (long long)u * 2 * kHeadsPerKV + tid, sml[tid]);
+  }
+  C.publish(a.cnt + c_att(a, L));
+  return C.chunk;
+}
 
-  // ===== final norm + lm_head + argmax
-  C.wait_ge(a.cnt + c_dn_done(a, a.L - 1), (unsigned)a.tiles[DOWN]);
-  stamp(a, c, 2 + 8 * kTraceLayers);
-  const float* x_fin = a.xbuf + (long long)a.L * H;
-  if (!C.aborted()) load_vec(C, sB, x_fin, H);
+// O: merge the (m, l, o) partials of every head (chunk order), GEMV over all rows for
+// this CTA's 32 columns, x_mid = x + o
+__device__ __noinline__ uint32_t o_phase(int L, uint32_t chunk) {
+  Cons C = make_cons(chunk);
+  const Args& a = C.a();
+  const Span sp = span_of(a, OPR, C.c);
+  if (sp.n == 0) return chunk;
+  int csz, nch;
+  attn_plan(C.pos + 1, C.G, a.nkvh, csz, nch);
+  const int nkvh = a.nkvh, K = a.K[OPR];
+  C.wait_ge(a.cnt + c_att(a, L), (unsigned)(nkvh * nch));
+  C.stamp(2 + 8 * min(L, kTraceLayers - 1) + 3);
+  // per query head h: M = max_ch m, w_ch = exp(m_ch - M), 1/l with l = sum l_ch w_ch;
+  // unit (chunk ch, kv head h/4) holds head h at slot h%4
+  float* mw = C.scratch + kOffB;  // [nh][nch], then 1/l [nh]
+  float* invl = mw + a.nh * nch;
+#pragma unroll 1
+  for (int h = C.warp; h < a.nh; h += kCW) {
+    const float* ml = a.att_ml + h * 2;
+    const long long ustride = (long long)nkvh * kHeadsPerKV * 2;  // next chunk, same head
+    float mx = -INFINITY;
+#pragma unroll 1
+    for (int ch = C.lane; ch < nch; ch += 32) mx = fmaxf(mx, __ldcg(ml + ch * ustride));
+    mx = warp_max(mx);
+    float l = 0.0f;
+#pragma unroll 1
+    for (int ch = C.lane; ch < nch; ch += 32) {
+      const float2 v = __ldcg(reinterpret_cast<const float2*>(ml + ch * ustride));
+      const float w = expf(v.x - mx);
+      mw[h * nch + ch] = w;
+      l = __fmaf_rn(v.y, w, l);
+    }
+    l = warp_sum(l);
+    if (C.lane == 0) invl[h] = __fdiv_rn(1.0f, l);
+  }
   C.bar();
+  // xs[r] = (sum_ch o_ch[r] w_ch) / l, r = head * 128 + dim; 5 rows x 4 chunks of loads
+  // in flight per batch
   {
-    const float inv = C.sync_aborted() ? 1.0f : rms_inv_of(C, sB, H);
-    for (int i = tid; i < H; i += kCT) sB[i] = __fmul_rn(__fmul_rn(sB[i], inv), a.final_gamma[i]);
+    float* xs = C.scratch;
+    const long long ostride = (long long)nkvh * kHeadsPerKV * kHeadDim;  // next chunk, same head
+    float acc[kXsPer];
+#pragma unroll
+    for (int j = 0; j < kXsPer; ++j) acc[j] = 0.0f;
+#pragma unroll 1
+    for (int c0 = 0; c0 < nch; c0 += 4) {
+      float v[kXsPer][4];
+#pragma unroll
+      for (int j = 0; j < kXsPer; ++j) {
+        const int r = C.tid + j * kCT;
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          v[j][k] = (r < K && c0 + k < nch) ? __ldcg(a.att_o + (c0 + k) * ostride + r) : 0.0f;
+      }
+#pragma unroll
+      for (int j = 0; j < kXsPer; ++j) {
+        const int r = C.tid + j * kCT, h = r / kHeadDim;
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          if (r < K && c0 + k < nch) acc[j] = __fmaf_rn(v[j][k], mw[h * nch + c0 + k], acc[j]);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kXsPer; ++j) {
+      const int r = C.tid + j * kCT;
+      if (r < K) xs[r] = __fmul_rn(acc[j], invl[r / kHeadDim]) * kTwo64;
+    }
   }
+  C.bar();
+  C.fstamp();
+  return gemv_stream<1>(OPR, L, C.chunk);
+}
+
+// GU (all): RMSNorm(x_mid) . [gate|up] -> split-K partials per tile
+__device__ __noinline__ uint32_t gu_phase(int L, uint32_t chunk) {
+  Cons C = make_cons(chunk);
+  const Args& a = C.a();
+  const Span sp = span_of(a, GU, C.c);
+  const int H = a.H;
+  float* sB = C.scratch + kOffB;
+  float gam[kXsPer];
+  prefetch_gains(C, a.layers[L].g_post, sp, a.K[GU], gam);
+  C.wait_ge(a.cnt + c_o(a, L), (unsigned)a.subn[OPR]);
+  C.stamp(2 + 8 * min(L, kTraceLayers - 1) + 5);
+  const float ss = load_x(C, sB, a.xmid + (long long)L * H, H);
+  const float inv = rms_inv_from(C.csum(ss), H);
+  fill_norm_inputs(C, sB, inv, gam, sp, a.K[GU]);
+  C.bar();
+  C.fstamp();
+  return gemv_stream<8>(GU, L, C.chunk);
+}
+
+// DOWN (all): SwiGLU of the rows it needs from the gate/up partials (src/gemv.rs:412-502),
+// split-K GEMV
+__device__ __noinline__ uint32_t down_phase(int L, uint32_t chunk) {
+  Cons C = make_cons(chunk);
+  const Args& a = C.a();
+  const Span sp = span_of(a, DOWN, C.c);
+  const int K = a.K[DOWN];
+  constexpr int kHalfTile = 128;  // gate (then up) outputs per gate/up tile
+  // gate/up tiles of this CTA's rows: one range per segment (the host checks <= 2)
+  int tr[4] = {0, -1, 0, -1};
+  {
+    int k = 0;
+    for_each_seg(a, DOWN, C.c, [&](int, int r0, int r1) {
+      if (k < 2) {
+        tr[2 * k] = r0 / kHalfTile;
+        tr[2 * k + 1] = (r1 - 1) / kHalfTile;
+      }
+      ++k;
+    });
+  }
+  if (C.warp == 0) {  // lanes poll one tile each, warp-uniform exit
+    const uint64_t t0 = ptx::globaltimer();
+    const int n0 = tr[1] - tr[0] + 1, n1 = tr[3] - tr[2] + 1;
+#pragma unroll 1
+    for (;;) {
+      bool mine = true;
+#pragma unroll 1
+      for (int k = C.lane; k < n0 + n1; k += 32) {
+        const int t = k < n0 ? tr[0] + k : tr[2] + (k - n0);
+        mine &= ptx::ld_relaxed(a.cnt + c_gu_arr(a, L, t)) >= (unsigned)C.ns(GU, t);
+      }
+      if (__all_sync(0xffffffffu, mine)) break;
+      int stop = 0;
+      if (C.lane == 0) stop = C.aborted() ? 1 : (ptx::globaltimer() - t0 > a.timeout_ns ? 2 : 0);
+      stop = __shfl_sync(0xffffffffu, stop, 0);
+      if (stop) {
+        if (stop == 2 && C.lane == 0) C.set_abort(2);
+        break;
+      }
+    }
+    ptx::fence_acq_rel_gpu();
+  }
+  C.bar();
+  // rows i = tid, tid + kCT: both rows' gate and up partials (4 slots each) in flight
+  {
+    float* xs = C.scratch;
+    int r = (sp.lin0 + C.tid) % K;
+#pragma unroll 1
+    for (int i = C.tid; i < sp.n; i += 2 * kCT) {
+      const int r2 = row_next(r, K);
+      const bool two = i + kCT < sp.n;
+      const int t1 = r / kHalfTile, t2 = r2 / kHalfTile;
+      const int n1 = C.ns(GU, t1), n2 = two ? C.ns(GU, t2) : 0;
+      const float* p1 = a.part[GU] + (long long)t1 * a.slots[GU] * 256 + r % kHalfTile;
+      const float* p2 = a.part[GU] + (long long)t2 * a.slots[GU] * 256 + r2 % kHalfTile;
+      float g1 = 0.0f, u1 = 0.0f, g2 = 0.0f, u2 = 0.0f;
+#pragma unroll 1
+      for (int k0 = 0; k0 < max(n1, n2); k0 += 4) {
+        float v[4][4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const bool ok1 = k0 + k < n1, ok2 = k0 + k < n2;
+          v[0][k] = ok1 ? __ldcg(p1 + (k0 + k) * 256) : 0.0f;
+          v[1][k] = ok1 ? __ldcg(p1 + (k0 + k) * 256 + kHalfTile) : 0.0f;
+          v[2][k] = ok2 ? __ldcg(p2 + (k0 + k) * 256) : 0.0f;
+          v[3][k] = ok2 ? __ldcg(p2 + (k0 + k) * 256 + kHalfTile) : 0.0f;
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          if (k0 + k < n1) {
+            g1 = __fadd_rn(g1, v[0][k]);
+            u1 = __fadd_rn(u1, v[1][k]);
+          }
+          if (k0 + k < n2) {
+            g2 = __fadd_rn(g2, v[2][k]);
+            u2 = __fadd_rn(u2, v[3][k]);
+          }
+        }
+      }
+      xs[i] = __fmul_rn(__fdiv_rn(g1, __fadd_rn(1.0f, expf(-g1))), u1) * kTwo64;
+      if (two) xs[i + kCT] = __fmul_rn(__fdiv_rn(g2, __fadd_rn(1.0f, expf(-g2))), u2) * kTwo64;
+      r = row_next(r2, K);
+    }
+  }
+  C.bar();
+  C.fstamp();
+  return gemv_stream<8>(DOWN, L, C.chunk);
+}
+
+// Drain after an abort: wait (bounded) for the producer to stop and for the copies it
+// issued last to land, so that no bulk copy targets this CTA's shared memory after it
+// exits.
+__device__ __noinline__ void drain() {
+  Cons C = make_cons(0);
+  C.bar();
+  if (C.tid == 0 && C.aborted()) {
+    const uint64_t t0 = ptx::globaltimer();
+    while (C.flags[4] == 0 && ptx::globaltimer() - t0 < C.ap->timeout_ns) {
+    }
+    const uint32_t issued = (uint32_t)C.flags[3];
+    const uint32_t first = issued > (uint32_t)kStages ? issued - kStages : 0u;
+    for (uint32_t j = first; j < issued; ++j) {
+      const uint64_t t1 = ptx::globaltimer();
+      while (!ptx::mbar_try_wait(&C.full[j % kStages], (j / kStages) & 1u) &&
+             ptx::globaltimer() - t1 < C.ap->timeout_ns) {
+      }
+    }
+  }
+  C.bar();
+}
+
+// final RMSNorm + lm_head rows of this CTA (src/gemv.rs:825-864, 1015) with the greedy
+// first-maximum argmax (src/generate.rs:346-352); per-warp bests into MISC
+template <int GPL>
+__device__ __noinline__ void lm_phase(uint32_t chunk) {
+  Cons C = make_cons(chunk);
+  const Args& a = C.a();
+  const int H = a.H, lane = C.lane, warp = C.warp;
+  float* sB = C.scratch + kOffB;
+  C.wait_ge(a.cnt + c_dn_done(a, a.L - 1), (unsigned)a.tiles[DOWN]);
+  C.stamp(2 + 8 * kTraceLayers);
+  const float ss = load_x(C, sB, a.xbuf + (long long)a.L * H, H);
+  const float inv = rms_inv_from(C.csum(ss), H);
+  for (int i = C.tid; i < H; i += kCT) sB[i] = __fmul_rn(__fmul_rn(sB[i], inv), a.final_gamma[i]);
   C.bar();
   constexpr int EPL = GPL * 32;
   float2 xs2[EPL / 2];
@@ -905,57 +1028,157 @@ __global__ void __launch_bounds__(kThreads, 1) decode_megakernel(const Args a) {
   }
   float best = -INFINITY;
   unsigned besti = 0xFFFFFFFFu;
-  {
-    const long long v0 = (long long)c * a.vocab / G, v1 = (long long)(c + 1) * a.vocab / G;
-    const float k64 = 18446744073709551616.0f;
-    for (long long r = v0; r < v1; r += a.lm_rows_per_stage) {
-      const uint8_t* stg = C.acquire_stage();
-      const int nr = (int)min((long long)a.lm_rows_per_stage, v1 - r);
-      if (C.stage_ok) {
-        for (int i = warp; i < nr; i += kCW) {
-          const uint8_t* row = stg + (size_t)i * a.lm_row_bytes;
-          const uint4* wp = reinterpret_cast<const uint4*>(row) + lane * GPL;
-          const uint16_t* sp = reinterpret_cast<const uint16_t*>(row + H / 2) + lane * GPL;
-          float acc = 0.0f;
+  const int v0 = (int)((long long)C.c * a.vocab / C.G), v1 = (int)((long long)(C.c + 1) * a.vocab / C.G);
+#pragma unroll 1
+  for (int r = v0; r < v1; r += a.lm_rows_per_stage) {
+    const uint8_t* stg = C.acquire_stage();
+    const int nr = min(a.lm_rows_per_stage, v1 - r);
+    if (C.stage_ok) {
+#pragma unroll 1
+      for (int i = warp; i < nr; i += kCW) {
+        const uint8_t* row = stg + (size_t)i * a.lm_row_bytes;
+        const uint4* wp = reinterpret_cast<const uint4*>(row) + lane * GPL;
+        const uint16_t* sp = reinterpret_cast<const uint16_t*>(row + H / 2) + lane * GPL;
+        float acc = 0.0f;
 #pragma unroll
-          for (int g = 0; g < GPL; ++g) {
-            const uint4 w = wp[g];
-            float2 dd = make_float2(0.0f, 0.0f);
-            const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+        for (int g = 0; g < GPL; ++g) {
+          const uint4 w = wp[g];
+          float2 dd = make_float2(0.0f, 0.0f);
+          const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const uint32_t uu = ws[k], bb = uu >> 12;
-              const int base = (g * 32 + k * 8) / 2;
-              dd = __ffma2_rn(make_float2(__uint_as_float(uu & 0xFu), __uint_as_float(uu & 0xF0u)), xs2[base + 0], dd);
-              dd = __ffma2_rn(make_float2(__uint_as_float(uu & 0xF00u), __uint_as_float(uu & 0xF000u)), xs2[base + 1], dd);
-              dd = __ffma2_rn(make_float2(__uint_as_float(uu & 0xF0000u), __uint_as_float(bb & 0xF00u)), xs2[base + 2], dd);
-              dd = __ffma2_rn(make_float2(__uint_as_float(bb & 0xF000u), __uint_as_float(bb & 0xF0000u)), xs2[base + 3], dd);
-            }
-            const float dot = __fmaf_rn(dd.x + dd.y, k64, -xg[g]);
-            acc = __fmaf_rn(__half2float(__ushort_as_half(sp[g])), dot, acc);
+          for (int k = 0; k < 4; ++k) {
+            const uint32_t uu = ws[k], bb = uu >> 12;
+            const int base = (g * 32 + k * 8) / 2;
+            dd = __ffma2_rn(make_float2(__uint_as_float(uu & 0xFu), __uint_as_float(uu & 0xF0u)), xs2[base + 0], dd);
+            dd = __ffma2_rn(make_float2(__uint_as_float(uu & 0xF00u), __uint_as_float(uu & 0xF000u)), xs2[base + 1], dd);
+            dd = __ffma2_rn(make_float2(__uint_as_float(uu & 0xF0000u), __uint_as_float(bb & 0xF00u)), xs2[base + 2], dd);
+            dd = __ffma2_rn(make_float2(__uint_as_float(bb & 0xF000u), __uint_as_float(bb & 0xF0000u)), xs2[base + 3], dd);
           }
-          acc = warp_sum(acc);
-          const unsigned vi = (unsigned)(r + i);
-          if (lane == 0) a.logits[vi] = acc;
-          if (better(acc, vi, best, besti)) {
-            best = acc;
-            besti = vi;
-          }
+          const float dot = __fmaf_rn(dd.x + dd.y, kTwo64, -xg[g]);
+          acc = __fmaf_rn(__half2float(__ushort_as_half(sp[g])), dot, acc);
+        }
+        acc = warp_sum(acc);
+        const unsigned vi = (unsigned)(r + i);
+        if (lane == 0) a.logits[vi] = acc;
+        if (better(acc, vi, best, besti)) {
+          best = acc;
+          besti = vi;
         }
       }
-      C.release_stage();
+    }
+    C.release_stage();
+  }
+  if (lane == 0) {
+    C.scratch[kOffMisc + 16 + warp] = best;
+    reinterpret_cast<unsigned*>(C.scratch + kOffMisc + 32)[warp] = besti;
+  }
+}
+
+// ------------------------------------------------------------------ the kernel
+template <int GPL>
+__global__ void __launch_bounds__(kThreads, 1) decode_megakernel(const Args args) {
+  float* scratch = sm_scratch();
+  uint64_t* full = sm_full();
+  uint64_t* empty = sm_empty();
+  volatile int* flags = sm_flags();
+  Args* sa = sm_args();
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int c = blockIdx.x, G = gridDim.x;
+
+  if (tid == 0) {
+    *sa = args;
+    for (int s = 0; s < kStages; ++s) {
+      ptx::mbar_init(&full[s], 1);
+      ptx::mbar_init(&empty[s], kCW);
+    }
+    const int pos0 = args.st->pos, tok0 = args.st->token;
+    flags[0] = (tok0 < 0 || tok0 >= args.vocab || pos0 < 0 || pos0 >= args.max_pos) ? 1 : 0;
+    flags[1] = 0;
+    flags[2] = pos0;
+    flags[3] = 0;
+    flags[4] = 0;
+    flags[5] = tok0;
+    flags[6] = 0;
+    flags[7] = 0;
+    ptx::fence_mbar_init();
+  }
+  {  // split-K slots per tile of gate/up, then down
+    int* tab = reinterpret_cast<int*>(scratch + kOffTab);
+    for (int t = tid; t < args.tiles[GU]; t += kThreads) tab[t] = nslots(args, GU, t);
+    for (int t = tid; t < args.tiles[DOWN]; t += kThreads) tab[args.tiles[GU] + t] = nslots(args, DOWN, t);
+  }
+  __syncthreads();  // last block-wide barrier: the producer warp leaves below
+  const Args& a = *sa;
+  const int pos = flags[2];
+  const int token = flags[5];
+
+  if (warp == kCW) {
+    // ---------------- producer: stream this CTA's bytes in consumption order
+    if (lane == 0) {
+      uint32_t chunk = flags[0] ? kDead : 0u;
+#pragma unroll 1
+      for (int L = 0; L < a.L; ++L) {
+        chunk = produce_gemv(QKV, L, chunk);
+        chunk = produce_kv(L, chunk);
+        chunk = produce_gemv(OPR, L, chunk);
+        chunk = produce_gemv(GU, L, chunk);
+        chunk = produce_gemv(DOWN, L, chunk);
+        if (a.trace && L < kTraceLayers)
+          a.trace[(long long)G * kTracePerCta + (long long)c * kTraceLayers + L] = ptx::globaltimer();
+      }
+      produce_lm(chunk);
+      __threadfence_block();
+      flags[4] = 1;
+    }
+    return;
+  }
+
+  // ---------------- consumers
+  Cons C = make_cons(0);
+  C.stamp(0);
+  if (flags[0] && tid == 0) atomicExch(&a.st->error, 1);
+  const int H = a.H;
+  float* sB = scratch + kOffB;  // x copy for the norms
+
+  // embedding row (embed_lookup_q4, src/gemv.rs:710-736): every CTA builds x_0 locally
+  if (!C.aborted()) {
+    const uint8_t* row = a.lm + (long long)token * a.lm_row_bytes;
+    const uint16_t* sc = reinterpret_cast<const uint16_t*>(row + H / 2);
+    for (int e = tid; e < H; e += kCT) {
+      const uint8_t b = row[e >> 1];
+      const int q = ((e & 1) ? (b >> 4) : (b & 0xF)) - 8;
+      const float v = __fmul_rn(__half2float(__ushort_as_half(sc[e / kGroup])), (float)q);
+      sB[e] = v;
+      if (c == 0) a.xbuf[e] = v;
     }
   }
-  stamp(a, c, 2 + 8 * kTraceLayers + 1);
-  C.drain();
-  // CTA argmax -> global partial -> last CTA finishes the step
-  float* bvs = sMisc;
-  unsigned* bis = reinterpret_cast<unsigned*>(sMisc + kCW);
-  if (lane == 0) {
-    bvs[warp] = best;
-    bis[warp] = besti;
-  }
   C.bar();
+  C.stamp(1);
+
+  uint32_t chunk = 0;
+#pragma unroll 1
+  for (int L = 0; L < a.L; ++L) {
+    if (tid == 0) flags[7] = L;
+    const int tb = 2 + 8 * min(L, kTraceLayers - 1);
+    chunk = qkv_phase(L, chunk);
+    C.stamp(tb + 1);
+    chunk = attention_phase(L, chunk);
+    C.stamp(tb + 2);
+    chunk = o_phase(L, chunk);
+    C.stamp(tb + 4);
+    chunk = gu_phase(L, chunk);
+    C.stamp(tb + 6);
+    chunk = down_phase(L, chunk);
+    C.stamp(tb + 7);
+  }
+  if (tid == 0) flags[7] = -1;
+
+  lm_phase<GPL>(chunk);
+  C.stamp(2 + 8 * kTraceLayers + 1);
+  drain();
+  // CTA argmax -> global partial -> last CTA finishes the step
+  const float* bvs = scratch + kOffMisc + 16;
+  const unsigned* bis = reinterpret_cast<const unsigned*>(scratch + kOffMisc + 32);
   if (tid == 0) {
     float b = bvs[0];
     unsigned bi = bis[0];
@@ -964,10 +1187,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_megakernel(const Args a) {
     __stcg(a.lm_v + c, b);
     __stcg(a.lm_i + c, bi);
     const unsigned prev = ptx::atom_add_acqrel(a.cnt + c_lm(a), 1u);
-    sm.flags[1] = (prev == (unsigned)(G - 1));
+    flags[1] = (prev == (unsigned)(G - 1));
   }
   C.bar();
-  if (!sm.flags[1]) return;
+  if (!flags[1]) return;
   if (tid == 0) {
     float b = -INFINITY;
     unsigned bi = 0xFFFFFFFFu;

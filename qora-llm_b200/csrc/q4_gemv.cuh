@@ -150,16 +150,21 @@ struct EpiSwiGLU {
 // that position (src/gemv.rs:909-911).
 struct EpiQKV {
   float* q;
-  float* kc;  // this layer's K cache [max_seq][nkv]
+  float* kc;  // this layer's K cache, head-major [kv head][max_seq][128]
   float* vc;
+  long long hs;  // head stride of the cache (max_seq * 128)
   const StepState* st;
   const float* cos_t;
   const float* sin_t;
   int nq, nkv, rope, max_pos;
   QORA_DEV void store(int c, float v, int pos) const {
-    if (c < nq) q[c] = v;
-    else if (c < nq + nkv) kc[(long long)pos * nkv + (c - nq)] = v;
-    else vc[(long long)pos * nkv + (c - nq - nkv)] = v;
+    if (c < nq) {
+      q[c] = v;
+    } else {
+      const int j = (c < nq + nkv) ? c - nq : c - nq - nkv;  // within k or v
+      float* dst = (c < nq + nkv) ? kc : vc;
+      dst[(j / kHeadDim) * hs + (long long)pos * kHeadDim + (j % kHeadDim)] = v;
+    }
   }
   QORA_DEV void operator()(int t, const float* y) const {
     const int pos = st->pos;

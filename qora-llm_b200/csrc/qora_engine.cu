@@ -119,20 +119,32 @@ struct GroupRef {
   int g;
 };
 
-// Tile-major Q4 bytes for fused group list `refs` (all sources share K rows).
-std::vector<uint8_t> build_tiled(int K, const std::vector<GroupRef>& refs) {
+// Tile-major Q4 bytes for fused group list `refs` (all sources share K rows). tg == 8:
+// tiles of 8 groups, each 144-byte tile row = 8 groups' 16 nibble bytes then their 8
+// f16 scales. tg == 1: one group per tile, stored as 144-byte blocks of 8 consecutive
+// rows (8 x 16 nibble bytes, then the 8 rows' scales; K % 8 == 0), which keeps every
+// 16-byte row load aligned. Either way a tile row costs 18 bytes per group.
+std::vector<uint8_t> build_tiled(int K, const std::vector<GroupRef>& refs, int tg = kTileGroups) {
   const int G = (int)refs.size();
-  const int tiles = (G + kTileGroups - 1) / kTileGroups;
-  std::vector<uint8_t> buf((size_t)tiles * K * kTiledRowBytes, 0);
+  const int tiles = (G + tg - 1) / tg;
+  std::vector<uint8_t> buf((size_t)tiles * K * tg * 18, 0);
   for (int r = 0; r < K; ++r) {
-    for (int f = 0; f < tiles * kTileGroups; ++f) {
-      const int t = f / kTileGroups, gi = f % kTileGroups;
-      uint8_t* dst = buf.data() + ((size_t)t * K + r) * kTiledRowBytes;
+    for (int f = 0; f < tiles * tg; ++f) {
+      const int t = f / tg, gi = f % tg;
+      uint8_t* blk;  // 144-byte block holding this (group, row)
+      int slot;      // 16-byte slot within the block
+      if (tg == 1) {
+        blk = buf.data() + ((size_t)t * K + (r & ~7)) * 18;
+        slot = r & 7;
+      } else {
+        blk = buf.data() + ((size_t)t * K + r) * kTiledRowBytes;
+        slot = gi;
+      }
       if (f >= G || refs[f].m == nullptr) continue;  // zeros: scale 0 -> contributes 0
       const qora_matrix_view* m = refs[f].m;
       const size_t gpr = m->n / kGroup;
-      std::memcpy(dst + gi * 16, m->packed + ((size_t)r * gpr + refs[f].g) * 16, 16);
-      std::memcpy(dst + kTileGroups * 16 + gi * 2, m->scales + (size_t)r * gpr + refs[f].g, 2);
+      std::memcpy(blk + slot * 16, m->packed + ((size_t)r * gpr + refs[f].g) * 16, 16);
+      std::memcpy(blk + 128 + slot * 2, m->scales + (size_t)r * gpr + refs[f].g, 2);
     }
   }
   return buf;
@@ -204,6 +216,7 @@ std::vector<float> f16_to_f32(const uint16_t* h, size_t n) {
 
 struct LayerDev {
   DevQ4 qkv, o, gu, down;
+  DevQ4 qkv1, o1;  // one-group tiles of q|k|v and o_proj for the persistent kernel
   float* g_in = nullptr;
   float* g_post = nullptr;
   int rope = 0;
@@ -243,7 +256,10 @@ struct qora_engine {
   std::string mk_why;
   int mk_G = 0;
   int mk_slots[4] = {0, 0, 0, 0};
-  int mk_sub0[4] = {0, 0, 0, 0}, mk_subn[4] = {0, 0, 0, 0}, mk_segs[4] = {0, 0, 0, 0};
+  int mk_sub0[4] = {0, 0, 0, 0}, mk_subn[4] = {0, 0, 0, 0};
+  uint32_t mk_max_seq = 0;
+  float* mk_xmid = nullptr;
+  float* mk_qkv = nullptr;
   int mk_cpl = 0, mk_ncnt = 0;
   float* mk_xbuf = nullptr;
   float* mk_part[4] = {nullptr, nullptr, nullptr, nullptr};
@@ -384,11 +400,13 @@ qora_status upload(qora_engine* e, void* dst, const void* src, size_t bytes) {
   return QORA_OK;
 }
 
-qora_status upload_q4(qora_engine* e, int K, const std::vector<GroupRef>& refs, DevQ4& out) {
+qora_status upload_q4(qora_engine* e, int K, const std::vector<GroupRef>& refs, DevQ4& out,
+                      int tg = kTileGroups) {
+  if (tg != kTileGroups && (tg != 1 || K % 8 != 0)) return fail(QORA_ERR_UNSUPPORTED, "tile shape");
   out.K = K;
   out.G = (int)refs.size();
-  out.tiles = (out.G + kTileGroups - 1) / kTileGroups;
-  std::vector<uint8_t> host = build_tiled(K, refs);
+  out.tiles = (out.G + tg - 1) / tg;
+  std::vector<uint8_t> host = build_tiled(K, refs, tg);
   QCHECK(e->alloc(&out.buf, host.size()));
   return upload(e, out.buf, host.data(), host.size());
 }
@@ -406,9 +424,11 @@ qora_status build_layer(qora_engine* e, const qora_weights_view* w, uint32_t i) 
   add_all(L.k_proj);
   add_all(L.v_proj);
   QCHECK(upload_q4(e, H, refs, d.qkv));
+  QCHECK(upload_q4(e, H, refs, d.qkv1, 1));
   refs.clear();
   add_all(L.o_proj);
   QCHECK(upload_q4(e, (int)L.o_proj.k, refs, d.o));
+  QCHECK(upload_q4(e, (int)L.o_proj.k, refs, d.o1, 1));
   refs.clear();
   const int gI = (int)(L.gate_proj.n / kGroup);
   for (int t = 0; t < gI / 4; ++t) {
@@ -543,20 +563,6 @@ qora_status mega_occupancy(int* blocks) {
   return QORA_OK;
 }
 
-// Segments (tile, first row, end row) of CTA lc of a g-CTA subset over a tiles x K
-// matrix, in the order the kernel walks them (mirrors mk::for_each_segment).
-template <class F>
-void host_segments(int K, int tiles, int g, int lc, F&& f) {
-  const long long total = (long long)tiles * K;
-  const long long lin0 = (long long)lc * total / g, lin1 = (long long)(lc + 1) * total / g;
-  for (long long p = lin0; p < lin1;) {
-    const long long t = p / K, r0 = p - t * K;
-    const long long pe = std::min(lin1, (t + 1) * K);
-    f((int)t, (int)r0, (int)(pe - t * K));
-    p = pe;
-  }
-}
-
 // Decide whether the persistent kernel can run this geometry and allocate its buffers.
 // q|k|v runs on the last gq CTAs and o_proj on the go CTAs before them, so that their
 // few split-K partials can be summed directly by the consumers; gate/up and down run on
@@ -565,47 +571,41 @@ qora_status mega_init(qora_engine* e) {
   e->mk_ok = false;
   const int H = (int)e->hidden, G = e->sms;
   const LayerDev& d0 = e->layers[0];
-  const int nh = (int)e->nh;
+  const int nh = (int)e->nh, nkvh = (int)e->nkv;
   auto no = [&](const char* why) {
     e->mk_why = why;
     return QORA_OK;
   };
   if (H != 1024 && H != 2048) return no("hidden must be 1024 or 2048");
-  if (nh != 8 && nh != 16) return no("num_heads must be 8 or 16");
+  if (nh != mk::kHeadsPerKV * nkvh || nh > 16) return no("needs 4 query heads per KV head and at most 16 heads");
   if (G < 16 || G > mk::kMaxUnits) return no("SM count outside the supported range");
-  const int gq = std::min(48, G / 3), go = std::min(32, G / 4);
-  const int sub0[4] = {G - gq, G - gq - go, 0, 0};
-  const int subn[4] = {gq, go, G, G};
-  const DevQ4* mats[4] = {&d0.qkv, &d0.o, &d0.gu, &d0.down};
+  // q|k|v and o_proj: one CTA per 32-column group (q|k|v on the last CTAs, o_proj on the
+  // first); gate/up and down: split-K over all CTAs
+  const DevQ4* mats[4] = {&d0.qkv1, &d0.o1, &d0.gu, &d0.down};
+  if (d0.qkv1.G > G || d0.o1.G > G) return no("more q|k|v or o_proj column groups than SMs");
+  const int sub0[4] = {G - d0.qkv1.G, 0, 0, 0};
+  const int subn[4] = {d0.qkv1.G, d0.o1.G, G, G};
   for (int m = 0; m < 4; ++m) {
     const long long total = (long long)mats[m]->tiles * mats[m]->K;
-    if (total < subn[m]) return no("matrix too small for one segment per CTA");
-    if ((total + subn[m] - 1) / subn[m] + 1 > mk::kXsCap) return no("per-CTA rows exceed the shared input buffer");
-    int segs = 0;
-    for (int lc = 0; lc < subn[m]; ++lc) {
-      bool bad = false;
-      host_segments(mats[m]->K, mats[m]->tiles, subn[m], lc, [&](int, int r0, int r1) {
-        ++segs;
-        // o_proj: the attention rows of one segment must come from at most 8 heads
-        if (m == 1 && (r1 - 1) / kHeadDim - r0 / kHeadDim + 1 > 8) bad = true;
-      });
-      if (bad) return no("o_proj segment spans too many heads");
-    }
+    if ((m < 2 && mats[m]->K > mk::kXsCap) || (total + subn[m] - 1) / subn[m] > mk::kXsCap)
+      return no("per-CTA rows exceed the shared input buffer");
+    if (total * subn[m] >= (1ll << 31)) return no("matrix too large for 32-bit split-K indexing");
+    if ((total + subn[m] - 1) / subn[m] > mats[m]->K) return no("a CTA's rows would span more than two tiles");
+    if (mats[m]->K <= mk::kCT) return no("matrix with too few rows");
     e->mk_sub0[m] = sub0[m];
     e->mk_subn[m] = subn[m];
-    e->mk_segs[m] = segs;
   }
+  if (d0.gu.tiles + d0.down.tiles > mk::kMaxTabTiles) return no("too many gate/up and down tiles");
   if (H > mk::kBFloats) return no("hidden larger than the shared x buffer");
-  if ((int)e->nkv * kHeadDim > mk::kMaxVItems * mk::kCT) return no("too many KV heads for the P.V pass");
-  if ((int)e->nkv * kHeadDim * 2 > 1024) return no("new k|v row larger than its shared buffer");
-  if ((int)e->nh > 16 || (int)e->nh % (int)e->nkv != 0 || (int)(e->nh / e->nkv) > 4) return no("head grouping");
+  if (nh * (mk::kMaxUnits / nkvh + 1) > mk::kBFloats) return no("attention merge weights do not fit");
   if (e->lm_row_bytes > mk::kStageBytes) return no("embedding row larger than a stage");
-  if ((int)e->nkv * kHeadDim * 4 > mk::kStageBytes) return no("KV row larger than a stage");
   int blocks = 0;
   if (H == 2048) QCHECK(mega_occupancy<2>(&blocks)); else QCHECK(mega_occupancy<1>(&blocks));
   if (blocks < 1) return no("megakernel does not fit one CTA per SM");
   e->mk_G = G;
-  for (int m = 0; m < 4; ++m) {
+  // longest cache whose attention units (kv head x chunk of <= kMaxAttnChunk) fit the grid
+  e->mk_max_seq = (uint32_t)mk::kMaxAttnChunk * (uint32_t)(G / nkvh);
+  for (int m = 2; m < 4; ++m) {
     GemvShape sh = plan_gemv(mats[m]->K, mats[m]->tiles, subn[m]);
     e->mk_slots[m] = sh.plan.max_slots;
     QCHECK(e->alloc(&e->mk_part[m], (size_t)mats[m]->tiles * sh.plan.max_slots * kTileCols));
@@ -615,6 +615,8 @@ qora_status mega_init(qora_engine* e) {
   QCHECK(e->alloc(&e->mk_cnt, e->mk_ncnt));
   QCUDA(cudaMemset(e->mk_cnt, 0, (size_t)e->mk_ncnt * sizeof(unsigned)));
   QCHECK(e->alloc(&e->mk_xbuf, (size_t)(e->num_layers + 1) * H));
+  QCHECK(e->alloc(&e->mk_xmid, (size_t)e->num_layers * H));
+  QCHECK(e->alloc(&e->mk_qkv, (size_t)d0.qkv1.G * kGroup));
   QCHECK(e->alloc(&e->mk_lm_v, G));
   QCHECK(e->alloc(&e->mk_lm_i, G));
   e->mk_ok = true;
@@ -627,8 +629,8 @@ qora_status mega_prepare(qora_engine* e, qora_kv* kv) {
   std::vector<mk::Layer> hl(L);
   for (int i = 0; i < L; ++i) {
     const LayerDev& d = e->layers[i];
-    hl[i].w[0] = d.qkv.buf;
-    hl[i].w[1] = d.o.buf;
+    hl[i].w[0] = d.qkv1.buf;
+    hl[i].w[1] = d.o1.buf;
     hl[i].w[2] = d.gu.buf;
     hl[i].w[3] = d.down.buf;
     hl[i].g_in = d.g_in;
@@ -639,15 +641,14 @@ qora_status mega_prepare(qora_engine* e, qora_kv* kv) {
   }
   QCHECK(kv->alloc(&kv->mk_layers, L));
   QCUDA(cudaMemcpy(kv->mk_layers, hl.data(), L * sizeof(mk::Layer), cudaMemcpyHostToDevice));
-  const int max_units = std::max<int>(G, (int)((kv->max_seq + mk::kMaxAttnChunk - 1) / mk::kMaxAttnChunk));
-  QCHECK(kv->alloc(&kv->mk_att_o, (size_t)max_units * e->nh * kHeadDim));
-  QCHECK(kv->alloc(&kv->mk_att_ml, (size_t)max_units * e->nh * 2));
+  QCHECK(kv->alloc(&kv->mk_att_o, (size_t)G * mk::kHeadsPerKV * kHeadDim));
+  QCHECK(kv->alloc(&kv->mk_att_ml, (size_t)G * mk::kHeadsPerKV * 2));
   mk::Args& a = kv->mk_args;
   a = mk::Args{};
   a.layers = kv->mk_layers;
   a.L = L;
   const LayerDev& d0 = e->layers[0];
-  const DevQ4* mats[4] = {&d0.qkv, &d0.o, &d0.gu, &d0.down};
+  const DevQ4* mats[4] = {&d0.qkv1, &d0.o1, &d0.gu, &d0.down};
   for (int m = 0; m < 4; ++m) {
     a.K[m] = mats[m]->K;
     a.tiles[m] = mats[m]->tiles;
@@ -655,15 +656,12 @@ qora_status mega_prepare(qora_engine* e, qora_kv* kv) {
     a.part[m] = e->mk_part[m];
     a.sub0[m] = e->mk_sub0[m];
     a.subn[m] = e->mk_subn[m];
-    a.segs[m] = e->mk_segs[m];
   }
   a.H = (int)e->hidden;
-  a.I = (int)e->inter;
   a.nq = d0.nq;
   a.nkvw = d0.nkv;
   a.nh = (int)e->nh;
   a.nkvh = (int)e->nkv;
-  a.grp = kGrp;
   a.vocab = (int)e->vocab;
   a.lm_row_bytes = (int)e->lm_row_bytes;
   {
@@ -672,6 +670,7 @@ qora_status mega_prepare(qora_engine* e, qora_kv* kv) {
     if (rows >= mk::kCW) rows -= rows % mk::kCW;
     a.lm_rows_per_stage = rows;
   }
+  a.head_stride = (long long)kv->max_seq * kHeadDim;
   a.lm = e->lm_table;
   a.final_gamma = e->final_gamma;
   a.cos_t = e->rope_cos;
@@ -680,10 +679,11 @@ qora_status mega_prepare(qora_engine* e, qora_kv* kv) {
   for (auto& Ld : e->layers) any_rope |= (Ld.rope != 0);
   a.max_pos = (int)std::min<uint32_t>(kv->max_seq, any_rope ? e->rope_rows : kv->max_seq);
   a.xbuf = e->mk_xbuf;
+  a.xmid = e->mk_xmid;
+  a.qkv = e->mk_qkv;
   a.logits = e->logits;
   a.att_o = kv->mk_att_o;
   a.att_ml = kv->mk_att_ml;
-  a.max_units = max_units;
   a.cnt = e->mk_cnt;
   a.cpl = e->mk_cpl;
   a.n_cnt = e->mk_ncnt;
@@ -735,7 +735,7 @@ qora_status launch_layer(qora_engine* e, qora_kv* kv, uint32_t li) {
   cudaStream_t s = e->stream;
   float* kc = kv->k + li * kv->layer_stride();
   float* vc = kv->v + li * kv->layer_stride();
-  EpiQKV eq{e->q, kc, vc, kv->st, e->rope_cos, e->rope_sin, d.nq, d.nkv, d.rope,
+  EpiQKV eq{e->q, kc, vc, (long long)kv->max_seq * kHeadDim, kv->st, e->rope_cos, e->rope_sin, d.nq, d.nkv, d.rope,
             (int)std::min<uint32_t>(kv->max_seq, d.rope ? e->rope_rows : kv->max_seq)};
   QCHECK(launch_gemv(d.qkv.src(), e->sh_qkv, e->partials, e->counters,
                      ProNorm{e->x, d.g_in, (int)e->hidden}, eq, s));
@@ -743,6 +743,7 @@ qora_status launch_layer(qora_engine* e, qora_kv* kv, uint32_t li) {
   aa.q = e->q;
   aa.kc = kc;
   aa.vc = vc;
+  aa.hs = (long long)kv->max_seq * kHeadDim;
   aa.out = e->attn;
   aa.st = kv->st;
   aa.nkv = (int)e->nkv;
@@ -813,7 +814,7 @@ qora_status ensure_graph(qora_engine* e, qora_kv* kv) {
 // prepare whichever decode path this engine uses (graph of per-op kernels, or the
 // persistent megakernel)
 bool kv_uses_mega(const qora_engine* e, const qora_kv* kv) {
-  return e->mk_ok && e->use_mega && kv->max_seq <= (uint32_t)(mk::kMaxAttnChunk * mk::kMaxUnits);
+  return e->mk_ok && e->use_mega && kv->max_seq <= e->mk_max_seq;
 }
 
 qora_status step_prepare(qora_engine* e, qora_kv* kv) {
@@ -1160,10 +1161,12 @@ qora_status qora_kv_import(qora_kv* kv, uint32_t layer, const float* k, const fl
   if (layer >= kv->e->num_layers) return fail(QORA_ERR_RANGE, "layer %u", layer);
   if (seq_len > kv->max_seq) return fail(QORA_ERR_RANGE, "seq_len %u > max_seq %u", seq_len, kv->max_seq);
   QCUDA(cudaSetDevice(kv->e->device));
-  const size_t bytes = (size_t)seq_len * kv->e->nkv * kHeadDim * sizeof(float);
-  if (bytes) {
-    QCUDA(cudaMemcpy(kv->k + layer * kv->layer_stride(), k, bytes, cudaMemcpyHostToDevice));
-    QCUDA(cudaMemcpy(kv->v + layer * kv->layer_stride(), v, bytes, cudaMemcpyHostToDevice));
+  // host rows [seq][nkv*128] -> device head-major [nkv][max_seq][128]
+  const size_t row = (size_t)kv->e->nkv * kHeadDim * sizeof(float), hb = kHeadDim * sizeof(float);
+  for (uint32_t j = 0; seq_len && j < kv->e->nkv; ++j) {
+    const size_t off = layer * kv->layer_stride() + (size_t)j * kv->max_seq * kHeadDim;
+    QCUDA(cudaMemcpy2D(kv->k + off, hb, k + (size_t)j * kHeadDim, row, hb, seq_len, cudaMemcpyHostToDevice));
+    QCUDA(cudaMemcpy2D(kv->v + off, hb, v + (size_t)j * kHeadDim, row, hb, seq_len, cudaMemcpyHostToDevice));
   }
   kv->len[layer] = seq_len;
   return QORA_OK;
@@ -1178,9 +1181,12 @@ qora_status qora_kv_export(const qora_kv* kv, uint32_t layer, float* k, float* v
   if (seq_len > kv->len[layer]) return fail(QORA_ERR_RANGE, "seq_len %u > length %u", seq_len, kv->len[layer]);
   QCUDA(cudaSetDevice(kv->e->device));
   QCUDA(cudaStreamSynchronize(kv->e->stream));
-  const size_t bytes = (size_t)seq_len * kv->e->nkv * kHeadDim * sizeof(float);
-  QCUDA(cudaMemcpy(k, kv->k + layer * kv->layer_stride(), bytes, cudaMemcpyDeviceToHost));
-  QCUDA(cudaMemcpy(v, kv->v + layer * kv->layer_stride(), bytes, cudaMemcpyDeviceToHost));
+  const size_t row = (size_t)kv->e->nkv * kHeadDim * sizeof(float), hb = kHeadDim * sizeof(float);
+  for (uint32_t j = 0; seq_len && j < kv->e->nkv; ++j) {
+    const size_t off = layer * kv->layer_stride() + (size_t)j * kv->max_seq * kHeadDim;
+    QCUDA(cudaMemcpy2D(k + (size_t)j * kHeadDim, row, kv->k + off, hb, hb, seq_len, cudaMemcpyDeviceToHost));
+    QCUDA(cudaMemcpy2D(v + (size_t)j * kHeadDim, row, kv->v + off, hb, hb, seq_len, cudaMemcpyDeviceToHost));
+  }
   return QORA_OK;
 }
 
@@ -1337,14 +1343,15 @@ qora_status qora_engine_time_kernel(qora_engine* e, qora_kv* kv, int kernel, uin
     float* vc = kv->v + li * kv->layer_stride();
     switch (kernel) {
       case QORA_KERNEL_QKV: {
-        EpiQKV eq{e->q, kc, vc, kv->st, e->rope_cos, e->rope_sin, d.nq, d.nkv, d.rope,
+        EpiQKV eq{e->q, kc, vc, (long long)kv->max_seq * kHeadDim, kv->st, e->rope_cos, e->rope_sin, d.nq, d.nkv, d.rope,
                   (int)std::min<uint32_t>(kv->max_seq, d.rope ? e->rope_rows : kv->max_seq)};
         return launch_gemv(d.qkv.src(), e->sh_qkv, e->partials, e->counters,
                            ProNorm{e->x, d.g_in, (int)e->hidden}, eq, s);
       }
       case QORA_KERNEL_ATTENTION: {
         AttnArgs aa{};
-        aa.q = e->q; aa.kc = kc; aa.vc = vc; aa.out = e->attn; aa.st = kv->st;
+        aa.q = e->q; aa.kc = kc; aa.vc = vc; aa.hs = (long long)kv->max_seq * kHeadDim;
+        aa.out = e->attn; aa.st = kv->st;
         aa.nkv = (int)e->nkv; aa.nc = kv->attn_nc; aa.scale = 1.0f / std::sqrt((float)kHeadDim);
         aa.part_o = kv->attn_o; aa.part_ml = kv->attn_ml; aa.counters = kv->attn_counters;
         attn_decode_kernel<<<dim3(e->nkv, kv->attn_nc), kAttnThreads, 0, s>>>(aa);
