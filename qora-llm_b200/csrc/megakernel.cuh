@@ -50,10 +50,10 @@ namespace mk {
 constexpr int kCW = 15;                // consumer warps
 constexpr int kCT = kCW * 32;          // consumer threads
 constexpr int kThreads = kCT + 32;     // + one producer warp
-constexpr int kStageBytes = 17280;     // 960 one-group rows = 120 eight-group rows = 15 embedding rows
-constexpr int kStages = 11;
+constexpr int kStageBytes = 34560;     // 1920 one-group rows = 240 eight-group rows = 30 embedding rows
+constexpr int kStages = 5;
 constexpr int kBar = 1;                // named barrier of the consumer warps
-constexpr int kKVRows = kStageBytes / (kHeadDim * 4);  // K or V rows of one head per stage (33)
+constexpr int kKVRows = kStageBytes / (kHeadDim * 4);  // K or V rows of one head per stage (67)
 constexpr int kMinAttnChunk = 64;
 constexpr int kMaxAttnChunk = 1024;
 constexpr int kMaxUnits = 256;         // attention units (kv head x chunk); units <= CTAs
@@ -471,7 +471,9 @@ template <int TG>
 __device__ __noinline__ uint32_t gemv_stream(int m, int L, uint32_t chunk) {
   constexpr int W = 32 / TG;        // rows per warp pass
   constexpr int RPS = kStageBytes / (18 * TG);  // rows per stage
+  constexpr int NP = RPS / (kCW * W);            // rows per lane per stage
   static_assert(TG == 1 || TG == 8, "tile width");
+  static_assert(NP * kCW * W == RPS, "stage rows");
   Cons C = make_cons(chunk);
   const Args& a = C.a();
   const float* xs = C.scratch;
@@ -495,23 +497,27 @@ __device__ __noinline__ uint32_t gemv_stream(int m, int L, uint32_t chunk) {
       const uint8_t* stg = C.acquire_stage();
       const int R = min(RPS, r1 - cr);
       if (C.stage_ok) {
+        // NP rows per lane, all loads issued before the math; 144-byte blocks: TG == 8
+        // one row of 8 groups, TG == 1 eight rows of one group
         const float* xr = xs + off + (cr - r0);
-        const int i0 = C.warp * W + sub, i1 = i0 + kCW * W;
-        const bool v0 = i0 < R, v1 = i1 < R;
-        // 144-byte blocks: TG == 8 one row of 8 groups, TG == 1 eight rows of one group
-        const int j0 = v0 ? i0 : 0, j1 = v1 ? i1 : 0;
-        const uint8_t* blk0 = stg + (TG == 8 ? j0 : j0 >> 3) * 144;
-        const uint8_t* blk1 = stg + (TG == 8 ? j1 : j1 >> 3) * 144;
-        const int q0 = TG == 8 ? gi : (j0 & 7), q1 = TG == 8 ? gi : (j1 & 7);
-        const uint4 w0 = *reinterpret_cast<const uint4*>(blk0 + q0 * 16);
-        const uint4 w1 = *reinterpret_cast<const uint4*>(blk1 + q1 * 16);
-        const uint16_t s0 = *reinterpret_cast<const uint16_t*>(blk0 + 128 + q0 * 2);
-        const uint16_t s1 = *reinterpret_cast<const uint16_t*>(blk1 + 128 + q1 * 2);
-        const float c0 = v0 ? __half2float(__ushort_as_half(s0)) * xr[i0] : 0.0f;
-        const float c1 = v1 ? __half2float(__ushort_as_half(s1)) * xr[i1] : 0.0f;
-        cs += c0 + c1;
-        q4_fma_chunk(w0, c0, acc);
-        q4_fma_chunk(w1, c1, acc);
+        uint4 w[NP];
+        float cf[NP];
+#pragma unroll
+        for (int k = 0; k < NP; ++k) {
+          const int i = C.warp * W + sub + k * kCW * W;
+          const bool ok = i < R;
+          const int j = ok ? i : 0;
+          const uint8_t* blk = stg + (TG == 8 ? j : j >> 3) * 144;
+          const int q = TG == 8 ? gi : (j & 7);
+          w[k] = *reinterpret_cast<const uint4*>(blk + q * 16);
+          const uint16_t sv = *reinterpret_cast<const uint16_t*>(blk + 128 + q * 2);
+          cf[k] = ok ? __half2float(__ushort_as_half(sv)) * xr[j] : 0.0f;
+        }
+#pragma unroll
+        for (int k = 0; k < NP; ++k) {
+          cs += cf[k];
+          q4_fma_chunk(w[k], cf[k], acc);
+        }
       }
       C.release_stage();
       C.fstamp();
@@ -725,14 +731,19 @@ __device__ __noinline__ uint32_t attention_phase(int L, uint32_t chunk) {
     vc[(long long)pos * kHeadDim + d] = v;
   }
   C.bar();
-  // scores: 4 rows per warp pass (8 lanes each), 60 row slots >= kKVRows
+  // scores: 4 rows per warp pass (8 lanes each), 60 rows per CTA pass
   const int li = lane & 7, ri = warp * 4 + (lane >> 3);
 #pragma unroll 1
   for (int s = s0; s < sc1; s += kKVRows) {
     const uint8_t* stg = C.acquire_stage();
     const int nr = min(kKVRows, sc1 - s);
-    if (C.stage_ok)
-      kscore(sq, reinterpret_cast<const float*>(stg) + min(ri, nr - 1) * kHeadDim, sc, s - s0 + ri, ri < nr, li);
+    if (C.stage_ok) {
+#pragma unroll 1
+      for (int rb = 0; rb < nr; rb += kCW * 4) {
+        const int i = rb + ri;
+        kscore(sq, reinterpret_cast<const float*>(stg) + min(i, nr - 1) * kHeadDim, sc, s - s0 + i, i < nr, li);
+      }
+    }
     C.release_stage();
     C.fstamp();
   }
