@@ -142,7 +142,7 @@ QORA_DEV Args* sm_args() { return reinterpret_cast<Args*>(reinterpret_cast<uint8
 // 1: QKV done, 2: attention done, 3: attention partials ready (O CTAs), 4: O done,
 // 5: x_mid ready, 6: GU done, 7: DOWN done}, then [2+8*kTraceLayers] lm start, [+1] end.
 // Then, per CTA, one stamp per layer when the producer has issued that layer's last
-// copy; then kTraceFine stamps of layer 1 at finer points (stages, barriers) per CTA.
+// copy; then kTraceFine stamps of layer 1 at finer points (phase steps) per CTA.
 constexpr int kTraceLayers = 64;
 constexpr int kTracePerCta = 2 + 8 * kTraceLayers + 2;
 constexpr int kTraceFine = 64;
@@ -278,16 +278,6 @@ __device__ __noinline__ uint32_t produce_lm(uint32_t chunk) {
 }
 
 // ------------------------------------------------------------------ consumer state
-// fine-grained trace stamp of layer 1 (thread 0, tracing enabled)
-__device__ __noinline__ void fstamp_write() {
-  volatile int* flags = sm_flags();
-  const int fine = flags[6];
-  if (fine < kTraceFine)
-    sm_args()->trace[(long long)gridDim.x * (kTracePerCta + kTraceLayers) + (long long)blockIdx.x * kTraceFine +
-                     fine] = ptx::globaltimer();
-  flags[6] = fine + 1;
-}
-
 struct Cons {
   const Args* ap;         // shared-memory copy of the kernel arguments
   uint8_t* ring;
@@ -320,8 +310,14 @@ struct Cons {
     if (ap->trace && tid == 0) ap->trace[(long long)c * kTracePerCta + idx] = ptx::globaltimer();
   }
 
-  QORA_DEV void fstamp() {
-    if (tid == 0 && flags[7] == 1 && ap->trace) fstamp_write();
+  QORA_DEV void fstamp() {  // fine-grained trace stamp of layer 1 (thread 0, tracing enabled)
+    if (tid == 0 && flags[7] == 1 && ap->trace) {
+      const int fine = flags[6];
+      if (fine < kTraceFine)
+        ap->trace[(long long)G * (kTracePerCta + kTraceLayers) + (long long)c * kTraceFine + fine] =
+            ptx::globaltimer();
+      flags[6] = fine + 1;
+    }
   }
 
   // thread 0 spins (bounded) until *p >= target, then an acquire fence; no barrier
@@ -416,7 +412,7 @@ QORA_DEV Cons make_cons(uint32_t chunk) {
   return C;
 }
 
-QORA_DEV float rms_inv_from(float sumsq, int H) {
+__device__ __noinline__ float rms_inv_from(float sumsq, int H) {
   return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sumsq, (float)H), 1e-6f)));
 }
 
@@ -461,10 +457,11 @@ QORA_DEV void fill_norm_inputs(const Cons& C, const float* sB, float inv, const 
 }
 
 // ------------------------------------------------------------------ phases
-__device__ __noinline__ void seg_done(int m, int L, int t, int slot);
+__device__ __noinline__ void seg_store(int m, int L, int t, int slot);
+__device__ __noinline__ void gemv_finish(int m, int L, int t);
 
 // Stream this CTA's segments of matrix m (TG groups per tile) through the ring and
-// reduce each segment's 32*TG sums into Y, then run seg_done. xs holds the (pre-scaled)
+// reduce each segment's 32*TG sums into Y, then store and publish them. xs holds the (pre-scaled)
 // inputs of all segments back to back. Lane (sub, gi) takes group gi of rows sub and
 // sub + 15*(32/TG) of each warp's share of a stage.
 template <int TG>
@@ -520,7 +517,6 @@ __device__ __noinline__ uint32_t gemv_stream(int m, int L, uint32_t chunk) {
         }
       }
       C.release_stage();
-      C.fstamp();
     }
     off += r1 - r0;
 
@@ -555,75 +551,85 @@ __device__ __noinline__ uint32_t gemv_stream(int m, int L, uint32_t chunk) {
     }
     C.bar();
     C.fstamp();
-    seg_done(m, L, t, slot);
+    seg_store(m, L, t, slot);
+    gemv_finish(m, L, t);
     C.fstamp();
     p += r1 - r0;
   }
   return C.chunk;
 }
 
-// What happens to a finished segment: q|k|v and o_proj results are final (one group
-// per CTA); gate/up and down store their split-K partial; the last down segment of an
-// output tile writes the next residual for the tile.
-__device__ __noinline__ void seg_done(int m, int L, int t, int slot) {
+// A finished segment's sums (Y): q|k|v and o_proj results are final (one group per
+// CTA); gate/up and down store their split-K partial.
+__device__ __noinline__ void seg_store(int m, int L, int t, int slot) {
   Cons C = make_cons(0);
   const Args& a = C.a();
   const float* y = C.scratch + kOffY;
-  const int H = a.H;
   if (m == QKV) {
     if (C.tid < 32) a.qkv[t * 32 + C.tid] = y[C.tid];
-    C.publish(a.cnt + c_qkv(a, L));
-    return;
-  }
-  if (m == OPR) {
+  } else if (m == OPR) {
     if (C.tid < 32) {
-      const long long col = (long long)L * H + t * 32 + C.tid;
+      const long long col = (long long)L * a.H + t * 32 + C.tid;
       a.xmid[col] = __fadd_rn(__ldcg(a.xbuf + col), y[C.tid]);
     }
-    C.publish(a.cnt + c_o(a, L));
+  } else if (C.tid < 256) {
+    __stcg(a.part[m] + ((long long)t * a.slots[m] + slot) * 256 + C.tid, y[C.tid]);
+  }
+}
+
+// Publish a stored segment of tile t (a release: barrier, fence, relaxed increment);
+// the last down segment of an output tile writes the next residual for the tile.
+__device__ __noinline__ void gemv_finish(int m, int L, int t) {
+  Cons C = make_cons(0);
+  const Args& a = C.a();
+  const int H = a.H;
+  C.bar();
+  if (m != DOWN) {
+    if (C.tid == 0) {
+      ptx::fence_acq_rel_gpu();
+      if (m == QKV) ptx::red_add_relaxed(a.cnt + c_qkv(a, L), 1u);
+      if (m == OPR) ptx::red_add_relaxed(a.cnt + c_o(a, L), 1u);
+      if (m == GU) ptx::red_add_relaxed(a.cnt + c_gu_arr(a, L, t), 1u);
+    }
     return;
   }
-  if (C.tid < 256) __stcg(a.part[m] + ((long long)t * a.slots[m] + slot) * 256 + C.tid, y[C.tid]);
-  if (m == GU) {
-    C.publish(a.cnt + c_gu_arr(a, L, t));
-    return;
-  }
-  C.bar();
-  if (C.tid == 0) {
-    const unsigned prev = ptx::atom_add_acqrel(a.cnt + c_dn_arr(a, L, t), 1u);
-    C.flags[1] = (prev == (unsigned)(C.ns(DOWN, t) - 1));
-  }
-  C.bar();
-  if (C.flags[1]) {
-    float4* parts = reinterpret_cast<float4*>(C.scratch + kOffB);  // [kDnParts][64]
-    const int b = C.tid & 63, p = C.tid >> 6;
-    const long long col = (long long)L * H + t * 256 + 4 * b;
-    const float4 xm = (C.tid < 64) ? ldcg4(a.xmid + col) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    if (p < kDnParts) {
-      const int ns = C.ns(DOWN, t);
-      const float* pd = a.part[DOWN] + (long long)t * a.slots[DOWN] * 256 + 4 * b;
-      float4 s = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-#pragma unroll 1
-      for (int k0 = p; k0 < ns; k0 += 4 * kDnParts) {
-        float4 v[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) v[j] = (k0 + j * kDnParts < ns) ? ldcg4(pd + (k0 + j * kDnParts) * 256) : s;
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          if (k0 + j * kDnParts < ns) s = f4add(s, v[j]);
-      }
-      parts[p * 64 + b] = s;
+  {
+    if (C.tid == 0) {
+      const unsigned prev = ptx::atom_add_acqrel(a.cnt + c_dn_arr(a, L, t), 1u);
+      C.flags[1] = (prev == (unsigned)(C.ns(DOWN, t) - 1));
     }
     C.bar();
-    if (C.tid < 64) {
-      float4 d = parts[b];
+    if (C.flags[1]) {
+      float4* parts = reinterpret_cast<float4*>(C.scratch + kOffB);  // [kDnParts][64]
+      const int b = C.tid & 63, p = C.tid >> 6;
+      const long long col = (long long)L * H + t * 256 + 4 * b;
+      const float4 xm = (C.tid < 64) ? ldcg4(a.xmid + col) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      if (p < kDnParts) {
+        const int ns = C.ns(DOWN, t);
+        const float* pd = a.part[DOWN] + (long long)t * a.slots[DOWN] * 256 + 4 * b;
+        float4 s = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 #pragma unroll 1
-      for (int q = 1; q < kDnParts; ++q) d = f4add(d, parts[q * 64 + b]);
-      *reinterpret_cast<float4*>(a.xbuf + col + H) = f4add(xm, d);
+        for (int k0 = p; k0 < ns; k0 += 4 * kDnParts) {
+          float4 v[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) v[j] = (k0 + j * kDnParts < ns) ? ldcg4(pd + (k0 + j * kDnParts) * 256) : s;
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            if (k0 + j * kDnParts < ns) s = f4add(s, v[j]);
+        }
+        parts[p * 64 + b] = s;
+      }
+      C.bar();
+      if (C.tid < 64) {
+        float4 d = parts[b];
+#pragma unroll 1
+        for (int q = 1; q < kDnParts; ++q) d = f4add(d, parts[q * 64 + b]);
+        *reinterpret_cast<float4*>(a.xbuf + col + H) = f4add(xm, d);
+      }
+      C.publish(a.cnt + c_dn_done(a, L));
     }
-    C.publish(a.cnt + c_dn_done(a, L));
+    C.bar();
   }
-  C.bar();
 }
 
 // QKV: RMSNorm(x) . W for this CTA's 32-column group, all rows
@@ -700,18 +706,22 @@ __device__ __noinline__ uint32_t attention_phase(int L, uint32_t chunk) {
   float* sc = C.scratch + kAttS;
   float* sml = C.scratch + kAttML;
   float* skv = C.scratch + kAttKV;
+  // RoPE pairs (d, d+64): threads 0..255 the 4 query heads, 256..319 k; 320..447 copy v
+  const bool rope = ly.rope != 0;
+  float cs = 1.0f, sn = 0.0f;
+  if (rope && tid < 320) {  // the tables do not depend on this step's activations
+    cs = __ldg(a.cos_t + (long long)pos * kHalfDim + (tid & 63));
+    sn = __ldg(a.sin_t + (long long)pos * kHalfDim + (tid & 63));
+  }
   C.wait_ge(a.cnt + c_qkv(a, L), (unsigned)a.subn[QKV]);
   C.fstamp();
-  // RoPE pairs (d, d+64): threads 0..255 the 4 query heads, 256..319 k; 320..447 copy v
   if (tid < 320 && (tid < 256 || has_pos)) {
     const bool isk = tid >= 256;
     const int hh = (tid >> 6) & 3, d = tid & 63;
     const float* src = isk ? a.qkv + a.nq + g * kHeadDim : a.qkv + (g * kHeadsPerKV + hh) * kHeadDim;
     const float x1 = __ldcg(src + d), x2 = __ldcg(src + d + kHalfDim);
     float y1 = x1, y2 = x2;
-    if (ly.rope) {
-      const float cs = __ldg(a.cos_t + (long long)pos * kHalfDim + d);
-      const float sn = __ldg(a.sin_t + (long long)pos * kHalfDim + d);
+    if (rope) {
       y1 = __fsub_rn(__fmul_rn(x1, cs), __fmul_rn(x2, sn));
       y2 = __fadd_rn(__fmul_rn(x2, cs), __fmul_rn(x1, sn));
     }
@@ -745,7 +755,6 @@ __device__ __noinline__ uint32_t attention_phase(int L, uint32_t chunk) {
       }
     }
     C.release_stage();
-    C.fstamp();
   }
   if (has_pos && warp == 0 && !C.aborted_w()) kscore(sq, skv, sc, pos - s0, (lane >> 3) == 0, li);
   C.bar();
@@ -787,7 +796,6 @@ __device__ __noinline__ uint32_t attention_phase(int L, uint32_t chunk) {
       }
     }
     C.release_stage();
-    C.fstamp();
   }
   if (tid < kHeadDim && !C.aborted()) {
     if (has_pos) {

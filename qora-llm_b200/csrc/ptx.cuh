@@ -78,6 +78,10 @@ __device__ __forceinline__ unsigned atom_add_acqrel(unsigned* p, unsigned v) {
   return old;
 }
 
+__device__ __forceinline__ void red_add_relaxed(unsigned* p, unsigned v) {
+  asm volatile("red.relaxed.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 __device__ __forceinline__ void red_add_release(unsigned* p, unsigned v) {
   asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
