@@ -510,10 +510,14 @@ __device__ __noinline__ uint32_t gemv_stream(int m, int L, uint32_t chunk) {
           const uint16_t sv = *reinterpret_cast<const uint16_t*>(blk + 128 + q * 2);
           cf[k] = ok ? __half2float(__ushort_as_half(sv)) * xr[j] : 0.0f;
         }
+        // passes whose rows all lie past the stage's end are skipped (warp-uniform)
+        const int base = C.warp * W;
 #pragma unroll
         for (int k = 0; k < NP; ++k) {
-          cs += cf[k];
-          q4_fma_chunk(w[k], cf[k], acc);
+          if (base + k * kCW * W < R) {
+            cs += cf[k];
+            q4_fma_chunk(w[k], cf[k], acc);
+          }
         }
       }
       C.release_stage();
