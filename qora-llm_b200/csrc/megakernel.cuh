@@ -12,16 +12,23 @@
 //
 // Per layer (CTA sets in brackets):
 //   QKV  [one CTA per 32-column group of q|k|v] RMSNorm(x) . W over all rows -> final
-//        q|k|v values (before RoPE), no split-K                               (c_qkv)
+//        q|k|v values (before RoPE), no split-K
 //   ATTN [one CTA per (kv head, chunk of positions)] RoPE on its 4 query heads (and,
 //        for the chunk holding the new position, on k, which it appends with v to the
-//        head-major cache), scores, softmax numerators, P.V -> (m, l, o)     (c_att)
+//        head-major cache), scores, softmax numerators, P.V -> (m, l, o)
 //   O    [one CTA per 32-column group of o_proj] merge the (m, l, o) partials of all
-//        heads, GEMV over all rows, x_mid = x + o for its columns            (c_o)
+//        heads, GEMV over all rows, x_mid = x + o for its columns
 //   GU   [all] RMSNorm(x_mid) . [gate|up], split-K over 256-column tiles -> partials
 //   DOWN [all] SwiGLU of its rows from the gate/up partials, split-K GEMV; the last CTA
-//        of an output tile writes x_next = x_mid + down for the tile      (dn_done)
+//        of an output tile (atomic arrival count) writes x_next = x_mid + down for it
 // then lm_head rows (a contiguous slice per CTA) with a fused first-maximum argmax.
+//
+// Hand-off between CTAs: every value one CTA passes to another (q|k|v, attention
+// partials, x_mid, gate/up partials, x_next) travels as a 64-bit word (tag << 32 | f32
+// bits) written and read with single-copy-atomic relaxed accesses; the tag names the
+// launch and the layer. A reader first polls one word per producer (warp 0), then loads
+// its values and re-reads any whose tag is not yet the current one. No release fence or
+// counter sits between a producer and its consumers.
 //
 // Instruction-cache discipline: B200's per-SM instruction cache holds ~60 KB of code
 // (measured: straight-line code runs at ~2.7 cycles per instruction up to 61 KB and
@@ -103,14 +110,16 @@ struct Args {
   const float* cos_t;
   const float* sin_t;
   int max_pos;                // positions the KV cache (and RoPE table) can hold
-  float* xbuf;                // [L+1][H] residual stream into each layer (x_0 = embedding)
-  float* xmid;                // [L][H] residual after attention
-  float* qkv;                 // [nq + 2 nkvw] this step's q|k|v (before RoPE)
+  uint64_t* xbuf;             // tagged [L+1][H] residual stream into each layer (x_0 = embedding)
+  uint64_t* xmid;             // tagged [L][H] residual after attention
+  uint64_t* qkv;              // tagged [nq + 2 nkvw] this step's q|k|v (before RoPE)
   float* logits;              // [vocab]
-  float* part[4];             // GU, DOWN split-K partials [tiles][slots][256]
-  float* att_o;               // [kMaxUnits][4][128]
-  float* att_ml;              // [kMaxUnits][4][2]
-  unsigned* cnt;              // dependency counters, zero between launches
+  uint64_t* gu_part;          // tagged gate/up split-K partials [tiles][slots][256]
+  float* dn_part;             // down split-K partials [tiles][slots][256]
+  uint64_t* att_o;            // tagged [kMaxUnits][4][128]
+  uint64_t* att_ml;           // tagged [kMaxUnits][4][2]
+  unsigned* epoch;            // launches so far (the tag base); advanced by the last CTA
+  unsigned* cnt;              // down arrival counters [L][tiles] + the final arrival, zero between launches
   int cpl;                    // counters per layer
   int n_cnt;
   float* lm_v;                // [gridDim.x]
@@ -135,7 +144,7 @@ QORA_DEV uint64_t* sm_empty() { return sm_full() + kStages; }
 QORA_DEV volatile int* sm_flags() { return reinterpret_cast<volatile int*>(sm_empty() + kStages); }
 QORA_DEV Args* sm_args() { return reinterpret_cast<Args*>(reinterpret_cast<uint8_t*>(sm_empty() + kStages) + 64); }
 // flags: [0] abort, [1] last-arriver, [2] pos, [3] chunks issued, [4] producer done,
-// [5] token, [6] fine-trace counter, [7] current layer
+// [5] token, [6] fine-trace counter, [7] current layer, [8] tag base (epoch * 64)
 
 // Trace layout: per CTA kTracePerCta u64 globaltimer stamps written by consumer thread 0:
 // [0] start, [1] after embedding, then per layer L at 2 + 8L + {0: x ready (QKV CTAs),
@@ -147,13 +156,8 @@ constexpr int kTraceLayers = 64;
 constexpr int kTracePerCta = 2 + 8 * kTraceLayers + 2;
 constexpr int kTraceFine = 64;
 
-// ---- counter layout (per layer L)
-QORA_DEV int c_qkv(const Args& a, int L) { return L * a.cpl + 0; }   // QKV groups done
-QORA_DEV int c_att(const Args& a, int L) { return L * a.cpl + 1; }   // attention units done
-QORA_DEV int c_o(const Args& a, int L) { return L * a.cpl + 2; }     // O groups done
-QORA_DEV int c_gu_arr(const Args& a, int L, int t) { return L * a.cpl + 3 + t; }
-QORA_DEV int c_dn_arr(const Args& a, int L, int t) { return L * a.cpl + 3 + a.tiles[GU] + t; }
-QORA_DEV int c_dn_done(const Args& a, int L) { return L * a.cpl + 3 + a.tiles[GU] + a.tiles[DOWN]; }
+// ---- counter layout: down arrivals per (layer, output tile), then the final arrival
+QORA_DEV int c_dn_arr(const Args& a, int L, int t) { return L * a.cpl + t; }
 QORA_DEV int c_lm(const Args& a) { return a.L * a.cpl; }
 
 // Attention units: (kv head, chunk of `chunk` positions), about one unit per CTA.
@@ -304,7 +308,7 @@ struct Cons {
     atomicExch(&ap->st->error, code);
   }
 
-  QORA_DEV void bar() { ptx::named_bar(kBar, kCT); }
+  QORA_DEV void bar() const { ptx::named_bar(kBar, kCT); }
 
   QORA_DEV void stamp(int idx) {
     if (ap->trace && tid == 0) ap->trace[(long long)c * kTracePerCta + idx] = ptx::globaltimer();
@@ -318,27 +322,6 @@ struct Cons {
             ptx::globaltimer();
       flags[6] = fine + 1;
     }
-  }
-
-  // thread 0 spins (bounded) until *p >= target, then an acquire fence; no barrier
-  QORA_DEV void spin_ge(const unsigned* p, unsigned target) {
-    if (aborted()) return;
-    if (ptx::ld_relaxed(p) < target) {
-      const uint64_t t0 = ptx::globaltimer();
-      while (ptx::ld_relaxed(p) < target) {
-        if (ptx::globaltimer() - t0 > ap->timeout_ns) {
-          set_abort(2);
-          return;
-        }
-      }
-    }
-    ptx::fence_acq_rel_gpu();
-  }
-
-  // thread 0 waits until *p >= target; all consumers then see the outcome
-  QORA_DEV void wait_ge(const unsigned* p, unsigned target) {
-    if (tid == 0) spin_ge(p, target);
-    bar();
   }
 
   // next stage of the ring (every consumer warp calls this for every chunk, in order).
@@ -383,11 +366,6 @@ struct Cons {
     return t;
   }
 
-  // publish: every consumer's prior global writes, then a release increment
-  QORA_DEV void publish(unsigned* ctr) {
-    bar();
-    if (tid == 0) ptx::red_add_release(ctr, 1u);
-  }
 };
 
 // the consumer view of this CTA, rebuilt in registers by every phase (phases take only
@@ -416,19 +394,99 @@ __device__ __noinline__ float rms_inv_from(float sumsq, int H) {
   return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sumsq, (float)H), 1e-6f)));
 }
 
-// x (H floats, global) -> sB (shared) as float4, returns this thread's sum of squares
-QORA_DEV float load_x(const Cons& C, float* sB, const float* x, int H) {
-  float ss = 0.0f;
+// ---- tagged hand-off values: (tag << 32) | f32 bits
+QORA_DEV uint32_t tag_of(const Cons& C, int L) { return (uint32_t)C.flags[8] + (uint32_t)L + 1u; }
+QORA_DEV void st_tagged(uint64_t* p, float v, uint32_t tag) {
+  ptx::st_relaxed_b64(p, ((uint64_t)tag << 32) | __float_as_uint(v));
+}
+QORA_DEV bool tag_ok(uint64_t w, uint32_t tag) { return (uint32_t)(w >> 32) == tag; }
+QORA_DEV float tag_val(uint64_t w) { return __uint_as_float((uint32_t)w); }
+
+// Retry control for a batch of tagged loads that found a stale tag (the producer's
+// store had not arrived yet): true = give up (abort set, or the CTA already aborted).
+QORA_DEV bool retry_stop(const Cons& C, uint64_t& t0, int it) {
+  if (it == 0) {
+    t0 = ptx::globaltimer();
+    return false;
+  }
+  if (C.aborted()) return true;
+  if (ptx::globaltimer() - t0 > C.ap->timeout_ns) {
+    C.flags[0] = 1;
+    atomicExch(&C.ap->st->error, 2);
+    return true;
+  }
+  return false;
+}
+
+// Warp 0 polls the sentinel words addr(0..n-1) until each carries `tag` (bounded; abort
+// on timeout), then every consumer thread passes the barrier.
+template <class Addr>
+QORA_DEV void await_tags(const Cons& C, int n, uint32_t tag, Addr&& addr) {
+  if (C.warp == 0 && !C.aborted_w()) {
+    const uint64_t t0 = ptx::globaltimer();
 #pragma unroll 1
-  for (int b = C.tid; b < H / 4; b += kCT) {
-    const float4 v = ldcg4(x + 4 * b);
-    reinterpret_cast<float4*>(sB)[b] = v;
-    ss = __fmaf_rn(v.x, v.x, ss);
-    ss = __fmaf_rn(v.y, v.y, ss);
-    ss = __fmaf_rn(v.z, v.z, ss);
-    ss = __fmaf_rn(v.w, v.w, ss);
+    for (;;) {
+      bool mine = true;
+#pragma unroll 1
+      for (int i = C.lane; i < n; i += 32) mine &= tag_ok(ptx::ld_relaxed_b64(addr(i)), tag);
+      if (__all_sync(0xffffffffu, mine)) break;
+      int stop = 0;
+      if (C.lane == 0) stop = C.aborted() ? 1 : (ptx::globaltimer() - t0 > C.ap->timeout_ns ? 2 : 0);
+      stop = __shfl_sync(0xffffffffu, stop, 0);
+      if (stop) {
+        if (stop == 2 && C.lane == 0) {
+          C.flags[0] = 1;
+          atomicExch(&C.ap->st->error, 2);
+        }
+        break;
+      }
+    }
+  }
+  C.bar();
+}
+
+// tagged x (H <= 2048 values) -> sB (shared), returns this thread's sum of squares
+QORA_DEV float load_x(const Cons& C, float* sB, const uint64_t* x, int H, uint32_t tag) {
+  constexpr int kPairs = (2048 / 2 + kCT - 1) / kCT;
+  uint64_t w[kPairs][2];
+  uint64_t t0 = 0;
+#pragma unroll 1
+  for (int it = 0;; ++it) {
+    bool ok = true;
+#pragma unroll
+    for (int j = 0; j < kPairs; ++j) {
+      const int b = C.tid + j * kCT;
+      if (b < H / 2) {
+        ptx::ld_relaxed_v2_b64(x + 2 * b, w[j][0], w[j][1]);
+        ok &= tag_ok(w[j][0], tag) & tag_ok(w[j][1], tag);
+      }
+    }
+    if (ok || retry_stop(C, t0, it)) break;
+  }
+  float ss = 0.0f;
+#pragma unroll
+  for (int j = 0; j < kPairs; ++j) {
+    const int b = C.tid + j * kCT;
+    if (b < H / 2) {
+      const float v0 = tag_val(w[j][0]), v1 = tag_val(w[j][1]);
+      sB[2 * b] = v0;
+      sB[2 * b + 1] = v1;
+      ss = __fmaf_rn(v0, v0, ss);
+      ss = __fmaf_rn(v1, v1, ss);
+    }
   }
   return ss;
+}
+
+// one tagged value, re-read until it carries `tag` (bounded)
+QORA_DEV float ld_checked(const Cons& C, const uint64_t* p, uint32_t tag) {
+  uint64_t w, t0 = 0;
+#pragma unroll 1
+  for (int it = 0;; ++it) {
+    w = ptx::ld_relaxed_b64(p);
+    if (tag_ok(w, tag) || retry_stop(C, t0, it)) break;
+  }
+  return tag_val(w);
 }
 
 // Rows of this thread's xs entries i = tid + j*kCT of a span: (lin0 + i) mod K, stepped
@@ -564,76 +622,84 @@ __device__ __noinline__ uint32_t gemv_stream(int m, int L, uint32_t chunk) {
 }
 
 // A finished segment's sums (Y): q|k|v and o_proj results are final (one group per
-// CTA); gate/up and down store their split-K partial.
+// CTA) and go out tagged; gate/up partials go out tagged; down partials are plain
+// floats, published by the arrival count in gemv_finish.
 __device__ __noinline__ void seg_store(int m, int L, int t, int slot) {
   Cons C = make_cons(0);
   const Args& a = C.a();
   const float* y = C.scratch + kOffY;
+  const uint32_t tag = tag_of(C, L);
   if (m == QKV) {
-    if (C.tid < 32) a.qkv[t * 32 + C.tid] = y[C.tid];
+    if (C.tid < 32) st_tagged(a.qkv + t * 32 + C.tid, y[C.tid], tag);
   } else if (m == OPR) {
     if (C.tid < 32) {
       const long long col = (long long)L * a.H + t * 32 + C.tid;
-      a.xmid[col] = __fadd_rn(__ldcg(a.xbuf + col), y[C.tid]);
+      st_tagged(a.xmid + col, __fadd_rn(ld_checked(C, a.xbuf + col, tag), y[C.tid]), tag);
     }
   } else if (C.tid < 256) {
-    __stcg(a.part[m] + ((long long)t * a.slots[m] + slot) * 256 + C.tid, y[C.tid]);
+    const long long o = ((long long)t * a.slots[m] + slot) * 256 + C.tid;
+    if (m == GU) st_tagged(a.gu_part + o, y[C.tid], tag);
+    else __stcg(a.dn_part + o, y[C.tid]);
   }
 }
 
-// Publish a stored segment of tile t (a release: barrier, fence, relaxed increment);
-// the last down segment of an output tile writes the next residual for the tile.
+// Down: count this segment's arrival at tile t; the last arriver writes the tile's next
+// residual x_{L+1} = x_mid + (down partials summed over the slots).
 __device__ __noinline__ void gemv_finish(int m, int L, int t) {
+  if (m != DOWN) return;
   Cons C = make_cons(0);
   const Args& a = C.a();
   const int H = a.H;
   C.bar();
-  if (m != DOWN) {
-    if (C.tid == 0) {
-      ptx::fence_acq_rel_gpu();
-      if (m == QKV) ptx::red_add_relaxed(a.cnt + c_qkv(a, L), 1u);
-      if (m == OPR) ptx::red_add_relaxed(a.cnt + c_o(a, L), 1u);
-      if (m == GU) ptx::red_add_relaxed(a.cnt + c_gu_arr(a, L, t), 1u);
-    }
-    return;
+  if (C.tid == 0) {
+    const unsigned prev = ptx::atom_add_acqrel(a.cnt + c_dn_arr(a, L, t), 1u);
+    C.flags[1] = (prev == (unsigned)(C.ns(DOWN, t) - 1));
   }
-  {
-    if (C.tid == 0) {
-      const unsigned prev = ptx::atom_add_acqrel(a.cnt + c_dn_arr(a, L, t), 1u);
-      C.flags[1] = (prev == (unsigned)(C.ns(DOWN, t) - 1));
+  C.bar();
+  if (C.flags[1]) {
+    const uint32_t tag = tag_of(C, L);
+    float4* parts = reinterpret_cast<float4*>(C.scratch + kOffB);  // [kDnParts][64]
+    const int b = C.tid & 63, p = C.tid >> 6;
+    const long long col = (long long)L * H + t * 256 + 4 * b;
+    uint64_t xw[4] = {0, 0, 0, 0};
+    if (C.tid < 64) {
+      uint64_t t0 = 0;
+#pragma unroll 1
+      for (int it = 0;; ++it) {
+        ptx::ld_relaxed_v2_b64(a.xmid + col, xw[0], xw[1]);
+        ptx::ld_relaxed_v2_b64(a.xmid + col + 2, xw[2], xw[3]);
+        const bool ok = tag_ok(xw[0], tag) & tag_ok(xw[1], tag) & tag_ok(xw[2], tag) & tag_ok(xw[3], tag);
+        if (ok || retry_stop(C, t0, it)) break;
+      }
+    }
+    if (p < kDnParts) {
+      const int ns = C.ns(DOWN, t);
+      const float* pd = a.dn_part + (long long)t * a.slots[DOWN] * 256 + 4 * b;
+      float4 s = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll 1
+      for (int k0 = p; k0 < ns; k0 += 4 * kDnParts) {
+        float4 v[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[j] = (k0 + j * kDnParts < ns) ? ldcg4(pd + (k0 + j * kDnParts) * 256) : s;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (k0 + j * kDnParts < ns) s = f4add(s, v[j]);
+      }
+      parts[p * 64 + b] = s;
     }
     C.bar();
-    if (C.flags[1]) {
-      float4* parts = reinterpret_cast<float4*>(C.scratch + kOffB);  // [kDnParts][64]
-      const int b = C.tid & 63, p = C.tid >> 6;
-      const long long col = (long long)L * H + t * 256 + 4 * b;
-      const float4 xm = (C.tid < 64) ? ldcg4(a.xmid + col) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-      if (p < kDnParts) {
-        const int ns = C.ns(DOWN, t);
-        const float* pd = a.part[DOWN] + (long long)t * a.slots[DOWN] * 256 + 4 * b;
-        float4 s = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (C.tid < 64) {
+      float4 d = parts[b];
 #pragma unroll 1
-        for (int k0 = p; k0 < ns; k0 += 4 * kDnParts) {
-          float4 v[4];
+      for (int q = 1; q < kDnParts; ++q) d = f4add(d, parts[q * 64 + b]);
+      const float dv[4] = {d.x, d.y, d.z, d.w};
+      const uint32_t tn = tag + 1u;  // x_{L+1} carries layer L+1's tag
 #pragma unroll
-          for (int j = 0; j < 4; ++j) v[j] = (k0 + j * kDnParts < ns) ? ldcg4(pd + (k0 + j * kDnParts) * 256) : s;
-#pragma unroll
-          for (int j = 0; j < 4; ++j)
-            if (k0 + j * kDnParts < ns) s = f4add(s, v[j]);
-        }
-        parts[p * 64 + b] = s;
-      }
-      C.bar();
-      if (C.tid < 64) {
-        float4 d = parts[b];
-#pragma unroll 1
-        for (int q = 1; q < kDnParts; ++q) d = f4add(d, parts[q * 64 + b]);
-        *reinterpret_cast<float4*>(a.xbuf + col + H) = f4add(xm, d);
-      }
-      C.publish(a.cnt + c_dn_done(a, L));
+      for (int j = 0; j < 4; ++j)
+        st_tagged(a.xbuf + col + H + j, __fadd_rn(tag_val(xw[j]), dv[j]), tn);
     }
-    C.bar();
   }
+  C.bar();
 }
 
 // QKV: RMSNorm(x) . W for this CTA's 32-column group, all rows
@@ -648,8 +714,10 @@ __device__ __noinline__ uint32_t qkv_phase(int L, uint32_t chunk) {
   prefetch_gains(C, a.layers[L].g_in, sp, H, gam);
   float ss = 0.0f;
   if (L > 0) {
-    C.wait_ge(a.cnt + c_dn_done(a, L - 1), (unsigned)a.tiles[DOWN]);
-    ss = load_x(C, sB, a.xbuf + (long long)L * H, H);
+    const uint32_t tag = tag_of(C, L);
+    const uint64_t* x = a.xbuf + (long long)L * H;
+    await_tags(C, a.tiles[DOWN], tag, [&](int i) { return x + i * 256; });  // one word per down tile
+    ss = load_x(C, sB, x, H, tag);
   } else {
 #pragma unroll 1
     for (int i = C.tid; i < H; i += kCT) ss = __fmaf_rn(sB[i], sB[i], ss);
@@ -717,13 +785,24 @@ __device__ __noinline__ uint32_t attention_phase(int L, uint32_t chunk) {
     cs = __ldg(a.cos_t + (long long)pos * kHalfDim + (tid & 63));
     sn = __ldg(a.sin_t + (long long)pos * kHalfDim + (tid & 63));
   }
-  C.wait_ge(a.cnt + c_qkv(a, L), (unsigned)a.subn[QKV]);
+  // one sentinel per producing group: the 16 q groups of heads 4g..4g+3, then the 4 k
+  // and 4 v groups of head g
+  const uint32_t tag = tag_of(C, L);
+  const int gq0 = g * kHeadsPerKV * 4, gk0 = a.nq / 32 + g * 4, gv0 = (a.nq + a.nkvw) / 32 + g * 4;
+  await_tags(C, 24, tag, [&](int i) { return a.qkv + 32 * (i < 16 ? gq0 + i : i < 20 ? gk0 + i - 16 : gv0 + i - 20); });
   C.fstamp();
   if (tid < 320 && (tid < 256 || has_pos)) {
     const bool isk = tid >= 256;
     const int hh = (tid >> 6) & 3, d = tid & 63;
-    const float* src = isk ? a.qkv + a.nq + g * kHeadDim : a.qkv + (g * kHeadsPerKV + hh) * kHeadDim;
-    const float x1 = __ldcg(src + d), x2 = __ldcg(src + d + kHalfDim);
+    const uint64_t* src = isk ? a.qkv + a.nq + g * kHeadDim : a.qkv + (g * kHeadsPerKV + hh) * kHeadDim;
+    uint64_t w1, w2, t0 = 0;
+#pragma unroll 1
+    for (int it = 0;; ++it) {
+      w1 = ptx::ld_relaxed_b64(src + d);
+      w2 = ptx::ld_relaxed_b64(src + d + kHalfDim);
+      if ((tag_ok(w1, tag) & tag_ok(w2, tag)) || retry_stop(C, t0, it)) break;
+    }
+    const float x1 = tag_val(w1), x2 = tag_val(w2);
     float y1 = x1, y2 = x2;
     if (rope) {
       y1 = __fsub_rn(__fmul_rn(x1, cs), __fmul_rn(x2, sn));
@@ -740,7 +819,7 @@ __device__ __noinline__ uint32_t attention_phase(int L, uint32_t chunk) {
     }
   } else if (tid >= 320 && tid < 448 && has_pos) {
     const int d = tid - 320;
-    const float v = __ldcg(a.qkv + a.nq + a.nkvw + g * kHeadDim + d);
+    const float v = ld_checked(C, a.qkv + a.nq + a.nkvw + g * kHeadDim + d, tag);
     skv[kHeadDim + d] = v;
     vc[(long long)pos * kHeadDim + d] = v;
   }
@@ -808,10 +887,9 @@ __device__ __noinline__ uint32_t attention_phase(int L, uint32_t chunk) {
       for (int h = 0; h < kHeadsPerKV; ++h) o[h] = __fmaf_rn(sc[h * kMaxAttnChunk + pos - s0], v, o[h]);
     }
 #pragma unroll
-    for (int h = 0; h < kHeadsPerKV; ++h) __stcg(a.att_o + ((long long)u * kHeadsPerKV + h) * kHeadDim + tid, o[h]);
-    if (tid < 2 * kHeadsPerKV) __stcg(a.att_ml + (long long)u * 2 * kHeadsPerKV + tid, sml[tid]);
+    for (int h = 0; h < kHeadsPerKV; ++h) st_tagged(a.att_o + ((long long)u * kHeadsPerKV + h) * kHeadDim + tid, o[h], tag);
+    if (tid < 2 * kHeadsPerKV) st_tagged(a.att_ml + (long long)u * 2 * kHeadsPerKV + tid, sml[tid], tag);
   }
-  C.publish(a.cnt + c_att(a, L));
   return C.chunk;
 }
 
@@ -825,7 +903,8 @@ __device__ __noinline__ uint32_t o_phase(int L, uint32_t chunk) {
   int csz, nch;
   attn_plan(C.pos + 1, C.G, a.nkvh, csz, nch);
   const int nkvh = a.nkvh, K = a.K[OPR];
-  C.wait_ge(a.cnt + c_att(a, L), (unsigned)(nkvh * nch));
+  const uint32_t tag = tag_of(C, L);
+  await_tags(C, nkvh * nch, tag, [&](int i) { return a.att_ml + (long long)i * 2 * kHeadsPerKV; });
   C.stamp(2 + 8 * min(L, kTraceLayers - 1) + 3);
   // per query head h: M = max_ch m, w_ch = exp(m_ch - M), 1/l with l = sum l_ch w_ch;
   // unit (chunk ch, kv head h/4) holds head h at slot h%4
@@ -833,19 +912,18 @@ __device__ __noinline__ uint32_t o_phase(int L, uint32_t chunk) {
   float* invl = mw + a.nh * nch;
 #pragma unroll 1
   for (int h = C.warp; h < a.nh; h += kCW) {
-    const float* ml = a.att_ml + h * 2;
+    const uint64_t* ml = a.att_ml + h * 2;
     const long long ustride = (long long)nkvh * kHeadsPerKV * 2;  // next chunk, same head
     float mx = -INFINITY;
 #pragma unroll 1
-    for (int ch = C.lane; ch < nch; ch += 32) mx = fmaxf(mx, __ldcg(ml + ch * ustride));
+    for (int ch = C.lane; ch < nch; ch += 32) mx = fmaxf(mx, ld_checked(C, ml + ch * ustride, tag));
     mx = warp_max(mx);
     float l = 0.0f;
 #pragma unroll 1
     for (int ch = C.lane; ch < nch; ch += 32) {
-      const float2 v = __ldcg(reinterpret_cast<const float2*>(ml + ch * ustride));
-      const float w = expf(v.x - mx);
+      const float w = expf(ld_checked(C, ml + ch * ustride, tag) - mx);
       mw[h * nch + ch] = w;
-      l = __fmaf_rn(v.y, w, l);
+      l = __fmaf_rn(ld_checked(C, ml + ch * ustride + 1, tag), w, l);
     }
     l = warp_sum(l);
     if (C.lane == 0) invl[h] = __fdiv_rn(1.0f, l);
@@ -861,20 +939,28 @@ __device__ __noinline__ uint32_t o_phase(int L, uint32_t chunk) {
     for (int j = 0; j < kXsPer; ++j) acc[j] = 0.0f;
 #pragma unroll 1
     for (int c0 = 0; c0 < nch; c0 += 4) {
-      float v[kXsPer][4];
+      uint64_t v[kXsPer][4], t0 = 0;
+#pragma unroll 1
+      for (int it = 0;; ++it) {
+        bool ok = true;
 #pragma unroll
-      for (int j = 0; j < kXsPer; ++j) {
-        const int r = C.tid + j * kCT;
+        for (int j = 0; j < kXsPer; ++j) {
+          const int r = C.tid + j * kCT;
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-          v[j][k] = (r < K && c0 + k < nch) ? __ldcg(a.att_o + (c0 + k) * ostride + r) : 0.0f;
+          for (int k = 0; k < 4; ++k) {
+            const bool in = r < K && c0 + k < nch;
+            v[j][k] = in ? ptx::ld_relaxed_b64(a.att_o + (c0 + k) * ostride + r) : 0ull;
+            ok &= !in || tag_ok(v[j][k], tag);
+          }
+        }
+        if (ok || retry_stop(C, t0, it)) break;
       }
 #pragma unroll
       for (int j = 0; j < kXsPer; ++j) {
         const int r = C.tid + j * kCT, h = r / kHeadDim;
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          if (r < K && c0 + k < nch) acc[j] = __fmaf_rn(v[j][k], mw[h * nch + c0 + k], acc[j]);
+          if (r < K && c0 + k < nch) acc[j] = __fmaf_rn(tag_val(v[j][k]), mw[h * nch + c0 + k], acc[j]);
       }
     }
 #pragma unroll
@@ -897,9 +983,11 @@ __device__ __noinline__ uint32_t gu_phase(int L, uint32_t chunk) {
   float* sB = C.scratch + kOffB;
   float gam[kXsPer];
   prefetch_gains(C, a.layers[L].g_post, sp, a.K[GU], gam);
-  C.wait_ge(a.cnt + c_o(a, L), (unsigned)a.subn[OPR]);
+  const uint32_t tag = tag_of(C, L);
+  const uint64_t* xm = a.xmid + (long long)L * H;
+  await_tags(C, H / 32, tag, [&](int i) { return xm + i * 32; });  // one word per o_proj group
   C.stamp(2 + 8 * min(L, kTraceLayers - 1) + 5);
-  const float ss = load_x(C, sB, a.xmid + (long long)L * H, H);
+  const float ss = load_x(C, sB, xm, H, tag);
   const float inv = rms_inv_from(C.csum(ss), H);
   fill_norm_inputs(C, sB, inv, gam, sp, a.K[GU]);
   C.bar();
@@ -927,29 +1015,15 @@ __device__ __noinline__ uint32_t down_phase(int L, uint32_t chunk) {
       ++k;
     });
   }
-  if (C.warp == 0) {  // lanes poll one tile each, warp-uniform exit
-    const uint64_t t0 = ptx::globaltimer();
-    const int n0 = tr[1] - tr[0] + 1, n1 = tr[3] - tr[2] + 1;
-#pragma unroll 1
-    for (;;) {
-      bool mine = true;
-#pragma unroll 1
-      for (int k = C.lane; k < n0 + n1; k += 32) {
-        const int t = k < n0 ? tr[0] + k : tr[2] + (k - n0);
-        mine &= ptx::ld_relaxed(a.cnt + c_gu_arr(a, L, t)) >= (unsigned)C.ns(GU, t);
-      }
-      if (__all_sync(0xffffffffu, mine)) break;
-      int stop = 0;
-      if (C.lane == 0) stop = C.aborted() ? 1 : (ptx::globaltimer() - t0 > a.timeout_ns ? 2 : 0);
-      stop = __shfl_sync(0xffffffffu, stop, 0);
-      if (stop) {
-        if (stop == 2 && C.lane == 0) C.set_abort(2);
-        break;
-      }
-    }
-    ptx::fence_acq_rel_gpu();
+  // one sentinel per (gate/up tile, split-K slot) this CTA reads
+  const uint32_t tag = tag_of(C, L);
+  {
+    const int S = a.slots[GU], n0 = tr[1] - tr[0] + 1, n1 = tr[3] - tr[2] + 1;
+    await_tags(C, (n0 + n1) * S, tag, [&](int i) {
+      const int k = i / S, t = k < n0 ? tr[0] + k : tr[2] + (k - n0);
+      return a.gu_part + ((long long)t * S + min(i % S, C.ns(GU, t) - 1)) * 256;
+    });
   }
-  C.bar();
   // rows i = tid, tid + kCT: both rows' gate and up partials (4 slots each) in flight
   {
     float* xs = C.scratch;
@@ -960,29 +1034,36 @@ __device__ __noinline__ uint32_t down_phase(int L, uint32_t chunk) {
       const bool two = i + kCT < sp.n;
       const int t1 = r / kHalfTile, t2 = r2 / kHalfTile;
       const int n1 = C.ns(GU, t1), n2 = two ? C.ns(GU, t2) : 0;
-      const float* p1 = a.part[GU] + (long long)t1 * a.slots[GU] * 256 + r % kHalfTile;
-      const float* p2 = a.part[GU] + (long long)t2 * a.slots[GU] * 256 + r2 % kHalfTile;
+      const uint64_t* p1 = a.gu_part + (long long)t1 * a.slots[GU] * 256 + r % kHalfTile;
+      const uint64_t* p2 = a.gu_part + (long long)t2 * a.slots[GU] * 256 + r2 % kHalfTile;
       float g1 = 0.0f, u1 = 0.0f, g2 = 0.0f, u2 = 0.0f;
 #pragma unroll 1
       for (int k0 = 0; k0 < max(n1, n2); k0 += 4) {
-        float v[4][4];
+        uint64_t v[4][4], t0 = 0;
+#pragma unroll 1
+        for (int it = 0;; ++it) {
+          bool ok = true;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const bool ok1 = k0 + k < n1, ok2 = k0 + k < n2;
-          v[0][k] = ok1 ? __ldcg(p1 + (k0 + k) * 256) : 0.0f;
-          v[1][k] = ok1 ? __ldcg(p1 + (k0 + k) * 256 + kHalfTile) : 0.0f;
-          v[2][k] = ok2 ? __ldcg(p2 + (k0 + k) * 256) : 0.0f;
-          v[3][k] = ok2 ? __ldcg(p2 + (k0 + k) * 256 + kHalfTile) : 0.0f;
+          for (int k = 0; k < 4; ++k) {
+            const bool ok1 = k0 + k < n1, ok2 = k0 + k < n2;
+            v[0][k] = ok1 ? ptx::ld_relaxed_b64(p1 + (k0 + k) * 256) : 0ull;
+            v[1][k] = ok1 ? ptx::ld_relaxed_b64(p1 + (k0 + k) * 256 + kHalfTile) : 0ull;
+            v[2][k] = ok2 ? ptx::ld_relaxed_b64(p2 + (k0 + k) * 256) : 0ull;
+            v[3][k] = ok2 ? ptx::ld_relaxed_b64(p2 + (k0 + k) * 256 + kHalfTile) : 0ull;
+            ok &= (!ok1 || (tag_ok(v[0][k], tag) & tag_ok(v[1][k], tag))) &&
+                  (!ok2 || (tag_ok(v[2][k], tag) & tag_ok(v[3][k], tag)));
+          }
+          if (ok || retry_stop(C, t0, it)) break;
         }
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           if (k0 + k < n1) {
-            g1 = __fadd_rn(g1, v[0][k]);
-            u1 = __fadd_rn(u1, v[1][k]);
+            g1 = __fadd_rn(g1, tag_val(v[0][k]));
+            u1 = __fadd_rn(u1, tag_val(v[1][k]));
           }
           if (k0 + k < n2) {
-            g2 = __fadd_rn(g2, v[2][k]);
-            u2 = __fadd_rn(u2, v[3][k]);
+            g2 = __fadd_rn(g2, tag_val(v[2][k]));
+            u2 = __fadd_rn(u2, tag_val(v[3][k]));
           }
         }
       }
@@ -1026,9 +1107,11 @@ __device__ __noinline__ void lm_phase(uint32_t chunk) {
   const Args& a = C.a();
   const int H = a.H, lane = C.lane, warp = C.warp;
   float* sB = C.scratch + kOffB;
-  C.wait_ge(a.cnt + c_dn_done(a, a.L - 1), (unsigned)a.tiles[DOWN]);
+  const uint32_t tag = tag_of(C, a.L);
+  const uint64_t* x = a.xbuf + (long long)a.L * H;
+  await_tags(C, a.tiles[DOWN], tag, [&](int i) { return x + i * 256; });
   C.stamp(2 + 8 * kTraceLayers);
-  const float ss = load_x(C, sB, a.xbuf + (long long)a.L * H, H);
+  const float ss = load_x(C, sB, x, H, tag);
   const float inv = rms_inv_from(C.csum(ss), H);
   for (int i = C.tid; i < H; i += kCT) sB[i] = __fmul_rn(__fmul_rn(sB[i], inv), a.final_gamma[i]);
   C.bar();
@@ -1123,6 +1206,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_megakernel(const Args args
     flags[5] = tok0;
     flags[6] = 0;
     flags[7] = 0;
+    flags[8] = (int)(*args.epoch * 64u);  // tags of this launch: tag base + layer + 1
     ptx::fence_mbar_init();
   }
   {  // split-K slots per tile of gate/up, then down
@@ -1172,7 +1256,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_megakernel(const Args args
       const int q = ((e & 1) ? (b >> 4) : (b & 0xF)) - 8;
       const float v = __fmul_rn(__half2float(__ushort_as_half(sc[e / kGroup])), (float)q);
       sB[e] = v;
-      if (c == 0) a.xbuf[e] = v;
+      if (c == 0) st_tagged(a.xbuf + e, v, tag_of(C, 0));
     }
   }
   C.bar();
@@ -1230,8 +1314,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_megakernel(const Args args
     st->step = s + 1;
     st->token = (int)am;
     st->pos = pos + 1;
+    *a.epoch = *a.epoch + 1u;  // next launch's tags
   }
-  // every CTA has arrived: reset the dependency counters for the next launch
+  // every CTA has arrived: reset the arrival counters for the next launch
   for (int i = tid; i < a.n_cnt; i += kCT) a.cnt[i] = 0u;
 }
 

@@ -72,6 +72,22 @@ __device__ __forceinline__ unsigned ld_relaxed(const unsigned* p) {
 // after a relaxed read that observed a release: makes the releaser's writes visible
 __device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 
+// 64-bit relaxed accesses (single-copy atomic for an aligned 8-byte word)
+__device__ __forceinline__ void st_relaxed_b64(uint64_t* p, uint64_t v) {
+  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ uint64_t ld_relaxed_b64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// two independent 64-bit relaxed loads in one instruction (16-byte aligned)
+__device__ __forceinline__ void ld_relaxed_v2_b64(const uint64_t* p, uint64_t& a, uint64_t& b) {
+  asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
 __device__ __forceinline__ unsigned atom_add_acqrel(unsigned* p, unsigned v) {
   unsigned old;
   asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");

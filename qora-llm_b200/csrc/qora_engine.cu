@@ -258,11 +258,13 @@ struct qora_engine {
   int mk_slots[4] = {0, 0, 0, 0};
   int mk_sub0[4] = {0, 0, 0, 0}, mk_subn[4] = {0, 0, 0, 0};
   uint32_t mk_max_seq = 0;
-  float* mk_xmid = nullptr;
-  float* mk_qkv = nullptr;
+  uint64_t* mk_xmid = nullptr;  // tagged hand-off buffers: (tag << 32) | f32 bits
+  uint64_t* mk_qkv = nullptr;
+  uint64_t* mk_gu_part = nullptr;
+  float* mk_dn_part = nullptr;
+  unsigned* mk_epoch = nullptr;
   int mk_cpl = 0, mk_ncnt = 0;
-  float* mk_xbuf = nullptr;
-  float* mk_part[4] = {nullptr, nullptr, nullptr, nullptr};
+  uint64_t* mk_xbuf = nullptr;
   unsigned* mk_cnt = nullptr;
   float* mk_lm_v = nullptr;
   unsigned* mk_lm_i = nullptr;
@@ -306,8 +308,8 @@ struct qora_kv {
   bool mk_ready = false;
   mk::Args mk_args{};
   mk::Layer* mk_layers = nullptr;
-  float* mk_att_o = nullptr;
-  float* mk_att_ml = nullptr;
+  uint64_t* mk_att_o = nullptr;  // tagged
+  uint64_t* mk_att_ml = nullptr;
   std::vector<void*> allocs;
   // free the device-side state (the engine's stream must be idle or synchronised)
   void release_device() {
@@ -605,18 +607,30 @@ qora_status mega_init(qora_engine* e) {
   e->mk_G = G;
   // longest cache whose attention units (kv head x chunk of <= kMaxAttnChunk) fit the grid
   e->mk_max_seq = (uint32_t)mk::kMaxAttnChunk * (uint32_t)(G / nkvh);
+  if (e->num_layers > 62) return no("more than 62 layers (hand-off tags hold layer + 1 in 6 bits)");
   for (int m = 2; m < 4; ++m) {
     GemvShape sh = plan_gemv(mats[m]->K, mats[m]->tiles, subn[m]);
     e->mk_slots[m] = sh.plan.max_slots;
-    QCHECK(e->alloc(&e->mk_part[m], (size_t)mats[m]->tiles * sh.plan.max_slots * kTileCols));
   }
-  e->mk_cpl = 3 + d0.gu.tiles + d0.down.tiles + 1;
+  const size_t np_gu = (size_t)d0.gu.tiles * e->mk_slots[2] * kTileCols;
+  const size_t np_dn = (size_t)d0.down.tiles * e->mk_slots[3] * kTileCols;
+  e->mk_cpl = d0.down.tiles;
   e->mk_ncnt = (int)e->num_layers * e->mk_cpl + 2;
   QCHECK(e->alloc(&e->mk_cnt, e->mk_ncnt));
   QCUDA(cudaMemset(e->mk_cnt, 0, (size_t)e->mk_ncnt * sizeof(unsigned)));
-  QCHECK(e->alloc(&e->mk_xbuf, (size_t)(e->num_layers + 1) * H));
-  QCHECK(e->alloc(&e->mk_xmid, (size_t)e->num_layers * H));
-  QCHECK(e->alloc(&e->mk_qkv, (size_t)d0.qkv1.G * kGroup));
+  QCHECK(e->alloc(&e->mk_epoch, 1));
+  QCUDA(cudaMemset(e->mk_epoch, 0, sizeof(unsigned)));
+  // tagged buffers start at tag 0, which no launch uses
+  auto alloc_tagged = [&](uint64_t** p, size_t n) -> qora_status {
+    QCHECK(e->alloc(p, n));
+    QCUDA(cudaMemset(*p, 0, n * sizeof(uint64_t)));
+    return QORA_OK;
+  };
+  QCHECK(alloc_tagged(&e->mk_xbuf, (size_t)(e->num_layers + 1) * H));
+  QCHECK(alloc_tagged(&e->mk_xmid, (size_t)e->num_layers * H));
+  QCHECK(alloc_tagged(&e->mk_qkv, (size_t)d0.qkv1.G * kGroup));
+  QCHECK(alloc_tagged(&e->mk_gu_part, np_gu));
+  QCHECK(e->alloc(&e->mk_dn_part, np_dn));
   QCHECK(e->alloc(&e->mk_lm_v, G));
   QCHECK(e->alloc(&e->mk_lm_i, G));
   e->mk_ok = true;
@@ -643,6 +657,8 @@ qora_status mega_prepare(qora_engine* e, qora_kv* kv) {
   QCUDA(cudaMemcpy(kv->mk_layers, hl.data(), L * sizeof(mk::Layer), cudaMemcpyHostToDevice));
   QCHECK(kv->alloc(&kv->mk_att_o, (size_t)G * mk::kHeadsPerKV * kHeadDim));
   QCHECK(kv->alloc(&kv->mk_att_ml, (size_t)G * mk::kHeadsPerKV * 2));
+  QCUDA(cudaMemset(kv->mk_att_o, 0, (size_t)G * mk::kHeadsPerKV * kHeadDim * sizeof(uint64_t)));
+  QCUDA(cudaMemset(kv->mk_att_ml, 0, (size_t)G * mk::kHeadsPerKV * 2 * sizeof(uint64_t)));
   mk::Args& a = kv->mk_args;
   a = mk::Args{};
   a.layers = kv->mk_layers;
@@ -653,7 +669,6 @@ qora_status mega_prepare(qora_engine* e, qora_kv* kv) {
     a.K[m] = mats[m]->K;
     a.tiles[m] = mats[m]->tiles;
     a.slots[m] = e->mk_slots[m];
-    a.part[m] = e->mk_part[m];
     a.sub0[m] = e->mk_sub0[m];
     a.subn[m] = e->mk_subn[m];
   }
@@ -681,6 +696,9 @@ qora_status mega_prepare(qora_engine* e, qora_kv* kv) {
   a.xbuf = e->mk_xbuf;
   a.xmid = e->mk_xmid;
   a.qkv = e->mk_qkv;
+  a.gu_part = e->mk_gu_part;
+  a.dn_part = e->mk_dn_part;
+  a.epoch = e->mk_epoch;
   a.logits = e->logits;
   a.att_o = kv->mk_att_o;
   a.att_ml = kv->mk_att_ml;
