@@ -75,11 +75,20 @@ typedef struct qora_weights_view {
 typedef struct qora_engine qora_engine;
 typedef struct qora_kv qora_kv;
 
-/* Engine options. Zero-initialise and set what you need. */
+/* Engine options. Zero-initialise and set what you need.
+ *
+ * Tensor parallelism runs one engine per GPU, each in its own process (or thread):
+ * set tp_size > 1 and this engine's tp_rank, create the engine on its device, pass every
+ * rank's qora_tp_export() bytes to every rank's qora_tp_connect(), then drive all ranks
+ * through the same sequence of calls (same tokens; each rank owns its own KV cache).
+ * q|k|v and gate/up are column-split, o_proj and down row-split, lm_head split by vocab
+ * (the reference itself has no tensor parallelism; its math is unchanged by the split). */
 typedef struct qora_engine_options {
-    int32_t  n_gpus;        /* tensor-parallel degree; 0 or 1 = single GPU          */
-    int32_t  first_device;  /* CUDA ordinal of rank 0 (ranks use first_device + r) */
+    int32_t  n_gpus;        /* single-process multi-GPU engines: must be 0 or 1     */
+    int32_t  first_device;  /* CUDA ordinal this engine runs on                     */
     uint32_t flags;         /* QORA_FLAG_* bits                                     */
+    int32_t  tp_size;       /* tensor-parallel degree: 0/1 (none), 2, 4 or 8         */
+    int32_t  tp_rank;       /* this engine's rank in [0, tp_size)                   */
 } qora_engine_options;
 
 /* Run each decode step as a CUDA graph of per-operation kernels instead of the
@@ -104,6 +113,14 @@ qora_status qora_engine_create(const qora_weights_view* weights,
                                qora_engine** out);
 
 void qora_engine_destroy(qora_engine* engine);
+
+/* Tensor-parallel set-up (no counterpart in the reference). qora_tp_export writes this
+ * rank's opaque peer handle (an IPC handle of its receive buffers) to buf and its size to
+ * *len (call with buf == NULL to query the size). qora_tp_connect takes all tp_size
+ * ranks' handles concatenated in rank order and maps the peers' buffers; decode steps
+ * are refused until it succeeds. All ranks must run on GPUs of one NVLink domain. */
+qora_status qora_tp_export(qora_engine* engine, void* buf, size_t cap, size_t* len);
+qora_status qora_tp_connect(qora_engine* engine, const void* handles, size_t len_per_rank);
 
 /* Geometry of a loaded engine. */
 qora_status qora_engine_info(const qora_engine* engine, uint32_t* num_layers,

@@ -32,7 +32,8 @@ class WeightsView(C.Structure):
 
 
 class EngineOptions(C.Structure):
-    _fields_ = [("n_gpus", C.c_int32), ("first_device", C.c_int32), ("flags", C.c_uint32)]
+    _fields_ = [("n_gpus", C.c_int32), ("first_device", C.c_int32), ("flags", C.c_uint32),
+                ("tp_size", C.c_int32), ("tp_rank", C.c_int32)]
 
 
 def _ptr(a: np.ndarray | None):

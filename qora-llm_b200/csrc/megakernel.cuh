@@ -129,6 +129,14 @@ struct Args {
   int ring_cap;
   unsigned long long timeout_ns;
   unsigned long long* trace;  // optional phase timestamps, or nullptr
+  // tensor parallelism (tp = 1: none): this rank's shard, its lm_head vocab rows
+  // [v0, v1), and every rank's receive buffers (own included), written over NVLink
+  int tp, rank, hpk;          // hpk: query heads per local KV head
+  int v0, v1;
+  uint64_t* peer_o[8];        // tagged o_proj partials [L][tp][H]
+  uint64_t* peer_d[8];        // tagged down partials [L][tp][H]
+  uint64_t* peer_lm[8];       // tagged lm_head bests [tp][2] (value, index)
+  float* peer_logits[8];      // full logits [vocab]
 };
 
 constexpr size_t smem_bytes() {
@@ -272,8 +280,8 @@ __device__ __noinline__ uint32_t produce_kv(int L, uint32_t chunk) {
 
 __device__ __noinline__ uint32_t produce_lm(uint32_t chunk) {
   const Args& a = *sm_args();
-  const int c = blockIdx.x, G = gridDim.x;
-  const int v0 = (int)((long long)c * a.vocab / G), v1 = (int)((long long)(c + 1) * a.vocab / G);
+  const int c = blockIdx.x, G = gridDim.x, nv = a.v1 - a.v0;  // this rank's vocab rows
+  const int v0 = a.v0 + (int)((long long)c * nv / G), v1 = a.v0 + (int)((long long)(c + 1) * nv / G);
 #pragma unroll 1
   for (int r = v0; r < v1; r += a.lm_rows_per_stage)
     chunk = issue(a.lm + (long long)r * a.lm_row_bytes,
@@ -514,6 +522,35 @@ QORA_DEV void fill_norm_inputs(const Cons& C, const float* sB, float inv, const 
   }
 }
 
+// Tensor parallelism: this rank's partial value v of column `col` goes to every rank's
+// receive buffer bufs[p][(L*tp + rank)*H + col]; the sum over ranks (rank order, the same
+// on every rank) comes back once all tp partials of the column have arrived (bounded).
+QORA_DEV void tp_push(const Cons& C, uint64_t* const* bufs, int L, int col, float v, uint32_t tag) {
+  const Args& a = C.a();
+  const long long o = ((long long)L * a.tp + a.rank) * a.H + col;
+  const uint64_t w = ((uint64_t)tag << 32) | __float_as_uint(v);
+  for (int p = 0; p < a.tp; ++p) ptx::st_relaxed_sys_b64(bufs[p] + o, w);
+}
+QORA_DEV float tp_sum(const Cons& C, const uint64_t* own, int L, int col, uint32_t tag) {
+  const Args& a = C.a();
+  const uint64_t* q = own + (long long)L * a.tp * a.H + col;
+  float s = 0.0f;
+  uint64_t t0 = 0;
+#pragma unroll 1
+  for (int it = 0;; ++it) {
+    bool ok = true;
+    s = 0.0f;
+#pragma unroll 1
+    for (int p = 0; p < a.tp; ++p) {
+      const uint64_t w = ptx::ld_relaxed_sys_b64(q + (long long)p * a.H);
+      ok &= tag_ok(w, tag);
+      s = __fadd_rn(s, tag_val(w));
+    }
+    if (ok || retry_stop(C, t0, it)) break;
+  }
+  return s;
+}
+
 // ------------------------------------------------------------------ phases
 __device__ __noinline__ void seg_store(int m, int L, int t, int slot);
 __device__ __noinline__ void gemv_finish(int m, int L, int t);
@@ -634,7 +671,12 @@ __device__ __noinline__ void seg_store(int m, int L, int t, int slot) {
   } else if (m == OPR) {
     if (C.tid < 32) {
       const long long col = (long long)L * a.H + t * 32 + C.tid;
-      st_tagged(a.xmid + col, __fadd_rn(ld_checked(C, a.xbuf + col, tag), y[C.tid]), tag);
+      float o = y[C.tid];
+      if (a.tp > 1) {  // row-split o_proj: sum the ranks' partials of this column
+        tp_push(C, a.peer_o, L, t * 32 + C.tid, o, tag);
+        o = tp_sum(C, a.peer_o[a.rank], L, t * 32 + C.tid, tag);
+      }
+      st_tagged(a.xmid + col, __fadd_rn(ld_checked(C, a.xbuf + col, tag), o), tag);
     }
   } else if (C.tid < 256) {
     const long long o = ((long long)t * a.slots[m] + slot) * 256 + C.tid;
@@ -692,7 +734,14 @@ __device__ __noinline__ void gemv_finish(int m, int L, int t) {
       float4 d = parts[b];
 #pragma unroll 1
       for (int q = 1; q < kDnParts; ++q) d = f4add(d, parts[q * 64 + b]);
-      const float dv[4] = {d.x, d.y, d.z, d.w};
+      float dv[4] = {d.x, d.y, d.z, d.w};
+      if (a.tp > 1) {  // row-split down: sum the ranks' partials of these columns
+        const int c0 = t * 256 + 4 * b;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) tp_push(C, a.peer_d, L, c0 + j, dv[j], tag);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) dv[j] = tp_sum(C, a.peer_d[a.rank], L, c0 + j, tag);
+      }
       const uint32_t tn = tag + 1u;  // x_{L+1} carries layer L+1's tag
 #pragma unroll
       for (int j = 0; j < 4; ++j)
@@ -778,23 +827,27 @@ __device__ __noinline__ uint32_t attention_phase(int L, uint32_t chunk) {
   float* sc = C.scratch + kAttS;
   float* sml = C.scratch + kAttML;
   float* skv = C.scratch + kAttKV;
-  // RoPE pairs (d, d+64): threads 0..255 the 4 query heads, 256..319 k; 320..447 copy v
+  // RoPE pairs (d, d+64): threads 0..64*hpk-1 the query heads of g, 256..319 k;
+  // 320..447 copy v
+  const int hpk = a.hpk;
   const bool rope = ly.rope != 0;
   float cs = 1.0f, sn = 0.0f;
   if (rope && tid < 320) {  // the tables do not depend on this step's activations
     cs = __ldg(a.cos_t + (long long)pos * kHalfDim + (tid & 63));
     sn = __ldg(a.sin_t + (long long)pos * kHalfDim + (tid & 63));
   }
-  // one sentinel per producing group: the 16 q groups of heads 4g..4g+3, then the 4 k
-  // and 4 v groups of head g
+  // one sentinel per producing group: the 4*hpk q groups of g's query heads, then the 4
+  // k and 4 v groups of head g
   const uint32_t tag = tag_of(C, L);
-  const int gq0 = g * kHeadsPerKV * 4, gk0 = a.nq / 32 + g * 4, gv0 = (a.nq + a.nkvw) / 32 + g * 4;
-  await_tags(C, 24, tag, [&](int i) { return a.qkv + 32 * (i < 16 ? gq0 + i : i < 20 ? gk0 + i - 16 : gv0 + i - 20); });
+  const int nqg = 4 * hpk;
+  const int gq0 = g * nqg, gk0 = a.nq / 32 + g * 4, gv0 = (a.nq + a.nkvw) / 32 + g * 4;
+  await_tags(C, nqg + 8, tag,
+             [&](int i) { return a.qkv + 32 * (i < nqg ? gq0 + i : i < nqg + 4 ? gk0 + i - nqg : gv0 + i - nqg - 4); });
   C.fstamp();
-  if (tid < 320 && (tid < 256 || has_pos)) {
+  if (tid < 320 && (tid < 64 * hpk || (tid >= 256 && has_pos))) {
     const bool isk = tid >= 256;
     const int hh = (tid >> 6) & 3, d = tid & 63;
-    const uint64_t* src = isk ? a.qkv + a.nq + g * kHeadDim : a.qkv + (g * kHeadsPerKV + hh) * kHeadDim;
+    const uint64_t* src = isk ? a.qkv + a.nq + g * kHeadDim : a.qkv + (g * hpk + hh) * kHeadDim;
     uint64_t w1, w2, t0 = 0;
 #pragma unroll 1
     for (int it = 0;; ++it) {
@@ -842,7 +895,7 @@ __device__ __noinline__ uint32_t attention_phase(int L, uint32_t chunk) {
   if (has_pos && warp == 0 && !C.aborted_w()) kscore(sq, skv, sc, pos - s0, (lane >> 3) == 0, li);
   C.bar();
   // chunk softmax numerators, one warp per query head
-  if (warp < kHeadsPerKV && !C.aborted_w()) {
+  if (warp < hpk && !C.aborted_w()) {
     float* row = sc + warp * kMaxAttnChunk;
     float mx = -INFINITY;
 #pragma unroll 1
@@ -887,8 +940,9 @@ __device__ __noinline__ uint32_t attention_phase(int L, uint32_t chunk) {
       for (int h = 0; h < kHeadsPerKV; ++h) o[h] = __fmaf_rn(sc[h * kMaxAttnChunk + pos - s0], v, o[h]);
     }
 #pragma unroll
-    for (int h = 0; h < kHeadsPerKV; ++h) st_tagged(a.att_o + ((long long)u * kHeadsPerKV + h) * kHeadDim + tid, o[h], tag);
-    if (tid < 2 * kHeadsPerKV) st_tagged(a.att_ml + (long long)u * 2 * kHeadsPerKV + tid, sml[tid], tag);
+    for (int h = 0; h < kHeadsPerKV; ++h)
+      if (h < hpk) st_tagged(a.att_o + ((long long)u * kHeadsPerKV + h) * kHeadDim + tid, o[h], tag);
+    if (tid < 2 * hpk) st_tagged(a.att_ml + (long long)u * 2 * kHeadsPerKV + tid, sml[tid], tag);
   }
   return C.chunk;
 }
@@ -907,12 +961,13 @@ __device__ __noinline__ uint32_t o_phase(int L, uint32_t chunk) {
   await_tags(C, nkvh * nch, tag, [&](int i) { return a.att_ml + (long long)i * 2 * kHeadsPerKV; });
   C.stamp(2 + 8 * min(L, kTraceLayers - 1) + 3);
   // per query head h: M = max_ch m, w_ch = exp(m_ch - M), 1/l with l = sum l_ch w_ch;
-  // unit (chunk ch, kv head h/4) holds head h at slot h%4
+  // unit (chunk ch, kv head h/hpk) holds head h at slot h%hpk
+  const int hpk = a.hpk;
   float* mw = C.scratch + kOffB;  // [nh][nch], then 1/l [nh]
   float* invl = mw + a.nh * nch;
 #pragma unroll 1
   for (int h = C.warp; h < a.nh; h += kCW) {
-    const uint64_t* ml = a.att_ml + h * 2;
+    const uint64_t* ml = a.att_ml + ((h / hpk) * kHeadsPerKV + h % hpk) * 2;
     const long long ustride = (long long)nkvh * kHeadsPerKV * 2;  // next chunk, same head
     float mx = -INFINITY;
 #pragma unroll 1
@@ -935,8 +990,13 @@ __device__ __noinline__ uint32_t o_phase(int L, uint32_t chunk) {
     float* xs = C.scratch;
     const long long ostride = (long long)nkvh * kHeadsPerKV * kHeadDim;  // next chunk, same head
     float acc[kXsPer];
+    int orow[kXsPer];  // row r = head*128 + dim -> offset in a unit's [4][128] block
 #pragma unroll
-    for (int j = 0; j < kXsPer; ++j) acc[j] = 0.0f;
+    for (int j = 0; j < kXsPer; ++j) {
+      acc[j] = 0.0f;
+      const int r = C.tid + j * kCT, h = r / kHeadDim;
+      orow[j] = ((h / hpk) * kHeadsPerKV + h % hpk) * kHeadDim + r % kHeadDim;
+    }
 #pragma unroll 1
     for (int c0 = 0; c0 < nch; c0 += 4) {
       uint64_t v[kXsPer][4], t0 = 0;
@@ -949,7 +1009,7 @@ __device__ __noinline__ uint32_t o_phase(int L, uint32_t chunk) {
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const bool in = r < K && c0 + k < nch;
-            v[j][k] = in ? ptx::ld_relaxed_b64(a.att_o + (c0 + k) * ostride + r) : 0ull;
+            v[j][k] = in ? ptx::ld_relaxed_b64(a.att_o + (c0 + k) * ostride + orow[j]) : 0ull;
             ok &= !in || tag_ok(v[j][k], tag);
           }
         }
@@ -1134,7 +1194,8 @@ __device__ __noinline__ void lm_phase(uint32_t chunk) {
   }
   float best = -INFINITY;
   unsigned besti = 0xFFFFFFFFu;
-  const int v0 = (int)((long long)C.c * a.vocab / C.G), v1 = (int)((long long)(C.c + 1) * a.vocab / C.G);
+  const int nv = a.v1 - a.v0;  // this rank's vocab rows
+  const int v0 = a.v0 + (int)((long long)C.c * nv / C.G), v1 = a.v0 + (int)((long long)(C.c + 1) * nv / C.G);
 #pragma unroll 1
   for (int r = v0; r < v1; r += a.lm_rows_per_stage) {
     const uint8_t* stg = C.acquire_stage();
@@ -1165,7 +1226,13 @@ __device__ __noinline__ void lm_phase(uint32_t chunk) {
         }
         acc = warp_sum(acc);
         const unsigned vi = (unsigned)(r + i);
-        if (lane == 0) a.logits[vi] = acc;
+        if (lane == 0) {
+          if (a.tp > 1) {  // every rank holds the full logits
+            for (int p = 0; p < a.tp; ++p) a.peer_logits[p][vi] = acc;
+          } else {
+            a.logits[vi] = acc;
+          }
+        }
         if (better(acc, vi, best, besti)) {
           best = acc;
           besti = vi;
@@ -1305,6 +1372,30 @@ __global__ void __launch_bounds__(kThreads, 1) decode_megakernel(const Args args
       const float v = __ldcg(a.lm_v + k);
       const unsigned ii = __ldcg(a.lm_i + k);
       if (better(v, ii, b, bi)) { b = v; bi = ii; }
+    }
+    if (a.tp > 1) {
+      // cross-rank first maximum: each rank releases its (value, index) to every rank
+      // (the release also covers this rank's logits stores), then reads all of them
+      const uint32_t tag = tag_of(C, a.L);
+      for (int p = 0; p < a.tp; ++p) {
+        ptx::st_release_sys_b64(a.peer_lm[p] + 2 * a.rank, ((uint64_t)tag << 32) | __float_as_uint(b));
+        ptx::st_release_sys_b64(a.peer_lm[p] + 2 * a.rank + 1, ((uint64_t)tag << 32) | bi);
+      }
+      const uint64_t* mine = a.peer_lm[a.rank];
+      b = -INFINITY;
+      bi = 0xFFFFFFFFu;
+      for (int p = 0; p < a.tp; ++p) {
+        uint64_t wv = 0, wi = 0, t0 = 0;
+        for (int it = 0;; ++it) {
+          wv = ptx::ld_acquire_sys_b64(mine + 2 * p);
+          wi = ptx::ld_acquire_sys_b64(mine + 2 * p + 1);
+          if ((tag_ok(wv, tag) & tag_ok(wi, tag)) || retry_stop(C, t0, it)) break;
+        }
+        if (better(tag_val(wv), (unsigned)wi, b, bi)) {
+          b = tag_val(wv);
+          bi = (unsigned)wi;
+        }
+      }
     }
     const unsigned am = (bi == 0xFFFFFFFFu) ? 0u : bi;
     StepState* st = a.st;

@@ -83,6 +83,24 @@ __device__ __forceinline__ uint64_t ld_relaxed_b64(const uint64_t* p) {
   return v;
 }
 
+// system scope: values exchanged with peer GPUs over NVLink
+__device__ __forceinline__ void st_relaxed_sys_b64(uint64_t* p, uint64_t v) {
+  asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_relaxed_sys_b64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys_b64(uint64_t* p, uint64_t v) {
+  asm volatile("st.release.sys.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_acquire_sys_b64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // two independent 64-bit relaxed loads in one instruction (16-byte aligned)
 __device__ __forceinline__ void ld_relaxed_v2_b64(const uint64_t* p, uint64_t& a, uint64_t& b) {
   asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");

@@ -124,7 +124,8 @@ struct GroupRef {
 // f16 scales. tg == 1: one group per tile, stored as 144-byte blocks of 8 consecutive
 // rows (8 x 16 nibble bytes, then the 8 rows' scales; K % 8 == 0), which keeps every
 // 16-byte row load aligned. Either way a tile row costs 18 bytes per group.
-std::vector<uint8_t> build_tiled(int K, const std::vector<GroupRef>& refs, int tg = kTileGroups) {
+std::vector<uint8_t> build_tiled(int K, const std::vector<GroupRef>& refs, int tg = kTileGroups,
+                                 int row0 = 0) {
   const int G = (int)refs.size();
   const int tiles = (G + tg - 1) / tg;
   std::vector<uint8_t> buf((size_t)tiles * K * tg * 18, 0);
@@ -143,8 +144,9 @@ std::vector<uint8_t> build_tiled(int K, const std::vector<GroupRef>& refs, int t
       if (f >= G || refs[f].m == nullptr) continue;  // zeros: scale 0 -> contributes 0
       const qora_matrix_view* m = refs[f].m;
       const size_t gpr = m->n / kGroup;
-      std::memcpy(blk + slot * 16, m->packed + ((size_t)r * gpr + refs[f].g) * 16, 16);
-      std::memcpy(blk + 128 + slot * 2, m->scales + (size_t)r * gpr + refs[f].g, 2);
+      const size_t sr = (size_t)(row0 + r);  // source row (row-split shards start at row0)
+      std::memcpy(blk + slot * 16, m->packed + (sr * gpr + refs[f].g) * 16, 16);
+      std::memcpy(blk + 128 + slot * 2, m->scales + sr * gpr + refs[f].g, 2);
     }
   }
   return buf;
@@ -232,7 +234,16 @@ struct qora_engine {
   cudaStream_t stream = nullptr;
   uint32_t format = QORA_FORMAT_Q4;
   uint32_t num_layers = 0, vocab = 0, hidden = 0, inter = 0;
-  uint32_t nh = 0, nkv = 0, rope_rows = 0;
+  uint32_t nh = 0, nkv = 0, rope_rows = 0;  // nkv: KV heads this engine's caches hold
+  uint32_t nkv_total = 0;                    // KV heads of the model
+  // tensor parallelism: this engine is rank `rank` of `tp` (1 = whole model)
+  int tp = 1, rank = 0;
+  int nh_l = 0, nkv_l = 0, kv0 = 0, inter_l = 0;  // local q heads, kv heads, first kv head, MLP width
+  uint8_t* tp_region = nullptr;                   // receive buffers peers write into (IPC-exported)
+  size_t tp_region_bytes = 0, tp_off_d = 0, tp_off_lm = 0, tp_off_logits = 0;
+  uint8_t* tp_peer[8] = {};                       // every rank's region (own included), after connect
+  bool tp_connected = false;
+  std::vector<void*> tp_opened;                   // IPC mappings to close
   std::vector<LayerDev> layers;
   uint8_t* lm_table = nullptr;   // embedding rows: hidden/2 packed bytes | hidden/32 f16 scales
   long long lm_row_bytes = 0;
@@ -350,6 +361,8 @@ qora_engine::~qora_engine() {
     kv->e = nullptr;
   }
   kvs.clear();
+  if (!tp_opened.empty()) cudaSetDevice(device);
+  for (void* p : tp_opened) cudaIpcCloseMemHandle(p);
   for (void* p : allocs) cudaFree(p);
   if (stream) cudaStreamDestroy(stream);
 }
@@ -403,52 +416,58 @@ qora_status upload(qora_engine* e, void* dst, const void* src, size_t bytes) {
 }
 
 qora_status upload_q4(qora_engine* e, int K, const std::vector<GroupRef>& refs, DevQ4& out,
-                      int tg = kTileGroups) {
+                      int tg = kTileGroups, int row0 = 0) {
   if (tg != kTileGroups && (tg != 1 || K % 8 != 0)) return fail(QORA_ERR_UNSUPPORTED, "tile shape");
   out.K = K;
   out.G = (int)refs.size();
   out.tiles = (out.G + tg - 1) / tg;
-  std::vector<uint8_t> host = build_tiled(K, refs, tg);
+  std::vector<uint8_t> host = build_tiled(K, refs, tg, row0);
   QCHECK(e->alloc(&out.buf, host.size()));
   return upload(e, out.buf, host.data(), host.size());
 }
 
+// Layer i of this engine: the whole layer, or rank `rank`'s tensor-parallel shard of it
+// (q heads [rank*nh_l, +nh_l) with their kv heads; o_proj rows of those heads; gate/up
+// columns and down rows [rank*I_l, +I_l)).
 qora_status build_layer(qora_engine* e, const qora_weights_view* w, uint32_t i) {
   const qora_layer_view& L = w->layers[i];
   LayerDev& d = e->layers[i];
   const int H = (int)w->hidden;
+  const int nh_l = e->nh_l, nkv_l = e->nkv_l, h0 = e->rank * nh_l;
   std::vector<GroupRef> refs;
-  auto add_all = [&](const qora_matrix_view& m) {
-    for (int g = 0; g < (int)(m.n / kGroup); ++g) refs.push_back({&m, g});
+  auto add_groups = [&](const qora_matrix_view& m, int g0, int ng) {
+    for (int g = g0; g < g0 + ng; ++g) refs.push_back({&m, g});
   };
+  constexpr int kGpH = kHeadDim / kGroup;  // groups per head
   refs.clear();
-  add_all(L.q_proj);
-  add_all(L.k_proj);
-  add_all(L.v_proj);
+  add_groups(L.q_proj, h0 * kGpH, nh_l * kGpH);
+  add_groups(L.k_proj, e->kv0 * kGpH, nkv_l * kGpH);
+  add_groups(L.v_proj, e->kv0 * kGpH, nkv_l * kGpH);
   QCHECK(upload_q4(e, H, refs, d.qkv));
   QCHECK(upload_q4(e, H, refs, d.qkv1, 1));
   refs.clear();
-  add_all(L.o_proj);
-  QCHECK(upload_q4(e, (int)L.o_proj.k, refs, d.o));
-  QCHECK(upload_q4(e, (int)L.o_proj.k, refs, d.o1, 1));
+  add_groups(L.o_proj, 0, (int)(L.o_proj.n / kGroup));
+  QCHECK(upload_q4(e, nh_l * kHeadDim, refs, d.o, kTileGroups, h0 * kHeadDim));
+  QCHECK(upload_q4(e, nh_l * kHeadDim, refs, d.o1, 1, h0 * kHeadDim));
   refs.clear();
-  const int gI = (int)(L.gate_proj.n / kGroup);
-  for (int t = 0; t < gI / 4; ++t) {
-    for (int j = 0; j < 4; ++j) refs.push_back({&L.gate_proj, 4 * t + j});
-    for (int j = 0; j < 4; ++j) refs.push_back({&L.up_proj, 4 * t + j});
+  // gate/up tiles: 4 gate groups then the same 4 up groups (zero-padded at the end)
+  const int gI_l = e->inter_l / kGroup, gi0 = e->rank * gI_l;
+  for (int t = 0; t < (gI_l + 3) / 4; ++t) {
+    for (int j = 0; j < 4; ++j) refs.push_back({4 * t + j < gI_l ? &L.gate_proj : nullptr, gi0 + 4 * t + j});
+    for (int j = 0; j < 4; ++j) refs.push_back({4 * t + j < gI_l ? &L.up_proj : nullptr, gi0 + 4 * t + j});
   }
   QCHECK(upload_q4(e, H, refs, d.gu));
   refs.clear();
-  add_all(L.down_proj);
-  QCHECK(upload_q4(e, (int)L.down_proj.k, refs, d.down));
+  add_groups(L.down_proj, 0, (int)(L.down_proj.n / kGroup));
+  QCHECK(upload_q4(e, e->inter_l, refs, d.down, kTileGroups, e->rank * e->inter_l));
   std::vector<float> g1 = f16_to_f32(L.input_norm_gamma, H), g2 = f16_to_f32(L.post_attn_norm_gamma, H);
   QCHECK(e->alloc(&d.g_in, H));
   QCHECK(e->alloc(&d.g_post, H));
   QCHECK(upload(e, d.g_in, g1.data(), H * 4));
   QCHECK(upload(e, d.g_post, g2.data(), H * 4));
   d.rope = w->no_rope_layers[i] ? 1 : 0;
-  d.nq = (int)(L.num_heads * kHeadDim);
-  d.nkv = (int)(L.num_kv_heads * kHeadDim);
+  d.nq = nh_l * kHeadDim;
+  d.nkv = nkv_l * kHeadDim;
   return QORA_OK;
 }
 
@@ -462,8 +481,21 @@ qora_status engine_init(qora_engine* e, const qora_weights_view* w) {
   e->hidden = w->hidden;
   e->inter = (uint32_t)L0.gate_proj.n;
   e->nh = L0.num_heads;
-  e->nkv = L0.num_kv_heads;
+  e->nkv_total = L0.num_kv_heads;
   e->rope_rows = (uint32_t)w->rope_rows;
+  {
+    // tensor-parallel shard of this rank: q heads split evenly; kv heads split while
+    // they divide, otherwise each rank keeps the one kv head its q heads use
+    const int T = e->tp, nh = (int)e->nh, nkvh = (int)e->nkv_total, I = (int)e->inter;
+    if (nh % T != 0 || (nkvh % T != 0 && T % nkvh != 0) || (I / kGroup) % T != 0)
+      return fail(QORA_ERR_UNSUPPORTED, "tp_size %d does not divide heads %d/%d and MLP groups %d", T, nh,
+                  nkvh, I / kGroup);
+    e->nh_l = nh / T;
+    e->nkv_l = nkvh % T == 0 ? nkvh / T : 1;
+    e->kv0 = nkvh % T == 0 ? e->rank * e->nkv_l : e->rank / (T / nkvh);
+    e->inter_l = I / T;
+    e->nkv = (uint32_t)e->nkv_l;  // KV heads held by this engine's caches
+  }
   e->sms = sm_count(e->device);
   QCUDA(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
   e->layers.resize(w->num_layers);
@@ -485,6 +517,12 @@ qora_status engine_init(qora_engine* e, const qora_weights_view* w) {
           // allocation bookkeeping is not thread-safe: build into a private engine shell
           qora_engine tmp;
           tmp.device = e->device;
+          tmp.tp = e->tp;
+          tmp.rank = e->rank;
+          tmp.nh_l = e->nh_l;
+          tmp.nkv_l = e->nkv_l;
+          tmp.kv0 = e->kv0;
+          tmp.inter_l = e->inter_l;
           tmp.layers.resize(w->num_layers);
           st[i] = build_layer(&tmp, w, i);
           if (st[i] != QORA_OK) errs[i] = g_last_error;
@@ -573,13 +611,14 @@ qora_status mega_init(qora_engine* e) {
   e->mk_ok = false;
   const int H = (int)e->hidden, G = e->sms;
   const LayerDev& d0 = e->layers[0];
-  const int nh = (int)e->nh, nkvh = (int)e->nkv;
+  const int nh = e->nh_l, nkvh = e->nkv_l;  // this engine's (shard's) heads
   auto no = [&](const char* why) {
     e->mk_why = why;
     return QORA_OK;
   };
   if (H != 1024 && H != 2048) return no("hidden must be 1024 or 2048");
-  if (nh != mk::kHeadsPerKV * nkvh || nh > 16) return no("needs 4 query heads per KV head and at most 16 heads");
+  if (nh % nkvh != 0 || nh / nkvh > mk::kHeadsPerKV || nh > 16)
+    return no("needs at most 4 query heads per KV head and at most 16 heads");
   if (G < 16 || G > mk::kMaxUnits) return no("SM count outside the supported range");
   // q|k|v and o_proj: one CTA per 32-column group (q|k|v on the last CTAs, o_proj on the
   // first); gate/up and down: split-K over all CTAs
@@ -589,11 +628,11 @@ qora_status mega_init(qora_engine* e) {
   const int subn[4] = {d0.qkv1.G, d0.o1.G, G, G};
   for (int m = 0; m < 4; ++m) {
     const long long total = (long long)mats[m]->tiles * mats[m]->K;
-    if ((m < 2 && mats[m]->K > mk::kXsCap) || (total + subn[m] - 1) / subn[m] > mk::kXsCap)
+    if ((m < mk::GU && mats[m]->K > mk::kXsCap) || (total + subn[m] - 1) / subn[m] > mk::kXsCap)
       return no("per-CTA rows exceed the shared input buffer");
     if (total * subn[m] >= (1ll << 31)) return no("matrix too large for 32-bit split-K indexing");
     if ((total + subn[m] - 1) / subn[m] > mats[m]->K) return no("a CTA's rows would span more than two tiles");
-    if (mats[m]->K <= mk::kCT) return no("matrix with too few rows");
+    if (m != mk::OPR && mats[m]->K <= mk::kCT) return no("matrix with too few rows");
     e->mk_sub0[m] = sub0[m];
     e->mk_subn[m] = subn[m];
   }
@@ -631,6 +670,18 @@ qora_status mega_init(qora_engine* e) {
   QCHECK(alloc_tagged(&e->mk_qkv, (size_t)d0.qkv1.G * kGroup));
   QCHECK(alloc_tagged(&e->mk_gu_part, np_gu));
   QCHECK(e->alloc(&e->mk_dn_part, np_dn));
+  if (e->tp > 1) {
+    // receive buffers the peers write into: o and down partials [L][tp][H] (tagged), the
+    // ranks' lm_head bests [tp][2] (tagged), the full logits [vocab]
+    const size_t L = e->num_layers, T = e->tp;
+    e->tp_off_d = L * T * H * 8;
+    e->tp_off_lm = 2 * L * T * H * 8;
+    e->tp_off_logits = (e->tp_off_lm + T * 16 + 255) / 256 * 256;
+    e->tp_region_bytes = e->tp_off_logits + (size_t)e->vocab * 4;
+    QCHECK(e->alloc(&e->tp_region, e->tp_region_bytes));
+    QCUDA(cudaMemset(e->tp_region, 0, e->tp_region_bytes));
+    e->logits = reinterpret_cast<float*>(e->tp_region + e->tp_off_logits);
+  }
   QCHECK(e->alloc(&e->mk_lm_v, G));
   QCHECK(e->alloc(&e->mk_lm_i, G));
   e->mk_ok = true;
@@ -675,8 +726,8 @@ qora_status mega_prepare(qora_engine* e, qora_kv* kv) {
   a.H = (int)e->hidden;
   a.nq = d0.nq;
   a.nkvw = d0.nkv;
-  a.nh = (int)e->nh;
-  a.nkvh = (int)e->nkv;
+  a.nh = e->nh_l;
+  a.nkvh = e->nkv_l;
   a.vocab = (int)e->vocab;
   a.lm_row_bytes = (int)e->lm_row_bytes;
   {
@@ -712,6 +763,18 @@ qora_status mega_prepare(qora_engine* e, qora_kv* kv) {
   a.ring_cap = (int)kv->max_seq;
   a.timeout_ns = 2000000000ull;
   a.trace = e->mk_trace;
+  a.tp = e->tp;
+  a.rank = e->rank;
+  a.hpk = e->nh_l / e->nkv_l;
+  a.v0 = (int)((long long)e->rank * e->vocab / e->tp);
+  a.v1 = (int)((long long)(e->rank + 1) * e->vocab / e->tp);
+  for (int p = 0; p < e->tp && e->tp > 1; ++p) {
+    uint8_t* base = e->tp_peer[p];
+    a.peer_o[p] = reinterpret_cast<uint64_t*>(base);
+    a.peer_d[p] = reinterpret_cast<uint64_t*>(base + e->tp_off_d);
+    a.peer_lm[p] = reinterpret_cast<uint64_t*>(base + e->tp_off_lm);
+    a.peer_logits[p] = reinterpret_cast<float*>(base + e->tp_off_logits);
+  }
   kv->mk_ready = true;
   return QORA_OK;
 }
@@ -836,6 +899,10 @@ bool kv_uses_mega(const qora_engine* e, const qora_kv* kv) {
 }
 
 qora_status step_prepare(qora_engine* e, qora_kv* kv) {
+  if (e->tp > 1 && !e->tp_connected)
+    return fail(QORA_ERR_UNSUPPORTED, "tensor-parallel engine: call qora_tp_connect first");
+  if (e->tp > 1 && !kv_uses_mega(e, kv))
+    return fail(QORA_ERR_UNSUPPORTED, "tensor-parallel engines need caches of at most %u positions", e->mk_max_seq);
   if (kv_uses_mega(e, kv)) return mega_prepare(e, kv);
   return ensure_graph(e, kv);
 }
@@ -1049,9 +1116,17 @@ qora_status qora_engine_create(const qora_weights_view* weights, const qora_engi
   QCHECK(validate_view(weights));
   const int n_gpus = opts ? opts->n_gpus : 1;
   if (n_gpus > 1)
-    return fail(QORA_ERR_UNSUPPORTED, "tensor-parallel engines (n_gpus=%d) are not in this build", n_gpus);
+    return fail(QORA_ERR_UNSUPPORTED,
+                "single-process multi-GPU engines (n_gpus=%d) are not in this build; use tp_size/tp_rank with "
+                "one engine per GPU",
+                n_gpus);
   if (opts && (opts->flags & ~QORA_FLAG_PER_OP_KERNELS))
     return fail(QORA_ERR_INVALID, "unknown option flags 0x%x", opts->flags);
+  const int tp = (opts && opts->tp_size > 1) ? opts->tp_size : 1, rank = (opts && tp > 1) ? opts->tp_rank : 0;
+  if (tp != 1 && tp != 2 && tp != 4 && tp != 8) return fail(QORA_ERR_INVALID, "tp_size %d (1, 2, 4 or 8)", tp);
+  if (rank < 0 || rank >= tp) return fail(QORA_ERR_INVALID, "tp_rank %d of %d", rank, tp);
+  if (tp > 1 && opts && (opts->flags & QORA_FLAG_PER_OP_KERNELS))
+    return fail(QORA_ERR_UNSUPPORTED, "tensor-parallel engines run the persistent kernel only");
   int ndev = 0;
   QCUDA(cudaGetDeviceCount(&ndev));
   const int dev = opts ? opts->first_device : 0;
@@ -1059,8 +1134,12 @@ qora_status qora_engine_create(const qora_weights_view* weights, const qora_engi
   QCUDA(cudaSetDevice(dev));
   std::unique_ptr<qora_engine> e(new qora_engine());
   e->device = dev;
+  e->tp = tp;
+  e->rank = rank;
   e->use_mega = !(opts && (opts->flags & QORA_FLAG_PER_OP_KERNELS));
   QCHECK(engine_init(e.get(), weights));
+  if (tp > 1 && !e->mk_ok)
+    return fail(QORA_ERR_UNSUPPORTED, "tensor-parallel shard has no persistent kernel: %s", e->mk_why.c_str());
   *out = e.release();
   return QORA_OK;
 }
@@ -1109,6 +1188,66 @@ void qora_engine_destroy(qora_engine* engine) {
   if (!engine) return;
   cudaSetDevice(engine->device);
   delete engine;
+}
+
+namespace {
+struct TpBlob {  // what one rank hands to the others
+  uint32_t magic, tp, rank, pad;
+  uint64_t region_bytes;
+  cudaIpcMemHandle_t handle;
+};
+constexpr uint32_t kTpMagic = 0x51545031u;  // "QTP1"
+}  // namespace
+
+qora_status qora_tp_export(qora_engine* e, void* buf, size_t cap, size_t* len) {
+  if (!e || !len) return fail(QORA_ERR_INVALID, "NULL argument");
+  if (e->tp < 2) return fail(QORA_ERR_INVALID, "not a tensor-parallel engine");
+  *len = sizeof(TpBlob);
+  if (!buf) return QORA_OK;
+  if (cap < sizeof(TpBlob)) return fail(QORA_ERR_INVALID, "buffer of %zu bytes, need %zu", cap, sizeof(TpBlob));
+  QCUDA(cudaSetDevice(e->device));
+  TpBlob b{};
+  b.magic = kTpMagic;
+  b.tp = (uint32_t)e->tp;
+  b.rank = (uint32_t)e->rank;
+  b.region_bytes = e->tp_region_bytes;
+  QCUDA(cudaIpcGetMemHandle(&b.handle, e->tp_region));
+  std::memcpy(buf, &b, sizeof(b));
+  return QORA_OK;
+}
+
+qora_status qora_tp_connect(qora_engine* e, const void* handles, size_t len_per_rank) {
+  if (!e || !handles) return fail(QORA_ERR_INVALID, "NULL argument");
+  if (e->tp < 2) return fail(QORA_ERR_INVALID, "not a tensor-parallel engine");
+  if (e->tp_connected) return fail(QORA_ERR_INVALID, "already connected");
+  if (len_per_rank != sizeof(TpBlob)) return fail(QORA_ERR_INVALID, "handle size %zu, expected %zu", len_per_rank,
+                                                   sizeof(TpBlob));
+  QCUDA(cudaSetDevice(e->device));
+  std::vector<TpBlob> bs(e->tp);
+  std::memcpy(bs.data(), handles, sizeof(TpBlob) * e->tp);
+  for (int p = 0; p < e->tp; ++p)
+    if (bs[p].magic != kTpMagic || (int)bs[p].tp != e->tp || (int)bs[p].rank != p ||
+        bs[p].region_bytes != e->tp_region_bytes)
+      return fail(QORA_ERR_INVALID, "handle %d is not rank %d of this %d-way group", p, p, e->tp);
+  std::vector<void*> opened;
+  for (int p = 0; p < e->tp; ++p) {
+    if (p == e->rank) {
+      e->tp_peer[p] = e->tp_region;
+      continue;
+    }
+    void* ptr = nullptr;
+    const cudaError_t ce = cudaIpcOpenMemHandle(&ptr, bs[p].handle, cudaIpcMemLazyEnablePeerAccess);
+    if (ce != cudaSuccess) {
+      for (void* q : opened) cudaIpcCloseMemHandle(q);
+      return fail(QORA_ERR_CUDA, "opening rank %d's buffers: %s", p, cudaGetErrorString(ce));
+    }
+    opened.push_back(ptr);
+    e->tp_peer[p] = static_cast<uint8_t*>(ptr);
+  }
+  e->tp_opened = opened;
+  e->tp_connected = true;
+  for (qora_kv* kv : e->kvs) kv->mk_ready = false;  // rebuild kernel arguments with the peers
+  return QORA_OK;
 }
 
 qora_status qora_engine_info(const qora_engine* e, uint32_t* num_layers, uint32_t* vocab,
@@ -1179,12 +1318,14 @@ qora_status qora_kv_import(qora_kv* kv, uint32_t layer, const float* k, const fl
   if (layer >= kv->e->num_layers) return fail(QORA_ERR_RANGE, "layer %u", layer);
   if (seq_len > kv->max_seq) return fail(QORA_ERR_RANGE, "seq_len %u > max_seq %u", seq_len, kv->max_seq);
   QCUDA(cudaSetDevice(kv->e->device));
-  // host rows [seq][nkv*128] -> device head-major [nkv][max_seq][128]
-  const size_t row = (size_t)kv->e->nkv * kHeadDim * sizeof(float), hb = kHeadDim * sizeof(float);
+  // host rows [seq][all kv heads*128] -> device head-major [local kv heads][max_seq][128]
+  // (a tensor-parallel rank keeps heads kv0 .. kv0 + nkv - 1)
+  const size_t row = (size_t)kv->e->nkv_total * kHeadDim * sizeof(float), hb = kHeadDim * sizeof(float);
   for (uint32_t j = 0; seq_len && j < kv->e->nkv; ++j) {
     const size_t off = layer * kv->layer_stride() + (size_t)j * kv->max_seq * kHeadDim;
-    QCUDA(cudaMemcpy2D(kv->k + off, hb, k + (size_t)j * kHeadDim, row, hb, seq_len, cudaMemcpyHostToDevice));
-    QCUDA(cudaMemcpy2D(kv->v + off, hb, v + (size_t)j * kHeadDim, row, hb, seq_len, cudaMemcpyHostToDevice));
+    const size_t src = (size_t)(kv->e->kv0 + j) * kHeadDim;
+    QCUDA(cudaMemcpy2D(kv->k + off, hb, k + src, row, hb, seq_len, cudaMemcpyHostToDevice));
+    QCUDA(cudaMemcpy2D(kv->v + off, hb, v + src, row, hb, seq_len, cudaMemcpyHostToDevice));
   }
   kv->len[layer] = seq_len;
   return QORA_OK;
@@ -1199,11 +1340,12 @@ qora_status qora_kv_export(const qora_kv* kv, uint32_t layer, float* k, float* v
   if (seq_len > kv->len[layer]) return fail(QORA_ERR_RANGE, "seq_len %u > length %u", seq_len, kv->len[layer]);
   QCUDA(cudaSetDevice(kv->e->device));
   QCUDA(cudaStreamSynchronize(kv->e->stream));
-  const size_t row = (size_t)kv->e->nkv * kHeadDim * sizeof(float), hb = kHeadDim * sizeof(float);
-  for (uint32_t j = 0; seq_len && j < kv->e->nkv; ++j) {
+  const size_t row = (size_t)kv->e->nkv_total * kHeadDim * sizeof(float), hb = kHeadDim * sizeof(float);
+  for (uint32_t j = 0; seq_len && j < kv->e->nkv; ++j) {  // a rank fills only its own heads' columns
     const size_t off = layer * kv->layer_stride() + (size_t)j * kv->max_seq * kHeadDim;
-    QCUDA(cudaMemcpy2D(k + (size_t)j * kHeadDim, row, kv->k + off, hb, hb, seq_len, cudaMemcpyDeviceToHost));
-    QCUDA(cudaMemcpy2D(v + (size_t)j * kHeadDim, row, kv->v + off, hb, hb, seq_len, cudaMemcpyDeviceToHost));
+    const size_t dst = (size_t)(kv->e->kv0 + j) * kHeadDim;
+    QCUDA(cudaMemcpy2D(k + dst, row, kv->k + off, hb, hb, seq_len, cudaMemcpyDeviceToHost));
+    QCUDA(cudaMemcpy2D(v + dst, row, kv->v + off, hb, hb, seq_len, cudaMemcpyDeviceToHost));
   }
   return QORA_OK;
 }

@@ -57,6 +57,8 @@ SIGNATURES = {
     "qora_engine_launches_per_step": (C.c_int, [_vp, _P(_u32)]),
     "qora_engine_set_trace": (C.c_int, [_vp, C.c_int]),
     "qora_engine_get_trace": (C.c_int, [_vp, _vp, C.c_size_t, _P(C.c_size_t)]),
+    "qora_tp_export": (C.c_int, [_vp, _vp, C.c_size_t, _P(C.c_size_t)]),
+    "qora_tp_connect": (C.c_int, [_vp, C.c_char_p, C.c_size_t]),
     "qora_q4_gemv": (C.c_int, [_vp, _vp, _vp, _u64, _u64, _vp, _vp]),
     "qora_q4_gemv_static": (C.c_int, [_vp, _vp, _vp, _u64, _u64, _vp, _vp]),
     "qora_q4_dequant": (C.c_int, [_vp, _vp, _u64, _u64, _u64, _vp, _vp]),
@@ -102,9 +104,14 @@ class DecodeWeights:
     """An engine: the model resident on the GPU (the `DecodeWeights` of src/gemv.rs:195)."""
 
     def __init__(self, model: Optional[Model] = None, path: Optional[str] = None,
-                 device: int = 0, n_gpus: int = 1, per_op_kernels: bool = False):
+                 device: int = 0, n_gpus: int = 1, per_op_kernels: bool = False,
+                 tp_size: int = 1, tp_rank: int = 0):
+        """tp_size > 1: this engine is rank tp_rank of a tensor-parallel group (one engine
+        per GPU); call tp_export() on every rank and tp_connect(all_handles) on each."""
         self.per_op_kernels = per_op_kernels
-        opts = abi.EngineOptions(n_gpus, device, FLAG_PER_OP_KERNELS if per_op_kernels else 0)
+        self.tp_size, self.tp_rank = tp_size, tp_rank
+        opts = abi.EngineOptions(n_gpus, device, FLAG_PER_OP_KERNELS if per_op_kernels else 0,
+                                 tp_size, tp_rank)
         h = C.c_void_p()
         if path is not None:
             check(lib().qora_engine_create_from_file(os.fsencode(path), C.byref(opts), C.byref(h)))
@@ -122,6 +129,24 @@ class DecodeWeights:
         if getattr(self, "h", None):
             lib().qora_engine_destroy(self.h)
             self.h = None
+
+    def tp_export(self) -> bytes:
+        """This rank's opaque peer handle (qora_tp_export)."""
+        n = C.c_size_t()
+        check(lib().qora_tp_export(self.h, None, 0, C.byref(n)))
+        buf = C.create_string_buffer(n.value)
+        check(lib().qora_tp_export(self.h, buf, n.value, C.byref(n)))
+        return buf.raw[: n.value]
+
+    def tp_connect(self, handles) -> None:
+        """Map every rank's buffers; `handles` lists all ranks' tp_export() bytes in rank
+        order (qora_tp_connect)."""
+        handles = list(handles)
+        size = len(handles[0])
+        if len(handles) != self.tp_size or any(len(h) != size for h in handles):
+            raise ValueError("need one handle of equal size per rank")
+        blob = b"".join(handles)
+        check(lib().qora_tp_connect(self.h, blob, size))
 
     def __del__(self):
         try:
