@@ -498,10 +498,11 @@ QORA_DEV float ld_checked(const Cons& C, const uint64_t* p, uint32_t tag) {
 }
 
 // Rows of this thread's xs entries i = tid + j*kCT of a span: (lin0 + i) mod K, stepped
-// without divisions (kCT < K for every matrix).
+// without a division when kCT < K (every matrix of the full-size model).
 QORA_DEV int row_next(int r, int K) {
   r += kCT;
-  return r >= K ? r - K : r;
+  if (r >= K) r -= K;
+  return r >= K ? r % K : r;
 }
 
 QORA_DEV void prefetch_gains(const Cons& C, const float* g, Span sp, int K, float (&gam)[kXsPer]) {

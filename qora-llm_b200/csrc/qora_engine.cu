@@ -632,7 +632,6 @@ qora_status mega_init(qora_engine* e) {
       return no("per-CTA rows exceed the shared input buffer");
     if (total * subn[m] >= (1ll << 31)) return no("matrix too large for 32-bit split-K indexing");
     if ((total + subn[m] - 1) / subn[m] > mats[m]->K) return no("a CTA's rows would span more than two tiles");
-    if (m != mk::OPR && mats[m]->K <= mk::kCT) return no("matrix with too few rows");
     e->mk_sub0[m] = sub0[m];
     e->mk_subn[m] = subn[m];
   }
