@@ -878,6 +878,7 @@ __device__ __noinline__ uint32_t attention_phase(int L, uint32_t chunk) {
     vc[(long long)pos * kHeadDim + d] = v;
   }
   C.bar();
+  C.fstamp();
   // scores: 4 rows per warp pass (8 lanes each), 60 rows per CTA pass
   const int li = lane & 7, ri = warp * 4 + (lane >> 3);
 #pragma unroll 1
@@ -895,6 +896,7 @@ __device__ __noinline__ uint32_t attention_phase(int L, uint32_t chunk) {
   }
   if (has_pos && warp == 0 && !C.aborted_w()) kscore(sq, skv, sc, pos - s0, (lane >> 3) == 0, li);
   C.bar();
+  C.fstamp();
   // chunk softmax numerators, one warp per query head
   if (warp < hpk && !C.aborted_w()) {
     float* row = sc + warp * kMaxAttnChunk;
@@ -961,46 +963,93 @@ __device__ __noinline__ uint32_t o_phase(int L, uint32_t chunk) {
   const uint32_t tag = tag_of(C, L);
   await_tags(C, nkvh * nch, tag, [&](int i) { return a.att_ml + (long long)i * 2 * kHeadsPerKV; });
   C.stamp(2 + 8 * min(L, kTraceLayers - 1) + 3);
+  C.fstamp();
   // per query head h: M = max_ch m, w_ch = exp(m_ch - M), 1/l with l = sum l_ch w_ch;
   // unit (chunk ch, kv head h/hpk) holds head h at slot h%hpk
   const int hpk = a.hpk;
   float* mw = C.scratch + kOffB;  // [nh][nch], then 1/l [nh]
   float* invl = mw + a.nh * nch;
+  const long long ustride = (long long)nkvh * kHeadsPerKV * 2;          // (m, l): next chunk, same head
+  const long long ostride = (long long)nkvh * kHeadsPerKV * kHeadDim;   // o: next chunk, same head
+  auto ml_of = [&](int h) { return a.att_ml + ((h / hpk) * kHeadsPerKV + h % hpk) * 2; };
+  int orow[kXsPer];  // row r = head*128 + dim -> offset in a unit's [4][128] block
+#pragma unroll
+  for (int j = 0; j < kXsPer; ++j) {
+    const int r = C.tid + j * kCT, h = r / kHeadDim;
+    orow[j] = ((h / hpk) * kHeadsPerKV + h % hpk) * kHeadDim + r % kHeadDim;
+  }
+  // One round trip for short contexts: this thread's o values of chunks [0, 4) and, per
+  // warp, the (m, l) of chunks [0, 32) of its query heads (warp, warp + kCW)
+  uint64_t v[kXsPer][4], mlv[2][2];
+  {
+    uint64_t t0 = 0;
 #pragma unroll 1
-  for (int h = C.warp; h < a.nh; h += kCW) {
-    const uint64_t* ml = a.att_ml + ((h / hpk) * kHeadsPerKV + h % hpk) * 2;
-    const long long ustride = (long long)nkvh * kHeadsPerKV * 2;  // next chunk, same head
-    float mx = -INFINITY;
-#pragma unroll 1
-    for (int ch = C.lane; ch < nch; ch += 32) mx = fmaxf(mx, ld_checked(C, ml + ch * ustride, tag));
-    mx = warp_max(mx);
-    float l = 0.0f;
-#pragma unroll 1
-    for (int ch = C.lane; ch < nch; ch += 32) {
-      const float w = expf(ld_checked(C, ml + ch * ustride, tag) - mx);
-      mw[h * nch + ch] = w;
-      l = __fmaf_rn(ld_checked(C, ml + ch * ustride + 1, tag), w, l);
+    for (int it = 0;; ++it) {
+      bool ok = true;
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const int h = C.warp + q * kCW;
+        const bool in = h < a.nh && C.lane < nch;
+        if (in) ptx::ld_relaxed_v2_b64(ml_of(h) + C.lane * ustride, mlv[q][0], mlv[q][1]);
+        ok &= !in || (tag_ok(mlv[q][0], tag) & tag_ok(mlv[q][1], tag));
+      }
+#pragma unroll
+      for (int j = 0; j < kXsPer; ++j) {
+        const int r = C.tid + j * kCT;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const bool in = r < K && k < nch;
+          v[j][k] = in ? ptx::ld_relaxed_b64(a.att_o + k * ostride + orow[j]) : 0ull;
+          ok &= !in || tag_ok(v[j][k], tag);
+        }
+      }
+      if (ok || retry_stop(C, t0, it)) break;
     }
-    l = warp_sum(l);
-    if (C.lane == 0) invl[h] = __fdiv_rn(1.0f, l);
+  }
+  C.fstamp();
+  // per query head h: M = max_ch m, w_ch = exp(m_ch - M), 1/l with l = sum l_ch w_ch
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const int h = C.warp + q * kCW;
+    if (h < a.nh) {  // warp-uniform
+      const uint64_t* ml = ml_of(h);
+      float mx = C.lane < nch ? tag_val(mlv[q][0]) : -INFINITY;
+#pragma unroll 1
+      for (int ch = C.lane + 32; ch < nch; ch += 32) mx = fmaxf(mx, ld_checked(C, ml + ch * ustride, tag));
+      mx = warp_max(mx);
+      float l = 0.0f;
+      if (C.lane < nch) {
+        const float w = expf(tag_val(mlv[q][0]) - mx);
+        mw[h * nch + C.lane] = w;
+        l = __fmul_rn(tag_val(mlv[q][1]), w);
+      }
+#pragma unroll 1
+      for (int ch = C.lane + 32; ch < nch; ch += 32) {
+        const float w = expf(ld_checked(C, ml + ch * ustride, tag) - mx);
+        mw[h * nch + ch] = w;
+        l = __fmaf_rn(ld_checked(C, ml + ch * ustride + 1, tag), w, l);
+      }
+      l = warp_sum(l);
+      if (C.lane == 0) invl[h] = __fdiv_rn(1.0f, l);
+    }
   }
   C.bar();
-  // xs[r] = (sum_ch o_ch[r] w_ch) / l, r = head * 128 + dim; 5 rows x 4 chunks of loads
-  // in flight per batch
+  C.fstamp();
+  // xs[r] = (sum_ch o_ch[r] w_ch) / l, r = head * 128 + dim
   {
     float* xs = C.scratch;
-    const long long ostride = (long long)nkvh * kHeadsPerKV * kHeadDim;  // next chunk, same head
     float acc[kXsPer];
-    int orow[kXsPer];  // row r = head*128 + dim -> offset in a unit's [4][128] block
 #pragma unroll
     for (int j = 0; j < kXsPer; ++j) {
-      acc[j] = 0.0f;
       const int r = C.tid + j * kCT, h = r / kHeadDim;
-      orow[j] = ((h / hpk) * kHeadsPerKV + h % hpk) * kHeadDim + r % kHeadDim;
+      acc[j] = 0.0f;
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        if (r < K && k < nch) acc[j] = __fmaf_rn(tag_val(v[j][k]), mw[h * nch + k], acc[j]);
     }
 #pragma unroll 1
-    for (int c0 = 0; c0 < nch; c0 += 4) {
-      uint64_t v[kXsPer][4], t0 = 0;
+    for (int c0 = 4; c0 < nch; c0 += 4) {  // longer contexts: further batches of 4 chunks
+      uint64_t t0 = 0;
 #pragma unroll 1
       for (int it = 0;; ++it) {
         bool ok = true;
