@@ -35,8 +35,12 @@ SEED = 0
 HIDDEN, LAYERS, VOCAB = 2048, 36, 128256
 # algorithmic bytes of one decode step excluding KV (weights + norms + lm_head embedding
 # read in full + final norm + the embedding row), and KV bytes per cached position
-WEIGHT_BYTES_PER_TOKEN = 36 * (43_941_888 + 8_192) + 147_750_912 + 4_096 + 1_152
-KV_BYTES_PER_POS = 36 * 2 * 4 * 128 * 4
+def weight_bytes_per_token(layers=LAYERS):
+    return layers * (43_941_888 + 8_192) + 147_750_912 + 4_096 + 1_152
+
+
+def kv_bytes_per_pos(layers=LAYERS):
+    return layers * 2 * 4 * 128 * 4
 
 
 def peaks():
@@ -105,10 +109,10 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def synth():
+def synth(layers=36):
     import importlib
     qf = importlib.import_module("qora-llm_b200").qora_format
-    model = qf.synth_model(seed=SEED)
+    model = qf.synth_model(seed=SEED, num_layers=layers)
     prompt = np.random.default_rng(1).integers(0, VOCAB, size=PROMPT).astype(np.uint32)
     return model, prompt
 
@@ -149,7 +153,7 @@ def cpu_model():
 def run_reference(args, rank):
     if rank != 0:
         return 0
-    model, prompt = synth()
+    model, prompt = synth(args.layers)
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle
     threads = os.cpu_count() or 1
@@ -193,7 +197,7 @@ def run_ours(args, rank, world, local_rank):
         import datetime
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
-    model, prompt = synth()
+    model, prompt = synth(args.layers)
     if world > 1:
         # tensor parallelism: one engine per GPU; exchange the ranks' peer handles
         eng = pkg.DecodeWeights(model=model, device=local_rank, tp_size=world, tp_rank=rank)
@@ -245,7 +249,7 @@ def run_ours(args, rank, world, local_rank):
     peak, peak_kind = peaks()
     mega = eng.launches_per_step() == 1
     mean_kv = kv_start + (K - 1) / 2.0 + 1
-    step_bytes = WEIGHT_BYTES_PER_TOKEN + KV_BYTES_PER_POS * (mean_kv + 1)
+    step_bytes = weight_bytes_per_token(args.layers) + kv_bytes_per_pos(args.layers) * (mean_kv + 1)
     rank_bytes = step_bytes / world  # weights, lm_head rows and (up to tp 4) KV heads split evenly
     traffic = None
     tpath = os.path.join(ROOT, "profiles", "decode_megakernel_dram.json")
@@ -275,7 +279,7 @@ def run_ours(args, rank, world, local_rank):
         "config": {
             "workload": "config 3: SmolLM3-3B Q4 (36 layers, vocab 128256), 32-token prompt, "
                         "greedy decode at batch 1",
-            "prompt": PROMPT, "kv_len_mean": mean_kv,
+            "prompt": PROMPT, "kv_len_mean": mean_kv, "layers": args.layers,
             "parallelism": "single GPU" if world == 1 else f"tp{world} (tensor parallel, NVLink peer all-reduce)",
             "l2": "inputs larger than L2: 1.73 GB of weights streamed per step",
             "bytes_per_step": step_bytes,
@@ -310,6 +314,9 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--layers", type=int, default=36,
+                    help="decoder layers of the synthetic model (36 = SmolLM3-3B; fewer only for "
+                         "small profiling captures, never for a reported number)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
