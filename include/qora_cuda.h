@@ -127,9 +127,10 @@ qora_status qora_engine_info(const qora_engine* engine, uint32_t* num_layers,
                              uint32_t* vocab, uint32_t* hidden, uint32_t* format,
                              uint64_t* device_bytes);
 
-/* KV cache with capacity max_seq positions for `batch` independent sequences, f32,
- * token-major [seq][kv_heads][head_dim] per layer. Replaces `empty_kv_cache`
- * (src/gemv.rs:159) / `RawKvCache` (src/gemv.rs:156). batch must be 1 for now. */
+/* KV cache with capacity max_seq positions for `batch` independent sequences, f32.
+ * Replaces `empty_kv_cache` (src/gemv.rs:159) / `RawKvCache` (src/gemv.rs:156), one per
+ * sequence. Q4 engines take batch 1 (the batch-1 decode of the reference); F16 engines
+ * take 1..128 sequences that decode together (each decode step advances all of them). */
 qora_status qora_kv_create(qora_engine* engine, uint32_t max_seq, uint32_t batch,
                            qora_kv** out);
 void qora_kv_destroy(qora_kv* kv);
@@ -171,6 +172,14 @@ qora_status qora_decode_step(qora_engine* engine, qora_kv* kv, const uint32_t* t
  * the n_tokens argmax ids to out_tokens. */
 qora_status qora_generate_greedy(qora_engine* engine, qora_kv* kv, uint32_t first_token,
                                  uint32_t n_tokens, uint32_t* out_tokens);
+
+/* Greedy generation for every sequence of a cache at once: first_tokens [batch], then
+ * n_tokens batched decode steps on the device, each feeding its argmax back. out_tokens:
+ * [n_tokens][batch]. device_ms (optional) receives the CUDA-event time of the steps.
+ * The batched form of the loop of src/generate.rs:299-331 (temperature 0). */
+qora_status qora_generate_greedy_batch(qora_engine* engine, qora_kv* kv,
+                                       const uint32_t* first_tokens, uint32_t n_tokens,
+                                       uint32_t* out_tokens, float* device_ms);
 
 /* One decoder layer at batch 1 (the body of the layer loop, src/gemv.rs:883-1012):
  * x ([hidden] host f32) is the residual stream in and out; the layer's K/V row is

@@ -27,6 +27,7 @@
 #include "../../include/qora_cuda.h"
 #include "attention.cuh"
 #include "common.cuh"
+#include "f16_batch.cuh"
 #include "lm_head.cuh"
 #include "megakernel.cuh"
 #include "q4_gemv.cuh"
@@ -225,6 +226,18 @@ struct LayerDev {
   int nq = 0, nkv = 0;
 };
 
+// F16 weights (format 0) for the batched path: N-major [k][n] f16 as in the file, with
+// q|k|v and gate|up concatenated along n so one GEMM serves each pair.
+struct F16Layer {
+  __half* wqkv = nullptr;   // [hidden][nq + 2 nkv*128]
+  __half* wo = nullptr;     // [nq][hidden]
+  __half* wgu = nullptr;    // [hidden][2 I]: gate columns then up columns
+  __half* wdown = nullptr;  // [I][hidden]
+  float* g_in = nullptr;
+  float* g_post = nullptr;
+  int rope = 0;
+};
+
 }  // namespace
 
 // ================================================================== engine / kv objects
@@ -245,6 +258,14 @@ struct qora_engine {
   bool tp_connected = false;
   std::vector<void*> tp_opened;                   // IPC mappings to close
   std::vector<LayerDev> layers;
+  // F16 weights: batched per-op path (f16_batch.cuh)
+  std::vector<F16Layer> fl;
+  __half* f_embed = nullptr;       // [vocab][hidden]: embedding rows and the tied lm_head
+  int f_nqkv = 0;                  // q|k|v columns
+  int f_split[4] = {1, 1, 1, 1};   // K slices of the q|k|v, o, gate|up and down GEMMs
+  float *f_x = nullptr, *f_qkv = nullptr, *f_attn = nullptr, *f_h = nullptr;  // [rows][...]
+  float *f_logits = nullptr, *f_part = nullptr;
+  __half *f_xh = nullptr, *f_xl = nullptr;  // GEMM operand: activations as f16 hi + lo
   uint8_t* lm_table = nullptr;   // embedding rows: hidden/2 packed bytes | hidden/32 f16 scales
   long long lm_row_bytes = 0;
   float* final_gamma = nullptr;
@@ -304,9 +325,14 @@ struct qora_engine {
 struct qora_kv {
   qora_engine* e = nullptr;
   uint32_t max_seq = 0;
-  float* k = nullptr;  // [layers][max_seq][nkv*128]
+  uint32_t batch = 1;  // independent sequences
+  float* k = nullptr;  // [layers][batch][nkv][max_seq][128]
   float* v = nullptr;
-  std::vector<uint32_t> len;
+  std::vector<uint32_t> len;  // [batch][layers] positions filled
+  int* rows = nullptr;        // F16 path: row table (f16b::RowInfo)
+  int* rows_host = nullptr;   // pinned staging of the row table
+  unsigned* f_argmax = nullptr;  // [batch]
+  cudaGraphExec_t f_graph = nullptr;  // one batched F16 decode step
   StepState* st = nullptr;
   StepState* st_host = nullptr;  // pinned staging
   unsigned* ring = nullptr;      // greedy output ring [max_seq]
@@ -326,6 +352,10 @@ struct qora_kv {
   void release_device() {
     if (graph) cudaGraphExecDestroy(graph);
     graph = nullptr;
+    if (f_graph) cudaGraphExecDestroy(f_graph);
+    f_graph = nullptr;
+    if (rows_host) cudaFreeHost(rows_host);
+    rows_host = nullptr;
     for (void* p : allocs) cudaFree(p);
     allocs.clear();
     if (st_host) cudaFreeHost(st_host);
@@ -351,7 +381,9 @@ struct qora_kv {
     *p = static_cast<T*>(d);
     return QORA_OK;
   }
-  size_t layer_stride() const { return (size_t)max_seq * e->nkv * kHeadDim; }
+  size_t seq_stride() const { return (size_t)max_seq * e->nkv * kHeadDim; }
+  size_t layer_stride() const { return batch * seq_stride(); }
+  uint32_t& lenof(uint32_t seq, uint32_t layer) { return len[(size_t)seq * (len.size() / batch) + layer]; }
 };
 
 qora_engine::~qora_engine() {
@@ -371,16 +403,19 @@ namespace {
 
 qora_status validate_view(const qora_weights_view* w) {
   if (!w) return fail(QORA_ERR_INVALID, "weights view is NULL");
-  if (w->format == QORA_FORMAT_F16)
-    return fail(QORA_ERR_UNSUPPORTED, "F16 weights are not supported by this build yet");
-  if (w->format != QORA_FORMAT_Q4) return fail(QORA_ERR_INVALID, "unknown format %u", w->format);
+  if (w->format != QORA_FORMAT_Q4 && w->format != QORA_FORMAT_F16)
+    return fail(QORA_ERR_INVALID, "unknown format %u", w->format);
+  const bool q4 = w->format == QORA_FORMAT_Q4;
+  auto present = [q4](const qora_matrix_view& m) { return q4 ? (m.packed && m.scales) : m.data != nullptr; };
   if (w->num_layers == 0 || !w->layers) return fail(QORA_ERR_INVALID, "no layers");
   if (w->hidden == 0 || w->hidden % 1024 != 0 || w->hidden > 4096)
     return fail(QORA_ERR_UNSUPPORTED, "hidden=%u must be a multiple of 1024 up to 4096", w->hidden);
   if (w->rope_half_dim != kHalfDim)
     return fail(QORA_ERR_UNSUPPORTED, "rope_half_dim=%u, only 64 supported", w->rope_half_dim);
-  if (w->embed.k != w->vocab || w->embed.n != w->hidden || !w->embed.packed || !w->embed.scales)
-    return fail(QORA_ERR_INVALID, "embedding must be Q4 [vocab][hidden]");
+  if (w->embed.k != w->vocab || w->embed.n != w->hidden || !present(w->embed))
+    return fail(QORA_ERR_INVALID, "embedding must be [vocab][hidden] in the model's format");
+  if (!q4 && w->vocab % 64 != 0)
+    return fail(QORA_ERR_UNSUPPORTED, "F16 weights: vocab %u must be a multiple of 64", w->vocab);
   if (!w->final_norm_gamma || !w->no_rope_layers || !w->rope_cos || !w->rope_sin)
     return fail(QORA_ERR_INVALID, "missing final norm / rope tables / no_rope_layers");
   const qora_layer_view& L0 = w->layers[0];
@@ -399,10 +434,10 @@ qora_status validate_view(const qora_weights_view* w) {
         {&L.o_proj, nq, H, "o_proj"}, {&L.gate_proj, H, I, "gate_proj"}, {&L.up_proj, H, I, "up_proj"},
         {&L.down_proj, I, H, "down_proj"}};
     for (auto& wm : want) {
-      if (wm.m->k != wm.k || wm.m->n != wm.n || !wm.m->packed || !wm.m->scales)
-        return fail(QORA_ERR_INVALID, "layer %u %s: shape %llux%llu, expected %llux%llu (Q4)", i, wm.name,
+      if (wm.m->k != wm.k || wm.m->n != wm.n || !present(*wm.m))
+        return fail(QORA_ERR_INVALID, "layer %u %s: shape %llux%llu, expected %llux%llu (%s)", i, wm.name,
                     (unsigned long long)wm.m->k, (unsigned long long)wm.m->n,
-                    (unsigned long long)wm.k, (unsigned long long)wm.n);
+                    (unsigned long long)wm.k, (unsigned long long)wm.n, q4 ? "Q4" : "F16");
     }
     if (I % 128 != 0 || I == 0) return fail(QORA_ERR_UNSUPPORTED, "intermediate %llu not a multiple of 128", (unsigned long long)I);
     if (!L.input_norm_gamma || !L.post_attn_norm_gamma) return fail(QORA_ERR_INVALID, "layer %u norms missing", i);
@@ -938,6 +973,357 @@ qora_status check_step_error(qora_engine* e, qora_kv* kv) {
   return QORA_OK;
 }
 
+// ------------------------------------------------------------------ F16 weights: batched path
+// Every F16 forward pass runs M rows (f16_batch.cuh): one row per sequence in a batched
+// decode step, one row per prompt token in a prefill chunk.
+
+int f16_splits(int sms, int N, int K) {  // K slices so that a GEMM fills the SMs twice over
+  const int tiles = N / f16b::kTileN, chunks = K / f16b::kChunkK;
+  const int s = (2 * sms + tiles - 1) / tiles;
+  return std::max(1, std::min(s, chunks / 2));
+}
+
+template <bool KM, int MT>
+qora_status f16_gemm_mt(qora_engine* e, const f16b::GemmArgs& g) {
+  const size_t smem = f16b::gemm_smem_bytes(MT);
+  f16b::gemm_f16_kernel<KM, MT><<<dim3(g.N / f16b::kTileN, g.splits), f16b::kThreads, smem, e->stream>>>(g);
+  QCUDA(cudaGetLastError());
+  return QORA_OK;
+}
+
+template <bool KM>
+qora_status f16_gemm(qora_engine* e, const __half* w, long long ldw, int M, int K, int N, int splits, float* out) {
+  const f16b::GemmArgs g{w, ldw, e->f_xh, e->f_xl, M, K, N, splits, out};
+  if (M <= 8) return f16_gemm_mt<KM, 1>(e, g);
+  if (M <= 16) return f16_gemm_mt<KM, 2>(e, g);
+  if (M <= 32) return f16_gemm_mt<KM, 4>(e, g);
+  if (M <= 64) return f16_gemm_mt<KM, 8>(e, g);
+  return f16_gemm_mt<KM, 16>(e, g);
+}
+
+template <bool KM>
+qora_status f16_gemm_attrs() {
+  QCUDA(cudaFuncSetAttribute(f16b::gemm_f16_kernel<KM, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)f16b::gemm_smem_bytes(8)));
+  QCUDA(cudaFuncSetAttribute(f16b::gemm_f16_kernel<KM, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)f16b::gemm_smem_bytes(16)));
+  return QORA_OK;
+}
+
+qora_status f16_reduce(qora_engine* e, int splits, int M, int N, int mode, const float* res, float* y) {
+  const long long total = (long long)M * (mode == 2 ? N / 2 : N);
+  const int blocks = (int)std::min<long long>((total + 255) / 256, 8LL * e->sms);
+  f16b::reduce_kernel<<<blocks, 256, 0, e->stream>>>(e->f_part, splits, M, N, mode, res, y);
+  QCUDA(cudaGetLastError());
+  return QORA_OK;
+}
+
+qora_status f16_norm_split(qora_engine* e, const float* x, const float* gamma, int M, int K) {
+  f16b::norm_split_kernel<<<M, 256, 0, e->stream>>>(x, gamma, K, e->f_xh, e->f_xl, nullptr);
+  QCUDA(cudaGetLastError());
+  return QORA_OK;
+}
+
+// Upload the F16 weights (exact copies; q|k|v and gate|up joined along n) and size the
+// activation scratch for f16b::kMaxRows rows.
+qora_status f16_engine_init(qora_engine* e, const qora_weights_view* w) {
+  const qora_layer_view& L0 = w->layers[0];
+  e->format = w->format;
+  e->num_layers = w->num_layers;
+  e->vocab = w->vocab;
+  e->hidden = w->hidden;
+  e->inter = (uint32_t)L0.gate_proj.n;
+  e->nh = L0.num_heads;
+  e->nkv_total = L0.num_kv_heads;
+  e->nh_l = (int)e->nh;
+  e->nkv_l = (int)e->nkv_total;
+  e->kv0 = 0;
+  e->inter_l = (int)e->inter;
+  e->nkv = e->nkv_total;
+  e->rope_rows = (uint32_t)w->rope_rows;
+  e->sms = sm_count(e->device);
+  e->mk_ok = false;
+  e->mk_why = "F16 weights run the batched path";
+  QCUDA(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
+  const int H = (int)e->hidden, nq = (int)e->nh * kHeadDim, nkvw = (int)e->nkv * kHeadDim, I = (int)e->inter;
+  const int V = (int)e->vocab;
+  e->f_nqkv = nq + 2 * nkvw;
+  e->fl.resize(e->num_layers);
+  auto put_cols = [&](__half* dst, int ldd, int col0, const qora_matrix_view& m) -> qora_status {
+    // rows of m ([k][n]) into columns [col0, col0 + n) of dst ([k][ldd])
+    QCUDA(cudaMemcpy2D(dst + col0, (size_t)ldd * 2, m.data, (size_t)m.n * 2, (size_t)m.n * 2, m.k,
+                       cudaMemcpyHostToDevice));
+    return QORA_OK;
+  };
+  for (uint32_t i = 0; i < e->num_layers; ++i) {
+    const qora_layer_view& L = w->layers[i];
+    F16Layer& d = e->fl[i];
+    QCHECK(e->alloc(&d.wqkv, (size_t)H * e->f_nqkv));
+    QCHECK(put_cols(d.wqkv, e->f_nqkv, 0, L.q_proj));
+    QCHECK(put_cols(d.wqkv, e->f_nqkv, nq, L.k_proj));
+    QCHECK(put_cols(d.wqkv, e->f_nqkv, nq + nkvw, L.v_proj));
+    QCHECK(e->alloc(&d.wo, (size_t)nq * H));
+    QCHECK(upload(e, d.wo, L.o_proj.data, (size_t)nq * H * 2));
+    QCHECK(e->alloc(&d.wgu, (size_t)H * 2 * I));
+    QCHECK(put_cols(d.wgu, 2 * I, 0, L.gate_proj));
+    QCHECK(put_cols(d.wgu, 2 * I, I, L.up_proj));
+    QCHECK(e->alloc(&d.wdown, (size_t)I * H));
+    QCHECK(upload(e, d.wdown, L.down_proj.data, (size_t)I * H * 2));
+    std::vector<float> g1 = f16_to_f32(L.input_norm_gamma, H), g2 = f16_to_f32(L.post_attn_norm_gamma, H);
+    QCHECK(e->alloc(&d.g_in, H));
+    QCHECK(e->alloc(&d.g_post, H));
+    QCHECK(upload(e, d.g_in, g1.data(), (size_t)H * 4));
+    QCHECK(upload(e, d.g_post, g2.data(), (size_t)H * 4));
+    d.rope = w->no_rope_layers[i] ? 1 : 0;
+  }
+  QCHECK(e->alloc(&e->f_embed, (size_t)V * H));
+  QCHECK(upload(e, e->f_embed, w->embed.data, (size_t)V * H * 2));
+  std::vector<float> fg = f16_to_f32(w->final_norm_gamma, H);
+  QCHECK(e->alloc(&e->final_gamma, H));
+  QCHECK(upload(e, e->final_gamma, fg.data(), (size_t)H * 4));
+  const size_t rt = (size_t)w->rope_rows * kHalfDim;
+  QCHECK(e->alloc(&e->rope_cos, rt));
+  QCHECK(e->alloc(&e->rope_sin, rt));
+  QCHECK(upload(e, e->rope_cos, w->rope_cos, rt * 4));
+  QCHECK(upload(e, e->rope_sin, w->rope_sin, rt * 4));
+
+  e->f_split[0] = f16_splits(e->sms, e->f_nqkv, H);
+  e->f_split[1] = f16_splits(e->sms, H, nq);
+  e->f_split[2] = f16_splits(e->sms, 2 * I, H);
+  e->f_split[3] = f16_splits(e->sms, H, I);
+  const size_t R = f16b::kMaxRows;
+  size_t part = 0;
+  const int ns[4] = {e->f_nqkv, H, 2 * I, H};
+  for (int j = 0; j < 4; ++j) part = std::max(part, (size_t)e->f_split[j] * R * ns[j]);
+  const size_t kmax = (size_t)std::max(std::max(H, nq), I);
+  QCHECK(e->alloc(&e->f_part, part));
+  QCHECK(e->alloc(&e->f_x, R * H));
+  QCHECK(e->alloc(&e->f_qkv, R * e->f_nqkv));
+  QCHECK(e->alloc(&e->f_attn, R * nq));
+  QCHECK(e->alloc(&e->f_h, R * I));
+  QCHECK(e->alloc(&e->f_logits, R * V));
+  QCHECK(e->alloc(&e->f_xh, R * kmax));
+  QCHECK(e->alloc(&e->f_xl, R * kmax));
+  e->logits = e->f_logits;
+  QCHECK(f16_gemm_attrs<false>());
+  QCHECK(f16_gemm_attrs<true>());
+  QCUDA(cudaDeviceSynchronize());
+  return QORA_OK;
+}
+
+// Launch count of f16_forward (reported as the engine's launches per step).
+int f16_launches(const qora_engine* e, bool lm) {
+  // embedding; per layer 4 x (norm/split, GEMM, reduce) + RoPE/KV + attention; final
+  // norm/split, lm_head GEMM, argmax
+  return 1 + 14 * (int)e->num_layers + (lm ? 3 : 0);
+}
+
+// The layer stack over the M rows of kv's row table, then (rows [lm0, M) only) the final
+// RMSNorm, the tied lm_head into f_logits rows [0, M - lm0) and the greedy argmax.
+// Mirrors forward_decode_raw / raw_prefill (src/gemv.rs:872-1019, :1027-1190) per row.
+qora_status f16_forward(qora_engine* e, qora_kv* kv, int M, int lm0) {
+  const int H = (int)e->hidden, nq = (int)e->nh * kHeadDim, nkvw = (int)e->nkv * kHeadDim, I = (int)e->inter;
+  const int V = (int)e->vocab, NQKV = e->f_nqkv;
+  const f16b::RowInfo ri = f16b::row_info(kv->rows);
+  cudaStream_t s = e->stream;
+  f16b::embed_rows_kernel<<<M, 256, 0, s>>>(e->f_embed, H, V, ri, e->f_x);
+  QCUDA(cudaGetLastError());
+  const long long hs = (long long)kv->max_seq * kHeadDim, ss = (long long)kv->seq_stride();
+  for (uint32_t li = 0; li < e->num_layers; ++li) {
+    const F16Layer& d = e->fl[li];
+    float* kc = kv->k + li * kv->layer_stride();
+    float* vc = kv->v + li * kv->layer_stride();
+    // attention block
+    QCHECK(f16_norm_split(e, e->f_x, d.g_in, M, H));
+    QCHECK(f16_gemm<false>(e, d.wqkv, NQKV, M, H, NQKV, e->f_split[0], e->f_part));
+    QCHECK(f16_reduce(e, e->f_split[0], M, NQKV, 0, nullptr, e->f_qkv));
+    f16b::rope_kv_kernel<<<M, 256, 0, s>>>(e->f_qkv, nq, nkvw, d.rope, e->rope_cos, e->rope_sin, ri, kc, vc, ss, hs);
+    QCUDA(cudaGetLastError());
+    f16b::attention_rows_kernel<<<dim3(e->nkv, M), f16b::kAttnRowThreads, 0, s>>>(e->f_qkv, nq, nkvw, kGrp, ri, kc,
+                                                                                  vc, ss, hs, e->f_attn);
+    QCUDA(cudaGetLastError());
+    QCHECK(f16_norm_split(e, e->f_attn, nullptr, M, nq));
+    QCHECK(f16_gemm<false>(e, d.wo, H, M, nq, H, e->f_split[1], e->f_part));
+    QCHECK(f16_reduce(e, e->f_split[1], M, H, 1, e->f_x, e->f_x));
+    // MLP block
+    QCHECK(f16_norm_split(e, e->f_x, d.g_post, M, H));
+    QCHECK(f16_gemm<false>(e, d.wgu, 2 * I, M, H, 2 * I, e->f_split[2], e->f_part));
+    QCHECK(f16_reduce(e, e->f_split[2], M, 2 * I, 2, nullptr, e->f_h));
+    QCHECK(f16_norm_split(e, e->f_h, nullptr, M, I));
+    QCHECK(f16_gemm<false>(e, d.wdown, H, M, I, H, e->f_split[3], e->f_part));
+    QCHECK(f16_reduce(e, e->f_split[3], M, H, 1, e->f_x, e->f_x));
+  }
+  if (lm0 < M) {
+    const int ml = M - lm0;
+    QCHECK(f16_norm_split(e, e->f_x + (size_t)lm0 * H, e->final_gamma, ml, H));
+    QCHECK(f16_gemm<true>(e, e->f_embed, H, ml, H, V, 1, e->f_logits));
+    f16b::argmax_rows_kernel<<<ml, 256, 0, s>>>(e->f_logits, V, kv->f_argmax);
+    QCUDA(cudaGetLastError());
+  }
+  return QORA_OK;
+}
+
+// The batched decode step of all kv->batch rows as one CUDA graph (captured once per
+// cache; the row table it reads stays at a fixed address).
+qora_status f16_ensure_graph(qora_engine* e, qora_kv* kv) {
+  if (kv->f_graph) return QORA_OK;
+  cudaGraph_t g = nullptr;
+  QCUDA(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+  const qora_status st = f16_forward(e, kv, (int)kv->batch, 0);
+  const cudaError_t ce = cudaStreamEndCapture(e->stream, &g);
+  if (st != QORA_OK) {
+    if (g) cudaGraphDestroy(g);
+    return st;
+  }
+  if (ce != cudaSuccess) return fail(QORA_ERR_CUDA, "graph capture: %s", cudaGetErrorString(ce));
+  const cudaError_t ie = cudaGraphInstantiate(&kv->f_graph, g, 0);
+  cudaGraphDestroy(g);
+  if (ie != cudaSuccess) return fail(QORA_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(ie));
+  return QORA_OK;
+}
+
+// Host lengths of every sequence (uniform over layers), as positions of the next row.
+qora_status f16_seq_lens(qora_kv* kv, std::vector<uint32_t>& lens) {
+  const uint32_t L = (uint32_t)(kv->len.size() / kv->batch);
+  lens.resize(kv->batch);
+  for (uint32_t b = 0; b < kv->batch; ++b) {
+    lens[b] = kv->lenof(b, 0);
+    for (uint32_t l = 1; l < L; ++l)
+      if (kv->lenof(b, l) != lens[b])
+        return fail(QORA_ERR_INVALID, "sequence %u: KV layers have different lengths", b);
+  }
+  return QORA_OK;
+}
+
+// Row table of a decode step: row b = sequence b at its current length with tokens[b].
+qora_status f16_stage_decode_rows(qora_engine* e, qora_kv* kv, const uint32_t* tokens,
+                                  const std::vector<uint32_t>& lens) {
+  int* h = kv->rows_host;
+  for (uint32_t b = 0; b < kv->batch; ++b) {
+    h[b] = (int)b;
+    h[f16b::kMaxRows + b] = (int)lens[b];
+    h[2 * f16b::kMaxRows + b] = (int)tokens[b];
+  }
+  h[3 * f16b::kMaxRows] = 0;      // greedy step
+  h[3 * f16b::kMaxRows + 1] = 0;  // error
+  QCUDA(cudaMemcpyAsync(kv->rows, h, f16b::kRowInts * sizeof(int), cudaMemcpyHostToDevice, e->stream));
+  return QORA_OK;
+}
+
+qora_status f16_check_error(qora_engine* e, qora_kv* kv) {
+  int err = 0;
+  QCUDA(cudaMemcpyAsync(kv->rows_host + 3 * f16b::kMaxRows + 1, kv->rows + 3 * f16b::kMaxRows + 1, sizeof(int),
+                        cudaMemcpyDeviceToHost, e->stream));
+  QCUDA(cudaStreamSynchronize(e->stream));
+  err = kv->rows_host[3 * f16b::kMaxRows + 1];
+  if (err) return fail(QORA_ERR_RANGE, "device rejected a token id");
+  return QORA_OK;
+}
+
+qora_status f16_decode_step(qora_engine* e, qora_kv* kv, const uint32_t* tokens, float* logits, uint32_t* argmax) {
+  for (uint32_t b = 0; b < kv->batch; ++b)
+    if (tokens[b] >= e->vocab) return fail(QORA_ERR_RANGE, "token %u (row %u) >= vocab %u", tokens[b], b, e->vocab);
+  std::vector<uint32_t> lens;
+  QCHECK(f16_seq_lens(kv, lens));
+  for (uint32_t b = 0; b < kv->batch; ++b)
+    if (lens[b] >= kv->max_seq) return fail(QORA_ERR_RANGE, "sequence %u: KV cache full (%u positions)", b, kv->max_seq);
+  QCUDA(cudaSetDevice(e->device));
+  QCHECK(f16_ensure_graph(e, kv));
+  QCHECK(f16_stage_decode_rows(e, kv, tokens, lens));
+  QCUDA(cudaGraphLaunch(kv->f_graph, e->stream));
+  if (logits)
+    QCUDA(cudaMemcpyAsync(logits, e->f_logits, (size_t)kv->batch * e->vocab * 4, cudaMemcpyDeviceToHost, e->stream));
+  if (argmax) QCUDA(cudaMemcpyAsync(argmax, kv->f_argmax, kv->batch * 4, cudaMemcpyDeviceToHost, e->stream));
+  QCHECK(f16_check_error(e, kv));
+  for (uint32_t b = 0; b < kv->batch; ++b)
+    for (uint32_t l = 0; l < e->num_layers; ++l) kv->lenof(b, l) = lens[b] + 1;
+  return QORA_OK;
+}
+
+// Greedy generation for every sequence of the cache: n_tokens batched steps on the
+// device, each feeding its argmax back (f16b::advance_rows_kernel). out: [n_tokens][batch].
+qora_status f16_generate(qora_engine* e, qora_kv* kv, const uint32_t* first, uint32_t n_tokens, uint32_t* out,
+                         float* device_ms) {
+  for (uint32_t b = 0; b < kv->batch; ++b)
+    if (first[b] >= e->vocab) return fail(QORA_ERR_RANGE, "token %u (row %u) >= vocab %u", first[b], b, e->vocab);
+  std::vector<uint32_t> lens;
+  QCHECK(f16_seq_lens(kv, lens));
+  for (uint32_t b = 0; b < kv->batch; ++b)
+    if ((uint64_t)lens[b] + n_tokens > kv->max_seq)
+      return fail(QORA_ERR_RANGE, "sequence %u: %u tokens after %u positions exceed max_seq %u", b, n_tokens,
+                  lens[b], kv->max_seq);
+  if (n_tokens == 0) return QORA_OK;
+  QCUDA(cudaSetDevice(e->device));
+  QCHECK(f16_ensure_graph(e, kv));
+  QCHECK(f16_stage_decode_rows(e, kv, first, lens));
+  const f16b::RowInfo ri = f16b::row_info(kv->rows);
+  cudaEvent_t a = nullptr, b = nullptr;
+  if (device_ms) {
+    QCUDA(cudaEventCreate(&a));
+    QCUDA(cudaEventCreate(&b));
+    QCUDA(cudaEventRecord(a, e->stream));
+  }
+  qora_status st = QORA_OK;
+  for (uint32_t i = 0; i < n_tokens && st == QORA_OK; ++i) {
+    cudaError_t ce = cudaGraphLaunch(kv->f_graph, e->stream);
+    if (ce == cudaSuccess) {
+      f16b::advance_rows_kernel<<<1, f16b::kMaxRows, 0, e->stream>>>((int)kv->batch, ri, kv->f_argmax, kv->ring,
+                                                                   (int)kv->max_seq);
+      ce = cudaGetLastError();
+    }
+    if (ce != cudaSuccess) st = fail(QORA_ERR_CUDA, "greedy step %u: %s", i, cudaGetErrorString(ce));
+  }
+  if (device_ms) {
+    cudaEventRecord(b, e->stream);
+    cudaError_t ce = cudaEventSynchronize(b);
+    float ms = 0.0f;
+    if (ce == cudaSuccess) ce = cudaEventElapsedTime(&ms, a, b);
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    if (st == QORA_OK && ce != cudaSuccess) st = fail(QORA_ERR_CUDA, "event timing: %s", cudaGetErrorString(ce));
+    *device_ms = ms;
+  }
+  QCHECK(st);
+  QCUDA(cudaMemcpyAsync(out, kv->ring, (size_t)n_tokens * kv->batch * 4, cudaMemcpyDeviceToHost, e->stream));
+  QCHECK(f16_check_error(e, kv));
+  for (uint32_t r = 0; r < kv->batch; ++r)
+    for (uint32_t l = 0; l < e->num_layers; ++l) kv->lenof(r, l) = lens[r] + n_tokens;
+  return QORA_OK;
+}
+
+__global__ void f16_prompt_rows_kernel(int* rows, const uint32_t* ids, int n, int seq, int pos0) {
+  const f16b::RowInfo ri = f16b::row_info(rows);
+  for (int m = threadIdx.x; m < n; m += blockDim.x) {
+    ri.seq[m] = seq;
+    ri.pos[m] = pos0 + m;
+    ri.token[m] = (int)ids[m];
+  }
+  if (threadIdx.x == 0) *ri.error = 0;
+}
+
+// Prompt pass of one sequence in chunks of up to f16b::kMaxRows rows.
+qora_status f16_prefill(qora_engine* e, qora_kv* kv, const uint32_t* ids, uint32_t n, uint32_t seq, float* logits,
+                        uint32_t* argmax) {
+  std::vector<uint32_t> lens;
+  QCHECK(f16_seq_lens(kv, lens));
+  const uint32_t len = lens[seq];
+  if ((uint64_t)len + n > kv->max_seq)
+    return fail(QORA_ERR_RANGE, "prompt of %u after %u positions exceeds max_seq %u", n, len, kv->max_seq);
+  QCUDA(cudaSetDevice(e->device));
+  QCUDA(cudaMemcpyAsync(kv->ids, ids, (size_t)n * 4, cudaMemcpyHostToDevice, e->stream));
+  for (uint32_t c0 = 0; c0 < n; c0 += f16b::kMaxRows) {
+    const int c = (int)std::min<uint32_t>(f16b::kMaxRows, n - c0);
+    f16_prompt_rows_kernel<<<1, f16b::kMaxRows, 0, e->stream>>>(kv->rows, kv->ids + c0, c, (int)seq, (int)(len + c0));
+    QCUDA(cudaGetLastError());
+    QCHECK(f16_forward(e, kv, c, c0 + c == n ? c - 1 : c));
+  }
+  if (logits) QCUDA(cudaMemcpyAsync(logits, e->f_logits, (size_t)e->vocab * 4, cudaMemcpyDeviceToHost, e->stream));
+  if (argmax) QCUDA(cudaMemcpyAsync(argmax, kv->f_argmax, 4, cudaMemcpyDeviceToHost, e->stream));
+  QCHECK(f16_check_error(e, kv));
+  for (uint32_t l = 0; l < e->num_layers; ++l) kv->lenof(seq, l) = len + n;
+  return QORA_OK;
+}
+
 struct EntryScratch {
   float* partials = nullptr;
   size_t partial_floats = 0;
@@ -1126,6 +1512,8 @@ qora_status qora_engine_create(const qora_weights_view* weights, const qora_engi
   if (rank < 0 || rank >= tp) return fail(QORA_ERR_INVALID, "tp_rank %d of %d", rank, tp);
   if (tp > 1 && opts && (opts->flags & QORA_FLAG_PER_OP_KERNELS))
     return fail(QORA_ERR_UNSUPPORTED, "tensor-parallel engines run the persistent kernel only");
+  if (tp > 1 && weights->format == QORA_FORMAT_F16)
+    return fail(QORA_ERR_UNSUPPORTED, "tensor parallelism with F16 weights is not in this build");
   int ndev = 0;
   QCUDA(cudaGetDeviceCount(&ndev));
   const int dev = opts ? opts->first_device : 0;
@@ -1136,7 +1524,10 @@ qora_status qora_engine_create(const qora_weights_view* weights, const qora_engi
   e->tp = tp;
   e->rank = rank;
   e->use_mega = !(opts && (opts->flags & QORA_FLAG_PER_OP_KERNELS));
-  QCHECK(engine_init(e.get(), weights));
+  if (weights->format == QORA_FORMAT_F16)
+    QCHECK(f16_engine_init(e.get(), weights));
+  else
+    QCHECK(engine_init(e.get(), weights));
   if (tp > 1 && !e->mk_ok)
     return fail(QORA_ERR_UNSUPPORTED, "tensor-parallel shard has no persistent kernel: %s", e->mk_why.c_str());
   *out = e.release();
@@ -1263,24 +1654,42 @@ qora_status qora_engine_info(const qora_engine* e, uint32_t* num_layers, uint32_
 qora_status qora_kv_create(qora_engine* e, uint32_t max_seq, uint32_t batch, qora_kv** out) {
   if (!e || !out) return fail(QORA_ERR_INVALID, "NULL argument");
   *out = nullptr;
-  if (batch != 1) return fail(QORA_ERR_UNSUPPORTED, "batch=%u: only batch 1 in this build", batch);
+  const bool f16 = e->format == QORA_FORMAT_F16;
+  if (batch == 0) return fail(QORA_ERR_INVALID, "batch must be > 0");
+  if (!f16 && batch != 1) return fail(QORA_ERR_UNSUPPORTED, "batch=%u: Q4 engines decode batch 1", batch);
+  if (batch > (uint32_t)f16b::kMaxRows)
+    return fail(QORA_ERR_UNSUPPORTED, "batch=%u: at most %d sequences", batch, f16b::kMaxRows);
   if (max_seq == 0) return fail(QORA_ERR_INVALID, "max_seq must be > 0");
   bool any_rope = false;
   for (auto& L : e->layers) any_rope |= (L.rope != 0);
+  for (auto& L : e->fl) any_rope |= (L.rope != 0);
   if (any_rope && max_seq > e->rope_rows)
     return fail(QORA_ERR_RANGE, "max_seq %u exceeds the %u RoPE table rows", max_seq, e->rope_rows);
   QCUDA(cudaSetDevice(e->device));
   std::unique_ptr<qora_kv> kv(new qora_kv());
   kv->e = e;
   kv->max_seq = max_seq;
-  kv->len.assign(e->num_layers, 0);
+  kv->batch = batch;
+  kv->len.assign((size_t)batch * e->num_layers, 0);
   const size_t per = kv->layer_stride() * e->num_layers;
   QCHECK(kv->alloc(&kv->k, per));
   QCHECK(kv->alloc(&kv->v, per));
   QCHECK(kv->alloc(&kv->st, 1));
-  QCHECK(kv->alloc(&kv->ring, max_seq));
+  QCHECK(kv->alloc(&kv->ring, (size_t)max_seq * batch));
   QCHECK(kv->alloc(&kv->ids, max_seq));
   QCUDA(cudaMallocHost(&kv->st_host, sizeof(StepState)));
+  if (f16) {
+    QCHECK(kv->alloc(&kv->rows, f16b::kRowInts));
+    QCHECK(kv->alloc(&kv->f_argmax, f16b::kMaxRows));
+    QCUDA(cudaMemset(kv->rows, 0, f16b::kRowInts * sizeof(int)));
+    QCUDA(cudaMallocHost(&kv->rows_host, f16b::kRowInts * sizeof(int)));
+    std::memset(kv->rows_host, 0, f16b::kRowInts * sizeof(int));
+    QCUDA(cudaMemset(kv->st, 0, sizeof(StepState)));
+    QCUDA(cudaDeviceSynchronize());
+    e->kvs.push_back(kv.get());
+    *out = kv.release();
+    return QORA_OK;
+  }
   kv->attn_nc = std::max<int>(std::max(1, e->sms / (int)e->nkv), (int)((max_seq + kAttnMaxChunk - 1) / kAttnMaxChunk));
   QCHECK(kv->alloc(&kv->attn_o, (size_t)e->nkv * kv->attn_nc * kGrp * kHeadDim));
   QCHECK(kv->alloc(&kv->attn_ml, (size_t)e->nkv * kv->attn_nc * kGrp * 2));
@@ -1297,15 +1706,16 @@ void qora_kv_destroy(qora_kv* kv) { delete kv; }
 
 qora_status qora_kv_length(const qora_kv* kv, uint32_t seq_idx, uint32_t* len) {
   if (!kv || !len) return fail(QORA_ERR_INVALID, "NULL argument");
-  if (seq_idx != 0) return fail(QORA_ERR_RANGE, "seq_idx %u", seq_idx);
-  *len = kv->len[0];
+  if (seq_idx >= kv->batch) return fail(QORA_ERR_RANGE, "seq_idx %u of %u sequences", seq_idx, kv->batch);
+  *len = kv->len[(size_t)seq_idx * (kv->len.size() / kv->batch)];
   return QORA_OK;
 }
 
 qora_status qora_kv_reset(qora_kv* kv, uint32_t seq_idx) {
   if (!kv) return fail(QORA_ERR_INVALID, "NULL kv");
-  if (seq_idx != 0) return fail(QORA_ERR_RANGE, "seq_idx %u", seq_idx);
-  std::fill(kv->len.begin(), kv->len.end(), 0u);
+  if (seq_idx >= kv->batch) return fail(QORA_ERR_RANGE, "seq_idx %u of %u sequences", seq_idx, kv->batch);
+  const size_t L = kv->len.size() / kv->batch;
+  std::fill(kv->len.begin() + seq_idx * L, kv->len.begin() + (seq_idx + 1) * L, 0u);
   return QORA_OK;
 }
 
@@ -1313,7 +1723,7 @@ qora_status qora_kv_import(qora_kv* kv, uint32_t layer, const float* k, const fl
                            uint32_t seq_len, uint32_t seq_idx) {
   if (!kv || (!k && seq_len) || (!v && seq_len)) return fail(QORA_ERR_INVALID, "NULL argument");
   if (!kv->e) return fail(QORA_ERR_INVALID, "the KV cache's engine was destroyed");
-  if (seq_idx != 0) return fail(QORA_ERR_RANGE, "seq_idx %u", seq_idx);
+  if (seq_idx >= kv->batch) return fail(QORA_ERR_RANGE, "seq_idx %u of %u sequences", seq_idx, kv->batch);
   if (layer >= kv->e->num_layers) return fail(QORA_ERR_RANGE, "layer %u", layer);
   if (seq_len > kv->max_seq) return fail(QORA_ERR_RANGE, "seq_len %u > max_seq %u", seq_len, kv->max_seq);
   QCUDA(cudaSetDevice(kv->e->device));
@@ -1321,12 +1731,12 @@ qora_status qora_kv_import(qora_kv* kv, uint32_t layer, const float* k, const fl
   // (a tensor-parallel rank keeps heads kv0 .. kv0 + nkv - 1)
   const size_t row = (size_t)kv->e->nkv_total * kHeadDim * sizeof(float), hb = kHeadDim * sizeof(float);
   for (uint32_t j = 0; seq_len && j < kv->e->nkv; ++j) {
-    const size_t off = layer * kv->layer_stride() + (size_t)j * kv->max_seq * kHeadDim;
+    const size_t off = layer * kv->layer_stride() + seq_idx * kv->seq_stride() + (size_t)j * kv->max_seq * kHeadDim;
     const size_t src = (size_t)(kv->e->kv0 + j) * kHeadDim;
     QCUDA(cudaMemcpy2D(kv->k + off, hb, k + src, row, hb, seq_len, cudaMemcpyHostToDevice));
     QCUDA(cudaMemcpy2D(kv->v + off, hb, v + src, row, hb, seq_len, cudaMemcpyHostToDevice));
   }
-  kv->len[layer] = seq_len;
+  kv->lenof(seq_idx, layer) = seq_len;
   return QORA_OK;
 }
 
@@ -1334,14 +1744,15 @@ qora_status qora_kv_export(const qora_kv* kv, uint32_t layer, float* k, float* v
                            uint32_t seq_idx) {
   if (!kv || !k || !v) return fail(QORA_ERR_INVALID, "NULL argument");
   if (!kv->e) return fail(QORA_ERR_INVALID, "the KV cache's engine was destroyed");
-  if (seq_idx != 0) return fail(QORA_ERR_RANGE, "seq_idx %u", seq_idx);
+  if (seq_idx >= kv->batch) return fail(QORA_ERR_RANGE, "seq_idx %u of %u sequences", seq_idx, kv->batch);
   if (layer >= kv->e->num_layers) return fail(QORA_ERR_RANGE, "layer %u", layer);
-  if (seq_len > kv->len[layer]) return fail(QORA_ERR_RANGE, "seq_len %u > length %u", seq_len, kv->len[layer]);
+  const uint32_t have = kv->len[(size_t)seq_idx * (kv->len.size() / kv->batch) + layer];
+  if (seq_len > have) return fail(QORA_ERR_RANGE, "seq_len %u > length %u", seq_len, have);
   QCUDA(cudaSetDevice(kv->e->device));
   QCUDA(cudaStreamSynchronize(kv->e->stream));
   const size_t row = (size_t)kv->e->nkv_total * kHeadDim * sizeof(float), hb = kHeadDim * sizeof(float);
   for (uint32_t j = 0; seq_len && j < kv->e->nkv; ++j) {  // a rank fills only its own heads' columns
-    const size_t off = layer * kv->layer_stride() + (size_t)j * kv->max_seq * kHeadDim;
+    const size_t off = layer * kv->layer_stride() + seq_idx * kv->seq_stride() + (size_t)j * kv->max_seq * kHeadDim;
     const size_t dst = (size_t)(kv->e->kv0 + j) * kHeadDim;
     QCUDA(cudaMemcpy2D(k + dst, row, kv->k + off, hb, hb, seq_len, cudaMemcpyDeviceToHost));
     QCUDA(cudaMemcpy2D(v + dst, row, kv->v + off, hb, hb, seq_len, cudaMemcpyDeviceToHost));
@@ -1352,6 +1763,7 @@ qora_status qora_kv_export(const qora_kv* kv, uint32_t layer, float* k, float* v
 qora_status qora_decode_step(qora_engine* e, qora_kv* kv, const uint32_t* tokens,
                              float* logits_or_null, uint32_t* argmax_out) {
   if (!e || !kv || !tokens || kv->e != e) return fail(QORA_ERR_INVALID, "bad engine/kv/tokens");
+  if (e->format == QORA_FORMAT_F16) return f16_decode_step(e, kv, tokens, logits_or_null, argmax_out);
   if (tokens[0] >= e->vocab) return fail(QORA_ERR_RANGE, "token %u >= vocab %u", tokens[0], e->vocab);
   uint32_t len = 0;
   QCHECK(check_uniform_len(kv, &len));
@@ -1374,10 +1786,11 @@ qora_status qora_decode_step(qora_engine* e, qora_kv* kv, const uint32_t* tokens
 qora_status qora_prefill(qora_engine* e, qora_kv* kv, const uint32_t* ids, uint32_t n,
                          uint32_t seq_idx, float* logits_or_null, uint32_t* argmax_out) {
   if (!e || !kv || kv->e != e || (!ids && n)) return fail(QORA_ERR_INVALID, "bad arguments");
-  if (seq_idx != 0) return fail(QORA_ERR_RANGE, "seq_idx %u", seq_idx);
+  if (seq_idx >= kv->batch) return fail(QORA_ERR_RANGE, "seq_idx %u of %u sequences", seq_idx, kv->batch);
   if (n == 0) return fail(QORA_ERR_INVALID, "empty prompt");
   for (uint32_t i = 0; i < n; ++i)
     if (ids[i] >= e->vocab) return fail(QORA_ERR_RANGE, "token %u at %u >= vocab %u", ids[i], i, e->vocab);
+  if (e->format == QORA_FORMAT_F16) return f16_prefill(e, kv, ids, n, seq_idx, logits_or_null, argmax_out);
   uint32_t len = 0;
   QCHECK(check_uniform_len(kv, &len));
   if ((uint64_t)len + n > kv->max_seq)
@@ -1405,6 +1818,8 @@ qora_status qora_generate_greedy(qora_engine* e, qora_kv* kv, uint32_t first_tok
                                  uint32_t n_tokens, uint32_t* out_tokens) {
   if (!e || !kv || kv->e != e || (!out_tokens && n_tokens)) return fail(QORA_ERR_INVALID, "bad arguments");
   if (first_token >= e->vocab) return fail(QORA_ERR_RANGE, "token %u >= vocab", first_token);
+  if (kv->batch != 1) return fail(QORA_ERR_INVALID, "batched cache: use qora_generate_greedy_batch");
+  if (e->format == QORA_FORMAT_F16) return f16_generate(e, kv, &first_token, n_tokens, out_tokens, nullptr);
   uint32_t len = 0;
   QCHECK(check_uniform_len(kv, &len));
   if ((uint64_t)len + n_tokens > kv->max_seq)
@@ -1422,6 +1837,7 @@ qora_status qora_generate_greedy(qora_engine* e, qora_kv* kv, uint32_t first_tok
 
 qora_status qora_layer_step(qora_engine* e, qora_kv* kv, uint32_t layer, float* x_inout) {
   if (!e || !kv || kv->e != e || !x_inout) return fail(QORA_ERR_INVALID, "bad arguments");
+  if (e->format != QORA_FORMAT_Q4) return fail(QORA_ERR_UNSUPPORTED, "qora_layer_step runs Q4 engines");
   if (layer >= e->num_layers) return fail(QORA_ERR_RANGE, "layer %u", layer);
   const uint32_t len = kv->len[layer];
   if (len >= kv->max_seq) return fail(QORA_ERR_RANGE, "KV cache full");
@@ -1440,6 +1856,8 @@ qora_status qora_generate_greedy_timed(qora_engine* e, qora_kv* kv, uint32_t fir
   if (!e || !kv || kv->e != e || (!out_tokens && n_tokens) || !device_ms)
     return fail(QORA_ERR_INVALID, "bad arguments");
   if (first_token >= e->vocab) return fail(QORA_ERR_RANGE, "token %u >= vocab", first_token);
+  if (kv->batch != 1) return fail(QORA_ERR_INVALID, "batched cache: use qora_generate_greedy_batch");
+  if (e->format == QORA_FORMAT_F16) return f16_generate(e, kv, &first_token, n_tokens, out_tokens, device_ms);
   uint32_t len = 0;
   QCHECK(check_uniform_len(kv, &len));
   if ((uint64_t)len + n_tokens > kv->max_seq)
@@ -1478,6 +1896,7 @@ qora_status qora_engine_time_kernel(qora_engine* e, qora_kv* kv, int kernel, uin
                                     float* ms_per_launch, uint64_t* bytes_per_launch,
                                     uint32_t* launches) {
   if (!e || !kv || kv->e != e || !ms_per_launch || reps == 0) return fail(QORA_ERR_INVALID, "bad arguments");
+  if (e->format != QORA_FORMAT_Q4) return fail(QORA_ERR_UNSUPPORTED, "kernel timing runs Q4 engines");
   if (kernel < QORA_KERNEL_QKV || kernel > QORA_KERNEL_LM_HEAD) return fail(QORA_ERR_INVALID, "kernel %d", kernel);
   uint32_t len = 0;
   QCHECK(check_uniform_len(kv, &len));
@@ -1585,8 +2004,20 @@ qora_status qora_engine_get_trace(qora_engine* e, uint64_t* out, size_t cap, siz
 
 qora_status qora_engine_launches_per_step(const qora_engine* e, uint32_t* launches) {
   if (!e || !launches) return fail(QORA_ERR_INVALID, "NULL argument");
-  *launches = (e->mk_ok && e->use_mega) ? 1u : 1 + 5 * e->num_layers + 2;
+  if (e->format == QORA_FORMAT_F16)
+    *launches = (uint32_t)f16_launches(e, true);
+  else
+    *launches = (e->mk_ok && e->use_mega) ? 1u : 1 + 5 * e->num_layers + 2;
   return QORA_OK;
+}
+
+qora_status qora_generate_greedy_batch(qora_engine* e, qora_kv* kv, const uint32_t* first_tokens,
+                                       uint32_t n_tokens, uint32_t* out_tokens, float* device_ms) {
+  if (!e || !kv || kv->e != e || !first_tokens || (!out_tokens && n_tokens))
+    return fail(QORA_ERR_INVALID, "bad arguments");
+  if (e->format == QORA_FORMAT_F16) return f16_generate(e, kv, first_tokens, n_tokens, out_tokens, device_ms);
+  if (device_ms) return qora_generate_greedy_timed(e, kv, first_tokens[0], n_tokens, out_tokens, device_ms);
+  return qora_generate_greedy(e, kv, first_tokens[0], n_tokens, out_tokens);
 }
 
 // ------------------------------------------------------------------ kernel-level entries

@@ -50,6 +50,7 @@ SIGNATURES = {
     "qora_prefill": (C.c_int, [_vp, _vp, _vp, _u32, _u32, _vp, _vp]),
     "qora_decode_step": (C.c_int, [_vp, _vp, _vp, _vp, _vp]),
     "qora_generate_greedy": (C.c_int, [_vp, _vp, _u32, _u32, _vp]),
+    "qora_generate_greedy_batch": (C.c_int, [_vp, _vp, _vp, _u32, _vp, _P(C.c_float)]),
     "qora_layer_step": (C.c_int, [_vp, _vp, _u32, _vp]),
     "qora_generate_greedy_timed": (C.c_int, [_vp, _vp, _u32, _u32, _vp, _P(C.c_float)]),
     "qora_engine_time_kernel": (C.c_int, [_vp, _vp, C.c_int, _u32, _P(C.c_float), _P(_u64),
@@ -161,8 +162,9 @@ class DecodeWeights:
         self.close()
 
     # ---- KV
-    def new_kv(self, max_seq: int) -> "KVCache":
-        return KVCache(self, max_seq)
+    def new_kv(self, max_seq: int, batch: int = 1) -> "KVCache":
+        """A cache for `batch` independent sequences (batch > 1: F16 engines)."""
+        return KVCache(self, max_seq, batch)
 
     # ---- steps
     def decode_step(self, kv: "KVCache", token: int, want_logits: bool = False):
@@ -173,13 +175,36 @@ class DecodeWeights:
                                      _ptr(logits) if logits is not None else None, _ptr(am)))
         return (int(am[0]), logits) if want_logits else int(am[0])
 
-    def prefill(self, kv: "KVCache", ids, want_logits: bool = True):
+    def decode_batch(self, kv: "KVCache", tokens, want_logits: bool = False):
+        """One decode step of every sequence of `kv`: (argmax [batch], logits [batch][vocab]
+        or None)."""
+        tok = np.ascontiguousarray(tokens, dtype=np.uint32)
+        if tok.size != kv.batch:
+            raise ValueError(f"{tok.size} tokens for {kv.batch} sequences")
+        am = np.zeros(kv.batch, np.uint32)
+        logits = np.empty((kv.batch, self.vocab), np.float32) if want_logits else None
+        check(lib().qora_decode_step(self.h, kv.h, _ptr(tok),
+                                     _ptr(logits) if logits is not None else None, _ptr(am)))
+        return am, logits
+
+    def prefill(self, kv: "KVCache", ids, want_logits: bool = True, seq: int = 0):
         ids = np.ascontiguousarray(ids, dtype=np.uint32)
         am = np.zeros(1, np.uint32)
         logits = np.empty(self.vocab, np.float32) if want_logits else None
-        check(lib().qora_prefill(self.h, kv.h, _ptr(ids), ids.size, 0,
+        check(lib().qora_prefill(self.h, kv.h, _ptr(ids), ids.size, int(seq),
                                  _ptr(logits) if logits is not None else None, _ptr(am)))
         return int(am[0]), logits
+
+    def generate_greedy_batch(self, kv: "KVCache", first_tokens, n: int, timed: bool = False):
+        """n greedy tokens for every sequence: out [n][batch] (and device ms if timed)."""
+        first = np.ascontiguousarray(first_tokens, dtype=np.uint32)
+        if first.size != kv.batch:
+            raise ValueError(f"{first.size} tokens for {kv.batch} sequences")
+        out = np.zeros((n, kv.batch), np.uint32)
+        ms = C.c_float()
+        check(lib().qora_generate_greedy_batch(self.h, kv.h, _ptr(first), int(n), _ptr(out),
+                                               C.byref(ms) if timed else None))
+        return (out, ms.value) if timed else out
 
     def generate_greedy(self, kv: "KVCache", first_token: int, n: int) -> np.ndarray:
         out = np.zeros(n, np.uint32)
@@ -228,10 +253,10 @@ class DecodeWeights:
 class KVCache:
     """Device KV cache, f32 token-major [seq][kv_heads][128] per layer (RawKvCache)."""
 
-    def __init__(self, w: DecodeWeights, max_seq: int):
+    def __init__(self, w: DecodeWeights, max_seq: int, batch: int = 1):
         h = C.c_void_p()
-        check(lib().qora_kv_create(w.h, int(max_seq), 1, C.byref(h)))
-        self.h, self.w, self.max_seq = h, w, max_seq
+        check(lib().qora_kv_create(w.h, int(max_seq), int(batch), C.byref(h)))
+        self.h, self.w, self.max_seq, self.batch = h, w, max_seq, batch
 
     def close(self):
         if getattr(self, "h", None):
@@ -245,22 +270,25 @@ class KVCache:
             pass
 
     def __len__(self):
+        return self.length(0)
+
+    def length(self, seq: int = 0) -> int:
         n = _u32()
-        check(lib().qora_kv_length(self.h, 0, C.byref(n)))
+        check(lib().qora_kv_length(self.h, int(seq), C.byref(n)))
         return n.value
 
-    def reset(self):
-        check(lib().qora_kv_reset(self.h, 0))
+    def reset(self, seq: int = 0):
+        check(lib().qora_kv_reset(self.h, int(seq)))
 
-    def import_layer(self, layer: int, k, v):
+    def import_layer(self, layer: int, k, v, seq: int = 0):
         k = np.ascontiguousarray(k, dtype=np.float32)
         v = np.ascontiguousarray(v, dtype=np.float32)
-        check(lib().qora_kv_import(self.h, int(layer), _ptr(k), _ptr(v), k.shape[0], 0))
+        check(lib().qora_kv_import(self.h, int(layer), _ptr(k), _ptr(v), k.shape[0], int(seq)))
 
-    def export_layer(self, layer: int, n: int, stride: int) -> Tuple[np.ndarray, np.ndarray]:
+    def export_layer(self, layer: int, n: int, stride: int, seq: int = 0) -> Tuple[np.ndarray, np.ndarray]:
         k = np.empty((n, stride), np.float32)
         v = np.empty((n, stride), np.float32)
-        check(lib().qora_kv_export(self.h, int(layer), _ptr(k), _ptr(v), int(n), 0))
+        check(lib().qora_kv_export(self.h, int(layer), _ptr(k), _ptr(v), int(n), int(seq)))
         return k, v
 
 

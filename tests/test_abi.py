@@ -74,8 +74,15 @@ def test_invalid_view_rejected_before_device_use(pkg, qf):
     m.layers[0].q_proj.n = 1000  # wrong shape
     with pytest.raises(pkg.QoraError, match="INVALID"):
         pkg.DecodeWeights(model=m)
-    m2 = qf.synth_model(seed=0, num_layers=1, vocab=64, hidden=1024, intermediate=512,
+    # F16: the batched GEMM tiles the vocab by 64
+    m2 = qf.synth_model(seed=0, num_layers=1, vocab=100, hidden=1024, intermediate=512,
                         num_heads=8, num_kv_heads=2, head_dim=128, rope_rows=8,
                         fmt=qf.FORMAT_F16)
     with pytest.raises(pkg.QoraError, match="UNSUPPORTED"):
         pkg.DecodeWeights(model=m2)
+    # F16 engines are single-GPU in this build
+    m3 = qf.synth_model(seed=0, num_layers=1, vocab=64, hidden=1024, intermediate=512,
+                        num_heads=8, num_kv_heads=2, head_dim=128, rope_rows=8,
+                        fmt=qf.FORMAT_F16)
+    with pytest.raises(pkg.QoraError, match="UNSUPPORTED"):
+        pkg.DecodeWeights(model=m3, tp_size=2, tp_rank=0)
