@@ -231,6 +231,14 @@ qora_status qora_q4_gate_up(const float* d_x, const uint8_t* d_gate_packed,
                             const uint16_t* d_up_scales, uint64_t k, uint64_t n,
                             float* d_out, void* stream);
 
+/* F16 GEMM y[m][n] = x[m][k] . W[k][n] on the tcgen05 tensor cores (replaces `gemm_f16`,
+ * src/gemv.rs:571-588, and `gemv_f16` at m = 1, src/gemv.rs:534-567). W is the
+ * reference's row-major [k][n] f16 bit patterns; k must be a multiple of 64 and n of 128.
+ * Each call re-tiles W into device scratch (the engine does this once at load); x keeps
+ * ~22 bits through an f16 hi + lo split. Synchronises the stream before returning. */
+qora_status qora_f16_gemm(const float* d_x, const uint16_t* d_w, uint64_t m, uint64_t k,
+                          uint64_t n, float* d_y, void* stream);
+
 /* Row-dot Q4 lm_head + first-maximum argmax over rows (replaces `lm_head_parallel_q4`,
  * src/gemv.rs:825-864, and the greedy branch of src/generate.rs:346-352). d_logits may
  * be NULL; d_argmax receives one uint32. */

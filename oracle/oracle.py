@@ -130,6 +130,14 @@ def gemv_f16(x, m):
     return y
 
 
+def gemm_f16(x, m):
+    """gemm_f16 (src/gemv.rs:571-588): scalar, single-threaded, no FMA."""
+    x = f32(x)
+    y = np.empty((x.shape[0], m.n), np.float32)
+    lib().orc_gemm_f16(x, x.shape[0], m.data, m.k, m.n, y)
+    return y
+
+
 def gemm_q4(x, m):
     x = f32(x)
     y = np.empty((x.shape[0], m.n), np.float32)

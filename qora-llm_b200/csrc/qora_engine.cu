@@ -29,6 +29,7 @@
 #include "common.cuh"
 #include "f16_batch.cuh"
 #include "lm_head.cuh"
+#include "umma_gemm.cuh"
 #include "megakernel.cuh"
 #include "q4_gemv.cuh"
 #include "small_kernels.cuh"
@@ -226,13 +227,14 @@ struct LayerDev {
   int nq = 0, nkv = 0;
 };
 
-// F16 weights (format 0) for the batched path: N-major [k][n] f16 as in the file, with
-// q|k|v and gate|up concatenated along n so one GEMM serves each pair.
+// F16 weights (format 0) for the batched path, re-tiled for the tensor cores
+// (umma_gemm.cuh: [N/128 tiles][K/64 chunks][16 KB]); q|k|v and gate|up are joined
+// along n so one GEMM serves each group. Values are the file's f16 bits, unchanged.
 struct F16Layer {
-  __half* wqkv = nullptr;   // [hidden][nq + 2 nkv*128]
-  __half* wo = nullptr;     // [nq][hidden]
-  __half* wgu = nullptr;    // [hidden][2 I]: gate columns then up columns
-  __half* wdown = nullptr;  // [I][hidden]
+  uint8_t* wqkv = nullptr;   // n = nq + 2 nkv*128, k = hidden
+  uint8_t* wo = nullptr;     // n = hidden, k = nq
+  uint8_t* wgu = nullptr;    // n = 2 I (gate channels then up channels), k = hidden
+  uint8_t* wdown = nullptr;  // n = hidden, k = I
   float* g_in = nullptr;
   float* g_post = nullptr;
   int rope = 0;
@@ -260,12 +262,14 @@ struct qora_engine {
   std::vector<LayerDev> layers;
   // F16 weights: batched per-op path (f16_batch.cuh)
   std::vector<F16Layer> fl;
-  __half* f_embed = nullptr;       // [vocab][hidden]: embedding rows and the tied lm_head
+  uint8_t* f_lm = nullptr;         // tiled embedding (n = vocab, k = hidden): lookup + tied lm_head
   int f_nqkv = 0;                  // q|k|v columns
-  int f_split[4] = {1, 1, 1, 1};   // K slices of the q|k|v, o, gate|up and down GEMMs
   float *f_x = nullptr, *f_qkv = nullptr, *f_attn = nullptr, *f_h = nullptr;  // [rows][...]
   float *f_logits = nullptr, *f_part = nullptr;
-  __half *f_xh = nullptr, *f_xl = nullptr;  // GEMM operand: activations as f16 hi + lo
+  size_t f_part_floats = 0;
+  uint8_t* f_xt = nullptr;         // GEMM operand: activations as tiled f16 hi | lo rows
+  float* f_rowinv = nullptr;       // per-row power-of-two unscale of the operand
+  int* f_err = nullptr;            // set by a GEMM whose bounded wait timed out
   uint8_t* lm_table = nullptr;   // embedding rows: hidden/2 packed bytes | hidden/32 f16 scales
   long long lm_row_bytes = 0;
   float* final_gamma = nullptr;
@@ -414,8 +418,8 @@ qora_status validate_view(const qora_weights_view* w) {
     return fail(QORA_ERR_UNSUPPORTED, "rope_half_dim=%u, only 64 supported", w->rope_half_dim);
   if (w->embed.k != w->vocab || w->embed.n != w->hidden || !present(w->embed))
     return fail(QORA_ERR_INVALID, "embedding must be [vocab][hidden] in the model's format");
-  if (!q4 && w->vocab % 64 != 0)
-    return fail(QORA_ERR_UNSUPPORTED, "F16 weights: vocab %u must be a multiple of 64", w->vocab);
+  if (!q4 && w->vocab % 128 != 0)
+    return fail(QORA_ERR_UNSUPPORTED, "F16 weights: vocab %u must be a multiple of 128", w->vocab);
   if (!w->final_norm_gamma || !w->no_rope_layers || !w->rope_cos || !w->rope_sin)
     return fail(QORA_ERR_INVALID, "missing final norm / rope tables / no_rope_layers");
   const qora_layer_view& L0 = w->layers[0];
@@ -977,50 +981,107 @@ qora_status check_step_error(qora_engine* e, qora_kv* kv) {
 // Every F16 forward pass runs M rows (f16_batch.cuh): one row per sequence in a batched
 // decode step, one row per prompt token in a prefill chunk.
 
-int f16_splits(int sms, int N, int K) {  // K slices so that a GEMM fills the SMs twice over
-  const int tiles = N / f16b::kTileN, chunks = K / f16b::kChunkK;
-  const int s = (2 * sms + tiles - 1) / tiles;
-  return std::max(1, std::min(s, chunks / 2));
+// Persistent CTAs and partial slots per CTA of one tcgen05 GEMM (umma_gemm.cuh).
+struct UmmaPlan {
+  int G = 1, maxseg = 1;
+};
+UmmaPlan umma_plan(int sms, int tiles, int chunks) {
+  UmmaPlan p;
+  const long long T = (long long)tiles * chunks;
+  p.G = (int)std::min<long long>(sms, T);
+  p.maxseg = 1;
+  for (int c = 0; c < p.G; ++c) {
+    const long long b0 = umma::range_begin(c, T, p.G), b1 = umma::range_begin(c + 1, T, p.G);
+    if (b1 > b0) p.maxseg = std::max(p.maxseg, (int)((b1 - 1) / chunks - b0 / chunks + 1));
+  }
+  return p;
 }
 
-template <bool KM, int MT>
-qora_status f16_gemm_mt(qora_engine* e, const f16b::GemmArgs& g) {
-  const size_t smem = f16b::gemm_smem_bytes(MT);
-  f16b::gemm_f16_kernel<KM, MT><<<dim3(g.N / f16b::kTileN, g.splits), f16b::kThreads, smem, e->stream>>>(g);
+// Device scratch of the tensor-core GEMM: the staged operand, its row scales, the
+// partial slots and the timeout flag.
+struct UmmaCtx {
+  int sms;
+  cudaStream_t stream;
+  uint8_t* xt;
+  float* rowinv;
+  float* part;
+  size_t part_floats;
+  int* err;
+};
+
+qora_status umma_norm_split(const UmmaCtx& u, const float* x, const float* gamma, int M, int K) {
+  const int R = (M + 7) / 8 * 8;
+  umma::norm_split_tiled_kernel<<<R, 256, 0, u.stream>>>(x, gamma, K, M, R, u.xt, u.rowinv);
   QCUDA(cudaGetLastError());
   return QORA_OK;
 }
 
-template <bool KM>
-qora_status f16_gemm(qora_engine* e, const __half* w, long long ldw, int M, int K, int N, int splits, float* out) {
-  const f16b::GemmArgs g{w, ldw, e->f_xh, e->f_xl, M, K, N, splits, out};
-  if (M <= 8) return f16_gemm_mt<KM, 1>(e, g);
-  if (M <= 16) return f16_gemm_mt<KM, 2>(e, g);
-  if (M <= 32) return f16_gemm_mt<KM, 4>(e, g);
-  if (M <= 64) return f16_gemm_mt<KM, 8>(e, g);
-  return f16_gemm_mt<KM, 16>(e, g);
-}
-
-template <bool KM>
-qora_status f16_gemm_attrs() {
-  QCUDA(cudaFuncSetAttribute(f16b::gemm_f16_kernel<KM, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)f16b::gemm_smem_bytes(8)));
-  QCUDA(cudaFuncSetAttribute(f16b::gemm_f16_kernel<KM, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)f16b::gemm_smem_bytes(16)));
-  return QORA_OK;
-}
-
-qora_status f16_reduce(qora_engine* e, int splits, int M, int N, int mode, const float* res, float* y) {
+// Y = X . W for the M rows staged in u.xt (umma_norm_split), followed by the slot
+// reduction with epilogue `mode` into y (row stride ldy).
+qora_status umma_gemm(const UmmaCtx& u, const uint8_t* wt, int N, int K, int M, int mode, const float* res, float* y,
+                      int ldy) {
+  const int R = (M + 7) / 8 * 8, tiles = N / umma::kTileN, chunks = K / umma::kChunkK;
+  const UmmaPlan p = umma_plan(u.sms, tiles, chunks);
+  if ((size_t)p.G * p.maxseg * R * umma::kTileN > u.part_floats)
+    return fail(QORA_ERR_INVALID, "GEMM partials exceed the scratch (%d x %d x %d)", p.G, p.maxseg, R);
+  umma::GemmArgs g{};
+  g.w = wt;
+  g.x = u.xt;
+  g.row_inv = u.rowinv;
+  g.part = u.part;
+  g.tiles = tiles;
+  g.chunks = chunks;
+  g.R = R;
+  g.stages = umma::gemm_stages(R);
+  g.maxseg = p.maxseg;
+  g.err = u.err;
+  g.timeout_ns = 2000000000ull;
+  umma::umma_gemm_kernel<<<p.G, umma::kThreads, umma::gemm_smem(R, g.stages), u.stream>>>(g);
+  QCUDA(cudaGetLastError());
+  umma::ReduceArgs r{};
+  r.part = u.part;
+  r.tiles = tiles;
+  r.chunks = chunks;
+  r.R = R;
+  r.M = M;
+  r.maxseg = p.maxseg;
+  r.G = p.G;
+  r.N = N;
+  r.mode = mode;
+  r.res = res;
+  r.y = y;
+  r.ldy = ldy;
   const long long total = (long long)M * (mode == 2 ? N / 2 : N);
-  const int blocks = (int)std::min<long long>((total + 255) / 256, 8LL * e->sms);
-  f16b::reduce_kernel<<<blocks, 256, 0, e->stream>>>(e->f_part, splits, M, N, mode, res, y);
+  const int blocks = (int)std::min<long long>((total + 255) / 256, 8LL * u.sms);
+  umma::reduce_tiles_kernel<<<blocks, 256, 0, u.stream>>>(r);
   QCUDA(cudaGetLastError());
   return QORA_OK;
 }
 
-qora_status f16_norm_split(qora_engine* e, const float* x, const float* gamma, int M, int K) {
-  f16b::norm_split_kernel<<<M, 256, 0, e->stream>>>(x, gamma, K, e->f_xh, e->f_xl, nullptr);
+// opt the GEMM kernel in to its largest shared-memory footprint (once per process)
+qora_status umma_attrs() {
+  int maxsm = 0;
+  for (int r = 8; r <= umma::kMaxRows; r += 8) maxsm = std::max(maxsm, (int)umma::gemm_smem(r, umma::gemm_stages(r)));
+  QCUDA(cudaFuncSetAttribute(umma::umma_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, maxsm));
+  return QORA_OK;
+}
+
+UmmaCtx umma_ctx(const qora_engine* e) {
+  return UmmaCtx{e->sms, e->stream, e->f_xt, e->f_rowinv, e->f_part, e->f_part_floats, e->f_err};
+}
+
+// Copy one f16 matrix view to the device and re-tile it into tiles [t0, t0 + n/128) of
+// dst (a matrix of k/64 chunks per tile). kmajor: the view is [n][k] (the embedding).
+qora_status f16_tile_upload(qora_engine* e, const qora_matrix_view& m, bool kmajor, int t0, uint8_t* dst,
+                            __half* tmp) {
+  const size_t elems = (size_t)m.k * m.n;
+  QCUDA(cudaMemcpy(tmp, m.data, elems * 2, cudaMemcpyHostToDevice));
+  const int K = kmajor ? (int)m.n : (int)m.k, N = kmajor ? (int)m.k : (int)m.n;
+  const long long units = (long long)N * (K / 8);
+  const int blocks = (int)std::min<long long>((units + 255) / 256, 16LL * e->sms);
+  umma::tile_weights_kernel<<<blocks, 256>>>(tmp, (long long)m.n, kmajor ? 1 : 0, K, N, 0, t0, dst);
   QCUDA(cudaGetLastError());
+  QCUDA(cudaDeviceSynchronize());
   return QORA_OK;
 }
 
@@ -1049,26 +1110,31 @@ qora_status f16_engine_init(qora_engine* e, const qora_weights_view* w) {
   const int V = (int)e->vocab;
   e->f_nqkv = nq + 2 * nkvw;
   e->fl.resize(e->num_layers);
-  auto put_cols = [&](__half* dst, int ldd, int col0, const qora_matrix_view& m) -> qora_status {
-    // rows of m ([k][n]) into columns [col0, col0 + n) of dst ([k][ldd])
-    QCUDA(cudaMemcpy2D(dst + col0, (size_t)ldd * 2, m.data, (size_t)m.n * 2, (size_t)m.n * 2, m.k,
-                       cudaMemcpyHostToDevice));
-    return QORA_OK;
-  };
+  // staging buffer for one source matrix (freed at the end of the load)
+  size_t tmp_elems = (size_t)V * H;
+  tmp_elems = std::max(tmp_elems, (size_t)H * I);
+  tmp_elems = std::max(tmp_elems, (size_t)H * nq);
+  __half* tmp = nullptr;
+  QCUDA(cudaMalloc(&tmp, tmp_elems * 2));
+  struct TmpFree {
+    __half* p;
+    ~TmpFree() { cudaFree(p); }
+  } tmp_free{tmp};
+  constexpr int TN = umma::kTileN;
   for (uint32_t i = 0; i < e->num_layers; ++i) {
     const qora_layer_view& L = w->layers[i];
     F16Layer& d = e->fl[i];
-    QCHECK(e->alloc(&d.wqkv, (size_t)H * e->f_nqkv));
-    QCHECK(put_cols(d.wqkv, e->f_nqkv, 0, L.q_proj));
-    QCHECK(put_cols(d.wqkv, e->f_nqkv, nq, L.k_proj));
-    QCHECK(put_cols(d.wqkv, e->f_nqkv, nq + nkvw, L.v_proj));
-    QCHECK(e->alloc(&d.wo, (size_t)nq * H));
-    QCHECK(upload(e, d.wo, L.o_proj.data, (size_t)nq * H * 2));
-    QCHECK(e->alloc(&d.wgu, (size_t)H * 2 * I));
-    QCHECK(put_cols(d.wgu, 2 * I, 0, L.gate_proj));
-    QCHECK(put_cols(d.wgu, 2 * I, I, L.up_proj));
-    QCHECK(e->alloc(&d.wdown, (size_t)I * H));
-    QCHECK(upload(e, d.wdown, L.down_proj.data, (size_t)I * H * 2));
+    QCHECK(e->alloc(&d.wqkv, (size_t)H * e->f_nqkv * 2));
+    QCHECK(f16_tile_upload(e, L.q_proj, false, 0, d.wqkv, tmp));
+    QCHECK(f16_tile_upload(e, L.k_proj, false, nq / TN, d.wqkv, tmp));
+    QCHECK(f16_tile_upload(e, L.v_proj, false, (nq + nkvw) / TN, d.wqkv, tmp));
+    QCHECK(e->alloc(&d.wo, (size_t)nq * H * 2));
+    QCHECK(f16_tile_upload(e, L.o_proj, false, 0, d.wo, tmp));
+    QCHECK(e->alloc(&d.wgu, (size_t)H * 2 * I * 2));
+    QCHECK(f16_tile_upload(e, L.gate_proj, false, 0, d.wgu, tmp));
+    QCHECK(f16_tile_upload(e, L.up_proj, false, I / TN, d.wgu, tmp));
+    QCHECK(e->alloc(&d.wdown, (size_t)I * H * 2));
+    QCHECK(f16_tile_upload(e, L.down_proj, false, 0, d.wdown, tmp));
     std::vector<float> g1 = f16_to_f32(L.input_norm_gamma, H), g2 = f16_to_f32(L.post_attn_norm_gamma, H);
     QCHECK(e->alloc(&d.g_in, H));
     QCHECK(e->alloc(&d.g_post, H));
@@ -1076,8 +1142,8 @@ qora_status f16_engine_init(qora_engine* e, const qora_weights_view* w) {
     QCHECK(upload(e, d.g_post, g2.data(), (size_t)H * 4));
     d.rope = w->no_rope_layers[i] ? 1 : 0;
   }
-  QCHECK(e->alloc(&e->f_embed, (size_t)V * H));
-  QCHECK(upload(e, e->f_embed, w->embed.data, (size_t)V * H * 2));
+  QCHECK(e->alloc(&e->f_lm, (size_t)V * H * 2));
+  QCHECK(f16_tile_upload(e, w->embed, true, 0, e->f_lm, tmp));
   std::vector<float> fg = f16_to_f32(w->final_norm_gamma, H);
   QCHECK(e->alloc(&e->final_gamma, H));
   QCHECK(upload(e, e->final_gamma, fg.data(), (size_t)H * 4));
@@ -1087,26 +1153,27 @@ qora_status f16_engine_init(qora_engine* e, const qora_weights_view* w) {
   QCHECK(upload(e, e->rope_cos, w->rope_cos, rt * 4));
   QCHECK(upload(e, e->rope_sin, w->rope_sin, rt * 4));
 
-  e->f_split[0] = f16_splits(e->sms, e->f_nqkv, H);
-  e->f_split[1] = f16_splits(e->sms, H, nq);
-  e->f_split[2] = f16_splits(e->sms, 2 * I, H);
-  e->f_split[3] = f16_splits(e->sms, H, I);
   const size_t R = f16b::kMaxRows;
-  size_t part = 0;
-  const int ns[4] = {e->f_nqkv, H, 2 * I, H};
-  for (int j = 0; j < 4; ++j) part = std::max(part, (size_t)e->f_split[j] * R * ns[j]);
+  size_t slots = 0;  // partial slots of the largest GEMM plan, in [R][128] blocks
+  const int gn[5] = {e->f_nqkv, H, 2 * I, H, V}, gk[5] = {H, nq, H, I, H};
+  for (int j = 0; j < 5; ++j) {
+    const UmmaPlan p = umma_plan(e->sms, gn[j] / umma::kTileN, gk[j] / umma::kChunkK);
+    slots = std::max(slots, (size_t)p.G * p.maxseg);
+  }
   const size_t kmax = (size_t)std::max(std::max(H, nq), I);
-  QCHECK(e->alloc(&e->f_part, part));
+  e->f_part_floats = slots * R * umma::kTileN;
+  QCHECK(e->alloc(&e->f_part, e->f_part_floats));
   QCHECK(e->alloc(&e->f_x, R * H));
   QCHECK(e->alloc(&e->f_qkv, R * e->f_nqkv));
   QCHECK(e->alloc(&e->f_attn, R * nq));
   QCHECK(e->alloc(&e->f_h, R * I));
   QCHECK(e->alloc(&e->f_logits, R * V));
-  QCHECK(e->alloc(&e->f_xh, R * kmax));
-  QCHECK(e->alloc(&e->f_xl, R * kmax));
+  QCHECK(e->alloc(&e->f_xt, kmax * R * 2 * 2));
+  QCHECK(e->alloc(&e->f_rowinv, R));
+  QCHECK(e->alloc(&e->f_err, 1));
+  QCUDA(cudaMemset(e->f_err, 0, sizeof(int)));
   e->logits = e->f_logits;
-  QCHECK(f16_gemm_attrs<false>());
-  QCHECK(f16_gemm_attrs<true>());
+  QCHECK(umma_attrs());
   QCUDA(cudaDeviceSynchronize());
   return QORA_OK;
 }
@@ -1126,7 +1193,8 @@ qora_status f16_forward(qora_engine* e, qora_kv* kv, int M, int lm0) {
   const int V = (int)e->vocab, NQKV = e->f_nqkv;
   const f16b::RowInfo ri = f16b::row_info(kv->rows);
   cudaStream_t s = e->stream;
-  f16b::embed_rows_kernel<<<M, 256, 0, s>>>(e->f_embed, H, V, ri, e->f_x);
+  const UmmaCtx u = umma_ctx(e);
+  f16b::embed_rows_kernel<<<M, 256, 0, s>>>(e->f_lm, H, V, ri, e->f_x);
   QCUDA(cudaGetLastError());
   const long long hs = (long long)kv->max_seq * kHeadDim, ss = (long long)kv->seq_stride();
   for (uint32_t li = 0; li < e->num_layers; ++li) {
@@ -1134,29 +1202,25 @@ qora_status f16_forward(qora_engine* e, qora_kv* kv, int M, int lm0) {
     float* kc = kv->k + li * kv->layer_stride();
     float* vc = kv->v + li * kv->layer_stride();
     // attention block
-    QCHECK(f16_norm_split(e, e->f_x, d.g_in, M, H));
-    QCHECK(f16_gemm<false>(e, d.wqkv, NQKV, M, H, NQKV, e->f_split[0], e->f_part));
-    QCHECK(f16_reduce(e, e->f_split[0], M, NQKV, 0, nullptr, e->f_qkv));
+    QCHECK(umma_norm_split(u, e->f_x, d.g_in, M, H));
+    QCHECK(umma_gemm(u, d.wqkv, NQKV, H, M, 0, nullptr, e->f_qkv, NQKV));
     f16b::rope_kv_kernel<<<M, 256, 0, s>>>(e->f_qkv, nq, nkvw, d.rope, e->rope_cos, e->rope_sin, ri, kc, vc, ss, hs);
     QCUDA(cudaGetLastError());
     f16b::attention_rows_kernel<<<dim3(e->nkv, M), f16b::kAttnRowThreads, 0, s>>>(e->f_qkv, nq, nkvw, kGrp, ri, kc,
                                                                                   vc, ss, hs, e->f_attn);
     QCUDA(cudaGetLastError());
-    QCHECK(f16_norm_split(e, e->f_attn, nullptr, M, nq));
-    QCHECK(f16_gemm<false>(e, d.wo, H, M, nq, H, e->f_split[1], e->f_part));
-    QCHECK(f16_reduce(e, e->f_split[1], M, H, 1, e->f_x, e->f_x));
+    QCHECK(umma_norm_split(u, e->f_attn, nullptr, M, nq));
+    QCHECK(umma_gemm(u, d.wo, H, nq, M, 1, e->f_x, e->f_x, H));
     // MLP block
-    QCHECK(f16_norm_split(e, e->f_x, d.g_post, M, H));
-    QCHECK(f16_gemm<false>(e, d.wgu, 2 * I, M, H, 2 * I, e->f_split[2], e->f_part));
-    QCHECK(f16_reduce(e, e->f_split[2], M, 2 * I, 2, nullptr, e->f_h));
-    QCHECK(f16_norm_split(e, e->f_h, nullptr, M, I));
-    QCHECK(f16_gemm<false>(e, d.wdown, H, M, I, H, e->f_split[3], e->f_part));
-    QCHECK(f16_reduce(e, e->f_split[3], M, H, 1, e->f_x, e->f_x));
+    QCHECK(umma_norm_split(u, e->f_x, d.g_post, M, H));
+    QCHECK(umma_gemm(u, d.wgu, 2 * I, H, M, 2, nullptr, e->f_h, I));
+    QCHECK(umma_norm_split(u, e->f_h, nullptr, M, I));
+    QCHECK(umma_gemm(u, d.wdown, H, I, M, 1, e->f_x, e->f_x, H));
   }
   if (lm0 < M) {
     const int ml = M - lm0;
-    QCHECK(f16_norm_split(e, e->f_x + (size_t)lm0 * H, e->final_gamma, ml, H));
-    QCHECK(f16_gemm<true>(e, e->f_embed, H, ml, H, V, 1, e->f_logits));
+    QCHECK(umma_norm_split(u, e->f_x + (size_t)lm0 * H, e->final_gamma, ml, H));
+    QCHECK(umma_gemm(u, e->f_lm, V, H, ml, 0, nullptr, e->f_logits, V));
     f16b::argmax_rows_kernel<<<ml, 256, 0, s>>>(e->f_logits, V, kv->f_argmax);
     QCUDA(cudaGetLastError());
   }
@@ -1211,12 +1275,15 @@ qora_status f16_stage_decode_rows(qora_engine* e, qora_kv* kv, const uint32_t* t
 }
 
 qora_status f16_check_error(qora_engine* e, qora_kv* kv) {
-  int err = 0;
-  QCUDA(cudaMemcpyAsync(kv->rows_host + 3 * f16b::kMaxRows + 1, kv->rows + 3 * f16b::kMaxRows + 1, sizeof(int),
-                        cudaMemcpyDeviceToHost, e->stream));
+  int* h = kv->rows_host + 3 * f16b::kMaxRows;
+  QCUDA(cudaMemcpyAsync(h + 1, kv->rows + 3 * f16b::kMaxRows + 1, sizeof(int), cudaMemcpyDeviceToHost, e->stream));
+  QCUDA(cudaMemcpyAsync(h, e->f_err, sizeof(int), cudaMemcpyDeviceToHost, e->stream));
   QCUDA(cudaStreamSynchronize(e->stream));
-  err = kv->rows_host[3 * f16b::kMaxRows + 1];
-  if (err) return fail(QORA_ERR_RANGE, "device rejected a token id");
+  if (h[0]) {
+    cudaMemsetAsync(e->f_err, 0, sizeof(int), e->stream);
+    return fail(QORA_ERR_TIMEOUT, "a bounded wait in the tensor-core GEMM timed out");
+  }
+  if (h[1]) return fail(QORA_ERR_RANGE, "device rejected a token id");
   return QORA_OK;
 }
 
@@ -2138,6 +2205,56 @@ qora_status qora_q4_lm_head(const float* d_x, const uint8_t* d_packed, const uin
   a.part_i = sc->lm_i;
   a.counter = sc->lm_c;
   return launch_lm_head((int)hidden, a, ctas, (cudaStream_t)stream);
+}
+
+qora_status qora_f16_gemm(const float* d_x, const uint16_t* d_w, uint64_t m, uint64_t k, uint64_t n,
+                          float* d_y, void* stream) {
+  if (!d_x || !d_w || !d_y) return fail(QORA_ERR_INVALID, "NULL pointer");
+  if (m == 0 || k == 0 || n == 0) return fail(QORA_ERR_INVALID, "empty GEMM");
+  if (k % umma::kChunkK || n % umma::kTileN || k > (1u << 16) || n > (1u << 20))
+    return fail(QORA_ERR_UNSUPPORTED, "k=%llu must be a multiple of 64 (<= 65536), n=%llu of 128", (unsigned long long)k,
+                (unsigned long long)n);
+  int dev = 0;
+  QCUDA(cudaGetDevice(&dev));
+  const cudaStream_t s = (cudaStream_t)stream;
+  const int K = (int)k, N = (int)n, sms = sm_count(dev);
+  const UmmaPlan p = umma_plan(sms, N / umma::kTileN, K / umma::kChunkK);
+  struct Scratch {
+    std::vector<void*> ptrs;
+    ~Scratch() {
+      for (void* q : ptrs) cudaFree(q);
+    }
+  } sc;
+  auto grab = [&](size_t bytes, void** out) -> qora_status {
+    QCUDA(cudaMalloc(out, std::max<size_t>(bytes, 16)));
+    sc.ptrs.push_back(*out);
+    return QORA_OK;
+  };
+  void *wt = nullptr, *xt = nullptr, *rowinv = nullptr, *part = nullptr, *err = nullptr;
+  QCHECK(grab((size_t)K * N * 2, &wt));
+  QCHECK(grab((size_t)K * umma::kMaxRows * 4, &xt));
+  QCHECK(grab(umma::kMaxRows * 4, &rowinv));
+  const size_t part_floats = (size_t)p.G * p.maxseg * umma::kMaxRows * umma::kTileN;
+  QCHECK(grab(part_floats * 4, &part));
+  QCHECK(grab(sizeof(int), &err));
+  QCUDA(cudaMemset(err, 0, sizeof(int)));
+  QCHECK(umma_attrs());
+  const long long units = (long long)N * (K / 8);
+  umma::tile_weights_kernel<<<(int)std::min<long long>((units + 255) / 256, 16LL * sms), 256, 0, s>>>(
+      reinterpret_cast<const __half*>(d_w), N, 0, K, N, 0, 0, static_cast<uint8_t*>(wt));
+  QCUDA(cudaGetLastError());
+  const UmmaCtx u{sms, s, static_cast<uint8_t*>(xt), static_cast<float*>(rowinv), static_cast<float*>(part),
+                  part_floats, static_cast<int*>(err)};
+  for (uint64_t m0 = 0; m0 < m; m0 += umma::kMaxRows) {
+    const int mb = (int)std::min<uint64_t>(umma::kMaxRows, m - m0);
+    QCHECK(umma_norm_split(u, d_x + m0 * k, nullptr, mb, K));
+    QCHECK(umma_gemm(u, static_cast<uint8_t*>(wt), N, K, mb, 0, nullptr, d_y + m0 * n, N));
+  }
+  int herr = 0;
+  QCUDA(cudaMemcpyAsync(&herr, err, sizeof(int), cudaMemcpyDeviceToHost, s));
+  QCUDA(cudaStreamSynchronize(s));
+  if (herr) return fail(QORA_ERR_TIMEOUT, "a bounded wait in the tensor-core GEMM timed out");
+  return QORA_OK;
 }
 
 }  // extern "C"

@@ -65,6 +65,7 @@ SIGNATURES = {
     "qora_q4_dequant": (C.c_int, [_vp, _vp, _u64, _u64, _u64, _vp, _vp]),
     "qora_q4_gate_up": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _u64, _u64, _vp, _vp]),
     "qora_q4_lm_head": (C.c_int, [_vp, _vp, _vp, _u64, _u64, _vp, _vp, _vp]),
+    "qora_f16_gemm": (C.c_int, [_vp, _vp, _u64, _u64, _u64, _vp, _vp]),
 }
 
 
@@ -338,3 +339,8 @@ def q4_gate_up(x_ptr, gp, gs, up, us, k, n, out_ptr, stream=None):
 def q4_lm_head(x_ptr, packed_ptr, scales_ptr, vocab, hidden, logits_ptr, argmax_ptr, stream=None):
     check(lib().qora_q4_lm_head(x_ptr, packed_ptr, scales_ptr, vocab, hidden, logits_ptr,
                                 argmax_ptr, _stream_ptr(stream)))
+
+
+def f16_gemm(x_ptr, w_ptr, m, k, n, y_ptr, stream=None):
+    """y[m][n] = x[m][k] . W[k][n], W f16 row-major (qora_f16_gemm, tcgen05)."""
+    check(lib().qora_f16_gemm(x_ptr, w_ptr, m, k, n, y_ptr, _stream_ptr(stream)))

@@ -143,3 +143,43 @@ def test_lm_head_argmax_tie_takes_lowest_index(pkg, qf, torch):
                           am.data_ptr())
     torch.cuda.synchronize()
     assert int(am.item()) == min(17, best)
+
+
+# ---------------------------------------------------------------- F16 GEMM (tcgen05)
+def run_f16_gemm(pkg, torch, x, m):
+    dx, dw = dev(torch, x), dev(torch, m.data.view(np.int16))
+    y = torch.empty((x.shape[0], m.n), dtype=torch.float32, device="cuda")
+    pkg.engine.f16_gemm(dx.data_ptr(), dw.data_ptr(), x.shape[0], m.k, m.n, y.data_ptr())
+    torch.cuda.synchronize()
+    return y.cpu().numpy()
+
+
+def test_f16_gemm_matches_oracle(pkg, qf, orc, torch):
+    """Small case against the oracle's gemm_f16 (the reference's scalar F16 GEMM)."""
+    rng = np.random.default_rng(3)
+    m = qf.synth_f16_matrix(rng, 256, 384)
+    x = rng.standard_normal((5, 256)).astype(np.float32)
+    y = run_f16_gemm(pkg, torch, x, m)
+    ref = orc.gemm_f16(x, m)
+    assert rel_l2(y, ref) < GEMV_TOL, rel_l2(y, ref)
+
+
+@pytest.mark.parametrize("rows,k,n", [(1, 2048, 3072), (8, 2048, 2048), (32, 11008, 2048),
+                                      (128, 2048, 1536), (200, 512, 256), (3, 64, 128),
+                                      (16, 2048, 22016)])
+def test_f16_gemm_shapes(pkg, qf, torch, rows, k, n):
+    """SmolLM3 projection shapes at batch 1/8/32, a full prefill chunk, two row blocks,
+    the smallest tile, and gate|up: against an f64 product of the same f16 weights."""
+    rng = np.random.default_rng(rows * 7 + k)
+    m = qf.synth_f16_matrix(rng, k, n)
+    x = rng.standard_normal((rows, k)).astype(np.float32)
+    x[0, :7] *= 1e-3  # small and large magnitudes within one row
+    if rows > 1:
+        x[1] *= 300.0  # a row far above f16's comfortable range before its row scale
+    y = run_f16_gemm(pkg, torch, x, m)
+    w = qf.f16_bits_to_f32(m.data).reshape(k, n).astype(np.float64)
+    ref = x.astype(np.float64) @ w
+    assert rel_l2(y, ref) < GEMV_TOL, rel_l2(y, ref)
+    # per element: error within a small multiple of f32 rounding of |x|.|w|
+    bound = np.abs(x.astype(np.float64)) @ np.abs(w)
+    assert np.all(np.abs(y - ref) <= 1e-5 * bound + 1e-30)
