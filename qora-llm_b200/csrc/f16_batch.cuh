@@ -3,12 +3,13 @@
 // row is one token of one sequence at one position; a batched decode step has one row
 // per sequence, a prefill chunk one row per prompt token of a sequence. Per layer:
 //
-//   umma::norm_split_tiled  RMSNorm (optional) of each row into the tensor-core operand
-//   umma::umma_gemm_kernel  q|k|v, o, gate|up, down and the tied lm_head on tcgen05
-//   umma::reduce_tiles      partial slots summed (+ residual, or SwiGLU)
-//   rope_kv                 RoPE on q/k at each row's position, k/v appended to its cache
-//   attention_rows          causal attention of each row over its sequence's cache prefix
-//   argmax_rows             first maximum per row
+//   umma::fused_gemm  RMSNorm + q|k|v GEMM + RoPE + KV-cache append
+//   attention_split   causal attention of each row over its sequence's cache prefix
+//   umma::fused_gemm  o_proj GEMM + residual
+//   umma::fused_gemm  RMSNorm + gate|up GEMM + SwiGLU
+//   umma::fused_gemm  down_proj GEMM + residual
+// and per step: embed_rows at the start, umma::fused_gemm (final RMSNorm + tied lm_head
+// + greedy argmax) at the end, advance_rows between greedy steps.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -20,46 +21,42 @@ namespace qora {
 namespace f16b {
 
 constexpr int kMaxRows = umma::kMaxRows;  // rows per step (prefill chunk / batch)
-
-// ---------------------------------------------------------------- per-row helpers
-// Row table in device memory (one per KV cache): seq | pos | token, kMaxRows ints each,
-// then the greedy step counter and an error flag. Kernels read it at run time, so one
-// captured graph serves every step.
-struct RowInfo {
-  int* seq;    // [M] sequence of each row
-  int* pos;    // [M] position of each row
-  int* token;  // [M] token id of each row (embedding)
-  int* step;   // greedy step counter (ring row)
-  int* error;  // nonzero: a token id was out of range
-};
-constexpr int kRowInts = 3 * kMaxRows + 2;
-__host__ __device__ inline RowInfo row_info(int* base) {
-  return RowInfo{base, base + kMaxRows, base + 2 * kMaxRows, base + 3 * kMaxRows, base + 3 * kMaxRows + 1};
-}
+using umma::RowInfo;
+using umma::kRowInts;
+using umma::row_info;
 
 // x[m] = f32(E[token[m]]) (embed_lookup, src/gemv.rs:515-526), read from the tiled
-// embedding (umma tile layout, n = vocab, k = hidden). One CTA per row.
-__global__ void embed_rows_kernel(const uint8_t* emb_t, int H, int vocab, RowInfo ri, float* x) {
-  const int m = blockIdx.x;
+// embedding (n = vocab, k = hidden), with the per-128-channel statistics (sum of squares,
+// max |x|) the first RMSNorm reads. Grid (hidden / 128, M), 128 threads.
+__global__ void __launch_bounds__(128) embed_rows_kernel(const uint8_t* emb_t, int H, int vocab, RowInfo ri,
+                                                          float* x, float* st_ss, float* st_mx) {
+  __shared__ float red[2][4];
+  const int t = blockIdx.x, m = blockIdx.y, i = threadIdx.x;
   const int tok = ri.token[m];
   if (tok < 0 || tok >= vocab) {  // the host validates ids; this keeps the read in bounds
-    if (threadIdx.x == 0) *ri.error = 1;
+    if (i == 0 && t == 0) *ri.error = 1;
     return;
   }
-  const int chunks = H / umma::kChunkK, t = tok / umma::kTileN, o = tok % umma::kTileN;
-  for (int g = threadIdx.x; g < H / 8; g += blockDim.x) {
-    const int k = g * 8;
-    const uint8_t* p = emb_t + ((size_t)t * chunks + k / umma::kChunkK) * umma::kATile + umma::tile_off(o, k % umma::kChunkK);
-    const uint4 v = *reinterpret_cast<const uint4*>(p);
-    const __half* h = reinterpret_cast<const __half*>(&v);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) x[(long long)m * H + k + i] = __half2float(h[i]);
+  const int chunks = H / umma::kChunkK, k = t * umma::kTileN + i;
+  const uint8_t* p = emb_t + ((size_t)(tok / umma::kTileN) * chunks + k / umma::kChunkK) * umma::kATile +
+                     umma::tile_off(tok % umma::kTileN, k % umma::kChunkK);
+  const float v = __half2float(*reinterpret_cast<const __half*>(p));
+  x[(size_t)m * H + k] = v;
+  float ss = warp_sum(__fmul_rn(v, v)), mx = warp_max(fabsf(v));
+  if ((i & 31) == 0) {
+    red[0][i >> 5] = ss;
+    red[1][i >> 5] = mx;
+  }
+  __syncthreads();
+  if (i == 0) {
+    st_ss[(size_t)t * kMaxRows + m] = __fadd_rn(__fadd_rn(red[0][0], red[0][1]), __fadd_rn(red[0][2], red[0][3]));
+    st_mx[(size_t)t * kMaxRows + m] = fmaxf(fmaxf(red[1][0], red[1][1]), fmaxf(red[1][2], red[1][3]));
   }
 }
 
 // End of a batched greedy step: each row's greedy token becomes its next input, its
 // position advances, and the token is recorded at ring[step][m].
-__global__ void advance_rows_kernel(int M, RowInfo ri, const unsigned* am, unsigned* ring, int ring_rows) {
+__global__ void advance_rows_kernel(int M, umma::RowInfo ri, const unsigned* am, unsigned* ring, int ring_rows) {
   const int m = threadIdx.x;
   const int s = *ri.step;
   if (m < M) {
@@ -71,149 +68,177 @@ __global__ void advance_rows_kernel(int M, RowInfo ri, const unsigned* am, unsig
   if (m == 0) *ri.step = s + 1;
 }
 
-// RoPE on q and k of each row at its position (layers with the flag; src/gemv.rs:757-778),
-// then k and v appended to the row's sequence cache, head-major [kvh][max_seq][128] per
-// sequence (sequence stride seq_stride floats).
-__global__ void rope_kv_kernel(float* qkv, int nq, int nkvw, int rope, const float* cos_t, const float* sin_t,
-                               RowInfo ri, float* kc, float* vc, long long seq_stride, long long head_stride) {
-  const int m = blockIdx.x, pos = ri.pos[m];
-  float* row = qkv + (long long)m * (nq + 2 * nkvw);
-  const int pairs = (nq + nkvw) / 2;  // (d, d+64) pairs of the q and k heads
-  for (int i = threadIdx.x; i < pairs; i += blockDim.x) {
-    const int h = i / kHalfDim, d = i % kHalfDim, c = h * kHeadDim + d;
-    float* p = row + c;
-    const float x1 = p[0], x2 = p[kHalfDim];
-    float y1 = x1, y2 = x2;
-    if (rope) {
-      const float cs = cos_t[(long long)pos * kHalfDim + d], sn = sin_t[(long long)pos * kHalfDim + d];
-      y1 = __fsub_rn(__fmul_rn(x1, cs), __fmul_rn(x2, sn));
-      y2 = __fadd_rn(__fmul_rn(x2, cs), __fmul_rn(x1, sn));
-    }
-    p[0] = y1;
-    p[kHalfDim] = y2;
-  }
-  __syncthreads();
-  float* kd = kc + (long long)ri.seq[m] * seq_stride;
-  float* vd = vc + (long long)ri.seq[m] * seq_stride;
-  for (int i = threadIdx.x; i < nkvw; i += blockDim.x) {
-    const int j = i / kHeadDim, d = i % kHeadDim;
-    kd[j * head_stride + (long long)pos * kHeadDim + d] = row[nq + i];
-    vd[j * head_stride + (long long)pos * kHeadDim + d] = row[nq + nkvw + i];
-  }
-}
+// Attention of row m's 4 query heads of KV head j over positions [0, pos[m]] of its
+// sequence (q rows [M][nq] after RoPE; the K/V cache rows already hold position pos[m]).
+// Decode attention of the reference (src/gemv.rs:914-989, softmax_raw :782-793), split
+// over positions: CTA (j, m, p) takes chunk p of the row's positions (chunk = a multiple
+// of 64 sized so that a row has at most kAttSplits chunks) and keeps a running maximum
+// over 64-position blocks; the last chunk to finish (per-(m, j) counter, self-resetting)
+// merges the chunks in order and writes the normalised output and the row's max |out|
+// (the o_proj operand's scale). Grid (kv heads, M, kAttSplits), 128 threads.
+constexpr int kAttThreads = 128;
+constexpr int kAttSplits = 16;
+constexpr int kAttBlock = 64;
 
-// Attention of row m's query heads of KV head j over positions [0, pos[m]] of its
-// sequence (decode attention, src/gemv.rs:914-989; softmax_raw :782-793): scores in
-// chunks of 256 with a running maximum, normalised at the end. One CTA per (j, m).
-constexpr int kAttnRowThreads = 128;
-__global__ void __launch_bounds__(kAttnRowThreads)
-    attention_rows_kernel(const float* qkv, int nq, int nkvw, int grp, RowInfo ri, const float* kc,
-                          const float* vc, long long seq_stride, long long head_stride, float* out) {
-  __shared__ float qs[4][kHeadDim];
-  __shared__ float sc[4][256];
-  __shared__ float s_m[4], s_l[4], s_a[4];
-  const int j = blockIdx.x, m = blockIdx.y;
+struct AttnRowsArgs {
+  const float* q;       // [M][nq]
+  int nq, nkv;
+  RowInfo rows;
+  const float* kc;      // this layer's caches [batch][kv heads][max_seq][128]
+  const float* vc;
+  long long seq_stride, head_stride;
+  float* out;           // [M][nq]
+  float* st_mx;         // [kv heads][kMaxRows]
+  float* o_part;        // [kMaxRows][nkv][kAttSplits][4][128] chunk partials
+  float* ml_part;       // [kMaxRows][nkv][kAttSplits][4][2] chunk (max, sum)
+  unsigned* cnt;        // [kMaxRows][nkv] arrivals
+};
+
+__global__ void __launch_bounds__(kAttThreads) attention_split_kernel(const AttnRowsArgs a) {
+  __shared__ __align__(16) float qs[4][kHeadDim];
+  __shared__ float sc[4][kAttBlock];
+  __shared__ float s_a[4], s_red[4];
+  __shared__ int s_last;
+  const int j = blockIdx.x, m = blockIdx.y, p = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int len = ri.pos[m] + 1;
-  const float* q = qkv + (long long)m * (nq + 2 * nkvw) + (long long)j * grp * kHeadDim;
-  const float* K = kc + (long long)ri.seq[m] * seq_stride + j * head_stride;
-  const float* V = vc + (long long)ri.seq[m] * seq_stride + j * head_stride;
+  const int len = a.rows.pos[m] + 1;
+  const int per = kAttSplits * kAttBlock;
+  const int cs = kAttBlock * ((len + per - 1) / per);  // chunk length (multiple of 64)
+  const int n = (len + cs - 1) / cs;                    // chunks of this row
+  if (p >= n) return;
+  const int sb = p * cs, se = min(len, sb + cs);
+  const float* K = a.kc + (long long)a.rows.seq[m] * a.seq_stride + j * a.head_stride;
+  const float* V = a.vc + (long long)a.rows.seq[m] * a.seq_stride + j * a.head_stride;
   const float scale = 0.08838834764831845f;  // 1/sqrt(128): the f32 quotient of 1 and f32 sqrt(128)
-  for (int i = tid; i < grp * kHeadDim; i += kAttnRowThreads) qs[i / kHeadDim][i % kHeadDim] = q[i];
-  if (tid < 4) {
-    s_m[tid] = -INFINITY;
-    s_l[tid] = 0.0f;
+  {
+    const float* q = a.q + (size_t)m * a.nq + (size_t)j * 4 * kHeadDim;
+    for (int i = tid; i < 4 * kHeadDim; i += kAttThreads) qs[i / kHeadDim][i % kHeadDim] = q[i];
   }
-  float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  float mrun = -INFINITY, lrun = 0.0f;  // held by warp h = head h
+  float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // thread = dim d
   __syncthreads();
-  for (int s0 = 0; s0 < len; s0 += 256) {
-    const int n = min(256, len - s0);
-    // scores: warp w takes positions s0+w, +4, ...; lanes split the 128 dims
-    for (int s = warp; s < n; s += 4) {
-      const float4 k4 = reinterpret_cast<const float4*>(K + (long long)(s0 + s) * kHeadDim)[lane];
-      for (int h = 0; h < grp; ++h) {
-        const float4 q4 = reinterpret_cast<const float4*>(qs[h])[lane];
-        float d = q4.x * k4.x;
-        d = __fmaf_rn(q4.y, k4.y, d);
-        d = __fmaf_rn(q4.z, k4.z, d);
-        d = __fmaf_rn(q4.w, k4.w, d);
-        d = warp_sum(d);
-        if (lane == 0) sc[h][s] = __fmul_rn(d, scale);
+  const int pi = 16 * warp + (lane & 15), half = lane >> 4;
+  for (int s0 = sb; s0 < se; s0 += kAttBlock) {
+    const int nn = min(kAttBlock, se - s0);
+    // scores: lane -> position s0 + pi, dims [64 half, 64 half + 64); halves combined
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    if (pi < nn) {
+      const float4* kr = reinterpret_cast<const float4*>(K + (long long)(s0 + pi) * kHeadDim + half * 64);
+      float4 kv[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) kv[i] = kr[i];
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const float4* qh = reinterpret_cast<const float4*>(&qs[h][half * 64]);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float4 qv = qh[i];
+          acc[h] = __fmaf_rn(qv.x, kv[i].x, acc[h]);
+          acc[h] = __fmaf_rn(qv.y, kv[i].y, acc[h]);
+          acc[h] = __fmaf_rn(qv.z, kv[i].z, acc[h]);
+          acc[h] = __fmaf_rn(qv.w, kv[i].w, acc[h]);
+        }
       }
     }
+#pragma unroll
+    for (int h = 0; h < 4; ++h) acc[h] = __fadd_rn(acc[h], __shfl_xor_sync(0xffffffffu, acc[h], 16));
+    if (pi < nn && half == 0) {
+#pragma unroll
+      for (int h = 0; h < 4; ++h) sc[h][pi] = __fmul_rn(acc[h], scale);
+    }
     __syncthreads();
-    // running softmax per head (warp h)
-    if (warp < grp) {
+    {  // running softmax of head h = warp
       const int h = warp;
-      float mx = s_m[h];
-      for (int i = lane; i < n; i += 32) mx = fmaxf(mx, sc[h][i]);
-      mx = warp_max(mx);
-      float l = 0.0f;
-      for (int i = lane; i < n; i += 32) {
-        const float e = expf(sc[h][i] - mx);
-        sc[h][i] = e;
-        l += e;
-      }
-      l = warp_sum(l);
-      if (lane == 0) {
-        const float a = expf(s_m[h] - mx);  // rescale of what was accumulated so far
-        s_a[h] = a;
-        s_l[h] = __fmaf_rn(s_l[h], a, l);
-        s_m[h] = mx;
-      }
+      const float v0 = lane < nn ? sc[h][lane] : -INFINITY, v1 = lane + 32 < nn ? sc[h][lane + 32] : -INFINITY;
+      const float mx = warp_max(fmaxf(v0, v1));
+      const float mnew = fmaxf(mrun, mx);
+      const float e0 = lane < nn ? expf(v0 - mnew) : 0.0f, e1 = lane + 32 < nn ? expf(v1 - mnew) : 0.0f;
+      if (lane < nn) sc[h][lane] = e0;
+      if (lane + 32 < nn) sc[h][lane + 32] = e1;
+      const float l = warp_sum(__fadd_rn(e0, e1));
+      const float al = expf(mrun - mnew);  // 0 on the first block
+      lrun = __fmaf_rn(lrun, al, l);
+      mrun = mnew;
+      if (lane == 0) s_a[h] = al;
     }
     __syncthreads();
-    // P.V: thread d accumulates dim d of the grp heads
-    {
+    {  // P.V: thread d
       const int d = tid;
-      for (int h = 0; h < grp; ++h) o[h] = __fmul_rn(o[h], s_a[h]);
-      for (int i = 0; i < n; ++i) {
-        const float v = V[(long long)(s0 + i) * kHeadDim + d];
-        for (int h = 0; h < grp; ++h) o[h] = __fmaf_rn(sc[h][i], v, o[h]);
+#pragma unroll
+      for (int h = 0; h < 4; ++h) o[h] = __fmul_rn(o[h], s_a[h]);
+      const float* vr = V + (long long)s0 * kHeadDim + d;
+      int i = 0;
+      for (; i + 8 <= nn; i += 8) {
+        float v[8];
+#pragma unroll
+        for (int r = 0; r < 8; ++r) v[r] = vr[(long long)(i + r) * kHeadDim];
+#pragma unroll
+        for (int r = 0; r < 8; ++r)
+#pragma unroll
+          for (int h = 0; h < 4; ++h) o[h] = __fmaf_rn(sc[h][i + r], v[r], o[h]);
+      }
+      for (; i < nn; ++i) {
+        const float v = vr[(long long)i * kHeadDim];
+#pragma unroll
+        for (int h = 0; h < 4; ++h) o[h] = __fmaf_rn(sc[h][i], v, o[h]);
       }
     }
     __syncthreads();
   }
-  float* dst = out + (long long)m * nq + (long long)j * grp * kHeadDim;
-  for (int h = 0; h < grp; ++h) dst[h * kHeadDim + tid] = __fmul_rn(o[h], __fdiv_rn(1.0f, s_l[h]));
-}
-
-// First maximum of each row of logits (src/generate.rs:346-352); one CTA per row.
-__global__ void argmax_rows_kernel(const float* logits, int V, unsigned* out) {
-  __shared__ float bv[8];
-  __shared__ unsigned bi[8];
-  const int m = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const float* row = logits + (long long)m * V;
-  float best = -INFINITY;
-  unsigned besti = 0xFFFFFFFFu;
-  for (int v = tid; v < V; v += blockDim.x)
-    if (better(row[v], (unsigned)v, best, besti)) {
-      best = row[v];
-      besti = (unsigned)v;
+  const size_t slot = ((size_t)m * a.nkv + j) * kAttSplits;
+  float* dst = a.out + (size_t)m * a.nq + (size_t)j * 4 * kHeadDim;
+  float mxo = 0.0f;
+  if (n == 1) {
+    if (lane == 0) s_red[warp] = lrun;  // warp h holds head h's sum
+    __syncthreads();
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const float r = __fmul_rn(o[h], __fdiv_rn(1.0f, s_red[h]));
+      dst[h * kHeadDim + tid] = r;
+      mxo = fmaxf(mxo, fabsf(r));
     }
-  for (int o = 16; o > 0; o >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-    const unsigned oi = __shfl_xor_sync(0xffffffffu, besti, o);
-    if (better(ov, oi, best, besti)) {
-      best = ov;
-      besti = oi;
+  } else {
+#pragma unroll
+    for (int h = 0; h < 4; ++h) a.o_part[((slot + p) * 4 + h) * kHeadDim + tid] = o[h];
+    if (lane == 0) {
+      a.ml_part[((slot + p) * 4 + warp) * 2] = mrun;
+      a.ml_part[((slot + p) * 4 + warp) * 2 + 1] = lrun;
     }
-  }
-  if (lane == 0) {
-    bv[warp] = best;
-    bi[warp] = besti;
-  }
-  __syncthreads();
-  if (tid == 0) {
-    float b = bv[0];
-    unsigned i0 = bi[0];
-    for (int w = 1; w < (int)(blockDim.x / 32); ++w)
-      if (better(bv[w], bi[w], b, i0)) {
-        b = bv[w];
-        i0 = bi[w];
+    __syncthreads();
+    if (tid == 0) {
+      __threadfence();
+      const unsigned old = atomicAdd(&a.cnt[(size_t)m * a.nkv + j], 1u);
+      const bool last = old == (unsigned)(n - 1);
+      if (last) {
+        a.cnt[(size_t)m * a.nkv + j] = 0u;
+        __threadfence();
       }
-    out[m] = (i0 == 0xFFFFFFFFu) ? 0u : i0;
+      s_last = last ? 1 : 0;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    // merge the chunks in order
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      float mg = -INFINITY;
+      for (int c = 0; c < n; ++c) mg = fmaxf(mg, __ldcg(&a.ml_part[((slot + c) * 4 + h) * 2]));
+      float l = 0.0f, acc = 0.0f;
+      for (int c = 0; c < n; ++c) {
+        const float w = expf(__ldcg(&a.ml_part[((slot + c) * 4 + h) * 2]) - mg);
+        l = __fmaf_rn(__ldcg(&a.ml_part[((slot + c) * 4 + h) * 2 + 1]), w, l);
+        acc = __fmaf_rn(__ldcg(&a.o_part[((slot + c) * 4 + h) * kHeadDim + tid]), w, acc);
+      }
+      const float r = __fmul_rn(acc, __fdiv_rn(1.0f, l));
+      dst[h * kHeadDim + tid] = r;
+      mxo = fmaxf(mxo, fabsf(r));
+    }
   }
+  // max |out| of this (row, kv head): the o_proj operand's row scale
+  mxo = warp_max(mxo);
+  __syncthreads();
+  if (lane == 0) s_red[warp] = mxo;
+  __syncthreads();
+  if (tid == 0) a.st_mx[(size_t)j * kMaxRows + m] = fmaxf(fmaxf(s_red[0], s_red[1]), fmaxf(s_red[2], s_red[3]));
 }
 
 }  // namespace f16b

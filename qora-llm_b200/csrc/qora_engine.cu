@@ -237,6 +237,7 @@ struct F16Layer {
   uint8_t* wdown = nullptr;  // n = hidden, k = I
   float* g_in = nullptr;
   float* g_post = nullptr;
+  float gmax_in = 0.0f, gmax_post = 0.0f;  // max |gamma| (operand row-scale bounds)
   int rope = 0;
 };
 
@@ -268,7 +269,15 @@ struct qora_engine {
   float *f_logits = nullptr, *f_part = nullptr;
   size_t f_part_floats = 0;
   uint8_t* f_xt = nullptr;         // GEMM operand: activations as tiled f16 hi | lo rows
-  float* f_rowinv = nullptr;       // per-row power-of-two unscale of the operand
+  float *f_xss = nullptr, *f_xmx = nullptr;  // statistics of f_x rows [hidden/128][128]
+  float* f_hmx = nullptr;          // max |h| [I/64][128]
+  float* f_amx = nullptr;          // max |attention out| [kv heads][128]
+  float *f_att_part = nullptr, *f_att_ml = nullptr;  // split attention chunk partials
+  unsigned* f_att_cnt = nullptr;
+  unsigned* f_tcnt = nullptr;      // per-tile arrival counters of the fused GEMMs
+  unsigned* f_sync = nullptr;      // grid barrier + finished-tile counter
+  unsigned long long* f_amkey = nullptr;  // [128] greedy argmax keys
+  float f_gmax_final = 0.0f;
   int* f_err = nullptr;            // set by a GEMM whose bounded wait timed out
   uint8_t* lm_table = nullptr;   // embedding rows: hidden/2 packed bytes | hidden/32 f16 scales
   long long lm_row_bytes = 0;
@@ -997,92 +1006,112 @@ UmmaPlan umma_plan(int sms, int tiles, int chunks) {
   return p;
 }
 
-// Device scratch of the tensor-core GEMM: the staged operand, its row scales, the
-// partial slots and the timeout flag.
+// Device scratch shared by the fused tensor-core GEMMs of one engine (or one call).
 struct UmmaCtx {
   int sms;
   cudaStream_t stream;
   uint8_t* xt;
-  float* rowinv;
   float* part;
   size_t part_floats;
+  unsigned* tcnt;
+  size_t ntcnt;
+  unsigned* sync;
   int* err;
 };
 
-qora_status umma_norm_split(const UmmaCtx& u, const float* x, const float* gamma, int M, int K) {
-  const int R = (M + 7) / 8 * 8;
-  umma::norm_split_tiled_kernel<<<R, 256, 0, u.stream>>>(x, gamma, K, M, R, u.xt, u.rowinv);
-  QCUDA(cudaGetLastError());
-  return QORA_OK;
-}
+// Operand source of one fused GEMM: rows xin [M][ldx], RMSNorm with gamma when set, and
+// the producer's statistics [st_n][128].
+struct UmmaIn {
+  const float* xin;
+  int ldx;
+  const float* gamma;
+  float gmax;
+  const float* st_ss;
+  const float* st_mx;
+  int st_n;
+};
 
-// Y = X . W for the M rows staged in u.xt (umma_norm_split), followed by the slot
-// reduction with epilogue `mode` into y (row stride ldy).
-qora_status umma_gemm(const UmmaCtx& u, const uint8_t* wt, int N, int K, int M, int mode, const float* res, float* y,
-                      int ldy) {
+// One fused GEMM (umma::fused_gemm_kernel): N outputs over K, M rows, epilogue in `ep`
+// (its output fields filled by the caller), cooperative launch on u.stream.
+qora_status umma_fused(const UmmaCtx& u, const uint8_t* wt, int N, int K, int M, const UmmaIn& in,
+                       umma::FusedArgs ep) {
   const int R = (M + 7) / 8 * 8, tiles = N / umma::kTileN, chunks = K / umma::kChunkK;
   const UmmaPlan p = umma_plan(u.sms, tiles, chunks);
-  if ((size_t)p.G * p.maxseg * R * umma::kTileN > u.part_floats)
-    return fail(QORA_ERR_INVALID, "GEMM partials exceed the scratch (%d x %d x %d)", p.G, p.maxseg, R);
-  umma::GemmArgs g{};
-  g.w = wt;
-  g.x = u.xt;
-  g.row_inv = u.rowinv;
-  g.part = u.part;
-  g.tiles = tiles;
-  g.chunks = chunks;
-  g.R = R;
-  g.stages = umma::gemm_stages(R);
-  g.maxseg = p.maxseg;
-  g.err = u.err;
-  g.timeout_ns = 2000000000ull;
-  umma::umma_gemm_kernel<<<p.G, umma::kThreads, umma::gemm_smem(R, g.stages), u.stream>>>(g);
-  QCUDA(cudaGetLastError());
-  umma::ReduceArgs r{};
-  r.part = u.part;
-  r.tiles = tiles;
-  r.chunks = chunks;
-  r.R = R;
-  r.M = M;
-  r.maxseg = p.maxseg;
-  r.G = p.G;
-  r.N = N;
-  r.mode = mode;
-  r.res = res;
-  r.y = y;
-  r.ldy = ldy;
-  const long long total = (long long)M * (mode == 2 ? N / 2 : N);
-  const int blocks = (int)std::min<long long>((total + 255) / 256, 8LL * u.sms);
-  umma::reduce_tiles_kernel<<<blocks, 256, 0, u.stream>>>(r);
-  QCUDA(cudaGetLastError());
+  if ((size_t)p.G * p.maxseg * R * umma::kTileN > u.part_floats || (size_t)tiles > u.ntcnt || p.G > umma::kMaxContrib)
+    return fail(QORA_ERR_INVALID, "GEMM plan exceeds the scratch (%d x %d x %d, %d tiles)", p.G, p.maxseg, R, tiles);
+  umma::FusedArgs a = ep;
+  a.w = wt;
+  a.tiles = tiles;
+  a.chunks = chunks;
+  a.M = M;
+  a.R = R;
+  a.stages = umma::gemm_stages(R);
+  a.maxseg = p.maxseg;
+  a.xin = in.xin;
+  a.ldx = in.ldx;
+  a.gamma = in.gamma;
+  a.gmax = in.gmax;
+  a.st_ss = in.st_ss;
+  a.st_mx = in.st_mx;
+  a.st_n = in.st_n;
+  a.xt = u.xt;
+  a.part = u.part;
+  a.tile_cnt = u.tcnt;
+  a.sync = u.sync;
+  a.err = u.err;
+  a.timeout_ns = 2000000000ull;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(p.G);
+  cfg.blockDim = dim3(umma::kThreads);
+  cfg.dynamicSmemBytes = umma::gemm_smem(R, a.stages);
+  cfg.stream = u.stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  QCUDA(cudaLaunchKernelEx(&cfg, umma::fused_gemm_kernel, a));
   return QORA_OK;
 }
 
-// opt the GEMM kernel in to its largest shared-memory footprint (once per process)
+// opt the GEMM kernel in to its largest shared-memory footprint and check that one CTA
+// fits on every SM (the cooperative launch needs all CTAs resident)
 qora_status umma_attrs() {
   int maxsm = 0;
   for (int r = 8; r <= umma::kMaxRows; r += 8) maxsm = std::max(maxsm, (int)umma::gemm_smem(r, umma::gemm_stages(r)));
-  QCUDA(cudaFuncSetAttribute(umma::umma_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, maxsm));
+  QCUDA(cudaFuncSetAttribute(umma::fused_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, maxsm));
+  int blocks = 0;
+  QCUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, umma::fused_gemm_kernel, umma::kThreads, maxsm));
+  if (blocks < 1) return fail(QORA_ERR_UNSUPPORTED, "tensor-core GEMM does not fit on an SM");
   return QORA_OK;
 }
 
 UmmaCtx umma_ctx(const qora_engine* e) {
-  return UmmaCtx{e->sms, e->stream, e->f_xt, e->f_rowinv, e->f_part, e->f_part_floats, e->f_err};
+  const int V = (int)e->vocab;
+  return UmmaCtx{e->sms, e->stream, e->f_xt, e->f_part, e->f_part_floats, e->f_tcnt,
+                 (size_t)std::max(V, 2 * (int)e->inter) / umma::kTileN + 1, e->f_sync, e->f_err};
 }
 
-// Copy one f16 matrix view to the device and re-tile it into tiles [t0, t0 + n/128) of
-// dst (a matrix of k/64 chunks per tile). kmajor: the view is [n][k] (the embedding).
-qora_status f16_tile_upload(qora_engine* e, const qora_matrix_view& m, bool kmajor, int t0, uint8_t* dst,
-                            __half* tmp) {
+// Copy one f16 matrix view to the device and re-tile it: channel n goes to tile
+// t0 + n / group, row o0 + n % group, of dst (k/64 chunks per tile). kmajor: the view is
+// [n][k] (the embedding).
+qora_status f16_tile_upload(qora_engine* e, const qora_matrix_view& m, bool kmajor, int t0, int group, int o0,
+                            uint8_t* dst, __half* tmp) {
   const size_t elems = (size_t)m.k * m.n;
   QCUDA(cudaMemcpy(tmp, m.data, elems * 2, cudaMemcpyHostToDevice));
   const int K = kmajor ? (int)m.n : (int)m.k, N = kmajor ? (int)m.k : (int)m.n;
   const long long units = (long long)N * (K / 8);
   const int blocks = (int)std::min<long long>((units + 255) / 256, 16LL * e->sms);
-  umma::tile_weights_kernel<<<blocks, 256>>>(tmp, (long long)m.n, kmajor ? 1 : 0, K, N, 0, t0, dst);
+  umma::tile_weights_kernel<<<blocks, 256>>>(tmp, (long long)m.n, kmajor ? 1 : 0, K, N, 0, t0, group, o0, dst);
   QCUDA(cudaGetLastError());
   QCUDA(cudaDeviceSynchronize());
   return QORA_OK;
+}
+
+float max_abs_f16(const uint16_t* h, size_t n) {
+  float m = 0.0f;
+  for (float v : f16_to_f32(h, n)) m = std::max(m, std::fabs(v));
+  return m;
 }
 
 // Upload the F16 weights (exact copies; q|k|v and gate|up joined along n) and size the
@@ -1125,25 +1154,30 @@ qora_status f16_engine_init(qora_engine* e, const qora_weights_view* w) {
     const qora_layer_view& L = w->layers[i];
     F16Layer& d = e->fl[i];
     QCHECK(e->alloc(&d.wqkv, (size_t)H * e->f_nqkv * 2));
-    QCHECK(f16_tile_upload(e, L.q_proj, false, 0, d.wqkv, tmp));
-    QCHECK(f16_tile_upload(e, L.k_proj, false, nq / TN, d.wqkv, tmp));
-    QCHECK(f16_tile_upload(e, L.v_proj, false, (nq + nkvw) / TN, d.wqkv, tmp));
+    QCHECK(f16_tile_upload(e, L.q_proj, false, 0, TN, 0, d.wqkv, tmp));
+    QCHECK(f16_tile_upload(e, L.k_proj, false, nq / TN, TN, 0, d.wqkv, tmp));
+    QCHECK(f16_tile_upload(e, L.v_proj, false, (nq + nkvw) / TN, TN, 0, d.wqkv, tmp));
     QCHECK(e->alloc(&d.wo, (size_t)nq * H * 2));
-    QCHECK(f16_tile_upload(e, L.o_proj, false, 0, d.wo, tmp));
+    QCHECK(f16_tile_upload(e, L.o_proj, false, 0, TN, 0, d.wo, tmp));
+    // gate|up interleaved per tile: rows 0-63 gate channels 64t.., rows 64-127 the same up
+    // channels, so one tile holds both operands of its 64 SwiGLU outputs
     QCHECK(e->alloc(&d.wgu, (size_t)H * 2 * I * 2));
-    QCHECK(f16_tile_upload(e, L.gate_proj, false, 0, d.wgu, tmp));
-    QCHECK(f16_tile_upload(e, L.up_proj, false, I / TN, d.wgu, tmp));
+    QCHECK(f16_tile_upload(e, L.gate_proj, false, 0, 64, 0, d.wgu, tmp));
+    QCHECK(f16_tile_upload(e, L.up_proj, false, 0, 64, 64, d.wgu, tmp));
     QCHECK(e->alloc(&d.wdown, (size_t)I * H * 2));
-    QCHECK(f16_tile_upload(e, L.down_proj, false, 0, d.wdown, tmp));
+    QCHECK(f16_tile_upload(e, L.down_proj, false, 0, TN, 0, d.wdown, tmp));
     std::vector<float> g1 = f16_to_f32(L.input_norm_gamma, H), g2 = f16_to_f32(L.post_attn_norm_gamma, H);
     QCHECK(e->alloc(&d.g_in, H));
     QCHECK(e->alloc(&d.g_post, H));
     QCHECK(upload(e, d.g_in, g1.data(), (size_t)H * 4));
     QCHECK(upload(e, d.g_post, g2.data(), (size_t)H * 4));
+    d.gmax_in = max_abs_f16(L.input_norm_gamma, H);
+    d.gmax_post = max_abs_f16(L.post_attn_norm_gamma, H);
     d.rope = w->no_rope_layers[i] ? 1 : 0;
   }
   QCHECK(e->alloc(&e->f_lm, (size_t)V * H * 2));
-  QCHECK(f16_tile_upload(e, w->embed, true, 0, e->f_lm, tmp));
+  QCHECK(f16_tile_upload(e, w->embed, true, 0, TN, 0, e->f_lm, tmp));
+  e->f_gmax_final = max_abs_f16(w->final_norm_gamma, H);
   std::vector<float> fg = f16_to_f32(w->final_norm_gamma, H);
   QCHECK(e->alloc(&e->final_gamma, H));
   QCHECK(upload(e, e->final_gamma, fg.data(), (size_t)H * 4));
@@ -1169,7 +1203,21 @@ qora_status f16_engine_init(qora_engine* e, const qora_weights_view* w) {
   QCHECK(e->alloc(&e->f_h, R * I));
   QCHECK(e->alloc(&e->f_logits, R * V));
   QCHECK(e->alloc(&e->f_xt, kmax * R * 2 * 2));
-  QCHECK(e->alloc(&e->f_rowinv, R));
+  QCHECK(e->alloc(&e->f_xss, (size_t)(H / umma::kTileN) * R));
+  QCHECK(e->alloc(&e->f_xmx, (size_t)(H / umma::kTileN) * R));
+  QCHECK(e->alloc(&e->f_hmx, (size_t)(I / 64) * R));
+  QCHECK(e->alloc(&e->f_amx, (size_t)e->nkv * R));
+  QCHECK(e->alloc(&e->f_att_part, R * e->nkv * f16b::kAttSplits * 4 * kHeadDim));
+  QCHECK(e->alloc(&e->f_att_ml, R * e->nkv * f16b::kAttSplits * 4 * 2));
+  QCHECK(e->alloc(&e->f_att_cnt, R * e->nkv));
+  QCUDA(cudaMemset(e->f_att_cnt, 0, R * e->nkv * sizeof(unsigned)));
+  const size_t ntc = (size_t)std::max(V, 2 * I) / umma::kTileN + 1;
+  QCHECK(e->alloc(&e->f_tcnt, ntc));
+  QCUDA(cudaMemset(e->f_tcnt, 0, ntc * sizeof(unsigned)));
+  QCHECK(e->alloc(&e->f_sync, 4));
+  QCUDA(cudaMemset(e->f_sync, 0, 4 * sizeof(unsigned)));
+  QCHECK(e->alloc(&e->f_amkey, R));
+  QCUDA(cudaMemset(e->f_amkey, 0, R * sizeof(unsigned long long)));
   QCHECK(e->alloc(&e->f_err, 1));
   QCUDA(cudaMemset(e->f_err, 0, sizeof(int)));
   e->logits = e->f_logits;
@@ -1180,50 +1228,101 @@ qora_status f16_engine_init(qora_engine* e, const qora_weights_view* w) {
 
 // Launch count of f16_forward (reported as the engine's launches per step).
 int f16_launches(const qora_engine* e, bool lm) {
-  // embedding; per layer 4 x (norm/split, GEMM, reduce) + RoPE/KV + attention; final
-  // norm/split, lm_head GEMM, argmax
-  return 1 + 14 * (int)e->num_layers + (lm ? 3 : 0);
+  // embedding; per layer the q|k|v, o, gate|up and down GEMMs and attention; lm_head
+  return 1 + 5 * (int)e->num_layers + (lm ? 1 : 0);
 }
 
 // The layer stack over the M rows of kv's row table, then (rows [lm0, M) only) the final
 // RMSNorm, the tied lm_head into f_logits rows [0, M - lm0) and the greedy argmax.
 // Mirrors forward_decode_raw / raw_prefill (src/gemv.rs:872-1019, :1027-1190) per row.
 qora_status f16_forward(qora_engine* e, qora_kv* kv, int M, int lm0) {
-  const int H = (int)e->hidden, nq = (int)e->nh * kHeadDim, nkvw = (int)e->nkv * kHeadDim, I = (int)e->inter;
-  const int V = (int)e->vocab, NQKV = e->f_nqkv;
+  const int H = (int)e->hidden, nq = (int)e->nh * kHeadDim, I = (int)e->inter;
+  const int V = (int)e->vocab, NQKV = e->f_nqkv, R = f16b::kMaxRows;
   const f16b::RowInfo ri = f16b::row_info(kv->rows);
   cudaStream_t s = e->stream;
   const UmmaCtx u = umma_ctx(e);
-  f16b::embed_rows_kernel<<<M, 256, 0, s>>>(e->f_lm, H, V, ri, e->f_x);
+  const int xt_n = H / umma::kTileN;
+  f16b::embed_rows_kernel<<<dim3(xt_n, M), 128, 0, s>>>(e->f_lm, H, V, ri, e->f_x, e->f_xss, e->f_xmx);
   QCUDA(cudaGetLastError());
   const long long hs = (long long)kv->max_seq * kHeadDim, ss = (long long)kv->seq_stride();
   for (uint32_t li = 0; li < e->num_layers; ++li) {
     const F16Layer& d = e->fl[li];
     float* kc = kv->k + li * kv->layer_stride();
     float* vc = kv->v + li * kv->layer_stride();
-    // attention block
-    QCHECK(umma_norm_split(u, e->f_x, d.g_in, M, H));
-    QCHECK(umma_gemm(u, d.wqkv, NQKV, H, M, 0, nullptr, e->f_qkv, NQKV));
-    f16b::rope_kv_kernel<<<M, 256, 0, s>>>(e->f_qkv, nq, nkvw, d.rope, e->rope_cos, e->rope_sin, ri, kc, vc, ss, hs);
-    QCUDA(cudaGetLastError());
-    f16b::attention_rows_kernel<<<dim3(e->nkv, M), f16b::kAttnRowThreads, 0, s>>>(e->f_qkv, nq, nkvw, kGrp, ri, kc,
-                                                                                  vc, ss, hs, e->f_attn);
-    QCUDA(cudaGetLastError());
-    QCHECK(umma_norm_split(u, e->f_attn, nullptr, M, nq));
-    QCHECK(umma_gemm(u, d.wo, H, nq, M, 1, e->f_x, e->f_x, H));
-    // MLP block
-    QCHECK(umma_norm_split(u, e->f_x, d.g_post, M, H));
-    QCHECK(umma_gemm(u, d.wgu, 2 * I, H, M, 2, nullptr, e->f_h, I));
-    QCHECK(umma_norm_split(u, e->f_h, nullptr, M, I));
-    QCHECK(umma_gemm(u, d.wdown, H, I, M, 1, e->f_x, e->f_x, H));
+    // RMSNorm + q|k|v + RoPE + KV append (q rows to f_qkv)
+    umma::FusedArgs a{};
+    a.ep = umma::kEpQKV;
+    a.y = e->f_qkv;
+    a.ldy = nq;
+    a.q_tiles = nq / umma::kTileN;
+    a.k_tiles = (int)e->nkv;
+    a.rope = d.rope;
+    a.cos_t = e->rope_cos;
+    a.sin_t = e->rope_sin;
+    a.rows = ri;
+    a.kc = kc;
+    a.vc = vc;
+    a.seq_stride = ss;
+    a.head_stride = hs;
+    QCHECK(umma_fused(u, d.wqkv, NQKV, H, M, UmmaIn{e->f_x, H, d.g_in, d.gmax_in, e->f_xss, e->f_xmx, xt_n}, a));
+    {
+      f16b::AttnRowsArgs at{};
+      at.q = e->f_qkv;
+      at.nq = nq;
+      at.nkv = (int)e->nkv;
+      at.rows = ri;
+      at.kc = kc;
+      at.vc = vc;
+      at.seq_stride = ss;
+      at.head_stride = hs;
+      at.out = e->f_attn;
+      at.st_mx = e->f_amx;
+      at.o_part = e->f_att_part;
+      at.ml_part = e->f_att_ml;
+      at.cnt = e->f_att_cnt;
+      f16b::attention_split_kernel<<<dim3(e->nkv, M, f16b::kAttSplits), f16b::kAttThreads, 0, s>>>(at);
+      QCUDA(cudaGetLastError());
+    }
+    // o_proj + residual (and the statistics of the new x)
+    a = umma::FusedArgs{};
+    a.ep = umma::kEpResidual;
+    a.y = e->f_x;
+    a.res = e->f_x;
+    a.ldy = H;
+    a.o_ss = e->f_xss;
+    a.o_mx = e->f_xmx;
+    QCHECK(umma_fused(u, d.wo, H, nq, M, UmmaIn{e->f_attn, nq, nullptr, 0.0f, nullptr, e->f_amx, (int)e->nkv}, a));
+    // RMSNorm + gate|up + SwiGLU
+    a = umma::FusedArgs{};
+    a.ep = umma::kEpSwiGLU;
+    a.y = e->f_h;
+    a.ldy = I;
+    a.o_mx = e->f_hmx;
+    QCHECK(umma_fused(u, d.wgu, 2 * I, H, M, UmmaIn{e->f_x, H, d.g_post, d.gmax_post, e->f_xss, e->f_xmx, xt_n}, a));
+    // down_proj + residual
+    a = umma::FusedArgs{};
+    a.ep = umma::kEpResidual;
+    a.y = e->f_x;
+    a.res = e->f_x;
+    a.ldy = H;
+    a.o_ss = e->f_xss;
+    a.o_mx = e->f_xmx;
+    QCHECK(umma_fused(u, d.wdown, H, I, M, UmmaIn{e->f_h, I, nullptr, 0.0f, nullptr, e->f_hmx, I / 64}, a));
   }
   if (lm0 < M) {
-    const int ml = M - lm0;
-    QCHECK(umma_norm_split(u, e->f_x + (size_t)lm0 * H, e->final_gamma, ml, H));
-    QCHECK(umma_gemm(u, e->f_lm, V, H, ml, 0, nullptr, e->f_logits, V));
-    f16b::argmax_rows_kernel<<<ml, 256, 0, s>>>(e->f_logits, V, kv->f_argmax);
-    QCUDA(cudaGetLastError());
+    // final RMSNorm + tied lm_head + greedy argmax for rows [lm0, M)
+    umma::FusedArgs a{};
+    a.ep = umma::kEpLogits;
+    a.y = e->f_logits;
+    a.ldy = V;
+    a.am_key = e->f_amkey;
+    a.am_out = kv->f_argmax;
+    QCHECK(umma_fused(u, e->f_lm, V, H, M - lm0,
+                      UmmaIn{e->f_x + (size_t)lm0 * H, H, e->final_gamma, e->f_gmax_final, e->f_xss + lm0,
+                             e->f_xmx + lm0, xt_n},
+                      a));
   }
+  (void)R;
   return QORA_OK;
 }
 
@@ -2217,7 +2316,7 @@ qora_status qora_f16_gemm(const float* d_x, const uint16_t* d_w, uint64_t m, uin
   int dev = 0;
   QCUDA(cudaGetDevice(&dev));
   const cudaStream_t s = (cudaStream_t)stream;
-  const int K = (int)k, N = (int)n, sms = sm_count(dev);
+  const int K = (int)k, N = (int)n, sms = sm_count(dev), R = umma::kMaxRows;
   const UmmaPlan p = umma_plan(sms, N / umma::kTileN, K / umma::kChunkK);
   struct Scratch {
     std::vector<void*> ptrs;
@@ -2227,28 +2326,37 @@ qora_status qora_f16_gemm(const float* d_x, const uint16_t* d_w, uint64_t m, uin
   } sc;
   auto grab = [&](size_t bytes, void** out) -> qora_status {
     QCUDA(cudaMalloc(out, std::max<size_t>(bytes, 16)));
+    QCUDA(cudaMemset(*out, 0, std::max<size_t>(bytes, 16)));
     sc.ptrs.push_back(*out);
     return QORA_OK;
   };
-  void *wt = nullptr, *xt = nullptr, *rowinv = nullptr, *part = nullptr, *err = nullptr;
+  void *wt = nullptr, *xt = nullptr, *mx = nullptr, *part = nullptr, *tcnt = nullptr, *sync = nullptr, *err = nullptr;
+  const size_t tiles = (size_t)N / umma::kTileN;
   QCHECK(grab((size_t)K * N * 2, &wt));
-  QCHECK(grab((size_t)K * umma::kMaxRows * 4, &xt));
-  QCHECK(grab(umma::kMaxRows * 4, &rowinv));
-  const size_t part_floats = (size_t)p.G * p.maxseg * umma::kMaxRows * umma::kTileN;
+  QCHECK(grab((size_t)K * R * 4, &xt));
+  QCHECK(grab((size_t)R * 4, &mx));
+  const size_t part_floats = (size_t)p.G * p.maxseg * R * umma::kTileN;
   QCHECK(grab(part_floats * 4, &part));
+  QCHECK(grab(tiles * 4, &tcnt));
+  QCHECK(grab(16, &sync));
   QCHECK(grab(sizeof(int), &err));
-  QCUDA(cudaMemset(err, 0, sizeof(int)));
   QCHECK(umma_attrs());
   const long long units = (long long)N * (K / 8);
   umma::tile_weights_kernel<<<(int)std::min<long long>((units + 255) / 256, 16LL * sms), 256, 0, s>>>(
-      reinterpret_cast<const __half*>(d_w), N, 0, K, N, 0, 0, static_cast<uint8_t*>(wt));
+      reinterpret_cast<const __half*>(d_w), N, 0, K, N, 0, 0, umma::kTileN, 0, static_cast<uint8_t*>(wt));
   QCUDA(cudaGetLastError());
-  const UmmaCtx u{sms, s, static_cast<uint8_t*>(xt), static_cast<float*>(rowinv), static_cast<float*>(part),
-                  part_floats, static_cast<int*>(err)};
+  const UmmaCtx u{sms, s, static_cast<uint8_t*>(xt), static_cast<float*>(part), part_floats,
+                  static_cast<unsigned*>(tcnt), tiles, static_cast<unsigned*>(sync), static_cast<int*>(err)};
   for (uint64_t m0 = 0; m0 < m; m0 += umma::kMaxRows) {
     const int mb = (int)std::min<uint64_t>(umma::kMaxRows, m - m0);
-    QCHECK(umma_norm_split(u, d_x + m0 * k, nullptr, mb, K));
-    QCHECK(umma_gemm(u, static_cast<uint8_t*>(wt), N, K, mb, 0, nullptr, d_y + m0 * n, N));
+    umma::row_max_kernel<<<mb, 256, 0, s>>>(d_x + m0 * k, K, static_cast<float*>(mx));
+    QCUDA(cudaGetLastError());
+    umma::FusedArgs a{};
+    a.ep = umma::kEpStore;
+    a.y = d_y + m0 * n;
+    a.ldy = N;
+    QCHECK(umma_fused(u, static_cast<uint8_t*>(wt), N, K, mb,
+                      UmmaIn{d_x + m0 * k, K, nullptr, 0.0f, nullptr, static_cast<float*>(mx), 1}, a));
   }
   int herr = 0;
   QCUDA(cudaMemcpyAsync(&herr, err, sizeof(int), cudaMemcpyDeviceToHost, s));

@@ -1,28 +1,35 @@
-// umma_gemm.cuh — F16-weight GEMM on the 5th-generation tensor cores (tcgen05 + TMEM)
-// for the batched paths: Y[rows][N] = X[rows][K] . W[K][N] with W f16 and X f32.
+// umma_gemm.cuh — F16-weight GEMMs of the batched paths on the 5th-generation tensor
+// cores (tcgen05 + TMEM), with the surrounding per-row work fused in:
+//   Y[rows][N] = op( prologue(X)[rows][K] . W[K][N] )
 //
 // Operands. W is re-tiled once at load into 128-channel x 64-k tiles of 16 KB, each in
 // the UMMA "K-major, no swizzle" canonical layout (8x8 core matrices of 128 contiguous
 // bytes; 8-row groups 1024 B apart, k-groups 128 B apart), stored tile-major so one
-// 16 KB bulk copy moves one tile chunk. X is written by its producer (norm_split_tiled)
-// in the same layout per 64-k chunk, as 2R rows: rows 0..R-1 the f16 "hi" terms of the
-// rows (after a per-row power-of-two scale), rows R..2R-1 the f16 "lo" terms
-// (x - hi). One MMA (M=128 channels, N=2R, K=16) multiplies both; the epilogue adds
-// the hi and lo columns in f32 and undoes the row scale, so each product carries ~22
-// bits of x, and the weights are exact.
+// 16 KB bulk copy moves one tile chunk. The activation operand is built by the GEMM's
+// own prologue: every CTA writes a slice of it (per row: optional RMSNorm with the row's
+// inverse RMS from the producer's per-tile statistics, a power-of-two row scale, then
+// f16 hi = f16(y) and lo = f16(y - hi)) into a global staging buffer in the same tile
+// layout as 2R rows (hi rows, then lo rows); a grid barrier (cooperative launch) then
+// opens the activation copies, while the weight copies of the first ring stages are
+// already in flight. One MMA (M=128 channels, N=2R, K=16) multiplies both halves; the
+// drain adds the hi and lo columns in f32 and undoes the row scale, so every product
+// carries ~22 bits of x, and the weights are exact.
 //
-// Work split. The (tile, k-chunk) units of one GEMM are cut into gridDim.x equal
-// contiguous ranges (one persistent CTA per SM). A CTA's range covers a few "segments"
-// (one tile's chunk run each); each segment accumulates in TMEM and is written to its
-// own partial slot [R][128]. reduce_tiles_kernel then sums a tile's slots in CTA order
-// (deterministic) and applies the epilogue (residual add / SwiGLU).
+// Work split. The (tile, k-chunk) units are cut into gridDim.x equal contiguous ranges
+// (one persistent CTA per SM). A CTA's range covers a few segments (one tile's chunk run
+// each); each segment accumulates in TMEM (double-buffered) and is drained to its own
+// partial slot [R][128]. The CTA that completes a tile's last slot (per-tile counter,
+// self-resetting) sums the slots in CTA order (deterministic) and applies the fused
+// epilogue: store; q|k|v with RoPE and the KV-cache append; residual add with the
+// row statistics the next RMSNorm needs; SwiGLU of the tile's gate|up halves; logits
+// with the greedy argmax (64-bit atomic max of ordered keys, finished by the last tile).
 //
-// Roles (192 threads): warp 0 lane 0 issues the bulk copies into an S-stage ring; warp 1
-// owns the TMEM allocation and its lane 0 issues the MMAs (tcgen05.commit releases each
-// stage and signals each finished accumulator); warps 2-5 drain the double-buffered
-// accumulators (tcgen05.ld) to the partial slots. Every wait is bounded (globaltimer):
-// on a timeout the CTA sets *err, stops issuing, waits for its copies and MMAs in
-// flight, frees its TMEM and returns.
+// Roles (192 threads): all warps build the operand slice; then warp 0 lane 0 issues the
+// bulk copies into an S-stage ring, warp 1 owns the TMEM allocation and its lane 0 issues
+// the MMAs (tcgen05.commit releases each stage and signals each finished accumulator),
+// warps 2-5 drain the accumulators and finish tiles. Every wait is bounded (globaltimer):
+// on a timeout the CTA sets *err, stops issuing, waits for its copies and MMAs in flight,
+// frees its TMEM and returns.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -116,13 +123,56 @@ QORA_DEV bool wait_bar(uint64_t* bar, uint32_t parity, unsigned long long limit_
   }
 }
 
-struct GemmArgs {
-  const uint8_t* w;         // tiled weights [tiles][chunks][16 KB]
-  const uint8_t* x;         // tiled activations [chunks][R * 256 B]
-  const float* row_inv;     // [R] power-of-two unscale of each row
-  float* part;              // [gridDim.x][maxseg][R][128] partial slots
-  int tiles, chunks, R, stages, maxseg;
-  int* err;                 // set to 1 when a wait timed out
+
+// Per-row table of the batched F16 steps (device memory, one per KV cache): seq | pos |
+// token (kMaxRows ints each), then the greedy step counter and an error flag.
+struct RowInfo {
+  int* seq;
+  int* pos;
+  int* token;
+  int* step;
+  int* error;
+};
+constexpr int kRowInts = 3 * kMaxRows + 2;
+__host__ __device__ inline RowInfo row_info(int* base) {
+  return RowInfo{base, base + kMaxRows, base + 2 * kMaxRows, base + 3 * kMaxRows, base + 3 * kMaxRows + 1};
+}
+
+enum : int { kEpStore = 0, kEpQKV = 1, kEpResidual = 2, kEpSwiGLU = 3, kEpLogits = 4 };
+
+struct FusedArgs {
+  // weights and work split
+  const uint8_t* w;          // tiled weights [tiles][chunks][16 KB]
+  int tiles, chunks, M, R, stages, maxseg;
+  // activation operand: xin rows [M][ldx] f32; RMSNorm with gamma (f32 [K]) when set
+  const float* xin;
+  int ldx;
+  const float* gamma;
+  float gmax;                // max |gamma|
+  const float* st_ss;        // producer statistics of xin: [st_n][kMaxRows] sum of squares
+  const float* st_mx;        //                               [st_n][kMaxRows] max |x|
+  int st_n;
+  uint8_t* xt;               // staged operand [chunks][R * 256 B]
+  float* part;               // partial slots [gridDim.x][maxseg][R][128]
+  unsigned* tile_cnt;        // [tiles] arrivals (self-resetting)
+  unsigned* sync;            // [0] grid barrier count, [1] generation, [2] tiles finished (logits)
+  // epilogue
+  int ep;
+  float* y;                  // output rows, row stride ldy
+  int ldy;
+  const float* res;          // kEpResidual: residual rows (may alias y)
+  float* o_ss;               // output statistics [tiles][kMaxRows] (residual: ss and mx; SwiGLU: mx)
+  float* o_mx;
+  int q_tiles, k_tiles, rope;  // kEpQKV: q heads, k heads (v heads follow), RoPE on/off
+  const float* cos_t;
+  const float* sin_t;
+  RowInfo rows;
+  float* kc;                 // KV caches of this layer: [batch][kv_heads][max_seq][128]
+  float* vc;
+  long long seq_stride, head_stride;
+  unsigned long long* am_key;  // kEpLogits: [M] ordered keys (zero between launches)
+  unsigned* am_out;          //            [M] greedy token of each row
+  int* err;
   unsigned long long timeout_ns;
 };
 
@@ -136,11 +186,175 @@ inline int gemm_stages(int R) {
   return s < 2 ? 2 : (s > 8 ? 8 : s);
 }
 
-__global__ void __launch_bounds__(kThreads, 1) umma_gemm_kernel(const GemmArgs a) {
-  extern __shared__ __align__(1024) uint8_t smem[];
+QORA_DEV void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
+// ordered key: larger value wins, ties go to the lower index, NaN never wins
+QORA_DEV unsigned long long am_key(float v, unsigned idx) {
+  if (v != v) return 0ull;
+  const unsigned b = __float_as_uint(v);
+  const unsigned o = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return ((unsigned long long)o << 32) | (unsigned long long)(0xFFFFFFFFu - idx);
+}
+
+// Grid-wide barrier of a cooperative launch (count + generation, self-resetting).
+QORA_DEV void grid_sync(unsigned* sync, unsigned long long limit_ns, volatile int* abort) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    volatile unsigned* gen = sync + 1;
+    const unsigned g0 = *gen;
+    __threadfence();
+    const unsigned old = atomicAdd(sync, 1u);
+    if (old == gridDim.x - 1) {
+      atomicExch(sync, 0u);
+      __threadfence();
+      atomicAdd(sync + 1, 1u);
+    } else {
+      const uint64_t t0 = ptx::globaltimer();
+      while (*gen == g0) {
+        if (ptx::globaltimer() - t0 > limit_ns) {
+          *abort = 1;
+          break;
+        }
+      }
+    }
+    __threadfence();
+  }
+  __syncthreads();
+}
+
+// Epilogue of one finished output pair: row m, channels j and j + 64 of tile t, with the
+// summed partials s0, s1. Warp-collective (all lanes of a warp share m).
+QORA_DEV void finish_pair(const FusedArgs& a, int t, int m, int j, float s0, float s1, float (*red)[2][kMaxRows],
+                          int wih, int lane) {
+  if (a.ep == kEpStore) {
+    float* yr = a.y + (size_t)m * a.ldy + t * kTileN;
+    yr[j] = s0;
+    yr[j + 64] = s1;
+  } else if (a.ep == kEpQKV) {
+    const int pos = a.rows.pos[m];
+    const bool isv = t >= a.q_tiles + a.k_tiles;
+    float y0 = s0, y1 = s1;
+    if (a.rope && !isv) {  // apply_rope_raw (src/gemv.rs:757-778)
+      const float cs = a.cos_t[(size_t)pos * kHalfDim + j], sn = a.sin_t[(size_t)pos * kHalfDim + j];
+      y0 = __fsub_rn(__fmul_rn(s0, cs), __fmul_rn(s1, sn));
+      y1 = __fadd_rn(__fmul_rn(s1, cs), __fmul_rn(s0, sn));
+    }
+    if (t < a.q_tiles) {
+      float* yr = a.y + (size_t)m * a.ldy + t * kTileN;
+      yr[j] = y0;
+      yr[j + 64] = y1;
+    } else {
+      const int kh = isv ? t - a.q_tiles - a.k_tiles : t - a.q_tiles;
+      float* dst = (isv ? a.vc : a.kc) + (long long)a.rows.seq[m] * a.seq_stride + kh * a.head_stride +
+                   (long long)pos * kHeadDim;
+      dst[j] = y0;
+      dst[j + 64] = y1;
+    }
+  } else if (a.ep == kEpResidual) {
+    const size_t n = (size_t)m * a.ldy + t * kTileN + j;
+    const float v0 = __fadd_rn(a.res[n], s0), v1 = __fadd_rn(a.res[n + 64], s1);
+    a.y[n] = v0;
+    a.y[n + 64] = v1;
+    float ss = __fmaf_rn(v1, v1, __fmul_rn(v0, v0)), mx = fmaxf(fabsf(v0), fabsf(v1));
+    ss = warp_sum(ss);
+    mx = warp_max(mx);
+    if (lane == 0) {
+      red[0][wih][m] = ss;
+      red[1][wih][m] = mx;
+    }
+  } else if (a.ep == kEpSwiGLU) {  // fused_gate_up_gemv's silu(g) * u (src/gemv.rs:497-499)
+    const float h = __fmul_rn(__fdiv_rn(s0, __fadd_rn(1.0f, expf(-s0))), s1);
+    a.y[(size_t)m * a.ldy + t * 64 + j] = h;
+    const float mx = warp_max(fabsf(h));
+    if (lane == 0) red[1][wih][m] = mx;
+  } else {  // kEpLogits
+    float* yr = a.y + (size_t)m * a.ldy + t * kTileN;
+    yr[j] = s0;
+    yr[j + 64] = s1;
+    unsigned long long k = am_key(s0, (unsigned)(t * kTileN + j));
+    const unsigned long long k1 = am_key(s1, (unsigned)(t * kTileN + j + 64));
+    if (k1 > k) k = k1;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long ok = __shfl_xor_sync(0xffffffffu, k, o);
+      if (ok > k) k = ok;
+    }
+    if (lane == 0) atomicMax(&a.am_key[m], k);
+  }
+}
+
+constexpr int kMaxContrib = 160;  // >= CTAs of a launch (one per SM)
+
+// Finish tile t (all its slots are written): 128 epilogue threads; thread e handles the
+// channel pair (j, j + 64), j = e % 64, for rows m = e / 64, e / 64 + 2, ...; the slots
+// are summed in CTA order, eight rows at a time so their loads overlap.
+QORA_DEV void finish_tile(const FusedArgs& a, int t, float (*red)[2][kMaxRows], long long* s_cb) {
+  const int e = threadIdx.x - 64, j = e & 63, half = e >> 6, wih = (e >> 5) & 1, lane = threadIdx.x & 31;
+  const long long T = (long long)a.tiles * a.chunks;
+  const int G = gridDim.x;
+  const int c0 = owner_of((long long)t * a.chunks, T, G), c1 = owner_of((long long)(t + 1) * a.chunks - 1, T, G);
+  const int nc = c1 - c0 + 1;
+  for (int i = e; i < nc; i += 128) {
+    const int c = c0 + i, seg = t - (int)(range_begin(c, T, G) / a.chunks);
+    s_cb[i] = (long long)(c * a.maxseg + seg) * a.R * kTileN;
+  }
+  ptx::named_bar(1, 128);
+  for (int mb = half; mb < a.M; mb += 16) {
+    float s0[8], s1[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      s0[r] = 0.0f;
+      s1[r] = 0.0f;
+    }
+    for (int i = 0; i < nc; ++i) {
+      const float* p = a.part + s_cb[i] + j;
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        const int m = mb + 2 * r;
+        if (m < a.M) {
+          s0[r] = __fadd_rn(s0[r], p[(size_t)m * kTileN]);
+          s1[r] = __fadd_rn(s1[r], p[(size_t)m * kTileN + 64]);
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      const int m = mb + 2 * r;
+      if (m < a.M) finish_pair(a, t, m, j, s0[r], s1[r], red, wih, lane);
+    }
+  }
+  ptx::named_bar(1, 128);
+  if (a.ep == kEpResidual || a.ep == kEpSwiGLU) {
+    for (int m = e; m < a.M; m += 128) {
+      if (a.ep == kEpResidual) a.o_ss[(size_t)t * kMaxRows + m] = __fadd_rn(red[0][0][m], red[0][1][m]);
+      a.o_mx[(size_t)t * kMaxRows + m] = fmaxf(red[1][0][m], red[1][1][m]);
+    }
+    ptx::named_bar(1, 128);
+  } else if (a.ep == kEpLogits) {
+    if (e == 0) {
+      __threadfence();
+      const unsigned old = atomicAdd(a.sync + 2, 1u);
+      if (old == (unsigned)a.tiles - 1) {
+        __threadfence();
+        for (int m = 0; m < a.M; ++m) {
+          const unsigned long long k = atomicExch(&a.am_key[m], 0ull);
+          a.am_out[m] = k ? 0xFFFFFFFFu - (unsigned)(k & 0xFFFFFFFFull) : 0u;
+        }
+        atomicExch(a.sync + 2, 0u);
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 1) fused_gemm_kernel(const FusedArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint32_t s_tmem;
-  __shared__ int s_abort;
-  const int S = a.stages, R = a.R, C = a.chunks;
+  __shared__ int s_abort, s_last, s_eok[4];
+  __shared__ float s_inv[kMaxRows], s_sc[kMaxRows], s_rowinv[kMaxRows];
+  __shared__ float s_red[2][2][kMaxRows];
+  __shared__ long long s_cb[kMaxContrib];
+  const int S = a.stages, R = a.R, C = a.chunks, M = a.M;
+  const int K = C * kChunkK;
   const uint32_t SB = stage_bytes(R);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * SB);
   uint64_t* empty = full + S;
@@ -150,6 +364,7 @@ __global__ void __launch_bounds__(kThreads, 1) umma_gemm_kernel(const GemmArgs a
   volatile int* abort = &s_abort;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t ncols = tmem_cols(R);
+  const unsigned long long lim = a.timeout_ns;
 
   if (threadIdx.x == 0) {
     s_abort = 0;
@@ -164,6 +379,34 @@ __global__ void __launch_bounds__(kThreads, 1) umma_gemm_kernel(const GemmArgs a
     ptx::mbar_init(fin, 1);
     ptx::fence_mbar_init();
   }
+  // row constants: inverse RMS (rms_norm_f16, src/gemv.rs:744-747) from the producer's
+  // per-tile sums of squares, and a power-of-two scale that puts the row's largest
+  // operand value in [2^13, 2^14) (from a bound: max|x| * inv * max|gamma|)
+  for (int m = threadIdx.x; m < R; m += blockDim.x) {
+    float inv = 1.0f, sc = 0.0f, ri = 0.0f;
+    if (m < M) {
+      float mx = 0.0f;
+      for (int t = 0; t < a.st_n; ++t) mx = fmaxf(mx, a.st_mx[(size_t)t * kMaxRows + m]);
+      float bound = mx;
+      if (a.gamma) {
+        float ss = 0.0f;
+        for (int t = 0; t < a.st_n; ++t) ss = __fadd_rn(ss, a.st_ss[(size_t)t * kMaxRows + m]);
+        inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), 1e-6f)));
+        bound = mx * inv * a.gmax;
+      }
+      int e = 0;
+      if (bound > 0.0f && bound < INFINITY) {
+        int ex;
+        frexpf(bound, &ex);
+        e = min(100, max(-100, 14 - ex));
+      }
+      sc = ldexpf(1.0f, e);
+      ri = ldexpf(1.0f, -e);
+    }
+    s_inv[m] = inv;
+    s_sc[m] = sc;
+    s_rowinv[m] = ri;
+  }
   if (warp == 1) {
     tmem_alloc(&s_tmem, ncols);
     tmem_relinquish();
@@ -175,21 +418,71 @@ __global__ void __launch_bounds__(kThreads, 1) umma_gemm_kernel(const GemmArgs a
 
   const long long T = (long long)a.tiles * C, G = gridDim.x;
   const long long b0 = range_begin(blockIdx.x, T, G), b1 = range_begin(blockIdx.x + 1, T, G);
-  const unsigned long long lim = a.timeout_ns;
+  const long long n_units = b1 - b0;
+  const int pre = (int)(n_units < S ? n_units : S);
+
+  // weight copies of the first ring stages go out before the operand exists
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < pre; ++i) {
+      const long long u = b0 + i, t = u / C, c = u % C;
+      ptx::mbar_arrive_expect_tx(&full[i], SB);
+      ptx::bulk_g2s(smem + (size_t)i * SB, a.w + ((size_t)t * C + c) * kATile, kATile, &full[i]);
+    }
+  }
+  // this CTA's slice of the operand: units (chunk c, row r, 8 k) in that order
+  {
+    const long long U = (long long)C * R * 8;
+    const long long u0 = range_begin(blockIdx.x, U, G), u1 = range_begin(blockIdx.x + 1, U, G);
+    for (long long u = u0 + threadIdx.x; u < u1; u += blockDim.x) {
+      const int g = (int)(u & 7), r = (int)((u >> 3) % R), c = (int)(u / (8LL * R));
+      const int k = c * kChunkK + g * 8;
+      uint8_t* base = a.xt + (size_t)c * R * 256;
+      uint4 hv = make_uint4(0, 0, 0, 0), lv = make_uint4(0, 0, 0, 0);
+      if (r < M) {
+        const float4* xp = reinterpret_cast<const float4*>(a.xin + (size_t)r * a.ldx + k);
+        const float4 x0 = xp[0], x1 = xp[1];
+        float v[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+        if (a.gamma) {
+          const float4* gp = reinterpret_cast<const float4*>(a.gamma + k);
+          const float4 g0 = gp[0], g1 = gp[1];
+          const float gv[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(__fmul_rn(v[i], s_inv[r]), gv[i]);
+        }
+        __align__(16) __half h[8], l[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float ys = __fmul_rn(v[i], s_sc[r]);
+          h[i] = __float2half_rn(ys);
+          l[i] = __float2half_rn(__fsub_rn(ys, __half2float(h[i])));
+        }
+        hv = *reinterpret_cast<const uint4*>(h);
+        lv = *reinterpret_cast<const uint4*>(l);
+      }
+      *reinterpret_cast<uint4*>(base + tile_off(r, g * 8)) = hv;
+      *reinterpret_cast<uint4*>(base + tile_off(R + r, g * 8)) = lv;
+    }
+  }
+  grid_sync(a.sync, lim, abort);
 
   if (warp == 0) {
     if (lane == 0) {
-      // ---- producer: bulk copies of weight + activation chunks into the ring
-      long long issued = 0;
-      for (long long u = b0; u < b1 && !*abort; ++u, ++issued) {
+      // ---- producer: activation copies of the pre-issued stages, then both per stage
+      fence_proxy_async_global();
+      long long issued = pre;
+      for (int i = 0; i < pre; ++i) {  // issued even after an abort, so those stages complete
+        const long long c = (b0 + i) % C;
+        ptx::bulk_g2s(smem + (size_t)i * SB + kATile, a.xt + (size_t)c * R * 256, (uint32_t)R * 256, &full[i]);
+      }
+      for (long long u = b0 + pre; u < b1 && !*abort; ++u, ++issued) {
         const int s = (int)(issued % S);
         const uint32_t k = (uint32_t)(issued / S);
-        if (k > 0 && !wait_bar(&empty[s], (k - 1) & 1, lim, abort)) break;
+        if (!wait_bar(&empty[s], (k - 1) & 1, lim, abort)) break;
         const long long t = u / C, c = u % C;
         uint8_t* st = smem + (size_t)s * SB;
         ptx::mbar_arrive_expect_tx(&full[s], SB);
         ptx::bulk_g2s(st, a.w + ((size_t)t * C + c) * kATile, kATile, &full[s]);
-        ptx::bulk_g2s(st + kATile, a.x + (size_t)c * R * 256, (uint32_t)R * 256, &full[s]);
+        ptx::bulk_g2s(st + kATile, a.xt + (size_t)c * R * 256, (uint32_t)R * 256, &full[s]);
       }
       // copies still in flight land before the CTA can exit
       const long long first = issued > S ? issued - S : 0;
@@ -234,17 +527,23 @@ __global__ void __launch_bounds__(kThreads, 1) umma_gemm_kernel(const GemmArgs a
       wait_bar(fin, 0, lim, &no_abort);
     }
   } else {
-    // ---- epilogue: accumulator (128 channels x [hi | lo] columns) -> partial slot
+    // ---- epilogue: accumulator (128 channels x [hi | lo] columns) -> partial slot, then
+    // the CTA that completes a tile finishes it
     const int q = warp & 3;  // TMEM lanes 32q .. 32q+31 = channels of this warp
+    const int e = threadIdx.x - 64;
     long long u = b0;
     int seg = 0;
-    while (u < b1 && !*abort) {
-      const long long t = u / C, e = (t + 1) * C < b1 ? (t + 1) * C : b1;
-      u = e;
+    while (u < b1) {
+      const long long t = u / C, end = (t + 1) * C < b1 ? (t + 1) * C : b1;
+      u = end;
       const int buf = seg & 1;
-      // every lane waits; the warp leaves together (tcgen05.ld is warp-collective)
+      // every lane waits; the four warps agree before any of them goes on, so that they
+      // all take the same named barriers (and tcgen05.ld stays warp-collective)
       const bool ok = wait_bar(&accf[buf], (seg >> 1) & 1, lim, abort);
-      if (!__all_sync(0xffffffffu, ok)) break;
+      const bool wok = __all_sync(0xffffffffu, ok);
+      if (lane == 0) s_eok[q] = wok ? 1 : 0;
+      ptx::named_bar(1, 128);
+      if (!(s_eok[0] && s_eok[1] && s_eok[2] && s_eok[3])) break;
       tc_fence_after();
       const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * 2 * R);
       float* dst = a.part + ((size_t)(blockIdx.x * a.maxseg + seg) * R) * kTileN + q * 32 + lane;
@@ -255,15 +554,37 @@ __global__ void __launch_bounds__(kThreads, 1) umma_gemm_kernel(const GemmArgs a
         tmem_wait_ld();
 #pragma unroll
         for (int r = 0; r < 8; ++r)
-          dst[(size_t)(j + r) * kTileN] = __fmul_rn(__fadd_rn(__uint_as_float(h[r]), __uint_as_float(l[r])),
-                                                    a.row_inv[j + r]);
+          dst[(size_t)(j + r) * kTileN] =
+              __fmul_rn(__fadd_rn(__uint_as_float(h[r]), __uint_as_float(l[r])), s_rowinv[j + r]);
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(&acce[buf]);
       ++seg;
+      // tile bookkeeping: contributors are the CTAs whose ranges meet tile t
+      const int c0 = owner_of(t * C, T, (int)G), c1 = owner_of((t + 1) * C - 1, T, (int)G);
+      ptx::named_bar(1, 128);  // this CTA's slot is written
+      bool last = true;
+      if (c1 > c0) {
+        if (e == 0) {
+          __threadfence();
+          const unsigned old = atomicAdd(&a.tile_cnt[t], 1u);
+          const bool l = old == (unsigned)(c1 - c0);
+          if (l) {
+            a.tile_cnt[t] = 0u;
+            __threadfence();
+          }
+          s_last = l ? 1 : 0;
+        }
+        ptx::named_bar(1, 128);
+        last = s_last != 0;
+      }
+      if (last) finish_tile(a, (int)t, s_red, s_cb);
     }
   }
+  // lanes 1-31 of warps 0 and 1 wait here for their role lane: every warp reaches the
+  // block barrier converged, so it counts each warp once
+  __syncwarp();
   tc_fence_before();
   __syncthreads();
   if (threadIdx.x == 0 && s_abort) atomicExch(a.err, 1);
@@ -273,107 +594,29 @@ __global__ void __launch_bounds__(kThreads, 1) umma_gemm_kernel(const GemmArgs a
   }
 }
 
-// ---------------------------------------------------------------- producers / consumers
-// Row m of X (RMSNorm'd with gamma when given, rms_norm_f16 src/gemv.rs:744-753) into the
-// tiled hi|lo operand for R padded rows: y is scaled by 2^e (e puts max|y| in
-// [2^13, 2^14)), hi = f16(y'), lo = f16(y' - hi); row_inv[m] = 2^-e. Rows M..R-1 are
-// zero. One CTA per padded row.
-__global__ void __launch_bounds__(256) norm_split_tiled_kernel(const float* x, const float* gamma, int K, int M,
-                                                                int R, uint8_t* xt, float* row_inv) {
+// Per-row statistics of rows stored flat [M][K] for the generic GEMM entry: max |x|
+// over the row (one statistics tile, no RMSNorm).
+__global__ void row_max_kernel(const float* x, int K, float* mx) {
   __shared__ float red[8];
   const int m = blockIdx.x;
-  const int nk8 = K / 8;
-  if (m >= M) {
-    for (int g = threadIdx.x; g < nk8; g += blockDim.x) {
-      const int k = g * 8, c = k / kChunkK, kk = k % kChunkK;
-      uint8_t* base = xt + (size_t)c * R * 256;
-      *reinterpret_cast<uint4*>(base + tile_off(m, kk)) = make_uint4(0, 0, 0, 0);
-      *reinterpret_cast<uint4*>(base + tile_off(R + m, kk)) = make_uint4(0, 0, 0, 0);
-    }
-    if (threadIdx.x == 0) row_inv[m] = 0.0f;
-    return;
-  }
-  const float* xr = x + (size_t)m * K;
-  float inv = 1.0f;
-  if (gamma) inv = rms_inv(xr, K, red);
-  float mx = 0.0f;
-  for (int k = threadIdx.x; k < K; k += blockDim.x) {
-    const float y = gamma ? __fmul_rn(__fmul_rn(xr[k], inv), gamma[k]) : xr[k];
-    mx = fmaxf(mx, fabsf(y));
-  }
-  mx = warp_max(mx);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+  float v = 0.0f;
+  for (int k = threadIdx.x; k < K; k += blockDim.x) v = fmaxf(v, fabsf(x[(size_t)m * K + k]));
+  v = warp_max(v);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
   __syncthreads();
-  mx = 0.0f;
-  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) mx = fmaxf(mx, red[w]);
-  int e = 0;
-  if (mx > 0.0f && mx < INFINITY) {
-    int ex;
-    frexpf(mx, &ex);  // mx in [2^(ex-1), 2^ex)
-    e = min(100, max(-100, 14 - ex));
-  }
-  const float sc = ldexpf(1.0f, e);
-  for (int g = threadIdx.x; g < nk8; g += blockDim.x) {
-    const int k = g * 8, c = k / kChunkK, kk = k % kChunkK;
-    __align__(16) __half hv[8], lv[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float y = gamma ? __fmul_rn(__fmul_rn(xr[k + i], inv), gamma[k + i]) : xr[k + i];
-      const float ys = __fmul_rn(y, sc);
-      hv[i] = __float2half_rn(ys);
-      lv[i] = __float2half_rn(__fsub_rn(ys, __half2float(hv[i])));
-    }
-    uint8_t* base = xt + (size_t)c * R * 256;
-    *reinterpret_cast<uint4*>(base + tile_off(m, kk)) = *reinterpret_cast<const uint4*>(hv);
-    *reinterpret_cast<uint4*>(base + tile_off(R + m, kk)) = *reinterpret_cast<const uint4*>(lv);
-  }
-  if (threadIdx.x == 0) row_inv[m] = ldexpf(1.0f, -e);
-}
-
-struct ReduceArgs {
-  const float* part;
-  int tiles, chunks, R, M, maxseg, G;
-  int N;            // GEMM outputs (tiles * 128)
-  int mode;         // 0: y = sum; 1: y = res + sum; 2: SwiGLU over gate|up halves
-  const float* res;
-  float* y;         // [M][N] (mode 2: [M][N/2])
-  int ldy;
-};
-
-__device__ inline float tile_sum(const ReduceArgs& a, int m, int n) {
-  const int t = n / kTileN, o = n % kTileN;
-  const long long T = (long long)a.tiles * a.chunks;
-  const int c0 = owner_of((long long)t * a.chunks, T, a.G), c1 = owner_of((long long)(t + 1) * a.chunks - 1, T, a.G);
-  float s = 0.0f;
-  for (int c = c0; c <= c1; ++c) {
-    const int seg = t - (int)(range_begin(c, T, a.G) / a.chunks);
-    s = __fadd_rn(s, a.part[((size_t)(c * a.maxseg + seg) * a.R + m) * kTileN + o]);
-  }
-  return s;
-}
-
-__global__ void reduce_tiles_kernel(const ReduceArgs a) {
-  const int cols = a.mode == 2 ? a.N / 2 : a.N;
-  const long long total = (long long)a.M * cols;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
-    const int m = (int)(i / cols), n = (int)(i - (long long)m * cols);
-    const float s = tile_sum(a, m, n);
-    float v;
-    if (a.mode == 2) {
-      const float u = tile_sum(a, m, n + cols);
-      v = __fmul_rn(__fdiv_rn(s, __fadd_rn(1.0f, expf(-s))), u);
-    } else {
-      v = a.mode == 1 ? __fadd_rn(a.res[(size_t)m * a.ldy + n], s) : s;
-    }
-    a.y[(size_t)m * a.ldy + n] = v;
+  if (threadIdx.x == 0) {
+    float r = 0.0f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) r = fmaxf(r, red[w]);
+    mx[m] = r;
   }
 }
 
 // One-time re-tiling of an f16 matrix into [tiles][chunks][16 KB] UMMA tiles. src is
-// N-major [K][ld] (columns col0..col0+N-1 taken) or K-major [N][ld]; the N channels land
-// in tiles t0.. of a matrix with `chunks` = K/64 chunks per tile.
+// N-major [K][ld] (columns col0..col0+N-1 taken) or K-major [N][ld]. Channel n lands in
+// tile t0 + n / group at row o0 + n % group (group 128: whole tiles; group 64: one half
+// of each tile, for the interleaved gate|up matrix).
 __global__ void tile_weights_kernel(const __half* src, long long ld, int kmajor, int K, int N, int col0,
-                                    int t0, uint8_t* dst) {
+                                    int t0, int group, int o0, uint8_t* dst) {
   const long long units = (long long)N * (K / 8);  // 16-byte output units: 8 k of one channel
   const int chunks = K / kChunkK;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < units; i += (long long)gridDim.x * blockDim.x) {
@@ -384,7 +627,7 @@ __global__ void tile_weights_kernel(const __half* src, long long ld, int kmajor,
 #pragma unroll
     for (int j = 0; j < 8; ++j)
       v[j] = kmajor ? src[(long long)n * ld + k + j] : src[(long long)(k + j) * ld + col0 + n];
-    const int t = t0 + n / kTileN, o = n % kTileN, c = k / kChunkK;
+    const int t = t0 + n / group, o = o0 + n % group, c = k / kChunkK;
     uint8_t* tile = dst + ((size_t)t * chunks + c) * kATile;
     *reinterpret_cast<uint4*>(tile + tile_off(o, k % kChunkK)) = *reinterpret_cast<const uint4*>(v);
   }
