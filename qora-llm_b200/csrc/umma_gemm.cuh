@@ -222,74 +222,122 @@ QORA_DEV void grid_sync(unsigned* sync, unsigned long long limit_ns, volatile in
   __syncthreads();
 }
 
-// Epilogue of one finished output pair: row m, channels j and j + 64 of tile t, with the
-// summed partials s0, s1. Warp-collective (all lanes of a warp share m).
-QORA_DEV void finish_pair(const FusedArgs& a, int t, int m, int j, float s0, float s1, float (*red)[2][kMaxRows],
-                          int wih, int lane) {
+// half-warp reductions (lanes 0-15 and 16-31 each hold one row)
+QORA_DEV float hw_sum(float v) {
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+QORA_DEV float hw_max(float v) {
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Epilogue of row m, channels j0..j0+3 and j0+64..j0+67 of tile t (s0 / s1: the summed
+// partials). Called by all lanes; rows are held by half-warps (q = lane % 16 picks j0 =
+// 4q), `act` false for rows past M. Statistics are reduced within the half-warp.
+QORA_DEV void finish_quad(const FusedArgs& a, int t, int m, int q, bool act, const float (&s0)[4],
+                          const float (&s1)[4]) {
+  const int j0 = 4 * q;
   if (a.ep == kEpStore) {
-    float* yr = a.y + (size_t)m * a.ldy + t * kTileN;
-    yr[j] = s0;
-    yr[j + 64] = s1;
-  } else if (a.ep == kEpQKV) {
-    const int pos = a.rows.pos[m];
-    const bool isv = t >= a.q_tiles + a.k_tiles;
-    float y0 = s0, y1 = s1;
-    if (a.rope && !isv) {  // apply_rope_raw (src/gemv.rs:757-778)
-      const float cs = a.cos_t[(size_t)pos * kHalfDim + j], sn = a.sin_t[(size_t)pos * kHalfDim + j];
-      y0 = __fsub_rn(__fmul_rn(s0, cs), __fmul_rn(s1, sn));
-      y1 = __fadd_rn(__fmul_rn(s1, cs), __fmul_rn(s0, sn));
+    if (act) {
+      float* yr = a.y + (size_t)m * a.ldy + t * kTileN + j0;
+      *reinterpret_cast<float4*>(yr) = make_float4(s0[0], s0[1], s0[2], s0[3]);
+      *reinterpret_cast<float4*>(yr + 64) = make_float4(s1[0], s1[1], s1[2], s1[3]);
     }
-    if (t < a.q_tiles) {
-      float* yr = a.y + (size_t)m * a.ldy + t * kTileN;
-      yr[j] = y0;
-      yr[j + 64] = y1;
-    } else {
-      const int kh = isv ? t - a.q_tiles - a.k_tiles : t - a.q_tiles;
-      float* dst = (isv ? a.vc : a.kc) + (long long)a.rows.seq[m] * a.seq_stride + kh * a.head_stride +
-                   (long long)pos * kHeadDim;
-      dst[j] = y0;
-      dst[j + 64] = y1;
+  } else if (a.ep == kEpQKV) {
+    if (act) {
+      const int pos = a.rows.pos[m];
+      const bool isv = t >= a.q_tiles + a.k_tiles;
+      float y0[4], y1[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        y0[i] = s0[i];
+        y1[i] = s1[i];
+        if (a.rope && !isv) {  // apply_rope_raw (src/gemv.rs:757-778)
+          const float cs = a.cos_t[(size_t)pos * kHalfDim + j0 + i], sn = a.sin_t[(size_t)pos * kHalfDim + j0 + i];
+          y0[i] = __fsub_rn(__fmul_rn(s0[i], cs), __fmul_rn(s1[i], sn));
+          y1[i] = __fadd_rn(__fmul_rn(s1[i], cs), __fmul_rn(s0[i], sn));
+        }
+      }
+      float* dst;
+      if (t < a.q_tiles) {
+        dst = a.y + (size_t)m * a.ldy + t * kTileN;
+      } else {
+        const int kh = isv ? t - a.q_tiles - a.k_tiles : t - a.q_tiles;
+        dst = (isv ? a.vc : a.kc) + (long long)a.rows.seq[m] * a.seq_stride + kh * a.head_stride +
+              (long long)pos * kHeadDim;
+      }
+      *reinterpret_cast<float4*>(dst + j0) = make_float4(y0[0], y0[1], y0[2], y0[3]);
+      *reinterpret_cast<float4*>(dst + j0 + 64) = make_float4(y1[0], y1[1], y1[2], y1[3]);
     }
   } else if (a.ep == kEpResidual) {
-    const size_t n = (size_t)m * a.ldy + t * kTileN + j;
-    const float v0 = __fadd_rn(a.res[n], s0), v1 = __fadd_rn(a.res[n + 64], s1);
-    a.y[n] = v0;
-    a.y[n + 64] = v1;
-    float ss = __fmaf_rn(v1, v1, __fmul_rn(v0, v0)), mx = fmaxf(fabsf(v0), fabsf(v1));
-    ss = warp_sum(ss);
-    mx = warp_max(mx);
-    if (lane == 0) {
-      red[0][wih][m] = ss;
-      red[1][wih][m] = mx;
+    float ss = 0.0f, mx = 0.0f;
+    if (act) {
+      float* yr = a.y + (size_t)m * a.ldy + t * kTileN + j0;
+      const float* rr = a.res + (size_t)m * a.ldy + t * kTileN + j0;
+      const float4 r0 = *reinterpret_cast<const float4*>(rr), r1 = *reinterpret_cast<const float4*>(rr + 64);
+      const float v0[4] = {__fadd_rn(r0.x, s0[0]), __fadd_rn(r0.y, s0[1]), __fadd_rn(r0.z, s0[2]), __fadd_rn(r0.w, s0[3])};
+      const float v1[4] = {__fadd_rn(r1.x, s1[0]), __fadd_rn(r1.y, s1[1]), __fadd_rn(r1.z, s1[2]), __fadd_rn(r1.w, s1[3])};
+      *reinterpret_cast<float4*>(yr) = make_float4(v0[0], v0[1], v0[2], v0[3]);
+      *reinterpret_cast<float4*>(yr + 64) = make_float4(v1[0], v1[1], v1[2], v1[3]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        ss = __fmaf_rn(v0[i], v0[i], ss);
+        ss = __fmaf_rn(v1[i], v1[i], ss);
+        mx = fmaxf(mx, fmaxf(fabsf(v0[i]), fabsf(v1[i])));
+      }
+    }
+    ss = hw_sum(ss);
+    mx = hw_max(mx);
+    if (act && q == 0) {
+      a.o_ss[(size_t)t * kMaxRows + m] = ss;
+      a.o_mx[(size_t)t * kMaxRows + m] = mx;
     }
   } else if (a.ep == kEpSwiGLU) {  // fused_gate_up_gemv's silu(g) * u (src/gemv.rs:497-499)
-    const float h = __fmul_rn(__fdiv_rn(s0, __fadd_rn(1.0f, expf(-s0))), s1);
-    a.y[(size_t)m * a.ldy + t * 64 + j] = h;
-    const float mx = warp_max(fabsf(h));
-    if (lane == 0) red[1][wih][m] = mx;
-  } else {  // kEpLogits
-    float* yr = a.y + (size_t)m * a.ldy + t * kTileN;
-    yr[j] = s0;
-    yr[j + 64] = s1;
-    unsigned long long k = am_key(s0, (unsigned)(t * kTileN + j));
-    const unsigned long long k1 = am_key(s1, (unsigned)(t * kTileN + j + 64));
-    if (k1 > k) k = k1;
+    float mx = 0.0f;
+    if (act) {
+      float h[4];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
+      for (int i = 0; i < 4; ++i) {
+        h[i] = __fmul_rn(__fdiv_rn(s0[i], __fadd_rn(1.0f, expf(-s0[i]))), s1[i]);
+        mx = fmaxf(mx, fabsf(h[i]));
+      }
+      *reinterpret_cast<float4*>(a.y + (size_t)m * a.ldy + t * 64 + j0) = make_float4(h[0], h[1], h[2], h[3]);
+    }
+    mx = hw_max(mx);
+    if (act && q == 0) a.o_mx[(size_t)t * kMaxRows + m] = mx;
+  } else {  // kEpLogits
+    unsigned long long k = 0ull;
+    if (act) {
+      float* yr = a.y + (size_t)m * a.ldy + t * kTileN + j0;
+      *reinterpret_cast<float4*>(yr) = make_float4(s0[0], s0[1], s0[2], s0[3]);
+      *reinterpret_cast<float4*>(yr + 64) = make_float4(s1[0], s1[1], s1[2], s1[3]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const unsigned long long k0 = am_key(s0[i], (unsigned)(t * kTileN + j0 + i));
+        const unsigned long long k1 = am_key(s1[i], (unsigned)(t * kTileN + j0 + 64 + i));
+        if (k0 > k) k = k0;
+        if (k1 > k) k = k1;
+      }
+    }
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) {
       const unsigned long long ok = __shfl_xor_sync(0xffffffffu, k, o);
       if (ok > k) k = ok;
     }
-    if (lane == 0) atomicMax(&a.am_key[m], k);
+    if (act && q == 0) atomicMax(&a.am_key[m], k);
   }
 }
 
 constexpr int kMaxContrib = 160;  // >= CTAs of a launch (one per SM)
 
-// Finish tile t (all its slots are written): 128 epilogue threads; thread e handles the
-// channel pair (j, j + 64), j = e % 64, for rows m = e / 64, e / 64 + 2, ...; the slots
-// are summed in CTA order, eight rows at a time so their loads overlap.
-QORA_DEV void finish_tile(const FusedArgs& a, int t, float (*red)[2][kMaxRows], long long* s_cb) {
-  const int e = threadIdx.x - 64, j = e & 63, half = e >> 6, wih = (e >> 5) & 1, lane = threadIdx.x & 31;
+// Finish tile t (all its slots are written): 128 epilogue threads, 16 per row (thread q
+// of a row owns channels 4q..4q+3 and 64+4q..64+4q+3), 8 rows per pass; each channel's
+// slots are summed in CTA order, eight contributors' loads in flight at a time.
+QORA_DEV void finish_tile(const FusedArgs& a, int t, long long* s_cb) {
+  const int e = threadIdx.x - 64, q = e & 15, rsub = e >> 4;
   const long long T = (long long)a.tiles * a.chunks;
   const int G = gridDim.x;
   const int c0 = owner_of((long long)t * a.chunks, T, G), c1 = owner_of((long long)(t + 1) * a.chunks - 1, T, G);
@@ -299,49 +347,45 @@ QORA_DEV void finish_tile(const FusedArgs& a, int t, float (*red)[2][kMaxRows], 
     s_cb[i] = (long long)(c * a.maxseg + seg) * a.R * kTileN;
   }
   ptx::named_bar(1, 128);
-  for (int mb = half; mb < a.M; mb += 16) {
-    float s0[8], s1[8];
+  for (int m0 = 0; m0 < a.M; m0 += 8) {
+    const int m = m0 + rsub;
+    const bool act = m < a.M;
+    float s0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, s1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (int i0 = 0; i0 < nc; i0 += 8) {
+      float4 v0[8], v1[8];
 #pragma unroll
-    for (int r = 0; r < 8; ++r) {
-      s0[r] = 0.0f;
-      s1[r] = 0.0f;
-    }
-    for (int i = 0; i < nc; ++i) {
-      const float* p = a.part + s_cb[i] + j;
-#pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        const int m = mb + 2 * r;
-        if (m < a.M) {
-          s0[r] = __fadd_rn(s0[r], p[(size_t)m * kTileN]);
-          s1[r] = __fadd_rn(s1[r], p[(size_t)m * kTileN + 64]);
-        }
+      for (int k = 0; k < 8; ++k) {
+        const bool ok = act && i0 + k < nc;
+        const float* p = a.part + s_cb[i0 + k < nc ? i0 + k : i0] + (size_t)(act ? m : 0) * kTileN + 4 * q;
+        v0[k] = ok ? __ldcg(reinterpret_cast<const float4*>(p)) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        v1[k] = ok ? __ldcg(reinterpret_cast<const float4*>(p + 64)) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       }
-    }
 #pragma unroll
-    for (int r = 0; r < 8; ++r) {
-      const int m = mb + 2 * r;
-      if (m < a.M) finish_pair(a, t, m, j, s0[r], s1[r], red, wih, lane);
+      for (int k = 0; k < 8; ++k)
+        if (i0 + k < nc) {
+          s0[0] = __fadd_rn(s0[0], v0[k].x);
+          s0[1] = __fadd_rn(s0[1], v0[k].y);
+          s0[2] = __fadd_rn(s0[2], v0[k].z);
+          s0[3] = __fadd_rn(s0[3], v0[k].w);
+          s1[0] = __fadd_rn(s1[0], v1[k].x);
+          s1[1] = __fadd_rn(s1[1], v1[k].y);
+          s1[2] = __fadd_rn(s1[2], v1[k].z);
+          s1[3] = __fadd_rn(s1[3], v1[k].w);
+        }
     }
+    finish_quad(a, t, m, q, act, s0, s1);
   }
-  ptx::named_bar(1, 128);
-  if (a.ep == kEpResidual || a.ep == kEpSwiGLU) {
-    for (int m = e; m < a.M; m += 128) {
-      if (a.ep == kEpResidual) a.o_ss[(size_t)t * kMaxRows + m] = __fadd_rn(red[0][0][m], red[0][1][m]);
-      a.o_mx[(size_t)t * kMaxRows + m] = fmaxf(red[1][0][m], red[1][1][m]);
-    }
-    ptx::named_bar(1, 128);
-  } else if (a.ep == kEpLogits) {
-    if (e == 0) {
+  ptx::named_bar(1, 128);  // s_cb is free again
+  if (a.ep == kEpLogits && e == 0) {
+    __threadfence();
+    const unsigned old = atomicAdd(a.sync + 2, 1u);
+    if (old == (unsigned)a.tiles - 1) {
       __threadfence();
-      const unsigned old = atomicAdd(a.sync + 2, 1u);
-      if (old == (unsigned)a.tiles - 1) {
-        __threadfence();
-        for (int m = 0; m < a.M; ++m) {
-          const unsigned long long k = atomicExch(&a.am_key[m], 0ull);
-          a.am_out[m] = k ? 0xFFFFFFFFu - (unsigned)(k & 0xFFFFFFFFull) : 0u;
-        }
-        atomicExch(a.sync + 2, 0u);
+      for (int m = 0; m < a.M; ++m) {
+        const unsigned long long k = atomicExch(&a.am_key[m], 0ull);
+        a.am_out[m] = k ? 0xFFFFFFFFu - (unsigned)(k & 0xFFFFFFFFull) : 0u;
       }
+      atomicExch(a.sync + 2, 0u);
     }
   }
 }
@@ -351,7 +395,6 @@ __global__ void __launch_bounds__(kThreads, 1) fused_gemm_kernel(const FusedArgs
   __shared__ uint32_t s_tmem;
   __shared__ int s_abort, s_last, s_eok[4];
   __shared__ float s_inv[kMaxRows], s_sc[kMaxRows], s_rowinv[kMaxRows];
-  __shared__ float s_red[2][2][kMaxRows];
   __shared__ long long s_cb[kMaxContrib];
   const int S = a.stages, R = a.R, C = a.chunks, M = a.M;
   const int K = C * kChunkK;
@@ -386,10 +429,12 @@ __global__ void __launch_bounds__(kThreads, 1) fused_gemm_kernel(const FusedArgs
     float inv = 1.0f, sc = 0.0f, ri = 0.0f;
     if (m < M) {
       float mx = 0.0f;
+#pragma unroll 8
       for (int t = 0; t < a.st_n; ++t) mx = fmaxf(mx, a.st_mx[(size_t)t * kMaxRows + m]);
       float bound = mx;
       if (a.gamma) {
         float ss = 0.0f;
+#pragma unroll 8
         for (int t = 0; t < a.st_n; ++t) ss = __fadd_rn(ss, a.st_ss[(size_t)t * kMaxRows + m]);
         inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), 1e-6f)));
         bound = mx * inv * a.gmax;
@@ -579,7 +624,7 @@ __global__ void __launch_bounds__(kThreads, 1) fused_gemm_kernel(const FusedArgs
         ptx::named_bar(1, 128);
         last = s_last != 0;
       }
-      if (last) finish_tile(a, (int)t, s_red, s_cb);
+      if (last) finish_tile(a, (int)t, s_cb);
     }
   }
   // lanes 1-31 of warps 0 and 1 wait here for their role lane: every warp reaches the
