@@ -5,6 +5,7 @@ at batch 1. A "step" is one decode step (one token through all 36 layers + lm_he
 argmax).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py --workload f16-batch [--batch 32] [--steps 128]
 
 Prints one JSON line (rank 0). `value` is device time (CUDA events on the engine's
 stream) of K greedy steps, each one launch of the persistent decode kernel, with the
@@ -306,6 +307,140 @@ def run_ours(args, rank, world, local_rank):
     return 0
 
 
+F16_METRIC = "decode tok/s (batched, SmolLM3-3B F16)"
+F16_PROMPT = 128
+def f16_bytes_per_step(layers=LAYERS):  # every f16 weight once (+ norms, negligible)
+    return 2 * (layers * 78_118_912 + VOCAB * HIDDEN)
+
+
+def synth_f16(layers=36):
+    import importlib
+    qf = importlib.import_module("qora-llm_b200").qora_format
+    return qf.synth_model(seed=SEED + 5, fmt=qf.FORMAT_F16, num_layers=layers, rope_rows=1024)
+
+
+def f16_prompts(batch):
+    return np.random.default_rng(2).integers(0, VOCAB, size=(batch, F16_PROMPT)).astype(np.uint32)
+
+
+def f16_cpu_sample(model, budget_s, threads):
+    """The reference's F16 CPU decode (forward_decode_raw with gemv_f16, oracle/) on this
+    host: steps of one sequence from an empty cache, bounded to ~budget_s. The CPU path has
+    no batching; B sequences cost B times one."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    oracle.set_threads(threads)
+    om = oracle.OracleModel(model)
+    kv = om.new_kv()
+    ids = f16_prompts(1)[0]
+    om.forward_decode(int(ids[0]), kv)  # warm-up
+    t0 = time.perf_counter()
+    n = 0
+    while n < len(ids) - 1 and (n < 2 or time.perf_counter() - t0 < budget_s):
+        om.forward_decode(int(ids[1 + n]), kv)
+        n += 1
+    dt = time.perf_counter() - t0
+    om.close()
+    return n / dt, n
+
+
+def run_f16(args, rank, world, local_rank):
+    """B independent sequences, 128-token prompts, greedy batched
+    decode on one GPU (tcgen05 GEMMs)."""
+    if world > 1:
+        if rank == 0:
+            print(json.dumps({"metric": F16_METRIC, "unavailable": "tensor parallelism of F16 engines is not in this build"}))
+        return 0
+    B, K, W = args.batch, args.steps, args.warmup
+    threads = os.cpu_count() or 1
+    model = synth_f16(args.layers)
+    if args.impl == "reference":
+        v, n = f16_cpu_sample(model, args.cpu_seconds, threads)
+        line = {"impl": "reference", "metric": F16_METRIC, "value": v, "unit": "tok/s", "n_gpus": 1, "steps": n,
+                "warmup": 1, "ms_per_step": 1000.0 / v, "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random-init SmolLM3-3B F16)",
+                "config": {"workload": f"config 5: SmolLM3-3B F16, batch {B}, 128-token prompts, greedy decode",
+                           "batch": B},
+                "cpu_baseline": {"value": v, "unit": "tok/s", "cores": threads, "kind": "port",
+                                 "sample": f"{n} forward_decode_raw steps of one sequence (the CPU path decodes "
+                                           f"sequences one at a time), {threads} threads", "cpu": cpu_model()},
+                "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return 0
+    import importlib
+    import torch
+    pkg = importlib.import_module("qora-llm_b200")
+    torch.cuda.set_device(local_rank)
+    eng = pkg.DecodeWeights(model=model, device=local_rank)
+    prompts = f16_prompts(B)
+    cap = F16_PROMPT + W + K + 8
+
+    def prefilled():
+        kv = eng.new_kv(cap, batch=B)
+        firsts = [eng.prefill(kv, prompts[b], want_logits=False, seq=b)[0] for b in range(B)]
+        return kv, firsts
+
+    # ---- device-timed batched greedy decode (value)
+    kv, firsts = prefilled()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    kv_p, _ = prefilled()
+    torch.cuda.synchronize()
+    prefill_s = time.perf_counter() - t0
+    kv_p.close()
+    warm = eng.generate_greedy_batch(kv, firsts, W)
+    nxt = warm[-1]
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clk:
+        _, ms = eng.generate_greedy_batch(kv, nxt, K, timed=True)
+    torch.cuda.synchronize()
+    value = B * K / (ms / 1000.0)
+    # ---- end to end through the C ABI: host tokens in, host argmax out, every step
+    kv2, firsts2 = prefilled()
+    t = np.asarray(firsts2, np.uint32)
+    for _ in range(W):
+        t, _ = eng.decode_batch(kv2, t)
+    t0 = time.perf_counter()
+    for _ in range(K):
+        t, _ = eng.decode_batch(kv2, t)
+    e2e_s = time.perf_counter() - t0
+    e2e = B * K / e2e_s
+    peak, peak_kind = peaks()
+    mean_pos = F16_PROMPT + W + (K - 1) / 2.0 + 1
+    step_bytes = f16_bytes_per_step(args.layers) + B * kv_bytes_per_pos(args.layers) * mean_pos
+    achieved = step_bytes / (ms / K / 1000.0) / 1e9
+    line = {
+        "metric": F16_METRIC, "value": value, "unit": "tok/s", "n_gpus": 1, "steps": K, "warmup": W,
+        "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f16 weights x f32 activations (f16 hi+lo split), f32 accumulate",
+        "data": "synthetic (seeded random-init SmolLM3-3B F16 weights, random prompt ids)",
+        "config": {"workload": f"config 5: SmolLM3-3B F16 (36 layers, vocab 128256), batch {B}, "
+                               f"{F16_PROMPT}-token prompts, greedy decode",
+                   "batch": B, "prompt": F16_PROMPT, "layers": args.layers, "kv_len_mean": mean_pos,
+                   "parallelism": "single GPU", "bytes_per_step": step_bytes,
+                   "l2": f"inputs larger than L2: {f16_bytes_per_step(args.layers) / 1e9:.2f} GB of weights "
+                         "streamed per step",
+                   "prefill_tok_s": B * F16_PROMPT / prefill_s},
+        "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4 * B, "d2h_bytes_per_step": 4 * B},
+        "gpu_launches": (eng.launches_per_step() + 1) * K,
+        "roofline": dict(bound="hbm", achieved=achieved, peak=peak, peak_kind=f"{peak_kind} hbm_gbs (copy)",
+                         unit="GB/s", frac=achieved / peak, traffic=None,
+                         kernel="whole batched decode step (4 tcgen05 GEMMs + attention per layer, lm_head)",
+                         bytes_per_launch=step_bytes, us_per_launch=1000 * ms / K, launches_timed=K),
+        "clocks": clk.summary(),
+    }
+    if not args.no_cpu_baseline:
+        v, n = f16_cpu_sample(model, args.cpu_seconds, threads)
+        line["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": threads, "kind": "port",
+                                "sample": f"{n} forward_decode_raw steps of one F16 sequence, {threads} threads "
+                                          f"(the CPU path has no batching)", "cpu": cpu_model()}
+    kv.close()
+    kv2.close()
+    eng.close()
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -314,6 +449,9 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--workload", choices=("q4", "f16-batch"), default="q4",
+                    help="q4: config 3 batch-1 decode (the headline); f16-batch: config 5")
+    ap.add_argument("--batch", type=int, default=32, help="sequences for --workload f16-batch")
     ap.add_argument("--layers", type=int, default=36,
                     help="decoder layers of the synthetic model (36 = SmolLM3-3B; fewer only for "
                          "small profiling captures, never for a reported number)")
@@ -323,6 +461,8 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.workload == "f16-batch":
+        return run_f16(args, rank, world, local_rank)
     if args.impl == "reference":
         return run_reference(args, rank)
     return run_ours(args, rank, world, local_rank)

@@ -97,6 +97,7 @@ struct AttnRowsArgs {
 __global__ void __launch_bounds__(kAttThreads) attention_split_kernel(const AttnRowsArgs a) {
   __shared__ __align__(16) float qs[4][kHeadDim];
   __shared__ float sc[4][kAttBlock];
+  __shared__ __align__(16) float s_o[4][4][kHeadDim];  // per-warp P.V partials [warp][head][dim]
   __shared__ float s_a[4], s_red[4];
   __shared__ int s_last;
   const int j = blockIdx.x, m = blockIdx.y, p = blockIdx.z;
@@ -115,7 +116,10 @@ __global__ void __launch_bounds__(kAttThreads) attention_split_kernel(const Attn
     for (int i = tid; i < 4 * kHeadDim; i += kAttThreads) qs[i / kHeadDim][i % kHeadDim] = q[i];
   }
   float mrun = -INFINITY, lrun = 0.0f;  // held by warp h = head h
-  float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // thread = dim d
+  // P.V accumulators: warp w sums its 16 positions of each block, lane l owns dims 4l..4l+3
+  float4 o4[4];
+#pragma unroll
+  for (int h = 0; h < 4; ++h) o4[h] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
   __syncthreads();
   const int pi = 16 * warp + (lane & 15), half = lane >> 4;
   for (int s0 = sb; s0 < se; s0 += kAttBlock) {
@@ -162,29 +166,42 @@ __global__ void __launch_bounds__(kAttThreads) attention_split_kernel(const Attn
       if (lane == 0) s_a[h] = al;
     }
     __syncthreads();
-    {  // P.V: thread d
-      const int d = tid;
+    {  // P.V: warp w takes positions 16w..16w+15 of the block (loads all in flight)
 #pragma unroll
-      for (int h = 0; h < 4; ++h) o[h] = __fmul_rn(o[h], s_a[h]);
-      const float* vr = V + (long long)s0 * kHeadDim + d;
-      int i = 0;
-      for (; i + 8 <= nn; i += 8) {
-        float v[8];
-#pragma unroll
-        for (int r = 0; r < 8; ++r) v[r] = vr[(long long)(i + r) * kHeadDim];
-#pragma unroll
-        for (int r = 0; r < 8; ++r)
-#pragma unroll
-          for (int h = 0; h < 4; ++h) o[h] = __fmaf_rn(sc[h][i + r], v[r], o[h]);
+      for (int h = 0; h < 4; ++h) {
+        const float al = s_a[h];
+        o4[h] = make_float4(__fmul_rn(o4[h].x, al), __fmul_rn(o4[h].y, al), __fmul_rn(o4[h].z, al),
+                            __fmul_rn(o4[h].w, al));
       }
-      for (; i < nn; ++i) {
-        const float v = vr[(long long)i * kHeadDim];
+      const float4* vr = reinterpret_cast<const float4*>(V + (long long)(s0 + 16 * warp) * kHeadDim) + lane;
+      float4 v[16];
 #pragma unroll
-        for (int h = 0; h < 4; ++h) o[h] = __fmaf_rn(sc[h][i], v, o[h]);
+      for (int i = 0; i < 16; ++i)
+        v[i] = 16 * warp + i < nn ? vr[i * (kHeadDim / 4)] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        if (16 * warp + i < nn) {
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            const float pw = sc[h][16 * warp + i];
+            o4[h].x = __fmaf_rn(pw, v[i].x, o4[h].x);
+            o4[h].y = __fmaf_rn(pw, v[i].y, o4[h].y);
+            o4[h].z = __fmaf_rn(pw, v[i].z, o4[h].z);
+            o4[h].w = __fmaf_rn(pw, v[i].w, o4[h].w);
+          }
+        }
       }
     }
     __syncthreads();
   }
+  // the four warps' partial sums, added in warp order: thread = dim d
+#pragma unroll
+  for (int h = 0; h < 4; ++h) *reinterpret_cast<float4*>(&s_o[warp][h][4 * lane]) = o4[h];
+  __syncthreads();
+  float o[4];
+#pragma unroll
+  for (int h = 0; h < 4; ++h)
+    o[h] = __fadd_rn(__fadd_rn(__fadd_rn(s_o[0][h][tid], s_o[1][h][tid]), s_o[2][h][tid]), s_o[3][h][tid]);
   const size_t slot = ((size_t)m * a.nkv + j) * kAttSplits;
   float* dst = a.out + (size_t)m * a.nq + (size_t)j * 4 * kHeadDim;
   float mxo = 0.0f;
