@@ -231,6 +231,37 @@ qora_status qora_q4_gate_up(const float* d_x, const uint8_t* d_gate_packed,
                             const uint16_t* d_up_scales, uint64_t k, uint64_t n,
                             float* d_out, void* stream);
 
+/* ------------------------------------------------------------------------------------
+ * On-device sampling (the sampling step of src/generate.rs:216-235): penalties, then
+ * sample_token_top_k (src/generate.rs:345-394) on the logits that stay on the device, so
+ * that only the token crosses PCIe when temperature > 0.
+ * ---------------------------------------------------------------------------------- */
+typedef struct qora_sampling {
+    float    temperature;         /* <= 0: greedy first maximum                        */
+    float    top_p;               /* nucleus cut within the top_k                      */
+    uint32_t top_k;               /* 1..1024 when temperature > 0                      */
+    float    repetition_penalty;  /* applied when > 1: each occurrence among the last
+                                     64 history tokens (apply_repetition_penalty)      */
+    float    presence_penalty;    /* applied when > 0: once per distinct history token
+                                     (apply_presence_penalty)                          */
+    int32_t  ban_token;           /* set to -inf after the penalties; -1: none (the
+                                     thinking branch bans EOS)                         */
+} qora_sampling;
+
+/* Sample from row `row` of the logits of the engine's last decode step or prefill
+ * (Q4 engines: row 0; F16 engines: the sequence's row of the last batched step, row 0
+ * after a prefill). history: host token ids (all generated tokens, oldest first).
+ * rng_state: the reference's xorshift64 Rng state (src/generate.rs:38-61), advanced by
+ * one draw only when the reference draws. Synchronises the engine's stream. */
+qora_status qora_sample(qora_engine* engine, uint32_t row, const uint32_t* history,
+                        uint32_t n_history, const qora_sampling* params,
+                        uint64_t* rng_state, uint32_t* token_out);
+
+/* The same on a caller's device logits [vocab] and device history (kernel level). */
+qora_status qora_sample_logits(const float* d_logits, uint32_t vocab, const uint32_t* d_history,
+                               uint32_t n_history, const qora_sampling* params,
+                               uint64_t* rng_state, uint32_t* token_out, void* stream);
+
 /* F16 GEMM y[m][n] = x[m][k] . W[k][n] on the tcgen05 tensor cores (replaces `gemm_f16`,
  * src/gemv.rs:571-588, and `gemv_f16` at m = 1, src/gemv.rs:534-567). W is the
  * reference's row-major [k][n] f16 bit patterns; k must be a multiple of 64 and n of 128.

@@ -75,6 +75,10 @@ def lib():
         "orc_lm_head_q4": (None, [_f32p, _u8p, _u16p, _sz, _sz, _f32p]),
         "orc_lm_head_f16": (None, [_f32p, _u16p, _sz, _sz, _f32p]),
         "orc_argmax": (C.c_uint32, [_f32p, _sz]),
+        "orc_rng_next_f32": (C.c_float, [C.POINTER(C.c_uint64)]),
+        "orc_sample_top_k": (C.c_uint32, [_f32p, _sz, C.c_float, C.c_float, _sz, C.POINTER(C.c_uint64)]),
+        "orc_sample": (C.c_uint32, [_f32p, _sz, _u32p, _sz, C.c_float, C.c_float, _sz, C.c_float, C.c_float,
+                                    C.c_int64, C.POINTER(C.c_uint64)]),
         "orc_forward_decode": (C.c_int, [C.c_void_p, C.c_uint32, C.c_void_p, _f32p]),
         "orc_layer_forward": (C.c_int, [C.c_void_p, C.c_uint32, _f32p, C.c_void_p]),
         "orc_prefill": (C.c_int, [C.c_void_p, _u32p, _sz, C.c_void_p, _f32p]),
@@ -186,6 +190,18 @@ def argmax(logits):
 
 
 # ------------------------------------------------------------------ model level
+def sample(logits, history, temperature, top_p, top_k, repetition_penalty=1.0, presence_penalty=0.0,
+           ban=-1, state=1):
+    """One sampling step of the reference generation loop (penalties, then
+    sample_token_top_k, src/generate.rs:64-92, :345-394). Returns (token, new_state)."""
+    hist = np.ascontiguousarray(history, dtype=np.uint32)
+    st = C.c_uint64(int(state))
+    tok = lib().orc_sample(f32(logits), len(logits), hist, hist.size, float(temperature), float(top_p),
+                           int(top_k), float(repetition_penalty), float(presence_penalty), int(ban),
+                           C.byref(st))
+    return int(tok), int(st.value)
+
+
 class OracleModel:
     """A model resident in the oracle (copied from a qora_format.Model or a file)."""
 

@@ -844,6 +844,95 @@ uint32_t orc_argmax(const float* logits, size_t n) {
   return (uint32_t)best;
 }
 
+// Rng::next_f32 (src/generate.rs:54-60): xorshift64, top 24 bits / 2^24
+float orc_rng_next_f32(uint64_t* state) {
+  uint64_t s = *state;
+  s ^= s << 13;
+  s ^= s >> 7;
+  s ^= s << 17;
+  *state = s;
+  return (float)(s >> 40) / 16777216.0f;
+}
+
+// apply_repetition_penalty (src/generate.rs:64-79): every occurrence in the last 64
+// history tokens, in order
+void orc_repetition_penalty(float* logits, size_t n, const uint32_t* hist, size_t nh, float penalty) {
+  if (penalty <= 1.0f) return;
+  const size_t window = std::min<size_t>(nh, 64);
+  for (size_t i = nh - window; i < nh; ++i) {
+    const size_t idx = hist[i];
+    if (idx < n) {
+      if (logits[idx] > 0.0f)
+        logits[idx] /= penalty;
+      else
+        logits[idx] *= penalty;
+    }
+  }
+}
+
+// apply_presence_penalty (src/generate.rs:82-92): once per distinct history token
+void orc_presence_penalty(float* logits, size_t n, const uint32_t* hist, size_t nh, float penalty) {
+  if (penalty <= 0.0f || nh == 0) return;
+  std::vector<bool> seen(n, false);
+  for (size_t i = 0; i < nh; ++i)
+    if (hist[i] < n) seen[hist[i]] = true;
+  for (size_t i = 0; i < n; ++i)
+    if (seen[i]) logits[i] -= penalty;
+}
+
+// sample_token_top_k (src/generate.rs:345-394): greedy when temperature <= 0, else
+// top-k by a stable descending sort, softmax at 1/temperature against the global
+// maximum, top-p cut on the cumulative sum, one draw of the generator.
+uint32_t orc_sample_top_k(const float* logits, size_t n, float temperature, float top_p, size_t top_k,
+                          uint64_t* state) {
+  if (temperature <= 0.0f) return orc_argmax(logits, n);
+  const float inv_temp = 1.0f / temperature;
+  float max_logit = -INFINITY;
+  for (size_t i = 0; i < n; ++i) max_logit = std::fmax(max_logit, logits[i]);
+  std::vector<std::pair<uint32_t, float>> idx(n);
+  for (size_t i = 0; i < n; ++i) idx[i] = {(uint32_t)i, logits[i]};
+  std::stable_sort(idx.begin(), idx.end(), [](const std::pair<uint32_t, float>& a,
+                                              const std::pair<uint32_t, float>& b) { return a.second > b.second; });
+  const size_t k = top_k > 0 ? std::min(top_k, n) : n;
+  std::vector<std::pair<uint32_t, float>> probs(k);
+  for (size_t i = 0; i < k; ++i) probs[i] = {idx[i].first, std::exp((idx[i].second - max_logit) * inv_temp)};
+  float sum = 0.0f;
+  for (auto& p : probs) sum += p.second;
+  if (sum <= 0.0f) return probs[0].first;
+  const float inv = 1.0f / sum;
+  for (auto& p : probs) p.second *= inv;
+  float cumsum = 0.0f;
+  size_t cutoff = probs.size();
+  for (size_t i = 0; i < probs.size(); ++i) {
+    cumsum += probs[i].second;
+    if (cumsum >= top_p) {
+      cutoff = i + 1;
+      break;
+    }
+  }
+  float total = 0.0f;
+  for (size_t i = 0; i < cutoff; ++i) total += probs[i].second;
+  if (total <= 0.0f) return probs[0].first;
+  const float rand_val = orc_rng_next_f32(state) * total;
+  float accum = 0.0f;
+  for (size_t i = 0; i < cutoff; ++i) {
+    accum += probs[i].second;
+    if (accum >= rand_val) return probs[i].first;
+  }
+  return probs[0].first;
+}
+
+// One sampling step of the generation loop (src/generate.rs:216-235, final-answer branch
+// and the thinking branch's banned token): penalties on a copy, then sample_token_top_k.
+uint32_t orc_sample(const float* logits, size_t n, const uint32_t* hist, size_t nh, float temperature, float top_p,
+                    size_t top_k, float repetition_penalty, float presence_penalty, int64_t ban, uint64_t* state) {
+  std::vector<float> l(logits, logits + n);
+  orc_repetition_penalty(l.data(), n, hist, nh, repetition_penalty);
+  orc_presence_penalty(l.data(), n, hist, nh, presence_penalty);
+  if (ban >= 0 && (size_t)ban < n) l[ban] = -INFINITY;
+  return orc_sample_top_k(l.data(), n, temperature, top_p, top_k, state);
+}
+
 int orc_layer_forward(const orc_model* m, uint32_t li, float* x, orc_kv* kv) {
   if (li >= m->num_layers) return 1;
   const Layer& L = m->layers[li];

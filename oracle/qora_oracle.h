@@ -96,6 +96,18 @@ void  orc_lm_head_f16(const float* x, const uint16_t* w, size_t vocab, size_t hi
                       float* logits);
 /* greedy branch of sample_token_top_k (src/generate.rs:346-352) */
 uint32_t orc_argmax(const float* logits, size_t n);
+/* Rng::next_f32 (src/generate.rs:54-60) */
+float orc_rng_next_f32(uint64_t* state);
+/* apply_repetition_penalty / apply_presence_penalty (src/generate.rs:64-92), in place */
+void orc_repetition_penalty(float* logits, size_t n, const uint32_t* hist, size_t nh, float penalty);
+void orc_presence_penalty(float* logits, size_t n, const uint32_t* hist, size_t nh, float penalty);
+/* sample_token_top_k (src/generate.rs:345-394) */
+uint32_t orc_sample_top_k(const float* logits, size_t n, float temperature, float top_p, size_t top_k,
+                          uint64_t* state);
+/* penalties (repetition, presence, banned token) on a copy, then sample_token_top_k */
+uint32_t orc_sample(const float* logits, size_t n, const uint32_t* hist, size_t nh, float temperature,
+                    float top_p, size_t top_k, float repetition_penalty, float presence_penalty, int64_t ban,
+                    uint64_t* state);
 
 /* ---- model-level ---- */
 /* forward_decode_raw (src/gemv.rs:872-1019); logits [vocab] */

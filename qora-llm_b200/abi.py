@@ -36,6 +36,13 @@ class EngineOptions(C.Structure):
                 ("tp_size", C.c_int32), ("tp_rank", C.c_int32)]
 
 
+class Sampling(C.Structure):
+    """qora_sampling (include/qora_cuda.h)."""
+    _fields_ = [("temperature", C.c_float), ("top_p", C.c_float), ("top_k", C.c_uint32),
+                ("repetition_penalty", C.c_float), ("presence_penalty", C.c_float),
+                ("ban_token", C.c_int32)]
+
+
 def _ptr(a: np.ndarray | None):
     if a is None:
         return None

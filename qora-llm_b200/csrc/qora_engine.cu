@@ -32,6 +32,7 @@
 #include "umma_gemm.cuh"
 #include "megakernel.cuh"
 #include "q4_gemv.cuh"
+#include "sampling.cuh"
 #include "small_kernels.cuh"
 
 using namespace qora;
@@ -279,6 +280,12 @@ struct qora_engine {
   unsigned long long* f_amkey = nullptr;  // [128] greedy argmax keys
   float f_gmax_final = 0.0f;
   int* f_err = nullptr;            // set by a GEMM whose bounded wait timed out
+  // on-device sampling scratch (allocated on first use)
+  float* smp_work = nullptr;       // [vocab] penalised logits
+  unsigned* smp_hist = nullptr;    // history tokens
+  size_t smp_hist_cap = 0;
+  smp::Out* smp_out = nullptr;
+  smp::Out* smp_out_host = nullptr;  // pinned
   uint8_t* lm_table = nullptr;   // embedding rows: hidden/2 packed bytes | hidden/32 f16 scales
   long long lm_row_bytes = 0;
   float* final_gamma = nullptr;
@@ -408,6 +415,7 @@ qora_engine::~qora_engine() {
   kvs.clear();
   if (!tp_opened.empty()) cudaSetDevice(device);
   for (void* p : tp_opened) cudaIpcCloseMemHandle(p);
+  if (smp_out_host) cudaFreeHost(smp_out_host);
   for (void* p : allocs) cudaFree(p);
   if (stream) cudaStreamDestroy(stream);
 }
@@ -2304,6 +2312,84 @@ qora_status qora_q4_lm_head(const float* d_x, const uint8_t* d_packed, const uin
   a.part_i = sc->lm_i;
   a.counter = sc->lm_c;
   return launch_lm_head((int)hidden, a, ctas, (cudaStream_t)stream);
+}
+
+namespace {
+qora_status sample_params(const qora_sampling* p, uint32_t vocab, smp::Params* out) {
+  if (!p) return fail(QORA_ERR_INVALID, "NULL sampling parameters");
+  if (vocab == 0 || vocab > (uint32_t)smp::kMaxVocabBits)
+    return fail(QORA_ERR_UNSUPPORTED, "vocab %u (at most %d for on-device sampling)", vocab, smp::kMaxVocabBits);
+  if (p->temperature > 0.0f && (p->top_k == 0 || p->top_k > (uint32_t)smp::kMaxTopK))
+    return fail(QORA_ERR_UNSUPPORTED, "top_k %u: on-device sampling takes 1..%d", p->top_k, smp::kMaxTopK);
+  out->temperature = p->temperature;
+  out->top_p = p->top_p;
+  out->top_k = (int)std::min<uint32_t>(p->top_k, vocab);
+  out->repetition_penalty = p->repetition_penalty;
+  out->presence_penalty = p->presence_penalty;
+  out->ban = p->ban_token;
+  return QORA_OK;
+}
+}  // namespace
+
+qora_status qora_sample(qora_engine* e, uint32_t row, const uint32_t* history, uint32_t n_history,
+                        const qora_sampling* params, uint64_t* rng_state, uint32_t* token_out) {
+  if (!e || !rng_state || !token_out || (!history && n_history)) return fail(QORA_ERR_INVALID, "NULL argument");
+  smp::Params sp{};
+  QCHECK(sample_params(params, e->vocab, &sp));
+  const uint32_t rows = e->format == QORA_FORMAT_F16 ? (uint32_t)f16b::kMaxRows : 1u;
+  if (row >= rows) return fail(QORA_ERR_RANGE, "logits row %u", row);
+  QCUDA(cudaSetDevice(e->device));
+  if (!e->smp_work) {
+    QCHECK(e->alloc(&e->smp_work, e->vocab));
+    QCHECK(e->alloc(&e->smp_out, 1));
+    QCUDA(cudaMallocHost(&e->smp_out_host, sizeof(smp::Out)));
+  }
+  if (n_history > e->smp_hist_cap) {
+    const size_t cap = std::max<size_t>(n_history, 4096);
+    QCHECK(e->alloc(&e->smp_hist, cap));
+    e->smp_hist_cap = cap;
+  }
+  if (n_history)
+    QCUDA(cudaMemcpyAsync(e->smp_hist, history, (size_t)n_history * 4, cudaMemcpyHostToDevice, e->stream));
+  const float* logits = e->logits + (size_t)row * e->vocab;
+  smp::sample_kernel<<<1, smp::kThreads, 0, e->stream>>>(logits, (int)e->vocab, e->smp_hist, (int)n_history, sp,
+                                                        (unsigned long long)*rng_state, e->smp_work, e->smp_out);
+  QCUDA(cudaGetLastError());
+  QCUDA(cudaMemcpyAsync(e->smp_out_host, e->smp_out, sizeof(smp::Out), cudaMemcpyDeviceToHost, e->stream));
+  QCUDA(cudaStreamSynchronize(e->stream));
+  *token_out = e->smp_out_host->token;
+  *rng_state = e->smp_out_host->state;
+  return QORA_OK;
+}
+
+qora_status qora_sample_logits(const float* d_logits, uint32_t vocab, const uint32_t* d_history,
+                               uint32_t n_history, const qora_sampling* params, uint64_t* rng_state,
+                               uint32_t* token_out, void* stream) {
+  if (!d_logits || !rng_state || !token_out || (!d_history && n_history))
+    return fail(QORA_ERR_INVALID, "NULL argument");
+  smp::Params sp{};
+  QCHECK(sample_params(params, vocab, &sp));
+  const cudaStream_t s = (cudaStream_t)stream;
+  float* work = nullptr;
+  smp::Out* out = nullptr;
+  QCUDA(cudaMalloc(&work, (size_t)vocab * 4));
+  const cudaError_t ae = cudaMalloc(&out, sizeof(smp::Out));
+  if (ae != cudaSuccess) {
+    cudaFree(work);
+    return fail(QORA_ERR_OOM, "cudaMalloc: %s", cudaGetErrorString(ae));
+  }
+  smp::sample_kernel<<<1, smp::kThreads, 0, s>>>(d_logits, (int)vocab, d_history, (int)n_history, sp,
+                                                (unsigned long long)*rng_state, work, out);
+  cudaError_t ce = cudaGetLastError();
+  smp::Out h{};
+  if (ce == cudaSuccess) ce = cudaMemcpyAsync(&h, out, sizeof(h), cudaMemcpyDeviceToHost, s);
+  if (ce == cudaSuccess) ce = cudaStreamSynchronize(s);
+  cudaFree(work);
+  cudaFree(out);
+  if (ce != cudaSuccess) return fail(QORA_ERR_CUDA, "sampling: %s", cudaGetErrorString(ce));
+  *token_out = h.token;
+  *rng_state = h.state;
+  return QORA_OK;
 }
 
 qora_status qora_f16_gemm(const float* d_x, const uint16_t* d_w, uint64_t m, uint64_t k, uint64_t n,

@@ -66,6 +66,8 @@ SIGNATURES = {
     "qora_q4_gate_up": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _u64, _u64, _vp, _vp]),
     "qora_q4_lm_head": (C.c_int, [_vp, _vp, _vp, _u64, _u64, _vp, _vp, _vp]),
     "qora_f16_gemm": (C.c_int, [_vp, _vp, _u64, _u64, _u64, _vp, _vp]),
+    "qora_sample": (C.c_int, [_vp, _u32, _vp, _u32, _vp, _P(_u64), _P(_u32)]),
+    "qora_sample_logits": (C.c_int, [_vp, _u32, _vp, _u32, _vp, _P(_u64), _P(_u32), _vp]),
 }
 
 
@@ -240,6 +242,18 @@ class DecodeWeights:
         check(lib().qora_engine_get_trace(self.h, _ptr(out), out.size, C.byref(n)))
         return out
 
+    def sample(self, history, temperature: float, top_p: float, top_k: int,
+               repetition_penalty: float = 1.0, presence_penalty: float = 0.0, ban_token: int = -1,
+               state: int = 1, row: int = 0):
+        """Sample from the last step's logits on the device (qora_sample): the reference's
+        penalties + sample_token_top_k. Returns (token, new xorshift64 state)."""
+        hist = np.ascontiguousarray(history, dtype=np.uint32)
+        p = abi.Sampling(temperature, top_p, top_k, repetition_penalty, presence_penalty, ban_token)
+        st, tok = _u64(int(state)), _u32()
+        check(lib().qora_sample(self.h, int(row), _ptr(hist) if hist.size else None, hist.size, C.byref(p),
+                                C.byref(st), C.byref(tok)))
+        return tok.value, st.value
+
     def launches_per_step(self) -> int:
         n = _u32()
         check(lib().qora_engine_launches_per_step(self.h, C.byref(n)))
@@ -344,3 +358,13 @@ def q4_lm_head(x_ptr, packed_ptr, scales_ptr, vocab, hidden, logits_ptr, argmax_
 def f16_gemm(x_ptr, w_ptr, m, k, n, y_ptr, stream=None):
     """y[m][n] = x[m][k] . W[k][n], W f16 row-major (qora_f16_gemm, tcgen05)."""
     check(lib().qora_f16_gemm(x_ptr, w_ptr, m, k, n, y_ptr, _stream_ptr(stream)))
+
+
+def sample_logits(logits_ptr, vocab, history_ptr, n_history, temperature, top_p, top_k,
+                  repetition_penalty=1.0, presence_penalty=0.0, ban_token=-1, state=1, stream=None):
+    """qora_sample_logits on device pointers. Returns (token, new state)."""
+    p = abi.Sampling(temperature, top_p, top_k, repetition_penalty, presence_penalty, ban_token)
+    st, tok = _u64(int(state)), _u32()
+    check(lib().qora_sample_logits(logits_ptr, vocab, history_ptr, n_history, C.byref(p), C.byref(st),
+                                   C.byref(tok), _stream_ptr(stream)))
+    return tok.value, st.value

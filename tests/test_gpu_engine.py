@@ -185,3 +185,22 @@ def test_engine_destroyed_before_cache(pkg, small):
     with pytest.raises(pkg.QoraError, match="INVALID"):
         kv.import_layer(0, np.zeros((1, 256), np.float32), np.zeros((1, 256), np.float32))
     kv.close()
+
+
+def test_sample_on_device_matches_oracle(small_engine, orc):
+    """qora_sample on the Q4 engine's last-step logits (kept on the device) against the
+    oracle's sampling step on the same logits; the generator state threads through."""
+    w = small_engine
+    kv = w.new_kv(64)
+    prompt = np.random.default_rng(31).integers(0, w.vocab, size=7).astype(np.uint32)
+    first, _ = w.prefill(kv, prompt, want_logits=False)
+    hist = list(prompt) + [first]
+    tok, state = first, 0x2545F4914F6CDD1D
+    for _ in range(6):
+        am, logits = w.decode_step(kv, tok, want_logits=True)
+        got = w.sample(hist, 0.7, 0.9, 20, 1.1, 1.5, -1, state)
+        want = orc.sample(logits, hist, 0.7, 0.9, 20, 1.1, 1.5, -1, state)
+        assert got == want
+        assert w.sample([], 0.0, 1.0, 1)[0] == am
+        tok, state = got
+        hist.append(tok)

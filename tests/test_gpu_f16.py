@@ -153,3 +153,23 @@ def test_f16_kv_roundtrip_and_errors(pkg, f16_engine, f16_model):
         w.prefill(kv, [1, 2, 3], seq=2)  # no such sequence
     kv.reset(1)
     assert kv.length(1) == 0
+
+
+def test_f16_sample_from_batched_logits(f16_engine, orc):
+    """qora_sample on each row of a batched step's logits (left on the device) equals the
+    oracle's sampling step on the same logits read back."""
+    w = f16_engine
+    kv = w.new_kv(64, batch=3)
+    prompts = _prompts(w.vocab, [4, 9, 6], 21)
+    for b, p in enumerate(prompts):
+        w.prefill(kv, p, want_logits=False, seq=b)
+    am, lg = w.decode_batch(kv, [3, 4, 5], want_logits=True)
+    state = 0x9E3779B97F4A7C15
+    for b in range(3):
+        hist = np.concatenate([prompts[b], [am[b]]]).astype(np.uint32)
+        got = w.sample(hist, 0.6, 0.95, 20, 1.1, 1.5, -1, state, row=b)
+        want = orc.sample(lg[b], hist, 0.6, 0.95, 20, 1.1, 1.5, -1, state)
+        assert got == want, (b, got, want)
+        state = got[1]
+    # greedy through the same entry returns the step's argmax
+    assert w.sample([], 0.0, 1.0, 1, row=1)[0] == am[1]

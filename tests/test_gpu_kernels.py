@@ -183,3 +183,27 @@ def test_f16_gemm_shapes(pkg, qf, torch, rows, k, n):
     # per element: error within a small multiple of f32 rounding of |x|.|w|
     bound = np.abs(x.astype(np.float64)) @ np.abs(w)
     assert np.all(np.abs(y - ref) <= 1e-5 * bound + 1e-30)
+
+
+# ---------------------------------------------------------------- on-device sampling
+@pytest.mark.parametrize("params", [(0.0, 0.95, 20, 1.0, 0.0, -1), (0.6, 0.95, 20, 1.1, 1.5, -1),
+                                    (1.0, 1.0, 1, 1.0, 0.0, -1), (0.3, 0.5, 50, 1.3, 0.0, 7),
+                                    (1.5, 0.99, 1000, 1.0, 0.7, 3), (0.6, 0.95, 20, 1.1, 1.5, 128012)])
+def test_sample_logits_matches_oracle(pkg, orc, torch, params):
+    """qora_sample_logits against the oracle's restatement of the reference sampling step
+    (penalties, top-k/top-p, xorshift64 draw): same token, same generator state."""
+    t, tp, k, rp, pp, ban = params
+    rng = np.random.default_rng(int(k * 10 + t * 100))
+    for V in (128256, 997):
+        for it in range(6):
+            logits = (rng.standard_normal(V) * rng.uniform(0.5, 6)).astype(np.float32)
+            logits[int(rng.integers(0, V))] = logits.max()  # a tie for the first place
+            hist = rng.integers(0, V, size=int(rng.integers(0, 300))).astype(np.uint32)
+            if hist.size > 3:
+                hist[-2] = hist[-1]
+            b = ban if ban < V else -1
+            state = int(rng.integers(1, 2**63))
+            dl, dh = dev(torch, logits), dev(torch, hist.view(np.int32) if hist.size else np.zeros(1, np.int32))
+            got = pkg.engine.sample_logits(dl.data_ptr(), V, dh.data_ptr(), hist.size, t, tp, k, rp, pp, b, state)
+            want = orc.sample(logits, hist, t, tp, k, rp, pp, b, state)
+            assert got == want, (V, it, got, want)

@@ -222,3 +222,76 @@ def test_golden_fixtures(qf, orc):
     x = orc.gemv_q4(g["gemv_x"], model.layers[0].gate_proj)
     assert np.array_equal(x, g["gemv_y"])
     orc.set_threads(1)
+
+
+# ---------------------------------------------------------------- sampling (src/generate.rs)
+def _py_sample(logits, hist, temperature, top_p, top_k, rep, pres, ban, state):
+    """Independent restatement of the reference sampling step (f32 arithmetic via numpy
+    scalars): penalties (src/generate.rs:64-92), sample_token_top_k (:345-394), Rng (:38-61)."""
+    f = np.float32
+    l = np.array(logits, np.float32)
+    if rep > 1.0:
+        for tok in hist[len(hist) - min(len(hist), 64):]:
+            l[tok] = l[tok] / f(rep) if l[tok] > 0 else l[tok] * f(rep)
+    if pres > 0.0 and len(hist):
+        for tok in sorted(set(int(t) for t in hist)):
+            l[tok] = l[tok] - f(pres)
+    if ban >= 0:
+        l[ban] = -np.inf
+    if temperature <= 0.0:
+        return int(np.argmax(l)), state
+    inv_temp = f(1.0) / f(temperature)
+    mx = f(np.max(l))
+    order = sorted(range(len(l)), key=lambda i: -float(l[i]))  # stable: ties keep index order
+    k = min(top_k, len(l)) if top_k > 0 else len(l)
+    probs = [(i, f(np.exp(f((l[i] - mx) * inv_temp)))) for i in order[:k]]
+    s = f(0.0)
+    for _, p in probs:
+        s = f(s + p)
+    if s <= 0:
+        return probs[0][0], state
+    inv = f(f(1.0) / s)
+    probs = [(i, f(p * inv)) for i, p in probs]
+    cum, cut = f(0.0), len(probs)
+    for j, (_, p) in enumerate(probs):
+        cum = f(cum + p)
+        if cum >= f(top_p):
+            cut = j + 1
+            break
+    tot = f(0.0)
+    for _, p in probs[:cut]:
+        tot = f(tot + p)
+    if tot <= 0:
+        return probs[0][0], state
+    m = (1 << 64) - 1
+    state ^= (state << 13) & m
+    state ^= state >> 7
+    state ^= (state << 17) & m
+    r = f(f(state >> 40) / f(16777216.0)) * tot
+    acc = f(0.0)
+    for i, p in probs[:cut]:
+        acc = f(acc + p)
+        if acc >= r:
+            return i, state
+    return probs[0][0], state
+
+
+def test_sampling_restatement_pins_oracle(orc):
+    """The oracle's sampling step against the Python restatement on seeded cases:
+    identical tokens and generator states (greedy, top-k/top-p, penalties with repeated
+    history tokens, a banned token)."""
+    rng = np.random.default_rng(5)
+    cases = [(0.0, 0.95, 20, 1.0, 0.0, -1), (0.6, 0.95, 20, 1.1, 1.5, -1), (1.0, 1.0, 1, 1.0, 0.0, -1),
+             (0.3, 0.5, 50, 1.3, 0.0, 7), (1.5, 0.99, 200, 1.0, 0.7, 3)]
+    for it in range(40):
+        V = int(rng.integers(50, 400))
+        logits = (rng.standard_normal(V) * rng.uniform(0.5, 4)).astype(np.float32)
+        hist = rng.integers(0, V, size=int(rng.integers(0, 90))).astype(np.uint32)
+        if hist.size > 3:
+            hist[-2] = hist[-1]  # a duplicate inside the 64-token window
+        t, tp, k, rp, pp, ban = cases[it % len(cases)]
+        ban = ban if ban < V else -1
+        state = int(rng.integers(1, 2**63))
+        a = orc.sample(logits, hist, t, tp, k, rp, pp, ban, state)
+        b = _py_sample(logits, hist, t, tp, k, rp, pp, ban, state)
+        assert a == b, (it, a, b)
