@@ -6,6 +6,7 @@ argmax).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     python bench.py --workload f16-batch [--batch 32] [--steps 128]
+    python bench.py --workload q4-long [--steps 128]
 
 Prints one JSON line (rank 0). `value` is device time (CUDA events on the engine's
 stream) of K greedy steps, each one launch of the persistent decode kernel, with the
@@ -441,6 +442,111 @@ def run_f16(args, rank, world, local_rank):
     return 0
 
 
+LONG_CTX = 32768
+
+
+def long_kv(layers, seed=4):
+    """Seeded f32 N(0,1) K/V rows for every layer, token-major [S][4*128] (config 4)."""
+    rng = np.random.default_rng(seed)
+    return [(rng.standard_normal((LONG_CTX, 512), dtype=np.float32),
+             rng.standard_normal((LONG_CTX, 512), dtype=np.float32)) for _ in range(layers)]
+
+
+def run_q4_long(args, rank, world, local_rank):
+    """the Q4 model with every layer's KV cache pre-filled to 32768
+    positions (qora_kv_import), then greedy decode at batch 1; attention KV reads
+    dominate the bytes per token."""
+    if world > 1:
+        if rank == 0:
+            print(json.dumps({"metric": METRIC + ", 32K context", "unavailable": "the long-context line is single-GPU"}))
+        return 0
+    K, W = args.steps, args.warmup
+    threads = os.cpu_count() or 1
+    model, prompt = synth(args.layers)
+    kvs = long_kv(args.layers)
+    first_tok = int(prompt[0])
+    metric = "decode tok/s (batch 1, SmolLM3-3B Q4, 32K-token KV cache)"
+    if args.impl == "reference":
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle
+        oracle.set_threads(threads)
+        om = oracle.OracleModel(model)
+        okv = om.new_kv()
+        for layer, (k, v) in enumerate(kvs):
+            okv.import_layer(layer, k, v)
+        tok = oracle.argmax(om.forward_decode(first_tok, okv))
+        t0 = time.perf_counter()
+        n = 0
+        while n < K and (n < 2 or time.perf_counter() - t0 < args.cpu_seconds):
+            tok = oracle.argmax(om.forward_decode(tok, okv))
+            n += 1
+        v = n / (time.perf_counter() - t0)
+        line = {"impl": "reference", "metric": metric, "value": v, "unit": "tok/s", "n_gpus": 1, "steps": n,
+                "warmup": 1, "ms_per_step": 1000.0 / v, "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random-init SmolLM3-3B Q4, N(0,1) KV)",
+                "config": {"workload": "config 4: SmolLM3-3B Q4, KV pre-filled to 32768 positions, greedy decode"},
+                "cpu_baseline": {"value": v, "unit": "tok/s", "cores": threads, "kind": "port",
+                                 "sample": f"{n} forward_decode_raw steps after the 32768-row import, {threads} threads",
+                                 "cpu": cpu_model()},
+                "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return 0
+    import importlib
+    import torch
+    pkg = importlib.import_module("qora-llm_b200")
+    torch.cuda.set_device(local_rank)
+    eng = pkg.DecodeWeights(model=model, device=local_rank)
+    cap = LONG_CTX + W + K + 8
+
+    def filled():
+        kv = eng.new_kv(cap)
+        for layer, (k, v) in enumerate(kvs):
+            kv.import_layer(layer, k, v)
+        return kv
+
+    kv = filled()
+    toks = eng.generate_greedy(kv, first_tok, W)
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clk:
+        _, ms = eng.generate_greedy_timed(kv, int(toks[-1]), K)
+    torch.cuda.synchronize()
+    value = K / (ms / 1000.0)
+    kv.close()
+    kv2 = filled()
+    t = first_tok
+    for _ in range(W):
+        t = eng.decode_step(kv2, t)
+    t0 = time.perf_counter()
+    for _ in range(K):
+        t = eng.decode_step(kv2, t)
+    e2e = K / (time.perf_counter() - t0)
+    kv2.close()
+    peak, peak_kind = peaks()
+    mean_kv = LONG_CTX + W + (K - 1) / 2.0 + 1
+    step_bytes = weight_bytes_per_token(args.layers) + kv_bytes_per_pos(args.layers) * (mean_kv + 1)
+    achieved = step_bytes / (ms / K / 1000.0) / 1e9
+    line = {
+        "metric": metric, "value": value, "unit": "tok/s", "n_gpus": 1, "steps": K, "warmup": W,
+        "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded random-init SmolLM3-3B Q4 weights, N(0,1) f32 KV rows)",
+        "config": {"workload": "config 4: SmolLM3-3B Q4, KV of all 36 layers pre-filled to 32768 positions, "
+                               "greedy decode at batch 1",
+                   "kv_len_mean": mean_kv, "layers": args.layers, "parallelism": "single GPU",
+                   "bytes_per_step": step_bytes,
+                   "l2": "inputs larger than L2: 6.6 GB of weights + KV streamed per step"},
+        "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
+        "gpu_launches": eng.launches_per_step() * K,
+        "roofline": dict(bound="hbm", achieved=achieved, peak=peak, peak_kind=f"{peak_kind} hbm_gbs (copy)",
+                         unit="GB/s", frac=achieved / peak, traffic=None,
+                         kernel="decode megakernel (whole step; attention over 32K cached rows per layer)",
+                         bytes_per_launch=step_bytes, us_per_launch=1000 * ms / K, launches_timed=K),
+        "clocks": clk.summary(),
+    }
+    eng.close()
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -449,8 +555,8 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
-    ap.add_argument("--workload", choices=("q4", "f16-batch"), default="q4",
-                    help="q4: config 3 batch-1 decode (the headline); f16-batch: config 5")
+    ap.add_argument("--workload", choices=("q4", "q4-long", "f16-batch"), default="q4",
+                    help="q4: config 3 batch-1 decode (the headline); q4-long: config 4; f16-batch: config 5")
     ap.add_argument("--batch", type=int, default=32, help="sequences for --workload f16-batch")
     ap.add_argument("--layers", type=int, default=36,
                     help="decoder layers of the synthetic model (36 = SmolLM3-3B; fewer only for "
@@ -463,6 +569,8 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.workload == "f16-batch":
         return run_f16(args, rank, world, local_rank)
+    if args.workload == "q4-long":
+        return run_q4_long(args, rank, world, local_rank)
     if args.impl == "reference":
         return run_reference(args, rank)
     return run_ours(args, rank, world, local_rank)

@@ -919,28 +919,57 @@ __device__ __noinline__ uint32_t attention_phase(int L, uint32_t chunk) {
   }
   C.bar();
   C.fstamp();
-  // P.V: thread d < 128 accumulates dim d of the 4 heads
+  // P.V: three groups of 128 threads (warps 0-3, 4-7, 8-11) take rows grp, grp + 3, ...
+  // of each stage, four rows per step with their loads issued together; thread d of a
+  // group accumulates dim d of the 4 heads; the groups' sums are added in group order
+  const int grp = tid >> 7, dd = tid & (kHeadDim - 1);
   float o[kHeadsPerKV] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll 1
   for (int s = s0; s < sc1; s += kKVRows) {
     const uint8_t* stg = C.acquire_stage();
     const int nr = min(kKVRows, sc1 - s);
-    if (C.stage_ok && tid < kHeadDim) {
-      const float* vr = reinterpret_cast<const float*>(stg) + tid;
+    if (C.stage_ok && grp < 3) {
+      const float* vr = reinterpret_cast<const float*>(stg) + dd;
+      const float* pr = sc + (s - s0);
+      int i = grp;
 #pragma unroll 1
-      for (int i = 0; i < nr; ++i) {
+      for (; i + 9 < nr; i += 12) {
+        float v[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) v[r] = vr[(i + 3 * r) * kHeadDim];
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+          for (int h = 0; h < kHeadsPerKV; ++h) o[h] = __fmaf_rn(pr[h * kMaxAttnChunk + i + 3 * r], v[r], o[h]);
+      }
+#pragma unroll 1
+      for (; i < nr; i += 3) {
         const float v = vr[i * kHeadDim];
 #pragma unroll
-        for (int h = 0; h < kHeadsPerKV; ++h) o[h] = __fmaf_rn(sc[h * kMaxAttnChunk + s - s0 + i], v, o[h]);
+        for (int h = 0; h < kHeadsPerKV; ++h) o[h] = __fmaf_rn(pr[h * kMaxAttnChunk + i], v, o[h]);
       }
     }
     C.release_stage();
   }
+  float ppos[kHeadsPerKV] = {0.0f, 0.0f, 0.0f, 0.0f};  // the new position's probabilities
+  if (has_pos && tid < kHeadDim) {
+#pragma unroll
+    for (int h = 0; h < kHeadsPerKV; ++h) ppos[h] = sc[h * kMaxAttnChunk + pos - s0];
+  }
+  C.bar();  // every read of the probabilities is done: groups 1 and 2 park their sums there
+  if ((grp == 1 || grp == 2) && !C.aborted()) {
+#pragma unroll
+    for (int h = 0; h < kHeadsPerKV; ++h) sc[(grp - 1) * kHeadsPerKV * kHeadDim + h * kHeadDim + dd] = o[h];
+  }
+  C.bar();
   if (tid < kHeadDim && !C.aborted()) {
+#pragma unroll
+    for (int h = 0; h < kHeadsPerKV; ++h)
+      o[h] = __fadd_rn(__fadd_rn(o[h], sc[h * kHeadDim + tid]), sc[kHeadsPerKV * kHeadDim + h * kHeadDim + tid]);
     if (has_pos) {
       const float v = skv[kHeadDim + tid];
 #pragma unroll
-      for (int h = 0; h < kHeadsPerKV; ++h) o[h] = __fmaf_rn(sc[h * kMaxAttnChunk + pos - s0], v, o[h]);
+      for (int h = 0; h < kHeadsPerKV; ++h) o[h] = __fmaf_rn(ppos[h], v, o[h]);
     }
 #pragma unroll
     for (int h = 0; h < kHeadsPerKV; ++h)
