@@ -169,6 +169,10 @@ QORA_DEV int c_dn_arr(const Args& a, int L, int t) { return L * a.cpl + t; }
 QORA_DEV int c_lm(const Args& a) { return a.L * a.cpl; }
 
 // Attention units: (kv head, chunk of `chunk` positions), about one unit per CTA.
+// Attention units run on the CTAs from the end of the grid (the q|k|v CTAs) so that the
+// o_proj CTAs at the front keep their o_proj weights queued in the ring behind nothing.
+QORA_DEV int attn_unit_of(int c, int G) { return G - 1 - c; }
+
 QORA_DEV void attn_plan(int len, int G, int nkvh, int& chunk, int& nch) {
   chunk = (len * nkvh + G - 1) / G;
   chunk = max(kMinAttnChunk, min(kMaxAttnChunk, chunk));
@@ -265,8 +269,9 @@ __device__ __noinline__ uint32_t produce_kv(int L, uint32_t chunk) {
   const int c = blockIdx.x, pos = sm_flags()[2], len = pos + 1;
   int csz, nch;
   attn_plan(len, gridDim.x, a.nkvh, csz, nch);
-  if (c >= a.nkvh * nch) return chunk;
-  const int g = c % a.nkvh, s0 = (c / a.nkvh) * csz, sc1 = min(min(len, s0 + csz), pos);
+  const int u = attn_unit_of(c, gridDim.x);
+  if (u >= a.nkvh * nch) return chunk;
+  const int g = u % a.nkvh, s0 = (u / a.nkvh) * csz, sc1 = min(min(len, s0 + csz), pos);
 #pragma unroll 1
   for (int kvs = 0; kvs < 2; ++kvs) {
     const float* src = (kvs ? a.layers[L].vc : a.layers[L].kc) + g * a.head_stride;
@@ -816,7 +821,7 @@ __device__ __noinline__ uint32_t attention_phase(int L, uint32_t chunk) {
   const int pos = C.pos, len = pos + 1, tid = C.tid, lane = C.lane, warp = C.warp;
   int csz, nch;
   attn_plan(len, C.G, a.nkvh, csz, nch);
-  const int u = C.c;
+  const int u = attn_unit_of(C.c, C.G);
   if (u >= a.nkvh * nch) return chunk;
   const int g = u % a.nkvh;
   const int s0 = (u / a.nkvh) * csz, s1 = min(len, s0 + csz), sc1 = min(s1, pos), n = s1 - s0;
