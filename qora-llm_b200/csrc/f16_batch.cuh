@@ -27,11 +27,13 @@ using umma::row_info;
 
 // x[m] = f32(E[token[m]]) (embed_lookup, src/gemv.rs:515-526), read from the tiled
 // embedding (n = vocab, k = hidden), with the per-128-channel statistics (sum of squares,
-// max |x|) the first RMSNorm reads. Grid (hidden / 128, M), 128 threads.
+// max |x|) the first RMSNorm reads; also advances the forward-pass counter. Grid
+// (hidden / 128, M), 128 threads.
 __global__ void __launch_bounds__(128) embed_rows_kernel(const uint8_t* emb_t, int H, int vocab, RowInfo ri,
-                                                          float* x, float* st_ss, float* st_mx) {
+                                                          float* x, float* st_ss, float* st_mx, unsigned* epoch) {
   __shared__ float red[2][4];
   const int t = blockIdx.x, m = blockIdx.y, i = threadIdx.x;
+  if (t == 0 && m == 0 && i == 0) *epoch += 1u;  // a new forward pass (exchange tags)
   const int tok = ri.token[m];
   if (tok < 0 || tok >= vocab) {  // the host validates ids; this keeps the read in bounds
     if (i == 0 && t == 0) *ri.error = 1;
@@ -83,6 +85,7 @@ constexpr int kAttBlock = 64;
 struct AttnRowsArgs {
   const float* q;       // [M][nq]
   int nq, nkv;
+  int hpk;              // query heads per KV head held here (4; 2 on a rank of 8-way TP)
   RowInfo rows;
   const float* kc;      // this layer's caches [batch][kv heads][max_seq][128]
   const float* vc;
@@ -112,8 +115,8 @@ __global__ void __launch_bounds__(kAttThreads) attention_split_kernel(const Attn
   const float* V = a.vc + (long long)a.rows.seq[m] * a.seq_stride + j * a.head_stride;
   const float scale = 0.08838834764831845f;  // 1/sqrt(128): the f32 quotient of 1 and f32 sqrt(128)
   {
-    const float* q = a.q + (size_t)m * a.nq + (size_t)j * 4 * kHeadDim;
-    for (int i = tid; i < 4 * kHeadDim; i += kAttThreads) qs[i / kHeadDim][i % kHeadDim] = q[i];
+    const float* q = a.q + (size_t)m * a.nq + (size_t)j * a.hpk * kHeadDim;
+    for (int i = tid; i < 4 * kHeadDim; i += kAttThreads) qs[i / kHeadDim][i % kHeadDim] = i / kHeadDim < a.hpk ? q[i] : 0.0f;
   }
   float mrun = -INFINITY, lrun = 0.0f;  // held by warp h = head h
   // P.V accumulators: warp w sums its 16 positions of each block, lane l owns dims 4l..4l+3
@@ -203,7 +206,7 @@ __global__ void __launch_bounds__(kAttThreads) attention_split_kernel(const Attn
   for (int h = 0; h < 4; ++h)
     o[h] = __fadd_rn(__fadd_rn(__fadd_rn(s_o[0][h][tid], s_o[1][h][tid]), s_o[2][h][tid]), s_o[3][h][tid]);
   const size_t slot = ((size_t)m * a.nkv + j) * kAttSplits;
-  float* dst = a.out + (size_t)m * a.nq + (size_t)j * 4 * kHeadDim;
+  float* dst = a.out + (size_t)m * a.nq + (size_t)j * a.hpk * kHeadDim;
   float mxo = 0.0f;
   if (n == 1) {
     if (lane == 0) s_red[warp] = lrun;  // warp h holds head h's sum
@@ -211,8 +214,10 @@ __global__ void __launch_bounds__(kAttThreads) attention_split_kernel(const Attn
 #pragma unroll
     for (int h = 0; h < 4; ++h) {
       const float r = __fmul_rn(o[h], __fdiv_rn(1.0f, s_red[h]));
-      dst[h * kHeadDim + tid] = r;
-      mxo = fmaxf(mxo, fabsf(r));
+      if (h < a.hpk) {
+        dst[h * kHeadDim + tid] = r;
+        mxo = fmaxf(mxo, fabsf(r));
+      }
     }
   } else {
 #pragma unroll
@@ -246,8 +251,10 @@ __global__ void __launch_bounds__(kAttThreads) attention_split_kernel(const Attn
         acc = __fmaf_rn(__ldcg(&a.o_part[((slot + c) * 4 + h) * kHeadDim + tid]), w, acc);
       }
       const float r = __fmul_rn(acc, __fdiv_rn(1.0f, l));
-      dst[h * kHeadDim + tid] = r;
-      mxo = fmaxf(mxo, fabsf(r));
+      if (h < a.hpk) {
+        dst[h * kHeadDim + tid] = r;
+        mxo = fmaxf(mxo, fabsf(r));
+      }
     }
   }
   // max |out| of this (row, kv head): the o_proj operand's row scale

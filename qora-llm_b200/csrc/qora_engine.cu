@@ -279,6 +279,9 @@ struct qora_engine {
   unsigned* f_sync = nullptr;      // grid barrier + finished-tile counter
   unsigned long long* f_amkey = nullptr;  // [128] greedy argmax keys
   float f_gmax_final = 0.0f;
+  int f_it = 0;                    // gate/up channels of this rank (before padding to inter_l)
+  int f_vt0 = 0, f_vt1 = 0;        // this rank's lm_head vocab tiles [f_vt0, f_vt1)
+  unsigned* f_epoch = nullptr;     // forward passes (tensor-parallel exchange tags)
   int* f_err = nullptr;            // set by a GEMM whose bounded wait timed out
   // on-device sampling scratch (allocated on first use)
   float* smp_work = nullptr;       // [vocab] penalised logits
@@ -1097,20 +1100,21 @@ qora_status umma_attrs() {
 UmmaCtx umma_ctx(const qora_engine* e) {
   const int V = (int)e->vocab;
   return UmmaCtx{e->sms, e->stream, e->f_xt, e->f_part, e->f_part_floats, e->f_tcnt,
-                 (size_t)std::max(V, 2 * (int)e->inter) / umma::kTileN + 1, e->f_sync, e->f_err};
+                 (size_t)std::max(V, 2 * e->inter_l) / umma::kTileN + 1, e->f_sync, e->f_err};
 }
 
-// Copy one f16 matrix view to the device and re-tile it: channel n goes to tile
-// t0 + n / group, row o0 + n % group, of dst (k/64 chunks per tile). kmajor: the view is
-// [n][k] (the embedding).
-qora_status f16_tile_upload(qora_engine* e, const qora_matrix_view& m, bool kmajor, int t0, int group, int o0,
-                            uint8_t* dst, __half* tmp) {
-  const size_t elems = (size_t)m.k * m.n;
-  QCUDA(cudaMemcpy(tmp, m.data, elems * 2, cudaMemcpyHostToDevice));
-  const int K = kmajor ? (int)m.n : (int)m.k, N = kmajor ? (int)m.k : (int)m.n;
+// Copy rows [r0, r0 + K) of an f16 matrix view to the device and re-tile them: for a
+// projection ([k][n]) its columns [col0, col0 + N) become channels, for the embedding
+// (kmajor, [vocab][hidden]) its rows do (then K = hidden, r0 = 0). Channel n goes to tile
+// t0 + n / group, row o0 + n % group, of dst (`chunks` chunks of 64 k per tile).
+qora_status f16_tile_upload(qora_engine* e, const qora_matrix_view& m, bool kmajor, uint64_t r0, int K, int col0,
+                            int N, int t0, int group, int o0, int chunks, uint8_t* dst, __half* tmp) {
+  const size_t rows = kmajor ? m.k : (size_t)K;
+  QCUDA(cudaMemcpy(tmp, m.data + (kmajor ? 0 : r0 * m.n), rows * m.n * 2, cudaMemcpyHostToDevice));
   const long long units = (long long)N * (K / 8);
   const int blocks = (int)std::min<long long>((units + 255) / 256, 16LL * e->sms);
-  umma::tile_weights_kernel<<<blocks, 256>>>(tmp, (long long)m.n, kmajor ? 1 : 0, K, N, 0, t0, group, o0, dst);
+  umma::tile_weights_kernel<<<blocks, 256>>>(tmp, (long long)m.n, kmajor ? 1 : 0, K, N, kmajor ? 0 : col0, t0, group,
+                                             o0, chunks, dst);
   QCUDA(cudaGetLastError());
   QCUDA(cudaDeviceSynchronize());
   return QORA_OK;
@@ -1133,47 +1137,66 @@ qora_status f16_engine_init(qora_engine* e, const qora_weights_view* w) {
   e->inter = (uint32_t)L0.gate_proj.n;
   e->nh = L0.num_heads;
   e->nkv_total = L0.num_kv_heads;
-  e->nh_l = (int)e->nh;
-  e->nkv_l = (int)e->nkv_total;
-  e->kv0 = 0;
-  e->inter_l = (int)e->inter;
-  e->nkv = e->nkv_total;
   e->rope_rows = (uint32_t)w->rope_rows;
+  const int T = e->tp, r = e->rank;
+  const int H = (int)e->hidden, I = (int)e->inter, V = (int)e->vocab;
+  {
+    // this rank's shard: q heads split evenly; kv heads split while they divide, else the
+    // kv head of the rank's q heads; gate/up columns and down rows [r*I/T, +I/T) padded
+    // to whole 64-channel tile halves; vocab split by 128-row tiles
+    const int nh = (int)e->nh, nkvh = (int)e->nkv_total;
+    if (nh % T != 0 || (nkvh % T != 0 && T % nkvh != 0) || I % T != 0 || (I / T) % 8 != 0)
+      return fail(QORA_ERR_UNSUPPORTED, "tp_size %d does not divide heads %d/%d and MLP width %d", T, nh, nkvh, I);
+    e->nh_l = nh / T;
+    e->nkv_l = nkvh % T == 0 ? nkvh / T : 1;
+    e->kv0 = nkvh % T == 0 ? r * e->nkv_l : r / (T / nkvh);
+    if (e->nh_l % e->nkv_l != 0 || e->nh_l / e->nkv_l > kGrp)
+      return fail(QORA_ERR_UNSUPPORTED, "tp_size %d: %d query heads over %d kv heads per rank", T, e->nh_l, e->nkv_l);
+    e->inter_l = (I / T + 63) / 64 * 64;
+    e->f_it = I / T;
+    const int vt = V / umma::kTileN;
+    e->f_vt0 = r * vt / T;
+    e->f_vt1 = (r + 1) * vt / T;
+  }
+  e->nkv = (uint32_t)e->nkv_l;
   e->sms = sm_count(e->device);
   e->mk_ok = false;
   e->mk_why = "F16 weights run the batched path";
   QCUDA(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
-  const int H = (int)e->hidden, nq = (int)e->nh * kHeadDim, nkvw = (int)e->nkv * kHeadDim, I = (int)e->inter;
-  const int V = (int)e->vocab;
+  const int nq = e->nh_l * kHeadDim, nkvw = e->nkv_l * kHeadDim, Il = e->inter_l, IT = e->f_it;
+  const int h0 = r * e->nh_l;
   e->f_nqkv = nq + 2 * nkvw;
   e->fl.resize(e->num_layers);
   // staging buffer for one source matrix (freed at the end of the load)
   size_t tmp_elems = (size_t)V * H;
   tmp_elems = std::max(tmp_elems, (size_t)H * I);
-  tmp_elems = std::max(tmp_elems, (size_t)H * nq);
+  tmp_elems = std::max(tmp_elems, (size_t)H * e->nh * kHeadDim);
   __half* tmp = nullptr;
   QCUDA(cudaMalloc(&tmp, tmp_elems * 2));
   struct TmpFree {
     __half* p;
     ~TmpFree() { cudaFree(p); }
   } tmp_free{tmp};
-  constexpr int TN = umma::kTileN;
+  constexpr int TN = umma::kTileN, CK = umma::kChunkK;
   for (uint32_t i = 0; i < e->num_layers; ++i) {
     const qora_layer_view& L = w->layers[i];
     F16Layer& d = e->fl[i];
     QCHECK(e->alloc(&d.wqkv, (size_t)H * e->f_nqkv * 2));
-    QCHECK(f16_tile_upload(e, L.q_proj, false, 0, TN, 0, d.wqkv, tmp));
-    QCHECK(f16_tile_upload(e, L.k_proj, false, nq / TN, TN, 0, d.wqkv, tmp));
-    QCHECK(f16_tile_upload(e, L.v_proj, false, (nq + nkvw) / TN, TN, 0, d.wqkv, tmp));
+    QCHECK(f16_tile_upload(e, L.q_proj, false, 0, H, h0 * kHeadDim, nq, 0, TN, 0, H / CK, d.wqkv, tmp));
+    QCHECK(f16_tile_upload(e, L.k_proj, false, 0, H, e->kv0 * kHeadDim, nkvw, nq / TN, TN, 0, H / CK, d.wqkv, tmp));
+    QCHECK(f16_tile_upload(e, L.v_proj, false, 0, H, e->kv0 * kHeadDim, nkvw, (nq + nkvw) / TN, TN, 0, H / CK,
+                           d.wqkv, tmp));
     QCHECK(e->alloc(&d.wo, (size_t)nq * H * 2));
-    QCHECK(f16_tile_upload(e, L.o_proj, false, 0, TN, 0, d.wo, tmp));
+    QCHECK(f16_tile_upload(e, L.o_proj, false, (uint64_t)h0 * kHeadDim, nq, 0, H, 0, TN, 0, nq / CK, d.wo, tmp));
     // gate|up interleaved per tile: rows 0-63 gate channels 64t.., rows 64-127 the same up
-    // channels, so one tile holds both operands of its 64 SwiGLU outputs
-    QCHECK(e->alloc(&d.wgu, (size_t)H * 2 * I * 2));
-    QCHECK(f16_tile_upload(e, L.gate_proj, false, 0, 64, 0, d.wgu, tmp));
-    QCHECK(f16_tile_upload(e, L.up_proj, false, 0, 64, 64, d.wgu, tmp));
-    QCHECK(e->alloc(&d.wdown, (size_t)I * H * 2));
-    QCHECK(f16_tile_upload(e, L.down_proj, false, 0, TN, 0, d.wdown, tmp));
+    // channels, so one tile holds both operands of its 64 SwiGLU outputs (padding: zero)
+    QCHECK(e->alloc(&d.wgu, (size_t)H * 2 * Il * 2));
+    QCUDA(cudaMemset(d.wgu, 0, (size_t)H * 2 * Il * 2));
+    QCHECK(f16_tile_upload(e, L.gate_proj, false, 0, H, r * IT, IT, 0, 64, 0, H / CK, d.wgu, tmp));
+    QCHECK(f16_tile_upload(e, L.up_proj, false, 0, H, r * IT, IT, 0, 64, 64, H / CK, d.wgu, tmp));
+    QCHECK(e->alloc(&d.wdown, (size_t)Il * H * 2));
+    QCUDA(cudaMemset(d.wdown, 0, (size_t)Il * H * 2));
+    QCHECK(f16_tile_upload(e, L.down_proj, false, (uint64_t)r * IT, IT, 0, H, 0, TN, 0, Il / CK, d.wdown, tmp));
     std::vector<float> g1 = f16_to_f32(L.input_norm_gamma, H), g2 = f16_to_f32(L.post_attn_norm_gamma, H);
     QCHECK(e->alloc(&d.g_in, H));
     QCHECK(e->alloc(&d.g_post, H));
@@ -1183,8 +1206,9 @@ qora_status f16_engine_init(qora_engine* e, const qora_weights_view* w) {
     d.gmax_post = max_abs_f16(L.post_attn_norm_gamma, H);
     d.rope = w->no_rope_layers[i] ? 1 : 0;
   }
+  // the whole table: any token's embedding row; lm_head reads this rank's tiles
   QCHECK(e->alloc(&e->f_lm, (size_t)V * H * 2));
-  QCHECK(f16_tile_upload(e, w->embed, true, 0, TN, 0, e->f_lm, tmp));
+  QCHECK(f16_tile_upload(e, w->embed, true, 0, H, 0, V, 0, TN, 0, H / CK, e->f_lm, tmp));
   e->f_gmax_final = max_abs_f16(w->final_norm_gamma, H);
   std::vector<float> fg = f16_to_f32(w->final_norm_gamma, H);
   QCHECK(e->alloc(&e->final_gamma, H));
@@ -1197,29 +1221,29 @@ qora_status f16_engine_init(qora_engine* e, const qora_weights_view* w) {
 
   const size_t R = f16b::kMaxRows;
   size_t slots = 0;  // partial slots of the largest GEMM plan, in [R][128] blocks
-  const int gn[5] = {e->f_nqkv, H, 2 * I, H, V}, gk[5] = {H, nq, H, I, H};
+  const int lmN = (e->f_vt1 - e->f_vt0) * TN;
+  const int gn[5] = {e->f_nqkv, H, 2 * Il, H, lmN}, gk[5] = {H, nq, H, Il, H};
   for (int j = 0; j < 5; ++j) {
     const UmmaPlan p = umma_plan(e->sms, gn[j] / umma::kTileN, gk[j] / umma::kChunkK);
     slots = std::max(slots, (size_t)p.G * p.maxseg);
   }
-  const size_t kmax = (size_t)std::max(std::max(H, nq), I);
+  const size_t kmax = (size_t)std::max(std::max(H, nq), Il);
   e->f_part_floats = slots * R * umma::kTileN;
   QCHECK(e->alloc(&e->f_part, e->f_part_floats));
   QCHECK(e->alloc(&e->f_x, R * H));
   QCHECK(e->alloc(&e->f_qkv, R * e->f_nqkv));
   QCHECK(e->alloc(&e->f_attn, R * nq));
-  QCHECK(e->alloc(&e->f_h, R * I));
-  QCHECK(e->alloc(&e->f_logits, R * V));
+  QCHECK(e->alloc(&e->f_h, R * Il));
   QCHECK(e->alloc(&e->f_xt, kmax * R * 2 * 2));
   QCHECK(e->alloc(&e->f_xss, (size_t)(H / umma::kTileN) * R));
   QCHECK(e->alloc(&e->f_xmx, (size_t)(H / umma::kTileN) * R));
-  QCHECK(e->alloc(&e->f_hmx, (size_t)(I / 64) * R));
+  QCHECK(e->alloc(&e->f_hmx, (size_t)(Il / 64) * R));
   QCHECK(e->alloc(&e->f_amx, (size_t)e->nkv * R));
   QCHECK(e->alloc(&e->f_att_part, R * e->nkv * f16b::kAttSplits * 4 * kHeadDim));
   QCHECK(e->alloc(&e->f_att_ml, R * e->nkv * f16b::kAttSplits * 4 * 2));
   QCHECK(e->alloc(&e->f_att_cnt, R * e->nkv));
   QCUDA(cudaMemset(e->f_att_cnt, 0, R * e->nkv * sizeof(unsigned)));
-  const size_t ntc = (size_t)std::max(V, 2 * I) / umma::kTileN + 1;
+  const size_t ntc = (size_t)std::max(V, 2 * Il) / umma::kTileN + 1;
   QCHECK(e->alloc(&e->f_tcnt, ntc));
   QCUDA(cudaMemset(e->f_tcnt, 0, ntc * sizeof(unsigned)));
   QCHECK(e->alloc(&e->f_sync, 4));
@@ -1228,6 +1252,22 @@ qora_status f16_engine_init(qora_engine* e, const qora_weights_view* w) {
   QCUDA(cudaMemset(e->f_amkey, 0, R * sizeof(unsigned long long)));
   QCHECK(e->alloc(&e->f_err, 1));
   QCUDA(cudaMemset(e->f_err, 0, sizeof(int)));
+  QCHECK(e->alloc(&e->f_epoch, 1));
+  QCUDA(cudaMemset(e->f_epoch, 0, sizeof(unsigned)));
+  if (T > 1) {
+    // receive region (IPC-exported): o_proj and down partial tiles of every rank, the
+    // ranks' lm_head candidates, and the full logits
+    const size_t xr = (size_t)T * (H / TN) * R * TN * sizeof(uint64_t);
+    e->tp_off_d = xr;
+    e->tp_off_lm = 2 * xr;
+    e->tp_off_logits = e->tp_off_lm + (size_t)T * R * 2 * sizeof(uint64_t);
+    e->tp_region_bytes = e->tp_off_logits + R * (size_t)V * sizeof(float);
+    QCHECK(e->alloc(&e->tp_region, e->tp_region_bytes));
+    QCUDA(cudaMemset(e->tp_region, 0, e->tp_region_bytes));
+    e->f_logits = reinterpret_cast<float*>(e->tp_region + e->tp_off_logits);
+  } else {
+    QCHECK(e->alloc(&e->f_logits, R * V));
+  }
   e->logits = e->f_logits;
   QCHECK(umma_attrs());
   QCUDA(cudaDeviceSynchronize());
@@ -1243,14 +1283,31 @@ int f16_launches(const qora_engine* e, bool lm) {
 // The layer stack over the M rows of kv's row table, then (rows [lm0, M) only) the final
 // RMSNorm, the tied lm_head into f_logits rows [0, M - lm0) and the greedy argmax.
 // Mirrors forward_decode_raw / raw_prefill (src/gemv.rs:872-1019, :1027-1190) per row.
+// Tensor-parallel exchange fields of one fused GEMM (every rank's receive region): the
+// residual GEMMs use the partial-tile block at `xr_off`, lm_head the candidate slots and
+// the full logits.
+void f16_tp_args(const qora_engine* e, umma::FusedArgs& a, int tag_slot, size_t xr_off) {
+  a.tp = e->tp;
+  a.rank = e->rank;
+  a.epoch = e->f_epoch;
+  a.tag_slot = tag_slot;
+  if (e->tp < 2) return;
+  for (int p = 0; p < e->tp; ++p) {
+    uint8_t* base = e->tp_peer[p];
+    a.xr_peer[p] = reinterpret_cast<unsigned long long*>(base + xr_off);
+    a.lg_peer[p] = reinterpret_cast<float*>(base + e->tp_off_logits);
+    a.key_peer[p] = reinterpret_cast<unsigned long long*>(base + e->tp_off_lm);
+  }
+}
+
 qora_status f16_forward(qora_engine* e, qora_kv* kv, int M, int lm0) {
-  const int H = (int)e->hidden, nq = (int)e->nh * kHeadDim, I = (int)e->inter;
+  const int H = (int)e->hidden, nq = e->nh_l * kHeadDim, I = e->inter_l;
   const int V = (int)e->vocab, NQKV = e->f_nqkv, R = f16b::kMaxRows;
   const f16b::RowInfo ri = f16b::row_info(kv->rows);
   cudaStream_t s = e->stream;
   const UmmaCtx u = umma_ctx(e);
   const int xt_n = H / umma::kTileN;
-  f16b::embed_rows_kernel<<<dim3(xt_n, M), 128, 0, s>>>(e->f_lm, H, V, ri, e->f_x, e->f_xss, e->f_xmx);
+  f16b::embed_rows_kernel<<<dim3(xt_n, M), 128, 0, s>>>(e->f_lm, H, V, ri, e->f_x, e->f_xss, e->f_xmx, e->f_epoch);
   QCUDA(cudaGetLastError());
   const long long hs = (long long)kv->max_seq * kHeadDim, ss = (long long)kv->seq_stride();
   for (uint32_t li = 0; li < e->num_layers; ++li) {
@@ -1263,7 +1320,7 @@ qora_status f16_forward(qora_engine* e, qora_kv* kv, int M, int lm0) {
     a.y = e->f_qkv;
     a.ldy = nq;
     a.q_tiles = nq / umma::kTileN;
-    a.k_tiles = (int)e->nkv;
+    a.k_tiles = e->nkv_l;
     a.rope = d.rope;
     a.cos_t = e->rope_cos;
     a.sin_t = e->rope_sin;
@@ -1278,6 +1335,7 @@ qora_status f16_forward(qora_engine* e, qora_kv* kv, int M, int lm0) {
       at.q = e->f_qkv;
       at.nq = nq;
       at.nkv = (int)e->nkv;
+      at.hpk = e->nh_l / e->nkv_l;
       at.rows = ri;
       at.kc = kc;
       at.vc = vc;
@@ -1299,6 +1357,7 @@ qora_status f16_forward(qora_engine* e, qora_kv* kv, int M, int lm0) {
     a.ldy = H;
     a.o_ss = e->f_xss;
     a.o_mx = e->f_xmx;
+    f16_tp_args(e, a, 2 * (int)li + 1, 0);  // o_proj partials: block at offset 0
     QCHECK(umma_fused(u, d.wo, H, nq, M, UmmaIn{e->f_attn, nq, nullptr, 0.0f, nullptr, e->f_amx, (int)e->nkv}, a));
     // RMSNorm + gate|up + SwiGLU
     a = umma::FusedArgs{};
@@ -1315,6 +1374,7 @@ qora_status f16_forward(qora_engine* e, qora_kv* kv, int M, int lm0) {
     a.ldy = H;
     a.o_ss = e->f_xss;
     a.o_mx = e->f_xmx;
+    f16_tp_args(e, a, 2 * (int)li + 2, e->tp_off_d);
     QCHECK(umma_fused(u, d.wdown, H, I, M, UmmaIn{e->f_h, I, nullptr, 0.0f, nullptr, e->f_hmx, I / 64}, a));
   }
   if (lm0 < M) {
@@ -1325,7 +1385,10 @@ qora_status f16_forward(qora_engine* e, qora_kv* kv, int M, int lm0) {
     a.ldy = V;
     a.am_key = e->f_amkey;
     a.am_out = kv->f_argmax;
-    QCHECK(umma_fused(u, e->f_lm, V, H, M - lm0,
+    a.col0 = e->f_vt0 * umma::kTileN;
+    f16_tp_args(e, a, 127, 0);
+    const uint8_t* lmw = e->f_lm + (size_t)e->f_vt0 * (H / umma::kChunkK) * umma::kATile;
+    QCHECK(umma_fused(u, lmw, (e->f_vt1 - e->f_vt0) * umma::kTileN, H, M - lm0,
                       UmmaIn{e->f_x + (size_t)lm0 * H, H, e->final_gamma, e->f_gmax_final, e->f_xss + lm0,
                              e->f_xmx + lm0, xt_n},
                       a));
@@ -1394,7 +1457,14 @@ qora_status f16_check_error(qora_engine* e, qora_kv* kv) {
   return QORA_OK;
 }
 
+qora_status f16_tp_ready(const qora_engine* e) {
+  if (e->tp > 1 && !e->tp_connected)
+    return fail(QORA_ERR_UNSUPPORTED, "tensor-parallel engine: call qora_tp_connect first");
+  return QORA_OK;
+}
+
 qora_status f16_decode_step(qora_engine* e, qora_kv* kv, const uint32_t* tokens, float* logits, uint32_t* argmax) {
+  QCHECK(f16_tp_ready(e));
   for (uint32_t b = 0; b < kv->batch; ++b)
     if (tokens[b] >= e->vocab) return fail(QORA_ERR_RANGE, "token %u (row %u) >= vocab %u", tokens[b], b, e->vocab);
   std::vector<uint32_t> lens;
@@ -1418,6 +1488,7 @@ qora_status f16_decode_step(qora_engine* e, qora_kv* kv, const uint32_t* tokens,
 // device, each feeding its argmax back (f16b::advance_rows_kernel). out: [n_tokens][batch].
 qora_status f16_generate(qora_engine* e, qora_kv* kv, const uint32_t* first, uint32_t n_tokens, uint32_t* out,
                          float* device_ms) {
+  QCHECK(f16_tp_ready(e));
   for (uint32_t b = 0; b < kv->batch; ++b)
     if (first[b] >= e->vocab) return fail(QORA_ERR_RANGE, "token %u (row %u) >= vocab %u", first[b], b, e->vocab);
   std::vector<uint32_t> lens;
@@ -1478,6 +1549,7 @@ __global__ void f16_prompt_rows_kernel(int* rows, const uint32_t* ids, int n, in
 // Prompt pass of one sequence in chunks of up to f16b::kMaxRows rows.
 qora_status f16_prefill(qora_engine* e, qora_kv* kv, const uint32_t* ids, uint32_t n, uint32_t seq, float* logits,
                         uint32_t* argmax) {
+  QCHECK(f16_tp_ready(e));
   std::vector<uint32_t> lens;
   QCHECK(f16_seq_lens(kv, lens));
   const uint32_t len = lens[seq];
@@ -1686,8 +1758,6 @@ qora_status qora_engine_create(const qora_weights_view* weights, const qora_engi
   if (rank < 0 || rank >= tp) return fail(QORA_ERR_INVALID, "tp_rank %d of %d", rank, tp);
   if (tp > 1 && opts && (opts->flags & QORA_FLAG_PER_OP_KERNELS))
     return fail(QORA_ERR_UNSUPPORTED, "tensor-parallel engines run the persistent kernel only");
-  if (tp > 1 && weights->format == QORA_FORMAT_F16)
-    return fail(QORA_ERR_UNSUPPORTED, "tensor parallelism with F16 weights is not in this build");
   int ndev = 0;
   QCUDA(cudaGetDeviceCount(&ndev));
   const int dev = opts ? opts->first_device : 0;
@@ -1702,7 +1772,7 @@ qora_status qora_engine_create(const qora_weights_view* weights, const qora_engi
     QCHECK(f16_engine_init(e.get(), weights));
   else
     QCHECK(engine_init(e.get(), weights));
-  if (tp > 1 && !e->mk_ok)
+  if (tp > 1 && weights->format == QORA_FORMAT_Q4 && !e->mk_ok)
     return fail(QORA_ERR_UNSUPPORTED, "tensor-parallel shard has no persistent kernel: %s", e->mk_why.c_str());
   *out = e.release();
   return QORA_OK;
@@ -2429,7 +2499,8 @@ qora_status qora_f16_gemm(const float* d_x, const uint16_t* d_w, uint64_t m, uin
   QCHECK(umma_attrs());
   const long long units = (long long)N * (K / 8);
   umma::tile_weights_kernel<<<(int)std::min<long long>((units + 255) / 256, 16LL * sms), 256, 0, s>>>(
-      reinterpret_cast<const __half*>(d_w), N, 0, K, N, 0, 0, umma::kTileN, 0, static_cast<uint8_t*>(wt));
+      reinterpret_cast<const __half*>(d_w), N, 0, K, N, 0, 0, umma::kTileN, 0, K / umma::kChunkK,
+      static_cast<uint8_t*>(wt));
   QCUDA(cudaGetLastError());
   const UmmaCtx u{sms, s, static_cast<uint8_t*>(xt), static_cast<float*>(part), part_floats,
                   static_cast<unsigned*>(tcnt), tiles, static_cast<unsigned*>(sync), static_cast<int*>(err)};

@@ -172,6 +172,15 @@ struct FusedArgs {
   long long seq_stride, head_stride;
   unsigned long long* am_key;  // kEpLogits: [M] ordered keys (zero between launches)
   unsigned* am_out;          //            [M] greedy token of each row
+  int col0;                  // kEpLogits: global column of local tile 0 (vocab split)
+  // tensor parallelism: the residual GEMMs (o_proj, down) exchange their partial tiles
+  // and the lm_head its row candidates (and logits) with every rank over NVLink
+  int tp, rank;
+  const unsigned* epoch;     // forward-pass counter; tag = epoch * 128 + tag_slot
+  int tag_slot;
+  unsigned long long* xr_peer[8];   // every rank's receive block [T][tiles][kMaxRows][128] words
+  float* lg_peer[8];                // every rank's full logits [kMaxRows][ldy]
+  unsigned long long* key_peer[8];  // every rank's candidates [T][kMaxRows][2] (key, tag)
   int* err;
   unsigned long long timeout_ns;
 };
@@ -234,11 +243,63 @@ QORA_DEV float hw_max(float v) {
   return v;
 }
 
+// Tensor parallelism: this rank's partial of (tile t, row m, channels j0..j0+3 and +64)
+// goes to every rank as tagged 64-bit words (tag << 32 | f32 bits, one single-copy-atomic
+// store each); then the T ranks' partials are read back from this rank's block and summed
+// in rank order, so every rank gets the same bits. Waits are bounded (the CTA's error
+// flag is set and zeros are used on expiry).
+QORA_DEV void tp_sum_partials(const FusedArgs& a, int t, int m, int j0, float (&s0)[4], float (&s1)[4]) {
+  const unsigned tag = *a.epoch * 128u + (unsigned)a.tag_slot;
+  const size_t mine = (((size_t)a.rank * a.tiles + t) * kMaxRows + m) * kTileN + j0;
+  for (int p = 0; p < a.tp; ++p) {
+    unsigned long long* dst = a.xr_peer[p] + mine;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      ptx::st_relaxed_sys_b64(reinterpret_cast<uint64_t*>(dst + i),
+                              ((uint64_t)tag << 32) | __float_as_uint(s0[i]));
+      ptx::st_relaxed_sys_b64(reinterpret_cast<uint64_t*>(dst + 64 + i),
+                              ((uint64_t)tag << 32) | __float_as_uint(s1[i]));
+    }
+  }
+  float u0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, u1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  const unsigned long long* own = a.xr_peer[a.rank];
+  for (int p = 0; p < a.tp; ++p) {
+    const uint64_t* src =
+        reinterpret_cast<const uint64_t*>(own + (((size_t)p * a.tiles + t) * kMaxRows + m) * kTileN + j0);
+    uint64_t w[8];
+    const uint64_t t0 = ptx::globaltimer();
+    for (;;) {
+      bool ok = true;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        w[i] = ptx::ld_relaxed_sys_b64(src + i);
+        w[4 + i] = ptx::ld_relaxed_sys_b64(src + 64 + i);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ok &= (unsigned)(w[i] >> 32) == tag;
+      if (ok) break;
+      if (ptx::globaltimer() - t0 > a.timeout_ns) {
+        atomicExch(a.err, 1);
+        break;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      u0[i] = __fadd_rn(u0[i], __uint_as_float((unsigned)w[i]));
+      u1[i] = __fadd_rn(u1[i], __uint_as_float((unsigned)w[4 + i]));
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    s0[i] = u0[i];
+    s1[i] = u1[i];
+  }
+}
+
 // Epilogue of row m, channels j0..j0+3 and j0+64..j0+67 of tile t (s0 / s1: the summed
 // partials). Called by all lanes; rows are held by half-warps (q = lane % 16 picks j0 =
 // 4q), `act` false for rows past M. Statistics are reduced within the half-warp.
-QORA_DEV void finish_quad(const FusedArgs& a, int t, int m, int q, bool act, const float (&s0)[4],
-                          const float (&s1)[4]) {
+QORA_DEV void finish_quad(const FusedArgs& a, int t, int m, int q, bool act, float (&s0)[4], float (&s1)[4]) {
   const int j0 = 4 * q;
   if (a.ep == kEpStore) {
     if (act) {
@@ -274,6 +335,7 @@ QORA_DEV void finish_quad(const FusedArgs& a, int t, int m, int q, bool act, con
     }
   } else if (a.ep == kEpResidual) {
     float ss = 0.0f, mx = 0.0f;
+    if (act && a.tp > 1) tp_sum_partials(a, t, m, j0, s0, s1);
     if (act) {
       float* yr = a.y + (size_t)m * a.ldy + t * kTileN + j0;
       const float* rr = a.res + (size_t)m * a.ldy + t * kTileN + j0;
@@ -311,13 +373,20 @@ QORA_DEV void finish_quad(const FusedArgs& a, int t, int m, int q, bool act, con
   } else {  // kEpLogits
     unsigned long long k = 0ull;
     if (act) {
-      float* yr = a.y + (size_t)m * a.ldy + t * kTileN + j0;
+      const size_t col = (size_t)a.col0 + t * kTileN + j0;
+      float* yr = a.y + (size_t)m * a.ldy + col;
       *reinterpret_cast<float4*>(yr) = make_float4(s0[0], s0[1], s0[2], s0[3]);
       *reinterpret_cast<float4*>(yr + 64) = make_float4(s1[0], s1[1], s1[2], s1[3]);
+      for (int p = 0; p < a.tp; ++p) {  // every other rank's copy of the full logits
+        if (p == a.rank) continue;
+        float* pr = a.lg_peer[p] + (size_t)m * a.ldy + col;
+        *reinterpret_cast<float4*>(pr) = make_float4(s0[0], s0[1], s0[2], s0[3]);
+        *reinterpret_cast<float4*>(pr + 64) = make_float4(s1[0], s1[1], s1[2], s1[3]);
+      }
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const unsigned long long k0 = am_key(s0[i], (unsigned)(t * kTileN + j0 + i));
-        const unsigned long long k1 = am_key(s1[i], (unsigned)(t * kTileN + j0 + 64 + i));
+        const unsigned long long k0 = am_key(s0[i], (unsigned)(col + i));
+        const unsigned long long k1 = am_key(s1[i], (unsigned)(col + 64 + i));
         if (k0 > k) k = k0;
         if (k1 > k) k = k1;
       }
@@ -376,16 +445,53 @@ QORA_DEV void finish_tile(const FusedArgs& a, int t, long long* s_cb) {
     finish_quad(a, t, m, q, act, s0, s1);
   }
   ptx::named_bar(1, 128);  // s_cb is free again
-  if (a.ep == kEpLogits && e == 0) {
-    __threadfence();
-    const unsigned old = atomicAdd(a.sync + 2, 1u);
-    if (old == (unsigned)a.tiles - 1) {
-      __threadfence();
-      for (int m = 0; m < a.M; ++m) {
-        const unsigned long long k = atomicExch(&a.am_key[m], 0ull);
+  if (a.ep == kEpLogits) {
+    int* s_flag = reinterpret_cast<int*>(s_cb);  // s_cb is free: reuse one word as a flag
+    if (e == 0) {
+      if (a.tp > 1)
+        __threadfence_system();  // this CTA's peer logits stores before its arrival
+      else
+        __threadfence();
+      const unsigned old = atomicAdd(a.sync + 2, 1u);
+      const bool last = old == (unsigned)a.tiles - 1;
+      if (last) __threadfence_system();
+      *s_flag = last ? 1 : 0;
+    }
+    ptx::named_bar(1, 128);
+    const bool last = *s_flag != 0;
+    ptx::named_bar(1, 128);
+    if (last) {
+      // every tile of this rank is done: its row candidates (and, under tensor
+      // parallelism, the exchange of candidates: release after this rank's logits, the
+      // first maximum over ranks in rank order — the same on every rank)
+      const unsigned tag = a.tp > 1 ? *a.epoch * 128u + (unsigned)a.tag_slot : 0u;
+      for (int m = e; m < a.M; m += 128) {
+        unsigned long long k = atomicExch(&a.am_key[m], 0ull);
+        if (a.tp > 1) {
+          for (int p = 0; p < a.tp; ++p) {
+            uint64_t* slot = reinterpret_cast<uint64_t*>(a.key_peer[p] + ((size_t)a.rank * kMaxRows + m) * 2);
+            ptx::st_relaxed_sys_b64(slot, k);
+            ptx::st_release_sys_b64(slot + 1, tag);
+          }
+          unsigned long long best = 0ull;
+          for (int p = 0; p < a.tp; ++p) {
+            const uint64_t* slot =
+                reinterpret_cast<const uint64_t*>(a.key_peer[a.rank] + ((size_t)p * kMaxRows + m) * 2);
+            const uint64_t t0 = ptx::globaltimer();
+            while (ptx::ld_acquire_sys_b64(slot + 1) != tag) {
+              if (ptx::globaltimer() - t0 > a.timeout_ns) {
+                atomicExch(a.err, 1);
+                break;
+              }
+            }
+            const unsigned long long kp = ptx::ld_relaxed_sys_b64(slot);
+            if (kp > best) best = kp;
+          }
+          k = best;
+        }
         a.am_out[m] = k ? 0xFFFFFFFFu - (unsigned)(k & 0xFFFFFFFFull) : 0u;
       }
-      atomicExch(a.sync + 2, 0u);
+      if (e == 0) atomicExch(a.sync + 2, 0u);
     }
   }
 }
@@ -657,13 +763,13 @@ __global__ void row_max_kernel(const float* x, int K, float* mx) {
 }
 
 // One-time re-tiling of an f16 matrix into [tiles][chunks][16 KB] UMMA tiles. src is
-// N-major [K][ld] (columns col0..col0+N-1 taken) or K-major [N][ld]. Channel n lands in
-// tile t0 + n / group at row o0 + n % group (group 128: whole tiles; group 64: one half
-// of each tile, for the interleaved gate|up matrix).
+// N-major [K][ld] (columns col0..col0+N-1 taken) or K-major [N][ld] (rows = channels).
+// Channel n lands in tile t0 + n / group at row o0 + n % group (group 128: whole tiles;
+// group 64: one half of each tile, for the interleaved gate|up matrix); `chunks` is the
+// destination's chunks per tile (>= K/64; k beyond K stays as the destination holds it).
 __global__ void tile_weights_kernel(const __half* src, long long ld, int kmajor, int K, int N, int col0,
-                                    int t0, int group, int o0, uint8_t* dst) {
+                                    int t0, int group, int o0, int chunks, uint8_t* dst) {
   const long long units = (long long)N * (K / 8);  // 16-byte output units: 8 k of one channel
-  const int chunks = K / kChunkK;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < units; i += (long long)gridDim.x * blockDim.x) {
     const int n = (int)(i % N);
     const int k8 = (int)(i / N);

@@ -80,9 +80,9 @@ def test_invalid_view_rejected_before_device_use(pkg, qf):
                         fmt=qf.FORMAT_F16)
     with pytest.raises(pkg.QoraError, match="UNSUPPORTED"):
         pkg.DecodeWeights(model=m2)
-    # F16 engines are single-GPU in this build
-    m3 = qf.synth_model(seed=0, num_layers=1, vocab=64, hidden=1024, intermediate=512,
+    # tensor-parallel degrees other than 1, 2, 4 and 8 are rejected for either format
+    m3 = qf.synth_model(seed=0, num_layers=1, vocab=128, hidden=1024, intermediate=512,
                         num_heads=8, num_kv_heads=2, head_dim=128, rope_rows=8,
                         fmt=qf.FORMAT_F16)
-    with pytest.raises(pkg.QoraError, match="UNSUPPORTED"):
-        pkg.DecodeWeights(model=m3, tp_size=2, tp_rank=0)
+    with pytest.raises(pkg.QoraError, match="tp_size 3"):
+        pkg.DecodeWeights(model=m3, tp_size=3, tp_rank=0)

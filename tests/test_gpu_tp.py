@@ -103,3 +103,101 @@ def test_tensor_parallel_matches_oracle(tp, qf, orc):
         assert np.array_equal(toks, ref[1:]), f"rank {rank}: min oracle margin {margins.min()}"
         assert np.array_equal(step_logits, results[0][4])  # every rank holds the same logits
     print(f"tp={tp}: prefill logits rel-L2 {rel_l2(results[0][1], lo):.3e}")
+
+
+# ---------------------------------------------------------------- F16 (config 5) under TP
+def _small_f16(qf):
+    # heads 8/2, MLP 1536 (768/384/192 channels per rank), vocab 2048 (16 tiles of 128)
+    return qf.synth_model(seed=23, fmt=qf.FORMAT_F16, num_layers=3, vocab=2048, hidden=1024,
+                          intermediate=1536, num_heads=8, num_kv_heads=2, head_dim=128, rope_rows=256)
+
+
+F16_LENS = [5, 12, 3, 9]
+F16_GEN = 12
+
+
+def _worker_f16(rank, tp, to_parent, from_parent):
+    try:
+        import importlib
+        import os
+        import sys
+        root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+        sys.path.insert(0, root)
+        pkg = importlib.import_module("qora-llm_b200")
+        model = _small_f16(pkg.qora_format)
+        w = pkg.DecodeWeights(model=model, device=rank, tp_size=tp, tp_rank=rank)
+        to_parent.put(("handle", rank, w.tp_export()))
+        w.tp_connect(from_parent.get(timeout=120))
+        rng = np.random.default_rng(6)
+        prompts = [rng.integers(0, w.vocab, size=n).astype(np.uint32) for n in F16_LENS]
+        kv = w.new_kv(64, batch=len(F16_LENS))
+        firsts, logits0 = [], None
+        for b, p in enumerate(prompts):
+            f, lg = w.prefill(kv, p, want_logits=(b == 0), seq=b)
+            firsts.append(f)
+            if b == 0:
+                logits0 = lg
+        toks = w.generate_greedy_batch(kv, firsts, F16_GEN)
+        am, step_logits = w.decode_batch(kv, toks[-1], want_logits=True)
+        to_parent.put(("done", rank, (firsts, logits0, toks, am, step_logits)))
+        w.close()
+    except Exception as exc:  # reported to the parent, which fails the test
+        to_parent.put(("error", rank, repr(exc)))
+
+
+def _run_tp_f16(tp):
+    ctx = mp.get_context("spawn")
+    to_parent = ctx.Queue()
+    inboxes = [ctx.Queue() for _ in range(tp)]
+    procs = [ctx.Process(target=_worker_f16, args=(r, tp, to_parent, inboxes[r]), daemon=True) for r in range(tp)]
+    for p in procs:
+        p.start()
+    try:
+        handles, results = {}, {}
+        while len(results) < tp:
+            kind, rank, payload = to_parent.get(timeout=600)
+            if kind == "error":
+                raise AssertionError(f"rank {rank}: {payload}")
+            if kind == "handle":
+                handles[rank] = payload
+                if len(handles) == tp:
+                    for q in inboxes:
+                        q.put([handles[r] for r in range(tp)])
+            else:
+                results[rank] = payload
+        return results
+    except queue.Empty:
+        raise AssertionError("tensor-parallel workers did not finish in time")
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.terminate()
+
+
+@pytest.mark.parametrize("tp", [2, 4, 8])
+def test_tensor_parallel_f16_batched_matches_oracle(tp, qf, orc):
+    """F16 engines split over tp GPUs (tcgen05 GEMMs with the o_proj / down partials and
+    the lm_head candidates exchanged over NVLink): 4 sequences prefilled then decoded
+    together; every rank returns the oracle's greedy tokens and the same logits."""
+    import torch
+    if torch.cuda.device_count() < tp:
+        pytest.skip(f"needs {tp} GPUs")
+    results = _run_tp_f16(tp)
+    model = _small_f16(qf)
+    orc.set_threads(8)
+    om = orc.OracleModel(model)
+    rng = np.random.default_rng(6)
+    prompts = [rng.integers(0, model.vocab, size=n).astype(np.uint32) for n in F16_LENS]
+    refs = [om.generate_greedy(p, F16_GEN + 1) for p in prompts]
+    lo = om.prefill(prompts[0], om.new_kv())
+    for rank in range(tp):
+        firsts, logits0, toks, am, step_logits = results[rank]
+        assert rel_l2(logits0, lo) < LOGIT_TOL, (rank, rel_l2(logits0, lo))
+        for b in range(len(F16_LENS)):
+            ref, margins = refs[b]
+            assert firsts[b] == ref[0]
+            assert np.array_equal(toks[:, b], ref[1:]), f"rank {rank} seq {b}: min margin {margins.min()}"
+        assert np.array_equal(step_logits, results[0][4])
+        assert np.array_equal(am, results[0][3])
+    print(f"F16 tp={tp}: prefill logits rel-L2 {rel_l2(results[0][1], lo):.3e}")
