@@ -348,14 +348,12 @@ def f16_cpu_sample(model, budget_s, threads):
 def run_f16(args, rank, world, local_rank):
     """B independent sequences, 128-token prompts, greedy batched
     decode on one GPU (tcgen05 GEMMs)."""
-    if world > 1:
-        if rank == 0:
-            print(json.dumps({"metric": F16_METRIC, "unavailable": "tensor parallelism of F16 engines is not in this build"}))
-        return 0
     B, K, W = args.batch, args.steps, args.warmup
     threads = os.cpu_count() or 1
     model = synth_f16(args.layers)
     if args.impl == "reference":
+        if rank != 0:
+            return 0
         v, n = f16_cpu_sample(model, args.cpu_seconds, threads)
         line = {"impl": "reference", "metric": F16_METRIC, "value": v, "unit": "tok/s", "n_gpus": 1, "steps": n,
                 "warmup": 1, "ms_per_step": 1000.0 / v, "higher_is_better": True, "scaling": "strong",
@@ -372,7 +370,17 @@ def run_f16(args, rank, world, local_rank):
     import torch
     pkg = importlib.import_module("qora-llm_b200")
     torch.cuda.set_device(local_rank)
-    eng = pkg.DecodeWeights(model=model, device=local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+        eng = pkg.DecodeWeights(model=model, device=local_rank, tp_size=world, tp_rank=rank)
+        handles = [None] * world
+        dist.all_gather_object(handles, eng.tp_export())
+        eng.tp_connect(handles)
+    else:
+        eng = pkg.DecodeWeights(model=model, device=local_rank)
     prompts = f16_prompts(B)
     cap = F16_PROMPT + W + K + 8
 
@@ -391,34 +399,48 @@ def run_f16(args, rank, world, local_rank):
     kv_p.close()
     warm = eng.generate_greedy_batch(kv, firsts, W)
     nxt = warm[-1]
+    if dist:
+        dist.barrier()
     torch.cuda.synchronize()
     with ClockSampler(local_rank) as clk:
         _, ms = eng.generate_greedy_batch(kv, nxt, K, timed=True)
     torch.cuda.synchronize()
+    if dist:
+        ms_t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+        ms = float(ms_t.item())
     value = B * K / (ms / 1000.0)
     # ---- end to end through the C ABI: host tokens in, host argmax out, every step
     kv2, firsts2 = prefilled()
     t = np.asarray(firsts2, np.uint32)
     for _ in range(W):
         t, _ = eng.decode_batch(kv2, t)
+    if dist:
+        dist.barrier()
     t0 = time.perf_counter()
     for _ in range(K):
         t, _ = eng.decode_batch(kv2, t)
     e2e_s = time.perf_counter() - t0
+    if dist:
+        e_t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
+        dist.all_reduce(e_t, op=dist.ReduceOp.MAX)
+        e2e_s = float(e_t.item())
     e2e = B * K / e2e_s
     peak, peak_kind = peaks()
     mean_pos = F16_PROMPT + W + (K - 1) / 2.0 + 1
     step_bytes = f16_bytes_per_step(args.layers) + B * kv_bytes_per_pos(args.layers) * mean_pos
-    achieved = step_bytes / (ms / K / 1000.0) / 1e9
+    rank_bytes = step_bytes / world  # weights, lm_head rows and (to tp 4) KV heads split evenly
+    achieved = rank_bytes / (ms / K / 1000.0) / 1e9
     line = {
-        "metric": F16_METRIC, "value": value, "unit": "tok/s", "n_gpus": 1, "steps": K, "warmup": W,
+        "metric": F16_METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
         "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "f16 weights x f32 activations (f16 hi+lo split), f32 accumulate",
         "data": "synthetic (seeded random-init SmolLM3-3B F16 weights, random prompt ids)",
         "config": {"workload": f"config 5: SmolLM3-3B F16 (36 layers, vocab 128256), batch {B}, "
                                f"{F16_PROMPT}-token prompts, greedy decode",
                    "batch": B, "prompt": F16_PROMPT, "layers": args.layers, "kv_len_mean": mean_pos,
-                   "parallelism": "single GPU", "bytes_per_step": step_bytes,
+                   "parallelism": "single GPU" if world == 1 else f"tp{world} (tensor parallel, NVLink peer exchange)",
+                   "bytes_per_step": step_bytes,
                    "l2": f"inputs larger than L2: {f16_bytes_per_step(args.layers) / 1e9:.2f} GB of weights "
                          "streamed per step",
                    "prefill_tok_s": B * F16_PROMPT / prefill_s},
@@ -426,11 +448,12 @@ def run_f16(args, rank, world, local_rank):
         "gpu_launches": (eng.launches_per_step() + 1) * K,
         "roofline": dict(bound="hbm", achieved=achieved, peak=peak, peak_kind=f"{peak_kind} hbm_gbs (copy)",
                          unit="GB/s", frac=achieved / peak, traffic=None,
-                         kernel="whole batched decode step (4 tcgen05 GEMMs + attention per layer, lm_head)",
-                         bytes_per_launch=step_bytes, us_per_launch=1000 * ms / K, launches_timed=K),
+                         kernel="whole batched decode step (4 tcgen05 GEMMs + attention per layer, lm_head)"
+                                + (f", per rank of a {world}-way tensor-parallel group" if world > 1 else ""),
+                         bytes_per_launch=rank_bytes, us_per_launch=1000 * ms / K, launches_timed=K),
         "clocks": clk.summary(),
     }
-    if not args.no_cpu_baseline:
+    if not args.no_cpu_baseline and rank == 0 and world == 1:
         v, n = f16_cpu_sample(model, args.cpu_seconds, threads)
         line["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": threads, "kind": "port",
                                 "sample": f"{n} forward_decode_raw steps of one F16 sequence, {threads} threads "
@@ -438,7 +461,11 @@ def run_f16(args, rank, world, local_rank):
     kv.close()
     kv2.close()
     eng.close()
-    print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
     return 0
 
 
