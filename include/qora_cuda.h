@@ -120,6 +120,21 @@ void qora_engine_destroy(qora_engine* engine);
  * ranks' handles concatenated in rank order and maps the peers' buffers; decode steps
  * are refused until it succeeds. All ranks must run on GPUs of one NVLink domain. */
 qora_status qora_tp_export(qora_engine* engine, void* buf, size_t cap, size_t* len);
+
+/* The shard rank tp_rank of a tp_size-way group holds (host-only arithmetic, no device
+ * needed): query heads [q_head0, +q_heads), KV heads [kv_head0, +kv_heads) (split while
+ * tp_size divides the KV heads, else the one KV head of the rank's query heads), gate/up
+ * columns = down rows [mlp0, +mlp_n) (F16: computed as mlp_padded channels, the extra
+ * ones zero), lm_head rows [vocab0, +vocab_n) (F16: whole 128-row tiles). */
+typedef struct qora_tp_shard {
+    uint32_t q_head0, q_heads;
+    uint32_t kv_head0, kv_heads;
+    uint32_t mlp0, mlp_n, mlp_padded;
+    uint32_t vocab0, vocab_n;
+} qora_tp_shard;
+qora_status qora_tp_plan(uint32_t format, uint32_t num_heads, uint32_t num_kv_heads,
+                         uint32_t intermediate, uint32_t vocab, int32_t tp_size,
+                         int32_t tp_rank, qora_tp_shard* out);
 qora_status qora_tp_connect(qora_engine* engine, const void* handles, size_t len_per_rank);
 
 /* Geometry of a loaded engine. */

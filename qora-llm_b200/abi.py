@@ -36,6 +36,12 @@ class EngineOptions(C.Structure):
                 ("tp_size", C.c_int32), ("tp_rank", C.c_int32)]
 
 
+class TpShard(C.Structure):
+    """qora_tp_shard (include/qora_cuda.h)."""
+    _fields_ = [(n, C.c_uint32) for n in ("q_head0", "q_heads", "kv_head0", "kv_heads", "mlp0", "mlp_n",
+                                          "mlp_padded", "vocab0", "vocab_n")]
+
+
 class Sampling(C.Structure):
     """qora_sampling (include/qora_cuda.h)."""
     _fields_ = [("temperature", C.c_float), ("top_p", C.c_float), ("top_k", C.c_uint32),

@@ -469,6 +469,43 @@ qora_status validate_view(const qora_weights_view* w) {
   return QORA_OK;
 }
 
+// The tensor-parallel shard of rank r of T (both formats): q heads split evenly; KV heads
+// split while they divide, else each rank keeps the KV head its q heads use; gate/up
+// columns and down rows [r*I/T, +I/T) (F16: padded to whole 64-channel tile halves);
+// lm_head rows split evenly (F16: by 128-row tiles).
+qora_status tp_plan(uint32_t format, uint32_t nh, uint32_t nkvh, uint32_t I, uint32_t V, int T, int r,
+                    qora_tp_shard* o) {
+  if (T != 1 && T != 2 && T != 4 && T != 8) return fail(QORA_ERR_INVALID, "tp_size %d (1, 2, 4 or 8)", T);
+  if (r < 0 || r >= T) return fail(QORA_ERR_INVALID, "tp_rank %d of %d", r, T);
+  if (nh == 0 || nkvh == 0 || nh % T != 0 || (nkvh % T != 0 && T % nkvh != 0))
+    return fail(QORA_ERR_UNSUPPORTED, "tp_size %d does not divide heads %u/%u", T, nh, nkvh);
+  o->q_heads = nh / T;
+  o->q_head0 = r * o->q_heads;
+  o->kv_heads = nkvh % T == 0 ? nkvh / T : 1;
+  o->kv_head0 = nkvh % T == 0 ? r * o->kv_heads : r / (T / nkvh);
+  if (o->q_heads % o->kv_heads != 0 || o->q_heads / o->kv_heads > (uint32_t)kGrp)
+    return fail(QORA_ERR_UNSUPPORTED, "tp_size %d: %u query heads over %u kv heads per rank", T, o->q_heads,
+                o->kv_heads);
+  if (format == QORA_FORMAT_Q4) {
+    if ((I / kGroup) % T != 0)
+      return fail(QORA_ERR_UNSUPPORTED, "tp_size %d does not divide the %u MLP groups", T, I / kGroup);
+    o->mlp_n = I / T;
+    o->mlp_padded = o->mlp_n;
+    o->vocab0 = (uint32_t)((uint64_t)r * V / T);
+    o->vocab_n = (uint32_t)((uint64_t)(r + 1) * V / T) - o->vocab0;
+  } else {
+    if (I % T != 0 || (I / T) % 8 != 0)
+      return fail(QORA_ERR_UNSUPPORTED, "tp_size %d does not divide the MLP width %u in multiples of 8", T, I);
+    o->mlp_n = I / T;
+    o->mlp_padded = (o->mlp_n + 63) / 64 * 64;
+    const uint32_t vt = V / 128;
+    o->vocab0 = (uint32_t)((uint64_t)r * vt / T) * 128;
+    o->vocab_n = (uint32_t)((uint64_t)(r + 1) * vt / T) * 128 - o->vocab0;
+  }
+  o->mlp0 = r * o->mlp_n;
+  return QORA_OK;
+}
+
 qora_status upload(qora_engine* e, void* dst, const void* src, size_t bytes) {
   QCUDA(cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice));
   return QORA_OK;
@@ -543,16 +580,12 @@ qora_status engine_init(qora_engine* e, const qora_weights_view* w) {
   e->nkv_total = L0.num_kv_heads;
   e->rope_rows = (uint32_t)w->rope_rows;
   {
-    // tensor-parallel shard of this rank: q heads split evenly; kv heads split while
-    // they divide, otherwise each rank keeps the one kv head its q heads use
-    const int T = e->tp, nh = (int)e->nh, nkvh = (int)e->nkv_total, I = (int)e->inter;
-    if (nh % T != 0 || (nkvh % T != 0 && T % nkvh != 0) || (I / kGroup) % T != 0)
-      return fail(QORA_ERR_UNSUPPORTED, "tp_size %d does not divide heads %d/%d and MLP groups %d", T, nh,
-                  nkvh, I / kGroup);
-    e->nh_l = nh / T;
-    e->nkv_l = nkvh % T == 0 ? nkvh / T : 1;
-    e->kv0 = nkvh % T == 0 ? e->rank * e->nkv_l : e->rank / (T / nkvh);
-    e->inter_l = I / T;
+    qora_tp_shard sh{};
+    QCHECK(tp_plan(QORA_FORMAT_Q4, e->nh, e->nkv_total, e->inter, e->vocab, e->tp, e->rank, &sh));
+    e->nh_l = (int)sh.q_heads;
+    e->nkv_l = (int)sh.kv_heads;
+    e->kv0 = (int)sh.kv_head0;
+    e->inter_l = (int)sh.mlp_n;
     e->nkv = (uint32_t)e->nkv_l;  // KV heads held by this engine's caches
   }
   e->sms = sm_count(e->device);
@@ -1141,22 +1174,15 @@ qora_status f16_engine_init(qora_engine* e, const qora_weights_view* w) {
   const int T = e->tp, r = e->rank;
   const int H = (int)e->hidden, I = (int)e->inter, V = (int)e->vocab;
   {
-    // this rank's shard: q heads split evenly; kv heads split while they divide, else the
-    // kv head of the rank's q heads; gate/up columns and down rows [r*I/T, +I/T) padded
-    // to whole 64-channel tile halves; vocab split by 128-row tiles
-    const int nh = (int)e->nh, nkvh = (int)e->nkv_total;
-    if (nh % T != 0 || (nkvh % T != 0 && T % nkvh != 0) || I % T != 0 || (I / T) % 8 != 0)
-      return fail(QORA_ERR_UNSUPPORTED, "tp_size %d does not divide heads %d/%d and MLP width %d", T, nh, nkvh, I);
-    e->nh_l = nh / T;
-    e->nkv_l = nkvh % T == 0 ? nkvh / T : 1;
-    e->kv0 = nkvh % T == 0 ? r * e->nkv_l : r / (T / nkvh);
-    if (e->nh_l % e->nkv_l != 0 || e->nh_l / e->nkv_l > kGrp)
-      return fail(QORA_ERR_UNSUPPORTED, "tp_size %d: %d query heads over %d kv heads per rank", T, e->nh_l, e->nkv_l);
-    e->inter_l = (I / T + 63) / 64 * 64;
-    e->f_it = I / T;
-    const int vt = V / umma::kTileN;
-    e->f_vt0 = r * vt / T;
-    e->f_vt1 = (r + 1) * vt / T;
+    qora_tp_shard sh{};
+    QCHECK(tp_plan(QORA_FORMAT_F16, e->nh, e->nkv_total, (uint32_t)I, (uint32_t)V, T, r, &sh));
+    e->nh_l = (int)sh.q_heads;
+    e->nkv_l = (int)sh.kv_heads;
+    e->kv0 = (int)sh.kv_head0;
+    e->inter_l = (int)sh.mlp_padded;
+    e->f_it = (int)sh.mlp_n;
+    e->f_vt0 = (int)(sh.vocab0 / umma::kTileN);
+    e->f_vt1 = (int)((sh.vocab0 + sh.vocab_n) / umma::kTileN);
   }
   e->nkv = (uint32_t)e->nkv_l;
   e->sms = sm_count(e->device);
@@ -1882,6 +1908,13 @@ qora_status qora_tp_connect(qora_engine* e, const void* handles, size_t len_per_
   e->tp_connected = true;
   for (qora_kv* kv : e->kvs) kv->mk_ready = false;  // rebuild kernel arguments with the peers
   return QORA_OK;
+}
+
+qora_status qora_tp_plan(uint32_t format, uint32_t num_heads, uint32_t num_kv_heads, uint32_t intermediate,
+                         uint32_t vocab, int32_t tp_size, int32_t tp_rank, qora_tp_shard* out) {
+  if (!out) return fail(QORA_ERR_INVALID, "NULL argument");
+  if (format != QORA_FORMAT_Q4 && format != QORA_FORMAT_F16) return fail(QORA_ERR_INVALID, "format %u", format);
+  return tp_plan(format, num_heads, num_kv_heads, intermediate, vocab, tp_size, tp_rank, out);
 }
 
 qora_status qora_engine_info(const qora_engine* e, uint32_t* num_layers, uint32_t* vocab,

@@ -60,6 +60,7 @@ SIGNATURES = {
     "qora_engine_get_trace": (C.c_int, [_vp, _vp, C.c_size_t, _P(C.c_size_t)]),
     "qora_tp_export": (C.c_int, [_vp, _vp, C.c_size_t, _P(C.c_size_t)]),
     "qora_tp_connect": (C.c_int, [_vp, C.c_char_p, C.c_size_t]),
+    "qora_tp_plan": (C.c_int, [_u32, _u32, _u32, _u32, _u32, _i32, _i32, _vp]),
     "qora_q4_gemv": (C.c_int, [_vp, _vp, _vp, _u64, _u64, _vp, _vp]),
     "qora_q4_gemv_static": (C.c_int, [_vp, _vp, _vp, _u64, _u64, _vp, _vp]),
     "qora_q4_dequant": (C.c_int, [_vp, _vp, _u64, _u64, _u64, _vp, _vp]),
@@ -368,3 +369,10 @@ def sample_logits(logits_ptr, vocab, history_ptr, n_history, temperature, top_p,
     check(lib().qora_sample_logits(logits_ptr, vocab, history_ptr, n_history, C.byref(p), C.byref(st),
                                    C.byref(tok), _stream_ptr(stream)))
     return tok.value, st.value
+
+
+def tp_plan(fmt: int, num_heads: int, num_kv_heads: int, intermediate: int, vocab: int, tp: int, rank: int) -> dict:
+    """The shard a tensor-parallel rank holds (qora_tp_plan; host arithmetic only)."""
+    out = abi.TpShard()
+    check(lib().qora_tp_plan(fmt, num_heads, num_kv_heads, intermediate, vocab, tp, rank, C.byref(out)))
+    return {n: getattr(out, n) for n, _ in abi.TpShard._fields_}
