@@ -16,6 +16,10 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
 #include <cstring>
 #include <map>
 #include <memory>
@@ -1644,12 +1648,27 @@ qora_status entry_scratch(int dev, size_t pf, size_t nc, int lm_n, EntryScratch*
 
 // ------------------------------------------------------------------ .qora reader
 // load_model (src/save.rs:154-210) into host vectors, then the borrowed view.
+// The file is memory-mapped read-only; the large arrays (Q4 nibbles, F16 weights) are
+// used in place (they are only copied byte-wise: to the device, or into the re-tiling),
+// the small ones (scales, norms, RoPE tables) are copied out aligned.
+struct MappedFile {
+  int fd = -1;
+  const uint8_t* base = nullptr;
+  size_t size = 0;
+  ~MappedFile() {
+    if (base) munmap(const_cast<uint8_t*>(base), size);
+    if (fd >= 0) close(fd);
+  }
+};
+
 struct FileMat {
   uint64_t k = 0, n = 0;
-  std::vector<uint8_t> packed;
-  std::vector<uint16_t> scales, data;
+  const uint8_t* packed = nullptr;   // in the mapping
+  std::vector<uint16_t> scales;
+  const uint16_t* data = nullptr;    // in the mapping (read byte-wise only)
 };
 struct FileModel {
+  MappedFile map;
   uint8_t format = 0;
   uint32_t num_layers = 0, vocab = 0, hidden = 0, half = 0;
   std::vector<uint8_t> no_rope;
@@ -1665,35 +1684,69 @@ struct FileModel {
 };
 
 struct FileReader {
-  FILE* f = nullptr;
+  const uint8_t* p = nullptr;
+  size_t left = 0;
   std::string err;
   bool ok = true;
-  void need(void* dst, size_t n) {
-    if (ok && n && std::fread(dst, 1, n, f) != n) { ok = false; err = "short read"; }
+  const uint8_t* take(size_t n) {  // n bytes at the cursor, or nullptr (short file)
+    if (!ok) return nullptr;
+    if (n > left) {
+      ok = false;
+      err = "short read";
+      return nullptr;
+    }
+    const uint8_t* q = p;
+    p += n;
+    left -= n;
+    return q;
   }
-  uint32_t u32() { uint32_t v = 0; need(&v, 4); return v; }
-  uint64_t u64() { uint64_t v = 0; need(&v, 8); return v; }
-  uint8_t u8() { uint8_t v = 0; need(&v, 1); return v; }
-  template <typename T> void vec(std::vector<T>& out) {
-    const uint64_t len = u64();
-    if (!ok) return;
-    if (len > (1ull << 36)) { ok = false; err = "implausible vector length"; return; }
+  template <typename T>
+  T scalar() {
+    T v{};
+    if (const uint8_t* q = take(sizeof(T))) std::memcpy(&v, q, sizeof(T));
+    return v;
+  }
+  uint32_t u32() { return scalar<uint32_t>(); }
+  uint64_t u64() { return scalar<uint64_t>(); }
+  uint8_t u8() { return scalar<uint8_t>(); }
+  // length-prefixed array: its place in the mapping
+  template <typename T>
+  const uint8_t* span(uint64_t& len) {
+    len = u64();
+    if (!ok) return nullptr;
+    if (len > (1ull << 36)) {
+      ok = false;
+      err = "implausible vector length";
+      return nullptr;
+    }
+    return take(len * sizeof(T));
+  }
+  template <typename T>
+  void vec(std::vector<T>& out) {
+    uint64_t len = 0;
+    const uint8_t* q = span<T>(len);
+    if (!q) return;
     out.resize(len);
-    need(out.data(), len * sizeof(T));
+    if (len) std::memcpy(out.data(), q, len * sizeof(T));
   }
   void mat(uint8_t fmt, FileMat& m) {
     m.k = u64();
     m.n = u64();
     if (fmt == 1) {
-      vec(m.packed);
+      uint64_t np = 0;
+      m.packed = span<uint8_t>(np);
       vec(m.scales);
-      if (ok && (m.n % kGroup || m.packed.size() != m.k * m.n / 2 || m.scales.size() != m.k * m.n / kGroup)) {
+      if (ok && (m.n % kGroup || np != m.k * m.n / 2 || m.scales.size() != m.k * m.n / kGroup)) {
         ok = false;
         err = "q4 weight size mismatch";
       }
     } else if (fmt == 0) {
-      vec(m.data);
-      if (ok && m.data.size() != m.k * m.n) { ok = false; err = "f16 weight size mismatch"; }
+      uint64_t nd = 0;
+      m.data = reinterpret_cast<const uint16_t*>(span<uint16_t>(nd));
+      if (ok && nd != m.k * m.n) {
+        ok = false;
+        err = "f16 weight size mismatch";
+      }
     } else {
       ok = false;
       err = "Unknown format id " + std::to_string(fmt);
@@ -1702,12 +1755,21 @@ struct FileReader {
 };
 
 qora_status read_qora_file(const char* path, FileModel& fm) {
+  fm.map.fd = open(path, O_RDONLY);
+  if (fm.map.fd < 0) return fail(QORA_ERR_IO, "cannot open %s", path);
+  struct stat st{};
+  if (fstat(fm.map.fd, &st) != 0) return fail(QORA_ERR_IO, "cannot stat %s", path);
+  fm.map.size = (size_t)st.st_size;
+  if (fm.map.size > 0) {
+    void* base = mmap(nullptr, fm.map.size, PROT_READ, MAP_PRIVATE, fm.map.fd, 0);
+    if (base == MAP_FAILED) return fail(QORA_ERR_IO, "cannot map %s", path);
+    fm.map.base = static_cast<const uint8_t*>(base);
+    madvise(base, fm.map.size, MADV_SEQUENTIAL);
+  }
   FileReader r;
-  r.f = std::fopen(path, "rb");
-  if (!r.f) return fail(QORA_ERR_IO, "cannot open %s", path);
-  std::setvbuf(r.f, nullptr, _IOFBF, 8 << 20);
-  char magic[4] = {0, 0, 0, 0};
-  r.need(magic, 4);
+  r.p = fm.map.base;
+  r.left = fm.map.size;
+  const uint8_t* magic = r.take(4);
   if (r.ok && std::memcmp(magic, "QOR3", 4) != 0) { r.ok = false; r.err = "Invalid magic bytes"; }
   const uint32_t version = r.u32();
   if (r.ok && version != 1) { r.ok = false; r.err = "Unsupported version " + std::to_string(version) + ", expected 1"; }
@@ -1734,7 +1796,6 @@ qora_status read_qora_file(const char* path, FileModel& fm) {
   r.vec(fm.cos_t);
   r.vec(fm.sin_t);
   const bool io_short = !r.ok && r.err == "short read";
-  std::fclose(r.f);
   if (!r.ok) return fail(io_short ? QORA_ERR_IO : QORA_ERR_INVALID, "%s: %s", path, r.err.c_str());
   if (fm.no_rope.size() != fm.num_layers) return fail(QORA_ERR_INVALID, "no_rope_layers length != num_layers");
   for (uint32_t i = 0; i < fm.num_layers; ++i) {
@@ -1749,9 +1810,9 @@ qora_status read_qora_file(const char* path, FileModel& fm) {
 
 qora_matrix_view mview(const FileMat& m) {
   qora_matrix_view v{};
-  v.packed = m.packed.empty() ? nullptr : m.packed.data();
+  v.packed = m.packed;
   v.scales = m.scales.empty() ? nullptr : m.scales.data();
-  v.data = m.data.empty() ? nullptr : m.data.data();
+  v.data = m.data;
   v.k = m.k;
   v.n = m.n;
   return v;

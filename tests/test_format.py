@@ -110,3 +110,31 @@ def test_quantizer_round_trip(qf):
     q[:, 0::2] = (packed.reshape(8, 32) & 15).astype(np.int16) - 8
     q[:, 1::2] = (packed.reshape(8, 32) >> 4).astype(np.int16) - 8
     assert np.abs(q).max() == 7
+
+
+@pytest.mark.parametrize("kind", sorted(CORRUPTIONS))
+def test_corrupted_engine_reader(tmp_path, qf, pkg, kind):
+    """The engine's own (memory-mapped) reader rejects the same files before any device
+    work: a truncated file is an I/O error, the rest are invalid contents."""
+    mut, msg = CORRUPTIONS[kind]
+    p = _corrupt(tmp_path, qf, mut)
+    with pytest.raises(pkg.QoraError) as ei:
+        pkg.DecodeWeights(path=str(p))
+    want = 2 if msg == "short read" else 1  # QORA_ERR_IO / QORA_ERR_INVALID
+    assert ei.value.status == want, str(ei.value)
+
+
+def test_engine_reader_accepts_valid_file(tmp_path, qf, pkg):
+    """A well-formed file passes the engine's reader and view validation; without a GPU the
+    first failure is the device (QORA_ERR_CUDA), with one the engine loads."""
+    try:
+        import torch
+        if torch.cuda.is_available():
+            pytest.skip("a GPU is present (the GPU tests load files)")
+    except Exception:
+        pass
+    p = tmp_path / "ok.qora"
+    qf.write_qora(tiny(qf), p)
+    with pytest.raises(pkg.QoraError) as ei:
+        pkg.DecodeWeights(path=str(p))
+    assert ei.value.status == 3, str(ei.value)
