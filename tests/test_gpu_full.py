@@ -105,3 +105,45 @@ def test_config4_long_context(full_engine, full_oracle, full):
     assert worst < LOGIT_TOL
     toks = w.generate_greedy(kv, 5, 125)  # 128 decode steps in total at ~32K context
     assert len(kv) == S + 128 and toks.max() < w.vocab
+
+
+def test_config5_full_size_f16_batched(pkg, qf, orc):
+    """BASELINE config 5 at full size: SmolLM3-3B with F16 weights, two sequences decoded
+    together on the tcgen05 path. The oracle follows each sequence with forward_decode_raw
+    steps (its F16 GEMV on all host threads; the reference's scalar single-thread gemm_f16
+    prefill is prohibitive at this size), within a bounded time budget: teacher-forced
+    logits within rel-L2 1e-3 and the same greedy tokens."""
+    model = qf.synth_model(seed=5, fmt=qf.FORMAT_F16, rope_rows=1024)
+    w = pkg.DecodeWeights(model=model)
+    orc.set_threads(os.cpu_count() or 1)
+    om = orc.OracleModel(model)
+    rng = np.random.default_rng(55)
+    prompts = [rng.integers(0, w.vocab, size=n).astype(np.uint32) for n in (12, 20)]
+    kv = w.new_kv(64, batch=2)
+    firsts, pre = [], []
+    for b, p in enumerate(prompts):
+        f, lg = w.prefill(kv, p, want_logits=True, seq=b)
+        firsts.append(f)
+        pre.append(lg)
+    n_gen = 16
+    toks = w.generate_greedy_batch(kv, firsts, n_gen)
+    del model
+    t0, worst, checked = time.time(), 0.0, 0
+    for b, p in enumerate(prompts):
+        okv = om.new_kv()
+        for t in p[:-1]:
+            om.forward_decode(int(t), okv)
+        lo = om.forward_decode(int(p[-1]), okv)
+        worst = max(worst, rel_l2(pre[b], lo))
+        assert firsts[b] == int(np.argmax(lo))
+        prev = firsts[b]
+        for s in range(n_gen):
+            if time.time() - t0 > 2 * ORACLE_BUDGET_S:
+                break
+            lo = om.forward_decode(int(prev), okv)
+            assert toks[s, b] == int(np.argmax(lo)), (b, s)
+            prev = int(toks[s, b])
+            checked += 1
+    print(f"config 5 full size: prefill logits worst rel-L2 {worst:.3e}, {checked} greedy tokens checked")
+    assert worst < LOGIT_TOL and checked >= 4
+    w.close()
