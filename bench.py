@@ -41,8 +41,9 @@ def weight_bytes_per_token(layers=LAYERS):
     return layers * (43_941_888 + 8_192) + 147_750_912 + 4_096 + 1_152
 
 
-def kv_bytes_per_pos(layers=LAYERS):
-    return layers * 2 * 4 * 128 * 4
+def kv_bytes_per_pos(layers=LAYERS, esz=4):
+    """K and V bytes of one cached position over all layers (esz 4: f32, 2: binary16)."""
+    return layers * 2 * 4 * 128 * esz
 
 
 def peaks():
@@ -492,13 +493,17 @@ def run_q4_long(args, rank, world, local_rank):
     model, prompt = synth(args.layers)
     kvs = long_kv(args.layers)
     first_tok = int(prompt[0])
+    f16kv = args.kv == "f16"
     metric = "decode tok/s (batch 1, SmolLM3-3B Q4, 32K-token KV cache)"
+    if f16kv:  # opt-in, reported separately: results differ from the f32 cache
+        metric = "decode tok/s (batch 1, SmolLM3-3B Q4, 32K-token binary16 KV cache)"
+    kv_note = ", binary16 KV (opt-in)" if f16kv else ""
     if args.impl == "reference":
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
         import oracle
         oracle.set_threads(threads)
         om = oracle.OracleModel(model)
-        okv = om.new_kv()
+        okv = om.new_kv(args.kv)
         for layer, (k, v) in enumerate(kvs):
             okv.import_layer(layer, k, v)
         tok = oracle.argmax(om.forward_decode(first_tok, okv))
@@ -511,7 +516,8 @@ def run_q4_long(args, rank, world, local_rank):
         line = {"impl": "reference", "metric": metric, "value": v, "unit": "tok/s", "n_gpus": 1, "steps": n,
                 "warmup": 1, "ms_per_step": 1000.0 / v, "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random-init SmolLM3-3B Q4, N(0,1) KV)",
-                "config": {"workload": "config 4: SmolLM3-3B Q4, KV pre-filled to 32768 positions, greedy decode"},
+                "config": {"workload": "config 4: SmolLM3-3B Q4, KV pre-filled to 32768 positions, greedy decode"
+                                       + kv_note, "kv": args.kv},
                 "cpu_baseline": {"value": v, "unit": "tok/s", "cores": threads, "kind": "port",
                                  "sample": f"{n} forward_decode_raw steps after the 32768-row import, {threads} threads",
                                  "cpu": cpu_model()},
@@ -526,7 +532,7 @@ def run_q4_long(args, rank, world, local_rank):
     cap = LONG_CTX + W + K + 8
 
     def filled():
-        kv = eng.new_kv(cap)
+        kv = eng.new_kv(cap, dtype=args.kv)
         for layer, (k, v) in enumerate(kvs):
             kv.import_layer(layer, k, v)
         return kv
@@ -550,15 +556,15 @@ def run_q4_long(args, rank, world, local_rank):
     kv2.close()
     peak, peak_kind = peaks()
     mean_kv = LONG_CTX + W + (K - 1) / 2.0 + 1
-    step_bytes = weight_bytes_per_token(args.layers) + kv_bytes_per_pos(args.layers) * (mean_kv + 1)
+    step_bytes = weight_bytes_per_token(args.layers) + kv_bytes_per_pos(args.layers, 2 if f16kv else 4) * (mean_kv + 1)
     achieved = step_bytes / (ms / K / 1000.0) / 1e9
     line = {
         "metric": metric, "value": value, "unit": "tok/s", "n_gpus": 1, "steps": K, "warmup": W,
         "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded random-init SmolLM3-3B Q4 weights, N(0,1) f32 KV rows)",
         "config": {"workload": "config 4: SmolLM3-3B Q4, KV of all 36 layers pre-filled to 32768 positions, "
-                               "greedy decode at batch 1",
-                   "kv_len_mean": mean_kv, "layers": args.layers, "parallelism": "single GPU",
+                               "greedy decode at batch 1" + kv_note,
+                   "kv": args.kv, "kv_len_mean": mean_kv, "layers": args.layers, "parallelism": "single GPU",
                    "bytes_per_step": step_bytes,
                    "l2": "inputs larger than L2: 6.6 GB of weights + KV streamed per step"},
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
@@ -585,6 +591,9 @@ def main():
     ap.add_argument("--workload", choices=("q4", "q4-long", "f16-batch"), default="q4",
                     help="q4: config 3 batch-1 decode (the headline); q4-long: config 4; f16-batch: config 5")
     ap.add_argument("--batch", type=int, default=32, help="sequences for --workload f16-batch")
+    ap.add_argument("--kv", choices=("f32", "f16"), default="f32",
+                    help="KV cache element type for --workload q4-long (f16: the opt-in binary16 cache, "
+                         "reported as its own metric)")
     ap.add_argument("--layers", type=int, default=36,
                     help="decoder layers of the synthetic model (36 = SmolLM3-3B; fewer only for "
                          "small profiling captures, never for a reported number)")

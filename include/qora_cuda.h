@@ -148,6 +148,21 @@ qora_status qora_engine_info(const qora_engine* engine, uint32_t* num_layers,
  * take 1..128 sequences that decode together (each decode step advances all of them). */
 qora_status qora_kv_create(qora_engine* engine, uint32_t max_seq, uint32_t batch,
                            qora_kv** out);
+
+/* Element types of a KV cache. QORA_KV_F32 is the reference's cache. QORA_KV_F16 is the
+ * opt-in lower-precision cache of long contexts (no counterpart in the reference): each
+ * K and V value is rounded to IEEE binary16 (nearest even; beyond +-65504 it becomes
+ * +-inf) when it enters the cache, by a decode step or by qora_kv_import, and attention
+ * reads the rounded values, which halves the bytes a decode step streams per cached
+ * position. Results then differ from the reference's f32 cache. Supported by Q4
+ * engines on the persistent step with tp_size 1; anything else is QORA_ERR_UNSUPPORTED.
+ * Import and export keep the f32 host layout. */
+#define QORA_KV_F32 0u
+#define QORA_KV_F16 1u
+
+/* qora_kv_create with an element type (QORA_KV_*). */
+qora_status qora_kv_create_ex(qora_engine* engine, uint32_t max_seq, uint32_t batch,
+                              uint32_t kv_dtype, qora_kv** out);
 void qora_kv_destroy(qora_kv* kv);
 
 /* Current length (positions filled) of sequence seq_idx. */

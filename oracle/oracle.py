@@ -60,6 +60,8 @@ def lib():
         "orc_kv_len": (C.c_uint32, [C.c_void_p, C.c_uint32]),
         "orc_kv_import": (C.c_int, [C.c_void_p, C.c_uint32, _f32p, _f32p, C.c_uint32]),
         "orc_kv_export": (C.c_int, [C.c_void_p, C.c_uint32, _f32p, _f32p, C.c_uint32]),
+        "orc_kv_set_f16": (C.c_int, [C.c_void_p, C.c_int]),
+        "orc_round_f16": (None, [_f32p, _f32p, C.c_size_t]),
         "orc_f16_to_f32": (C.c_float, [C.c_uint16]),
         "orc_gemv_q4": (None, [_f32p, _u8p, _u16p, _sz, _sz, _f32p]),
         "orc_gemv_q4_rows": (None, [_f32p, _u8p, _u16p, _sz, _sz, _sz, _f32p]),
@@ -230,8 +232,9 @@ class OracleModel:
         except Exception:
             pass
 
-    def new_kv(self):
-        return OracleKV(self)
+    def new_kv(self, dtype="f32"):
+        """dtype "f16": the opt-in binary16 cache (values rounded as they enter)."""
+        return OracleKV(self, dtype)
 
     def forward_decode(self, token, kv):
         out = np.empty(self.vocab, np.float32)
@@ -267,10 +270,22 @@ class OracleModel:
         return toks, margins
 
 
+def round_f16(x):
+    """x rounded to the nearest binary16 value (ties to even), as f32 (orc_round_f16)."""
+    x = f32(x)
+    out = np.empty_like(x)
+    lib().orc_round_f16(x.reshape(-1), out.reshape(-1), x.size)
+    return out
+
+
 class OracleKV:
-    def __init__(self, m: OracleModel):
+    def __init__(self, m: OracleModel, dtype="f32"):
+        if dtype not in ("f32", "f16"):
+            raise ValueError(f"KV dtype {dtype!r}")
         self.m = m
         self.h = lib().orc_kv_new(m.h)
+        if dtype == "f16" and lib().orc_kv_set_f16(self.h, 1):
+            raise ValueError("orc_kv_set_f16 failed")
 
     def __del__(self):
         try:

@@ -144,6 +144,24 @@ inline float h2f(uint16_t h) {
   return out;
 }
 
+// Nearest IEEE binary16 value of x (ties to even), returned as f32. From the format's
+// definition: the quantum of |x| is 2^(e-10) for binade e >= -14 and 2^-24 below
+// (subnormals); |x| >= 65520 (halfway between 65504 and 2^16) overflows to inf.
+// Scaling by a power of two is exact in double, and nearbyint rounds to nearest even.
+inline float round_f16(float x) {
+  uint32_t b;
+  std::memcpy(&b, &x, 4);
+  const uint32_t a = b & 0x7FFFFFFFu;
+  if (a >= 0x7F800000u) return x;  // inf, nan
+  const bool neg = (b >> 31) != 0;
+  if (a >= 0x477FF000u) return neg ? -INFINITY : INFINITY;
+  const int e = (int)(a >> 23) - 127;  // f32 subnormals give -127: they round to 0 or 2^-24 steps
+  const int qexp = std::max(e - 10, -24);
+  const double v = std::nearbyint(std::ldexp((double)std::fabs(x), -qexp));
+  const float r = (float)std::ldexp(v, qexp);
+  return neg ? -r : r;
+}
+
 // ---------------------------------------------------------------- Q4 row kernels
 // gemv_q4_inner scalar path (src/gemv.rs:605-640): per input row ki, s = scale*x,
 // a 16-entry table s*(q-8), and out[j] += table[nibble] in element order.
@@ -349,6 +367,7 @@ struct orc_kv {
   uint32_t kv_stride = 0;  // kv_heads * head_dim
   std::vector<std::vector<float>> k, v;
   std::vector<uint32_t> len;
+  bool f16 = false;        // opt-in binary16 cache (values rounded as they enter)
 };
 
 namespace {
@@ -778,8 +797,21 @@ int orc_kv_import(orc_kv* kv, uint32_t layer, const float* k, const float* v, ui
   const size_t n = (size_t)seq_len * kv->kv_stride;
   kv->k[layer].assign(k, k + n);
   kv->v[layer].assign(v, v + n);
+  if (kv->f16) {
+    for (float& x : kv->k[layer]) x = round_f16(x);
+    for (float& x : kv->v[layer]) x = round_f16(x);
+  }
   kv->len[layer] = seq_len;
   return 0;
+}
+int orc_kv_set_f16(orc_kv* kv, int on) {
+  for (uint32_t n : kv->len)
+    if (n) return 1;
+  kv->f16 = on != 0;
+  return 0;
+}
+void orc_round_f16(const float* x, float* out, size_t n) {
+  for (size_t i = 0; i < n; ++i) out[i] = round_f16(x[i]);
 }
 int orc_kv_export(const orc_kv* kv, uint32_t layer, float* k, float* v, uint32_t seq_len) {
   if (layer >= kv->len.size() || seq_len > kv->len[layer]) return 1;
@@ -950,6 +982,10 @@ int orc_layer_forward(const orc_model* m, uint32_t li, float* x, orc_kv* kv) {
     rope(q.data(), nh, hd, m->cos_t.data(), m->sin_t.data(), m->half_dim, pos);
     rope(kn.data(), nkv, hd, m->cos_t.data(), m->sin_t.data(), m->half_dim, pos);
   }
+  if (kv->f16) {
+    for (float& t : kn) t = round_f16(t);
+    for (float& t : vn) t = round_f16(t);
+  }
   kv->k[li].insert(kv->k[li].end(), kn.begin(), kn.end());
   kv->v[li].insert(kv->v[li].end(), vn.begin(), vn.end());
   kv->len[li] = (uint32_t)(pos + 1);
@@ -1014,6 +1050,10 @@ int orc_prefill(const orc_model* m, const uint32_t* ids, size_t n, orc_kv* kv, f
         rope(qa.data() + t * qs, nh, hd, m->cos_t.data(), m->sin_t.data(), m->half_dim, t);
         rope(ka.data() + t * ks, nkv, hd, m->cos_t.data(), m->sin_t.data(), m->half_dim, t);
       }
+    }
+    if (kv->f16) {  // every position attends to the cached (rounded) keys and values
+      for (float& t : ka) t = round_f16(t);
+      for (float& t : va) t = round_f16(t);
     }
     const float scale = 1.0f / std::sqrt((float)hd);
     std::vector<float> attn(n * qs, 0.0f);

@@ -59,6 +59,13 @@ uint32_t orc_kv_len(const orc_kv* kv, uint32_t layer);
 /* replace layer contents with seq_len token-major rows */
 int      orc_kv_import(orc_kv* kv, uint32_t layer, const float* k, const float* v, uint32_t seq_len);
 int      orc_kv_export(const orc_kv* kv, uint32_t layer, float* k, float* v, uint32_t seq_len);
+/* Opt-in binary16 cache (no counterpart in the reference; the engine's QORA_KV_F16):
+ * every K and V value is rounded to IEEE binary16 (nearest even) when it enters the cache
+ * (decode append, prefill, import) and attention reads the rounded values. Only on an
+ * empty cache; returns nonzero otherwise. */
+int      orc_kv_set_f16(orc_kv* kv, int on);
+/* out[i] = x[i] rounded to the nearest binary16 value (ties to even), as f32 */
+void     orc_round_f16(const float* x, float* out, size_t n);
 
 /* ---- primitive restatements ---- */
 float orc_f16_to_f32(uint16_t h);

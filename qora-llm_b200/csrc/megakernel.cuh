@@ -60,7 +60,8 @@ constexpr int kThreads = kCT + 32;     // + one producer warp
 constexpr int kStageBytes = 34560;     // 1920 one-group rows = 240 eight-group rows = 30 embedding rows
 constexpr int kStages = 5;
 constexpr int kBar = 1;                // named barrier of the consumer warps
-constexpr int kKVRows = kStageBytes / (kHeadDim * 4);  // K or V rows of one head per stage (67)
+constexpr int kKVRows = kStageBytes / (kHeadDim * 4);  // f32 K or V rows of one head per stage (67)
+constexpr int kKVRows16 = kStageBytes / (kHeadDim * 2);  // f16 rows (135)
 constexpr int kMinAttnChunk = 64;
 constexpr int kMaxAttnChunk = 1024;
 constexpr int kMaxUnits = 256;         // attention units (kv head x chunk); units <= CTAs
@@ -104,7 +105,9 @@ struct Args {
   int sub0[4], subn[4];       // CTA set [sub0, sub0+subn) that runs each matrix
   int H, nq, nkvw, nh, nkvh, vocab;
   int lm_row_bytes, lm_rows_per_stage;
-  long long head_stride;      // floats between KV heads of a layer's cache (max_seq * 128)
+  long long head_stride;      // elements between KV heads of a layer's cache (max_seq * 128)
+  int kv16;                   // 1: the cache holds IEEE binary16 K/V (opt-in), 0: f32
+  int kv_pad;
   const uint8_t* lm;          // [vocab][H/2 packed | H/16 scales]
   const float* final_gamma;
   const float* cos_t;
@@ -272,13 +275,14 @@ __device__ __noinline__ uint32_t produce_kv(int L, uint32_t chunk) {
   const int u = attn_unit_of(c, gridDim.x);
   if (u >= a.nkvh * nch) return chunk;
   const int g = u % a.nkvh, s0 = (u / a.nkvh) * csz, sc1 = min(min(len, s0 + csz), pos);
+  const int esz = a.kv16 ? 2 : 4, rps = a.kv16 ? kKVRows16 : kKVRows;
 #pragma unroll 1
   for (int kvs = 0; kvs < 2; ++kvs) {
-    const float* src = (kvs ? a.layers[L].vc : a.layers[L].kc) + g * a.head_stride;
+    const uint8_t* src = reinterpret_cast<const uint8_t*>(kvs ? a.layers[L].vc : a.layers[L].kc) +
+                         g * a.head_stride * esz;
 #pragma unroll 1
-    for (int s = s0; s < sc1; s += kKVRows)
-      chunk = issue(reinterpret_cast<const uint8_t*>(src + (long long)s * kHeadDim),
-                    (uint32_t)(min(kKVRows, sc1 - s) * kHeadDim * 4), chunk);
+    for (int s = s0; s < sc1; s += rps)
+      chunk = issue(src + (long long)s * kHeadDim * esz, (uint32_t)(min(rps, sc1 - s) * kHeadDim * esz), chunk);
   }
   return chunk;
 }
@@ -813,9 +817,61 @@ QORA_DEV void kscore(const float* sq, const float* krow, float* sc, int idx, boo
   }
 }
 
+// kscore for a binary16 K row (opt-in f16 cache): lane li takes dims [8li, 8li+8) and
+// [64+8li, 64+8li+8) as two 16-byte loads (conflict-free across the 8 lanes of a row)
+QORA_DEV void kscore16(const float* sq, const __half* krow, float* sc, int idx, bool valid, int li) {
+  float d[kHeadsPerKV] = {0.0f, 0.0f, 0.0f, 0.0f};
+  if (valid) {
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(krow + j * kHalfDim + li * 8);
+      const uint32_t wv[4] = {raw.x, raw.y, raw.z, raw.w};
+      float kf[8];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&wv[t]));
+        kf[2 * t] = f.x;
+        kf[2 * t + 1] = f.y;
+      }
+#pragma unroll
+      for (int h = 0; h < kHeadsPerKV; ++h) {
+        const float4 qa = *reinterpret_cast<const float4*>(sq + h * kHeadDim + j * kHalfDim + li * 8);
+        const float4 qb = *reinterpret_cast<const float4*>(sq + h * kHeadDim + j * kHalfDim + li * 8 + 4);
+        d[h] = __fmaf_rn(qa.x, kf[0], d[h]);
+        d[h] = __fmaf_rn(qa.y, kf[1], d[h]);
+        d[h] = __fmaf_rn(qa.z, kf[2], d[h]);
+        d[h] = __fmaf_rn(qa.w, kf[3], d[h]);
+        d[h] = __fmaf_rn(qb.x, kf[4], d[h]);
+        d[h] = __fmaf_rn(qb.y, kf[5], d[h]);
+        d[h] = __fmaf_rn(qb.z, kf[6], d[h]);
+        d[h] = __fmaf_rn(qb.w, kf[7], d[h]);
+      }
+    }
+  }
+  const float scale = 0.08838834764831845f;
+#pragma unroll
+  for (int h = 0; h < kHeadsPerKV; ++h) {
+    float v = d[h];
+    v += __shfl_xor_sync(0xffffffffu, v, 1);
+    v += __shfl_xor_sync(0xffffffffu, v, 2);
+    v += __shfl_xor_sync(0xffffffffu, v, 4);
+    if (valid && li == 0) sc[h * kMaxAttnChunk + idx] = __fmul_rn(v, scale);
+  }
+}
+
+// one cached V element as f32
+QORA_DEV float kv_elem(const float* p) { return *p; }
+QORA_DEV float kv_elem(const __half* p) { return __half2float(*p); }
+
 // ATTN: unit u = c = (kv head g = u % nkvh, chunk u / nkvh) for the 4 query heads of g
-// (src/gemv.rs:914-989, softmax_raw :782-793; RoPE src/gemv.rs:757-778)
-__device__ __noinline__ uint32_t attention_phase(int L, uint32_t chunk) {
+// (src/gemv.rs:914-989, softmax_raw :782-793; RoPE src/gemv.rs:757-778). KV is float
+// (the reference's f32 cache) or __half (the opt-in binary16 cache: the new k and v are
+// rounded to nearest-even as they enter the cache, and the new position's score and P.V
+// use the rounded values, exactly as if they were read back from it).
+template <class KV>
+__device__ __noinline__ uint32_t attention_phase_t(int L, uint32_t chunk) {
+  constexpr bool kF16 = sizeof(KV) == 2;
+  constexpr int kRows = kF16 ? kKVRows16 : kKVRows;
   Cons C = make_cons(chunk);
   const Args& a = C.a();
   const int pos = C.pos, len = pos + 1, tid = C.tid, lane = C.lane, warp = C.warp;
@@ -827,8 +883,8 @@ __device__ __noinline__ uint32_t attention_phase(int L, uint32_t chunk) {
   const int s0 = (u / a.nkvh) * csz, s1 = min(len, s0 + csz), sc1 = min(s1, pos), n = s1 - s0;
   const bool has_pos = pos < s1;
   const Layer& ly = a.layers[L];
-  float* kc = ly.kc + g * a.head_stride;
-  float* vc = ly.vc + g * a.head_stride;
+  KV* kc = reinterpret_cast<KV*>(ly.kc) + g * a.head_stride;
+  KV* vc = reinterpret_cast<KV*>(ly.vc) + g * a.head_stride;
   float* sq = C.scratch + kAttQ;
   float* sc = C.scratch + kAttS;
   float* sml = C.scratch + kAttML;
@@ -870,6 +926,12 @@ __device__ __noinline__ uint32_t attention_phase(int L, uint32_t chunk) {
     if (!isk) {
       sq[hh * kHeadDim + d] = y1;
       sq[hh * kHeadDim + d + kHalfDim] = y2;
+    } else if constexpr (kF16) {
+      const __half h1 = __float2half_rn(y1), h2 = __float2half_rn(y2);
+      skv[d] = __half2float(h1);
+      skv[d + kHalfDim] = __half2float(h2);
+      kc[(long long)pos * kHeadDim + d] = h1;
+      kc[(long long)pos * kHeadDim + d + kHalfDim] = h2;
     } else {
       skv[d] = y1;
       skv[d + kHalfDim] = y2;
@@ -879,22 +941,30 @@ __device__ __noinline__ uint32_t attention_phase(int L, uint32_t chunk) {
   } else if (tid >= 320 && tid < 448 && has_pos) {
     const int d = tid - 320;
     const float v = ld_checked(C, a.qkv + a.nq + a.nkvw + g * kHeadDim + d, tag);
-    skv[kHeadDim + d] = v;
-    vc[(long long)pos * kHeadDim + d] = v;
+    if constexpr (kF16) {
+      const __half hv = __float2half_rn(v);
+      skv[kHeadDim + d] = __half2float(hv);
+      vc[(long long)pos * kHeadDim + d] = hv;
+    } else {
+      skv[kHeadDim + d] = v;
+      vc[(long long)pos * kHeadDim + d] = v;
+    }
   }
   C.bar();
   C.fstamp();
   // scores: 4 rows per warp pass (8 lanes each), 60 rows per CTA pass
   const int li = lane & 7, ri = warp * 4 + (lane >> 3);
 #pragma unroll 1
-  for (int s = s0; s < sc1; s += kKVRows) {
+  for (int s = s0; s < sc1; s += kRows) {
     const uint8_t* stg = C.acquire_stage();
-    const int nr = min(kKVRows, sc1 - s);
+    const int nr = min(kRows, sc1 - s);
     if (C.stage_ok) {
 #pragma unroll 1
       for (int rb = 0; rb < nr; rb += kCW * 4) {
         const int i = rb + ri;
-        kscore(sq, reinterpret_cast<const float*>(stg) + min(i, nr - 1) * kHeadDim, sc, s - s0 + i, i < nr, li);
+        const KV* krow = reinterpret_cast<const KV*>(stg) + min(i, nr - 1) * kHeadDim;
+        if constexpr (kF16) kscore16(sq, krow, sc, s - s0 + i, i < nr, li);
+        else kscore(sq, krow, sc, s - s0 + i, i < nr, li);
       }
     }
     C.release_stage();
@@ -930,18 +1000,18 @@ __device__ __noinline__ uint32_t attention_phase(int L, uint32_t chunk) {
   const int grp = tid >> 7, dd = tid & (kHeadDim - 1);
   float o[kHeadsPerKV] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll 1
-  for (int s = s0; s < sc1; s += kKVRows) {
+  for (int s = s0; s < sc1; s += kRows) {
     const uint8_t* stg = C.acquire_stage();
-    const int nr = min(kKVRows, sc1 - s);
+    const int nr = min(kRows, sc1 - s);
     if (C.stage_ok && grp < 3) {
-      const float* vr = reinterpret_cast<const float*>(stg) + dd;
+      const KV* vr = reinterpret_cast<const KV*>(stg) + dd;
       const float* pr = sc + (s - s0);
       int i = grp;
 #pragma unroll 1
       for (; i + 9 < nr; i += 12) {
         float v[4];
 #pragma unroll
-        for (int r = 0; r < 4; ++r) v[r] = vr[(i + 3 * r) * kHeadDim];
+        for (int r = 0; r < 4; ++r) v[r] = kv_elem(vr + (i + 3 * r) * kHeadDim);
 #pragma unroll
         for (int r = 0; r < 4; ++r)
 #pragma unroll
@@ -949,7 +1019,7 @@ __device__ __noinline__ uint32_t attention_phase(int L, uint32_t chunk) {
       }
 #pragma unroll 1
       for (; i < nr; i += 3) {
-        const float v = vr[i * kHeadDim];
+        const float v = kv_elem(vr + i * kHeadDim);
 #pragma unroll
         for (int h = 0; h < kHeadsPerKV; ++h) o[h] = __fmaf_rn(pr[h * kMaxAttnChunk + i], v, o[h]);
       }
@@ -982,6 +1052,10 @@ __device__ __noinline__ uint32_t attention_phase(int L, uint32_t chunk) {
     if (tid < 2 * hpk) st_tagged(a.att_ml + (long long)u * 2 * kHeadsPerKV + tid, sml[tid], tag);
   }
   return C.chunk;
+}
+
+__device__ __noinline__ uint32_t attention_phase(int L, uint32_t chunk) {
+  return sm_args()->kv16 ? attention_phase_t<__half>(L, chunk) : attention_phase_t<float>(L, chunk);
 }
 
 // O: merge the (m, l, o) partials of every head (chunk order), GEMV over all rows for

@@ -353,7 +353,8 @@ struct qora_kv {
   qora_engine* e = nullptr;
   uint32_t max_seq = 0;
   uint32_t batch = 1;  // independent sequences
-  float* k = nullptr;  // [layers][batch][nkv][max_seq][128]
+  uint32_t dtype = QORA_KV_F32;
+  float* k = nullptr;  // [layers][batch][nkv][max_seq][128] f32, or binary16 (QORA_KV_F16)
   float* v = nullptr;
   std::vector<uint32_t> len;  // [batch][layers] positions filled
   int* rows = nullptr;        // F16 path: row table (f16b::RowInfo)
@@ -408,8 +409,12 @@ struct qora_kv {
     *p = static_cast<T*>(d);
     return QORA_OK;
   }
-  size_t seq_stride() const { return (size_t)max_seq * e->nkv * kHeadDim; }
+  size_t seq_stride() const { return (size_t)max_seq * e->nkv * kHeadDim; }  // elements
   size_t layer_stride() const { return batch * seq_stride(); }
+  size_t esz() const { return dtype == QORA_KV_F16 ? 2 : 4; }
+  // base of layer li's keys (values) in the cache's element type
+  void* k_layer(size_t li) const { return reinterpret_cast<uint8_t*>(k) + li * layer_stride() * esz(); }
+  void* v_layer(size_t li) const { return reinterpret_cast<uint8_t*>(v) + li * layer_stride() * esz(); }
   uint32_t& lenof(uint32_t seq, uint32_t layer) { return len[(size_t)seq * (len.size() / batch) + layer]; }
 };
 
@@ -795,8 +800,8 @@ qora_status mega_prepare(qora_engine* e, qora_kv* kv) {
     hl[i].w[3] = d.down.buf;
     hl[i].g_in = d.g_in;
     hl[i].g_post = d.g_post;
-    hl[i].kc = kv->k + (size_t)i * kv->layer_stride();
-    hl[i].vc = kv->v + (size_t)i * kv->layer_stride();
+    hl[i].kc = static_cast<float*>(kv->k_layer(i));
+    hl[i].vc = static_cast<float*>(kv->v_layer(i));
     hl[i].rope = d.rope;
   }
   QCHECK(kv->alloc(&kv->mk_layers, L));
@@ -832,6 +837,7 @@ qora_status mega_prepare(qora_engine* e, qora_kv* kv) {
     a.lm_rows_per_stage = rows;
   }
   a.head_stride = (long long)kv->max_seq * kHeadDim;
+  a.kv16 = kv->dtype == QORA_KV_F16 ? 1 : 0;
   a.lm = e->lm_table;
   a.final_gamma = e->final_gamma;
   a.cos_t = e->rope_cos;
@@ -1990,14 +1996,23 @@ qora_status qora_engine_info(const qora_engine* e, uint32_t* num_layers, uint32_
 }
 
 qora_status qora_kv_create(qora_engine* e, uint32_t max_seq, uint32_t batch, qora_kv** out) {
+  return qora_kv_create_ex(e, max_seq, batch, QORA_KV_F32, out);
+}
+
+qora_status qora_kv_create_ex(qora_engine* e, uint32_t max_seq, uint32_t batch, uint32_t kv_dtype, qora_kv** out) {
   if (!e || !out) return fail(QORA_ERR_INVALID, "NULL argument");
   *out = nullptr;
   const bool f16 = e->format == QORA_FORMAT_F16;
+  if (kv_dtype != QORA_KV_F32 && kv_dtype != QORA_KV_F16) return fail(QORA_ERR_INVALID, "kv_dtype %u", kv_dtype);
   if (batch == 0) return fail(QORA_ERR_INVALID, "batch must be > 0");
   if (!f16 && batch != 1) return fail(QORA_ERR_UNSUPPORTED, "batch=%u: Q4 engines decode batch 1", batch);
   if (batch > (uint32_t)f16b::kMaxRows)
     return fail(QORA_ERR_UNSUPPORTED, "batch=%u: at most %d sequences", batch, f16b::kMaxRows);
   if (max_seq == 0) return fail(QORA_ERR_INVALID, "max_seq must be > 0");
+  if (kv_dtype == QORA_KV_F16 && (f16 || !e->use_mega || !e->mk_ok || e->tp > 1 || max_seq > e->mk_max_seq))
+    return fail(QORA_ERR_UNSUPPORTED,
+                "binary16 KV caches need a Q4 engine on the persistent step, tp_size 1 and max_seq <= %u",
+                e->mk_max_seq);
   bool any_rope = false;
   for (auto& L : e->layers) any_rope |= (L.rope != 0);
   for (auto& L : e->fl) any_rope |= (L.rope != 0);
@@ -2008,8 +2023,9 @@ qora_status qora_kv_create(qora_engine* e, uint32_t max_seq, uint32_t batch, qor
   kv->e = e;
   kv->max_seq = max_seq;
   kv->batch = batch;
+  kv->dtype = kv_dtype;
   kv->len.assign((size_t)batch * e->num_layers, 0);
-  const size_t per = kv->layer_stride() * e->num_layers;
+  const size_t per = (kv->layer_stride() * e->num_layers * kv->esz() + 3) / 4;  // in floats
   QCHECK(kv->alloc(&kv->k, per));
   QCHECK(kv->alloc(&kv->v, per));
   QCHECK(kv->alloc(&kv->st, 1));
@@ -2057,6 +2073,40 @@ qora_status qora_kv_reset(qora_kv* kv, uint32_t seq_idx) {
   return QORA_OK;
 }
 
+// Import (to_device) or export one layer of a binary16 cache through an f32 device
+// staging buffer of the host rows [seq_len][nkv_total*128]; the conversion kernels round
+// to nearest even on the way in and widen exactly on the way out.
+static qora_status kv_f16_transfer(qora_kv* kv, uint32_t layer, float* k, float* v, uint32_t seq_len,
+                                   uint32_t seq_idx, bool to_device) {
+  if (seq_len == 0) return QORA_OK;
+  qora_engine* e = kv->e;
+  const size_t row_floats = (size_t)e->nkv_total * kHeadDim, n = (size_t)seq_len * row_floats;
+  float* tmp = nullptr;
+  cudaError_t err = cudaMalloc(&tmp, n * sizeof(float));
+  if (err != cudaSuccess) return fail(QORA_ERR_OOM, "cudaMalloc(%zu) failed: %s", n * 4, cudaGetErrorString(err));
+  std::unique_ptr<float, decltype(&cudaFree)> guard(tmp, &cudaFree);
+  const long long hs = (long long)kv->max_seq * kHeadDim;
+  const size_t off = seq_idx * kv->seq_stride();  // elements, within the layer
+  const int grid = e->sms * 4;
+  for (int side = 0; side < 2; ++side) {
+    float* host = side ? v : k;
+    __half* dev = static_cast<__half*>(side ? kv->v_layer(layer) : kv->k_layer(layer)) + off;
+    if (to_device) {
+      QCUDA(cudaMemcpy(tmp, host, n * sizeof(float), cudaMemcpyHostToDevice));
+      kv_pack_f16_kernel<<<grid, 256>>>(tmp, (int)row_floats, (int)e->kv0, (int)e->nkv, (int)seq_len, dev, hs);
+      QCUDA(cudaGetLastError());
+      QCUDA(cudaDeviceSynchronize());
+    } else {  // the rank's own heads' columns of the host rows
+      kv_unpack_f16_kernel<<<grid, 256>>>(dev, hs, (int)e->nkv, (int)seq_len, tmp);
+      QCUDA(cudaGetLastError());
+      const size_t lb = (size_t)e->nkv * kHeadDim * sizeof(float);
+      QCUDA(cudaMemcpy2D(host + (size_t)e->kv0 * kHeadDim, row_floats * sizeof(float), tmp, lb, lb, seq_len,
+                         cudaMemcpyDeviceToHost));
+    }
+  }
+  return QORA_OK;
+}
+
 qora_status qora_kv_import(qora_kv* kv, uint32_t layer, const float* k, const float* v,
                            uint32_t seq_len, uint32_t seq_idx) {
   if (!kv || (!k && seq_len) || (!v && seq_len)) return fail(QORA_ERR_INVALID, "NULL argument");
@@ -2065,6 +2115,11 @@ qora_status qora_kv_import(qora_kv* kv, uint32_t layer, const float* k, const fl
   if (layer >= kv->e->num_layers) return fail(QORA_ERR_RANGE, "layer %u", layer);
   if (seq_len > kv->max_seq) return fail(QORA_ERR_RANGE, "seq_len %u > max_seq %u", seq_len, kv->max_seq);
   QCUDA(cudaSetDevice(kv->e->device));
+  if (kv->dtype == QORA_KV_F16) {
+    QCHECK(kv_f16_transfer(kv, layer, const_cast<float*>(k), const_cast<float*>(v), seq_len, seq_idx, true));
+    kv->lenof(seq_idx, layer) = seq_len;
+    return QORA_OK;
+  }
   // host rows [seq][all kv heads*128] -> device head-major [local kv heads][max_seq][128]
   // (a tensor-parallel rank keeps heads kv0 .. kv0 + nkv - 1)
   const size_t row = (size_t)kv->e->nkv_total * kHeadDim * sizeof(float), hb = kHeadDim * sizeof(float);
@@ -2088,6 +2143,7 @@ qora_status qora_kv_export(const qora_kv* kv, uint32_t layer, float* k, float* v
   if (seq_len > have) return fail(QORA_ERR_RANGE, "seq_len %u > length %u", seq_len, have);
   QCUDA(cudaSetDevice(kv->e->device));
   QCUDA(cudaStreamSynchronize(kv->e->stream));
+  if (kv->dtype == QORA_KV_F16) return kv_f16_transfer(const_cast<qora_kv*>(kv), layer, k, v, seq_len, seq_idx, false);
   const size_t row = (size_t)kv->e->nkv_total * kHeadDim * sizeof(float), hb = kHeadDim * sizeof(float);
   for (uint32_t j = 0; seq_len && j < kv->e->nkv; ++j) {  // a rank fills only its own heads' columns
     const size_t off = layer * kv->layer_stride() + seq_idx * kv->seq_stride() + (size_t)j * kv->max_seq * kHeadDim;
@@ -2176,6 +2232,7 @@ qora_status qora_generate_greedy(qora_engine* e, qora_kv* kv, uint32_t first_tok
 qora_status qora_layer_step(qora_engine* e, qora_kv* kv, uint32_t layer, float* x_inout) {
   if (!e || !kv || kv->e != e || !x_inout) return fail(QORA_ERR_INVALID, "bad arguments");
   if (e->format != QORA_FORMAT_Q4) return fail(QORA_ERR_UNSUPPORTED, "qora_layer_step runs Q4 engines");
+  if (kv->dtype != QORA_KV_F32) return fail(QORA_ERR_UNSUPPORTED, "qora_layer_step runs f32 KV caches");
   if (layer >= e->num_layers) return fail(QORA_ERR_RANGE, "layer %u", layer);
   const uint32_t len = kv->len[layer];
   if (len >= kv->max_seq) return fail(QORA_ERR_RANGE, "KV cache full");
@@ -2235,6 +2292,7 @@ qora_status qora_engine_time_kernel(qora_engine* e, qora_kv* kv, int kernel, uin
                                     uint32_t* launches) {
   if (!e || !kv || kv->e != e || !ms_per_launch || reps == 0) return fail(QORA_ERR_INVALID, "bad arguments");
   if (e->format != QORA_FORMAT_Q4) return fail(QORA_ERR_UNSUPPORTED, "kernel timing runs Q4 engines");
+  if (kv->dtype != QORA_KV_F32) return fail(QORA_ERR_UNSUPPORTED, "kernel timing runs f32 KV caches");
   if (kernel < QORA_KERNEL_QKV || kernel > QORA_KERNEL_LM_HEAD) return fail(QORA_ERR_INVALID, "kernel %d", kernel);
   uint32_t len = 0;
   QCHECK(check_uniform_len(kv, &len));

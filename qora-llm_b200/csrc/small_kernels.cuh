@@ -48,4 +48,28 @@ __global__ void dequant_q4_kernel(const uint8_t* packed, const uint16_t* scales,
   }
 }
 
+// Opt-in binary16 KV cache. Host rows [n][row_floats] f32 (token-major, heads h0 .. h0+nh-1
+// of the row) -> head-major [nh][head_stride] binary16, rounded to nearest even.
+__global__ void kv_pack_f16_kernel(const float* src, int row_floats, int h0, int nh, int n, __half* dst,
+                                   long long head_stride) {
+  const long long total = (long long)nh * n * kHeadDim;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int d = (int)(i % kHeadDim);
+    const long long t = (i / kHeadDim) % n, h = i / ((long long)kHeadDim * n);
+    dst[h * head_stride + t * kHeadDim + d] = __float2half_rn(src[t * row_floats + (h0 + h) * kHeadDim + d]);
+  }
+}
+
+// The inverse: head-major binary16 -> rows [n][nh*128] f32 (exact).
+__global__ void kv_unpack_f16_kernel(const __half* src, long long head_stride, int nh, int n, float* dst) {
+  const long long total = (long long)nh * n * kHeadDim;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int d = (int)(i % kHeadDim);
+    const long long t = (i / kHeadDim) % n, h = i / ((long long)kHeadDim * n);
+    dst[t * nh * kHeadDim + h * kHeadDim + d] = __half2float(src[h * head_stride + t * kHeadDim + d]);
+  }
+}
+
 }  // namespace qora

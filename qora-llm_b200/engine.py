@@ -42,6 +42,7 @@ SIGNATURES = {
     "qora_engine_destroy": (None, [_vp]),
     "qora_engine_info": (C.c_int, [_vp, _P(_u32), _P(_u32), _P(_u32), _P(_u32), _P(_u64)]),
     "qora_kv_create": (C.c_int, [_vp, _u32, _u32, _P(_vp)]),
+    "qora_kv_create_ex": (C.c_int, [_vp, _u32, _u32, _u32, _P(_vp)]),
     "qora_kv_destroy": (None, [_vp]),
     "qora_kv_length": (C.c_int, [_vp, _u32, _P(_u32)]),
     "qora_kv_reset": (C.c_int, [_vp, _u32]),
@@ -166,9 +167,10 @@ class DecodeWeights:
         self.close()
 
     # ---- KV
-    def new_kv(self, max_seq: int, batch: int = 1) -> "KVCache":
-        """A cache for `batch` independent sequences (batch > 1: F16 engines)."""
-        return KVCache(self, max_seq, batch)
+    def new_kv(self, max_seq: int, batch: int = 1, dtype: str = "f32") -> "KVCache":
+        """A cache for `batch` independent sequences (batch > 1: F16 engines). dtype "f16"
+        is the opt-in binary16 cache (QORA_KV_F16: Q4 engines, persistent step)."""
+        return KVCache(self, max_seq, batch, dtype)
 
     # ---- steps
     def decode_step(self, kv: "KVCache", token: int, want_logits: bool = False):
@@ -266,13 +268,19 @@ class DecodeWeights:
         return x
 
 
-class KVCache:
-    """Device KV cache, f32 token-major [seq][kv_heads][128] per layer (RawKvCache)."""
+KV_DTYPES = {"f32": 0, "f16": 1}  # QORA_KV_F32, QORA_KV_F16
 
-    def __init__(self, w: DecodeWeights, max_seq: int, batch: int = 1):
+
+class KVCache:
+    """Device KV cache (RawKvCache); import/export use f32 token-major
+    [seq][kv_heads][128] host rows whatever the device element type."""
+
+    def __init__(self, w: DecodeWeights, max_seq: int, batch: int = 1, dtype: str = "f32"):
+        if dtype not in KV_DTYPES:
+            raise ValueError(f"KV dtype {dtype!r}: one of {sorted(KV_DTYPES)}")
         h = C.c_void_p()
-        check(lib().qora_kv_create(w.h, int(max_seq), int(batch), C.byref(h)))
-        self.h, self.w, self.max_seq, self.batch = h, w, max_seq, batch
+        check(lib().qora_kv_create_ex(w.h, int(max_seq), int(batch), KV_DTYPES[dtype], C.byref(h)))
+        self.h, self.w, self.max_seq, self.batch, self.dtype = h, w, max_seq, batch, dtype
 
     def close(self):
         if getattr(self, "h", None):

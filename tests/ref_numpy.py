@@ -7,9 +7,11 @@ import numpy as np
 
 
 class RefModel:
-    def __init__(self, model, qf):
+    def __init__(self, model, qf, kv_f16=False):
+        """kv_f16: the opt-in binary16 cache: K and V rounded to float16 as they enter it."""
         self.m = model
         self.qf = qf
+        self.kv_f16 = kv_f16
         deq = (lambda mat: qf.dequant_q4(mat, np.float64)) if model.format == qf.FORMAT_Q4 else \
             (lambda mat: qf.f16_bits_to_f32(mat.data).astype(np.float64).reshape(mat.k, mat.n))
         self.layers = []
@@ -50,6 +52,9 @@ class RefModel:
         if self.m.no_rope_layers[i]:
             q = self.rope(q, L["nh"], L["hd"], pos)
             k = self.rope(k, L["nkv"], L["hd"], pos)
+        if self.kv_f16:
+            k = k.astype(np.float16).astype(np.float64)
+            v = v.astype(np.float16).astype(np.float64)
         kv[i][0].append(k)
         kv[i][1].append(v)
         K = np.stack(kv[i][0]).reshape(pos + 1, L["nkv"], L["hd"])

@@ -295,3 +295,91 @@ def test_sampling_restatement_pins_oracle(orc):
         a = orc.sample(logits, hist, t, tp, k, rp, pp, ban, state)
         b = _py_sample(logits, hist, t, tp, k, rp, pp, ban, state)
         assert a == b, (it, a, b)
+
+
+# ---------------------------------------------------------------- opt-in binary16 KV
+def test_round_f16_matches_numpy(orc):
+    """orc_round_f16 against numpy's float32 -> float16 conversion (round to nearest
+    even), bit for bit: random bit patterns, every midpoint between adjacent positive
+    binary16 values (the ties) and its f32 neighbours, overflow and subnormal edges."""
+    rng = np.random.default_rng(0)
+    parts = [rng.integers(0, 2**32, size=200_000, dtype=np.uint64).astype(np.uint32).view(np.float32)]
+    for s in (1e-6, 1e-3, 1.0, 1e3, 6e4):
+        parts.append((rng.standard_normal(50_000) * s).astype(np.float32))
+    f = np.arange(0, 0x7C00, dtype=np.uint16).view(np.float16).astype(np.float64)
+    mids = ((f[:-1] + f[1:]) / 2).astype(np.float32)  # exact: <= 12 significant bits
+    parts += [mids, -mids, np.nextafter(mids, np.float32(np.inf)), np.nextafter(mids, np.float32(0))]
+    parts.append(np.array([0.0, -0.0, 65504.0, 65519.996, 65520.0, -65520.0, 2.0**-24, 2.0**-25,
+                           3 * 2.0**-26, 1e-45, np.inf, -np.inf, np.nan], np.float32))
+    x = np.concatenate(parts).astype(np.float32)
+    with np.errstate(over="ignore", invalid="ignore"):
+        want = x.astype(np.float16).astype(np.float32)
+    got = orc.round_f16(x)
+    nan = np.isnan(x)
+    assert np.array_equal(got[~nan].view(np.uint32), want[~nan].view(np.uint32))
+    assert np.all(np.isnan(got[nan]))
+
+
+def test_kv_f16_mode_vs_float64(qf, orc):
+    """The oracle's binary16 cache against the float64 restatement with float16-rounded
+    K/V, on one decoder layer: rounding amplifies differences of the last f32 bits into
+    whole binary16 steps (an element on the other side of a rounding boundary), which
+    compound over layers, so the pin uses one layer, where the two agree ~17x closer than
+    the f16 and f32 caches do."""
+    orc.set_threads(4)
+    m = qf.synth_model(seed=21, num_layers=1, vocab=512, hidden=1024, intermediate=1024,
+                       num_heads=8, num_kv_heads=2, head_dim=128, rope_rows=64)
+    om = orc.OracleModel(m)
+    kv, kv32 = om.new_kv("f16"), om.new_kv()
+    ref = RefModel(m, qf, kv_f16=True)
+    rkv = ref.new_kv()
+    for tok in (5, 77, 300, 1, 511, 42):
+        lo = om.forward_decode(tok, kv)
+        lr = ref.decode(tok, rkv)
+        l32 = om.forward_decode(tok, kv32)
+        assert rel_l2(lo, lr) < 3e-5
+        assert int(np.argmax(lo)) == int(np.argmax(lr))
+        assert 1e-4 < rel_l2(lo, l32) < 1e-2  # a different cache, close to the f32 one
+
+
+def test_kv_f16_cache_contents(orc, small_model):
+    """Every cached value is a binary16 value; layer 0 of the first step holds exactly the
+    rounded values of the f32 cache (same inputs up to there)."""
+    om = orc.OracleModel(small_model)
+    kv, kv32 = om.new_kv("f16"), om.new_kv()
+    toks = (5, 77, 300, 1)
+    for i, tok in enumerate(toks):
+        om.forward_decode(tok, kv)
+        om.forward_decode(tok, kv32)
+        if i == 0:
+            k16, v16 = kv.export_layer(0, 1, 256)
+            k32, v32 = kv32.export_layer(0, 1, 256)
+            assert np.array_equal(k16, orc.round_f16(k32)) and np.array_equal(v16, orc.round_f16(v32))
+    for layer in range(4):
+        k, v = kv.export_layer(layer, len(toks), 256)
+        assert np.array_equal(k, orc.round_f16(k)) and np.array_equal(v, orc.round_f16(v))
+
+
+def test_kv_f16_import_prefill_and_mode_switch(qf, orc):
+    """Import rounds; prefill attends to the rounded keys/values like a decode sequence
+    (one layer: see test_kv_f16_mode_vs_float64 on amplification); mode switch only on an
+    empty cache."""
+    orc.set_threads(3)
+    om = orc.OracleModel(qf.synth_model(seed=21, num_layers=1, vocab=512, hidden=1024, intermediate=1024,
+                                        num_heads=8, num_kv_heads=2, head_dim=128, rope_rows=64))
+    rng = np.random.default_rng(8)
+    K = rng.standard_normal((9, 256)).astype(np.float32)
+    V = rng.standard_normal((9, 256)).astype(np.float32)
+    kv = om.new_kv("f16")
+    kv.import_layer(0, K, V)
+    k, v = kv.export_layer(0, 9, 256)
+    assert np.array_equal(k, orc.round_f16(K)) and np.array_equal(v, orc.round_f16(V))
+    ids = np.array([3, 9, 100, 7, 200, 5, 6], np.uint32)
+    kv_a, kv_b = om.new_kv("f16"), om.new_kv("f16")
+    la = om.prefill(ids, kv_a)
+    for t in ids:
+        lb = om.forward_decode(int(t), kv_b)
+    assert rel_l2(la, lb) < 1e-5 and np.argmax(la) == np.argmax(lb)
+    assert orc.lib().orc_kv_set_f16(kv_b.h, 0) != 0  # not on a non-empty cache
+    with pytest.raises(ValueError):
+        om.new_kv("bf16")
