@@ -189,16 +189,55 @@ QORA_DEV int owner32(unsigned p, unsigned total, unsigned g) { return (int)(((p 
 struct Span {
   int lin0, n;
 };
+// Tile-aligned split-K (down_proj): tile t of T runs on CTAs [al_first(t), al_first(t+1))
+// of a g-CTA set (g >= T, so every tile gets floor or ceil of g/T CTAs), and CTA j of
+// the n on tile t owns its rows [j*K/n, (j+1)*K/n). No CTA crosses a tile boundary, so
+// none streams two partial segments or finishes two tiles.
+// (32-bit: the host checks tiles * g and g * K below 2^31)
+__host__ __device__ inline int al_first(int t, int g, int T) { return (int)((unsigned)(t * g) / (unsigned)T); }
+__host__ __device__ inline int al_tile(int lc, int g, int T) {  // the tile CTA lc works on
+  int t = (int)((unsigned)(lc * T) / (unsigned)g);
+  while (t + 1 < T && al_first(t + 1, g, T) <= lc) ++t;
+  while (t > 0 && al_first(t, g, T) > lc) --t;
+  return t;
+}
+
+// this CTA's span and first-CTA index of the tile-aligned matrix, computed once per launch
+// (al_span) and kept after the slot table: the phases read two words instead of carrying
+// the tile search
+QORA_DEV int al_slot_words(const Args& a) { return a.tiles[GU] + a.tiles[DOWN]; }
+QORA_DEV void al_span(const Args& a, int m, int lc, int* out) {  // out: lin0, n, first CTA of the tile
+  const int g = a.subn[m], T = a.tiles[m], K = a.K[m], t = al_tile(lc, g, T);
+  const int f0 = al_first(t, g, T), n = al_first(t + 1, g, T) - f0, j = lc - f0;
+  const int r0 = (int)((unsigned)(j * K) / (unsigned)n), r1 = (int)((unsigned)((j + 1) * K) / (unsigned)n);
+  out[0] = t * K + r0;
+  out[1] = r1 - r0;
+  out[2] = f0;
+}
+
 QORA_DEV Span span_of(const Args& a, int m, int c) {
   const int lc = c - a.sub0[m];
   const unsigned g = (unsigned)a.subn[m];
   if (lc < 0 || lc >= (int)g) return Span{0, 0};
+  if (m == DOWN) {  // tile-aligned: the calling CTA's own span (every caller passes blockIdx.x)
+    const int* w = reinterpret_cast<const int*>(sm_scratch() + kOffTab) + al_slot_words(a);
+    return Span{w[0], w[1]};
+  }
   const unsigned total = (unsigned)a.tiles[m] * (unsigned)a.K[m];
   const unsigned l0 = (unsigned)lc * total / g, l1 = (unsigned)(lc + 1) * total / g;
   return Span{(int)l0, (int)(l1 - l0)};
 }
 
+// the set-local index of the first CTA contributing to tile t (for the aligned matrix:
+// the calling CTA's own tile)
+QORA_DEV int slot0(const Args& a, int m, int t) {
+  if (m == DOWN) return reinterpret_cast<const int*>(sm_scratch() + kOffTab)[al_slot_words(a) + 2];
+  const unsigned K = (unsigned)a.K[m], total = (unsigned)a.tiles[m] * K;
+  return owner32((unsigned)t * K, total, (unsigned)a.subn[m]);
+}
+
 QORA_DEV int nslots(const Args& a, int m, int t) {
+  if (m == DOWN) return al_first(t + 1, a.subn[m], a.tiles[m]) - al_first(t, a.subn[m], a.tiles[m]);
   const unsigned K = (unsigned)a.K[m], total = (unsigned)a.tiles[m] * K, g = (unsigned)a.subn[m];
   return owner32((unsigned)(t + 1) * K - 1u, total, g) - owner32((unsigned)t * K, total, g) + 1;
 }
@@ -584,12 +623,11 @@ __device__ __noinline__ uint32_t gemv_stream(int m, int L, uint32_t chunk) {
   const int gi = C.lane % TG, sub = C.lane / TG;
   const Span sp = span_of(a, m, C.c);
   const int K = a.K[m], lc = C.c - a.sub0[m];
-  const unsigned total = (unsigned)a.tiles[m] * (unsigned)K;
   int off = 0;
 #pragma unroll 1
   for (int p = sp.lin0, e = sp.lin0 + sp.n; p < e;) {
     const int t = p / K, r0 = p - t * K, r1 = min(e, (t + 1) * K) - t * K;
-    const int slot = lc - owner32((unsigned)t * K, total, (unsigned)a.subn[m]);
+    const int slot = lc - slot0(a, m, t);
     float2 acc[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) acc[i] = make_float2(0.0f, 0.0f);
@@ -1438,6 +1476,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_megakernel(const Args args
     int* tab = reinterpret_cast<int*>(scratch + kOffTab);
     for (int t = tid; t < args.tiles[GU]; t += kThreads) tab[t] = nslots(args, GU, t);
     for (int t = tid; t < args.tiles[DOWN]; t += kThreads) tab[args.tiles[GU] + t] = nslots(args, DOWN, t);
+    const int lc = c - args.sub0[DOWN];
+    if (tid == 0 && lc >= 0 && lc < args.subn[DOWN])
+      al_span(args, DOWN, lc, tab + args.tiles[GU] + args.tiles[DOWN]);
   }
   __syncthreads();  // last block-wide barrier: the producer warp leaves below
   const Args& a = *sa;

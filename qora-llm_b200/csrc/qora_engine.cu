@@ -736,7 +736,7 @@ qora_status mega_init(qora_engine* e) {
     e->mk_sub0[m] = sub0[m];
     e->mk_subn[m] = subn[m];
   }
-  if (d0.gu.tiles + d0.down.tiles > mk::kMaxTabTiles) return no("too many gate/up and down tiles");
+  if (d0.gu.tiles + d0.down.tiles + 3 > mk::kMaxTabTiles) return no("too many gate/up and down tiles");
   if (H > mk::kBFloats) return no("hidden larger than the shared x buffer");
   if (nh * (mk::kMaxUnits / nkvh + 1) > mk::kBFloats) return no("attention merge weights do not fit");
   if (e->lm_row_bytes > mk::kStageBytes) return no("embedding row larger than a stage");
@@ -747,9 +747,20 @@ qora_status mega_init(qora_engine* e) {
   // longest cache whose attention units (kv head x chunk of <= kMaxAttnChunk) fit the grid
   e->mk_max_seq = (uint32_t)mk::kMaxAttnChunk * (uint32_t)(G / nkvh);
   if (e->num_layers > 62) return no("more than 62 layers (hand-off tags hold layer + 1 in 6 bits)");
-  for (int m = 2; m < 4; ++m) {
-    GemvShape sh = plan_gemv(mats[m]->K, mats[m]->tiles, subn[m]);
-    e->mk_slots[m] = sh.plan.max_slots;
+  {
+    GemvShape sh = plan_gemv(mats[mk::GU]->K, mats[mk::GU]->tiles, subn[mk::GU]);
+    e->mk_slots[mk::GU] = sh.plan.max_slots;
+  }
+  // down_proj: tile-aligned split (mk::al_first), at most ceil(G / tiles) CTAs per tile
+  const int dt = mats[mk::DOWN]->tiles;
+  if (dt > subn[mk::DOWN]) return no("more down_proj tiles than CTAs");
+  if ((long long)dt * subn[mk::DOWN] >= (1ll << 31) || (long long)subn[mk::DOWN] * mats[mk::DOWN]->K >= (1ll << 31))
+    return no("down_proj split outside 32-bit arithmetic");
+  e->mk_slots[mk::DOWN] = 0;
+  for (int t = 0; t < dt; ++t) {
+    const int n = mk::al_first(t + 1, subn[mk::DOWN], dt) - mk::al_first(t, subn[mk::DOWN], dt);
+    e->mk_slots[mk::DOWN] = std::max(e->mk_slots[mk::DOWN], n);
+    if ((mats[mk::DOWN]->K + n - 1) / n > mk::kXsCap) return no("per-CTA down_proj rows exceed the shared input buffer");
   }
   const size_t np_gu = (size_t)d0.gu.tiles * e->mk_slots[2] * kTileCols;
   const size_t np_dn = (size_t)d0.down.tiles * e->mk_slots[3] * kTileCols;
