@@ -121,6 +121,7 @@ struct Args {
   float* dn_part;             // down split-K partials [tiles][slots][256]
   uint64_t* att_o;            // tagged [kMaxUnits][4][128]
   uint64_t* att_ml;           // tagged [kMaxUnits][4][2]
+  uint64_t* att_fin;          // tagged [nh][128] merged attention output of the layer
   unsigned* epoch;            // launches so far (the tag base); advanced by the last CTA
   unsigned* cnt;              // down arrival counters [L][tiles] + the final arrival, zero between launches
   int cpl;                    // counters per layer
@@ -169,6 +170,8 @@ constexpr int kTraceFine = 64;
 
 // ---- counter layout: down arrivals per (layer, output tile), then the final arrival
 QORA_DEV int c_dn_arr(const Args& a, int L, int t) { return L * a.cpl + t; }
+// attention arrivals per (layer, kv head) after the down counters of the layer
+QORA_DEV int c_att(const Args& a, int L, int g) { return L * a.cpl + a.tiles[DOWN] + g; }
 QORA_DEV int c_lm(const Args& a) { return a.L * a.cpl; }
 
 // Attention units: (kv head, chunk of `chunk` positions), about one unit per CTA.
@@ -329,7 +332,7 @@ __device__ __noinline__ uint32_t produce_kv(int L, uint32_t chunk) {
 __device__ __noinline__ uint32_t produce_lm(uint32_t chunk) {
   const Args& a = *sm_args();
   const int c = blockIdx.x, G = gridDim.x, nv = a.v1 - a.v0;  // this rank's vocab rows
-  const int v0 = a.v0 + (int)((long long)c * nv / G), v1 = a.v0 + (int)((long long)(c + 1) * nv / G);
+  const int v0 = a.v0 + (int)((unsigned)(c * nv) / (unsigned)G), v1 = a.v0 + (int)((unsigned)((c + 1) * nv) / (unsigned)G);
 #pragma unroll 1
   for (int r = v0; r < v1; r += a.lm_rows_per_stage)
     chunk = issue(a.lm + (long long)r * a.lm_row_bytes,
@@ -855,6 +858,75 @@ QORA_DEV void kscore(const float* sq, const float* krow, float* sc, int idx, boo
   }
 }
 
+// Attention merge, run by the last of the nch units of KV head g to arrive (acq_rel
+// arrival count): per query head, M = max_ch m, w_ch = exp(m_ch - M), l = sum_ch l_ch w_ch,
+// out = (sum_ch o_ch w_ch, chunk order) * (1 / l), published tagged for o_proj.
+__device__ __noinline__ void attn_merge(int L, int g, int nch) {
+  Cons C = make_cons(0);
+  const Args& a = C.a();
+  const int hpk = a.hpk, nkvh = a.nkvh;
+  C.bar();  // every partial of this unit is stored
+  if (C.tid == 0) {
+    const unsigned prev = ptx::atom_add_acqrel(a.cnt + c_att(a, L, g), 1u);
+    C.flags[1] = (prev == (unsigned)(nch - 1));
+  }
+  C.bar();
+  if (!C.flags[1] || C.aborted()) return;
+  const uint32_t tag = tag_of(C, L);
+  float* mw = C.scratch + kOffB;            // [hpk][nch] chunk weights
+  float* invl = mw + kHeadsPerKV * nch;     // [hpk]
+  const long long ustride = (long long)nkvh * kHeadsPerKV * 2;         // (m, l): next chunk, same head
+  const long long ostride = (long long)nkvh * kHeadsPerKV * kHeadDim;  // o: next chunk, same head
+  if (C.warp < hpk) {  // one warp per query head, lane = chunk
+    const int h = C.warp;
+    const uint64_t* ml = a.att_ml + ((long long)g * kHeadsPerKV + h) * 2;
+    float mx = -INFINITY;
+#pragma unroll 1
+    for (int ch = C.lane; ch < nch; ch += 32) mx = fmaxf(mx, ld_checked(C, ml + ch * ustride, tag));
+    mx = warp_max(mx);
+    float l = 0.0f;
+    if (C.lane < nch) {
+      const float w = expf(ld_checked(C, ml + C.lane * ustride, tag) - mx);
+      mw[h * nch + C.lane] = w;
+      l = __fmul_rn(ld_checked(C, ml + C.lane * ustride + 1, tag), w);
+    }
+#pragma unroll 1
+    for (int ch = C.lane + 32; ch < nch; ch += 32) {
+      const float w = expf(ld_checked(C, ml + ch * ustride, tag) - mx);
+      mw[h * nch + ch] = w;
+      l = __fmaf_rn(ld_checked(C, ml + ch * ustride + 1, tag), w, l);
+    }
+    l = warp_sum(l);
+    if (C.lane == 0) invl[h] = __fdiv_rn(1.0f, l);
+  }
+  C.bar();
+  const uint64_t* o0 = a.att_o + (long long)g * kHeadsPerKV * kHeadDim;
+#pragma unroll 1
+  for (int r = C.tid; r < hpk * kHeadDim; r += kCT) {
+    const int h = r / kHeadDim;
+    float acc = 0.0f;
+#pragma unroll 1
+    for (int c0 = 0; c0 < nch; c0 += 4) {  // four chunks' values in flight
+      uint64_t v[4], t0 = 0;
+#pragma unroll 1
+      for (int it = 0;; ++it) {
+        bool ok = true;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const bool in = c0 + k < nch;
+          v[k] = in ? ptx::ld_relaxed_b64(o0 + (c0 + k) * ostride + r) : 0ull;
+          ok &= !in || tag_ok(v[k], tag);
+        }
+        if (ok || retry_stop(C, t0, it)) break;
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        if (c0 + k < nch) acc = __fmaf_rn(tag_val(v[k]), mw[h * nch + c0 + k], acc);
+    }
+    st_tagged(a.att_fin + (long long)(g * hpk) * kHeadDim + r, __fmul_rn(acc, invl[h]), tag);
+  }
+}
+
 // kscore for a binary16 K row (opt-in f16 cache): lane li takes dims [8li, 8li+8) and
 // [64+8li, 64+8li+8) as two 16-byte loads (conflict-free across the 8 lanes of a row)
 QORA_DEV void kscore16(const float* sq, const __half* krow, float* sc, int idx, bool valid, int li) {
@@ -1084,11 +1156,20 @@ __device__ __noinline__ uint32_t attention_phase_t(int L, uint32_t chunk) {
 #pragma unroll
       for (int h = 0; h < kHeadsPerKV; ++h) o[h] = __fmaf_rn(ppos[h], v, o[h]);
     }
+    if (nch == 1) {  // the whole context: publish o / l (exp(m - max) = 1 for the one chunk)
 #pragma unroll
-    for (int h = 0; h < kHeadsPerKV; ++h)
-      if (h < hpk) st_tagged(a.att_o + ((long long)u * kHeadsPerKV + h) * kHeadDim + tid, o[h], tag);
-    if (tid < 2 * hpk) st_tagged(a.att_ml + (long long)u * 2 * kHeadsPerKV + tid, sml[tid], tag);
+      for (int h = 0; h < kHeadsPerKV; ++h)
+        if (h < hpk)
+          st_tagged(a.att_fin + (long long)(g * hpk + h) * kHeadDim + tid,
+                    __fmul_rn(o[h], __fdiv_rn(1.0f, sml[h * 2 + 1])), tag);
+    } else {
+#pragma unroll
+      for (int h = 0; h < kHeadsPerKV; ++h)
+        if (h < hpk) st_tagged(a.att_o + ((long long)u * kHeadsPerKV + h) * kHeadDim + tid, o[h], tag);
+      if (tid < 2 * hpk) st_tagged(a.att_ml + (long long)u * 2 * kHeadsPerKV + tid, sml[tid], tag);
+    }
   }
+  if (nch > 1) attn_merge(L, g, nch);
   return C.chunk;
 }
 
@@ -1096,133 +1177,28 @@ __device__ __noinline__ uint32_t attention_phase(int L, uint32_t chunk) {
   return sm_args()->kv16 ? attention_phase_t<__half>(L, chunk) : attention_phase_t<float>(L, chunk);
 }
 
-// O: merge the (m, l, o) partials of every head (chunk order), GEMV over all rows for
-// this CTA's 32 columns, x_mid = x + o
+// O: the merged attention output of every head (tagged, one sentinel word per head), GEMV
+// over all rows for this CTA's 32 columns, x_mid = x + o
 __device__ __noinline__ uint32_t o_phase(int L, uint32_t chunk) {
   Cons C = make_cons(chunk);
   const Args& a = C.a();
   const Span sp = span_of(a, OPR, C.c);
   if (sp.n == 0) return chunk;
-  int csz, nch;
-  attn_plan(C.pos + 1, C.G, a.nkvh, csz, nch);
-  const int nkvh = a.nkvh, K = a.K[OPR];
+  const int K = a.K[OPR];
   const uint32_t tag = tag_of(C, L);
-  await_tags(C, nkvh * nch, tag, [&](int i) { return a.att_ml + (long long)i * 2 * kHeadsPerKV; });
+  await_tags(C, a.nh, tag, [&](int i) { return a.att_fin + (long long)i * kHeadDim; });
   C.stamp(2 + 8 * min(L, kTraceLayers - 1) + 3);
   C.fstamp();
-  // per query head h: M = max_ch m, w_ch = exp(m_ch - M), 1/l with l = sum l_ch w_ch;
-  // unit (chunk ch, kv head h/hpk) holds head h at slot h%hpk
-  const int hpk = a.hpk;
-  float* mw = C.scratch + kOffB;  // [nh][nch], then 1/l [nh]
-  float* invl = mw + a.nh * nch;
-  const long long ustride = (long long)nkvh * kHeadsPerKV * 2;          // (m, l): next chunk, same head
-  const long long ostride = (long long)nkvh * kHeadsPerKV * kHeadDim;   // o: next chunk, same head
-  auto ml_of = [&](int h) { return a.att_ml + ((h / hpk) * kHeadsPerKV + h % hpk) * 2; };
-  int orow[kXsPer];  // row r = head*128 + dim -> offset in a unit's [4][128] block
+  // xs = att * 2^64: each thread scales the pairs it loaded itself
+  float* xs = C.scratch;
+  load_x(C, xs, a.att_fin, K, tag);
+  constexpr int kPairs = (2048 / 2 + kCT - 1) / kCT;
 #pragma unroll
-  for (int j = 0; j < kXsPer; ++j) {
-    const int r = C.tid + j * kCT, h = r / kHeadDim;
-    orow[j] = ((h / hpk) * kHeadsPerKV + h % hpk) * kHeadDim + r % kHeadDim;
-  }
-  // One round trip for short contexts: this thread's o values of chunks [0, 4) and, per
-  // warp, the (m, l) of chunks [0, 32) of its query heads (warp, warp + kCW)
-  uint64_t v[kXsPer][4], mlv[2][2];
-  {
-    uint64_t t0 = 0;
-#pragma unroll 1
-    for (int it = 0;; ++it) {
-      bool ok = true;
-#pragma unroll
-      for (int q = 0; q < 2; ++q) {
-        const int h = C.warp + q * kCW;
-        const bool in = h < a.nh && C.lane < nch;
-        if (in) ptx::ld_relaxed_v2_b64(ml_of(h) + C.lane * ustride, mlv[q][0], mlv[q][1]);
-        ok &= !in || (tag_ok(mlv[q][0], tag) & tag_ok(mlv[q][1], tag));
-      }
-#pragma unroll
-      for (int j = 0; j < kXsPer; ++j) {
-        const int r = C.tid + j * kCT;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const bool in = r < K && k < nch;
-          v[j][k] = in ? ptx::ld_relaxed_b64(a.att_o + k * ostride + orow[j]) : 0ull;
-          ok &= !in || tag_ok(v[j][k], tag);
-        }
-      }
-      if (ok || retry_stop(C, t0, it)) break;
-    }
-  }
-  C.fstamp();
-  // per query head h: M = max_ch m, w_ch = exp(m_ch - M), 1/l with l = sum l_ch w_ch
-#pragma unroll
-  for (int q = 0; q < 2; ++q) {
-    const int h = C.warp + q * kCW;
-    if (h < a.nh) {  // warp-uniform
-      const uint64_t* ml = ml_of(h);
-      float mx = C.lane < nch ? tag_val(mlv[q][0]) : -INFINITY;
-#pragma unroll 1
-      for (int ch = C.lane + 32; ch < nch; ch += 32) mx = fmaxf(mx, ld_checked(C, ml + ch * ustride, tag));
-      mx = warp_max(mx);
-      float l = 0.0f;
-      if (C.lane < nch) {
-        const float w = expf(tag_val(mlv[q][0]) - mx);
-        mw[h * nch + C.lane] = w;
-        l = __fmul_rn(tag_val(mlv[q][1]), w);
-      }
-#pragma unroll 1
-      for (int ch = C.lane + 32; ch < nch; ch += 32) {
-        const float w = expf(ld_checked(C, ml + ch * ustride, tag) - mx);
-        mw[h * nch + ch] = w;
-        l = __fmaf_rn(ld_checked(C, ml + ch * ustride + 1, tag), w, l);
-      }
-      l = warp_sum(l);
-      if (C.lane == 0) invl[h] = __fdiv_rn(1.0f, l);
-    }
-  }
-  C.bar();
-  C.fstamp();
-  // xs[r] = (sum_ch o_ch[r] w_ch) / l, r = head * 128 + dim
-  {
-    float* xs = C.scratch;
-    float acc[kXsPer];
-#pragma unroll
-    for (int j = 0; j < kXsPer; ++j) {
-      const int r = C.tid + j * kCT, h = r / kHeadDim;
-      acc[j] = 0.0f;
-#pragma unroll
-      for (int k = 0; k < 4; ++k)
-        if (r < K && k < nch) acc[j] = __fmaf_rn(tag_val(v[j][k]), mw[h * nch + k], acc[j]);
-    }
-#pragma unroll 1
-    for (int c0 = 4; c0 < nch; c0 += 4) {  // longer contexts: further batches of 4 chunks
-      uint64_t t0 = 0;
-#pragma unroll 1
-      for (int it = 0;; ++it) {
-        bool ok = true;
-#pragma unroll
-        for (int j = 0; j < kXsPer; ++j) {
-          const int r = C.tid + j * kCT;
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const bool in = r < K && c0 + k < nch;
-            v[j][k] = in ? ptx::ld_relaxed_b64(a.att_o + (c0 + k) * ostride + orow[j]) : 0ull;
-            ok &= !in || tag_ok(v[j][k], tag);
-          }
-        }
-        if (ok || retry_stop(C, t0, it)) break;
-      }
-#pragma unroll
-      for (int j = 0; j < kXsPer; ++j) {
-        const int r = C.tid + j * kCT, h = r / kHeadDim;
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-          if (r < K && c0 + k < nch) acc[j] = __fmaf_rn(tag_val(v[j][k]), mw[h * nch + c0 + k], acc[j]);
-      }
-    }
-#pragma unroll
-    for (int j = 0; j < kXsPer; ++j) {
-      const int r = C.tid + j * kCT;
-      if (r < K) xs[r] = __fmul_rn(acc[j], invl[r / kHeadDim]) * kTwo64;
+  for (int j = 0; j < kPairs; ++j) {
+    const int b = C.tid + j * kCT;
+    if (b < K / 2) {
+      xs[2 * b] *= kTwo64;
+      xs[2 * b + 1] *= kTwo64;
     }
   }
   C.bar();
@@ -1391,7 +1367,7 @@ __device__ __noinline__ void lm_phase(uint32_t chunk) {
   float best = -INFINITY;
   unsigned besti = 0xFFFFFFFFu;
   const int nv = a.v1 - a.v0;  // this rank's vocab rows
-  const int v0 = a.v0 + (int)((long long)C.c * nv / C.G), v1 = a.v0 + (int)((long long)(C.c + 1) * nv / C.G);
+  const int v0 = a.v0 + (int)((unsigned)(C.c * nv) / (unsigned)C.G), v1 = a.v0 + (int)((unsigned)((C.c + 1) * nv) / (unsigned)C.G);
 #pragma unroll 1
   for (int r = v0; r < v1; r += a.lm_rows_per_stage) {
     const uint8_t* stg = C.acquire_stage();

@@ -375,6 +375,7 @@ struct qora_kv {
   mk::Layer* mk_layers = nullptr;
   uint64_t* mk_att_o = nullptr;  // tagged
   uint64_t* mk_att_ml = nullptr;
+  uint64_t* mk_att_fin = nullptr;  // tagged merged attention output [nh][128]
   std::vector<void*> allocs;
   // free the device-side state (the engine's stream must be idle or synchronised)
   void release_device() {
@@ -740,6 +741,7 @@ qora_status mega_init(qora_engine* e) {
   if (H > mk::kBFloats) return no("hidden larger than the shared x buffer");
   if (nh * (mk::kMaxUnits / nkvh + 1) > mk::kBFloats) return no("attention merge weights do not fit");
   if (e->lm_row_bytes > mk::kStageBytes) return no("embedding row larger than a stage");
+  if ((long long)G * e->vocab >= (1ll << 31)) return no("vocab split outside 32-bit arithmetic");
   int blocks = 0;
   if (H == 2048) QCHECK(mega_occupancy<2>(&blocks)); else QCHECK(mega_occupancy<1>(&blocks));
   if (blocks < 1) return no("megakernel does not fit one CTA per SM");
@@ -764,7 +766,7 @@ qora_status mega_init(qora_engine* e) {
   }
   const size_t np_gu = (size_t)d0.gu.tiles * e->mk_slots[2] * kTileCols;
   const size_t np_dn = (size_t)d0.down.tiles * e->mk_slots[3] * kTileCols;
-  e->mk_cpl = d0.down.tiles;
+  e->mk_cpl = d0.down.tiles + nkvh;  // per layer: down tile arrivals, then attention arrivals per KV head
   e->mk_ncnt = (int)e->num_layers * e->mk_cpl + 2;
   QCHECK(e->alloc(&e->mk_cnt, e->mk_ncnt));
   QCUDA(cudaMemset(e->mk_cnt, 0, (size_t)e->mk_ncnt * sizeof(unsigned)));
@@ -821,6 +823,8 @@ qora_status mega_prepare(qora_engine* e, qora_kv* kv) {
   QCHECK(kv->alloc(&kv->mk_att_ml, (size_t)G * mk::kHeadsPerKV * 2));
   QCUDA(cudaMemset(kv->mk_att_o, 0, (size_t)G * mk::kHeadsPerKV * kHeadDim * sizeof(uint64_t)));
   QCUDA(cudaMemset(kv->mk_att_ml, 0, (size_t)G * mk::kHeadsPerKV * 2 * sizeof(uint64_t)));
+  QCHECK(kv->alloc(&kv->mk_att_fin, (size_t)e->nh_l * kHeadDim));
+  QCUDA(cudaMemset(kv->mk_att_fin, 0, (size_t)e->nh_l * kHeadDim * sizeof(uint64_t)));
   mk::Args& a = kv->mk_args;
   a = mk::Args{};
   a.layers = kv->mk_layers;
@@ -865,6 +869,7 @@ qora_status mega_prepare(qora_engine* e, qora_kv* kv) {
   a.logits = e->logits;
   a.att_o = kv->mk_att_o;
   a.att_ml = kv->mk_att_ml;
+  a.att_fin = kv->mk_att_fin;
   a.cnt = e->mk_cnt;
   a.cpl = e->mk_cpl;
   a.n_cnt = e->mk_ncnt;
