@@ -209,7 +209,7 @@ __host__ __device__ inline int al_tile(int lc, int g, int T) {  // the tile CTA 
 // (al_span) and kept after the slot table: the phases read two words instead of carrying
 // the tile search
 QORA_DEV int al_slot_words(const Args& a) { return a.tiles[GU] + a.tiles[DOWN]; }
-QORA_DEV void al_span(const Args& a, int m, int lc, int* out) {  // out: lin0, n, first CTA of the tile
+__host__ __device__ __forceinline__ void al_span(const Args& a, int m, int lc, int* out) {  // out: lin0, n, first CTA of the tile
   const int g = a.subn[m], T = a.tiles[m], K = a.K[m], t = al_tile(lc, g, T);
   const int f0 = al_first(t, g, T), n = al_first(t + 1, g, T) - f0, j = lc - f0;
   const int r0 = (int)((unsigned)(j * K) / (unsigned)n), r1 = (int)((unsigned)((j + 1) * K) / (unsigned)n);

@@ -78,11 +78,14 @@ class DecodeWeights {
 };
 
 // A KV cache on the device: `batch` independent sequences of up to max_seq positions.
+// kv_dtype QORA_KV_F16 is the opt-in binary16 cache (Q4 engines; results differ from the
+// reference's f32 cache).
 class RawKvCache {
  public:
-  RawKvCache(const DecodeWeights& w, uint32_t max_seq, uint32_t batch = 1) : kv_(nullptr, &qora_kv_destroy) {
+  RawKvCache(const DecodeWeights& w, uint32_t max_seq, uint32_t batch = 1, uint32_t kv_dtype = QORA_KV_F32)
+      : kv_(nullptr, &qora_kv_destroy) {
     qora_kv* kv = nullptr;
-    check(qora_kv_create(w.raw(), max_seq, batch, &kv));
+    check(qora_kv_create_ex(w.raw(), max_seq, batch, kv_dtype, &kv));
     kv_.reset(kv);
     batch_ = batch;
   }
@@ -96,6 +99,14 @@ class RawKvCache {
   void import_layer(uint32_t layer, const std::vector<float>& k, const std::vector<float>& v, uint32_t seq_len,
                     uint32_t seq = 0) {
     check(qora_kv_import(kv_.get(), layer, k.data(), v.data(), seq_len, seq));
+  }
+  // the first seq_len rows of one layer, token-major [seq_len][kv_heads*128] (f32 whatever
+  // the cache's element type)
+  void export_layer(uint32_t layer, std::vector<float>& k, std::vector<float>& v, uint32_t seq_len, size_t kv_row,
+                    uint32_t seq = 0) const {
+    k.resize((size_t)seq_len * kv_row);
+    v.resize((size_t)seq_len * kv_row);
+    check(qora_kv_export(kv_.get(), layer, k.data(), v.data(), seq_len, seq));
   }
   uint32_t batch() const { return batch_; }
   qora_kv* raw() const { return kv_.get(); }
