@@ -446,6 +446,8 @@ qora_status validate_view(const qora_weights_view* w) {
     return fail(QORA_ERR_UNSUPPORTED, "hidden=%u must be a multiple of 1024 up to 4096", w->hidden);
   if (w->rope_half_dim != kHalfDim)
     return fail(QORA_ERR_UNSUPPORTED, "rope_half_dim=%u, only 64 supported", w->rope_half_dim);
+  if (w->vocab == 0 || w->vocab > (1u << 24)) return fail(QORA_ERR_UNSUPPORTED, "vocab %u (1 .. 2^24)", w->vocab);
+  if (w->num_layers > 4096) return fail(QORA_ERR_UNSUPPORTED, "num_layers %u", w->num_layers);
   if (w->embed.k != w->vocab || w->embed.n != w->hidden || !present(w->embed))
     return fail(QORA_ERR_INVALID, "embedding must be [vocab][hidden] in the model's format");
   if (!q4 && w->vocab % 128 != 0)
@@ -473,7 +475,8 @@ qora_status validate_view(const qora_weights_view* w) {
                     (unsigned long long)wm.m->k, (unsigned long long)wm.m->n,
                     (unsigned long long)wm.k, (unsigned long long)wm.n, q4 ? "Q4" : "F16");
     }
-    if (I % 128 != 0 || I == 0) return fail(QORA_ERR_UNSUPPORTED, "intermediate %llu not a multiple of 128", (unsigned long long)I);
+    if (I % 128 != 0 || I == 0 || I > (1u << 20))
+      return fail(QORA_ERR_UNSUPPORTED, "intermediate %llu not a multiple of 128 up to 2^20", (unsigned long long)I);
     if (!L.input_norm_gamma || !L.post_attn_norm_gamma) return fail(QORA_ERR_INVALID, "layer %u norms missing", i);
   }
   return QORA_OK;
@@ -1754,6 +1757,12 @@ struct FileReader {
   void mat(uint8_t fmt, FileMat& m) {
     m.k = u64();
     m.n = u64();
+    // bound the shape before any product of it (a wrapped k*n could match the stored size)
+    if (ok && (m.k >= (1ull << 32) || m.n >= (1ull << 32) || m.k * m.n > (1ull << 40))) {
+      ok = false;
+      err = "implausible matrix shape";
+      return;
+    }
     if (fmt == 1) {
       uint64_t np = 0;
       m.packed = span<uint8_t>(np);

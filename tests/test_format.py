@@ -138,3 +138,20 @@ def test_engine_reader_accepts_valid_file(tmp_path, qf, pkg):
     with pytest.raises(pkg.QoraError) as ei:
         pkg.DecodeWeights(path=str(p))
     assert ei.value.status == 3, str(ei.value)
+
+
+@pytest.mark.parametrize("k,n", [(1 << 32, 1 << 32), (1 << 40, 16), (1 << 21, 1 << 20)])
+def test_engine_reader_rejects_wrapping_shapes(tmp_path, qf, pkg, k, n):
+    """A matrix header whose k*n would wrap (or exceed 2^40 elements) is rejected before any
+    size arithmetic: the first layer's q_proj shape is overwritten in a valid file."""
+    m = tiny(qf)
+    p = tmp_path / "shape.qora"
+    qf.write_qora(m, p)
+    b = bytearray(p.read_bytes())
+    off = 4 + 4 + 1 + 4 * 4 + 8 + m.num_layers  # header, no_rope_layers vector
+    assert struct.unpack_from("<QQ", b, off) == (m.layers[0].q_proj.k, m.layers[0].q_proj.n)
+    struct.pack_into("<QQ", b, off, k, n)
+    p.write_bytes(bytes(b))
+    with pytest.raises(pkg.QoraError, match="implausible matrix shape") as ei:
+        pkg.DecodeWeights(path=str(p))
+    assert ei.value.status == 1
