@@ -519,7 +519,7 @@ qora_status tp_plan(uint32_t format, uint32_t nh, uint32_t nkvh, uint32_t I, uin
   return QORA_OK;
 }
 
-qora_status upload(qora_engine* e, void* dst, const void* src, size_t bytes) {
+qora_status upload(qora_engine* /*e*/, void* dst, const void* src, size_t bytes) {
   QCUDA(cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice));
   return QORA_OK;
 }

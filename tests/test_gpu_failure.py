@@ -8,7 +8,6 @@ usable (a plain engine on the same device decodes afterwards)."""
 import multiprocessing as mp
 import queue
 
-import numpy as np
 import pytest
 
 pytestmark = pytest.mark.gpu
