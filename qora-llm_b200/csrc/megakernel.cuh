@@ -15,12 +15,15 @@
 //        q|k|v values (before RoPE), no split-K
 //   ATTN [one CTA per (kv head, chunk of positions)] RoPE on its 4 query heads (and,
 //        for the chunk holding the new position, on k, which it appends with v to the
-//        head-major cache), scores, softmax numerators, P.V -> (m, l, o)
-//   O    [one CTA per 32-column group of o_proj] merge the (m, l, o) partials of all
+//        head-major cache), scores, softmax numerators, P.V -> (m, l, o); the last unit
+//        of a KV head (atomic arrival count) merges the chunks and publishes the heads'
+//        normalised output (one chunk: the unit publishes o / l itself)
+//   O    [one CTA per 32-column group of o_proj] the merged attention output of all
 //        heads, GEMV over all rows, x_mid = x + o for its columns
 //   GU   [all] RMSNorm(x_mid) . [gate|up], split-K over 256-column tiles -> partials
-//   DOWN [all] SwiGLU of its rows from the gate/up partials, split-K GEMV; the last CTA
-//        of an output tile (atomic arrival count) writes x_next = x_mid + down for it
+//   DOWN [all] SwiGLU of its rows from the gate/up partials, split-K GEMV with every
+//        CTA's rows inside one output tile; the last CTA of a tile (atomic arrival
+//        count) writes x_next = x_mid + down for it
 // then lm_head rows (a contiguous slice per CTA) with a fused first-maximum argmax.
 //
 // Hand-off between CTAs: every value one CTA passes to another (q|k|v, attention
