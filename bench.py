@@ -6,7 +6,8 @@ argmax).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     python bench.py --workload f16-batch [--batch 32] [--steps 128]
-    python bench.py --workload q4-long [--steps 128]
+    python bench.py --workload q4-long [--steps 128] [--kv f16]
+    python bench.py --workload q4-gemv                                 # BASELINE config 1 (GB/s)
 
 Prints one JSON line (rank 0). `value` is device time (CUDA events on the engine's
 stream) of K greedy steps, each one launch of the persistent decode kernel, with the
@@ -580,6 +581,138 @@ def run_q4_long(args, rank, world, local_rank):
     return 0
 
 
+# ---------------------------------------------------------------- config 1: Q4 GEMV
+GEMV_METRIC = "Q4 GEMV HBM GB/s (config 1: gate_proj, k=2048 in, n=11008 out, reference F1 layout)"
+GEMV_K, GEMV_N = 2048, 11008
+L2_BYTES = 126 * 1024 * 1024
+
+
+def gemv_bytes(k=GEMV_K, n=GEMV_N):
+    """Algorithmic bytes of one GEMV: packed nibbles + f16 scales + x + y (12,733,440 for
+    config 1)."""
+    return k * n // 2 + k * n // 32 * 2 + k * 4 + n * 4
+
+
+def config1():
+    import importlib
+    qf = importlib.import_module("qora-llm_b200").qora_format
+    rng = np.random.default_rng(0)
+    m = qf.synth_q4_matrix(rng, GEMV_K, GEMV_N)
+    x = rng.standard_normal(GEMV_K).astype(np.float32)
+    return m, x
+
+
+def gemv_cpu(m, x, steps, budget_s, threads):
+    """The reference's gemv_q4 (oracle/: k-split over the host threads, AVX-512) timed per
+    call on this host: median of >= 5 calls, bounded by ~budget_s. Returns (GB/s, calls)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    oracle.set_threads(threads)
+    oracle.gemv_q4(x, m)  # warm-up
+    times, t_end = [], time.perf_counter() + budget_s
+    while len(times) < max(5, steps) and (len(times) < 5 or time.perf_counter() < t_end):
+        t0 = time.perf_counter()
+        oracle.gemv_q4(x, m)
+        times.append(time.perf_counter() - t0)
+    return gemv_bytes() / statistics.median(times) / 1e9, len(times)
+
+
+def run_q4_gemv(args, rank, world, local_rank):
+    """the Q4 GEMV kernel alone (qora_q4_gemv on device buffers in the
+    reference's F1 layout). Every launch reads a different copy of the weights, rotating
+    over more than four times the L2 capacity, so each launch streams its weights from
+    HBM; the K launches are captured in one CUDA graph and timed with CUDA events."""
+    if world > 1:
+        if rank == 0:
+            print(json.dumps({"metric": GEMV_METRIC, "unavailable": "the config-1 GEMV line is single-GPU"}))
+        return 0
+    K, W = args.steps, args.warmup
+    threads = os.cpu_count() or 1
+    m, x = config1()
+    cfg = {"workload": "config 1: one Q4 GEMV, gate_proj 2048 x 11008 (F1 layout, seed 0), x ~ N(0,1)",
+           "k": GEMV_K, "n": GEMV_N, "bytes_per_gemv": gemv_bytes()}
+    if args.impl == "reference":
+        v, n = gemv_cpu(m, x, K, args.cpu_seconds, threads)
+        line = {"impl": "reference", "metric": GEMV_METRIC, "value": v, "unit": "GB/s", "n_gpus": 1, "steps": n,
+                "warmup": 1, "ms_per_step": gemv_bytes() / v / 1e6, "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded Q4 gate_proj)", "config": cfg,
+                "cpu_baseline": {"value": v, "unit": "GB/s", "cores": threads, "kind": "port",
+                                 "sample": f"median of {n} gemv_q4 calls, {threads} threads", "cpu": cpu_model()},
+                "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return 0
+    import importlib
+    import torch
+    pkg = importlib.import_module("qora-llm_b200")
+    torch.cuda.set_device(local_rank)
+    copies = max(2, -(-4 * L2_BYTES // gemv_bytes()))
+    packed = [torch.from_numpy(m.packed).cuda() for _ in range(copies)]
+    scales = [torch.from_numpy(m.scales.view(np.int16)).cuda() for _ in range(copies)]
+    dx = torch.from_numpy(x).cuda()
+    dy = torch.empty(GEMV_N, dtype=torch.float32, device="cuda")
+    stream = torch.cuda.Stream()
+
+    def gemv(i, s):
+        pkg.engine.q4_gemv(dx.data_ptr(), packed[i % copies].data_ptr(), scales[i % copies].data_ptr(),
+                           GEMV_K, GEMV_N, dy.data_ptr(), stream=s)
+
+    with torch.cuda.stream(stream):  # warm-up (also sizes the library's cached scratch)
+        for i in range(W):
+            gemv(i, stream)
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        cap = torch.cuda.current_stream()
+        for i in range(K):
+            gemv(i, cap)
+    graph.replay()  # untimed replay
+    stream.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        t0.record(stream)
+        with torch.cuda.stream(stream):
+            graph.replay()
+        t1.record(stream)
+        t1.synchronize()
+    ms = t0.elapsed_time(t1)
+    value = gemv_bytes() / (ms / K / 1000.0) / 1e9
+    # e2e: per step, x from pinned host memory, the GEMV through the C ABI, y back
+    hx = torch.from_numpy(x).pin_memory()
+    hy = torch.empty(GEMV_N, dtype=torch.float32).pin_memory()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    with torch.cuda.stream(stream):
+        for i in range(K):
+            dx.copy_(hx, non_blocking=True)
+            gemv(i, stream)
+            hy.copy_(dy, non_blocking=True)
+    e1.record(stream)
+    e1.synchronize()
+    e2e = gemv_bytes() / (e0.elapsed_time(e1) / K / 1000.0) / 1e9
+    del graph
+    peak, peak_kind = peaks()
+    line = {
+        "metric": GEMV_METRIC, "value": value, "unit": "GB/s", "n_gpus": 1, "steps": K, "warmup": W,
+        "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded Q4 gate_proj, N(0,1) input)",
+        "config": dict(cfg, weight_copies=copies,
+                       l2=f"weights rotated over {copies} copies ({copies * gemv_bytes() / 1e6:.0f} MB, > 4x L2)",
+                       timing="K launches in one CUDA graph, CUDA events around the replay"),
+        "e2e": {"value": e2e, "unit": "GB/s", "h2d_bytes_per_step": GEMV_K * 4, "d2h_bytes_per_step": GEMV_N * 4},
+        "gpu_launches": K,
+        "roofline": dict(bound="hbm", achieved=value, peak=peak, peak_kind=f"{peak_kind} hbm_gbs (copy)",
+                         unit="GB/s", frac=value / peak, traffic=None, kernel="q4 split-K GEMV (qora_q4_gemv)",
+                         bytes_per_launch=gemv_bytes(), us_per_launch=1000 * ms / K, launches_timed=K),
+        "clocks": clk.summary(),
+    }
+    if not args.no_cpu_baseline:
+        v, n = gemv_cpu(m, x, 5, args.cpu_seconds, threads)
+        line["cpu_baseline"] = {"value": v, "unit": "GB/s", "cores": threads, "kind": "port",
+                                "sample": f"median of {n} gemv_q4 calls, {threads} threads", "cpu": cpu_model()}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -588,8 +721,9 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
-    ap.add_argument("--workload", choices=("q4", "q4-long", "f16-batch"), default="q4",
-                    help="q4: config 3 batch-1 decode (the headline); q4-long: config 4; f16-batch: config 5")
+    ap.add_argument("--workload", choices=("q4", "q4-long", "f16-batch", "q4-gemv"), default="q4",
+                    help="q4: config 3 batch-1 decode (the headline); q4-long: config 4; f16-batch: config 5; "
+                         "q4-gemv: config 1 (the Q4 GEMV kernel alone, GB/s)")
     ap.add_argument("--batch", type=int, default=32, help="sequences for --workload f16-batch")
     ap.add_argument("--kv", choices=("f32", "f16"), default="f32",
                     help="KV cache element type for --workload q4-long (f16: the opt-in binary16 cache, "
@@ -607,6 +741,8 @@ def main():
         return run_f16(args, rank, world, local_rank)
     if args.workload == "q4-long":
         return run_q4_long(args, rank, world, local_rank)
+    if args.workload == "q4-gemv":
+        return run_q4_gemv(args, rank, world, local_rank)
     if args.impl == "reference":
         return run_reference(args, rank)
     return run_ours(args, rank, world, local_rank)

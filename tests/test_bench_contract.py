@@ -37,3 +37,13 @@ def test_reference_arm_line():
 def test_warmup_below_three_is_refused():
     out = _run("--impl", "reference", "--layers", "2", "--steps", "2", "--warmup", "2", timeout=120)
     assert out.returncode != 0 and "warmup" in out.stderr
+
+
+def test_reference_arm_gemv_line():
+    """Config 1 (the Q4 GEMV alone, GB/s): the reference arm times the oracle's gemv_q4."""
+    out = _run("--impl", "reference", "--workload", "q4-gemv", "--steps", "5", "--warmup", "3", "--cpu-seconds", "1")
+    assert out.returncode == 0, out.stderr[-2000:]
+    d = json.loads([l for l in out.stdout.splitlines() if l.startswith("{")][-1])
+    assert BASE_KEYS <= set(d) and d["unit"] == "GB/s" and d["value"] > 0 and d["steps"] >= 5
+    assert d["config"]["bytes_per_gemv"] == 2048 * 11008 // 2 + 2048 * 11008 // 32 * 2 + 2048 * 4 + 11008 * 4
+    assert d["cpu_baseline"]["unit"] == "GB/s"
