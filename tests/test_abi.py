@@ -13,7 +13,8 @@ HEADER = os.path.join(ROOT, "include", "qora_cuda.h")
 
 
 def declared_functions():
-    src = open(HEADER).read()
+    with open(HEADER) as f:
+        src = f.read()
     src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
     return sorted(set(re.findall(r"\b(qora_[a-z0-9_]+)\s*\(", src)))
 

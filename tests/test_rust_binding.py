@@ -19,6 +19,11 @@ BASE = {"uint8_t": "u8", "uint16_t": "u16", "uint32_t": "u32", "uint64_t": "u64"
         "qora_status": "qora_status"}
 
 
+def _read(path):
+    with open(path) as f:
+        return f.read()
+
+
 def _strip_c(src):
     src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
     return re.sub(r"//[^\n]*", "", src)
@@ -49,7 +54,7 @@ def _norm_rs(t):
 
 
 def header_functions():
-    src = _strip_c(open(HEADER).read())
+    src = _strip_c(_read(HEADER))
     out = {}
     for ret, name, params in re.findall(r"(qora_status|void|const char\s*\*)\s+(qora_\w+)\s*\(([^)]*)\)\s*;", src):
         ps = []
@@ -64,7 +69,7 @@ def header_functions():
 
 
 def crate_functions():
-    src = _strip_rs(open(os.path.join(CRATE, "src", "lib.rs")).read())
+    src = _strip_rs(_read(os.path.join(CRATE, "src", "lib.rs")))
     block = re.search(r'extern "C" \{(.*)\n\}', src, flags=re.S).group(1)
     out = {}
     for name, params, ret in re.findall(r"pub fn (\w+)\(([^)]*)\)\s*(?:->\s*([^;]+))?;", block, flags=re.S):
@@ -74,7 +79,7 @@ def crate_functions():
 
 
 def header_structs():
-    src = _strip_c(open(HEADER).read())
+    src = _strip_c(_read(HEADER))
     out = {}
     for body, name in re.findall(r"typedef struct \w+ \{(.*?)\}\s*(\w+)\s*;", src, flags=re.S):
         fields = []
@@ -91,7 +96,7 @@ def header_structs():
 
 
 def crate_structs():
-    src = _strip_rs(open(os.path.join(CRATE, "src", "lib.rs")).read())
+    src = _strip_rs(_read(os.path.join(CRATE, "src", "lib.rs")))
     out = {}
     for name, body in re.findall(r"pub struct (\w+) \{(.*?)\}", src, flags=re.S):
         out[name] = [(n, _norm_rs(t)) for n, t in re.findall(r"pub (\w+): ([^,]+),", body)]
@@ -103,12 +108,12 @@ def _eval(expr):
 
 
 def header_constants():
-    src = _strip_c(open(HEADER).read())
+    src = _strip_c(_read(HEADER))
     return {n: _eval(v) for n, v in re.findall(r"#define (QORA_\w+)\s+(.+)", src) if n != "QORA_CUDA_H"}
 
 
 def crate_constants():
-    src = _strip_rs(open(os.path.join(CRATE, "src", "lib.rs")).read())
+    src = _strip_rs(_read(os.path.join(CRATE, "src", "lib.rs")))
     return {n: _eval(v) for n, v in re.findall(r"pub const (QORA_\w+): \w+ = ([^;]+);", src)}
 
 
@@ -148,12 +153,12 @@ def test_every_constant_has_the_same_value():
                                   "try_forward_decode_raw", "try_raw_prefill", "generate_greedy", "greedy",
                                   "sample_next", "decode_greedy", "tp_plan"])
 def test_safe_layer_offers_the_reference_entry_points(name):
-    src = open(os.path.join(CRATE, "src", "safe.rs")).read()
+    src = _read(os.path.join(CRATE, "src", "safe.rs"))
     assert re.search(rf"pub (?:unsafe )?fn {name}\b", src), name
 
 
 def test_crate_manifest_links_the_library():
-    toml = open(os.path.join(CRATE, "Cargo.toml")).read()
+    toml = _read(os.path.join(CRATE, "Cargo.toml"))
     assert 'name = "qora-cuda-sys"' in toml and 'links = "qora_cuda"' in toml
-    build = open(os.path.join(CRATE, "build.rs")).read()
+    build = _read(os.path.join(CRATE, "build.rs"))
     assert "rustc-link-lib=dylib=qora_cuda" in build
