@@ -1,13 +1,13 @@
 #!/usr/bin/env python
-"""Decode throughput of the B200 engine on BASELINE config 3: SmolLM3-3B architecture,
+"""Decode throughput of the B200 engine on benchmark config 3: SmolLM3-3B architecture,
 seeded random-init Q4 weights (synthetic; no checkpoint), 32-token prompt, greedy decode
 at batch 1. A "step" is one decode step (one token through all 36 layers + lm_head +
 argmax).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-    python bench.py --workload f16-batch [--batch 32] [--steps 128]
-    python bench.py --workload q4-long [--steps 128] [--kv f16]
-    python bench.py --workload q4-gemv                                 # BASELINE config 1 (GB/s)
+    python bench.py --workload f16-batch [--batch 32] [--steps 128]   # benchmark config 5
+    python bench.py --workload q4-long [--steps 128] [--kv f16]         # benchmark config 4
+    python bench.py --workload q4-gemv                                 # benchmark config 1 (GB/s)
 
 Prints one JSON line (rank 0). `value` is device time (CUDA events on the engine's
 stream) of K greedy steps, each one launch of the persistent decode kernel, with the
@@ -348,7 +348,7 @@ def f16_cpu_sample(model, budget_s, threads):
 
 
 def run_f16(args, rank, world, local_rank):
-    """B independent sequences, 128-token prompts, greedy batched
+    """benchmark config 5: B independent sequences, 128-token prompts, greedy batched
     decode on one GPU (tcgen05 GEMMs)."""
     B, K, W = args.batch, args.steps, args.warmup
     threads = os.cpu_count() or 1
@@ -482,7 +482,7 @@ def long_kv(layers, seed=4):
 
 
 def run_q4_long(args, rank, world, local_rank):
-    """the Q4 model with every layer's KV cache pre-filled to 32768
+    """benchmark config 4: the Q4 model with every layer's KV cache pre-filled to 32768
     positions (qora_kv_import), then greedy decode at batch 1; attention KV reads
     dominate the bytes per token."""
     if world > 1:
@@ -618,7 +618,7 @@ def gemv_cpu(m, x, steps, budget_s, threads):
 
 
 def run_q4_gemv(args, rank, world, local_rank):
-    """the Q4 GEMV kernel alone (qora_q4_gemv on device buffers in the
+    """benchmark config 1: the Q4 GEMV kernel alone (qora_q4_gemv on device buffers in the
     reference's F1 layout). Every launch reads a different copy of the weights, rotating
     over more than four times the L2 capacity, so each launch streams its weights from
     HBM; the K launches are captured in one CUDA graph and timed with CUDA events."""

@@ -1,5 +1,5 @@
 // f16_batch.cuh — the per-row kernels of F16-weight decode and prefill for M "rows" at
-// once (batched decode of independent sequences; prompt prefill). A
+// once (benchmark config 5: batched decode of independent sequences; prompt prefill). A
 // row is one token of one sequence at one position; a batched decode step has one row
 // per sequence, a prefill chunk one row per prompt token of a sequence. Per layer:
 //

@@ -1,4 +1,4 @@
-"""Engine-level parity on the GPU: one decoder layer, whole decode
+"""Engine-level parity on the GPU: one decoder layer (benchmark config 2), whole decode
 steps teacher-forced with random tokens, prefill + greedy generation, the .qora file
 path, error behaviour and determinism — all through the C ABI, against the oracle.
 
@@ -40,7 +40,7 @@ def small_oracle(orc, small):
 
 
 def test_layer_config2(pkg, qf, orc):
-    """one SmolLM3 layer at batch 1, KV pre-filled with 512 rows of
+    """benchmark config 2: one SmolLM3 layer at batch 1, KV pre-filled with 512 rows of
     N(0,1), hidden N(0,1), position 512; a RoPE layer (index 3) and a NoPE layer."""
     model = qf.synth_model(seed=2, num_layers=4, vocab=256, rope_rows=1024)
     rng = np.random.default_rng(22)

@@ -1,4 +1,4 @@
-"""F16-weight engines (BASELINE config 5 at test sizes): batched decode of independent
+"""F16-weight engines (benchmark config 5 at test sizes): batched decode of independent
 sequences and chunked prefill, through the C ABI, against the CPU oracle.
 
 Bars: logits within rel-L2 1e-3 of the oracle (measured values are printed; the

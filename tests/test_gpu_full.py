@@ -1,4 +1,4 @@
-"""Full-size parity (BASELINE configs 3 and 4) on the GPU against the oracle: the
+"""Full-size parity (benchmark configs 3 and 4) on the GPU against the oracle: the
 SmolLM3-3B architecture with seeded random-init Q4 weights (36 layers, vocab 128256).
 
 Config 3: 32-token prompt, greedy decode. The GPU generates all 256 tokens; the oracle
@@ -108,7 +108,7 @@ def test_config4_long_context(full_engine, full_oracle, full):
 
 
 def test_config5_full_size_f16_batched(pkg, qf, orc):
-    """BASELINE config 5 at full size: SmolLM3-3B with F16 weights, two sequences decoded
+    """benchmark config 5 at full size: SmolLM3-3B with F16 weights, two sequences decoded
     together on the tcgen05 path. The oracle follows each sequence with forward_decode_raw
     steps (its F16 GEMV on all host threads; the reference's scalar single-thread gemm_f16
     prefill is prohibitive at this size), within a bounded time budget: teacher-forced

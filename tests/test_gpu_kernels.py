@@ -48,7 +48,7 @@ def test_dequant_bit_exact(pkg, qf, orc, torch):
 
 
 def config1(qf):
-    """gate_proj in the reference layout (k=2048 in, n=11008 out),
+    """benchmark config 1: gate_proj in the reference layout (k=2048 in, n=11008 out),
     seed 0, x ~ N(0,1)."""
     rng = np.random.default_rng(0)
     m = qf.synth_q4_matrix(rng, 2048, 11008)
