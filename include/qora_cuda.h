@@ -239,9 +239,13 @@ qora_status qora_q4_gemv(const float* d_x, const uint8_t* d_packed,
  * cudaMalloc would synchronise the device). Shapes whose plan needs more scratch than
  * the array holds are rejected with QORA_ERR_UNSUPPORTED. The first call on a device
  * looks up the array's address (a one-time set-up step; make it before any stream
- * capture). Every call shares the array: the counters start at zero and each call
- * leaves them at zero, so calls must not overlap in time (concurrent calls on
- * different streams of one device race on the shared partials). */
+ * capture). The address is kept for the life of the process: after a cudaDeviceReset
+ * (which unloads the library's device code) the cached address is stale, so do not call
+ * this entry again in that process. Every call shares the array: the counters start at
+ * zero and each call leaves them at zero, so calls must not overlap in time (concurrent
+ * calls on different streams of one device race on the shared partials). A call whose
+ * launch fails puts the counters back to zero before it returns the error; a kernel that
+ * faults mid-way loses the whole CUDA context, and with it every later call. */
 #define QORA_GEMV_STATIC_FLOATS (512u * 1024u)
 #define QORA_GEMV_STATIC_TILES 1024u
 qora_status qora_q4_gemv_static(const float* d_x, const uint8_t* d_packed,

@@ -140,6 +140,9 @@ struct Args {
   // [v0, v1), and every rank's receive buffers (own included), written over NVLink
   int tp, rank, hpk;          // hpk: query heads per local KV head
   int v0, v1;
+  int want_logits;            // tp > 1: assemble the full logits on every rank (else only
+                              // the (value, index) candidates cross NVLink)
+  int pad2;
   uint64_t* peer_o[8];        // tagged o_proj partials [L][tp][H]
   uint64_t* peer_d[8];        // tagged down partials [L][tp][H]
   uint64_t* peer_lm[8];       // tagged lm_head bests [tp][2] (value, index)
@@ -170,6 +173,14 @@ QORA_DEV Args* sm_args() { return reinterpret_cast<Args*>(reinterpret_cast<uint8
 constexpr int kTraceLayers = 64;
 constexpr int kTracePerCta = 2 + 8 * kTraceLayers + 2;
 constexpr int kTraceFine = 64;
+
+// After this long in one bounded wait, the waiter also polls the step's error word, so
+// that a timeout recorded by any CTA (or an earlier launch) stops the whole grid without
+// every dependent CTA running into its own full timeout.
+constexpr unsigned long long kGridCheckNs = 100000ull;
+QORA_DEV bool grid_failed(const Args& a) {
+  return ptx::ld_relaxed(reinterpret_cast<const unsigned*>(&a.st->error)) != 0u;
+}
 
 // ---- counter layout: down arrivals per (layer, output tile), then the final arrival
 QORA_DEV int c_dn_arr(const Args& a, int L, int t) { return L * a.cpl + t; }
@@ -285,9 +296,14 @@ __device__ __noinline__ uint32_t issue(const uint8_t* src, uint32_t bytes, uint3
     const uint64_t t0 = ptx::globaltimer();
     while (!ptx::mbar_try_wait(&empty[s], parity)) {
       if (flags[0] != 0) return kDead;  // consumers gave up: stop issuing
-      if (ptx::globaltimer() - t0 > sm_args()->timeout_ns) {
+      const uint64_t dt = ptx::globaltimer() - t0;
+      if (dt > sm_args()->timeout_ns) {
         flags[0] = 1;
         atomicExch(&sm_args()->st->error, 2);
+        return kDead;
+      }
+      if (dt > kGridCheckNs && grid_failed(*sm_args())) {
+        flags[0] = 1;
         return kDead;
       }
     }
@@ -472,9 +488,14 @@ QORA_DEV bool retry_stop(const Cons& C, uint64_t& t0, int it) {
     return false;
   }
   if (C.aborted()) return true;
-  if (ptx::globaltimer() - t0 > C.ap->timeout_ns) {
+  const uint64_t dt = ptx::globaltimer() - t0;
+  if (dt > C.ap->timeout_ns) {
     C.flags[0] = 1;
     atomicExch(&C.ap->st->error, 2);
+    return true;
+  }
+  if (dt > kGridCheckNs && grid_failed(*C.ap)) {  // another CTA gave up: its code stands
+    C.flags[0] = 1;
     return true;
   }
   return false;
@@ -493,12 +514,15 @@ QORA_DEV void await_tags(const Cons& C, int n, uint32_t tag, Addr&& addr) {
       for (int i = C.lane; i < n; i += 32) mine &= tag_ok(ptx::ld_relaxed_b64(addr(i)), tag);
       if (__all_sync(0xffffffffu, mine)) break;
       int stop = 0;
-      if (C.lane == 0) stop = C.aborted() ? 1 : (ptx::globaltimer() - t0 > C.ap->timeout_ns ? 2 : 0);
+      if (C.lane == 0) {
+        const uint64_t dt = ptx::globaltimer() - t0;
+        stop = C.aborted() ? 1 : dt > C.ap->timeout_ns ? 2 : (dt > kGridCheckNs && grid_failed(*C.ap)) ? 3 : 0;
+      }
       stop = __shfl_sync(0xffffffffu, stop, 0);
       if (stop) {
-        if (stop == 2 && C.lane == 0) {
+        if (stop >= 2 && C.lane == 0) {
           C.flags[0] = 1;
-          atomicExch(&C.ap->st->error, 2);
+          if (stop == 2) atomicExch(&C.ap->st->error, 2);
         }
         break;
       }
@@ -1402,8 +1426,9 @@ __device__ __noinline__ void lm_phase(uint32_t chunk) {
         acc = warp_sum(acc);
         const unsigned vi = (unsigned)(r + i);
         if (lane == 0) {
-          if (a.tp > 1) {  // every rank holds the full logits
-            for (int p = 0; p < a.tp; ++p) a.peer_logits[p][vi] = acc;
+          if (a.tp > 1) {  // every rank holds the full logits, when the caller wants them
+            if (a.want_logits)
+              for (int p = 0; p < a.tp; ++p) a.peer_logits[p][vi] = acc;
           } else {
             a.logits[vi] = acc;
           }
@@ -1440,7 +1465,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_megakernel(const Args args
       ptx::mbar_init(&empty[s], kCW);
     }
     const int pos0 = args.st->pos, tok0 = args.st->token;
-    flags[0] = (tok0 < 0 || tok0 >= args.vocab || pos0 < 0 || pos0 >= args.max_pos) ? 1 : 0;
+    // an error left by an earlier launch of this step sequence (a timeout, a rejected
+    // token) stops this one at once: the host reads the first error after the sequence
+    flags[0] = (tok0 < 0 || tok0 >= args.vocab || pos0 < 0 || pos0 >= args.max_pos || args.st->error != 0) ? 1 : 0;
     flags[1] = 0;
     flags[2] = pos0;
     flags[3] = 0;
@@ -1488,7 +1515,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_megakernel(const Args args
   // ---------------- consumers
   Cons C = make_cons(0);
   C.stamp(0);
-  if (flags[0] && tid == 0) atomicExch(&a.st->error, 1);
+  if (flags[0] && tid == 0) atomicCAS(&a.st->error, 0, 1);  // keep an earlier code (2: timeout)
   const int H = a.H;
   float* sB = scratch + kOffB;  // x copy for the norms
 

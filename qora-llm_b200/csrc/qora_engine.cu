@@ -886,6 +886,7 @@ qora_status mega_prepare(qora_engine* e, qora_kv* kv) {
   a.tp = e->tp;
   a.rank = e->rank;
   a.hpk = e->nh_l / e->nkv_l;
+  a.want_logits = 1;
   a.v0 = (int)((long long)e->rank * e->vocab / e->tp);
   a.v1 = (int)((long long)(e->rank + 1) * e->vocab / e->tp);
   for (int p = 0; p < e->tp && e->tp > 1; ++p) {
@@ -899,7 +900,8 @@ qora_status mega_prepare(qora_engine* e, qora_kv* kv) {
   return QORA_OK;
 }
 
-qora_status launch_mega(qora_engine* e, qora_kv* kv) {
+qora_status launch_mega(qora_engine* e, qora_kv* kv, bool want_logits) {
+  kv->mk_args.want_logits = want_logits ? 1 : 0;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(e->mk_G);
   cfg.blockDim = dim3(mk::kThreads);
@@ -1027,8 +1029,10 @@ qora_status step_prepare(qora_engine* e, qora_kv* kv) {
   return ensure_graph(e, kv);
 }
 
-qora_status step_launch(qora_engine* e, qora_kv* kv) {
-  if (kv_uses_mega(e, kv)) return launch_mega(e, kv);
+// want_logits = false: the caller reads only the argmax of this step (greedy loops, the
+// prompt tokens before the last), so tensor-parallel ranks exchange only their candidates
+qora_status step_launch(qora_engine* e, qora_kv* kv, bool want_logits = true) {
+  if (kv_uses_mega(e, kv)) return launch_mega(e, kv, want_logits);
   QCUDA(cudaGraphLaunch(kv->graph, e->stream));
   return QORA_OK;
 }
@@ -1634,6 +1638,9 @@ struct EntryScratch {
   unsigned* lm_i = nullptr;
   unsigned* lm_c = nullptr;
   int lm_n = 0;
+  float* smp_work = nullptr;  // qora_sample_logits: [vocab] work row and the result slot
+  size_t smp_n = 0;
+  smp::Out* smp_out = nullptr;
 };
 std::mutex g_entry_mu;
 std::map<int, EntryScratch> g_entry;
@@ -2220,7 +2227,7 @@ qora_status qora_prefill(qora_engine* e, qora_kv* kv, const uint32_t* ids, uint3
   QCHECK(set_state(e, kv, (int)len, (int)ids[0], 0));
   for (uint32_t i = 0; i < n; ++i) {
     QCUDA(cudaMemcpyAsync(&kv->st->token, kv->ids + i, 4, cudaMemcpyDeviceToDevice, e->stream));
-    QCHECK(step_launch(e, kv));
+    QCHECK(step_launch(e, kv, i + 1 == n));
   }
   QCUDA(cudaMemcpyAsync(kv->st_host, kv->st, sizeof(StepState), cudaMemcpyDeviceToHost, e->stream));
   if (logits_or_null)
@@ -2247,7 +2254,7 @@ qora_status qora_generate_greedy(qora_engine* e, qora_kv* kv, uint32_t first_tok
   QCUDA(cudaSetDevice(e->device));
   QCHECK(step_prepare(e, kv));
   QCHECK(set_state(e, kv, (int)len, (int)first_token, 0));
-  for (uint32_t i = 0; i < n_tokens; ++i) QCHECK(step_launch(e, kv));
+  for (uint32_t i = 0; i < n_tokens; ++i) QCHECK(step_launch(e, kv, false));
   QCUDA(cudaMemcpyAsync(out_tokens, kv->ring, (size_t)n_tokens * 4, cudaMemcpyDeviceToHost, e->stream));
   QCHECK(check_step_error(e, kv));
   for (auto& l : kv->len) l = len + n_tokens;
@@ -2290,7 +2297,7 @@ qora_status qora_generate_greedy_timed(qora_engine* e, qora_kv* kv, uint32_t fir
   QCUDA(cudaEventCreate(&b));
   cudaEventRecord(a, e->stream);
   for (uint32_t i = 0; i < n_tokens; ++i) {
-    const qora_status ls = step_launch(e, kv);
+    const qora_status ls = step_launch(e, kv, false);
     if (ls != QORA_OK) {
       cudaEventDestroy(a);
       cudaEventDestroy(b);
@@ -2497,8 +2504,12 @@ qora_status qora_q4_gemv_static(const float* d_x, const uint8_t* d_packed, const
   }
   float* partials = static_cast<float*>(base);
   unsigned* counters = reinterpret_cast<unsigned*>(partials + QORA_GEMV_STATIC_FLOATS);
-  return launch_gemv(src, sh, partials, counters, ProPlain{d_x}, EpiStore{d_y, (int)n},
-                     (cudaStream_t)stream);
+  const qora_status ls = launch_gemv(src, sh, partials, counters, ProPlain{d_x}, EpiStore{d_y, (int)n},
+                                     (cudaStream_t)stream);
+  // a launch that failed may have left arrival counts behind (the next call would then
+  // sum stale partials): put the counters of this plan back to zero (no allocation)
+  if (ls != QORA_OK) cudaMemsetAsync(counters, 0, (size_t)sh.tiles * sizeof(unsigned), (cudaStream_t)stream);
+  return ls;
 }
 
 qora_status qora_q4_dequant(const uint8_t* d_packed, const uint16_t* d_scales, uint64_t n,
@@ -2617,22 +2628,26 @@ qora_status qora_sample_logits(const float* d_logits, uint32_t vocab, const uint
   smp::Params sp{};
   QCHECK(sample_params(params, vocab, &sp));
   const cudaStream_t s = (cudaStream_t)stream;
-  float* work = nullptr;
-  smp::Out* out = nullptr;
-  QCUDA(cudaMalloc(&work, (size_t)vocab * 4));
-  const cudaError_t ae = cudaMalloc(&out, sizeof(smp::Out));
-  if (ae != cudaSuccess) {
-    cudaFree(work);
-    return fail(QORA_ERR_OOM, "cudaMalloc: %s", cudaGetErrorString(ae));
+  int dev = 0;
+  QCUDA(cudaGetDevice(&dev));
+  // the work row and result slot are cached per device (grown on demand) and used under
+  // the entry lock until this call's result is back on the host, so calls never share them
+  std::lock_guard<std::mutex> lk(g_entry_mu);
+  EntryScratch& es = g_entry[dev];
+  if (es.smp_n < vocab) {
+    if (es.smp_work) cudaFree(es.smp_work);
+    es.smp_work = nullptr;
+    es.smp_n = 0;
+    QCUDA(cudaMalloc(&es.smp_work, (size_t)vocab * 4));
+    es.smp_n = vocab;
   }
+  if (!es.smp_out) QCUDA(cudaMalloc(&es.smp_out, sizeof(smp::Out)));
   smp::sample_kernel<<<1, smp::kThreads, 0, s>>>(d_logits, (int)vocab, d_history, (int)n_history, sp,
-                                                (unsigned long long)*rng_state, work, out);
+                                                (unsigned long long)*rng_state, es.smp_work, es.smp_out);
   cudaError_t ce = cudaGetLastError();
   smp::Out h{};
-  if (ce == cudaSuccess) ce = cudaMemcpyAsync(&h, out, sizeof(h), cudaMemcpyDeviceToHost, s);
+  if (ce == cudaSuccess) ce = cudaMemcpyAsync(&h, es.smp_out, sizeof(h), cudaMemcpyDeviceToHost, s);
   if (ce == cudaSuccess) ce = cudaStreamSynchronize(s);
-  cudaFree(work);
-  cudaFree(out);
   if (ce != cudaSuccess) return fail(QORA_ERR_CUDA, "sampling: %s", cudaGetErrorString(ce));
   *token_out = h.token;
   *rng_state = h.state;

@@ -4,15 +4,20 @@ region and then only waits to be told to exit; it launches no kernel), rank 0 ru
 process on the same GPU and steps alone. Its persistent kernel waits for rank 1's partial
 sums — words nothing will ever write — until the bounded wait (2 s) runs out, then
 records QORA_ERR_TIMEOUT and returns; the host reads the status, and the context stays
-usable (a plain engine on the same device decodes afterwards)."""
+usable (a plain engine on the same device decodes afterwards). A multi-launch prompt pass
+against the same missing peer reports the timeout after about one wait, not one per
+launch."""
 import multiprocessing as mp
 import queue
+import time
 
+import numpy as np
 import pytest
 
 pytestmark = pytest.mark.gpu
 
 TIMEOUT = 6  # QORA_ERR_TIMEOUT
+DEVICE_WAIT_S = 2.0  # the kernels' bound on one wait
 
 
 def _model(qf):
@@ -52,6 +57,17 @@ def test_missing_tp_peer_times_out_and_context_survives(pkg, qf):
             w0.decode_step(kv, 17)
         assert ei.value.status == TIMEOUT, str(ei.value)
         kv.close()
+        # a prompt pass runs several launches: the first one times out, the ones after it
+        # see the recorded error and stop at once, so the whole call fails within about
+        # one timeout (not one per prompt token) and keeps the timeout code
+        kvp = w0.new_kv(64)
+        t0 = time.monotonic()
+        with pytest.raises(pkg.QoraError) as ei:
+            w0.prefill(kvp, np.arange(1, 13, dtype=np.uint32), want_logits=False)
+        took = time.monotonic() - t0
+        assert ei.value.status == TIMEOUT, str(ei.value)
+        assert took < 3 * DEVICE_WAIT_S, f"prefill took {took:.1f} s to report the timeout"
+        kvp.close()
         w0.close()
         # the device still works: a single-GPU engine decodes and matches itself
         w = pkg.DecodeWeights(model=model, device=0)

@@ -1,5 +1,7 @@
 """qora_q4_gemv_static — the Q4 GEMV whose split-K scratch is the library's fixed
-file-scope device array (no allocation) — against qora_q4_gemv, through the C ABI.
+file-scope device array (no allocation) — against the CPU oracle's gemv_q4 (the
+restatement of the reference's src/gemv.rs:646-675) on benchmark config 1's gate_proj,
+and against qora_q4_gemv, through the C ABI.
 
 The file name sorts last so that the test also runs after every other test of the
 session has used the library; it passes alone in a fresh process as well. Two calls in
@@ -62,6 +64,24 @@ def test_static_scratch_gemv_matches_allocating_gemv(pkg, qf, torch):
             assert np.isfinite(y).all()
             assert rel_l2(y, ref) < TOL, (k, n, rel_l2(y, ref))
         assert np.array_equal(y1, y2)
+
+
+def test_static_scratch_gemv_matches_oracle_config1(pkg, qf, orc, torch):
+    """Config 1 (gate_proj, k=2048 in, n=11008 out, F1 layout, seed 0, x ~ N(0,1)):
+    two calls in a row, each within rel-L2 1e-5 of the oracle and identical to the other."""
+    lib = pkg.engine.lib()
+    k, n = 2048, 11008
+    rng = np.random.default_rng(0)
+    m = qf.synth_q4_matrix(rng, k, n)
+    x = rng.standard_normal(k).astype(np.float32)
+    ref = orc.gemv_q4(x, m)
+    bufs = [_dev(torch, v) for v in (x, m.packed, m.scales.view(np.int16))]
+    y1 = _call(pkg, torch, lib.qora_q4_gemv_static, bufs, k, n)
+    y2 = _call(pkg, torch, lib.qora_q4_gemv_static, bufs, k, n)
+    for y in (y1, y2):
+        assert np.isfinite(y).all()
+        assert rel_l2(y, ref) < TOL, rel_l2(y, ref)
+    assert np.array_equal(y1, y2)
 
 
 def test_static_scratch_rejects_oversized_plans(pkg, torch):
