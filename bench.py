@@ -154,6 +154,14 @@ def cpu_model():
     return None
 
 
+def config3(args, kv_len_mean):
+    """The workload dict both arms print for config 3."""
+    return {"workload": "config 3: SmolLM3-3B Q4 (36 layers, vocab 128256), 32-token prompt, "
+                        "greedy decode at batch 1",
+            "prompt": PROMPT, "kv_len_mean": kv_len_mean, "layers": args.layers,
+            "l2": "inputs larger than L2: 1.73 GB of weights streamed per step"}
+
+
 def run_reference(args, rank):
     if rank != 0:
         return 0
@@ -178,8 +186,7 @@ def run_reference(args, rank):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * dt / args.steps,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded random-init SmolLM3-3B Q4)",
-        "config": {"workload": "config 3: SmolLM3-3B Q4, 32-token prompt, greedy decode, batch 1",
-                   "prompt": PROMPT, "kv_len_start": PROMPT + args.warmup},
+        "config": config3(args, PROMPT + args.warmup + (args.steps - 1) / 2.0 + 1),
         "cpu_baseline": {"value": v, "unit": "tok/s", "cores": threads, "kind": "port",
                          "sample": f"{args.steps} greedy decode steps after a {PROMPT}-token prefill "
                                    f"and {args.warmup} warm-up steps (oracle/ C++ restatement of "
@@ -213,22 +220,31 @@ def run_ours(args, rank, world, local_rank):
     K, W = args.steps, args.warmup
     cap = PROMPT + W + K + 8
 
-    # ---- device-timed greedy decode (value)
-    kv = eng.new_kv(cap)
-    first, _ = eng.prefill(kv, prompt, want_logits=False)
-    toks = eng.generate_greedy(kv, first, W)
-    nxt = int(toks[-1]) if W else first
-    kv_start = len(kv)
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize()
+    # ---- device-timed greedy decode (value): the same K steps (32-token prompt, W warm-up
+    # steps, then K timed greedy steps on a fresh cache) repeated until >= 1 s of timed
+    # decode has passed, so that the clock sampler sees the timed region; each repetition
+    # is the max over ranks, the line reports the median repetition. Every rank runs the
+    # same number of repetitions (fixed from K before timing).
+    reps_n = max(1, min(64, -(-1000 // max(1, int(K * 1.2)))))
+    rep_ms = []
     with ClockSampler(local_rank) as clk:
-        _, ms = eng.generate_greedy_timed(kv, nxt, K)
-    torch.cuda.synchronize()
-    ms_t = torch.tensor([ms], dtype=torch.float64, device="cuda")
-    if dist:
-        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
-    ms = float(ms_t.item())
+        for _ in range(reps_n):
+            kv = eng.new_kv(cap)
+            first, _ = eng.prefill(kv, prompt, want_logits=False)
+            toks = eng.generate_greedy(kv, first, W)
+            nxt = int(toks[-1]) if W else first
+            kv_start = len(kv)
+            if dist:
+                dist.barrier()
+            torch.cuda.synchronize()
+            _, ms = eng.generate_greedy_timed(kv, nxt, K)
+            torch.cuda.synchronize()
+            ms_t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+            if dist:
+                dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+            rep_ms.append(float(ms_t.item()))
+            kv.close()
+    ms = statistics.median(rep_ms)
     value = K / (ms / 1000.0)  # tokens of the one sequence all ranks decode together
 
     # ---- end to end through the C ABI: host token in, host argmax out, every step
@@ -271,7 +287,9 @@ def run_ours(args, rank, world, local_rank):
                 "launches_timed": K}
         achieved = rank_bytes / (ms / K / 1000.0) / 1e9
     else:
+        kv = eng.new_kv(cap)
         kern_ms, kern_bytes, kern_n = eng.time_kernel(kv, "gate_up", reps=5)
+        kv.close()
         kern = {"kernel": "q4 gate/up GEMV (+RMSNorm, SwiGLU)", "bytes_per_launch": kern_bytes,
                 "us_per_launch": kern_ms * 1000, "launches_timed": kern_n}
         achieved = kern_bytes / (kern_ms / 1000.0) / 1e9
@@ -280,12 +298,12 @@ def run_ours(args, rank, world, local_rank):
         "warmup": W, "ms_per_step": ms / K, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded random-init SmolLM3-3B Q4 weights, random prompt ids)",
-        "config": {
-            "workload": "config 3: SmolLM3-3B Q4 (36 layers, vocab 128256), 32-token prompt, "
-                        "greedy decode at batch 1",
-            "prompt": PROMPT, "kv_len_mean": mean_kv, "layers": args.layers,
-            "parallelism": "single GPU" if world == 1 else f"tp{world} (tensor parallel, NVLink peer all-reduce)",
-            "l2": "inputs larger than L2: 1.73 GB of weights streamed per step",
+        # the workload only (the reference arm prints the same dict); run details below
+        "config": config3(args, mean_kv),
+        "parallelism": "single GPU" if world == 1 else f"tp{world} (tensor parallel, NVLink peer all-reduce)",
+        "detail": {
+            "repetitions": f"median of {reps_n} repetitions of the {K} timed steps (fresh cache each)",
+            "repetition_ms": rep_ms,
             "bytes_per_step": step_bytes,
             "step_hbm_GBps": step_bytes * (K / (ms / 1000.0)) / 1e9,
             "step_hbm_frac": step_bytes * (K / (ms / 1000.0)) / 1e9 / peak,
@@ -299,7 +317,6 @@ def run_ours(args, rank, world, local_rank):
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(model, prompt, args.cpu_seconds)
-    kv.close()
     kv2.close()
     eng.close()
     if dist:
@@ -667,14 +684,19 @@ def run_q4_gemv(args, rank, world, local_rank):
             gemv(i, cap)
     graph.replay()  # untimed replay
     stream.synchronize()
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # replay the K-launch graph until >= 1 s has passed (so the clock sampler sees the
+    # timed region), each replay timed with CUDA events; report the median replay
+    reps, t_end = [], time.perf_counter() + 1.0
     with ClockSampler(local_rank) as clk:
-        t0.record(stream)
-        with torch.cuda.stream(stream):
-            graph.replay()
-        t1.record(stream)
-        t1.synchronize()
-    ms = t0.elapsed_time(t1)
+        while len(reps) < 3 or time.perf_counter() < t_end:
+            t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            t0.record(stream)
+            with torch.cuda.stream(stream):
+                graph.replay()
+            t1.record(stream)
+            t1.synchronize()
+            reps.append(t0.elapsed_time(t1))
+    ms = statistics.median(reps)
     value = gemv_bytes() / (ms / K / 1000.0) / 1e9
     # e2e: per step, x from pinned host memory, the GEMV through the C ABI, y back
     hx = torch.from_numpy(x).pin_memory()
@@ -697,7 +719,8 @@ def run_q4_gemv(args, rank, world, local_rank):
         "data": "synthetic (seeded Q4 gate_proj, N(0,1) input)",
         "config": dict(cfg, weight_copies=copies,
                        l2=f"weights rotated over {copies} copies ({copies * gemv_bytes() / 1e6:.0f} MB, > 4x L2)",
-                       timing="K launches in one CUDA graph, CUDA events around the replay"),
+                       timing=f"K launches in one CUDA graph, CUDA events around each replay; median of "
+                              f"{len(reps)} replays over >= 1 s"),
         "e2e": {"value": e2e, "unit": "GB/s", "h2d_bytes_per_step": GEMV_K * 4, "d2h_bytes_per_step": GEMV_N * 4},
         "gpu_launches": K,
         "roofline": dict(bound="hbm", achieved=value, peak=peak, peak_kind=f"{peak_kind} hbm_gbs (copy)",
