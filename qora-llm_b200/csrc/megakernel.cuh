@@ -7,45 +7,45 @@
 // weight byte ranges for the whole step (they do not depend on activations) and copies
 // them with bulk (TMA) copies into a ring of shared-memory stages; the consumer warps
 // walk the same list, waiting for (a) the stage to land and (b) the activation the phase
-// needs, published by other CTAs through gpu-scope release/acquire counters. While
-// consumers wait on a dependency the producer keeps filling the ring.
+// needs, published by other CTAs as tagged words. While consumers wait on a dependency
+// the producer keeps filling the ring.
 //
 // Per layer (CTA sets in brackets):
 //   QKV  [one CTA per 32-column group of q|k|v] RMSNorm(x) . W over all rows -> final
 //        q|k|v values (before RoPE), no split-K
-//   ATTN [one CTA per (kv head, chunk of positions)] RoPE on its 4 query heads (and,
-//        for the chunk holding the new position, on k, which it appends with v to the
-//        head-major cache), scores, softmax numerators, P.V -> (m, l, o); the last unit
-//        of a KV head (atomic arrival count) merges the chunks and publishes the heads'
-//        normalised output (one chunk: the unit publishes o / l itself)
+//   ATTN [one CTA per (kv head, chunk of positions)] RoPE on its query heads (and, for
+//        the chunk holding the new position, on k, which it appends with v to the
+//        head-major cache), scores, softmax numerators, P.V -> (m, l, o); with several
+//        chunks per KV head every unit of the head then merges one slice of the head's
+//        outputs from all chunks' partials (one chunk: the unit publishes o / l itself)
 //   O    [one CTA per 32-column group of o_proj] the merged attention output of all
 //        heads, GEMV over all rows, x_mid = x + o for its columns
 //   GU   [all] RMSNorm(x_mid) . [gate|up], split-K over 256-column tiles -> partials
 //   DOWN [all] SwiGLU of its rows from the gate/up partials, split-K GEMV with every
-//        CTA's rows inside one output tile; the last CTA of a tile (atomic arrival
-//        count) writes x_next = x_mid + down for it
+//        CTA's rows inside one output tile; then each CTA of a tile sums one slice of
+//        the tile's columns over all its split-K partials: x_next = x_mid + down
 // then lm_head rows (a contiguous slice per CTA) with a fused first-maximum argmax.
 //
-// Hand-off between CTAs: every value one CTA passes to another (q|k|v, attention
-// partials, x_mid, gate/up partials, x_next) travels as a 64-bit word (tag << 32 | f32
-// bits) written and read with single-copy-atomic relaxed accesses; the tag names the
-// launch and the layer. A reader first polls one word per producer (warp 0), then loads
-// its values and re-reads any whose tag is not yet the current one. No release fence or
-// counter sits between a producer and its consumers.
+// Hand-off between CTAs: every value one CTA passes to another travels as a 64-bit word
+// (tag << 32 | f32 bits) written and read with single-copy-atomic relaxed accesses; the
+// tag names the launch and the layer. A reader loads its words directly and re-reads
+// (after a short sleep) only those whose tag is not yet the current one: one L2 round
+// trip once the data is there, no separate flag, fence or arrival counter.
 //
 // Instruction-cache discipline: B200's per-SM instruction cache holds ~60 KB of code
-// (measured: straight-line code runs at ~2.7 cycles per instruction up to 61 KB and
-// 4-11 beyond 76 KB), and a layer executes every phase once, so the code of one layer
-// must stay below that. Every phase is a separate non-inlined function taking only
-// scalars (the consumer state is rebuilt in registers; nothing lives in local memory,
-// whose L1 is a few KB next to this kernel's shared memory), all GEMVs share two
-// streaming loops, and non-critical loops are not unrolled. Every dependent global read
-// of a phase is issued as one batch, so a phase costs one L2 round trip, not one per
-// value; counters are polled with relaxed loads and one acquire fence.
+// (a straight-line probe runs at ~2.7 cycles per instruction up to 61 KB and 4-11
+// beyond 76 KB) and every layer executes each phase once, so code a layer runs beyond
+// that is fetched again from L2 every layer (measured: phase prologues of ~150
+// instructions taking 1.3-2 us while each layer ran ~150 KB of code). So the code a
+// layer executes is kept small: one GEMV routine serves all four matrices (the tile
+// width is a runtime parameter), the attention unit and the hand-off helpers exist once,
+// out of line, and only the GEMV's inner loop is unrolled. Nothing of the consumer state
+// lives in local memory.
 //
-// Every wait (dependency counter, stage barrier, ring slot) is bounded by a timeout; on
-// expiry the CTA records QORA_ERR_TIMEOUT in the step state, stops computing, drains the
-// copies it has in flight and exits. No form of multicast is used.
+// Every wait (tagged word, stage barrier, ring slot) is bounded by a timeout; on expiry
+// the CTA records QORA_ERR_TIMEOUT in the step state, stops computing, drains the copies
+// it has in flight and exits; long waits also watch the step's error word, so that one
+// CTA's timeout stops the grid. No form of multicast is used.
 #pragma once
 
 #include "common.cuh"
@@ -69,24 +69,34 @@ constexpr int kMinAttnChunk = 64;
 constexpr int kMaxAttnChunk = 1024;
 constexpr int kMaxUnits = 256;         // attention units (kv head x chunk); units <= CTAs
 constexpr int kHeadsPerKV = 4;         // query heads per KV head (SmolLM3-3B: 16 / 4)
+constexpr int kRowsPerLane = 4;        // GEMV rows per lane per stage (both tile widths)
 // shared scratch (floats): XS = inputs of this CTA's GEMV (pre-scaled by 2^64); B = x
-// copy / cross-warp reduction / merge weights / epilogue parts; Y = a segment's reduced
-// sums; MISC = small reductions and tables; TAB = split-K slots per tile
+// copy / cross-warp reduction / down-tile slice; Y = a segment's reduced sums; MISC =
+// small reductions; TAB = split-K slots per tile; FIN = residual values of the columns
+// this CTA finishes (its o_proj columns, its slice of a down tile)
 constexpr int kXsCap = 2048;
-constexpr int kXsPer = (kXsCap + kCT - 1) / kCT;  // xs entries per thread (5)
 constexpr int kOffB = kXsCap;
 constexpr int kBFloats = kCW * 256;
 constexpr int kOffY = kOffB + kBFloats;
 constexpr int kOffMisc = kOffY + 256;
 constexpr int kOffTab = kOffMisc + 64;
 constexpr int kMaxTabTiles = 128;
-constexpr int kScratchFloats = kOffTab + kMaxTabTiles;
-// attention (overlaps XS and B): q [4][128] | scores [4][kMaxAttnChunk] | (m,l) [4][2] | new k,v
-constexpr int kAttQ = 0, kAttS = 512, kAttML = kAttS + 4 * kMaxAttnChunk, kAttKV = kAttML + 8;
-constexpr int kDnParts = 7;            // down epilogue: partial sums of the slots, [7][64] float4
+constexpr int kOffFin = kOffTab + kMaxTabTiles;
+constexpr int kFinCap = 256;
+constexpr int kOffPlan = kOffFin + kFinCap;  // this CTA's plan for the launch (ints, see make_plan)
+constexpr int kPlanInts = 64;
+constexpr int kScratchFloats = kOffPlan + kPlanInts;
+// attention (overlaps XS and B): q [4][128] | scores [4][kMaxAttnChunk] | (m,l) [4][2] |
+// 1/l [4] | the new position's k and v rows [2][128] in the cache's element type
+constexpr int kAttQ = 0, kAttS = 512, kAttML = kAttS + 4 * kMaxAttnChunk, kAttInv = kAttML + 8, kAttKV = kAttInv + 4;
+// attention merge staging (XS and B, once the unit's own partials are out): the slice's
+// o values [nch][slice], chunk (m, l) [nch][heads][2], weights [heads][nch], 1/l [heads]
+constexpr int kMgO = 0, kMgML = 1024, kMgW = kMgML + 2 * kHeadsPerKV * kMaxUnits, kMgInv = kMgW + kHeadsPerKV * kMaxUnits;
 static_assert(kAttKV + 256 <= kOffY, "attention scratch");
-static_assert(kDnParts * 64 * 4 <= kBFloats && kDnParts * 64 <= kCT, "down epilogue");
+static_assert(kMgO + kHeadsPerKV * kHeadDim + kMaxUnits <= kMgML && kMgInv + kHeadsPerKV <= kOffY, "merge staging");
 constexpr float kTwo64 = 18446744073709551616.0f;
+constexpr int kPairsMax = (kXsCap / 2 + kCT - 1) / kCT;  // tagged word pairs per thread of a vector (3)
+constexpr unsigned kPollSleepNs = 0;  // pause between re-reads of words that are not there yet (0: none)
 
 enum Mat { QKV = 0, OPR = 1, GU = 2, DOWN = 3 };
 
@@ -121,12 +131,12 @@ struct Args {
   uint64_t* qkv;              // tagged [nq + 2 nkvw] this step's q|k|v (before RoPE)
   float* logits;              // [vocab]
   uint64_t* gu_part;          // tagged gate/up split-K partials [tiles][slots][256]
-  float* dn_part;             // down split-K partials [tiles][slots][256]
+  uint64_t* dn_part;          // tagged down split-K partials [tiles][slots][256]
   uint64_t* att_o;            // tagged [kMaxUnits][4][128]
   uint64_t* att_ml;           // tagged [kMaxUnits][4][2]
   uint64_t* att_fin;          // tagged [nh][128] merged attention output of the layer
   unsigned* epoch;            // launches so far (the tag base); advanced by the last CTA
-  unsigned* cnt;              // down arrival counters [L][tiles] + the final arrival, zero between launches
+  unsigned* cnt;              // arrival counters (the step's final one at c_lm), zero between launches
   int cpl;                    // counters per layer
   int n_cnt;
   float* lm_v;                // [gridDim.x]
@@ -162,14 +172,14 @@ QORA_DEV uint64_t* sm_empty() { return sm_full() + kStages; }
 QORA_DEV volatile int* sm_flags() { return reinterpret_cast<volatile int*>(sm_empty() + kStages); }
 QORA_DEV Args* sm_args() { return reinterpret_cast<Args*>(reinterpret_cast<uint8_t*>(sm_empty() + kStages) + 64); }
 // flags: [0] abort, [1] last-arriver, [2] pos, [3] chunks issued, [4] producer done,
-// [5] token, [6] fine-trace counter, [7] current layer, [8] tag base (epoch * 64)
+// [5] token, [6] spare, [7] current layer, [8] tag base (epoch * 64)
 
 // Trace layout: per CTA kTracePerCta u64 globaltimer stamps written by consumer thread 0:
 // [0] start, [1] after embedding, then per layer L at 2 + 8L + {0: x ready (QKV CTAs),
-// 1: QKV done, 2: attention done, 3: attention partials ready (O CTAs), 4: O done,
+// 1: QKV done, 2: attention done, 3: attention output ready (O CTAs), 4: O done,
 // 5: x_mid ready, 6: GU done, 7: DOWN done}, then [2+8*kTraceLayers] lm start, [+1] end.
 // Then, per CTA, one stamp per layer when the producer has issued that layer's last
-// copy; then kTraceFine stamps of layer 1 at finer points (phase steps) per CTA.
+// copy; then kTraceFine spare words per CTA.
 constexpr int kTraceLayers = 64;
 constexpr int kTracePerCta = 2 + 8 * kTraceLayers + 2;
 constexpr int kTraceFine = 64;
@@ -182,34 +192,18 @@ QORA_DEV bool grid_failed(const Args& a) {
   return ptx::ld_relaxed(reinterpret_cast<const unsigned*>(&a.st->error)) != 0u;
 }
 
-// ---- counter layout: down arrivals per (layer, output tile), then the final arrival
-QORA_DEV int c_dn_arr(const Args& a, int L, int t) { return L * a.cpl + t; }
-// attention arrivals per (layer, kv head) after the down counters of the layer
-QORA_DEV int c_att(const Args& a, int L, int g) { return L * a.cpl + a.tiles[DOWN] + g; }
+// the step's final arrival counter (the last CTA to arrive finishes the argmax)
 QORA_DEV int c_lm(const Args& a) { return a.L * a.cpl; }
-
-// Attention units: (kv head, chunk of `chunk` positions), about one unit per CTA.
-// Attention units run on the CTAs from the end of the grid (the q|k|v CTAs) so that the
-// o_proj CTAs at the front keep their o_proj weights queued in the ring behind nothing.
-QORA_DEV int attn_unit_of(int c, int G) { return G - 1 - c; }
-
-QORA_DEV void attn_plan(int len, int G, int nkvh, int& chunk, int& nch) {
-  chunk = (len * nkvh + G - 1) / G;
-  chunk = max(kMinAttnChunk, min(kMaxAttnChunk, chunk));
-  nch = (len + chunk - 1) / chunk;
-}
 
 // ---- split-K geometry (32-bit: the host checks set size x tiles x K < 2^31)
 // CTA lc of a g-CTA set owns rows [lc*T/g, (lc+1)*T/g) of the tiles*K flattened rows
 QORA_DEV int owner32(unsigned p, unsigned total, unsigned g) { return (int)(((p + 1u) * g - 1u) / total); }
 
-struct Span {
-  int lin0, n;
-};
 // Tile-aligned split-K (down_proj): tile t of T runs on CTAs [al_first(t), al_first(t+1))
 // of a g-CTA set (g >= T, so every tile gets floor or ceil of g/T CTAs), and CTA j of
 // the n on tile t owns its rows [j*K/n, (j+1)*K/n). No CTA crosses a tile boundary, so
-// none streams two partial segments or finishes two tiles.
+// none streams two partial segments, and the n CTAs of a tile finish it together (each
+// one slice of its columns).
 // (32-bit: the host checks tiles * g and g * K below 2^31)
 __host__ __device__ inline int al_first(int t, int g, int T) { return (int)((unsigned)(t * g) / (unsigned)T); }
 __host__ __device__ inline int al_tile(int lc, int g, int T) {  // the tile CTA lc works on
@@ -219,10 +213,7 @@ __host__ __device__ inline int al_tile(int lc, int g, int T) {  // the tile CTA 
   return t;
 }
 
-// this CTA's span and first-CTA index of the tile-aligned matrix, computed once per launch
-// (al_span) and kept after the slot table: the phases read two words instead of carrying
-// the tile search
-QORA_DEV int al_slot_words(const Args& a) { return a.tiles[GU] + a.tiles[DOWN]; }
+// CTA lc's span of the tile-aligned matrix: first flattened row, rows, first CTA of its tile
 __host__ __device__ __forceinline__ void al_span(const Args& a, int m, int lc, int* out) {  // out: lin0, n, first CTA of the tile
   const int g = a.subn[m], T = a.tiles[m], K = a.K[m], t = al_tile(lc, g, T);
   const int f0 = al_first(t, g, T), n = al_first(t + 1, g, T) - f0, j = lc - f0;
@@ -230,27 +221,6 @@ __host__ __device__ __forceinline__ void al_span(const Args& a, int m, int lc, i
   out[0] = t * K + r0;
   out[1] = r1 - r0;
   out[2] = f0;
-}
-
-QORA_DEV Span span_of(const Args& a, int m, int c) {
-  const int lc = c - a.sub0[m];
-  const unsigned g = (unsigned)a.subn[m];
-  if (lc < 0 || lc >= (int)g) return Span{0, 0};
-  if (m == DOWN) {  // tile-aligned: the calling CTA's own span (every caller passes blockIdx.x)
-    const int* w = reinterpret_cast<const int*>(sm_scratch() + kOffTab) + al_slot_words(a);
-    return Span{w[0], w[1]};
-  }
-  const unsigned total = (unsigned)a.tiles[m] * (unsigned)a.K[m];
-  const unsigned l0 = (unsigned)lc * total / g, l1 = (unsigned)(lc + 1) * total / g;
-  return Span{(int)l0, (int)(l1 - l0)};
-}
-
-// the set-local index of the first CTA contributing to tile t (for the aligned matrix:
-// the calling CTA's own tile)
-QORA_DEV int slot0(const Args& a, int m, int t) {
-  if (m == DOWN) return reinterpret_cast<const int*>(sm_scratch() + kOffTab)[al_slot_words(a) + 2];
-  const unsigned K = (unsigned)a.K[m], total = (unsigned)a.tiles[m] * K;
-  return owner32((unsigned)t * K, total, (unsigned)a.subn[m]);
 }
 
 QORA_DEV int nslots(const Args& a, int m, int t) {
@@ -261,22 +231,89 @@ QORA_DEV int nslots(const Args& a, int m, int t) {
 
 QORA_DEV int row_bytes(int m) { return m < GU ? 18 : 144; }
 
-// tile pieces of CTA c's span: f(t, r0, r1)
-template <class F>
-QORA_DEV void for_each_seg(const Args& a, int m, int c, F&& f) {
-  const Span sp = span_of(a, m, c);
-  const int K = a.K[m];
-  for (int p = sp.lin0, e = sp.lin0 + sp.n; p < e;) {
-    const int t = p / K, r0 = p - t * K, pe = min(e, (t + 1) * K);
-    f(t, r0, pe - t * K);
+// ---- the CTA's plan for one launch, computed once at kernel start (make_plan) so that
+// no phase, and not the producer, repeats the integer divisions of the split geometry
+// in every layer. Ints in shared memory:
+//   [10 m ..]  matrix m: rows of the span, segments (<= 2), then per segment
+//              (tile, first row, end row, split-K slot)
+//   [40 ..]    attention unit: has a unit, kv head, chunk index, first position, end
+//              position, end of the cached rows (the new position excluded), chunks per
+//              KV head, holds the new position
+//   [48 ..]    its merge slice: first output, end output, first head, heads
+//   [52 ..]    down finish: tile, first column, end column, split-K slots of the tile
+constexpr int kPlMat = 10, kPlAtt = 40, kPlMerge = 48, kPlDown = 52;
+QORA_DEV int* plan_w() { return reinterpret_cast<int*>(sm_scratch() + kOffPlan); }
+QORA_DEV const int* plan() { return reinterpret_cast<const int*>(sm_scratch() + kOffPlan); }
+QORA_DEV const int* mat_plan(int m) { return plan() + kPlMat * m; }
+
+// matrix m's span of CTA c (one thread per matrix, kernel start)
+__device__ __noinline__ void make_mat_plan(const Args& a, int m, int c) {
+  int* P = plan_w() + kPlMat * m;
+  P[0] = P[1] = 0;
+  const int lc = c - a.sub0[m], g = a.subn[m], K = a.K[m];
+  if (lc < 0 || lc >= g) return;
+  if (m == DOWN) {  // tile-aligned: one segment, and this CTA's slice of the tile's columns
+    int sp[3];
+    al_span(a, DOWN, lc, sp);
+    const int t = sp[0] / K, j = lc - sp[2], ns = al_first(t + 1, g, a.tiles[m]) - sp[2];
+    P[0] = sp[1];
+    P[1] = sp[1] > 0 ? 1 : 0;
+    P[2] = t;
+    P[3] = sp[0] - t * K;
+    P[4] = P[3] + sp[1];
+    P[5] = j;
+    int* D = plan_w() + kPlDown;
+    D[0] = t;
+    D[1] = j * kTileCols / ns;
+    D[2] = (j + 1) * kTileCols / ns;
+    D[3] = ns;
+    return;
+  }
+  // CTA lc of the g-CTA set owns rows [lc*T/g, (lc+1)*T/g) of the tiles*K flattened rows
+  const unsigned total = (unsigned)a.tiles[m] * (unsigned)K;
+  const int l0 = (int)((unsigned)lc * total / (unsigned)g), l1 = (int)((unsigned)(lc + 1) * total / (unsigned)g);
+  P[0] = l1 - l0;
+  int ns = 0;
+  for (int p = l0; p < l1 && ns < 2; ++ns) {
+    const int t = p / K, pe = min(l1, (t + 1) * K);
+    P[2 + 4 * ns] = t;
+    P[3 + 4 * ns] = p - t * K;
+    P[4 + 4 * ns] = pe - t * K;
+    P[5 + 4 * ns] = lc - owner32((unsigned)t * (unsigned)K, total, (unsigned)g);
     p = pe;
   }
+  P[1] = ns;
 }
 
-QORA_DEV float4 f4add(float4 a, float4 b) {
-  return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
+// the attention unit of CTA c for a cache of len positions (the new one at len - 1):
+// (kv head, chunk of `chunk` positions), about one unit per CTA, on the CTAs from the end
+// of the grid (the q|k|v CTAs) so that the o_proj CTAs at the front keep their o_proj
+// weights queued in the ring behind nothing
+__device__ __noinline__ void make_att_plan(const Args& a, int c, int G, int pos) {
+  int* P = plan_w() + kPlAtt;
+  P[0] = 0;
+  if (pos < 0 || pos >= a.max_pos) return;  // rejected at kernel start: no unit, no cache write
+  const int len = pos + 1;
+  int csz = (len * a.nkvh + G - 1) / G;
+  csz = max(kMinAttnChunk, min(kMaxAttnChunk, csz));
+  const int nch = (len + csz - 1) / csz, u = G - 1 - c;
+  P[0] = u < a.nkvh * nch ? 1 : 0;
+  if (!P[0]) return;
+  const int g = u % a.nkvh, k = u / a.nkvh, s0 = k * csz, s1 = min(len, s0 + csz);
+  P[1] = g;
+  P[2] = k;
+  P[3] = s0;
+  P[4] = s1;
+  P[5] = min(s1, pos);
+  P[6] = nch;
+  P[7] = pos < s1 ? 1 : 0;
+  int* M = plan_w() + kPlMerge;  // outputs [r0, r1) of the head's hpk * 128
+  const int nout = a.hpk * kHeadDim, r0 = k * nout / nch, r1 = (k + 1) * nout / nch;
+  M[0] = r0;
+  M[1] = r1;
+  M[2] = r0 / kHeadDim;
+  M[3] = (r1 - 1) / kHeadDim + 1 - r0 / kHeadDim;
 }
-QORA_DEV float4 ldcg4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
 
 // ------------------------------------------------------------------ the producer
 // The producer walks exactly this sequence of (source, bytes) copies; the consumers
@@ -319,23 +356,23 @@ __device__ __noinline__ uint32_t produce_gemv(int m, int L, uint32_t chunk) {
   const uint8_t* base = a.layers[L].w[m];
   const int rb = row_bytes(m), rps = kStageBytes / rb;
   const long long K = a.K[m];
-  for_each_seg(a, m, blockIdx.x, [&](int t, int r0, int r1) {
+  const int* P = mat_plan(m);
 #pragma unroll 1
-    for (int r = r0; r < r1; r += rps)
+  for (int sg = 0; sg < P[1]; ++sg) {
+    const int t = P[2 + 4 * sg], r1 = P[4 + 4 * sg];
+#pragma unroll 1
+    for (int r = P[3 + 4 * sg]; r < r1; r += rps)
       chunk = issue(base + ((long long)t * K + r) * rb, (uint32_t)(min(rps, r1 - r) * rb), chunk);
-  });
+  }
   return chunk;
 }
 
 // the cached K rows, then V rows, of this CTA's attention unit (if it has one)
 __device__ __noinline__ uint32_t produce_kv(int L, uint32_t chunk) {
   const Args& a = *sm_args();
-  const int c = blockIdx.x, pos = sm_flags()[2], len = pos + 1;
-  int csz, nch;
-  attn_plan(len, gridDim.x, a.nkvh, csz, nch);
-  const int u = attn_unit_of(c, gridDim.x);
-  if (u >= a.nkvh * nch) return chunk;
-  const int g = u % a.nkvh, s0 = (u / a.nkvh) * csz, sc1 = min(min(len, s0 + csz), pos);
+  const int* P = plan() + kPlAtt;
+  if (!P[0]) return chunk;
+  const int g = P[1], s0 = P[3], sc1 = P[5];
   const int esz = a.kv16 ? 2 : 4, rps = a.kv16 ? kKVRows16 : kKVRows;
 #pragma unroll 1
   for (int kvs = 0; kvs < 2; ++kvs) {
@@ -376,75 +413,60 @@ struct Cons {
   QORA_DEV int ns(int m, int t) const {  // split-K slots of tile t (GU, DOWN)
     return reinterpret_cast<const int*>(scratch + kOffTab)[(m == GU ? 0 : ap->tiles[GU]) + t];
   }
-  // consistent across the consumer warps between named barriers
+  // this thread's view; a decision that gates a barrier goes through bar_or()
   QORA_DEV bool aborted() const { return flags[0] != 0; }
   // uniform within the calling warp at any point
   QORA_DEV bool aborted_w() const { return __shfl_sync(0xffffffffu, flags[0] != 0, 0); }
 
-  QORA_DEV void set_abort(int code) {
-    flags[0] = 1;
-    atomicExch(&ap->st->error, code);
-  }
-
   QORA_DEV void bar() const { ptx::named_bar(kBar, kCT); }
+  // barrier that also tells every consumer thread whether any of them saw an abort
+  QORA_DEV bool bar_aborted() const { return ptx::named_bar_or(kBar, kCT, flags[0] != 0); }
 
   QORA_DEV void stamp(int idx) {
     if (ap->trace && tid == 0) ap->trace[(long long)c * kTracePerCta + idx] = ptx::globaltimer();
   }
 
-  QORA_DEV void fstamp() {  // fine-grained trace stamp of layer 1 (thread 0, tracing enabled)
-    if (tid == 0 && flags[7] == 1 && ap->trace) {
-      const int fine = flags[6];
-      if (fine < kTraceFine)
-        ap->trace[(long long)G * (kTracePerCta + kTraceLayers) + (long long)c * kTraceFine + fine] =
-            ptx::globaltimer();
-      flags[6] = fine + 1;
-    }
-  }
-
   // next stage of the ring (every consumer warp calls this for every chunk, in order).
   // Once the CTA has aborted, stages are skipped without waiting (see drain()).
-  QORA_DEV const uint8_t* acquire_stage() {
-    stage_idx = chunk % kStages;
-    const uint32_t parity = (chunk / kStages) & 1u;
-    if (aborted_w()) {
-      stage_ok = false;
-      return ring;
-    }
-    bool timed_out = false;
-    if (!ptx::mbar_try_wait(&full[stage_idx], parity)) {
-      const uint64_t t0 = ptx::globaltimer();
-      while (!ptx::mbar_try_wait(&full[stage_idx], parity)) {
-        if (ptx::globaltimer() - t0 > ap->timeout_ns) {
-          timed_out = true;
-          break;
-        }
-      }
-    }
-    stage_ok = __all_sync(0xffffffffu, !timed_out);
-    if (!stage_ok && lane == 0) set_abort(2);
-    return ring + (size_t)stage_idx * kStageBytes;
-  }
+  QORA_DEV const uint8_t* acquire_stage();
 
   QORA_DEV void release_stage() {
     __syncwarp();
     if (lane == 0 && stage_ok) ptx::mbar_arrive(&empty[stage_idx]);
     ++chunk;
   }
-
-  // block sum over consumer threads (fixed order), result in every thread
-  QORA_DEV float csum(float v) {
-    float* red = scratch + kOffMisc;
-    v = warp_sum(v);
-    if (lane == 0) red[warp] = v;
-    bar();
-    float t = 0.0f;
-    for (int w = 0; w < kCW; ++w) t += red[w];
-    bar();
-    return t;
-  }
-
 };
+
+// Wait (bounded) for chunk `chunk` to land in its ring slot: true (warp-uniform) once
+// it has, false if the CTA has aborted or the wait timed out (recorded).
+__device__ __noinline__ bool stage_wait(uint32_t chunk) {
+  volatile int* flags = sm_flags();
+  if (__shfl_sync(0xffffffffu, flags[0] != 0, 0)) return false;
+  uint64_t* bar = sm_full() + chunk % kStages;
+  const uint32_t parity = (chunk / kStages) & 1u;
+  bool timed_out = false;
+  if (!ptx::mbar_try_wait(bar, parity)) {
+    const uint64_t t0 = ptx::globaltimer();
+    while (!ptx::mbar_try_wait(bar, parity)) {
+      if (ptx::globaltimer() - t0 > sm_args()->timeout_ns) {
+        timed_out = true;
+        break;
+      }
+    }
+  }
+  const bool ok = __all_sync(0xffffffffu, !timed_out);
+  if (!ok && (threadIdx.x & 31) == 0) {
+    flags[0] = 1;
+    atomicExch(&sm_args()->st->error, 2);
+  }
+  return ok;
+}
+
+QORA_DEV const uint8_t* Cons::acquire_stage() {
+  stage_idx = chunk % kStages;
+  stage_ok = stage_wait(chunk);
+  return ring + (size_t)stage_idx * kStageBytes;
+}
 
 // the consumer view of this CTA, rebuilt in registers by every phase (phases take only
 // scalars: nothing of the consumer state lives in local memory)
@@ -468,10 +490,6 @@ QORA_DEV Cons make_cons(uint32_t chunk) {
   return C;
 }
 
-__device__ __noinline__ float rms_inv_from(float sumsq, int H) {
-  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sumsq, (float)H), 1e-6f)));
-}
-
 // ---- tagged hand-off values: (tag << 32) | f32 bits
 QORA_DEV uint32_t tag_of(const Cons& C, int L) { return (uint32_t)C.flags[8] + (uint32_t)L + 1u; }
 QORA_DEV void st_tagged(uint64_t* p, float v, uint32_t tag) {
@@ -480,138 +498,133 @@ QORA_DEV void st_tagged(uint64_t* p, float v, uint32_t tag) {
 QORA_DEV bool tag_ok(uint64_t w, uint32_t tag) { return (uint32_t)(w >> 32) == tag; }
 QORA_DEV float tag_val(uint64_t w) { return __uint_as_float((uint32_t)w); }
 
-// Retry control for a batch of tagged loads that found a stale tag (the producer's
-// store had not arrived yet): true = give up (abort set, or the CTA already aborted).
-QORA_DEV bool retry_stop(const Cons& C, uint64_t& t0, int it) {
+// Retry control for tagged loads that found a stale tag (the producer's store had not
+// arrived yet), called with it = 0, 1, 2, ... for the failed attempts of one wait:
+// true = give up (this CTA or the grid aborted, or the wait timed out).
+__device__ __noinline__ bool retry_stop(uint64_t& t0, int it) {
+  const Args& a = *sm_args();
+  volatile int* flags = sm_flags();
   if (it == 0) {
     t0 = ptx::globaltimer();
     return false;
   }
-  if (C.aborted()) return true;
+  if (flags[0] != 0) return true;
   const uint64_t dt = ptx::globaltimer() - t0;
-  if (dt > C.ap->timeout_ns) {
-    C.flags[0] = 1;
-    atomicExch(&C.ap->st->error, 2);
+  if (dt > a.timeout_ns) {
+    flags[0] = 1;
+    atomicExch(&a.st->error, 2);
     return true;
   }
-  if (dt > kGridCheckNs && grid_failed(*C.ap)) {  // another CTA gave up: its code stands
-    C.flags[0] = 1;
+  if (dt > kGridCheckNs && grid_failed(a)) {  // another CTA gave up: its code stands
+    flags[0] = 1;
     return true;
   }
+  if (kPollSleepNs) __nanosleep(kPollSleepNs);
   return false;
 }
 
-// Warp 0 polls the sentinel words addr(0..n-1) until each carries `tag` (bounded; abort
-// on timeout), then every consumer thread passes the barrier.
-template <class Addr>
-QORA_DEV void await_tags(const Cons& C, int n, uint32_t tag, Addr&& addr) {
-  if (C.warp == 0 && !C.aborted_w()) {
-    const uint64_t t0 = ptx::globaltimer();
-#pragma unroll 1
-    for (;;) {
-      bool mine = true;
-#pragma unroll 1
-      for (int i = C.lane; i < n; i += 32) mine &= tag_ok(ptx::ld_relaxed_b64(addr(i)), tag);
-      if (__all_sync(0xffffffffu, mine)) break;
-      int stop = 0;
-      if (C.lane == 0) {
-        const uint64_t dt = ptx::globaltimer() - t0;
-        stop = C.aborted() ? 1 : dt > C.ap->timeout_ns ? 2 : (dt > kGridCheckNs && grid_failed(*C.ap)) ? 3 : 0;
-      }
-      stop = __shfl_sync(0xffffffffu, stop, 0);
-      if (stop) {
-        if (stop >= 2 && C.lane == 0) {
-          C.flags[0] = 1;
-          if (stop == 2) atomicExch(&C.ap->st->error, 2);
-        }
-        break;
-      }
-    }
-  }
-  C.bar();
-}
-
-// tagged x (H <= 2048 values) -> sB (shared), returns this thread's sum of squares
-QORA_DEV float load_x(const Cons& C, float* sB, const uint64_t* x, int H, uint32_t tag) {
-  constexpr int kPairs = (2048 / 2 + kCT - 1) / kCT;
-  uint64_t w[kPairs][2];
-  uint64_t t0 = 0;
+// one tagged value, re-read until it carries `tag` (bounded)
+QORA_DEV float ld_checked(const uint64_t* p, uint32_t tag) {
+  uint64_t w, t0 = 0;
 #pragma unroll 1
   for (int it = 0;; ++it) {
-    bool ok = true;
+    w = ptx::ld_relaxed_b64(p);
+    if (tag_ok(w, tag) || retry_stop(t0, it)) break;
+  }
+  return tag_val(w);
+}
+
+// n tagged words (n even, n <= 2 * kPairsMax * kCT) -> dst[i] = value * mul (shared).
+// Each thread loads its own pairs and re-reads only the stale ones until every word
+// carries `tag` (bounded). The caller's barrier publishes dst. Returns the sum of squares
+// of this thread's values (before `mul`), accumulated in a fixed order.
+__device__ __noinline__ float poll_vec(const uint64_t* src, int n, uint32_t tag, float* dst, float mul) {
+  const int tid = threadIdx.x, np = n >> 1;
+  uint32_t todo = 0;
 #pragma unroll
-    for (int j = 0; j < kPairs; ++j) {
-      const int b = C.tid + j * kCT;
-      if (b < H / 2) {
-        ptx::ld_relaxed_v2_b64(x + 2 * b, w[j][0], w[j][1]);
-        ok &= tag_ok(w[j][0], tag) & tag_ok(w[j][1], tag);
+  for (int j = 0; j < kPairsMax; ++j)
+    if (tid + j * kCT < np) todo |= 1u << j;
+  uint64_t t0 = 0;
+  float v[kPairsMax][2];
+#pragma unroll 1
+  for (int it = 0; todo != 0u; ++it) {
+    uint64_t w[kPairsMax][2];
+#pragma unroll
+    for (int j = 0; j < kPairsMax; ++j)
+      if (todo & (1u << j)) ptx::ld_relaxed_v2_b64(src + 2 * (tid + j * kCT), w[j][0], w[j][1]);
+#pragma unroll
+    for (int j = 0; j < kPairsMax; ++j)
+      if ((todo & (1u << j)) && tag_ok(w[j][0], tag) && tag_ok(w[j][1], tag)) {
+        v[j][0] = tag_val(w[j][0]);
+        v[j][1] = tag_val(w[j][1]);
+        todo &= ~(1u << j);
       }
-    }
-    if (ok || retry_stop(C, t0, it)) break;
+    if (todo != 0u && retry_stop(t0, it)) break;
   }
   float ss = 0.0f;
 #pragma unroll
-  for (int j = 0; j < kPairs; ++j) {
-    const int b = C.tid + j * kCT;
-    if (b < H / 2) {
-      const float v0 = tag_val(w[j][0]), v1 = tag_val(w[j][1]);
-      sB[2 * b] = v0;
-      sB[2 * b + 1] = v1;
-      ss = __fmaf_rn(v0, v0, ss);
-      ss = __fmaf_rn(v1, v1, ss);
+  for (int j = 0; j < kPairsMax; ++j) {
+    const int b = tid + j * kCT;
+    if (b < np && !(todo & (1u << j))) {
+      dst[2 * b] = __fmul_rn(v[j][0], mul);
+      dst[2 * b + 1] = __fmul_rn(v[j][1], mul);
+      ss = __fmaf_rn(v[j][0], v[j][0], ss);
+      ss = __fmaf_rn(v[j][1], v[j][1], ss);
     }
   }
   return ss;
 }
 
-// one tagged value, re-read until it carries `tag` (bounded)
-QORA_DEV float ld_checked(const Cons& C, const uint64_t* p, uint32_t tag) {
-  uint64_t w, t0 = 0;
+// block sum over consumer threads (fixed order), result in every thread
+__device__ __noinline__ float csum(float v) {
+  float* red = sm_scratch() + kOffMisc;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = warp_sum(v);
+  if (lane == 0) red[warp] = v;
+  ptx::named_bar(kBar, kCT);
+  float t = 0.0f;
+  for (int w = 0; w < kCW; ++w) t += red[w];
+  ptx::named_bar(kBar, kCT);
+  return t;
+}
+
+__device__ __noinline__ float rms_inv_from(float sumsq, int H) {
+  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sumsq, (float)H), 1e-6f)));
+}
+
+// Input row of entry i of matrix m's span (its segments' rows back to back)
+QORA_DEV int span_row(const int* P, int i) {
+  const int n0 = P[4] - P[3];
+  return i < n0 ? P[3] + i : P[7] + (i - n0);
+}
+// Norm gains gamma[row] of matrix m's span copied into xs asynchronously: issued before
+// the wait for the activations, used after it.
+__device__ __noinline__ void stage_gains(const float* gamma, int m) {
+  float* xs = sm_scratch();
+  const int* P = mat_plan(m);
 #pragma unroll 1
-  for (int it = 0;; ++it) {
-    w = ptx::ld_relaxed_b64(p);
-    if (tag_ok(w, tag) || retry_stop(C, t0, it)) break;
-  }
-  return tag_val(w);
+  for (int i = threadIdx.x; i < P[0]; i += kCT) ptx::cp_async_4(xs + i, gamma + span_row(P, i));
 }
-
-// Rows of this thread's xs entries i = tid + j*kCT of a span: (lin0 + i) mod K, stepped
-// without a division when kCT < K (every matrix of the full-size model).
-QORA_DEV int row_next(int r, int K) {
-  r += kCT;
-  if (r >= K) r -= K;
-  return r >= K ? r % K : r;
-}
-
-QORA_DEV void prefetch_gains(const Cons& C, const float* g, Span sp, int K, float (&gam)[kXsPer]) {
-  int r = (sp.lin0 + C.tid) % K;
-#pragma unroll
-  for (int j = 0; j < kXsPer; ++j, r = row_next(r, K)) gam[j] = (C.tid + j * kCT < sp.n) ? __ldg(g + r) : 0.0f;
-}
-
-// xs[i] = x[row] * inv * gamma[row] * 2^64 for the span's rows (gains prefetched)
-QORA_DEV void fill_norm_inputs(const Cons& C, const float* sB, float inv, const float (&gam)[kXsPer], Span sp,
-                               int K) {
-  float* xs = C.scratch;
-  int r = (sp.lin0 + C.tid) % K;
-#pragma unroll
-  for (int j = 0; j < kXsPer; ++j, r = row_next(r, K)) {
-    const int i = C.tid + j * kCT;
-    if (i < sp.n) xs[i] = __fmul_rn(__fmul_rn(sB[r], inv), gam[j]) * kTwo64;
-  }
+// xs[i] = x[row] * inv * gamma[row] * 2^64 (gamma from stage_gains, this thread's own
+// copies)
+__device__ __noinline__ void fill_norm_inputs(const float* x, float inv, int m) {
+  float* xs = sm_scratch();
+  const int* P = mat_plan(m);
+  ptx::cp_async_wait_all();
+#pragma unroll 1
+  for (int i = threadIdx.x; i < P[0]; i += kCT) xs[i] = __fmul_rn(__fmul_rn(x[span_row(P, i)], inv), xs[i]) * kTwo64;
 }
 
 // Tensor parallelism: this rank's partial value v of column `col` goes to every rank's
 // receive buffer bufs[p][(L*tp + rank)*H + col]; the sum over ranks (rank order, the same
 // on every rank) comes back once all tp partials of the column have arrived (bounded).
-QORA_DEV void tp_push(const Cons& C, uint64_t* const* bufs, int L, int col, float v, uint32_t tag) {
-  const Args& a = C.a();
+QORA_DEV void tp_push(const Args& a, uint64_t* const* bufs, int L, int col, float v, uint32_t tag) {
   const long long o = ((long long)L * a.tp + a.rank) * a.H + col;
   const uint64_t w = ((uint64_t)tag << 32) | __float_as_uint(v);
   for (int p = 0; p < a.tp; ++p) ptx::st_relaxed_sys_b64(bufs[p] + o, w);
 }
-QORA_DEV float tp_sum(const Cons& C, const uint64_t* own, int L, int col, uint32_t tag) {
-  const Args& a = C.a();
+__device__ __noinline__ float tp_sum(const uint64_t* own, int L, int col, uint32_t tag) {
+  const Args& a = *sm_args();
   const uint64_t* q = own + (long long)L * a.tp * a.H + col;
   float s = 0.0f;
   uint64_t t0 = 0;
@@ -625,39 +638,73 @@ QORA_DEV float tp_sum(const Cons& C, const uint64_t* own, int L, int col, uint32
       ok &= tag_ok(w, tag);
       s = __fadd_rn(s, tag_val(w));
     }
-    if (ok || retry_stop(C, t0, it)) break;
+    if (ok || retry_stop(t0, it)) break;
   }
   return s;
 }
 
-// ------------------------------------------------------------------ phases
-__device__ __noinline__ void seg_store(int m, int L, int t, int slot);
-__device__ __noinline__ void gemv_finish(int m, int L, int t);
+// ------------------------------------------------------------------ the GEMV
+// A finished segment's sums (Y) go out tagged: q|k|v values; x_mid = x + o for o_proj
+// columns (residual values from FIN); gate/up and down split-K partials.
+__device__ __noinline__ void seg_store(int m, int L, int t, int slot) {
+  const Cons C = make_cons(0);
+  const Args& a = C.a();
+  const float* y = C.scratch + kOffY;
+  const uint32_t tag = tag_of(C, L);
+  if (m == QKV) {
+    if (C.tid < kGroup) st_tagged(a.qkv + t * kGroup + C.tid, y[C.tid], tag);
+  } else if (m == OPR) {
+    if (C.tid < kGroup) {
+      const int col = t * kGroup + C.tid;
+      float o = y[C.tid];
+      if (a.tp > 1) {  // row-split o_proj: sum the ranks' partials of this column
+        tp_push(a, a.peer_o, L, col, o, tag);
+        o = tp_sum(a.peer_o[a.rank], L, col, tag);
+      }
+      st_tagged(a.xmid + (long long)L * a.H + col, __fadd_rn(C.scratch[kOffFin + C.tid], o), tag);
+    }
+  } else if (C.tid < kTileCols) {
+    const long long o = ((long long)t * a.slots[m] + slot) * kTileCols + C.tid;
+    st_tagged((m == GU ? a.gu_part : a.dn_part) + o, y[C.tid], tag);
+  }
+}
 
-// Stream this CTA's segments of matrix m (TG groups per tile) through the ring and
-// reduce each segment's 32*TG sums into Y, then store and publish them. xs holds the (pre-scaled)
-// inputs of all segments back to back. Lane (sub, gi) takes group gi of rows sub and
-// sub + 15*(32/TG) of each warp's share of a stage.
-template <int TG>
-__device__ __noinline__ uint32_t gemv_stream(int m, int L, uint32_t chunk) {
-  constexpr int W = 32 / TG;        // rows per warp pass
-  constexpr int RPS = kStageBytes / (18 * TG);  // rows per stage
-  constexpr int NP = RPS / (kCW * W);            // rows per lane per stage
-  static_assert(TG == 1 || TG == 8, "tile width");
-  static_assert(NP * kCW * W == RPS, "stage rows");
+// Stream this CTA's segments of matrix m through the ring, reduce each segment's sums
+// into Y and store them (seg_store). Eight-group tiles (gate/up, down; T8): lane (sub,
+// gi) takes group gi of 4 rows per warp pass; one-group tiles (q|k|v, o_proj): lane i
+// takes row i of 32 per warp pass. Both read one 16-byte chunk of a 144-byte block per
+// row and give every lane kRowsPerLane rows per stage; xs holds the (pre-scaled) inputs
+// of all segments back to back. The tile width is a template parameter: the inner loop
+// is bound by the ALU pipe (the nibble masks), and index arithmetic that depends on a
+// runtime width measured 7 % of the whole step.
+template <bool T8>
+__device__ __noinline__ uint32_t gemv_run(int m, int L, uint32_t chunk) {
   Cons C = make_cons(chunk);
   const Args& a = C.a();
+  constexpr bool t8 = T8;
+  const int W = t8 ? 4 : 32;                       // rows per warp pass
+  const int RPS = kStageBytes / (t8 ? 144 : 18);    // rows per stage (240 | 1920)
+  const int NO = t8 ? kTileCols : kGroup;          // outputs per segment
+  const int gi = t8 ? (C.lane & 7) : 0, sub = t8 ? (C.lane >> 3) : C.lane;
   const float* xs = C.scratch;
   float* red = C.scratch + kOffB;
   float* y = C.scratch + kOffY;
-  const int gi = C.lane % TG, sub = C.lane / TG;
-  const Span sp = span_of(a, m, C.c);
-  const int K = a.K[m], lc = C.c - a.sub0[m];
+  const int* P = mat_plan(m);
+  // this lane's rows of a stage (i = warp*W + sub + k*kCW*W, always inside the stage)
+  // and the byte offsets of their 16-byte chunks, the same for every stage
+  int row[kRowsPerLane], boff[kRowsPerLane], soff[kRowsPerLane];
+#pragma unroll
+  for (int k = 0; k < kRowsPerLane; ++k) {
+    row[k] = C.warp * W + sub + k * kCW * W;
+    const int blk = (t8 ? row[k] : (row[k] >> 3)) * 144, q = t8 ? gi : (row[k] & 7);
+    boff[k] = blk + q * 16;
+    soff[k] = blk + 128 + q * 2;
+  }
+  const int base = C.warp * W;
   int off = 0;
 #pragma unroll 1
-  for (int p = sp.lin0, e = sp.lin0 + sp.n; p < e;) {
-    const int t = p / K, r0 = p - t * K, r1 = min(e, (t + 1) * K) - t * K;
-    const int slot = lc - slot0(a, m, t);
+  for (int sg = 0; sg < P[1]; ++sg) {
+    const int r0 = P[3 + 4 * sg], r1 = P[4 + 4 * sg];
     float2 acc[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) acc[i] = make_float2(0.0f, 0.0f);
@@ -667,27 +714,20 @@ __device__ __noinline__ uint32_t gemv_stream(int m, int L, uint32_t chunk) {
       const uint8_t* stg = C.acquire_stage();
       const int R = min(RPS, r1 - cr);
       if (C.stage_ok) {
-        // NP rows per lane, all loads issued before the math; 144-byte blocks: TG == 8
-        // one row of 8 groups, TG == 1 eight rows of one group
         const float* xr = xs + off + (cr - r0);
-        uint4 w[NP];
-        float cf[NP];
+        uint4 w[kRowsPerLane];
+        float cf[kRowsPerLane];
 #pragma unroll
-        for (int k = 0; k < NP; ++k) {
-          const int i = C.warp * W + sub + k * kCW * W;
-          const bool ok = i < R;
-          const int j = ok ? i : 0;
-          const uint8_t* blk = stg + (TG == 8 ? j : j >> 3) * 144;
-          const int q = TG == 8 ? gi : (j & 7);
-          w[k] = *reinterpret_cast<const uint4*>(blk + q * 16);
-          const uint16_t sv = *reinterpret_cast<const uint16_t*>(blk + 128 + q * 2);
-          cf[k] = ok ? __half2float(__ushort_as_half(sv)) * xr[j] : 0.0f;
+        for (int k = 0; k < kRowsPerLane; ++k) {  // all loads issued before the math
+          // rows past R of a partial stage read stale stage bytes and get a zero factor
+          w[k] = *reinterpret_cast<const uint4*>(stg + boff[k]);
+          const uint16_t sv = *reinterpret_cast<const uint16_t*>(stg + soff[k]);
+          const float xv = xr[row[k]];
+          cf[k] = row[k] < R ? __half2float(__ushort_as_half(sv)) * xv : 0.0f;
         }
-        // passes whose rows all lie past the stage's end are skipped (warp-uniform)
-        const int base = C.warp * W;
 #pragma unroll
-        for (int k = 0; k < NP; ++k) {
-          if (base + k * kCW * W < R) {
+        for (int k = 0; k < kRowsPerLane; ++k) {
+          if (base + k * kCW * W < R) {  // passes past the stage's end are skipped (warp-uniform)
             cs += cf[k];
             q4_fma_chunk(w[k], cf[k], acc);
           }
@@ -697,8 +737,9 @@ __device__ __noinline__ uint32_t gemv_stream(int m, int L, uint32_t chunk) {
     }
     off += r1 - r0;
 
-    // this lane's 32 outputs, then a transposing reduction over the W lanes of each
-    // group (masks 16 .. TG): afterwards lane (sub, gi) holds outputs sub*TG + [0, TG)
+    // this lane's 32 outputs, then a transposing reduction over the lanes holding the
+    // same outputs (masks 16, 8; one-group tiles also 4, 2, 1): afterwards lane (sub, gi)
+    // holds outputs sub*8 + [0, 8) of group gi (eight-group) or output `lane` (one-group)
     const float bias = cs * 4.3368086899420177e-19f;  // 8 * 2^-64
     float v[32];
 #pragma unroll
@@ -707,7 +748,7 @@ __device__ __noinline__ uint32_t gemv_stream(int m, int L, uint32_t chunk) {
       v[2 * i + 1] = __fmaf_rn(acc[i].y, q4_scale_of_pos((2 * i + 1) & 7), -bias);
     }
 #pragma unroll
-    for (int msk = 16; msk >= TG; msk >>= 1) {
+    for (int msk = 16; msk >= (t8 ? 8 : 1); msk >>= 1) {
       const bool hi = (C.lane & msk) != 0;
 #pragma unroll
       for (int e2 = 0; e2 < msk; ++e2) {
@@ -716,585 +757,110 @@ __device__ __noinline__ uint32_t gemv_stream(int m, int L, uint32_t chunk) {
         v[e2] = keep + __shfl_xor_sync(0xffffffffu, send, msk);
       }
     }
-    float* dst = red + C.warp * (32 * TG) + gi * 32 + sub * TG;
+    {  // eight-group: 8 outputs per lane at [warp][gi*32 + sub*8]; one-group: 1 at [warp][lane]
+      float* dst = red + C.warp * NO + (t8 ? gi * 32 + sub * 8 : C.lane);
 #pragma unroll
-    for (int e2 = 0; e2 < TG; ++e2) dst[e2] = v[e2];
+      for (int e2 = 0; e2 < (t8 ? 8 : 1); ++e2) dst[e2] = v[e2];
+    }
     C.bar();
-    if (C.tid < 32 * TG) {
+    if (C.tid < NO) {
       float s = 0.0f;
-#pragma unroll
-      for (int w = 0; w < kCW; ++w) s += red[w * 32 * TG + C.tid];
+#pragma unroll 1
+      for (int w = 0; w < kCW; ++w) s += red[w * NO + C.tid];
       y[C.tid] = s;
     }
     C.bar();
-    C.fstamp();
-    seg_store(m, L, t, slot);
-    gemv_finish(m, L, t);
-    C.fstamp();
-    p += r1 - r0;
+    seg_store(m, L, P[2 + 4 * sg], P[5 + 4 * sg]);
   }
   return C.chunk;
 }
 
-// A finished segment's sums (Y): q|k|v and o_proj results are final (one group per
-// CTA) and go out tagged; gate/up partials go out tagged; down partials are plain
-// floats, published by the arrival count in gemv_finish.
-__device__ __noinline__ void seg_store(int m, int L, int t, int slot) {
-  Cons C = make_cons(0);
-  const Args& a = C.a();
-  const float* y = C.scratch + kOffY;
-  const uint32_t tag = tag_of(C, L);
-  if (m == QKV) {
-    if (C.tid < 32) st_tagged(a.qkv + t * 32 + C.tid, y[C.tid], tag);
-  } else if (m == OPR) {
-    if (C.tid < 32) {
-      const long long col = (long long)L * a.H + t * 32 + C.tid;
-      float o = y[C.tid];
-      if (a.tp > 1) {  // row-split o_proj: sum the ranks' partials of this column
-        tp_push(C, a.peer_o, L, t * 32 + C.tid, o, tag);
-        o = tp_sum(C, a.peer_o[a.rank], L, t * 32 + C.tid, tag);
-      }
-      st_tagged(a.xmid + col, __fadd_rn(ld_checked(C, a.xbuf + col, tag), o), tag);
-    }
-  } else if (C.tid < 256) {
-    const long long o = ((long long)t * a.slots[m] + slot) * 256 + C.tid;
-    if (m == GU) st_tagged(a.gu_part + o, y[C.tid], tag);
-    else __stcg(a.dn_part + o, y[C.tid]);
-  }
-}
-
-// Down: count this segment's arrival at tile t; the last arriver writes the tile's next
-// residual x_{L+1} = x_mid + (down partials summed over the slots).
-__device__ __noinline__ void gemv_finish(int m, int L, int t) {
-  if (m != DOWN) return;
-  Cons C = make_cons(0);
-  const Args& a = C.a();
-  const int H = a.H;
-  C.bar();
-  if (C.tid == 0) {
-    const unsigned prev = ptx::atom_add_acqrel(a.cnt + c_dn_arr(a, L, t), 1u);
-    C.flags[1] = (prev == (unsigned)(C.ns(DOWN, t) - 1));
-  }
-  C.bar();
-  if (C.flags[1]) {
-    const uint32_t tag = tag_of(C, L);
-    float4* parts = reinterpret_cast<float4*>(C.scratch + kOffB);  // [kDnParts][64]
-    const int b = C.tid & 63, p = C.tid >> 6;
-    const long long col = (long long)L * H + t * 256 + 4 * b;
-    uint64_t xw[4] = {0, 0, 0, 0};
-    if (C.tid < 64) {
-      uint64_t t0 = 0;
-#pragma unroll 1
-      for (int it = 0;; ++it) {
-        ptx::ld_relaxed_v2_b64(a.xmid + col, xw[0], xw[1]);
-        ptx::ld_relaxed_v2_b64(a.xmid + col + 2, xw[2], xw[3]);
-        const bool ok = tag_ok(xw[0], tag) & tag_ok(xw[1], tag) & tag_ok(xw[2], tag) & tag_ok(xw[3], tag);
-        if (ok || retry_stop(C, t0, it)) break;
-      }
-    }
-    if (p < kDnParts) {
-      const int ns = C.ns(DOWN, t);
-      const float* pd = a.dn_part + (long long)t * a.slots[DOWN] * 256 + 4 * b;
-      float4 s = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-#pragma unroll 1
-      for (int k0 = p; k0 < ns; k0 += 4 * kDnParts) {
-        float4 v[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) v[j] = (k0 + j * kDnParts < ns) ? ldcg4(pd + (k0 + j * kDnParts) * 256) : s;
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          if (k0 + j * kDnParts < ns) s = f4add(s, v[j]);
-      }
-      parts[p * 64 + b] = s;
-    }
-    C.bar();
-    if (C.tid < 64) {
-      float4 d = parts[b];
-#pragma unroll 1
-      for (int q = 1; q < kDnParts; ++q) d = f4add(d, parts[q * 64 + b]);
-      float dv[4] = {d.x, d.y, d.z, d.w};
-      if (a.tp > 1) {  // row-split down: sum the ranks' partials of these columns
-        const int c0 = t * 256 + 4 * b;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) tp_push(C, a.peer_d, L, c0 + j, dv[j], tag);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) dv[j] = tp_sum(C, a.peer_d[a.rank], L, c0 + j, tag);
-      }
-      const uint32_t tn = tag + 1u;  // x_{L+1} carries layer L+1's tag
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        st_tagged(a.xbuf + col + H + j, __fadd_rn(tag_val(xw[j]), dv[j]), tn);
-    }
-  }
-  C.bar();
-}
-
+// ------------------------------------------------------------------ phases
 // QKV: RMSNorm(x) . W for this CTA's 32-column group, all rows
 __device__ __noinline__ uint32_t qkv_phase(int L, uint32_t chunk) {
   Cons C = make_cons(chunk);
   const Args& a = C.a();
-  const Span sp = span_of(a, QKV, C.c);
-  if (sp.n == 0) return chunk;
+  if (mat_plan(QKV)[0] == 0) return chunk;
   const int H = a.H;
   float* sB = C.scratch + kOffB;
-  float gam[kXsPer];
-  prefetch_gains(C, a.layers[L].g_in, sp, H, gam);
+  stage_gains(a.layers[L].g_in, QKV);
   float ss = 0.0f;
   if (L > 0) {
-    const uint32_t tag = tag_of(C, L);
-    const uint64_t* x = a.xbuf + (long long)L * H;
-    await_tags(C, a.tiles[DOWN], tag, [&](int i) { return x + i * 256; });  // one word per down tile
-    ss = load_x(C, sB, x, H, tag);
-  } else {
+    ss = poll_vec(a.xbuf + (long long)L * H, H, tag_of(C, L), sB, 1.0f);
+  } else {  // x_0 (the embedding row) is already in sB
 #pragma unroll 1
     for (int i = C.tid; i < H; i += kCT) ss = __fmaf_rn(sB[i], sB[i], ss);
   }
+  C.bar();
   C.stamp(2 + 8 * min(L, kTraceLayers - 1) + 0);
-  const float inv = rms_inv_from(C.csum(ss), H);
-  fill_norm_inputs(C, sB, inv, gam, sp, H);
+  const float inv = rms_inv_from(csum(ss), H);
+  fill_norm_inputs(sB, inv, QKV);
   C.bar();
-  C.fstamp();
-  return gemv_stream<1>(QKV, L, C.chunk);
+  return gemv_run<false>(QKV, L, C.chunk);
 }
 
-// 4 query heads . one K row (8 lanes per row, 16 dims each); lane li == 0 writes
-QORA_DEV void kscore(const float* sq, const float* krow, float* sc, int idx, bool valid, int li) {
-  float d[kHeadsPerKV] = {0.0f, 0.0f, 0.0f, 0.0f};
-  if (valid) {
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float4 k4 = reinterpret_cast<const float4*>(krow + li * 16)[j];
-#pragma unroll
-      for (int h = 0; h < kHeadsPerKV; ++h) {
-        const float4 q4 = reinterpret_cast<const float4*>(sq + h * kHeadDim + li * 16)[j];
-        d[h] = __fmaf_rn(q4.x, k4.x, d[h]);
-        d[h] = __fmaf_rn(q4.y, k4.y, d[h]);
-        d[h] = __fmaf_rn(q4.z, k4.z, d[h]);
-        d[h] = __fmaf_rn(q4.w, k4.w, d[h]);
-      }
-    }
-  }
-  const float scale = 0.08838834764831845f;  // 1/sqrt(128): the f32 quotient of 1 and f32 sqrt(128)
-#pragma unroll
-  for (int h = 0; h < kHeadsPerKV; ++h) {
-    float v = d[h];
-    v += __shfl_xor_sync(0xffffffffu, v, 1);
-    v += __shfl_xor_sync(0xffffffffu, v, 2);
-    v += __shfl_xor_sync(0xffffffffu, v, 4);
-    if (valid && li == 0) sc[h * kMaxAttnChunk + idx] = __fmul_rn(v, scale);
-  }
-}
-
-// Attention merge, run by the last of the nch units of KV head g to arrive (acq_rel
-// arrival count): per query head, M = max_ch m, w_ch = exp(m_ch - M), l = sum_ch l_ch w_ch,
-// out = (sum_ch o_ch w_ch, chunk order) * (1 / l), published tagged for o_proj.
-__device__ __noinline__ void attn_merge(int L, int g, int nch) {
-  Cons C = make_cons(0);
-  const Args& a = C.a();
-  const int hpk = a.hpk, nkvh = a.nkvh;
-  C.bar();  // every partial of this unit is stored
-  if (C.tid == 0) {
-    const unsigned prev = ptx::atom_add_acqrel(a.cnt + c_att(a, L, g), 1u);
-    C.flags[1] = (prev == (unsigned)(nch - 1));
-  }
-  C.bar();
-  if (!C.flags[1] || C.aborted()) return;
-  const uint32_t tag = tag_of(C, L);
-  float* mw = C.scratch + kOffB;            // [hpk][nch] chunk weights
-  float* invl = mw + kHeadsPerKV * nch;     // [hpk]
-  const long long ustride = (long long)nkvh * kHeadsPerKV * 2;         // (m, l): next chunk, same head
-  const long long ostride = (long long)nkvh * kHeadsPerKV * kHeadDim;  // o: next chunk, same head
-  if (C.warp < hpk) {  // one warp per query head, lane = chunk
-    const int h = C.warp;
-    const uint64_t* ml = a.att_ml + ((long long)g * kHeadsPerKV + h) * 2;
-    float mx = -INFINITY;
-#pragma unroll 1
-    for (int ch = C.lane; ch < nch; ch += 32) mx = fmaxf(mx, ld_checked(C, ml + ch * ustride, tag));
-    mx = warp_max(mx);
-    float l = 0.0f;
-    if (C.lane < nch) {
-      const float w = expf(ld_checked(C, ml + C.lane * ustride, tag) - mx);
-      mw[h * nch + C.lane] = w;
-      l = __fmul_rn(ld_checked(C, ml + C.lane * ustride + 1, tag), w);
-    }
-#pragma unroll 1
-    for (int ch = C.lane + 32; ch < nch; ch += 32) {
-      const float w = expf(ld_checked(C, ml + ch * ustride, tag) - mx);
-      mw[h * nch + ch] = w;
-      l = __fmaf_rn(ld_checked(C, ml + ch * ustride + 1, tag), w, l);
-    }
-    l = warp_sum(l);
-    if (C.lane == 0) invl[h] = __fdiv_rn(1.0f, l);
-  }
-  C.bar();
-  const uint64_t* o0 = a.att_o + (long long)g * kHeadsPerKV * kHeadDim;
-#pragma unroll 1
-  for (int r = C.tid; r < hpk * kHeadDim; r += kCT) {
-    const int h = r / kHeadDim;
-    float acc = 0.0f;
-#pragma unroll 1
-    for (int c0 = 0; c0 < nch; c0 += 4) {  // four chunks' values in flight
-      uint64_t v[4], t0 = 0;
-#pragma unroll 1
-      for (int it = 0;; ++it) {
-        bool ok = true;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const bool in = c0 + k < nch;
-          v[k] = in ? ptx::ld_relaxed_b64(o0 + (c0 + k) * ostride + r) : 0ull;
-          ok &= !in || tag_ok(v[k], tag);
-        }
-        if (ok || retry_stop(C, t0, it)) break;
-      }
-#pragma unroll
-      for (int k = 0; k < 4; ++k)
-        if (c0 + k < nch) acc = __fmaf_rn(tag_val(v[k]), mw[h * nch + c0 + k], acc);
-    }
-    st_tagged(a.att_fin + (long long)(g * hpk) * kHeadDim + r, __fmul_rn(acc, invl[h]), tag);
-  }
-}
-
-// kscore for a binary16 K row (opt-in f16 cache): lane li takes dims [8li, 8li+8) and
-// [64+8li, 64+8li+8) as two 16-byte loads (conflict-free across the 8 lanes of a row)
-QORA_DEV void kscore16(const float* sq, const __half* krow, float* sc, int idx, bool valid, int li) {
-  float d[kHeadsPerKV] = {0.0f, 0.0f, 0.0f, 0.0f};
-  if (valid) {
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const uint4 raw = *reinterpret_cast<const uint4*>(krow + j * kHalfDim + li * 8);
-      const uint32_t wv[4] = {raw.x, raw.y, raw.z, raw.w};
-      float kf[8];
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&wv[t]));
-        kf[2 * t] = f.x;
-        kf[2 * t + 1] = f.y;
-      }
-#pragma unroll
-      for (int h = 0; h < kHeadsPerKV; ++h) {
-        const float4 qa = *reinterpret_cast<const float4*>(sq + h * kHeadDim + j * kHalfDim + li * 8);
-        const float4 qb = *reinterpret_cast<const float4*>(sq + h * kHeadDim + j * kHalfDim + li * 8 + 4);
-        d[h] = __fmaf_rn(qa.x, kf[0], d[h]);
-        d[h] = __fmaf_rn(qa.y, kf[1], d[h]);
-        d[h] = __fmaf_rn(qa.z, kf[2], d[h]);
-        d[h] = __fmaf_rn(qa.w, kf[3], d[h]);
-        d[h] = __fmaf_rn(qb.x, kf[4], d[h]);
-        d[h] = __fmaf_rn(qb.y, kf[5], d[h]);
-        d[h] = __fmaf_rn(qb.z, kf[6], d[h]);
-        d[h] = __fmaf_rn(qb.w, kf[7], d[h]);
-      }
-    }
-  }
-  const float scale = 0.08838834764831845f;
-#pragma unroll
-  for (int h = 0; h < kHeadsPerKV; ++h) {
-    float v = d[h];
-    v += __shfl_xor_sync(0xffffffffu, v, 1);
-    v += __shfl_xor_sync(0xffffffffu, v, 2);
-    v += __shfl_xor_sync(0xffffffffu, v, 4);
-    if (valid && li == 0) sc[h * kMaxAttnChunk + idx] = __fmul_rn(v, scale);
-  }
-}
-
-// one cached V element as f32
-QORA_DEV float kv_elem(const float* p) { return *p; }
-QORA_DEV float kv_elem(const __half* p) { return __half2float(*p); }
-
-// ATTN: unit u = c = (kv head g = u % nkvh, chunk u / nkvh) for the 4 query heads of g
-// (src/gemv.rs:914-989, softmax_raw :782-793; RoPE src/gemv.rs:757-778). KV is float
-// (the reference's f32 cache) or __half (the opt-in binary16 cache: the new k and v are
-// rounded to nearest-even as they enter the cache, and the new position's score and P.V
-// use the rounded values, exactly as if they were read back from it).
-template <class KV>
-__device__ __noinline__ uint32_t attention_phase_t(int L, uint32_t chunk) {
-  constexpr bool kF16 = sizeof(KV) == 2;
-  constexpr int kRows = kF16 ? kKVRows16 : kKVRows;
-  Cons C = make_cons(chunk);
-  const Args& a = C.a();
-  const int pos = C.pos, len = pos + 1, tid = C.tid, lane = C.lane, warp = C.warp;
-  int csz, nch;
-  attn_plan(len, C.G, a.nkvh, csz, nch);
-  const int u = attn_unit_of(C.c, C.G);
-  if (u >= a.nkvh * nch) return chunk;
-  const int g = u % a.nkvh;
-  const int s0 = (u / a.nkvh) * csz, s1 = min(len, s0 + csz), sc1 = min(s1, pos), n = s1 - s0;
-  const bool has_pos = pos < s1;
-  const Layer& ly = a.layers[L];
-  KV* kc = reinterpret_cast<KV*>(ly.kc) + g * a.head_stride;
-  KV* vc = reinterpret_cast<KV*>(ly.vc) + g * a.head_stride;
-  float* sq = C.scratch + kAttQ;
-  float* sc = C.scratch + kAttS;
-  float* sml = C.scratch + kAttML;
-  float* skv = C.scratch + kAttKV;
-  // RoPE pairs (d, d+64): threads 0..64*hpk-1 the query heads of g, 256..319 k;
-  // 320..447 copy v
-  const int hpk = a.hpk;
-  const bool rope = ly.rope != 0;
-  float cs = 1.0f, sn = 0.0f;
-  if (rope && tid < 320) {  // the tables do not depend on this step's activations
-    cs = __ldg(a.cos_t + (long long)pos * kHalfDim + (tid & 63));
-    sn = __ldg(a.sin_t + (long long)pos * kHalfDim + (tid & 63));
-  }
-  // one sentinel per producing group: the 4*hpk q groups of g's query heads, then the 4
-  // k and 4 v groups of head g
-  const uint32_t tag = tag_of(C, L);
-  const int nqg = 4 * hpk;
-  const int gq0 = g * nqg, gk0 = a.nq / 32 + g * 4, gv0 = (a.nq + a.nkvw) / 32 + g * 4;
-  await_tags(C, nqg + 8, tag,
-             [&](int i) { return a.qkv + 32 * (i < nqg ? gq0 + i : i < nqg + 4 ? gk0 + i - nqg : gv0 + i - nqg - 4); });
-  C.fstamp();
-  if (tid < 320 && (tid < 64 * hpk || (tid >= 256 && has_pos))) {
-    const bool isk = tid >= 256;
-    const int hh = (tid >> 6) & 3, d = tid & 63;
-    const uint64_t* src = isk ? a.qkv + a.nq + g * kHeadDim : a.qkv + (g * hpk + hh) * kHeadDim;
-    uint64_t w1, w2, t0 = 0;
-#pragma unroll 1
-    for (int it = 0;; ++it) {
-      w1 = ptx::ld_relaxed_b64(src + d);
-      w2 = ptx::ld_relaxed_b64(src + d + kHalfDim);
-      if ((tag_ok(w1, tag) & tag_ok(w2, tag)) || retry_stop(C, t0, it)) break;
-    }
-    const float x1 = tag_val(w1), x2 = tag_val(w2);
-    float y1 = x1, y2 = x2;
-    if (rope) {
-      y1 = __fsub_rn(__fmul_rn(x1, cs), __fmul_rn(x2, sn));
-      y2 = __fadd_rn(__fmul_rn(x2, cs), __fmul_rn(x1, sn));
-    }
-    if (!isk) {
-      sq[hh * kHeadDim + d] = y1;
-      sq[hh * kHeadDim + d + kHalfDim] = y2;
-    } else if constexpr (kF16) {
-      const __half h1 = __float2half_rn(y1), h2 = __float2half_rn(y2);
-      skv[d] = __half2float(h1);
-      skv[d + kHalfDim] = __half2float(h2);
-      kc[(long long)pos * kHeadDim + d] = h1;
-      kc[(long long)pos * kHeadDim + d + kHalfDim] = h2;
-    } else {
-      skv[d] = y1;
-      skv[d + kHalfDim] = y2;
-      kc[(long long)pos * kHeadDim + d] = y1;
-      kc[(long long)pos * kHeadDim + d + kHalfDim] = y2;
-    }
-  } else if (tid >= 320 && tid < 448 && has_pos) {
-    const int d = tid - 320;
-    const float v = ld_checked(C, a.qkv + a.nq + a.nkvw + g * kHeadDim + d, tag);
-    if constexpr (kF16) {
-      const __half hv = __float2half_rn(v);
-      skv[kHeadDim + d] = __half2float(hv);
-      vc[(long long)pos * kHeadDim + d] = hv;
-    } else {
-      skv[kHeadDim + d] = v;
-      vc[(long long)pos * kHeadDim + d] = v;
-    }
-  }
-  C.bar();
-  C.fstamp();
-  // scores: 4 rows per warp pass (8 lanes each), 60 rows per CTA pass
-  const int li = lane & 7, ri = warp * 4 + (lane >> 3);
-#pragma unroll 1
-  for (int s = s0; s < sc1; s += kRows) {
-    const uint8_t* stg = C.acquire_stage();
-    const int nr = min(kRows, sc1 - s);
-    if (C.stage_ok) {
-#pragma unroll 1
-      for (int rb = 0; rb < nr; rb += kCW * 4) {
-        const int i = rb + ri;
-        const KV* krow = reinterpret_cast<const KV*>(stg) + min(i, nr - 1) * kHeadDim;
-        if constexpr (kF16) kscore16(sq, krow, sc, s - s0 + i, i < nr, li);
-        else kscore(sq, krow, sc, s - s0 + i, i < nr, li);
-      }
-    }
-    C.release_stage();
-  }
-  if (has_pos && warp == 0 && !C.aborted_w()) kscore(sq, skv, sc, pos - s0, (lane >> 3) == 0, li);
-  C.bar();
-  C.fstamp();
-  // chunk softmax numerators, one warp per query head
-  if (warp < hpk && !C.aborted_w()) {
-    float* row = sc + warp * kMaxAttnChunk;
-    float mx = -INFINITY;
-#pragma unroll 1
-    for (int i = lane; i < n; i += 32) mx = fmaxf(mx, row[i]);
-    mx = warp_max(mx);
-    float l = 0.0f;
-#pragma unroll 1
-    for (int i = lane; i < n; i += 32) {
-      const float e = expf(row[i] - mx);
-      row[i] = e;
-      l += e;
-    }
-    l = warp_sum(l);
-    if (lane == 0) {
-      sml[warp * 2] = mx;
-      sml[warp * 2 + 1] = l;
-    }
-  }
-  C.bar();
-  C.fstamp();
-  // P.V: three groups of 128 threads (warps 0-3, 4-7, 8-11) take rows grp, grp + 3, ...
-  // of each stage, four rows per step with their loads issued together; thread d of a
-  // group accumulates dim d of the 4 heads; the groups' sums are added in group order
-  const int grp = tid >> 7, dd = tid & (kHeadDim - 1);
-  float o[kHeadsPerKV] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll 1
-  for (int s = s0; s < sc1; s += kRows) {
-    const uint8_t* stg = C.acquire_stage();
-    const int nr = min(kRows, sc1 - s);
-    if (C.stage_ok && grp < 3) {
-      const KV* vr = reinterpret_cast<const KV*>(stg) + dd;
-      const float* pr = sc + (s - s0);
-      int i = grp;
-#pragma unroll 1
-      for (; i + 9 < nr; i += 12) {
-        float v[4];
-#pragma unroll
-        for (int r = 0; r < 4; ++r) v[r] = kv_elem(vr + (i + 3 * r) * kHeadDim);
-#pragma unroll
-        for (int r = 0; r < 4; ++r)
-#pragma unroll
-          for (int h = 0; h < kHeadsPerKV; ++h) o[h] = __fmaf_rn(pr[h * kMaxAttnChunk + i + 3 * r], v[r], o[h]);
-      }
-#pragma unroll 1
-      for (; i < nr; i += 3) {
-        const float v = kv_elem(vr + i * kHeadDim);
-#pragma unroll
-        for (int h = 0; h < kHeadsPerKV; ++h) o[h] = __fmaf_rn(pr[h * kMaxAttnChunk + i], v, o[h]);
-      }
-    }
-    C.release_stage();
-  }
-  float ppos[kHeadsPerKV] = {0.0f, 0.0f, 0.0f, 0.0f};  // the new position's probabilities
-  if (has_pos && tid < kHeadDim) {
-#pragma unroll
-    for (int h = 0; h < kHeadsPerKV; ++h) ppos[h] = sc[h * kMaxAttnChunk + pos - s0];
-  }
-  C.bar();  // every read of the probabilities is done: groups 1 and 2 park their sums there
-  if ((grp == 1 || grp == 2) && !C.aborted()) {
-#pragma unroll
-    for (int h = 0; h < kHeadsPerKV; ++h) sc[(grp - 1) * kHeadsPerKV * kHeadDim + h * kHeadDim + dd] = o[h];
-  }
-  C.bar();
-  if (tid < kHeadDim && !C.aborted()) {
-#pragma unroll
-    for (int h = 0; h < kHeadsPerKV; ++h)
-      o[h] = __fadd_rn(__fadd_rn(o[h], sc[h * kHeadDim + tid]), sc[kHeadsPerKV * kHeadDim + h * kHeadDim + tid]);
-    if (has_pos) {
-      const float v = skv[kHeadDim + tid];
-#pragma unroll
-      for (int h = 0; h < kHeadsPerKV; ++h) o[h] = __fmaf_rn(ppos[h], v, o[h]);
-    }
-    if (nch == 1) {  // the whole context: publish o / l (exp(m - max) = 1 for the one chunk)
-#pragma unroll
-      for (int h = 0; h < kHeadsPerKV; ++h)
-        if (h < hpk)
-          st_tagged(a.att_fin + (long long)(g * hpk + h) * kHeadDim + tid,
-                    __fmul_rn(o[h], __fdiv_rn(1.0f, sml[h * 2 + 1])), tag);
-    } else {
-#pragma unroll
-      for (int h = 0; h < kHeadsPerKV; ++h)
-        if (h < hpk) st_tagged(a.att_o + ((long long)u * kHeadsPerKV + h) * kHeadDim + tid, o[h], tag);
-      if (tid < 2 * hpk) st_tagged(a.att_ml + (long long)u * 2 * kHeadsPerKV + tid, sml[tid], tag);
-    }
-  }
-  if (nch > 1) attn_merge(L, g, nch);
-  return C.chunk;
-}
-
-__device__ __noinline__ uint32_t attention_phase(int L, uint32_t chunk) {
-  return sm_args()->kv16 ? attention_phase_t<__half>(L, chunk) : attention_phase_t<float>(L, chunk);
-}
-
-// O: the merged attention output of every head (tagged, one sentinel word per head), GEMV
-// over all rows for this CTA's 32 columns, x_mid = x + o
+// O: the merged attention output of every head, GEMV over all rows for this CTA's 32
+// columns, x_mid = x + o (the residual x of the columns is read first: it is ready)
 __device__ __noinline__ uint32_t o_phase(int L, uint32_t chunk) {
   Cons C = make_cons(chunk);
   const Args& a = C.a();
-  const Span sp = span_of(a, OPR, C.c);
-  if (sp.n == 0) return chunk;
-  const int K = a.K[OPR];
+  const int* P = mat_plan(OPR);
+  if (P[0] == 0) return chunk;
   const uint32_t tag = tag_of(C, L);
-  await_tags(C, a.nh, tag, [&](int i) { return a.att_fin + (long long)i * kHeadDim; });
-  C.stamp(2 + 8 * min(L, kTraceLayers - 1) + 3);
-  C.fstamp();
-  // xs = att * 2^64: each thread scales the pairs it loaded itself
-  float* xs = C.scratch;
-  load_x(C, xs, a.att_fin, K, tag);
-  constexpr int kPairs = (2048 / 2 + kCT - 1) / kCT;
-#pragma unroll
-  for (int j = 0; j < kPairs; ++j) {
-    const int b = C.tid + j * kCT;
-    if (b < K / 2) {
-      xs[2 * b] *= kTwo64;
-      xs[2 * b + 1] *= kTwo64;
-    }
-  }
+  if (C.tid < kGroup) C.scratch[kOffFin + C.tid] = ld_checked(a.xbuf + (long long)L * a.H + P[2] * kGroup + C.tid, tag);
+  poll_vec(a.att_fin, a.K[OPR], tag, C.scratch, kTwo64);
   C.bar();
-  C.fstamp();
-  return gemv_stream<1>(OPR, L, C.chunk);
+  C.stamp(2 + 8 * min(L, kTraceLayers - 1) + 3);
+  return gemv_run<false>(OPR, L, C.chunk);
 }
 
 // GU (all): RMSNorm(x_mid) . [gate|up] -> split-K partials per tile
 __device__ __noinline__ uint32_t gu_phase(int L, uint32_t chunk) {
   Cons C = make_cons(chunk);
   const Args& a = C.a();
-  const Span sp = span_of(a, GU, C.c);
   const int H = a.H;
   float* sB = C.scratch + kOffB;
-  float gam[kXsPer];
-  prefetch_gains(C, a.layers[L].g_post, sp, a.K[GU], gam);
-  const uint32_t tag = tag_of(C, L);
-  const uint64_t* xm = a.xmid + (long long)L * H;
-  await_tags(C, H / 32, tag, [&](int i) { return xm + i * 32; });  // one word per o_proj group
-  C.stamp(2 + 8 * min(L, kTraceLayers - 1) + 5);
-  const float ss = load_x(C, sB, xm, H, tag);
-  const float inv = rms_inv_from(C.csum(ss), H);
-  fill_norm_inputs(C, sB, inv, gam, sp, a.K[GU]);
+  stage_gains(a.layers[L].g_post, GU);
+  const float ss = poll_vec(a.xmid + (long long)L * H, H, tag_of(C, L), sB, 1.0f);
   C.bar();
-  C.fstamp();
-  return gemv_stream<8>(GU, L, C.chunk);
+  C.stamp(2 + 8 * min(L, kTraceLayers - 1) + 5);
+  if (mat_plan(DOWN)[0] > 0) {  // keep x_mid of the down columns this CTA finishes (sB is reused below)
+    const int* D = plan() + kPlDown;
+    if (C.tid < D[2] - D[1]) C.scratch[kOffFin + C.tid] = sB[D[0] * kTileCols + D[1] + C.tid];
+  }
+  const float inv = rms_inv_from(csum(ss), H);
+  fill_norm_inputs(sB, inv, GU);
+  C.bar();
+  return gemv_run<true>(GU, L, C.chunk);
+}
+
+// silu(g) * u with silu(g) = g / (1 + exp(-g)) (src/gemv.rs:494-500), one copy of the code
+__device__ __noinline__ float swiglu(float g, float u) {
+  return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
 }
 
 // DOWN (all): SwiGLU of the rows it needs from the gate/up partials (src/gemv.rs:412-502),
-// split-K GEMV
+// split-K GEMV, then this CTA's slice of its tile: x_{L+1} = x_mid + the sum of the tile's
+// partials in slot order
 __device__ __noinline__ uint32_t down_phase(int L, uint32_t chunk) {
   Cons C = make_cons(chunk);
   const Args& a = C.a();
-  const Span sp = span_of(a, DOWN, C.c);
-  const int K = a.K[DOWN];
-  constexpr int kHalfTile = 128;  // gate (then up) outputs per gate/up tile
-  // gate/up tiles of this CTA's rows: one range per segment (the host checks <= 2)
-  int tr[4] = {0, -1, 0, -1};
-  {
-    int k = 0;
-    for_each_seg(a, DOWN, C.c, [&](int, int r0, int r1) {
-      if (k < 2) {
-        tr[2 * k] = r0 / kHalfTile;
-        tr[2 * k + 1] = (r1 - 1) / kHalfTile;
-      }
-      ++k;
-    });
-  }
-  // one sentinel per (gate/up tile, split-K slot) this CTA reads
+  const int* P = mat_plan(DOWN);
+  const int n = P[0];
+  if (n == 0) return chunk;
+  const int S = a.slots[GU];
+  constexpr int kHalfTile = kTileCols / 2;  // gate (then up) outputs per gate/up tile
   const uint32_t tag = tag_of(C, L);
-  {
-    const int S = a.slots[GU], n0 = tr[1] - tr[0] + 1, n1 = tr[3] - tr[2] + 1;
-    await_tags(C, (n0 + n1) * S, tag, [&](int i) {
-      const int k = i / S, t = k < n0 ? tr[0] + k : tr[2] + (k - n0);
-      return a.gu_part + ((long long)t * S + min(i % S, C.ns(GU, t) - 1)) * 256;
-    });
-  }
-  // rows i = tid, tid + kCT: both rows' gate and up partials (4 slots each) in flight
-  {
+  {  // rows i = tid, tid + kCT: both rows' gate and up partials (4 slots each) in flight
     float* xs = C.scratch;
-    int r = (sp.lin0 + C.tid) % K;
 #pragma unroll 1
-    for (int i = C.tid; i < sp.n; i += 2 * kCT) {
-      const int r2 = row_next(r, K);
-      const bool two = i + kCT < sp.n;
+    for (int i = C.tid; i < n; i += 2 * kCT) {
+      const int r = P[3] + i, r2 = r + kCT;  // one segment: rows P[3] + i
+      const bool two = i + kCT < n;
       const int t1 = r / kHalfTile, t2 = r2 / kHalfTile;
       const int n1 = C.ns(GU, t1), n2 = two ? C.ns(GU, t2) : 0;
-      const uint64_t* p1 = a.gu_part + (long long)t1 * a.slots[GU] * 256 + r % kHalfTile;
-      const uint64_t* p2 = a.gu_part + (long long)t2 * a.slots[GU] * 256 + r2 % kHalfTile;
+      const uint64_t* p1 = a.gu_part + (long long)t1 * S * kTileCols + r % kHalfTile;
+      const uint64_t* p2 = a.gu_part + (long long)t2 * S * kTileCols + r2 % kHalfTile;
       float g1 = 0.0f, u1 = 0.0f, g2 = 0.0f, u2 = 0.0f;
 #pragma unroll 1
       for (int k0 = 0; k0 < max(n1, n2); k0 += 4) {
@@ -1305,14 +871,14 @@ __device__ __noinline__ uint32_t down_phase(int L, uint32_t chunk) {
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const bool ok1 = k0 + k < n1, ok2 = k0 + k < n2;
-            v[0][k] = ok1 ? ptx::ld_relaxed_b64(p1 + (k0 + k) * 256) : 0ull;
-            v[1][k] = ok1 ? ptx::ld_relaxed_b64(p1 + (k0 + k) * 256 + kHalfTile) : 0ull;
-            v[2][k] = ok2 ? ptx::ld_relaxed_b64(p2 + (k0 + k) * 256) : 0ull;
-            v[3][k] = ok2 ? ptx::ld_relaxed_b64(p2 + (k0 + k) * 256 + kHalfTile) : 0ull;
+            v[0][k] = ok1 ? ptx::ld_relaxed_b64(p1 + (k0 + k) * kTileCols) : 0ull;
+            v[1][k] = ok1 ? ptx::ld_relaxed_b64(p1 + (k0 + k) * kTileCols + kHalfTile) : 0ull;
+            v[2][k] = ok2 ? ptx::ld_relaxed_b64(p2 + (k0 + k) * kTileCols) : 0ull;
+            v[3][k] = ok2 ? ptx::ld_relaxed_b64(p2 + (k0 + k) * kTileCols + kHalfTile) : 0ull;
             ok &= (!ok1 || (tag_ok(v[0][k], tag) & tag_ok(v[1][k], tag))) &&
                   (!ok2 || (tag_ok(v[2][k], tag) & tag_ok(v[3][k], tag)));
           }
-          if (ok || retry_stop(C, t0, it)) break;
+          if (ok || retry_stop(t0, it)) break;
         }
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
@@ -1326,14 +892,308 @@ __device__ __noinline__ uint32_t down_phase(int L, uint32_t chunk) {
           }
         }
       }
-      xs[i] = __fmul_rn(__fdiv_rn(g1, __fadd_rn(1.0f, expf(-g1))), u1) * kTwo64;
-      if (two) xs[i + kCT] = __fmul_rn(__fdiv_rn(g2, __fadd_rn(1.0f, expf(-g2))), u2) * kTwo64;
-      r = row_next(r2, K);
+      xs[i] = swiglu(g1, u1) * kTwo64;
+      if (two) xs[i + kCT] = swiglu(g2, u2) * kTwo64;
     }
   }
   C.bar();
-  C.fstamp();
-  return gemv_stream<8>(DOWN, L, C.chunk);
+  chunk = gemv_run<true>(DOWN, L, C.chunk);
+  // this CTA's slice [c0, c1) of tile t: entry i = (slot i / nc, column c0 + i % nc)
+  const int* D = plan() + kPlDown;
+  const int t = D[0], c0 = D[1], ns = D[3], nc = D[2] - D[1];
+  float* fin = C.scratch + kOffB;  // [ns][nc]
+  const uint64_t* base = a.dn_part + (long long)t * a.slots[DOWN] * kTileCols + c0;
+#pragma unroll 1
+  for (int i = C.tid; i < ns * nc; i += kCT) fin[i] = ld_checked(base + (long long)(i / nc) * kTileCols + i % nc, tag);
+  C.bar();
+  if (C.tid < nc) {
+    float d = 0.0f;
+#pragma unroll 1
+    for (int s = 0; s < ns; ++s) d = __fadd_rn(d, fin[s * nc + C.tid]);
+    const int col = t * kTileCols + c0 + C.tid;
+    if (a.tp > 1) {  // row-split down: sum the ranks' partials of this column
+      tp_push(a, a.peer_d, L, col, d, tag);
+      d = tp_sum(a.peer_d[a.rank], L, col, tag);
+    }
+    // x_{L+1} carries layer L+1's tag
+    st_tagged(a.xbuf + (long long)(L + 1) * a.H + col, __fadd_rn(C.scratch[kOffFin + C.tid], d), tag + 1u);
+  }
+  C.bar();  // the slice table (B) is read before the next phase reuses it
+  return chunk;
+}
+
+// ---- attention
+// Scores of 4 query heads (q in shared memory) against nr K rows at `rows` (8 lanes per
+// row, 16 dims each; 4 rows per warp pass), written to sc[h * kMaxAttnChunk + idx0 + i]
+// scaled by 1/sqrt(128). KV: float or __half rows.
+template <class KV>
+__device__ __noinline__ void score_rows(const KV* rows, int nr, int idx0) {
+  const float* sq = sm_scratch() + kAttQ;
+  float* sc = sm_scratch() + kAttS;
+  const int lane = threadIdx.x & 31, li = lane & 7;
+  const float scale = 0.08838834764831845f;  // 1/sqrt(128): the f32 quotient of 1 and f32 sqrt(128)
+#pragma unroll 1
+  for (int rb = 0; rb < nr; rb += kCW * 4) {
+    const int i = rb + (threadIdx.x >> 5) * 4 + (lane >> 3);
+    const bool valid = i < nr;
+    const KV* krow = rows + (long long)min(i, nr - 1) * kHeadDim;
+    float kf[16];
+    if constexpr (sizeof(KV) == 4) {  // dims [16 li, 16 li + 16)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float4 k4 = reinterpret_cast<const float4*>(krow + li * 16)[j];
+        kf[4 * j] = k4.x;
+        kf[4 * j + 1] = k4.y;
+        kf[4 * j + 2] = k4.z;
+        kf[4 * j + 3] = k4.w;
+      }
+    } else {  // dims [8 li, 8 li + 8) and [64 + 8 li, 64 + 8 li + 8): conflict-free 16-byte loads
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(krow + j * kHalfDim + li * 8);
+        const uint32_t wv[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&wv[q]));
+          kf[8 * j + 2 * q] = f.x;
+          kf[8 * j + 2 * q + 1] = f.y;
+        }
+      }
+    }
+#pragma unroll 1
+    for (int h = 0; h < kHeadsPerKV; ++h) {
+      float d = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int dim = sizeof(KV) == 4 ? li * 16 + 4 * j : (j >> 1) * kHalfDim + li * 8 + 4 * (j & 1);
+        const float4 q4 = *reinterpret_cast<const float4*>(sq + h * kHeadDim + dim);
+        d = __fmaf_rn(q4.x, kf[4 * j], d);
+        d = __fmaf_rn(q4.y, kf[4 * j + 1], d);
+        d = __fmaf_rn(q4.z, kf[4 * j + 2], d);
+        d = __fmaf_rn(q4.w, kf[4 * j + 3], d);
+      }
+      d += __shfl_xor_sync(0xffffffffu, d, 1);
+      d += __shfl_xor_sync(0xffffffffu, d, 2);
+      d += __shfl_xor_sync(0xffffffffu, d, 4);
+      if (valid && li == 0) sc[h * kMaxAttnChunk + idx0 + i] = __fmul_rn(d, scale);
+    }
+  }
+}
+
+// one cached V element as f32
+QORA_DEV float kv_elem(const float* p) { return *p; }
+QORA_DEV float kv_elem(const __half* p) { return __half2float(*p); }
+
+// P.V over nr V rows at `rows` for the 4 heads, added to o: thread (grp, d) of three
+// 128-thread groups takes rows grp, grp + 3, ...; probabilities sc[h * kMaxAttnChunk +
+// idx0 + i]. The accumulators travel in registers (argument and result).
+template <class KV>
+__device__ __noinline__ float4 pv_rows(const KV* rows, int nr, int idx0, int grp, int dd, float4 o) {
+  const float* sc = sm_scratch() + kAttS + idx0;
+#pragma unroll 1
+  for (int i = grp; i < nr; i += 3) {
+    const float v = kv_elem(rows + (long long)i * kHeadDim + dd);
+    o.x = __fmaf_rn(sc[i], v, o.x);
+    o.y = __fmaf_rn(sc[kMaxAttnChunk + i], v, o.y);
+    o.z = __fmaf_rn(sc[2 * kMaxAttnChunk + i], v, o.z);
+    o.w = __fmaf_rn(sc[3 * kMaxAttnChunk + i], v, o.w);
+  }
+  return o;
+}
+
+// Attention merge of KV head g (nch chunks): this unit (chunk k) produces outputs
+// [r0, r1) of the head's hpk * 128: per query head h, M = max_ch m, w_ch = exp(m_ch - M),
+// l = sum_ch l_ch w_ch (chunk order), out = (sum_ch o_ch w_ch, chunk order) * (1 / l),
+// published tagged for o_proj. Every unit of the head reads all chunks' partials of its
+// slice directly: one L2 round trip once they are there, no arrival counter.
+__device__ __noinline__ void attn_merge(int L, int g, int nch) {
+  const Cons C = make_cons(0);
+  const Args& a = C.a();
+  const int nout = a.hpk * kHeadDim;
+  const int* M = plan() + kPlMerge;
+  const int r0 = M[0], nr = M[1] - M[0], h0 = M[2], nh = M[3];  // the slice and its heads
+  const uint32_t tag = tag_of(C, L);
+  float* so = C.scratch + kMgO;      // [nch][nr]
+  float* sml = C.scratch + kMgML;    // [nch][nh][2]
+  float* mw = C.scratch + kMgW;      // [nh][nch]
+  float* invl = C.scratch + kMgInv;  // [nh]
+  const int nml = nch * nh * 2;
+#pragma unroll 1
+  for (int i = C.tid; i < nml + nch * nr; i += kCT) {
+    if (i < nml) {  // (m, l) of chunk ch, head h0 + (i % (2 nh)) / 2
+      const int ch = i / (2 * nh), rest = i % (2 * nh);
+      sml[i] = ld_checked(a.att_ml + ((long long)(ch * a.nkvh + g) * kHeadsPerKV + h0 + rest / 2) * 2 + (rest & 1), tag);
+    } else {  // o of chunk ch, output r0 + r
+      const int j = i - nml, ch = j / nr, r = j % nr;
+      so[j] = ld_checked(a.att_o + (long long)(ch * a.nkvh + g) * kHeadsPerKV * kHeadDim + r0 + r, tag);
+    }
+  }
+  C.bar();
+  if (C.tid < nh) {
+    const int h = C.tid;
+    float mx = -INFINITY;
+#pragma unroll 1
+    for (int ch = 0; ch < nch; ++ch) mx = fmaxf(mx, sml[(ch * nh + h) * 2]);
+    float l = 0.0f;
+#pragma unroll 1
+    for (int ch = 0; ch < nch; ++ch) {
+      const float w = expf(sml[(ch * nh + h) * 2] - mx);
+      mw[h * nch + ch] = w;
+      l = __fmaf_rn(sml[(ch * nh + h) * 2 + 1], w, l);
+    }
+    invl[h] = __fdiv_rn(1.0f, l);
+  }
+  C.bar();
+  if (C.tid < nr) {
+    const int r = r0 + C.tid, h = r / kHeadDim - h0;
+    float acc = 0.0f;
+#pragma unroll 1
+    for (int ch = 0; ch < nch; ++ch) acc = __fmaf_rn(so[ch * nr + C.tid], mw[h * nch + ch], acc);
+    st_tagged(a.att_fin + (long long)g * nout + r, __fmul_rn(acc, invl[h]), tag);
+  }
+  C.bar();  // the staging (XS, B) is read until here; the next phase writes it at once
+}
+
+// ATTN: unit u = c = (kv head g = u % nkvh, chunk u / nkvh) for the hpk query heads of g
+// (src/gemv.rs:914-989, softmax_raw :782-793; RoPE src/gemv.rs:757-778). KV is float
+// (the reference's f32 cache) or __half (the opt-in binary16 cache: the new k and v are
+// rounded to nearest-even as they enter the cache, and the new position's score and P.V
+// use the rounded values, exactly as if they were read back from it). The new
+// position's k and v rows are kept in shared memory in the cache's element type, so the
+// same routines score and weigh them as the cached rows streamed through the ring.
+template <class KV>
+__device__ __noinline__ uint32_t attention_phase_t(int L, uint32_t chunk) {
+  constexpr int kRows = sizeof(KV) == 2 ? kKVRows16 : kKVRows;
+  Cons C = make_cons(chunk);
+  const Args& a = C.a();
+  const int pos = C.pos, tid = C.tid;
+  const int* P = plan() + kPlAtt;
+  if (!P[0]) return chunk;
+  const int g = P[1], kch = P[2], s0 = P[3], n = P[4] - P[3], sc1 = P[5], nch = P[6];
+  const int u = kch * a.nkvh + g;
+  const bool has_pos = P[7] != 0;
+  const Layer& ly = a.layers[L];
+  float* sq = C.scratch + kAttQ;
+  float* sc = C.scratch + kAttS;
+  float* sml = C.scratch + kAttML;
+  float* sinv = C.scratch + kAttInv;
+  KV* skv = reinterpret_cast<KV*>(C.scratch + kAttKV);  // [k row | v row]
+  const int hpk = a.hpk;
+  const uint32_t tag = tag_of(C, L);
+  // RoPE pairs (d, d+64): threads 0..64*hpk-1 the query heads of g, 256..319 k (new
+  // position's chunk only); 320..447 copy v
+  if (tid < 64 * hpk || (has_pos && tid >= 256 && tid < 448)) {
+    const bool isv = tid >= 320, isk = tid >= 256 && !isv;
+    const int hh = (tid >> 6) & 3, d = isv ? tid - 320 : tid & 63;
+    const bool rot = ly.rope && !isv;
+    float cs = 1.0f, sn = 0.0f;
+    if (rot) {  // the tables do not depend on this step's activations: read before the wait
+      cs = __ldg(a.cos_t + (long long)pos * kHalfDim + d);
+      sn = __ldg(a.sin_t + (long long)pos * kHalfDim + d);
+    }
+    const uint64_t* src = (isv ? a.qkv + a.nq + a.nkvw + g * kHeadDim
+                               : isk ? a.qkv + a.nq + g * kHeadDim : a.qkv + (g * hpk + hh) * kHeadDim) + d;
+    uint64_t w1, w2, t0 = 0;
+#pragma unroll 1
+    for (int it = 0;; ++it) {
+      w1 = ptx::ld_relaxed_b64(src);
+      w2 = ptx::ld_relaxed_b64(src + (isv ? 0 : kHalfDim));
+      if ((tag_ok(w1, tag) & tag_ok(w2, tag)) || retry_stop(t0, it)) break;
+    }
+    float x1 = tag_val(w1), x2 = tag_val(w2);
+    if (rot) {  // split-half rotation with the table row of this position
+      const float y1 = __fsub_rn(__fmul_rn(x1, cs), __fmul_rn(x2, sn));
+      x2 = __fadd_rn(__fmul_rn(x2, cs), __fmul_rn(x1, sn));
+      x1 = y1;
+    }
+    if (!isk && !isv) {
+      sq[hh * kHeadDim + d] = x1;
+      sq[hh * kHeadDim + d + kHalfDim] = x2;
+    } else {  // append to the cache and keep the row (as stored) for this step
+      KV* cache = reinterpret_cast<KV*>(isv ? ly.vc : ly.kc) + g * a.head_stride + (long long)pos * kHeadDim;
+      KV* row = skv + (isv ? kHeadDim : 0);
+      const KV e1 = (KV)x1;  // binary16: round to nearest even
+      row[d] = e1;
+      cache[d] = e1;
+      if (!isv) {
+        const KV e2 = (KV)x2;
+        row[d + kHalfDim] = e2;
+        cache[d + kHalfDim] = e2;
+      }
+    }
+  }
+  C.bar();
+  // scores of the cached rows (streamed through the ring), then of the new position
+#pragma unroll 1
+  for (int s = s0; s < sc1; s += kRows) {
+    const uint8_t* stg = C.acquire_stage();
+    if (C.stage_ok) score_rows<KV>(reinterpret_cast<const KV*>(stg), min(kRows, sc1 - s), s - s0);
+    C.release_stage();
+  }
+  if (has_pos && C.warp == 0 && !C.aborted_w()) score_rows<KV>(skv, 1, pos - s0);
+  C.bar();
+  // chunk softmax numerators, one warp per query head
+  if (C.warp < hpk && !C.aborted_w()) {
+    float* row = sc + C.warp * kMaxAttnChunk;
+    float mx = -INFINITY;
+#pragma unroll 1
+    for (int i = C.lane; i < n; i += 32) mx = fmaxf(mx, row[i]);
+    mx = warp_max(mx);
+    float l = 0.0f;
+#pragma unroll 1
+    for (int i = C.lane; i < n; i += 32) {
+      const float e = expf(row[i] - mx);
+      row[i] = e;
+      l += e;
+    }
+    l = warp_sum(l);
+    if (C.lane == 0) {
+      sml[C.warp * 2] = mx;
+      sml[C.warp * 2 + 1] = l;
+      sinv[C.warp] = __fdiv_rn(1.0f, l);
+    }
+  }
+  C.bar();
+  // P.V: three groups of 128 threads; thread d of a group accumulates dim d of the 4
+  // heads over its rows; the groups' sums are added in group order
+  const int grp = tid >> 7, dd = tid & (kHeadDim - 1);
+  float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll 1
+  for (int s = s0; s < sc1; s += kRows) {
+    const uint8_t* stg = C.acquire_stage();
+    if (C.stage_ok && grp < 3) o = pv_rows<KV>(reinterpret_cast<const KV*>(stg), min(kRows, sc1 - s), s - s0, grp, dd, o);
+    C.release_stage();
+  }
+  if (has_pos && grp == 0) o = pv_rows<KV>(skv + kHeadDim, 1, pos - s0, 0, dd, o);
+  C.bar();  // every read of the probabilities is done: groups 1 and 2 park their sums there
+  if ((grp == 1 || grp == 2) && !C.aborted()) {
+    float* park = sc + (grp - 1) * kHeadsPerKV * kHeadDim + dd;
+    park[0] = o.x;
+    park[kHeadDim] = o.y;
+    park[2 * kHeadDim] = o.z;
+    park[3 * kHeadDim] = o.w;
+  }
+  C.bar();
+  if (tid < kHeadDim && !C.aborted()) {
+    const float ov[kHeadsPerKV] = {o.x, o.y, o.z, o.w};
+#pragma unroll
+    for (int h = 0; h < kHeadsPerKV; ++h) {
+      if (h >= hpk) break;
+      const float oh = __fadd_rn(__fadd_rn(ov[h], sc[h * kHeadDim + tid]), sc[kHeadsPerKV * kHeadDim + h * kHeadDim + tid]);
+      if (nch == 1)  // the whole context: publish o / l (exp(m - max) = 1 for the one chunk)
+        st_tagged(a.att_fin + (long long)(g * hpk + h) * kHeadDim + tid, __fmul_rn(oh, sinv[h]), tag);
+      else
+        st_tagged(a.att_o + ((long long)u * kHeadsPerKV + h) * kHeadDim + tid, oh, tag);
+    }
+    if (nch > 1 && tid < 2 * hpk) st_tagged(a.att_ml + (long long)u * 2 * kHeadsPerKV + tid, sml[tid], tag);
+  }
+  const bool ab = C.bar_aborted();  // the merge's barriers: every thread decides alike
+  if (nch > 1 && !ab) attn_merge(L, g, nch);
+  return C.chunk;
+}
+
+__device__ __noinline__ uint32_t attention_phase(int L, uint32_t chunk) {
+  return sm_args()->kv16 ? attention_phase_t<__half>(L, chunk) : attention_phase_t<float>(L, chunk);
 }
 
 // Drain after an abort: wait (bounded) for the producer to stop and for the copies it
@@ -1366,12 +1226,10 @@ __device__ __noinline__ void lm_phase(uint32_t chunk) {
   const Args& a = C.a();
   const int H = a.H, lane = C.lane, warp = C.warp;
   float* sB = C.scratch + kOffB;
-  const uint32_t tag = tag_of(C, a.L);
-  const uint64_t* x = a.xbuf + (long long)a.L * H;
-  await_tags(C, a.tiles[DOWN], tag, [&](int i) { return x + i * 256; });
+  const float ss = poll_vec(a.xbuf + (long long)a.L * H, H, tag_of(C, a.L), sB, 1.0f);
+  C.bar();
   C.stamp(2 + 8 * kTraceLayers);
-  const float ss = load_x(C, sB, x, H, tag);
-  const float inv = rms_inv_from(C.csum(ss), H);
+  const float inv = rms_inv_from(csum(ss), H);
   for (int i = C.tid; i < H; i += kCT) sB[i] = __fmul_rn(__fmul_rn(sB[i], inv), a.final_gamma[i]);
   C.bar();
   constexpr int EPL = GPL * 32;
@@ -1478,16 +1336,17 @@ __global__ void __launch_bounds__(kThreads, 1) decode_megakernel(const Args args
     flags[8] = (int)(*args.epoch * 64u);  // tags of this launch: tag base + layer + 1
     ptx::fence_mbar_init();
   }
-  {  // split-K slots per tile of gate/up, then down
+  __syncthreads();  // the shared copy of the arguments is complete
+  const Args& a = *sa;
+  {  // split-K slots per tile of gate/up, then down; this CTA's plan for the launch (built
+     // from the shared copy: the parameter struct itself is never addressed)
     int* tab = reinterpret_cast<int*>(scratch + kOffTab);
-    for (int t = tid; t < args.tiles[GU]; t += kThreads) tab[t] = nslots(args, GU, t);
-    for (int t = tid; t < args.tiles[DOWN]; t += kThreads) tab[args.tiles[GU] + t] = nslots(args, DOWN, t);
-    const int lc = c - args.sub0[DOWN];
-    if (tid == 0 && lc >= 0 && lc < args.subn[DOWN])
-      al_span(args, DOWN, lc, tab + args.tiles[GU] + args.tiles[DOWN]);
+    for (int t = tid; t < a.tiles[GU]; t += kThreads) tab[t] = nslots(a, GU, t);
+    for (int t = tid; t < a.tiles[DOWN]; t += kThreads) tab[a.tiles[GU] + t] = nslots(a, DOWN, t);
+    if (warp < 4 && lane == 0) make_mat_plan(a, warp, c);
+    if (warp == 4 && lane == 0) make_att_plan(a, c, G, flags[2]);
   }
   __syncthreads();  // last block-wide barrier: the producer warp leaves below
-  const Args& a = *sa;
   const int pos = flags[2];
   const int token = flags[5];
 
@@ -1594,7 +1453,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_megakernel(const Args args
         for (int it = 0;; ++it) {
           wv = ptx::ld_acquire_sys_b64(mine + 2 * p);
           wi = ptx::ld_acquire_sys_b64(mine + 2 * p + 1);
-          if ((tag_ok(wv, tag) & tag_ok(wi, tag)) || retry_stop(C, t0, it)) break;
+          if ((tag_ok(wv, tag) & tag_ok(wi, tag)) || retry_stop(t0, it)) break;
         }
         if (better(tag_val(wv), (unsigned)wi, b, bi)) {
           b = tag_val(wv);

@@ -131,5 +131,24 @@ __device__ __forceinline__ void named_bar(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// the same barrier, returning the OR of `p` over the participating threads (a decision
+// every participant takes the same way)
+__device__ __forceinline__ bool named_bar_or(int id, int nthreads, bool p) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred a, b;\n setp.ne.u32 a, %1, 0;\n bar.red.or.pred b, %2, %3, a;\n selp.u32 %0, 1, 0, b;\n}\n"
+      : "=r"(r)
+      : "r"((uint32_t)p), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
+}
+
+// asynchronous 4-byte copy global -> shared (the thread continues; cp_async_wait_all()
+// waits for this thread's copies)
+__device__ __forceinline__ void cp_async_4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 }  // namespace ptx
 }  // namespace qora

@@ -28,6 +28,8 @@
 #include <thread>
 #include <vector>
 
+#include <cudaTypedefs.h>
+
 #include "../../include/qora_cuda.h"
 #include "attention.cuh"
 #include "common.cuh"
@@ -36,6 +38,7 @@
 #include "umma_gemm.cuh"
 #include "megakernel.cuh"
 #include "q4_gemv.cuh"
+#include "q4_gemv_tma.cuh"
 #include "sampling.cuh"
 #include "small_kernels.cuh"
 
@@ -320,7 +323,7 @@ struct qora_engine {
   uint64_t* mk_xmid = nullptr;  // tagged hand-off buffers: (tag << 32) | f32 bits
   uint64_t* mk_qkv = nullptr;
   uint64_t* mk_gu_part = nullptr;
-  float* mk_dn_part = nullptr;
+  uint64_t* mk_dn_part = nullptr;  // tagged
   unsigned* mk_epoch = nullptr;
   int mk_cpl = 0, mk_ncnt = 0;
   uint64_t* mk_xbuf = nullptr;
@@ -742,7 +745,7 @@ qora_status mega_init(qora_engine* e) {
   }
   if (d0.gu.tiles + d0.down.tiles + 3 > mk::kMaxTabTiles) return no("too many gate/up and down tiles");
   if (H > mk::kBFloats) return no("hidden larger than the shared x buffer");
-  if (nh * (mk::kMaxUnits / nkvh + 1) > mk::kBFloats) return no("attention merge weights do not fit");
+
   if (e->lm_row_bytes > mk::kStageBytes) return no("embedding row larger than a stage");
   if ((long long)G * e->vocab >= (1ll << 31)) return no("vocab split outside 32-bit arithmetic");
   int blocks = 0;
@@ -785,7 +788,7 @@ qora_status mega_init(qora_engine* e) {
   QCHECK(alloc_tagged(&e->mk_xmid, (size_t)e->num_layers * H));
   QCHECK(alloc_tagged(&e->mk_qkv, (size_t)d0.qkv1.G * kGroup));
   QCHECK(alloc_tagged(&e->mk_gu_part, np_gu));
-  QCHECK(e->alloc(&e->mk_dn_part, np_dn));
+  QCHECK(alloc_tagged(&e->mk_dn_part, np_dn));
   if (e->tp > 1) {
     // receive buffers the peers write into: o and down partials [L][tp][H] (tagged), the
     // ranks' lm_head bests [tp][2] (tagged), the full logits [vocab]
@@ -2449,6 +2452,81 @@ qora_status qora_generate_greedy_batch(qora_engine* e, qora_kv* kv, const uint32
 }
 
 // ------------------------------------------------------------------ kernel-level entries
+}  // extern "C"
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link)
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D row-major tensor map over [rows][cols] elements of `esz` bytes, boxes of
+// box_cols x box_rows elements (no swizzle; rows past the end read as zero)
+static qora_status encode_2d(CUtensorMap* m, const void* base, CUtensorMapDataType type, int esz, uint64_t cols,
+                             uint64_t rows, uint32_t box_cols, uint32_t box_rows) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (!enc) return fail(QORA_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols * (cuuint64_t)esz};
+  const cuuint32_t box[2] = {box_cols, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(m, type, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(QORA_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return QORA_OK;
+}
+
+// The TMA GEMV (q4_gemv_tma.cuh) for shapes it takes: 256-column tiles, 16-byte-aligned
+// rows of both arrays, a per-CTA range of at most 7 boxes of rows; *used = false otherwise.
+static qora_status q4_gemv_tma(const float* d_x, const uint8_t* d_packed, const uint16_t* d_scales, int k, int n,
+                               float* d_y, cudaStream_t stream, int dev, bool* used) {
+  *used = false;
+  const int G = sm_count(dev);
+  const long long tiles = n / kTileCols, total = tiles * (long long)k;
+  if (n % kTileCols || ((uintptr_t)d_packed | (uintptr_t)d_scales) % 16 || total * G >= (1ll << 32) ||
+      (total + G - 1) / G > 7 * g1::kBoxRows)
+    return QORA_OK;
+  static std::once_flag attr_once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(attr_once, [] {
+    attr_err = cudaFuncSetAttribute(g1::q4_gemv_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)g1::kSmemBytes);
+  });
+  QCUDA(attr_err);
+  CUtensorMap mp, ms;
+  QCHECK(encode_2d(&mp, d_packed, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)n / 2, (uint64_t)k, 128, g1::kBoxRows));
+  QCHECK(encode_2d(&ms, d_scales, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, (uint64_t)n / kGroup, (uint64_t)k, 8, g1::kBoxRows));
+  // CTAs touching one tile: every CTA owns at least floor(total / G) rows of the range
+  const int slots = (int)(k / std::max(1ll, total / G)) + 2;
+  std::lock_guard<std::mutex> lk(g_entry_mu);
+  EntryScratch* sc = nullptr;
+  QCHECK(entry_scratch(dev, (size_t)tiles * slots * kTileCols, (size_t)tiles, 0, &sc));
+  g1::Args a{d_x, d_y, sc->partials, sc->counters, k, n, (int)tiles, slots};
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(G);
+  cfg.blockDim = dim3(g1::kThreads);
+  cfg.dynamicSmemBytes = g1::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  QCUDA(cudaLaunchKernelEx(&cfg, g1::q4_gemv_tma_kernel, mp, ms, a));
+  *used = true;
+  return QORA_OK;
+}
+
+extern "C" {
+
 qora_status qora_q4_gemv(const float* d_x, const uint8_t* d_packed, const uint16_t* d_scales,
                          uint64_t k, uint64_t n, float* d_y, void* stream) {
   if (!d_x || !d_packed || !d_scales || !d_y) return fail(QORA_ERR_INVALID, "NULL pointer");
@@ -2456,6 +2534,9 @@ qora_status qora_q4_gemv(const float* d_x, const uint8_t* d_packed, const uint16
     return fail(QORA_ERR_INVALID, "bad shape k=%llu n=%llu", (unsigned long long)k, (unsigned long long)n);
   int dev = 0;
   QCUDA(cudaGetDevice(&dev));
+  bool used = false;
+  QCHECK(q4_gemv_tma(d_x, d_packed, d_scales, (int)k, (int)n, d_y, (cudaStream_t)stream, dev, &used));
+  if (used) return QORA_OK;
   const Q4Src src = f1_src(d_packed, d_scales, (int)k, (int)n);
   const GemvShape sh = plan_gemv((int)k, src.tiles, 2 * sm_count(dev));
   std::lock_guard<std::mutex> lk(g_entry_mu);
