@@ -923,9 +923,12 @@ __device__ __noinline__ uint32_t down_phase(int L, uint32_t chunk) {
 }
 
 // ---- attention
-// Scores of 4 query heads (q in shared memory) against nr K rows at `rows` (8 lanes per
-// row, 16 dims each; 4 rows per warp pass), written to sc[h * kMaxAttnChunk + idx0 + i]
-// scaled by 1/sqrt(128). KV: float or __half rows.
+// Scores of the 4 query heads (q in shared memory) against nr K rows at `rows`, written
+// to sc[h * kMaxAttnChunk + idx0 + i] scaled by 1/sqrt(128). A row is taken by 8 lanes,
+// 4 rows per warp pass; lane li holds dims {4 li + 32 j + c} (j, c < 4), so the 8 lanes
+// of a row read 128 contiguous bytes per load (conflict-free; the 4 rows of a warp fill
+// the 4 wavefronts a 16-byte warp load needs) and q is a broadcast. The 4 heads
+// accumulate in 4 independent FMA chains. KV: float or __half rows.
 template <class KV>
 __device__ __noinline__ void score_rows(const KV* rows, int nr, int idx0) {
   const float* sq = sm_scratch() + kAttQ;
@@ -938,19 +941,19 @@ __device__ __noinline__ void score_rows(const KV* rows, int nr, int idx0) {
     const bool valid = i < nr;
     const KV* krow = rows + (long long)min(i, nr - 1) * kHeadDim;
     float kf[16];
-    if constexpr (sizeof(KV) == 4) {  // dims [16 li, 16 li + 16)
+    if constexpr (sizeof(KV) == 4) {  // 4 x 16 bytes: dims 4 li + 32 j .. + 3
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const float4 k4 = reinterpret_cast<const float4*>(krow + li * 16)[j];
+        const float4 k4 = *reinterpret_cast<const float4*>(krow + 4 * li + 32 * j);
         kf[4 * j] = k4.x;
         kf[4 * j + 1] = k4.y;
         kf[4 * j + 2] = k4.z;
         kf[4 * j + 3] = k4.w;
       }
-    } else {  // dims [8 li, 8 li + 8) and [64 + 8 li, 64 + 8 li + 8): conflict-free 16-byte loads
+    } else {  // 2 x 16 bytes of halves: dims 8 li + 64 j .. + 7
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
-        const uint4 raw = *reinterpret_cast<const uint4*>(krow + j * kHalfDim + li * 8);
+        const uint4 raw = *reinterpret_cast<const uint4*>(krow + 8 * li + 64 * j);
         const uint32_t wv[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -960,22 +963,27 @@ __device__ __noinline__ void score_rows(const KV* rows, int nr, int idx0) {
         }
       }
     }
-#pragma unroll 1
-    for (int h = 0; h < kHeadsPerKV; ++h) {
-      float d = 0.0f;
+    float d[kHeadsPerKV] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int dim = sizeof(KV) == 4 ? li * 16 + 4 * j : (j >> 1) * kHalfDim + li * 8 + 4 * (j & 1);
+    for (int j = 0; j < 4; ++j) {
+      // the q dims matching kf[4j .. 4j+3]
+      const int dim = sizeof(KV) == 4 ? 4 * li + 32 * j : 8 * li + 64 * (j >> 1) + 4 * (j & 1);
+#pragma unroll
+      for (int h = 0; h < kHeadsPerKV; ++h) {
         const float4 q4 = *reinterpret_cast<const float4*>(sq + h * kHeadDim + dim);
-        d = __fmaf_rn(q4.x, kf[4 * j], d);
-        d = __fmaf_rn(q4.y, kf[4 * j + 1], d);
-        d = __fmaf_rn(q4.z, kf[4 * j + 2], d);
-        d = __fmaf_rn(q4.w, kf[4 * j + 3], d);
+        d[h] = __fmaf_rn(q4.x, kf[4 * j], d[h]);
+        d[h] = __fmaf_rn(q4.y, kf[4 * j + 1], d[h]);
+        d[h] = __fmaf_rn(q4.z, kf[4 * j + 2], d[h]);
+        d[h] = __fmaf_rn(q4.w, kf[4 * j + 3], d[h]);
       }
-      d += __shfl_xor_sync(0xffffffffu, d, 1);
-      d += __shfl_xor_sync(0xffffffffu, d, 2);
-      d += __shfl_xor_sync(0xffffffffu, d, 4);
-      if (valid && li == 0) sc[h * kMaxAttnChunk + idx0 + i] = __fmul_rn(d, scale);
+    }
+#pragma unroll
+    for (int h = 0; h < kHeadsPerKV; ++h) {
+      float v = d[h];
+      v += __shfl_xor_sync(0xffffffffu, v, 1);
+      v += __shfl_xor_sync(0xffffffffu, v, 2);
+      v += __shfl_xor_sync(0xffffffffu, v, 4);
+      if (valid && li == 0) sc[h * kMaxAttnChunk + idx0 + i] = __fmul_rn(v, scale);
     }
   }
 }
@@ -985,14 +993,31 @@ QORA_DEV float kv_elem(const float* p) { return *p; }
 QORA_DEV float kv_elem(const __half* p) { return __half2float(*p); }
 
 // P.V over nr V rows at `rows` for the 4 heads, added to o: thread (grp, d) of three
-// 128-thread groups takes rows grp, grp + 3, ...; probabilities sc[h * kMaxAttnChunk +
-// idx0 + i]. The accumulators travel in registers (argument and result).
+// 128-thread groups takes rows grp, grp + 3, ..., four rows' loads in flight per step;
+// probabilities sc[h * kMaxAttnChunk + idx0 + i]. The accumulators travel in registers
+// (argument and result).
 template <class KV>
 __device__ __noinline__ float4 pv_rows(const KV* rows, int nr, int idx0, int grp, int dd, float4 o) {
   const float* sc = sm_scratch() + kAttS + idx0;
+  const KV* vr = rows + dd;
+  int i = grp;
 #pragma unroll 1
-  for (int i = grp; i < nr; i += 3) {
-    const float v = kv_elem(rows + (long long)i * kHeadDim + dd);
+  for (; i + 9 < nr; i += 12) {
+    float v[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) v[r] = kv_elem(vr + (long long)(i + 3 * r) * kHeadDim);
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int ii = i + 3 * r;
+      o.x = __fmaf_rn(sc[ii], v[r], o.x);
+      o.y = __fmaf_rn(sc[kMaxAttnChunk + ii], v[r], o.y);
+      o.z = __fmaf_rn(sc[2 * kMaxAttnChunk + ii], v[r], o.z);
+      o.w = __fmaf_rn(sc[3 * kMaxAttnChunk + ii], v[r], o.w);
+    }
+  }
+#pragma unroll 1
+  for (; i < nr; i += 3) {
+    const float v = kv_elem(vr + (long long)i * kHeadDim);
     o.x = __fmaf_rn(sc[i], v, o.x);
     o.y = __fmaf_rn(sc[kMaxAttnChunk + i], v, o.y);
     o.z = __fmaf_rn(sc[2 * kMaxAttnChunk + i], v, o.z);
