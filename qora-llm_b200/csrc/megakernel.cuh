@@ -406,7 +406,8 @@ struct Cons {
   volatile int* flags;
   int c, G, tid, lane, warp, pos;
   uint32_t chunk;
-  uint32_t stage_idx;
+  uint32_t stage_idx;     // chunk % kStages and the phase parity of chunk, kept incrementally
+  uint32_t parity;
   bool stage_ok;          // warp-uniform: the current stage landed and the CTA is healthy
 
   QORA_DEV const Args& a() const { return *ap; }
@@ -434,37 +435,42 @@ struct Cons {
     __syncwarp();
     if (lane == 0 && stage_ok) ptx::mbar_arrive(&empty[stage_idx]);
     ++chunk;
+    if (++stage_idx == (uint32_t)kStages) {
+      stage_idx = 0;
+      parity ^= 1u;
+    }
   }
 };
 
-// Wait (bounded) for chunk `chunk` to land in its ring slot: true (warp-uniform) once
-// it has, false if the CTA has aborted or the wait timed out (recorded).
-__device__ __noinline__ bool stage_wait(uint32_t chunk) {
+// The slow path of a stage acquisition (the stage had not landed when first tested):
+// wait (bounded) for ring slot s to complete the phase with the given parity; true
+// (warp-uniform) once it has, false if the CTA has aborted or the wait timed out
+// (recorded). Once the CTA has aborted, stages are skipped without waiting (drain()).
+__device__ __noinline__ bool stage_wait_slow(uint32_t s, uint32_t parity) {
   volatile int* flags = sm_flags();
-  if (__shfl_sync(0xffffffffu, flags[0] != 0, 0)) return false;
-  uint64_t* bar = sm_full() + chunk % kStages;
-  const uint32_t parity = (chunk / kStages) & 1u;
+  uint64_t* bar = sm_full() + s;
   bool timed_out = false;
-  if (!ptx::mbar_try_wait(bar, parity)) {
-    const uint64_t t0 = ptx::globaltimer();
-    while (!ptx::mbar_try_wait(bar, parity)) {
-      if (ptx::globaltimer() - t0 > sm_args()->timeout_ns) {
-        timed_out = true;
-        break;
-      }
+  const uint64_t t0 = ptx::globaltimer();
+  while (!ptx::mbar_try_wait(bar, parity)) {
+    if (flags[0] != 0 || ptx::globaltimer() - t0 > sm_args()->timeout_ns) {
+      timed_out = true;
+      break;
     }
   }
   const bool ok = __all_sync(0xffffffffu, !timed_out);
-  if (!ok && (threadIdx.x & 31) == 0) {
+  if (!ok && (threadIdx.x & 31) == 0 && flags[0] == 0) {
     flags[0] = 1;
     atomicExch(&sm_args()->st->error, 2);
   }
   return ok;
 }
 
+// Fast path inline (one test of the full barrier and a warp vote: a landed stage costs
+// no call, no division and no abort check; a stage only completes while the CTA is
+// healthy or its copy was issued before an abort, which the drain waits for anyway).
 QORA_DEV const uint8_t* Cons::acquire_stage() {
-  stage_idx = chunk % kStages;
-  stage_ok = stage_wait(chunk);
+  stage_ok = __all_sync(0xffffffffu, ptx::mbar_try_wait(&full[stage_idx], parity)) ||
+             stage_wait_slow(stage_idx, parity);
   return ring + (size_t)stage_idx * kStageBytes;
 }
 
@@ -485,7 +491,8 @@ QORA_DEV Cons make_cons(uint32_t chunk) {
   C.warp = threadIdx.x >> 5;
   C.pos = C.flags[2];
   C.chunk = chunk;
-  C.stage_idx = 0;
+  C.stage_idx = chunk % kStages;
+  C.parity = (chunk / kStages) & 1u;
   C.stage_ok = false;
   return C;
 }
@@ -576,14 +583,26 @@ __device__ __noinline__ float poll_vec(const uint64_t* src, int n, uint32_t tag,
 }
 
 // block sum over consumer threads (fixed order), result in every thread
+// Sum of kCW values in a fixed tree order (all loads first; no long dependent chain)
+QORA_DEV float sum15(const float* p, int stride) {
+  float v[kCW];
+#pragma unroll
+  for (int w = 0; w < kCW; ++w) v[w] = p[w * stride];
+#pragma unroll
+  for (int w = 0; w < 7; ++w) v[w] = __fadd_rn(v[2 * w], v[2 * w + 1]);  // 7 pairs, v[14] kept
+  v[7] = v[14];
+#pragma unroll
+  for (int w = 0; w < 4; ++w) v[w] = __fadd_rn(v[2 * w], v[2 * w + 1]);
+  return __fadd_rn(__fadd_rn(v[0], v[1]), __fadd_rn(v[2], v[3]));
+}
+
 __device__ __noinline__ float csum(float v) {
   float* red = sm_scratch() + kOffMisc;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   v = warp_sum(v);
   if (lane == 0) red[warp] = v;
   ptx::named_bar(kBar, kCT);
-  float t = 0.0f;
-  for (int w = 0; w < kCW; ++w) t += red[w];
+  const float t = sum15(red, 1);
   ptx::named_bar(kBar, kCT);
   return t;
 }
@@ -611,8 +630,12 @@ __device__ __noinline__ void fill_norm_inputs(const float* x, float inv, int m) 
   float* xs = sm_scratch();
   const int* P = mat_plan(m);
   ptx::cp_async_wait_all();
-#pragma unroll 1
-  for (int i = threadIdx.x; i < P[0]; i += kCT) xs[i] = __fmul_rn(__fmul_rn(x[span_row(P, i)], inv), xs[i]) * kTwo64;
+  constexpr int kPer = (kXsCap + kCT - 1) / kCT;  // entries per thread (5): independent, unrolled
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int i = threadIdx.x + j * kCT;
+    if (i < P[0]) xs[i] = __fmul_rn(__fmul_rn(x[span_row(P, i)], inv), xs[i]) * kTwo64;
+  }
 }
 
 // Tensor parallelism: this rank's partial value v of column `col` goes to every rank's
@@ -763,12 +786,7 @@ __device__ __noinline__ uint32_t gemv_run(int m, int L, uint32_t chunk) {
       for (int e2 = 0; e2 < (t8 ? 8 : 1); ++e2) dst[e2] = v[e2];
     }
     C.bar();
-    if (C.tid < NO) {
-      float s = 0.0f;
-#pragma unroll 1
-      for (int w = 0; w < kCW; ++w) s += red[w * NO + C.tid];
-      y[C.tid] = s;
-    }
+    if (C.tid < NO) y[C.tid] = sum15(red + C.tid, NO);
     C.bar();
     seg_store(m, L, P[2 + 4 * sg], P[5 + 4 * sg]);
   }
