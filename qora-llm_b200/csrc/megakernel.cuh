@@ -780,13 +780,16 @@ __device__ __noinline__ uint32_t gemv_run(int m, int L, uint32_t chunk) {
         v[e2] = keep + __shfl_xor_sync(0xffffffffu, send, msk);
       }
     }
-    {  // eight-group: 8 outputs per lane at [warp][gi*32 + sub*8]; one-group: 1 at [warp][lane]
-      float* dst = red + C.warp * NO + (t8 ? gi * 32 + sub * 8 : C.lane);
+    // warp w's sums at red[w][e2][lane] (consecutive lanes, consecutive words): output
+    // o = gi*32 + sub*8 + e2 of an eight-group tile sits at e2*32 + sub*8 + gi, output
+    // `lane` of a one-group tile at lane
 #pragma unroll
-      for (int e2 = 0; e2 < (t8 ? 8 : 1); ++e2) dst[e2] = v[e2];
-    }
+    for (int e2 = 0; e2 < (t8 ? 8 : 1); ++e2) red[C.warp * NO + e2 * 32 + C.lane] = v[e2];
     C.bar();
-    if (C.tid < NO) y[C.tid] = sum15(red + C.tid, NO);
+    if (C.tid < NO) {
+      const int o = C.tid;
+      y[o] = sum15(red + (t8 ? (o & 7) * 32 + ((o >> 3) & 3) * 8 + (o >> 5) : o), NO);
+    }
     C.bar();
     seg_store(m, L, P[2 + 4 * sg], P[5 + 4 * sg]);
   }
@@ -1273,7 +1276,22 @@ __device__ __noinline__ void lm_phase(uint32_t chunk) {
   C.bar();
   C.stamp(2 + 8 * kTraceLayers);
   const float inv = rms_inv_from(csum(ss), H);
-  for (int i = C.tid; i < H; i += kCT) sB[i] = __fmul_rn(__fmul_rn(sB[i], inv), a.final_gamma[i]);
+  // normed x into a padded copy (element i at i + i / 64: the 64-element block of lane l
+  // starts at bank l, so the lanes' loads below do not conflict)
+  float* sX = C.scratch;  // XS and the start of B (x is read into registers first)
+  constexpr int kPer = (kXsCap + kCT - 1) / kCT;
+  float xn[kPer];
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int i = C.tid + j * kCT;
+    xn[j] = i < H ? __fmul_rn(__fmul_rn(sB[i], inv), a.final_gamma[i]) : 0.0f;
+  }
+  C.bar();
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int i = C.tid + j * kCT;
+    if (i < H) sX[i + (i >> 6)] = xn[j];
+  }
   C.bar();
   constexpr int EPL = GPL * 32;
   float2 xs2[EPL / 2];
@@ -1283,7 +1301,8 @@ __device__ __noinline__ void lm_phase(uint32_t chunk) {
     float s = 0.0f;
 #pragma unroll
     for (int e = 0; e < 32; ++e) {
-      const float v = sB[lane * EPL + g * 32 + e];
+      const int xi = lane * EPL + g * 32 + e;
+      const float v = sX[xi + (xi >> 6)];
       s += v;
       const int mm = e & 7;
       const int p = (mm < 5) ? 4 * mm : 4 * mm - 12;
