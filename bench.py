@@ -264,6 +264,19 @@ def run_ours(args, rank, world, local_rank):
         dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
     e2e = K / float(e2e_t.item())
 
+    # ---- the prompt pass of the workload's 32-token prompt (host ids in, first token out;
+    # wall clock around the C-ABI call, fresh cache each time, median of 5)
+    pre_ms = []
+    for _ in range(5):
+        kvp = eng.new_kv(cap)
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        t0 = time.perf_counter()
+        eng.prefill(kvp, prompt, want_logits=False)
+        pre_ms.append((time.perf_counter() - t0) * 1000.0)
+        kvp.close()
+
     # ---- dominant kernel. With the persistent step the whole decode step is ONE kernel
     # launch; its algorithmic bytes are the weights + KV rows it must stream.
     peak, peak_kind = peaks()
@@ -307,6 +320,9 @@ def run_ours(args, rank, world, local_rank):
             "bytes_per_step": step_bytes,
             "step_hbm_GBps": step_bytes * (K / (ms / 1000.0)) / 1e9,
             "step_hbm_frac": step_bytes * (K / (ms / 1000.0)) / 1e9 / peak,
+            "prefill_ms": statistics.median(pre_ms),
+            "prefill_in_step_times": statistics.median(pre_ms) / (ms / K),
+            "prefill_path": eng.prefill_path(),
         },
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 32, "d2h_bytes_per_step": 32},
         "gpu_launches": eng.launches_per_step() * K,  # per rank

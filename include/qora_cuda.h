@@ -95,6 +95,10 @@ typedef struct qora_engine_options {
  * persistent single-kernel step (diagnostics and cross-checking). */
 #define QORA_FLAG_PER_OP_KERNELS 1u
 
+/* Q4 engines: run a prompt as one decode step per token instead of the tensor-core
+ * prompt pass (which holds a second copy of the projections, 0.5625 B per weight). */
+#define QORA_FLAG_TOKEN_PREFILL 2u
+
 /* Last error message of the calling thread ("" if none). */
 const char* qora_last_error(void);
 
@@ -347,6 +351,14 @@ qora_status qora_engine_get_trace(qora_engine* engine, uint64_t* out, size_t cap
 
 /* Number of kernel launches one decode step makes (the captured graph's nodes). */
 qora_status qora_engine_launches_per_step(const qora_engine* engine, uint32_t* launches);
+
+/* How qora_prefill runs a prompt of two or more tokens on this engine:
+ * QORA_PROMPT_TENSOR_CORES: all prompt rows at once, layer by layer, through tcgen05 GEMMs
+ * (F16 engines; Q4 engines at tp_size 1 with a binary32 KV cache, unless created with
+ * QORA_FLAG_TOKEN_PREFILL); QORA_PROMPT_TOKEN_STEPS: one decode step per token. */
+#define QORA_PROMPT_TOKEN_STEPS 0u
+#define QORA_PROMPT_TENSOR_CORES 1u
+qora_status qora_engine_prompt_path(const qora_engine* engine, uint32_t* path);
 
 #ifdef __cplusplus
 }

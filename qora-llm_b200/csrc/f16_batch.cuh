@@ -56,6 +56,39 @@ __global__ void __launch_bounds__(128) embed_rows_kernel(const uint8_t* emb_t, i
   }
 }
 
+// Q4 weights: x[m] = E[token[m]] from the row-interleaved Q4 table (row r: hidden/2 nibble
+// bytes, the low nibble the even element, then hidden/32 f16 scales), each element
+// scale * (q - 8) as embed_q4 does (src/gemv.rs:515-526), with the same statistics and
+// counter update as embed_rows_kernel. Grid (hidden / 128, M), 128 threads.
+__global__ void __launch_bounds__(128) embed_rows_q4_kernel(const uint8_t* table, long long row_bytes, int H, int vocab,
+                                                             RowInfo ri, float* x, float* st_ss, float* st_mx,
+                                                             unsigned* epoch) {
+  __shared__ float red[2][4];
+  const int t = blockIdx.x, m = blockIdx.y, i = threadIdx.x;
+  if (t == 0 && m == 0 && i == 0) *epoch += 1u;
+  const int tok = ri.token[m];
+  if (tok < 0 || tok >= vocab) {  // the host validates ids; this keeps the read in bounds
+    if (i == 0 && t == 0) *ri.error = 1;
+    return;
+  }
+  const int k = t * umma::kTileN + i;
+  const uint8_t* row = table + (size_t)tok * row_bytes;
+  const int q = (row[k >> 1] >> (4 * (k & 1))) & 0xF;
+  const float sc = __half2float(reinterpret_cast<const __half*>(row + H / 2)[k / 32]);
+  const float v = __fmul_rn(sc, (float)(q - 8));
+  x[(size_t)m * H + k] = v;
+  float ss = warp_sum(__fmul_rn(v, v)), mx = warp_max(fabsf(v));
+  if ((i & 31) == 0) {
+    red[0][i >> 5] = ss;
+    red[1][i >> 5] = mx;
+  }
+  __syncthreads();
+  if (i == 0) {
+    st_ss[(size_t)t * kMaxRows + m] = __fadd_rn(__fadd_rn(red[0][0], red[0][1]), __fadd_rn(red[0][2], red[0][3]));
+    st_mx[(size_t)t * kMaxRows + m] = fmaxf(fmaxf(red[1][0], red[1][1]), fmaxf(red[1][2], red[1][3]));
+  }
+}
+
 // End of a batched greedy step: each row's greedy token becomes its next input, its
 // position advances, and the token is recorded at ring[step][m].
 __global__ void advance_rows_kernel(int M, umma::RowInfo ri, const unsigned* am, unsigned* ring, int ring_rows) {

@@ -269,8 +269,12 @@ struct qora_engine {
   bool tp_connected = false;
   std::vector<void*> tp_opened;                   // IPC mappings to close
   std::vector<LayerDev> layers;
-  // F16 weights: batched per-op path (f16_batch.cuh)
+  // F16 weights: batched per-op path (f16_batch.cuh). Q4 weights: the same path serves
+  // the prompt pass, its projections held again as Q4 chunks of the dequantising GEMM
   std::vector<F16Layer> fl;
+  bool want_q4p = true;            // not disabled by QORA_FLAG_TOKEN_PREFILL
+  bool q4p = false;                // Q4 prompt pass on the tensor cores available
+  std::string q4p_why;             // why not
   uint8_t* f_lm = nullptr;         // tiled embedding (n = vocab, k = hidden): lookup + tied lm_head
   int f_nqkv = 0;                  // q|k|v columns
   float *f_x = nullptr, *f_qkv = nullptr, *f_attn = nullptr, *f_h = nullptr;  // [rows][...]
@@ -584,6 +588,7 @@ qora_status build_layer(qora_engine* e, const qora_weights_view* w, uint32_t i) 
 }
 
 qora_status mega_init(qora_engine* e);
+qora_status q4_prefill_init(qora_engine* e, const qora_weights_view* w);
 
 qora_status engine_init(qora_engine* e, const qora_weights_view* w) {
   const qora_layer_view& L0 = w->layers[0];
@@ -698,6 +703,7 @@ qora_status engine_init(qora_engine* e, const qora_weights_view* w) {
   QCHECK(e->alloc(&e->lm_counter, 1));
   QCUDA(cudaMemset(e->lm_counter, 0, sizeof(unsigned)));
   QCHECK(mega_init(e));
+  QCHECK(q4_prefill_init(e, w));
   QCUDA(cudaDeviceSynchronize());
   return QORA_OK;
 }
@@ -1097,6 +1103,7 @@ struct UmmaCtx {
   size_t ntcnt;
   unsigned* sync;
   int* err;
+  bool q4 = false;  // weights are Q4 chunks (the dequantising kernel)
 };
 
 // Operand source of one fused GEMM: rows xin [M][ldx], RMSNorm with gamma when set, and
@@ -1125,7 +1132,7 @@ qora_status umma_fused(const UmmaCtx& u, const uint8_t* wt, int N, int K, int M,
   a.chunks = chunks;
   a.M = M;
   a.R = R;
-  a.stages = umma::gemm_stages(R);
+  a.stages = umma::gemm_stages(R, u.q4);
   a.maxseg = p.maxseg;
   a.xin = in.xin;
   a.ldx = in.ldx;
@@ -1142,34 +1149,41 @@ qora_status umma_fused(const UmmaCtx& u, const uint8_t* wt, int N, int K, int M,
   a.timeout_ns = 2000000000ull;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(p.G);
-  cfg.blockDim = dim3(umma::kThreads);
-  cfg.dynamicSmemBytes = umma::gemm_smem(R, a.stages);
+  cfg.blockDim = dim3(u.q4 ? umma::kQ4Threads : umma::kThreads);
+  cfg.dynamicSmemBytes = umma::gemm_smem(R, a.stages, u.q4);
   cfg.stream = u.stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeCooperative;
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  QCUDA(cudaLaunchKernelEx(&cfg, umma::fused_gemm_kernel, a));
+  if (u.q4) {
+    QCUDA(cudaLaunchKernelEx(&cfg, umma::fused_gemm_kernel<true>, a));
+  } else {
+    QCUDA(cudaLaunchKernelEx(&cfg, umma::fused_gemm_kernel<false>, a));
+  }
   return QORA_OK;
 }
 
 // opt the GEMM kernel in to its largest shared-memory footprint and check that one CTA
 // fits on every SM (the cooperative launch needs all CTAs resident)
-qora_status umma_attrs() {
+qora_status umma_attrs(bool q4 = false) {
   int maxsm = 0;
-  for (int r = 8; r <= umma::kMaxRows; r += 8) maxsm = std::max(maxsm, (int)umma::gemm_smem(r, umma::gemm_stages(r)));
-  QCUDA(cudaFuncSetAttribute(umma::fused_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, maxsm));
+  for (int r = 8; r <= umma::kMaxRows; r += 8)
+    maxsm = std::max(maxsm, (int)umma::gemm_smem(r, umma::gemm_stages(r, q4), q4));
+  const void* fn = q4 ? (const void*)umma::fused_gemm_kernel<true> : (const void*)umma::fused_gemm_kernel<false>;
+  QCUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, maxsm));
   int blocks = 0;
-  QCUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, umma::fused_gemm_kernel, umma::kThreads, maxsm));
+  QCUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, fn, q4 ? umma::kQ4Threads : umma::kThreads, maxsm));
   if (blocks < 1) return fail(QORA_ERR_UNSUPPORTED, "tensor-core GEMM does not fit on an SM");
   return QORA_OK;
 }
 
 UmmaCtx umma_ctx(const qora_engine* e) {
   const int V = (int)e->vocab;
-  return UmmaCtx{e->sms, e->stream, e->f_xt, e->f_part, e->f_part_floats, e->f_tcnt,
-                 (size_t)std::max(V, 2 * e->inter_l) / umma::kTileN + 1, e->f_sync, e->f_err};
+  return UmmaCtx{e->sms,  e->stream, e->f_xt, e->f_part, e->f_part_floats, e->f_tcnt,
+                 (size_t)std::max(V, 2 * e->inter_l) / umma::kTileN + 1, e->f_sync, e->f_err,
+                 e->format == QORA_FORMAT_Q4};
 }
 
 // Copy rows [r0, r0 + K) of an f16 matrix view to the device and re-tile them: for a
@@ -1193,6 +1207,48 @@ float max_abs_f16(const uint16_t* h, size_t n) {
   float m = 0.0f;
   for (float v : f16_to_f32(h, n)) m = std::max(m, std::fabs(v));
   return m;
+}
+
+// Row scratch of the batched tensor-core path (activations, GEMM operand and partial
+// slots, statistics, attention partials, counters) for f16b::kMaxRows rows; lmN: lm_head
+// columns run as a fused GEMM (0 when a Q4 engine runs its lm_head as row dots).
+qora_status batched_scratch(qora_engine* e, int lmN) {
+  const int H = (int)e->hidden, V = (int)e->vocab, nq = e->nh_l * kHeadDim, Il = e->inter_l;
+  const size_t R = f16b::kMaxRows;
+  size_t slots = 0;  // partial slots of the largest GEMM plan, in [R][128] blocks
+  const int gn[5] = {e->f_nqkv, H, 2 * Il, H, lmN}, gk[5] = {H, nq, H, Il, H};
+  for (int j = 0; j < 5; ++j) {
+    const UmmaPlan p = umma_plan(e->sms, gn[j] / umma::kTileN, gk[j] / umma::kChunkK);
+    slots = std::max(slots, (size_t)p.G * p.maxseg);
+  }
+  const size_t kmax = (size_t)std::max(std::max(H, nq), Il);
+  e->f_part_floats = slots * R * umma::kTileN;
+  QCHECK(e->alloc(&e->f_part, e->f_part_floats));
+  QCHECK(e->alloc(&e->f_x, R * H));
+  QCHECK(e->alloc(&e->f_qkv, R * e->f_nqkv));
+  QCHECK(e->alloc(&e->f_attn, R * nq));
+  QCHECK(e->alloc(&e->f_h, R * Il));
+  QCHECK(e->alloc(&e->f_xt, kmax * R * 2 * 2));
+  QCHECK(e->alloc(&e->f_xss, (size_t)(H / umma::kTileN) * R));
+  QCHECK(e->alloc(&e->f_xmx, (size_t)(H / umma::kTileN) * R));
+  QCHECK(e->alloc(&e->f_hmx, (size_t)(Il / 64) * R));
+  QCHECK(e->alloc(&e->f_amx, (size_t)e->nkv * R));
+  QCHECK(e->alloc(&e->f_att_part, R * e->nkv * f16b::kAttSplits * 4 * kHeadDim));
+  QCHECK(e->alloc(&e->f_att_ml, R * e->nkv * f16b::kAttSplits * 4 * 2));
+  QCHECK(e->alloc(&e->f_att_cnt, R * e->nkv));
+  QCUDA(cudaMemset(e->f_att_cnt, 0, R * e->nkv * sizeof(unsigned)));
+  const size_t ntc = (size_t)std::max(V, 2 * Il) / umma::kTileN + 1;
+  QCHECK(e->alloc(&e->f_tcnt, ntc));
+  QCUDA(cudaMemset(e->f_tcnt, 0, ntc * sizeof(unsigned)));
+  QCHECK(e->alloc(&e->f_sync, 4));
+  QCUDA(cudaMemset(e->f_sync, 0, 4 * sizeof(unsigned)));
+  QCHECK(e->alloc(&e->f_amkey, R));
+  QCUDA(cudaMemset(e->f_amkey, 0, R * sizeof(unsigned long long)));
+  QCHECK(e->alloc(&e->f_err, 1));
+  QCUDA(cudaMemset(e->f_err, 0, sizeof(int)));
+  QCHECK(e->alloc(&e->f_epoch, 1));
+  QCUDA(cudaMemset(e->f_epoch, 0, sizeof(unsigned)));
+  return QORA_OK;
 }
 
 // Upload the F16 weights (exact copies; q|k|v and gate|up joined along n) and size the
@@ -1281,41 +1337,8 @@ qora_status f16_engine_init(qora_engine* e, const qora_weights_view* w) {
   QCHECK(upload(e, e->rope_cos, w->rope_cos, rt * 4));
   QCHECK(upload(e, e->rope_sin, w->rope_sin, rt * 4));
 
+  QCHECK(batched_scratch(e, (e->f_vt1 - e->f_vt0) * TN));
   const size_t R = f16b::kMaxRows;
-  size_t slots = 0;  // partial slots of the largest GEMM plan, in [R][128] blocks
-  const int lmN = (e->f_vt1 - e->f_vt0) * TN;
-  const int gn[5] = {e->f_nqkv, H, 2 * Il, H, lmN}, gk[5] = {H, nq, H, Il, H};
-  for (int j = 0; j < 5; ++j) {
-    const UmmaPlan p = umma_plan(e->sms, gn[j] / umma::kTileN, gk[j] / umma::kChunkK);
-    slots = std::max(slots, (size_t)p.G * p.maxseg);
-  }
-  const size_t kmax = (size_t)std::max(std::max(H, nq), Il);
-  e->f_part_floats = slots * R * umma::kTileN;
-  QCHECK(e->alloc(&e->f_part, e->f_part_floats));
-  QCHECK(e->alloc(&e->f_x, R * H));
-  QCHECK(e->alloc(&e->f_qkv, R * e->f_nqkv));
-  QCHECK(e->alloc(&e->f_attn, R * nq));
-  QCHECK(e->alloc(&e->f_h, R * Il));
-  QCHECK(e->alloc(&e->f_xt, kmax * R * 2 * 2));
-  QCHECK(e->alloc(&e->f_xss, (size_t)(H / umma::kTileN) * R));
-  QCHECK(e->alloc(&e->f_xmx, (size_t)(H / umma::kTileN) * R));
-  QCHECK(e->alloc(&e->f_hmx, (size_t)(Il / 64) * R));
-  QCHECK(e->alloc(&e->f_amx, (size_t)e->nkv * R));
-  QCHECK(e->alloc(&e->f_att_part, R * e->nkv * f16b::kAttSplits * 4 * kHeadDim));
-  QCHECK(e->alloc(&e->f_att_ml, R * e->nkv * f16b::kAttSplits * 4 * 2));
-  QCHECK(e->alloc(&e->f_att_cnt, R * e->nkv));
-  QCUDA(cudaMemset(e->f_att_cnt, 0, R * e->nkv * sizeof(unsigned)));
-  const size_t ntc = (size_t)std::max(V, 2 * Il) / umma::kTileN + 1;
-  QCHECK(e->alloc(&e->f_tcnt, ntc));
-  QCUDA(cudaMemset(e->f_tcnt, 0, ntc * sizeof(unsigned)));
-  QCHECK(e->alloc(&e->f_sync, 4));
-  QCUDA(cudaMemset(e->f_sync, 0, 4 * sizeof(unsigned)));
-  QCHECK(e->alloc(&e->f_amkey, R));
-  QCUDA(cudaMemset(e->f_amkey, 0, R * sizeof(unsigned long long)));
-  QCHECK(e->alloc(&e->f_err, 1));
-  QCUDA(cudaMemset(e->f_err, 0, sizeof(int)));
-  QCHECK(e->alloc(&e->f_epoch, 1));
-  QCUDA(cudaMemset(e->f_epoch, 0, sizeof(unsigned)));
   if (T > 1) {
     // receive region (IPC-exported): o_proj and down partial tiles of every rank, the
     // ranks' lm_head candidates, and the full logits
@@ -1333,6 +1356,100 @@ qora_status f16_engine_init(qora_engine* e, const qora_weights_view* w) {
   e->logits = e->f_logits;
   QCHECK(umma_attrs());
   QCUDA(cudaDeviceSynchronize());
+  return QORA_OK;
+}
+
+// Rows [r0, r0 + K) of a Q4 matrix view to the device (tmp_p / tmp_s), re-tiled as
+// dequantisation chunks: column col0 + n -> tile t0 + n / group, channel o0 + n % group.
+qora_status q4_chunk_upload(const qora_matrix_view& m, uint64_t r0, int K, int col0, int N, int t0, int group,
+                            int o0, int chunks, uint8_t* dst, uint8_t* tmp_p, uint16_t* tmp_s, int sms) {
+  QCUDA(cudaMemcpy(tmp_p, m.packed + r0 * (m.n / 2), (size_t)K * (m.n / 2), cudaMemcpyHostToDevice));
+  QCUDA(cudaMemcpy(tmp_s, m.scales + r0 * (m.n / kGroup), (size_t)K * (m.n / kGroup) * 2, cudaMemcpyHostToDevice));
+  const long long units = (long long)N * (K / 8);
+  const int blocks = (int)std::min<long long>((units + 255) / 256, 16LL * sms);
+  umma::tile_q4_kernel<<<blocks, 256>>>(tmp_p, tmp_s, (long long)m.n, K, N, col0, t0, group, o0, chunks, dst);
+  QCUDA(cudaGetLastError());
+  QCUDA(cudaDeviceSynchronize());
+  return QORA_OK;
+}
+
+// The Q4 prompt pass on the tensor cores (raw_prefill, src/gemv.rs:1027-1190, with
+// gemm_q4 :680-706): the batched path's layer loop over all prompt rows, each projection
+// a dequantising tcgen05 GEMM over a second, chunked copy of its Q4 weights (0.5625 B per
+// weight, 1.6 GB for SmolLM3-3B), the lm_head the decode step's row-dot kernel on the last
+// row. Not set up (prompts then run as decode steps) for tensor-parallel shards, on
+// request (QORA_FLAG_TOKEN_PREFILL), when the shapes do not tile, or when a scale times 8
+// would overflow binary16.
+qora_status q4_prefill_init(qora_engine* e, const qora_weights_view* w) {
+  e->q4p = false;
+  const int H = (int)e->hidden, I = (int)e->inter, nq = (int)e->nh * kHeadDim, nkvw = (int)e->nkv_total * kHeadDim;
+  if (!e->want_q4p) {
+    e->q4p_why = "disabled by QORA_FLAG_TOKEN_PREFILL";
+    return QORA_OK;
+  }
+  if (e->tp > 1) {
+    e->q4p_why = "tensor-parallel shard";
+    return QORA_OK;
+  }
+  if (H % umma::kTileN || I % 64 || nq % umma::kTileN || nq > 8192 || I > 65536 ||
+      (H != 1024 && H != 2048 && H != 3072 && H != 4096)) {
+    e->q4p_why = "shapes do not tile";
+    return QORA_OK;
+  }
+  // |q - 8| * |s| <= 8 |s| must stay finite in binary16: |s| <= 8188 (bits <= 0x6FFF)
+  for (uint32_t i = 0; i < e->num_layers; ++i) {
+    const qora_layer_view& L = w->layers[i];
+    for (const qora_matrix_view* m : {&L.q_proj, &L.k_proj, &L.v_proj, &L.o_proj, &L.gate_proj, &L.up_proj,
+                                      &L.down_proj}) {
+      const size_t ns = (size_t)m->k * (m->n / kGroup);
+      for (size_t j = 0; j < ns; ++j)
+        if ((m->scales[j] & 0x7FFFu) > 0x6FFFu) {
+          e->q4p_why = "a Q4 scale beyond 8188";
+          return QORA_OK;
+        }
+    }
+  }
+  constexpr int TN = umma::kTileN, CK = umma::kChunkK;
+  const size_t CH = umma::kQ4Chunk;
+  const size_t maxk = (size_t)std::max(H, std::max(nq, I)), maxn = (size_t)std::max(std::max(H, nq), I);
+  uint8_t* tmp_p = nullptr;
+  uint16_t* tmp_s = nullptr;
+  QCUDA(cudaMalloc(&tmp_p, maxk * maxn / 2));
+  QCUDA(cudaMalloc(&tmp_s, maxk * (maxn / kGroup) * 2));
+  struct TmpFree {
+    void *a, *b;
+    ~TmpFree() {
+      cudaFree(a);
+      cudaFree(b);
+    }
+  } tmp_free{tmp_p, tmp_s};
+  e->f_nqkv = nq + 2 * nkvw;
+  e->fl.assign(e->num_layers, F16Layer{});
+  for (uint32_t i = 0; i < e->num_layers; ++i) {
+    const qora_layer_view& L = w->layers[i];
+    F16Layer& d = e->fl[i];
+    const LayerDev& ld = e->layers[i];
+    QCHECK(e->alloc(&d.wqkv, (size_t)(e->f_nqkv / TN) * (H / CK) * CH));
+    QCHECK(q4_chunk_upload(L.q_proj, 0, H, 0, nq, 0, TN, 0, H / CK, d.wqkv, tmp_p, tmp_s, e->sms));
+    QCHECK(q4_chunk_upload(L.k_proj, 0, H, 0, nkvw, nq / TN, TN, 0, H / CK, d.wqkv, tmp_p, tmp_s, e->sms));
+    QCHECK(q4_chunk_upload(L.v_proj, 0, H, 0, nkvw, (nq + nkvw) / TN, TN, 0, H / CK, d.wqkv, tmp_p, tmp_s, e->sms));
+    QCHECK(e->alloc(&d.wo, (size_t)(H / TN) * (nq / CK) * CH));
+    QCHECK(q4_chunk_upload(L.o_proj, 0, nq, 0, H, 0, TN, 0, nq / CK, d.wo, tmp_p, tmp_s, e->sms));
+    // gate|up per tile: channels 0-63 gate 64t.., 64-127 the same up columns
+    QCHECK(e->alloc(&d.wgu, (size_t)(I / 64) * (H / CK) * CH));
+    QCHECK(q4_chunk_upload(L.gate_proj, 0, H, 0, I, 0, 64, 0, H / CK, d.wgu, tmp_p, tmp_s, e->sms));
+    QCHECK(q4_chunk_upload(L.up_proj, 0, H, 0, I, 0, 64, 64, H / CK, d.wgu, tmp_p, tmp_s, e->sms));
+    QCHECK(e->alloc(&d.wdown, (size_t)(H / TN) * (I / CK) * CH));
+    QCHECK(q4_chunk_upload(L.down_proj, 0, I, 0, H, 0, TN, 0, I / CK, d.wdown, tmp_p, tmp_s, e->sms));
+    d.g_in = ld.g_in;
+    d.g_post = ld.g_post;
+    d.gmax_in = max_abs_f16(L.input_norm_gamma, H);
+    d.gmax_post = max_abs_f16(L.post_attn_norm_gamma, H);
+    d.rope = ld.rope;
+  }
+  QCHECK(batched_scratch(e, 0));
+  QCHECK(umma_attrs(true));
+  e->q4p = true;
   return QORA_OK;
 }
 
@@ -1369,7 +1486,13 @@ qora_status f16_forward(qora_engine* e, qora_kv* kv, int M, int lm0) {
   cudaStream_t s = e->stream;
   const UmmaCtx u = umma_ctx(e);
   const int xt_n = H / umma::kTileN;
-  f16b::embed_rows_kernel<<<dim3(xt_n, M), 128, 0, s>>>(e->f_lm, H, V, ri, e->f_x, e->f_xss, e->f_xmx, e->f_epoch);
+  const bool q4 = e->format == QORA_FORMAT_Q4;
+  if (q4) {
+    f16b::embed_rows_q4_kernel<<<dim3(xt_n, M), 128, 0, s>>>(e->lm_table, e->lm_row_bytes, H, V, ri, e->f_x, e->f_xss,
+                                                              e->f_xmx, e->f_epoch);
+  } else {
+    f16b::embed_rows_kernel<<<dim3(xt_n, M), 128, 0, s>>>(e->f_lm, H, V, ri, e->f_x, e->f_xss, e->f_xmx, e->f_epoch);
+  }
   QCUDA(cudaGetLastError());
   const long long hs = (long long)kv->max_seq * kHeadDim, ss = (long long)kv->seq_stride();
   for (uint32_t li = 0; li < e->num_layers; ++li) {
@@ -1439,7 +1562,24 @@ qora_status f16_forward(qora_engine* e, qora_kv* kv, int M, int lm0) {
     f16_tp_args(e, a, 2 * (int)li + 2, e->tp_off_d);
     QCHECK(umma_fused(u, d.wdown, H, I, M, UmmaIn{e->f_h, I, nullptr, 0.0f, nullptr, e->f_hmx, I / 64}, a));
   }
-  if (lm0 < M) {
+  if (lm0 < M && q4) {
+    // Q4 (prompt pass): final RMSNorm + tied lm_head + greedy argmax of the last row, the
+    // decode step's kernel over the Q4 table
+    if (lm0 != M - 1) return fail(QORA_ERR_INVALID, "Q4 prompt pass: logits of the last row only");
+    LmArgs la{};
+    la.x = e->f_x + (size_t)(M - 1) * H;
+    la.gamma = e->final_gamma;
+    la.packed = e->lm_table;
+    la.scales = e->lm_table + H / 2;
+    la.row_stride_p = la.row_stride_s = e->lm_row_bytes;
+    la.vocab = V;
+    la.logits = e->logits;
+    la.argmax_out = &kv->st->argmax;
+    la.part_v = e->lm_part_v;
+    la.part_i = e->lm_part_i;
+    la.counter = e->lm_counter;
+    QCHECK(launch_lm_head(H, la, e->lm_ctas, s));
+  } else if (lm0 < M) {
     // final RMSNorm + tied lm_head + greedy argmax for rows [lm0, M)
     umma::FusedArgs a{};
     a.ep = umma::kEpLogits;
@@ -1629,6 +1769,39 @@ qora_status f16_prefill(qora_engine* e, qora_kv* kv, const uint32_t* ids, uint32
   if (argmax) QCUDA(cudaMemcpyAsync(argmax, kv->f_argmax, 4, cudaMemcpyDeviceToHost, e->stream));
   QCHECK(f16_check_error(e, kv));
   for (uint32_t l = 0; l < e->num_layers; ++l) kv->lenof(seq, l) = len + n;
+  return QORA_OK;
+}
+
+// Q4 prompt of n >= 2 tokens on the tensor cores (q4_prefill_init): chunks of up to
+// f16b::kMaxRows rows through the batched layer loop; the lm_head runs on the prompt's last
+// row only. Leaves the step state as the token-by-token prefill does (pos = len + n,
+// argmax = the greedy next token).
+qora_status q4_prefill(qora_engine* e, qora_kv* kv, const uint32_t* ids, uint32_t n, float* logits,
+                       uint32_t* argmax) {
+  uint32_t len = 0;
+  QCHECK(check_uniform_len(kv, &len));
+  if ((uint64_t)len + n > kv->max_seq)
+    return fail(QORA_ERR_RANGE, "prompt of %u after %u positions exceeds max_seq %u", n, len, kv->max_seq);
+  QCUDA(cudaSetDevice(e->device));
+  if (!kv->rows) {
+    QCHECK(kv->alloc(&kv->rows, f16b::kRowInts));
+    QCUDA(cudaMemset(kv->rows, 0, f16b::kRowInts * sizeof(int)));
+    QCUDA(cudaMallocHost(&kv->rows_host, f16b::kRowInts * sizeof(int)));
+    std::memset(kv->rows_host, 0, f16b::kRowInts * sizeof(int));
+  }
+  QCUDA(cudaMemcpyAsync(kv->ids, ids, (size_t)n * 4, cudaMemcpyHostToDevice, e->stream));
+  QCHECK(set_state(e, kv, (int)(len + n), (int)ids[n - 1], 0));
+  for (uint32_t c0 = 0; c0 < n; c0 += f16b::kMaxRows) {
+    const int c = (int)std::min<uint32_t>(f16b::kMaxRows, n - c0);
+    f16_prompt_rows_kernel<<<1, f16b::kMaxRows, 0, e->stream>>>(kv->rows, kv->ids + c0, c, 0, (int)(len + c0));
+    QCUDA(cudaGetLastError());
+    QCHECK(f16_forward(e, kv, c, c0 + c == n ? c - 1 : c));
+  }
+  QCUDA(cudaMemcpyAsync(kv->st_host, kv->st, sizeof(StepState), cudaMemcpyDeviceToHost, e->stream));
+  if (logits) QCUDA(cudaMemcpyAsync(logits, e->logits, (size_t)e->vocab * 4, cudaMemcpyDeviceToHost, e->stream));
+  QCHECK(f16_check_error(e, kv));
+  if (argmax) *argmax = kv->st_host->argmax;
+  for (auto& l : kv->len) l = len + n;
   return QORA_OK;
 }
 
@@ -1879,7 +2052,7 @@ qora_status qora_engine_create(const qora_weights_view* weights, const qora_engi
                 "single-process multi-GPU engines (n_gpus=%d) are not in this build; use tp_size/tp_rank with "
                 "one engine per GPU",
                 n_gpus);
-  if (opts && (opts->flags & ~QORA_FLAG_PER_OP_KERNELS))
+  if (opts && (opts->flags & ~(QORA_FLAG_PER_OP_KERNELS | QORA_FLAG_TOKEN_PREFILL)))
     return fail(QORA_ERR_INVALID, "unknown option flags 0x%x", opts->flags);
   const int tp = (opts && opts->tp_size > 1) ? opts->tp_size : 1, rank = (opts && tp > 1) ? opts->tp_rank : 0;
   if (tp != 1 && tp != 2 && tp != 4 && tp != 8) return fail(QORA_ERR_INVALID, "tp_size %d (1, 2, 4 or 8)", tp);
@@ -1896,6 +2069,7 @@ qora_status qora_engine_create(const qora_weights_view* weights, const qora_engi
   e->tp = tp;
   e->rank = rank;
   e->use_mega = !(opts && (opts->flags & QORA_FLAG_PER_OP_KERNELS));
+  e->want_q4p = !(opts && (opts->flags & QORA_FLAG_TOKEN_PREFILL));
   if (weights->format == QORA_FORMAT_F16)
     QCHECK(f16_engine_init(e.get(), weights));
   else
@@ -2220,6 +2394,7 @@ qora_status qora_prefill(qora_engine* e, qora_kv* kv, const uint32_t* ids, uint3
   for (uint32_t i = 0; i < n; ++i)
     if (ids[i] >= e->vocab) return fail(QORA_ERR_RANGE, "token %u at %u >= vocab %u", ids[i], i, e->vocab);
   if (e->format == QORA_FORMAT_F16) return f16_prefill(e, kv, ids, n, seq_idx, logits_or_null, argmax_out);
+  if (e->q4p && n >= 2 && kv->dtype == QORA_KV_F32) return q4_prefill(e, kv, ids, n, logits_or_null, argmax_out);
   uint32_t len = 0;
   QCHECK(check_uniform_len(kv, &len));
   if ((uint64_t)len + n > kv->max_seq)
@@ -2439,6 +2614,12 @@ qora_status qora_engine_launches_per_step(const qora_engine* e, uint32_t* launch
     *launches = (uint32_t)f16_launches(e, true);
   else
     *launches = (e->mk_ok && e->use_mega) ? 1u : 1 + 5 * e->num_layers + 2;
+  return QORA_OK;
+}
+
+qora_status qora_engine_prompt_path(const qora_engine* e, uint32_t* path) {
+  if (!e || !path) return fail(QORA_ERR_INVALID, "NULL argument");
+  *path = (e->format == QORA_FORMAT_F16 || e->q4p) ? QORA_PROMPT_TENSOR_CORES : QORA_PROMPT_TOKEN_STEPS;
   return QORA_OK;
 }
 

@@ -30,6 +30,15 @@
 // warps 2-5 drain the accumulators and finish tiles. Every wait is bounded (globaltimer):
 // on a timeout the CTA sets *err, stops issuing, waits for its copies and MMAs in flight,
 // frees its TMEM and returns.
+//
+// Q4 weights (the Q4 prompt pass, gemm_q4 of src/gemv.rs:680-706). The weights stay Q4
+// in HBM (0.5625 B per weight): each stage's bulk copy brings a 4.5 KB chunk of nibbles
+// and f16 scales, and four more warps (320 threads) dequantise it into two f16 tiles in
+// shared memory, hi = f16((q - 8) * s) and lo = (q - 8) * s - hi. The product of a 4-bit
+// integer and an f16 scale has at most 15 significant bits, so hi + lo is the weight
+// exactly (lo is a multiple of the scale's ulp, which f16 holds down to its subnormals);
+// the MMA issuer runs both tiles against the same operand, so the accumulator receives
+// (hi + lo) . x with x to ~22 bits, as for f16 weights.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -46,6 +55,13 @@ constexpr int kATile = kTileN * kChunkK * 2;  // 16 KB of weights per stage
 constexpr int kThreads = 192;
 constexpr int kMaxRows = 128;                // R <= 128 (N = 2R <= 256)
 constexpr int kSmemBudget = 200 * 1024;
+// Q4 weights: one chunk (128 channels x 64 k) = nibble words [1024] (word p holds the 8 k
+// of the 16-byte unit p of the f16 tile, see q4_unit) + f16 scales [4 channel groups of
+// 32][64 k]
+constexpr int kQ4Words = kTileN * kChunkK / 8;
+constexpr int kQ4Chunk = kQ4Words * 4 + 4 * kChunkK * 2;
+constexpr int kQ4Slot = 5 * 1024;            // its stage slot (stages stay 1 KB aligned)
+constexpr int kQ4Threads = kThreads + 128;   // + 4 dequantising warps
 
 // byte offset of element (r, k) of a [rows][64] f16 chunk tile
 __host__ __device__ constexpr int tile_off(int r, int k) {
@@ -185,13 +201,20 @@ struct FusedArgs {
   unsigned long long timeout_ns;
 };
 
-__host__ __device__ constexpr uint32_t stage_bytes(int R) { return (uint32_t)kATile + (uint32_t)R * 256u; }
+// Stage of the f16 kernel: weight tile [kATile] | operand [R * 256]. Stage of the Q4
+// kernel: weight tile hi [kATile] | lo [kATile] | operand [R * 256] | Q4 chunk [kQ4Chunk]
+// (the chunk and the operand arrive by bulk copy; the dequantising warps fill hi and lo).
+__host__ __device__ constexpr uint32_t stage_bytes(int R, bool q4 = false) {
+  return q4 ? 2u * kATile + (uint32_t)R * 256u + (uint32_t)kQ4Slot : (uint32_t)kATile + (uint32_t)R * 256u;
+}
 __host__ __device__ constexpr uint32_t tmem_cols(int R) {
   return 4 * R <= 32 ? 32u : 4 * R <= 64 ? 64u : 4 * R <= 128 ? 128u : 4 * R <= 256 ? 256u : 512u;
 }
-inline size_t gemm_smem(int R, int stages) { return (size_t)stages * stage_bytes(R) + (2 * stages + 5) * 8 + 16; }
-inline int gemm_stages(int R) {
-  const int s = (int)((kSmemBudget - 128) / stage_bytes(R));
+inline size_t gemm_smem(int R, int stages, bool q4 = false) {
+  return (size_t)stages * stage_bytes(R, q4) + ((q4 ? 3 : 2) * stages + 5) * 8 + 16;
+}
+inline int gemm_stages(int R, bool q4 = false) {
+  const int s = (int)((kSmemBudget - 128) / stage_bytes(R, q4));
   return s < 2 ? 2 : (s > 8 ? 8 : s);
 }
 
@@ -496,7 +519,44 @@ QORA_DEV void finish_tile(const FusedArgs& a, int t, long long* s_cb) {
   }
 }
 
-__global__ void __launch_bounds__(kThreads, 1) fused_gemm_kernel(const FusedArgs a) {
+QORA_DEV __half2 u32_h2(uint32_t v) {
+  __half2 h;
+  memcpy(&h, &v, 4);
+  return h;
+}
+QORA_DEV uint32_t h2_u32(__half2 h) {
+  uint32_t v;
+  memcpy(&v, &h, 4);
+  return v;
+}
+
+// Unit p (0..1023) of a Q4 chunk: the 16-byte row segment at byte 16p of the f16 tile,
+// i.e. channel o = 8 (p >> 6) + (p & 7), k = 8 ((p >> 3) & 7) + [0, 8). Its nibbles are
+// word p (bits 4j..4j+3: k = 2j, bits 16+4j..16+4j+3: k = 2j+1, so one mask per pair
+// gives a half2), its scales the 8 f16 of channel group p >> 8 at those k. 1024 + q is
+// exact in f16 (0x6400 | q), and so is q - 8; hi is the f16 rounding of (q - 8) s (one
+// rounding, no contraction) and lo = (q - 8) s - hi comes exact out of one fused
+// multiply-add.
+QORA_DEV void q4_unit(const uint8_t* chunk, int p, uint4& hv, uint4& lv) {
+  const uint32_t w = reinterpret_cast<const uint32_t*>(chunk)[p];
+  const uint4 sv = *reinterpret_cast<const uint4*>(chunk + kQ4Words * 4 + (p >> 8) * 128 + ((p >> 3) & 7) * 16);
+  const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w};
+  const __half2 bias = u32_h2(0x64086408u);  // 1032
+  uint32_t h[4], l[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const __half2 q = __hsub2(u32_h2(((w >> (4 * j)) & 0x000F000Fu) | 0x64006400u), bias);
+    const __half2 s = u32_h2(sw[j]);
+    const __half2 hi = __hmul2_rn(q, s);
+    h[j] = h2_u32(hi);
+    l[j] = h2_u32(__hfma2(q, s, __hneg2(hi)));
+  }
+  hv = make_uint4(h[0], h[1], h[2], h[3]);
+  lv = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+template <bool Q4>
+__global__ void __launch_bounds__(Q4 ? kQ4Threads : kThreads, 1) fused_gemm_kernel(const FusedArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint32_t s_tmem;
   __shared__ int s_abort, s_last, s_eok[4];
@@ -504,12 +564,18 @@ __global__ void __launch_bounds__(kThreads, 1) fused_gemm_kernel(const FusedArgs
   __shared__ long long s_cb[kMaxContrib];
   const int S = a.stages, R = a.R, C = a.chunks, M = a.M;
   const int K = C * kChunkK;
-  const uint32_t SB = stage_bytes(R);
+  const uint32_t SB = stage_bytes(R, Q4);
+  // stage layout: weights (f16: the tile; Q4: hi and lo tiles) | operand | (Q4 chunk)
+  const uint32_t OFF_B = Q4 ? 2u * kATile : (uint32_t)kATile;
+  const uint32_t OFF_W = Q4 ? OFF_B + (uint32_t)R * 256u : 0u;  // where the weight copy lands
+  const uint32_t WB = Q4 ? (uint32_t)kQ4Chunk : (uint32_t)kATile;  // weight bytes per unit
+  const uint32_t CB = WB + (uint32_t)R * 256u;                      // bytes copied per stage
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * SB);
   uint64_t* empty = full + S;
-  uint64_t* accf = empty + S;  // [2] accumulator ready
-  uint64_t* acce = accf + 2;   // [2] accumulator drained
-  uint64_t* fin = acce + 2;    // all MMAs complete
+  uint64_t* dq = empty + S;             // Q4: [S] tiles dequantised (4 warp arrivals)
+  uint64_t* accf = dq + (Q4 ? S : 0);  // [2] accumulator ready
+  uint64_t* acce = accf + 2;            // [2] accumulator drained
+  uint64_t* fin = acce + 2;             // all MMAs complete
   volatile int* abort = &s_abort;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t ncols = tmem_cols(R);
@@ -520,6 +586,7 @@ __global__ void __launch_bounds__(kThreads, 1) fused_gemm_kernel(const FusedArgs
     for (int s = 0; s < S; ++s) {
       ptx::mbar_init(&full[s], 1);
       ptx::mbar_init(&empty[s], 1);
+      if (Q4) ptx::mbar_init(&dq[s], 4);
     }
     ptx::mbar_init(&accf[0], 1);
     ptx::mbar_init(&accf[1], 1);
@@ -576,8 +643,8 @@ __global__ void __launch_bounds__(kThreads, 1) fused_gemm_kernel(const FusedArgs
   if (threadIdx.x == 0) {
     for (int i = 0; i < pre; ++i) {
       const long long u = b0 + i, t = u / C, c = u % C;
-      ptx::mbar_arrive_expect_tx(&full[i], SB);
-      ptx::bulk_g2s(smem + (size_t)i * SB, a.w + ((size_t)t * C + c) * kATile, kATile, &full[i]);
+      ptx::mbar_arrive_expect_tx(&full[i], CB);
+      ptx::bulk_g2s(smem + (size_t)i * SB + OFF_W, a.w + ((size_t)t * C + c) * WB, WB, &full[i]);
     }
   }
   // this CTA's slice of the operand: units (chunk c, row r, 8 k) in that order
@@ -623,7 +690,7 @@ __global__ void __launch_bounds__(kThreads, 1) fused_gemm_kernel(const FusedArgs
       long long issued = pre;
       for (int i = 0; i < pre; ++i) {  // issued even after an abort, so those stages complete
         const long long c = (b0 + i) % C;
-        ptx::bulk_g2s(smem + (size_t)i * SB + kATile, a.xt + (size_t)c * R * 256, (uint32_t)R * 256, &full[i]);
+        ptx::bulk_g2s(smem + (size_t)i * SB + OFF_B, a.xt + (size_t)c * R * 256, (uint32_t)R * 256, &full[i]);
       }
       for (long long u = b0 + pre; u < b1 && !*abort; ++u, ++issued) {
         const int s = (int)(issued % S);
@@ -631,9 +698,9 @@ __global__ void __launch_bounds__(kThreads, 1) fused_gemm_kernel(const FusedArgs
         if (!wait_bar(&empty[s], (k - 1) & 1, lim, abort)) break;
         const long long t = u / C, c = u % C;
         uint8_t* st = smem + (size_t)s * SB;
-        ptx::mbar_arrive_expect_tx(&full[s], SB);
-        ptx::bulk_g2s(st, a.w + ((size_t)t * C + c) * kATile, kATile, &full[s]);
-        ptx::bulk_g2s(st + kATile, a.xt + (size_t)c * R * 256, (uint32_t)R * 256, &full[s]);
+        ptx::mbar_arrive_expect_tx(&full[s], CB);
+        ptx::bulk_g2s(st + OFF_W, a.w + ((size_t)t * C + c) * WB, WB, &full[s]);
+        ptx::bulk_g2s(st + OFF_B, a.xt + (size_t)c * R * 256, (uint32_t)R * 256, &full[s]);
       }
       // copies still in flight land before the CTA can exit
       const long long first = issued > S ? issued - S : 0;
@@ -658,15 +725,19 @@ __global__ void __launch_bounds__(kThreads, 1) fused_gemm_kernel(const FusedArgs
         bool ok = true;
         for (const long long u0 = u; u < e; ++u, ++i) {
           const int s = (int)(i % S);
-          if (!wait_bar(&full[s], (uint32_t)(i / S) & 1, lim, abort)) {
+          const uint32_t ph = (uint32_t)(i / S) & 1;
+          // Q4: the operand copy (full) and the dequantised tiles (dq) both
+          if (!wait_bar(&full[s], ph, lim, abort) || (Q4 && !wait_bar(&dq[s], ph, lim, abort))) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t sa = sbase + (uint32_t)s * SB, sb = sa + kATile;
+          const uint32_t sa = sbase + (uint32_t)s * SB, sb = sa + OFF_B;
 #pragma unroll
-          for (int k16 = 0; k16 < kChunkK / 16; ++k16)
+          for (int k16 = 0; k16 < kChunkK / 16; ++k16) {
             mma_f16(d, smem_desc(sa + k16 * 256), smem_desc(sb + k16 * 256), idesc, (u > u0 || k16 > 0) ? 1u : 0u);
+            if (Q4) mma_f16(d, smem_desc(sa + kATile + k16 * 256), smem_desc(sb + k16 * 256), idesc, 1u);
+          }
           mma_commit(&empty[s]);
         }
         if (!ok) break;
@@ -676,6 +747,30 @@ __global__ void __launch_bounds__(kThreads, 1) fused_gemm_kernel(const FusedArgs
       mma_commit(fin);
       volatile int no_abort = 0;
       wait_bar(fin, 0, lim, &no_abort);
+    }
+  } else if (Q4 && warp >= 6) {
+    // ---- dequantisers (Q4): chunk of each landed stage -> f16 hi and lo tiles. A stage's
+    // tiles are free when its copies land: the producer reissued the stage only after the
+    // MMAs that read them had committed.
+    const int dw = warp - 6;
+    long long i = 0;
+    for (long long u = b0; u < b1; ++u, ++i) {
+      const int s = (int)(i % S);
+      const bool ok = wait_bar(&full[s], (uint32_t)(i / S) & 1, lim, abort);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      uint8_t* st = smem + (size_t)s * SB;
+      const uint8_t* chunk = st + OFF_W;
+#pragma unroll 2
+      for (int it = 0; it < kQ4Words / 128; ++it) {
+        const int p = it * 128 + dw * 32 + lane;
+        uint4 hv, lv;
+        q4_unit(chunk, p, hv, lv);
+        *reinterpret_cast<uint4*>(st + 16 * p) = hv;
+        *reinterpret_cast<uint4*>(st + kATile + 16 * p) = lv;
+      }
+      ptx::fence_proxy_async();  // the tiles are read by the tensor cores (async proxy)
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&dq[s]);
     }
   } else {
     // ---- epilogue: accumulator (128 channels x [hi | lo] columns) -> partial slot, then
@@ -781,6 +876,36 @@ __global__ void tile_weights_kernel(const __half* src, long long ld, int kmajor,
     const int t = t0 + n / group, o = o0 + n % group, c = k / kChunkK;
     uint8_t* tile = dst + ((size_t)t * chunks + c) * kATile;
     *reinterpret_cast<uint4*>(tile + tile_off(o, k % kChunkK)) = *reinterpret_cast<const uint4*>(v);
+  }
+}
+
+// One-time re-tiling of a Q4 matrix in the file's layout (nibbles [K][ld/2], the low
+// nibble of a byte the even column; f16 scales [K][ld/32]) into [tiles][chunks][kQ4Chunk]
+// chunks for the Q4 kernel. Column col0 + n lands in tile t0 + n / group at channel
+// o0 + n % group, as in tile_weights_kernel; col0, group and o0 are multiples of 32, so a
+// tile's 32-channel blocks each take one scale group.
+__global__ void tile_q4_kernel(const uint8_t* packed, const uint16_t* scales, long long ld, int K, int N, int col0,
+                               int t0, int group, int o0, int chunks, uint8_t* dst) {
+  const long long units = (long long)N * (K / 8);  // one nibble word: 8 k of one channel
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < units; i += (long long)gridDim.x * blockDim.x) {
+    const int n = (int)(i % N);
+    const int k = (int)(i / N) * 8;
+    const int col = col0 + n;
+    const int t = t0 + n / group, o = o0 + n % group, c = k / kChunkK, kk = k % kChunkK;
+    uint32_t w = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t q = (packed[(long long)(k + j) * (ld / 2) + col / 2] >> (4 * (col & 1))) & 0xFu;
+      w |= q << ((j & 1) ? 16 + 4 * (j >> 1) : 4 * (j >> 1));
+    }
+    uint8_t* chunk = dst + ((size_t)t * chunks + c) * kQ4Chunk;
+    const int p = (o >> 3) * 64 + (kk >> 3) * 8 + (o & 7);
+    reinterpret_cast<uint32_t*>(chunk)[p] = w;
+    if ((o & 31) == 0) {
+      uint16_t* sc = reinterpret_cast<uint16_t*>(chunk + kQ4Words * 4 + (o >> 5) * 128) + kk;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) sc[j] = scales[(long long)(k + j) * (ld / 32) + col / 32];
+    }
   }
 }
 

@@ -27,6 +27,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libqora_cuda.so")
 
 FLAG_PER_OP_KERNELS = 1  # QORA_FLAG_PER_OP_KERNELS
+FLAG_TOKEN_PREFILL = 2  # QORA_FLAG_TOKEN_PREFILL
 
 STATUS = {0: "OK", 1: "INVALID", 2: "IO", 3: "CUDA", 4: "OOM", 5: "RANGE", 6: "TIMEOUT",
           7: "UNSUPPORTED", 8: "NCCL"}
@@ -57,6 +58,7 @@ SIGNATURES = {
     "qora_engine_time_kernel": (C.c_int, [_vp, _vp, C.c_int, _u32, _P(C.c_float), _P(_u64),
                                           _P(_u32)]),
     "qora_engine_launches_per_step": (C.c_int, [_vp, _P(_u32)]),
+    "qora_engine_prompt_path": (C.c_int, [_vp, _P(_u32)]),
     "qora_engine_set_trace": (C.c_int, [_vp, C.c_int]),
     "qora_engine_get_trace": (C.c_int, [_vp, _vp, C.c_size_t, _P(C.c_size_t)]),
     "qora_tp_export": (C.c_int, [_vp, _vp, C.c_size_t, _P(C.c_size_t)]),
@@ -111,13 +113,15 @@ class DecodeWeights:
 
     def __init__(self, model: Optional[Model] = None, path: Optional[str] = None,
                  device: int = 0, n_gpus: int = 1, per_op_kernels: bool = False,
-                 tp_size: int = 1, tp_rank: int = 0):
+                 tp_size: int = 1, tp_rank: int = 0, token_prefill: bool = False):
         """tp_size > 1: this engine is rank tp_rank of a tensor-parallel group (one engine
-        per GPU); call tp_export() on every rank and tp_connect(all_handles) on each."""
+        per GPU); call tp_export() on every rank and tp_connect(all_handles) on each.
+        token_prefill: Q4 prompts run as one decode step per token (no tensor-core prompt
+        pass, no second copy of the projections)."""
         self.per_op_kernels = per_op_kernels
         self.tp_size, self.tp_rank = tp_size, tp_rank
-        opts = abi.EngineOptions(n_gpus, device, FLAG_PER_OP_KERNELS if per_op_kernels else 0,
-                                 tp_size, tp_rank)
+        flags = (FLAG_PER_OP_KERNELS if per_op_kernels else 0) | (FLAG_TOKEN_PREFILL if token_prefill else 0)
+        opts = abi.EngineOptions(n_gpus, device, flags, tp_size, tp_rank)
         h = C.c_void_p()
         if path is not None:
             check(lib().qora_engine_create_from_file(os.fsencode(path), C.byref(opts), C.byref(h)))
@@ -261,6 +265,13 @@ class DecodeWeights:
         n = _u32()
         check(lib().qora_engine_launches_per_step(self.h, C.byref(n)))
         return n.value
+
+    def prefill_path(self) -> str:
+        """How prefill() runs a prompt of two or more tokens: "tensor cores" (all rows at
+        once, layer by layer) or "token steps" (one decode step per token)."""
+        n = _u32()
+        check(lib().qora_engine_prompt_path(self.h, C.byref(n)))
+        return "tensor cores" if n.value == 1 else "token steps"
 
     def layer_step(self, kv: "KVCache", layer: int, x) -> np.ndarray:
         x = np.ascontiguousarray(x, dtype=np.float32).copy()

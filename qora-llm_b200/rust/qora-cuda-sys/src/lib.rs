@@ -24,6 +24,9 @@ pub const QORA_ERR_NCCL: qora_status = 8;
 pub const QORA_FORMAT_F16: u32 = 0;
 pub const QORA_FORMAT_Q4: u32 = 1;
 pub const QORA_FLAG_PER_OP_KERNELS: u32 = 1;
+pub const QORA_FLAG_TOKEN_PREFILL: u32 = 2;
+pub const QORA_PROMPT_TOKEN_STEPS: u32 = 0;
+pub const QORA_PROMPT_TENSOR_CORES: u32 = 1;
 pub const QORA_KV_F32: u32 = 0;
 pub const QORA_KV_F16: u32 = 1;
 pub const QORA_GEMV_STATIC_FLOATS: u32 = 512 * 1024;
@@ -320,4 +323,5 @@ extern "C" {
     pub fn qora_engine_set_trace(engine: *mut qora_engine, enable: c_int) -> qora_status;
     pub fn qora_engine_get_trace(engine: *mut qora_engine, out: *mut u64, cap: usize, n: *mut usize) -> qora_status;
     pub fn qora_engine_launches_per_step(engine: *const qora_engine, launches: *mut u32) -> qora_status;
+    pub fn qora_engine_prompt_path(engine: *const qora_engine, path: *mut u32) -> qora_status;
 }
