@@ -61,7 +61,8 @@ constexpr int kSmemBudget = 200 * 1024;
 constexpr int kQ4Words = kTileN * kChunkK / 8;
 constexpr int kQ4Chunk = kQ4Words * 4 + 4 * kChunkK * 2;
 constexpr int kQ4Slot = 5 * 1024;            // its stage slot (stages stay 1 KB aligned)
-constexpr int kQ4Threads = kThreads + 128;   // + 4 dequantising warps
+constexpr int kQ4DqWarps = 4;                // dequantising warps of the Q4 kernel
+constexpr int kQ4Threads = kThreads + 32 * kQ4DqWarps;
 
 // byte offset of element (r, k) of a [rows][64] f16 chunk tile
 __host__ __device__ constexpr int tile_off(int r, int k) {
@@ -426,8 +427,9 @@ QORA_DEV void finish_quad(const FusedArgs& a, int t, int m, int q, bool act, flo
 constexpr int kMaxContrib = 160;  // >= CTAs of a launch (one per SM)
 
 // Finish tile t (all its slots are written): 128 epilogue threads, 16 per row (thread q
-// of a row owns channels 4q..4q+3 and 64+4q..64+4q+3), 8 rows per pass; each channel's
-// slots are summed in CTA order, eight contributors' loads in flight at a time.
+// of a row owns channels 4q..4q+3 and 64+4q..64+4q+3), 16 rows per round (two rows per
+// thread); each channel's slots are summed in CTA order, eight contributors' loads for
+// both rows in flight at a time.
 QORA_DEV void finish_tile(const FusedArgs& a, int t, long long* s_cb) {
   const int e = threadIdx.x - 64, q = e & 15, rsub = e >> 4;
   const long long T = (long long)a.tiles * a.chunks;
@@ -439,33 +441,47 @@ QORA_DEV void finish_tile(const FusedArgs& a, int t, long long* s_cb) {
     s_cb[i] = (long long)(c * a.maxseg + seg) * a.R * kTileN;
   }
   ptx::named_bar(1, 128);
-  for (int m0 = 0; m0 < a.M; m0 += 8) {
-    const int m = m0 + rsub;
-    const bool act = m < a.M;
-    float s0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, s1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  // two row passes per round: every contributor's loads of 16 rows in flight together
+  for (int m0 = 0; m0 < a.M; m0 += 16) {
+    const int mA = m0 + rsub, mB = m0 + 8 + rsub;
+    const bool actA = mA < a.M, actB = mB < a.M;
+    float sA0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, sA1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    float sB0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, sB1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     for (int i0 = 0; i0 < nc; i0 += 8) {
-      float4 v0[8], v1[8];
+      float4 a0[8], a1[8], b0[8], b1[8];
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
-        const bool ok = act && i0 + k < nc;
-        const float* p = a.part + s_cb[i0 + k < nc ? i0 + k : i0] + (size_t)(act ? m : 0) * kTileN + 4 * q;
-        v0[k] = ok ? __ldcg(reinterpret_cast<const float4*>(p)) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        v1[k] = ok ? __ldcg(reinterpret_cast<const float4*>(p + 64)) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        const bool in = i0 + k < nc;
+        const float* p = a.part + s_cb[in ? i0 + k : i0] + 4 * q;
+        const float4 z = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        a0[k] = in && actA ? __ldcg(reinterpret_cast<const float4*>(p + (size_t)mA * kTileN)) : z;
+        a1[k] = in && actA ? __ldcg(reinterpret_cast<const float4*>(p + (size_t)mA * kTileN + 64)) : z;
+        b0[k] = in && actB ? __ldcg(reinterpret_cast<const float4*>(p + (size_t)mB * kTileN)) : z;
+        b1[k] = in && actB ? __ldcg(reinterpret_cast<const float4*>(p + (size_t)mB * kTileN + 64)) : z;
       }
 #pragma unroll
       for (int k = 0; k < 8; ++k)
         if (i0 + k < nc) {
-          s0[0] = __fadd_rn(s0[0], v0[k].x);
-          s0[1] = __fadd_rn(s0[1], v0[k].y);
-          s0[2] = __fadd_rn(s0[2], v0[k].z);
-          s0[3] = __fadd_rn(s0[3], v0[k].w);
-          s1[0] = __fadd_rn(s1[0], v1[k].x);
-          s1[1] = __fadd_rn(s1[1], v1[k].y);
-          s1[2] = __fadd_rn(s1[2], v1[k].z);
-          s1[3] = __fadd_rn(s1[3], v1[k].w);
+          sA0[0] = __fadd_rn(sA0[0], a0[k].x);
+          sA0[1] = __fadd_rn(sA0[1], a0[k].y);
+          sA0[2] = __fadd_rn(sA0[2], a0[k].z);
+          sA0[3] = __fadd_rn(sA0[3], a0[k].w);
+          sA1[0] = __fadd_rn(sA1[0], a1[k].x);
+          sA1[1] = __fadd_rn(sA1[1], a1[k].y);
+          sA1[2] = __fadd_rn(sA1[2], a1[k].z);
+          sA1[3] = __fadd_rn(sA1[3], a1[k].w);
+          sB0[0] = __fadd_rn(sB0[0], b0[k].x);
+          sB0[1] = __fadd_rn(sB0[1], b0[k].y);
+          sB0[2] = __fadd_rn(sB0[2], b0[k].z);
+          sB0[3] = __fadd_rn(sB0[3], b0[k].w);
+          sB1[0] = __fadd_rn(sB1[0], b1[k].x);
+          sB1[1] = __fadd_rn(sB1[1], b1[k].y);
+          sB1[2] = __fadd_rn(sB1[2], b1[k].z);
+          sB1[3] = __fadd_rn(sB1[3], b1[k].w);
         }
     }
-    finish_quad(a, t, m, q, act, s0, s1);
+    finish_quad(a, t, mA, q, actA, sA0, sA1);
+    if (m0 + 8 < a.M) finish_quad(a, t, mB, q, actB, sB0, sB1);
   }
   ptx::named_bar(1, 128);  // s_cb is free again
   if (a.ep == kEpLogits) {
@@ -572,7 +588,7 @@ __global__ void __launch_bounds__(Q4 ? kQ4Threads : kThreads, 1) fused_gemm_kern
   const uint32_t CB = WB + (uint32_t)R * 256u;                      // bytes copied per stage
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * SB);
   uint64_t* empty = full + S;
-  uint64_t* dq = empty + S;             // Q4: [S] tiles dequantised (4 warp arrivals)
+  uint64_t* dq = empty + S;             // Q4: [S] tiles dequantised (one arrival per dequantising warp)
   uint64_t* accf = dq + (Q4 ? S : 0);  // [2] accumulator ready
   uint64_t* acce = accf + 2;            // [2] accumulator drained
   uint64_t* fin = acce + 2;             // all MMAs complete
@@ -586,7 +602,7 @@ __global__ void __launch_bounds__(Q4 ? kQ4Threads : kThreads, 1) fused_gemm_kern
     for (int s = 0; s < S; ++s) {
       ptx::mbar_init(&full[s], 1);
       ptx::mbar_init(&empty[s], 1);
-      if (Q4) ptx::mbar_init(&dq[s], 4);
+      if (Q4) ptx::mbar_init(&dq[s], kQ4DqWarps);
     }
     ptx::mbar_init(&accf[0], 1);
     ptx::mbar_init(&accf[1], 1);
@@ -761,8 +777,7 @@ __global__ void __launch_bounds__(Q4 ? kQ4Threads : kThreads, 1) fused_gemm_kern
       uint8_t* st = smem + (size_t)s * SB;
       const uint8_t* chunk = st + OFF_W;
 #pragma unroll 2
-      for (int it = 0; it < kQ4Words / 128; ++it) {
-        const int p = it * 128 + dw * 32 + lane;
+      for (int p = dw * 32 + lane; p < kQ4Words; p += 32 * kQ4DqWarps) {
         uint4 hv, lv;
         q4_unit(chunk, p, hv, lv);
         *reinterpret_cast<uint4*>(st + 16 * p) = hv;
