@@ -946,10 +946,12 @@ __device__ __noinline__ uint32_t down_phase(int L, uint32_t chunk) {
 // ---- attention
 // Scores of the 4 query heads (q in shared memory) against nr K rows at `rows`, written
 // to sc[h * kMaxAttnChunk + idx0 + i] scaled by 1/sqrt(128). A row is taken by 8 lanes,
-// 4 rows per warp pass; lane li holds dims {4 li + 32 j + c} (j, c < 4), so the 8 lanes
-// of a row read 128 contiguous bytes per load (conflict-free; the 4 rows of a warp fill
-// the 4 wavefronts a 16-byte warp load needs) and q is a broadcast. The 4 heads
-// accumulate in 4 independent FMA chains. KV: float or __half rows.
+// each lane group two rows per pass (rows 4w + g and 60 later: 120 rows, a whole stage
+// of 67 f32 rows in one pass, the q loads shared by both); lane li holds dims
+// {4 li + 32 j + c} (j, c < 4), so the 8 lanes of a row read 128 contiguous bytes per load
+// (conflict-free; the 4 rows of a warp fill the 4 wavefronts a 16-byte warp load needs)
+// and q is a broadcast. The 4 heads accumulate in independent FMA chains. KV: float or
+// __half rows.
 template <class KV>
 __device__ __noinline__ void score_rows(const KV* rows, int nr, int idx0) {
   const float* sq = sm_scratch() + kAttQ;
@@ -957,55 +959,64 @@ __device__ __noinline__ void score_rows(const KV* rows, int nr, int idx0) {
   const int lane = threadIdx.x & 31, li = lane & 7;
   const float scale = 0.08838834764831845f;  // 1/sqrt(128): the f32 quotient of 1 and f32 sqrt(128)
 #pragma unroll 1
-  for (int rb = 0; rb < nr; rb += kCW * 4) {
-    const int i = rb + (threadIdx.x >> 5) * 4 + (lane >> 3);
-    const bool valid = i < nr;
-    const KV* krow = rows + (long long)min(i, nr - 1) * kHeadDim;
-    float kf[16];
-    if constexpr (sizeof(KV) == 4) {  // 4 x 16 bytes: dims 4 li + 32 j .. + 3
+  for (int rb = 0; rb < nr; rb += kCW * 8) {  // two rows per lane group: a whole stage per pass
+    int ir[2];
+    ir[0] = rb + (threadIdx.x >> 5) * 4 + (lane >> 3);
+    ir[1] = ir[0] + kCW * 4;
+    float kf[2][16];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float4 k4 = *reinterpret_cast<const float4*>(krow + 4 * li + 32 * j);
-        kf[4 * j] = k4.x;
-        kf[4 * j + 1] = k4.y;
-        kf[4 * j + 2] = k4.z;
-        kf[4 * j + 3] = k4.w;
-      }
-    } else {  // 2 x 16 bytes of halves: dims 8 li + 64 j .. + 7
+    for (int u = 0; u < 2; ++u) {
+      const KV* krow = rows + (long long)min(ir[u], nr - 1) * kHeadDim;
+      if constexpr (sizeof(KV) == 4) {  // 4 x 16 bytes: dims 4 li + 32 j .. + 3
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const uint4 raw = *reinterpret_cast<const uint4*>(krow + 8 * li + 64 * j);
-        const uint32_t wv[4] = {raw.x, raw.y, raw.z, raw.w};
+        for (int j = 0; j < 4; ++j) {
+          const float4 k4 = *reinterpret_cast<const float4*>(krow + 4 * li + 32 * j);
+          kf[u][4 * j] = k4.x;
+          kf[u][4 * j + 1] = k4.y;
+          kf[u][4 * j + 2] = k4.z;
+          kf[u][4 * j + 3] = k4.w;
+        }
+      } else {  // 2 x 16 bytes of halves: dims 8 li + 64 j .. + 7
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&wv[q]));
-          kf[8 * j + 2 * q] = f.x;
-          kf[8 * j + 2 * q + 1] = f.y;
+        for (int j = 0; j < 2; ++j) {
+          const uint4 raw = *reinterpret_cast<const uint4*>(krow + 8 * li + 64 * j);
+          const uint32_t wv[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&wv[q]));
+            kf[u][8 * j + 2 * q] = f.x;
+            kf[u][8 * j + 2 * q + 1] = f.y;
+          }
         }
       }
     }
-    float d[kHeadsPerKV] = {0.0f, 0.0f, 0.0f, 0.0f};
+    float d[2][kHeadsPerKV] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      // the q dims matching kf[4j .. 4j+3]
+      // the q dims matching kf[u][4j .. 4j+3]
       const int dim = sizeof(KV) == 4 ? 4 * li + 32 * j : 8 * li + 64 * (j >> 1) + 4 * (j & 1);
 #pragma unroll
       for (int h = 0; h < kHeadsPerKV; ++h) {
         const float4 q4 = *reinterpret_cast<const float4*>(sq + h * kHeadDim + dim);
-        d[h] = __fmaf_rn(q4.x, kf[4 * j], d[h]);
-        d[h] = __fmaf_rn(q4.y, kf[4 * j + 1], d[h]);
-        d[h] = __fmaf_rn(q4.z, kf[4 * j + 2], d[h]);
-        d[h] = __fmaf_rn(q4.w, kf[4 * j + 3], d[h]);
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          d[u][h] = __fmaf_rn(q4.x, kf[u][4 * j], d[u][h]);
+          d[u][h] = __fmaf_rn(q4.y, kf[u][4 * j + 1], d[u][h]);
+          d[u][h] = __fmaf_rn(q4.z, kf[u][4 * j + 2], d[u][h]);
+          d[u][h] = __fmaf_rn(q4.w, kf[u][4 * j + 3], d[u][h]);
+        }
       }
     }
 #pragma unroll
-    for (int h = 0; h < kHeadsPerKV; ++h) {
-      float v = d[h];
-      v += __shfl_xor_sync(0xffffffffu, v, 1);
-      v += __shfl_xor_sync(0xffffffffu, v, 2);
-      v += __shfl_xor_sync(0xffffffffu, v, 4);
-      if (valid && li == 0) sc[h * kMaxAttnChunk + idx0 + i] = __fmul_rn(v, scale);
-    }
+    for (int u = 0; u < 2; ++u)
+#pragma unroll
+      for (int h = 0; h < kHeadsPerKV; ++h) {
+        float v = d[u][h];
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        v += __shfl_xor_sync(0xffffffffu, v, 4);
+        if (ir[u] < nr && li == 0) sc[h * kMaxAttnChunk + idx0 + ir[u]] = __fmul_rn(v, scale);
+      }
   }
 }
 
