@@ -63,8 +63,10 @@ constexpr int kThreads = kCT + 32;     // + one producer warp
 constexpr int kStageBytes = 34560;     // 1920 one-group rows = 240 eight-group rows = 30 embedding rows
 constexpr int kStages = 5;
 constexpr int kBar = 1;                // named barrier of the consumer warps
-constexpr int kKVRows = kStageBytes / (kHeadDim * 4);  // f32 K or V rows of one head per stage (67)
-constexpr int kKVRows16 = kStageBytes / (kHeadDim * 2);  // f16 rows (135)
+// K or V rows of one head per stage: multiples of 4 (the P.V reads four rows'
+// probabilities as one float4), one score pass each (see score_rows)
+constexpr int kKVRows = 64;     // f32 rows (32 KB of the 34.5 KB stage)
+constexpr int kKVRows16 = 120;  // binary16 rows
 constexpr int kMinAttnChunk = 64;
 constexpr int kMaxAttnChunk = 1024;
 constexpr int kMaxUnits = 256;         // attention units (kv head x chunk); units <= CTAs
@@ -296,6 +298,7 @@ __device__ __noinline__ void make_att_plan(const Args& a, int c, int G, int pos)
   const int len = pos + 1;
   int csz = (len * a.nkvh + G - 1) / G;
   csz = max(kMinAttnChunk, min(kMaxAttnChunk, csz));
+  csz = (csz + 63) / 64 * 64;  // chunk starts stay multiples of 4 rows (float4 probabilities)
   const int nch = (len + csz - 1) / csz, u = G - 1 - c;
   P[0] = u < a.nkvh * nch ? 1 : 0;
   if (!P[0]) return;
@@ -1025,35 +1028,53 @@ QORA_DEV float kv_elem(const float* p) { return *p; }
 QORA_DEV float kv_elem(const __half* p) { return __half2float(*p); }
 
 // P.V over nr V rows at `rows` for the 4 heads, added to o: thread (grp, d) of three
-// 128-thread groups takes rows grp, grp + 3, ..., four rows' loads in flight per step;
-// probabilities sc[h * kMaxAttnChunk + idx0 + i]. The accumulators travel in registers
-// (argument and result).
+// 128-thread groups takes blocks of 4 consecutive rows (block b to group b % 3), the
+// block's four V loads in flight and its probabilities sc[h * kMaxAttnChunk + idx0 + i]
+// read as one float4 per head. The accumulators travel in registers (argument and
+// result).
 template <class KV>
 __device__ __noinline__ float4 pv_rows(const KV* rows, int nr, int idx0, int grp, int dd, float4 o) {
   const float* sc = sm_scratch() + kAttS + idx0;
   const KV* vr = rows + dd;
-  int i = grp;
+  // blocks of 4 consecutive rows, block b to group b % 3; a full block's probabilities
+  // are one float4 per head (idx0 is a multiple of 4 for the streamed stages)
+  int b = grp;
 #pragma unroll 1
-  for (; i + 9 < nr; i += 12) {
+  for (; 4 * b + 3 < nr; b += 3) {
+    const int i = 4 * b;
     float v[4];
 #pragma unroll
-    for (int r = 0; r < 4; ++r) v[r] = kv_elem(vr + (long long)(i + 3 * r) * kHeadDim);
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const int ii = i + 3 * r;
-      o.x = __fmaf_rn(sc[ii], v[r], o.x);
-      o.y = __fmaf_rn(sc[kMaxAttnChunk + ii], v[r], o.y);
-      o.z = __fmaf_rn(sc[2 * kMaxAttnChunk + ii], v[r], o.z);
-      o.w = __fmaf_rn(sc[3 * kMaxAttnChunk + ii], v[r], o.w);
-    }
+    for (int r = 0; r < 4; ++r) v[r] = kv_elem(vr + (long long)(i + r) * kHeadDim);
+    const float4 p0 = *reinterpret_cast<const float4*>(sc + i);
+    const float4 p1 = *reinterpret_cast<const float4*>(sc + kMaxAttnChunk + i);
+    const float4 p2 = *reinterpret_cast<const float4*>(sc + 2 * kMaxAttnChunk + i);
+    const float4 p3 = *reinterpret_cast<const float4*>(sc + 3 * kMaxAttnChunk + i);
+    o.x = __fmaf_rn(p0.x, v[0], o.x);
+    o.y = __fmaf_rn(p1.x, v[0], o.y);
+    o.z = __fmaf_rn(p2.x, v[0], o.z);
+    o.w = __fmaf_rn(p3.x, v[0], o.w);
+    o.x = __fmaf_rn(p0.y, v[1], o.x);
+    o.y = __fmaf_rn(p1.y, v[1], o.y);
+    o.z = __fmaf_rn(p2.y, v[1], o.z);
+    o.w = __fmaf_rn(p3.y, v[1], o.w);
+    o.x = __fmaf_rn(p0.z, v[2], o.x);
+    o.y = __fmaf_rn(p1.z, v[2], o.y);
+    o.z = __fmaf_rn(p2.z, v[2], o.z);
+    o.w = __fmaf_rn(p3.z, v[2], o.w);
+    o.x = __fmaf_rn(p0.w, v[3], o.x);
+    o.y = __fmaf_rn(p1.w, v[3], o.y);
+    o.z = __fmaf_rn(p2.w, v[3], o.z);
+    o.w = __fmaf_rn(p3.w, v[3], o.w);
   }
+  if (4 * b < nr) {  // the partial last block (also the new position's single row)
 #pragma unroll 1
-  for (; i < nr; i += 3) {
-    const float v = kv_elem(vr + (long long)i * kHeadDim);
-    o.x = __fmaf_rn(sc[i], v, o.x);
-    o.y = __fmaf_rn(sc[kMaxAttnChunk + i], v, o.y);
-    o.z = __fmaf_rn(sc[2 * kMaxAttnChunk + i], v, o.z);
-    o.w = __fmaf_rn(sc[3 * kMaxAttnChunk + i], v, o.w);
+    for (int i = 4 * b; i < nr; ++i) {
+      const float v = kv_elem(vr + (long long)i * kHeadDim);
+      o.x = __fmaf_rn(sc[i], v, o.x);
+      o.y = __fmaf_rn(sc[kMaxAttnChunk + i], v, o.y);
+      o.z = __fmaf_rn(sc[2 * kMaxAttnChunk + i], v, o.z);
+      o.w = __fmaf_rn(sc[3 * kMaxAttnChunk + i], v, o.w);
+    }
   }
   return o;
 }
