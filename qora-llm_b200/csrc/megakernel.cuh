@@ -599,7 +599,7 @@ QORA_DEV float sum15(const float* p, int stride) {
   return __fadd_rn(__fadd_rn(v[0], v[1]), __fadd_rn(v[2], v[3]));
 }
 
-__device__ __noinline__ float csum(float v) {
+__device__ __forceinline__ float csum(float v) {
   float* red = sm_scratch() + kOffMisc;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   v = warp_sum(v);
@@ -610,7 +610,7 @@ __device__ __noinline__ float csum(float v) {
   return t;
 }
 
-__device__ __noinline__ float rms_inv_from(float sumsq, int H) {
+__device__ __forceinline__ float rms_inv_from(float sumsq, int H) {
   return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sumsq, (float)H), 1e-6f)));
 }
 
@@ -621,7 +621,7 @@ QORA_DEV int span_row(const int* P, int i) {
 }
 // Norm gains gamma[row] of matrix m's span copied into xs asynchronously: issued before
 // the wait for the activations, used after it.
-__device__ __noinline__ void stage_gains(const float* gamma, int m) {
+__device__ __forceinline__ void stage_gains(const float* gamma, int m) {
   float* xs = sm_scratch();
   const int* P = mat_plan(m);
 #pragma unroll 1
@@ -629,7 +629,7 @@ __device__ __noinline__ void stage_gains(const float* gamma, int m) {
 }
 // xs[i] = x[row] * inv * gamma[row] * 2^64 (gamma from stage_gains, this thread's own
 // copies)
-__device__ __noinline__ void fill_norm_inputs(const float* x, float inv, int m) {
+__device__ __forceinline__ void fill_norm_inputs(const float* x, float inv, int m) {
   float* xs = sm_scratch();
   const int* P = mat_plan(m);
   ptx::cp_async_wait_all();
@@ -672,7 +672,7 @@ __device__ __noinline__ float tp_sum(const uint64_t* own, int L, int col, uint32
 // ------------------------------------------------------------------ the GEMV
 // A finished segment's sums (Y) go out tagged: q|k|v values; x_mid = x + o for o_proj
 // columns (residual values from FIN); gate/up and down split-K partials.
-__device__ __noinline__ void seg_store(int m, int L, int t, int slot) {
+__device__ __forceinline__ void seg_store(int m, int L, int t, int slot) {
   const Cons C = make_cons(0);
   const Args& a = C.a();
   const float* y = C.scratch + kOffY;
@@ -858,8 +858,8 @@ __device__ __noinline__ uint32_t gu_phase(int L, uint32_t chunk) {
   return gemv_run<true>(GU, L, C.chunk);
 }
 
-// silu(g) * u with silu(g) = g / (1 + exp(-g)) (src/gemv.rs:494-500), one copy of the code
-__device__ __noinline__ float swiglu(float g, float u) {
+// silu(g) * u with silu(g) = g / (1 + exp(-g)) (src/gemv.rs:494-500)
+__device__ __forceinline__ float swiglu(float g, float u) {
   return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
 }
 
@@ -950,7 +950,7 @@ __device__ __noinline__ uint32_t down_phase(int L, uint32_t chunk) {
 // Scores of the 4 query heads (q in shared memory) against nr K rows at `rows`, written
 // to sc[h * kMaxAttnChunk + idx0 + i] scaled by 1/sqrt(128). A row is taken by 8 lanes,
 // each lane group two rows per pass (rows 4w + g and 60 later: 120 rows, a whole stage
-// of 67 f32 rows in one pass, the q loads shared by both); lane li holds dims
+// of 64 f32 or 120 binary16 rows in one pass, the q loads shared by both); lane li holds dims
 // {4 li + 32 j + c} (j, c < 4), so the 8 lanes of a row read 128 contiguous bytes per load
 // (conflict-free; the 4 rows of a warp fill the 4 wavefronts a 16-byte warp load needs)
 // and q is a broadcast. The 4 heads accumulate in independent FMA chains. KV: float or
@@ -1270,7 +1270,7 @@ __device__ __noinline__ uint32_t attention_phase_t(int L, uint32_t chunk) {
   return C.chunk;
 }
 
-__device__ __noinline__ uint32_t attention_phase(int L, uint32_t chunk) {
+__device__ __forceinline__ uint32_t attention_phase(int L, uint32_t chunk) {
   return sm_args()->kv16 ? attention_phase_t<__half>(L, chunk) : attention_phase_t<float>(L, chunk);
 }
 
