@@ -15,9 +15,13 @@
 // of its range at once (about 86 KB for config 1: all of its bytes in flight from the
 // first cycle), then computes each box as it lands: lane (sub, gi) takes group gi of 4
 // rows per warp pass, with the shift-free dequantisation of q4_gemv.cuh. A range covers
-// one or two tiles (segments); each segment's sums are one split-K partial, and the last
-// CTA to finish a tile (arrival counter) adds the tile's partials in slot order, so the
-// result is deterministic.
+// one or two tiles (segments); each segment's sums are one split-K partial, published as
+// tagged 64-bit words ((1 << 32) | f32 bits, single-copy atomic: no fence, no arrival
+// counter). Once a CTA has published all of its partials, it finishes the tiles whose last
+// slot it holds: it reads every slot of the tile (re-reading, bounded, the words not yet
+// tagged), adds them in slot order (deterministic), stores y and puts the words back to
+// zero for the next launch. Nobody waits before publishing its own partials, and the
+// CTAs a finisher waits for hold lower slots, so no wait can go round in a circle.
 //
 // Back-to-back GEMVs overlap: launched with programmatic stream serialisation, a kernel
 // issues its weight loads (read-only inputs) before griddepcontrol.wait, and only reads x
@@ -47,13 +51,12 @@ constexpr unsigned long long kTimeoutNs = 2000000000ull;
 struct Args {
   const float* x;
   float* y;
-  float* partials;     // [tiles][slots][256]
-  unsigned* counters;  // [tiles], zero between launches
+  uint64_t* partials;  // tagged [tiles][slots][256], zero between launches
   int K, n, tiles, slots;
 };
 
 // shared memory: boxes [kMaxBoxes][kBoxBytes] | xs [kMaxRows] | red [kWarps][256] |
-// spare [256] | full barriers [kMaxBoxes] | last-arriver flag
+// spare [256] | full barriers [kMaxBoxes] | spare word
 constexpr int kOffXs = kMaxBoxes * kBoxBytes;
 constexpr int kOffRed = kOffXs + kMaxRows * 4;
 constexpr int kOffY = kOffRed + kWarps * kTileCols * 4;
@@ -91,7 +94,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* xs = reinterpret_cast<float*>(sm + kOffXs);
   float* red = reinterpret_cast<float*>(sm + kOffRed);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kOffBar);
-  volatile int* last = reinterpret_cast<volatile int*>(sm + kOffBar + kMaxBoxes * 8);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, gi = lane & 7, sub = lane >> 3;
   const int c = blockIdx.x, G = gridDim.x, K = a.K;
   const unsigned total = (unsigned)a.tiles * (unsigned)K;  // host: tiles * K * G < 2^32
@@ -123,6 +125,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
 
   int b = 0, off = 0;
+  int fin_t[2], fin_n[2], nfin = 0;  // tiles this CTA finishes (it holds their last slot)
   for (int s = 0; s < sg.n; ++s) {
     const int t = sg.t[s], r0 = sg.r0[s], r1 = sg.r1[s];
     float2 acc[16];
@@ -182,32 +185,49 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
     for (int e2 = 0; e2 < 8; ++e2) red[warp * kTileCols + gi * 32 + sub * 8 + e2] = v[e2];
     __syncthreads();
-    // this segment's partial, then the tile's arrival count
+    // this segment's partial (slot = CTA - first CTA of the tile), published tagged
     const unsigned K1 = (unsigned)K;
     const int slot_first = (int)(((unsigned)t * K1 + 1u) * (unsigned)G - 1u) / (int)total;
     const int slot_last = (int)((((unsigned)(t + 1) * K1 - 1u + 1u) * (unsigned)G - 1u) / total);
     const int slot = c - slot_first, nslots = slot_last - slot_first + 1;
-    float* part = a.partials + (size_t)t * a.slots * kTileCols;
     if (tid < kTileCols) {
       float y = 0.0f;
       for (int w = 0; w < kWarps; ++w) y += red[w * kTileCols + tid];
-      __stcg(part + (size_t)slot * kTileCols + tid, y);
+      ptx::st_relaxed_b64(a.partials + ((size_t)t * a.slots + slot) * kTileCols + tid,
+                          (1ull << 32) | __float_as_uint(y));
     }
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) *last = atomicAdd(a.counters + t, 1u) == (unsigned)(nslots - 1);
-    __syncthreads();
-    if (*last) {
-      __threadfence();
-      if (tid < kTileCols) {
-        float y = 0.0f;
-        for (int k = 0; k < nslots; ++k) y += __ldcg(part + (size_t)k * kTileCols + tid);
-        const int col = t * kTileCols + tid;
-        if (col < a.n) a.y[col] = y;
+    if (slot == nslots - 1) {
+      fin_t[nfin] = t;
+      fin_n[nfin] = nslots;
+      ++nfin;
+    }
+    __syncthreads();  // red is rewritten by the next segment
+  }
+  // finish the tiles whose last slot is ours: every slot's word of column tid, four loads
+  // in flight, stale ones re-read (bounded: a partial that never arrives counts as 0)
+  for (int f = 0; f < nfin && tid < kTileCols; ++f) {
+    uint64_t* part = a.partials + (size_t)fin_t[f] * a.slots * kTileCols + tid;
+    const int ns = fin_n[f];
+    float y = 0.0f;
+    for (int k0 = 0; k0 < ns; k0 += 4) {
+      uint64_t v[4];
+      const uint64_t t0 = ptx::globaltimer();
+      for (;;) {
+        bool ok = true;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          v[k] = k0 + k < ns ? ptx::ld_relaxed_b64(part + (size_t)(k0 + k) * kTileCols) : (1ull << 32);
+          ok &= (v[k] >> 32) == 1ull;
+        }
+        if (ok || ptx::globaltimer() - t0 > kTimeoutNs) break;
       }
-      if (tid == 0) a.counters[t] = 0u;
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        if (k0 + k < ns && (v[k] >> 32) == 1ull) y += __uint_as_float((uint32_t)v[k]);
     }
-    __syncthreads();
+    const int col = fin_t[f] * kTileCols + tid;
+    if (col < a.n) a.y[col] = y;
+    for (int k = 0; k < ns; ++k) ptx::st_relaxed_b64(part + (size_t)k * kTileCols, 0ull);
   }
 }
 

@@ -1810,6 +1810,8 @@ struct EntryScratch {
   size_t partial_floats = 0;
   unsigned* counters = nullptr;
   size_t ncounters = 0;
+  uint64_t* tagged = nullptr;  // tagged split-K partials of the TMA GEMV (zero between launches)
+  size_t ntagged = 0;
   float* lm_v = nullptr;
   unsigned* lm_i = nullptr;
   unsigned* lm_c = nullptr;
@@ -1821,8 +1823,16 @@ struct EntryScratch {
 std::mutex g_entry_mu;
 std::map<int, EntryScratch> g_entry;
 
-qora_status entry_scratch(int dev, size_t pf, size_t nc, int lm_n, EntryScratch** out) {
+qora_status entry_scratch(int dev, size_t pf, size_t nc, int lm_n, EntryScratch** out, size_t nt = 0) {
   EntryScratch& s = g_entry[dev];
+  if (s.ntagged < nt) {
+    if (s.tagged) cudaFree(s.tagged);
+    s.tagged = nullptr;
+    QCUDA(cudaMalloc(&s.tagged, nt * sizeof(uint64_t)));
+    QCUDA(cudaMemset(s.tagged, 0, nt * sizeof(uint64_t)));
+    QCUDA(cudaDeviceSynchronize());  // zero before any stream's first launch (growth only)
+    s.ntagged = nt;
+  }
   if (s.partial_floats < pf) {
     if (s.partials) cudaFree(s.partials);
     s.partials = nullptr;
@@ -2689,8 +2699,8 @@ static qora_status q4_gemv_tma(const float* d_x, const uint8_t* d_packed, const 
   const int slots = (int)(k / std::max(1ll, total / G)) + 2;
   std::lock_guard<std::mutex> lk(g_entry_mu);
   EntryScratch* sc = nullptr;
-  QCHECK(entry_scratch(dev, (size_t)tiles * slots * kTileCols, (size_t)tiles, 0, &sc));
-  g1::Args a{d_x, d_y, sc->partials, sc->counters, k, n, (int)tiles, slots};
+  QCHECK(entry_scratch(dev, 0, 0, 0, &sc, (size_t)tiles * slots * kTileCols));
+  g1::Args a{d_x, d_y, sc->tagged, k, n, (int)tiles, slots};
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(G);
   cfg.blockDim = dim3(g1::kThreads);
