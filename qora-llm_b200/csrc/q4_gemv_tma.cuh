@@ -37,13 +37,15 @@
 namespace qora {
 namespace g1 {
 
-constexpr int kThreads = 512;
+// Two CTAs fit one SM (registers and shared memory), so that the next launch's CTA on an
+// SM issues its weight loads while this launch's CTA there still computes and finishes.
+constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr int kBoxRows = 128;                  // rows per box
+constexpr int kBoxRows = 64;                   // rows per box (CTA ranges are whole boxes)
 constexpr int kPackBox = kBoxRows * 128;       // nibble bytes per box (256 outputs per row)
 constexpr int kScaleBox = kBoxRows * 16;       // scale bytes per box (8 groups per row)
 constexpr int kBoxBytes = kPackBox + kScaleBox;
-constexpr int kMaxBoxes = 8;                   // rows per CTA <= kMaxBoxes * kBoxRows - 2 * (kBoxRows - 1)
+constexpr int kMaxBoxes = 11;                  // rows per CTA <= kMaxBoxes * kBoxRows
 constexpr int kMaxRows = kMaxBoxes * kBoxRows;
 constexpr float kTwo64 = 18446744073709551616.0f;
 constexpr unsigned long long kTimeoutNs = 2000000000ull;
@@ -88,7 +90,7 @@ __device__ __forceinline__ Segs segs_of(int l0, int l1, int K) {
   return s;
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     q4_gemv_tma_kernel(const __grid_constant__ CUtensorMap mp, const __grid_constant__ CUtensorMap ms, const Args a) {
   extern __shared__ __align__(128) uint8_t sm[];
   float* xs = reinterpret_cast<float*>(sm + kOffXs);
@@ -96,8 +98,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kOffBar);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, gi = lane & 7, sub = lane >> 3;
   const int c = blockIdx.x, G = gridDim.x, K = a.K;
-  const unsigned total = (unsigned)a.tiles * (unsigned)K;  // host: tiles * K * G < 2^32
-  const int l0 = (int)((unsigned)c * total / (unsigned)G), l1 = (int)((unsigned)(c + 1) * total / (unsigned)G);
+  // CTA c owns boxes [c*B/G, (c+1)*B/G) of the B = tiles*K/kBoxRows flattened row boxes
+  // (host: K % kBoxRows == 0, B >= G, B * G < 2^32)
+  const unsigned total = (unsigned)a.tiles * (unsigned)(K / kBoxRows);
+  const int l0 = (int)((unsigned)c * total / (unsigned)G) * kBoxRows, l1 = (int)((unsigned)(c + 1) * total / (unsigned)G) * kBoxRows;
   const Segs sg = segs_of(l0, l1, K);
 
   if (tid == 0) {  // every box of the range at once
@@ -147,15 +151,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint4 w[2];
         float cf[2];
 #pragma unroll
-        for (int k = 0; k < 2; ++k) {  // rows warp*4 + sub and 64 later: loads first
-          const int i = warp * 4 + sub + k * 64, j = i < R ? i : 0;
+        for (int k = 0; k < 2; ++k) {  // rows warp*4 + sub and 32 later: loads first
+          const int i = warp * 4 + sub + k * 32, j = i < R ? i : 0;
           w[k] = *reinterpret_cast<const uint4*>(pk + j * 128 + gi * 16);
           const uint16_t sv = *reinterpret_cast<const uint16_t*>(sc + j * 16 + gi * 2);
           cf[k] = i < R ? __half2float(__ushort_as_half(sv)) * xr[j] : 0.0f;
         }
 #pragma unroll
         for (int k = 0; k < 2; ++k) {
-          if (warp * 4 + k * 64 < R) {  // warp-uniform skip of passes past the box's rows
+          if (warp * 4 + k * 32 < R) {  // warp-uniform skip of passes past the box's rows
             cs += cf[k];
             q4_fma_chunk(w[k], cf[k], acc);
           }
@@ -185,10 +189,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
     for (int e2 = 0; e2 < 8; ++e2) red[warp * kTileCols + gi * 32 + sub * 8 + e2] = v[e2];
     __syncthreads();
-    // this segment's partial (slot = CTA - first CTA of the tile), published tagged
-    const unsigned K1 = (unsigned)K;
-    const int slot_first = (int)(((unsigned)t * K1 + 1u) * (unsigned)G - 1u) / (int)total;
-    const int slot_last = (int)((((unsigned)(t + 1) * K1 - 1u + 1u) * (unsigned)G - 1u) / total);
+    // this segment's partial (slot = CTA - first CTA of the tile), published tagged; the
+    // owner of box p is ((p + 1) G - 1) / B
+    const unsigned K1 = (unsigned)(K / kBoxRows);
+    const int slot_first = (int)((((unsigned)t * K1 + 1u) * (unsigned)G - 1u) / total);
+    const int slot_last = (int)((((unsigned)(t + 1) * K1) * (unsigned)G - 1u) / total);
     const int slot = c - slot_first, nslots = slot_last - slot_first + 1;
     if (tid < kTileCols) {
       float y = 0.0f;

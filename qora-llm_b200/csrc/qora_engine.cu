@@ -2676,27 +2676,31 @@ static qora_status encode_2d(CUtensorMap* m, const void* base, CUtensorMapDataTy
 }
 
 // The TMA GEMV (q4_gemv_tma.cuh) for shapes it takes: 256-column tiles, 16-byte-aligned
-// rows of both arrays, a per-CTA range of at most 7 boxes of rows; *used = false otherwise.
+// rows of both arrays, whole boxes of rows per CTA (k a multiple of the box height, at
+// least one and at most kMaxBoxes boxes per CTA); *used = false otherwise.
 static qora_status q4_gemv_tma(const float* d_x, const uint8_t* d_packed, const uint16_t* d_scales, int k, int n,
                                float* d_y, cudaStream_t stream, int dev, bool* used) {
   *used = false;
   const int G = sm_count(dev);
-  const long long tiles = n / kTileCols, total = tiles * (long long)k;
-  if (n % kTileCols || ((uintptr_t)d_packed | (uintptr_t)d_scales) % 16 || total * G >= (1ll << 32) ||
-      (total + G - 1) / G > 7 * g1::kBoxRows)
+  const long long tiles = n / kTileCols, boxes = tiles * (long long)(k / g1::kBoxRows);
+  if (n % kTileCols || k % g1::kBoxRows || ((uintptr_t)d_packed | (uintptr_t)d_scales) % 16 || boxes < G ||
+      boxes * G >= (1ll << 32) || (boxes + G - 1) / G > g1::kMaxBoxes)
     return QORA_OK;
   static std::once_flag attr_once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(attr_once, [] {
     attr_err = cudaFuncSetAttribute(g1::q4_gemv_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     (int)g1::kSmemBytes);
+    if (attr_err == cudaSuccess)  // room for two CTAs per SM
+      attr_err = cudaFuncSetAttribute(g1::q4_gemv_tma_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                      cudaSharedmemCarveoutMaxShared);
   });
   QCUDA(attr_err);
   CUtensorMap mp, ms;
   QCHECK(encode_2d(&mp, d_packed, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)n / 2, (uint64_t)k, 128, g1::kBoxRows));
   QCHECK(encode_2d(&ms, d_scales, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, (uint64_t)n / kGroup, (uint64_t)k, 8, g1::kBoxRows));
-  // CTAs touching one tile: every CTA owns at least floor(total / G) rows of the range
-  const int slots = (int)(k / std::max(1ll, total / G)) + 2;
+  // CTAs touching one tile: every CTA owns at least floor(boxes / G) boxes of the range
+  const int slots = (int)((k / g1::kBoxRows) / std::max(1ll, boxes / G)) + 2;
   std::lock_guard<std::mutex> lk(g_entry_mu);
   EntryScratch* sc = nullptr;
   QCHECK(entry_scratch(dev, 0, 0, 0, &sc, (size_t)tiles * slots * kTileCols));
