@@ -64,11 +64,12 @@ constexpr int kStageBytes = 34560;     // 1920 one-group rows = 240 eight-group 
 constexpr int kStages = 5;
 constexpr int kBar = 1;                // named barrier of the consumer warps
 // K or V rows of one head per stage: multiples of 4 (the P.V reads four rows'
-// probabilities as one float4), one score pass each (see score_rows)
-constexpr int kKVRows = 64;     // f32 rows (32 KB of the 34.5 KB stage)
+// probabilities as one float4), one score pass each (see score_rows: one row per lane
+// group for f32, two for binary16); chunks are whole multiples of 60 rows
+constexpr int kKVRows = 60;     // f32 rows (30 KB of the 34.5 KB stage)
 constexpr int kKVRows16 = 120;  // binary16 rows
-constexpr int kMinAttnChunk = 64;
-constexpr int kMaxAttnChunk = 1024;
+constexpr int kMinAttnChunk = 60;
+constexpr int kMaxAttnChunk = 1020;
 constexpr int kMaxUnits = 256;         // attention units (kv head x chunk); units <= CTAs
 constexpr int kHeadsPerKV = 4;         // query heads per KV head (SmolLM3-3B: 16 / 4)
 constexpr int kRowsPerLane = 4;        // GEMV rows per lane per stage (both tile widths)
@@ -298,7 +299,7 @@ __device__ __noinline__ void make_att_plan(const Args& a, int c, int G, int pos)
   const int len = pos + 1;
   int csz = (len * a.nkvh + G - 1) / G;
   csz = max(kMinAttnChunk, min(kMaxAttnChunk, csz));
-  csz = (csz + 63) / 64 * 64;  // chunk starts stay multiples of 4 rows (float4 probabilities)
+  csz = (csz + 59) / 60 * 60;  // whole stages of either cache type (<= kMaxAttnChunk: a multiple of 60)
   const int nch = (len + csz - 1) / csz, u = G - 1 - c;
   P[0] = u < a.nkvh * nch ? 1 : 0;
   if (!P[0]) return;
@@ -949,8 +950,8 @@ __device__ __noinline__ uint32_t down_phase(int L, uint32_t chunk) {
 // ---- attention
 // Scores of the 4 query heads (q in shared memory) against nr K rows at `rows`, written
 // to sc[h * kMaxAttnChunk + idx0 + i] scaled by 1/sqrt(128). A row is taken by 8 lanes,
-// each lane group two rows per pass (rows 4w + g and 60 later: 120 rows, a whole stage
-// of 64 f32 or 120 binary16 rows in one pass, the q loads shared by both); lane li holds dims
+// each lane group NU rows per pass (rows 4w + g and, binary16, 60 later: a whole stage of
+// 60 f32 or 120 binary16 rows in one pass, the q loads shared by the rows); lane li holds dims
 // {4 li + 32 j + c} (j, c < 4), so the 8 lanes of a row read 128 contiguous bytes per load
 // (conflict-free; the 4 rows of a warp fill the 4 wavefronts a 16-byte warp load needs)
 // and q is a broadcast. The 4 heads accumulate in independent FMA chains. KV: float or
@@ -961,14 +962,16 @@ __device__ __noinline__ void score_rows(const KV* rows, int nr, int idx0) {
   float* sc = sm_scratch() + kAttS;
   const int lane = threadIdx.x & 31, li = lane & 7;
   const float scale = 0.08838834764831845f;  // 1/sqrt(128): the f32 quotient of 1 and f32 sqrt(128)
+  constexpr int NU = sizeof(KV) == 4 ? 1 : 2;
+  static_assert(kCW * 4 * NU == (sizeof(KV) == 4 ? kKVRows : kKVRows16), "one pass per stage");
 #pragma unroll 1
-  for (int rb = 0; rb < nr; rb += kCW * 8) {  // two rows per lane group: a whole stage per pass
+  for (int rb = 0; rb < nr; rb += kCW * 4 * NU) {  // a whole stage per pass
     int ir[2];
     ir[0] = rb + (threadIdx.x >> 5) * 4 + (lane >> 3);
     ir[1] = ir[0] + kCW * 4;
     float kf[2][16];
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
+    for (int u = 0; u < NU; ++u) {
       const KV* krow = rows + (long long)min(ir[u], nr - 1) * kHeadDim;
       if constexpr (sizeof(KV) == 4) {  // 4 x 16 bytes: dims 4 li + 32 j .. + 3
 #pragma unroll
@@ -1002,7 +1005,7 @@ __device__ __noinline__ void score_rows(const KV* rows, int nr, int idx0) {
       for (int h = 0; h < kHeadsPerKV; ++h) {
         const float4 q4 = *reinterpret_cast<const float4*>(sq + h * kHeadDim + dim);
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
+        for (int u = 0; u < NU; ++u) {
           d[u][h] = __fmaf_rn(q4.x, kf[u][4 * j], d[u][h]);
           d[u][h] = __fmaf_rn(q4.y, kf[u][4 * j + 1], d[u][h]);
           d[u][h] = __fmaf_rn(q4.z, kf[u][4 * j + 2], d[u][h]);
@@ -1011,7 +1014,7 @@ __device__ __noinline__ void score_rows(const KV* rows, int nr, int idx0) {
       }
     }
 #pragma unroll
-    for (int u = 0; u < 2; ++u)
+    for (int u = 0; u < NU; ++u)
 #pragma unroll
       for (int h = 0; h < kHeadsPerKV; ++h) {
         float v = d[u][h];
