@@ -600,16 +600,15 @@ QORA_DEV float sum15(const float* p, int stride) {
   return __fadd_rn(__fadd_rn(v[0], v[1]), __fadd_rn(v[2], v[3]));
 }
 
-__device__ __forceinline__ float csum(float v) {
-  float* red = sm_scratch() + kOffMisc;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+// Block sum of the consumer threads' v in two halves around a barrier the caller has
+// anyway (the one that publishes the polled vector): csum_put before it, csum_get after.
+// The warp sums sit in MISC[0, 15) until the next barrier after csum_get (every caller
+// has one before MISC is written again).
+__device__ __forceinline__ void csum_put(float v) {
   v = warp_sum(v);
-  if (lane == 0) red[warp] = v;
-  ptx::named_bar(kBar, kCT);
-  const float t = sum15(red, 1);
-  ptx::named_bar(kBar, kCT);
-  return t;
+  if ((threadIdx.x & 31) == 0) sm_scratch()[kOffMisc + (threadIdx.x >> 5)] = v;
 }
+__device__ __forceinline__ float csum_get() { return sum15(sm_scratch() + kOffMisc, 1); }
 
 __device__ __forceinline__ float rms_inv_from(float sumsq, int H) {
   return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sumsq, (float)H), 1e-6f)));
@@ -816,9 +815,10 @@ __device__ __noinline__ uint32_t qkv_phase(int L, uint32_t chunk) {
 #pragma unroll 1
     for (int i = C.tid; i < H; i += kCT) ss = __fmaf_rn(sB[i], sB[i], ss);
   }
+  csum_put(ss);
   C.bar();
   C.stamp(2 + 8 * min(L, kTraceLayers - 1) + 0);
-  const float inv = rms_inv_from(csum(ss), H);
+  const float inv = rms_inv_from(csum_get(), H);
   fill_norm_inputs(sB, inv, QKV);
   C.bar();
   return gemv_run<false>(QKV, L, C.chunk);
@@ -847,13 +847,14 @@ __device__ __noinline__ uint32_t gu_phase(int L, uint32_t chunk) {
   float* sB = C.scratch + kOffB;
   stage_gains(a.layers[L].g_post, GU);
   const float ss = poll_vec(a.xmid + (long long)L * H, H, tag_of(C, L), sB, 1.0f);
+  csum_put(ss);
   C.bar();
   C.stamp(2 + 8 * min(L, kTraceLayers - 1) + 5);
   if (mat_plan(DOWN)[0] > 0) {  // keep x_mid of the down columns this CTA finishes (sB is reused below)
     const int* D = plan() + kPlDown;
     if (C.tid < D[2] - D[1]) C.scratch[kOffFin + C.tid] = sB[D[0] * kTileCols + D[1] + C.tid];
   }
-  const float inv = rms_inv_from(csum(ss), H);
+  const float inv = rms_inv_from(csum_get(), H);
   fill_norm_inputs(sB, inv, GU);
   C.bar();
   return gemv_run<true>(GU, L, C.chunk);
@@ -1308,9 +1309,10 @@ __device__ __noinline__ void lm_phase(uint32_t chunk) {
   const int H = a.H, lane = C.lane, warp = C.warp;
   float* sB = C.scratch + kOffB;
   const float ss = poll_vec(a.xbuf + (long long)a.L * H, H, tag_of(C, a.L), sB, 1.0f);
+  csum_put(ss);
   C.bar();
   C.stamp(2 + 8 * kTraceLayers);
-  const float inv = rms_inv_from(csum(ss), H);
+  const float inv = rms_inv_from(csum_get(), H);
   // normed x into a padded copy (element i at i + i / 64: the 64-element block of lane l
   // starts at bank l, so the lanes' loads below do not conflict)
   float* sX = C.scratch;  // XS and the start of B (x is read into registers first)
