@@ -208,26 +208,26 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     __syncthreads();  // red is rewritten by the next segment
   }
-  // finish the tiles whose last slot is ours: every slot's word of column tid, four loads
+  // finish the tiles whose last slot is ours: every slot's word of column tid, eight loads
   // in flight, stale ones re-read (bounded: a partial that never arrives counts as 0)
   for (int f = 0; f < nfin && tid < kTileCols; ++f) {
     uint64_t* part = a.partials + (size_t)fin_t[f] * a.slots * kTileCols + tid;
     const int ns = fin_n[f];
     float y = 0.0f;
-    for (int k0 = 0; k0 < ns; k0 += 4) {
-      uint64_t v[4];
+    for (int k0 = 0; k0 < ns; k0 += 8) {
+      uint64_t v[8];
       const uint64_t t0 = ptx::globaltimer();
       for (;;) {
         bool ok = true;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
+        for (int k = 0; k < 8; ++k) {
           v[k] = k0 + k < ns ? ptx::ld_relaxed_b64(part + (size_t)(k0 + k) * kTileCols) : (1ull << 32);
           ok &= (v[k] >> 32) == 1ull;
         }
         if (ok || ptx::globaltimer() - t0 > kTimeoutNs) break;
       }
 #pragma unroll
-      for (int k = 0; k < 4; ++k)
+      for (int k = 0; k < 8; ++k)
         if (k0 + k < ns && (v[k] >> 32) == 1ull) y += __uint_as_float((uint32_t)v[k]);
     }
     const int col = fin_t[f] * kTileCols + tid;
