@@ -635,6 +635,14 @@ def config1():
     return m, x
 
 
+def gemv_traffic():
+    """DRAM bytes per launch of the config-1 GEMV from the committed ncu capture (or None)."""
+    try:
+        return json.load(open(os.path.join(ROOT, "profiles", "q4_gemv_config1_dram.json")))["dram_bytes_per_launch"]
+    except Exception:
+        return None
+
+
 def gemv_cpu(m, x, steps, budget_s, threads):
     """The reference's gemv_q4 (oracle/: k-split over the host threads, AVX-512) timed per
     call on this host: median of >= 5 calls, bounded by ~budget_s. Returns (GB/s, calls)."""
@@ -740,7 +748,7 @@ def run_q4_gemv(args, rank, world, local_rank):
         "e2e": {"value": e2e, "unit": "GB/s", "h2d_bytes_per_step": GEMV_K * 4, "d2h_bytes_per_step": GEMV_N * 4},
         "gpu_launches": K,
         "roofline": dict(bound="hbm", achieved=value, peak=peak, peak_kind=f"{peak_kind} hbm_gbs (copy)",
-                         unit="GB/s", frac=value / peak, traffic=None, kernel="q4 split-K GEMV (qora_q4_gemv)",
+                         unit="GB/s", frac=value / peak, traffic=gemv_traffic(), kernel="q4 split-K GEMV (qora_q4_gemv)",
                          bytes_per_launch=gemv_bytes(), us_per_launch=1000 * ms / K, launches_timed=K),
         "clocks": clk.summary(),
     }
