@@ -80,6 +80,30 @@ def test_gemv_shapes(pkg, qf, orc, torch, k, n):
     assert rel_l2(y, ref) < GEMV_TOL, rel_l2(y, ref)
 
 
+def test_gemv_alternating_shapes_reuse_scratch(pkg, qf, torch):
+    """The TMA GEMV's split-K partials travel as tagged words in one scratch that every
+    call reuses, and each tile's finisher zeroes them: calls alternating between shapes
+    with different tile and slot counts (config 1's gate_proj, a down_proj shape, a
+    narrower one) must each return their own result, bit-identical when repeated."""
+    rng = np.random.default_rng(29)
+    shapes = [(2048, 11008), (11008, 2048), (2048, 4096)]
+    cases = []
+    for k, n in shapes:
+        m = qf.synth_q4_matrix(rng, k, n)
+        x = rng.standard_normal(k).astype(np.float32)
+        cases.append((m, x, x.astype(np.float64) @ qf.dequant_q4(m, np.float64)))
+    first = {}
+    for rnd in range(3):
+        for i in (0, 1, 2, 1, 0, 2):
+            m, x, ref = cases[i]
+            y = run_gemv(pkg, torch, m, x)
+            assert rel_l2(y, ref) < GEMV_TOL, (rnd, i, rel_l2(y, ref))
+            if i in first:
+                assert np.array_equal(y, first[i]), (rnd, i)
+            else:
+                first[i] = y
+
+
 def test_gemv_extreme_scales(pkg, qf, torch):
     """Large and tiny f16 scales and inputs keep the subnormal-nibble arithmetic exact
     enough (no overflow of the 2^64 pre-scale, no flush of small products)."""
