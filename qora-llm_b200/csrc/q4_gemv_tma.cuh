@@ -73,11 +73,38 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
+// ---- split geometry (host and device; tests/cpp/gemv_split_check.cu checks it)
+// CTA c of G owns boxes [c*B/G, (c+1)*B/G) of the B = tiles * K / kBoxRows flattened row
+// boxes (tile-major): rows [*l0, *l1) of the flattened (tile, row) space
+__host__ __device__ inline void range_of(int c, int G, unsigned boxes, int* l0, int* l1) {
+  *l0 = (int)((unsigned)c * boxes / (unsigned)G) * kBoxRows;
+  *l1 = (int)((unsigned)(c + 1) * boxes / (unsigned)G) * kBoxRows;
+}
+// the CTAs holding rows of tile t: [*first, *last] (the owner of box p is ((p + 1) G - 1) / B)
+__host__ __device__ inline void tile_ctas(int t, int K, int G, unsigned boxes, int* first, int* last) {
+  const unsigned K1 = (unsigned)(K / kBoxRows);
+  *first = (int)((((unsigned)t * K1 + 1u) * (unsigned)G - 1u) / boxes);
+  *last = (int)((((unsigned)(t + 1) * K1) * (unsigned)G - 1u) / boxes);
+}
+// shapes the kernel takes on G CTAs: 256-column tiles, whole boxes of rows, at least one
+// and at most kMaxBoxes boxes per CTA, no more boxes per CTA than a tile has (so a range
+// touches at most two tiles: the kernel's two segments), 32-bit split arithmetic
+__host__ __device__ inline bool shape_ok(long long k, long long n, int G) {
+  if (k <= 0 || n <= 0 || n % kTileCols || k % kBoxRows) return false;
+  const long long boxes = (n / kTileCols) * (k / kBoxRows), per = (boxes + G - 1) / G;
+  return boxes >= G && boxes * G < (1ll << 32) && per <= kMaxBoxes && per <= k / kBoxRows;
+}
+// host: split-K slots per tile to allocate (every CTA owns at least floor(B / G) boxes)
+__host__ __device__ inline int slots_bound(int K, long long boxes, int G) {
+  const long long per = boxes / G > 0 ? boxes / G : 1;
+  return (int)((K / kBoxRows) / per) + 2;
+}
+
 // the CTA's segments (tile, first row, end row) of the flattened range [l0, l1)
 struct Segs {
   int n, t[2], r0[2], r1[2];
 };
-__device__ __forceinline__ Segs segs_of(int l0, int l1, int K) {
+__host__ __device__ __forceinline__ Segs segs_of(int l0, int l1, int K) {
   Segs s;
   s.n = 0;
   for (int p = l0; p < l1 && s.n < 2; ++s.n) {
@@ -98,10 +125,10 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kOffBar);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, gi = lane & 7, sub = lane >> 3;
   const int c = blockIdx.x, G = gridDim.x, K = a.K;
-  // CTA c owns boxes [c*B/G, (c+1)*B/G) of the B = tiles*K/kBoxRows flattened row boxes
-  // (host: K % kBoxRows == 0, B >= G, B * G < 2^32)
+  // whole boxes per CTA (host: K % kBoxRows == 0, B >= G, B * G < 2^32)
   const unsigned total = (unsigned)a.tiles * (unsigned)(K / kBoxRows);
-  const int l0 = (int)((unsigned)c * total / (unsigned)G) * kBoxRows, l1 = (int)((unsigned)(c + 1) * total / (unsigned)G) * kBoxRows;
+  int l0, l1;
+  range_of(c, G, total, &l0, &l1);
   const Segs sg = segs_of(l0, l1, K);
 
   if (tid == 0) {  // every box of the range at once
@@ -189,11 +216,9 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
     for (int e2 = 0; e2 < 8; ++e2) red[warp * kTileCols + gi * 32 + sub * 8 + e2] = v[e2];
     __syncthreads();
-    // this segment's partial (slot = CTA - first CTA of the tile), published tagged; the
-    // owner of box p is ((p + 1) G - 1) / B
-    const unsigned K1 = (unsigned)(K / kBoxRows);
-    const int slot_first = (int)((((unsigned)t * K1 + 1u) * (unsigned)G - 1u) / total);
-    const int slot_last = (int)((((unsigned)(t + 1) * K1) * (unsigned)G - 1u) / total);
+    // this segment's partial (slot = CTA - first CTA of the tile), published tagged
+    int slot_first, slot_last;
+    tile_ctas(t, K, G, total, &slot_first, &slot_last);
     const int slot = c - slot_first, nslots = slot_last - slot_first + 1;
     if (tid < kTileCols) {
       float y = 0.0f;

@@ -2682,10 +2682,8 @@ static qora_status q4_gemv_tma(const float* d_x, const uint8_t* d_packed, const 
                                float* d_y, cudaStream_t stream, int dev, bool* used) {
   *used = false;
   const int G = sm_count(dev);
+  if (!g1::shape_ok(k, n, G) || ((uintptr_t)d_packed | (uintptr_t)d_scales) % 16) return QORA_OK;
   const long long tiles = n / kTileCols, boxes = tiles * (long long)(k / g1::kBoxRows);
-  if (n % kTileCols || k % g1::kBoxRows || ((uintptr_t)d_packed | (uintptr_t)d_scales) % 16 || boxes < G ||
-      boxes * G >= (1ll << 32) || (boxes + G - 1) / G > g1::kMaxBoxes)
-    return QORA_OK;
   static std::once_flag attr_once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(attr_once, [] {
@@ -2700,7 +2698,7 @@ static qora_status q4_gemv_tma(const float* d_x, const uint8_t* d_packed, const 
   QCHECK(encode_2d(&mp, d_packed, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)n / 2, (uint64_t)k, 128, g1::kBoxRows));
   QCHECK(encode_2d(&ms, d_scales, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, (uint64_t)n / kGroup, (uint64_t)k, 8, g1::kBoxRows));
   // CTAs touching one tile: every CTA owns at least floor(boxes / G) boxes of the range
-  const int slots = (int)((k / g1::kBoxRows) / std::max(1ll, boxes / G)) + 2;
+  const int slots = g1::slots_bound(k, boxes, G);
   std::lock_guard<std::mutex> lk(g_entry_mu);
   EntryScratch* sc = nullptr;
   QCHECK(entry_scratch(dev, 0, 0, 0, &sc, (size_t)tiles * slots * kTileCols));

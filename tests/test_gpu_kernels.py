@@ -69,7 +69,8 @@ def test_gemv_config1(pkg, qf, orc, torch):
 
 
 @pytest.mark.parametrize("k,n", [(1, 32), (3, 64), (7, 96), (100, 288), (2048, 512),
-                                 (2048, 3072), (11008, 2048), (513, 11008), (4096, 256)])
+                                 (2048, 3072), (11008, 2048), (513, 11008), (4096, 256),
+                                 (64, 65536)])  # last: more tiles than CTAs, one box each
 def test_gemv_shapes(pkg, qf, orc, torch, k, n):
     rng = np.random.default_rng(k + 31 * n)
     m = qf.synth_q4_matrix(rng, k, n)
