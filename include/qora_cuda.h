@@ -229,7 +229,10 @@ qora_status qora_layer_step(qora_engine* engine, qora_kv* kv, uint32_t layer,
 /* Q4 GEMV in the reference layout: y[n] = x[k] . W[k][n] (replaces `gemv_q4`,
  * src/gemv.rs:646-675, and `gemv_q4_avx512`, src/simd.rs:44-83). packed/scales are the
  * F1-layout arrays as in the file; n % 32 == 0. Scratch for the split-K partial sums is
- * allocated on first use and cached by the library (per device). */
+ * allocated (zeroed) on first use and cached by the library (per device); every call
+ * leaves it zeroed again, and calls on one device share it, so calls that may run at the
+ * same time on different streams must be ordered by the caller. Results are
+ * deterministic (fixed summation order, no float atomics). */
 qora_status qora_q4_gemv(const float* d_x, const uint8_t* d_packed,
                          const uint16_t* d_scales, uint64_t k, uint64_t n, float* d_y,
                          void* stream);
